@@ -1,0 +1,151 @@
+/*
+ * tk_kernels.h -- C ABI of libtk_kernels.so, the sm_100a kernel library behind
+ * torch_kunlun's dense-op hot path.
+ *
+ * Conventions (every entry point):
+ *   - returns int status: 0 (TK_OK) on success, > 0 on error; the message of
+ *     the last error on the calling thread is tk_last_error_string();
+ *   - no C++ exceptions cross the boundary; no allocation: device scratch is
+ *     a caller-provided workspace sized by the matching *_workspace_size call;
+ *   - all pointers are device pointers unless stated; `stream` is a
+ *     cudaStream_t (NULL = legacy default stream of the current device);
+ *   - work is enqueued asynchronously on `stream`; nothing synchronises;
+ *   - element strides are in elements, not bytes;
+ *   - functions are reentrant and keep no per-call global state.
+ *
+ * Each function names the reference interface it replaces: the reference
+ * calls Baidu XDNN (baidu::xpu::api::*) from the files cited.
+ */
+#ifndef TK_KERNELS_H
+#define TK_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TK_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define TK_API __attribute__((visibility("default")))
+#else
+#define TK_API
+#endif
+
+typedef enum {
+    TK_OK = 0,
+    TK_ERR_INVALID_ARG = 1,
+    TK_ERR_UNSUPPORTED = 2,
+    TK_ERR_CUDA = 3,
+    TK_ERR_WORKSPACE = 4,
+    TK_ERR_DEVICE = 5
+} tk_status_t;
+
+typedef enum { TK_DTYPE_F16 = 0, TK_DTYPE_F32 = 1 } tk_dtype_t;
+
+typedef enum {
+    TK_ACT_NONE = 0,
+    TK_ACT_RELU = 1,
+    TK_ACT_GELU = 2,      /* erf form */
+    TK_ACT_GELU_TANH = 3, /* tanh approximation */
+    TK_ACT_SILU = 4
+} tk_act_t;
+
+/* ---- library ------------------------------------------------------------- */
+
+TK_API int tk_abi_version(void);
+TK_API const char* tk_last_error_string(void);
+
+/* Reads and clears the device-side error word of `device` (a bounded wait
+ * inside a kernel that timed out records a code there).  Synchronises the
+ * device.  *code_out = 0 means no error was recorded. */
+TK_API int tk_device_error(int device, unsigned* code_out);
+
+/* ---- quantisation ----------------------------------------------------------
+ * Replaces the max-abs and int16-quantise steps that XDNN performs inside
+ * fc/conv2d when the max pointers are null (csrc/ops.cpp:224-227,
+ * csrc/ops.cpp:264-268, csrc/ops_nn.cpp:214-218).
+ */
+
+/* amax_out[s] = max |x[s*slice_stride + i]|, i in [0, slice_len), NaN
+ * dominating.  Each slice is a dense memory range of slice_len elements. */
+TK_API int tk_amax(tk_dtype_t dtype, const void* x, int64_t nslices, int64_t slice_stride,
+            int64_t slice_len, float* amax_out, void* stream);
+
+/* Quantise a batch of strided [rows, cols] views to int16 with scale
+ * 32767/amax[b * amax_stride] and store them as two limb planes,
+ * q = 256*hi + lo: limbs + ((b*2 + 0)*rows + r)*ld holds the signed high
+ * limbs and plane 1 the unsigned low limbs, ld = round_up(cols, 16); columns
+ * [cols, ld) are written as zero.  View element (b, r, c) is at
+ * x[b*sb + r*sr + c*sc]. */
+TK_API int tk_quantize_limbs(tk_dtype_t dtype, const void* x, int64_t batch, int64_t rows,
+                      int64_t cols, int64_t sb, int64_t sr, int64_t sc, const float* amax,
+                      int64_t amax_stride, int8_t* limbs, void* stream);
+
+/* ---- quantised GEMM ---------------------------------------------------------
+ * Replaces baidu::xpu::api::fc<T,T,T,TGEMM> as called by fc_impl
+ * (csrc/ops.cpp:210-230, mm and linear), by bmm_impl (csrc/ops_nn.cpp:199-221,
+ * one fc per slice), and the separate epilogue launches that follow it: the
+ * bias add of linear (csrc/ops.cpp:491-493), the alpha/beta scale and add of
+ * addmm (csrc/autograd.cpp:192-218) and baddbmm
+ * (csrc/linalg_extra.cpp:85-93), and activations (csrc/ops.cpp:151-160,
+ * csrc/ops_nn.cpp:132-147, csrc/ops_extra.cpp:71).
+ *
+ *   out[b][m][n] = epilogue( sum_k q(A[b][m][k]) * q(B[b][n][k]) )
+ *
+ * A element (b,m,k) is at a[b*a_sb + m*a_sm + k*a_sk]; B element (b,n,k) at
+ * b[b*b_sb + n*b_sn + k*b_sk] (so a row-major W[N,K] of linear has
+ * b_sn = K, b_sk = 1 and a row-major [K,N] operand of mm has b_sn = 1,
+ * b_sk = N).  out has unit stride along n.  With per_slice_scales = 1 every
+ * batch slice of A and of B gets its own amax (bmm); with 0 one amax covers
+ * the whole operand (every slice must then be laid out densely).
+ * The epilogue (in order): dequantise and round to dtype; if alpha != 1
+ * multiply by alpha and round; if bias add bias[n] and round; if addend and
+ * beta != 0 add beta*addend (addend element (b,m,n) at
+ * addend[b*add_sb + m*add_sm + n*add_sn], strides may be 0 to broadcast) and
+ * round; apply act.  K must be <= 32768.
+ */
+typedef struct {
+    tk_dtype_t dtype;
+    int64_t batch, m, n, k;
+    const void* a;
+    int64_t a_sb, a_sm, a_sk;
+    const void* b;
+    int64_t b_sb, b_sn, b_sk;
+    void* out;
+    int64_t out_sb, out_sm;
+    const void* bias;
+    const void* addend;
+    int64_t add_sb, add_sm, add_sn;
+    float alpha, beta;
+    tk_act_t act;
+    int per_slice_scales;
+    /* Optional precomputed amax (device, one float per slice or one per
+     * operand); NULL means computed by the call (the reference's null
+     * x_maxptr / w_maxptr, csrc/ops.cpp:227). */
+    const float* amax_a;
+    const float* amax_b;
+} tk_qgemm_desc_t;
+
+TK_API size_t tk_qgemm_workspace_size(const tk_qgemm_desc_t* desc);
+TK_API int tk_qgemm(const tk_qgemm_desc_t* desc, void* workspace, size_t workspace_bytes,
+             void* stream);
+
+/* Same contract computed by a plain CUDA-core kernel (one output per thread).
+ * Used to cross-check the tensor-core path on the device; not fast. */
+TK_API int tk_qgemm_simt(const tk_qgemm_desc_t* desc, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+/* Debug view of the tensor-core GEMM: writes the three int32 limb-product
+ * accumulators (hi*hi, hi*lo + lo*hi, lo*lo) of slice 0 to acc3
+ * ([3][m][n], int32) in addition to out. */
+TK_API int tk_qgemm_debug(const tk_qgemm_desc_t* desc, void* workspace, size_t workspace_bytes,
+                   int32_t* acc3, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TK_KERNELS_H */

@@ -1,0 +1,336 @@
+"""CPU oracle for the int16-quantised dense path (test infrastructure only).
+
+Nothing in the shipped package imports this module: only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s ``cpu_baseline`` leg do, and
+only as the checker.  The arithmetic contract is stated in ``tk_oracle.c``;
+this module wraps the C restatement with numpy and composes the reference's
+operator-level dataflow from it:
+
+* ``fc``       -- csrc/ops.cpp:210-230 (per-tensor quantised fc), with the bias
+                  added after rounding as in csrc/ops.cpp:480-495 and the
+                  addmm alpha/beta order of csrc/autograd.cpp:192-218.
+* ``bmm``      -- csrc/ops_nn.cpp:199-221 (one fc per batch slice, so every
+                  slice has its own scales).
+* ``baddbmm``  -- csrc/linalg_extra.cpp:85-93.
+* ``conv2d``   -- csrc/ops.cpp:237-285 (whole-tensor scales, bias afterwards).
+* ``sdpa``     -- torch_kunlun/kunlun/attention.py:36-107 (bmm, scale, mask
+                  add, softmax, bmm).
+
+Parity status: unpinned at bit level -- the reference's arithmetic is in a
+closed vendor library with no golden vectors; see tk_oracle.c.
+
+Large GEMMs use an exact shortcut: int16 x int16 products are < 2^30 and, for
+K < 2^23, every partial sum is an integer below 2^53, so a float64 matmul of
+the integer-valued matrices is exact.  ``tests/test_oracle.py`` checks the
+shortcut against the scalar int64 loop.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "libtk_oracle.so")
+_lib = None
+
+F16 = 0
+F32 = 1
+ACT_NONE = 0
+ACT_RELU = 1
+Q = 32767.0
+
+
+def build() -> str:
+    """Compile the C oracle with its Makefile (strict IEEE flags)."""
+    src = os.path.join(_HERE, "tk_oracle.c")
+    if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+        subprocess.check_call(["make", "-s", "-C", _HERE])
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(_LIB_PATH)
+        p, i64, f32, f64, i32 = (ctypes.c_void_p, ctypes.c_int64, ctypes.c_float,
+                                 ctypes.c_double, ctypes.c_int)
+        L.tko_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.tko_f16_to_f32.restype = f32
+        L.tko_f64_to_f16.argtypes = [f64]
+        L.tko_f64_to_f16.restype = ctypes.c_uint16
+        L.tko_f32_to_f16.argtypes = [f32]
+        L.tko_f32_to_f16.restype = ctypes.c_uint16
+        L.tko_amax2d.argtypes = [p, i32, i64, i64, i64, i64]
+        L.tko_amax2d.restype = f32
+        L.tko_amax.argtypes = [p, i32, i64]
+        L.tko_amax.restype = f32
+        L.tko_quant_inv.argtypes = [f32]
+        L.tko_quant_inv.restype = f32
+        L.tko_quant2d.argtypes = [p, i32, i64, i64, i64, i64, f32, p]
+        L.tko_quant.argtypes = [p, i32, i64, f32, p]
+        L.tko_limbs.argtypes = [p, i64, p, p]
+        L.tko_gemm_i16.argtypes = [i64, i64, i64, p, i64, i64, p, i64, i64, p]
+        L.tko_dequant_scale.argtypes = [f32, f32]
+        L.tko_dequant_scale.restype = f64
+        L.tko_epilogue.argtypes = [i32, i64, i64, p, f32, f32, f32, p, p, i64, i64,
+                                   f32, i32, p, i64]
+        L.tko_conv2d_i16.argtypes = [i64] * 14 + [p, p, p]
+        _lib = L
+    return _lib
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def _dt(a: np.ndarray) -> int:
+    if a.dtype == np.float16:
+        return F16
+    if a.dtype == np.float32:
+        return F32
+    raise TypeError(f"oracle supports float16/float32, got {a.dtype}")
+
+
+# ---- scalar helpers --------------------------------------------------------
+
+
+def f64_to_f16_bits(v: float) -> int:
+    return int(lib().tko_f64_to_f16(float(v)))
+
+
+def amax(x: np.ndarray) -> np.float32:
+    x = np.ascontiguousarray(x)
+    return np.float32(lib().tko_amax(_ptr(x), _dt(x), x.size))
+
+
+def quant(x: np.ndarray, a: float | None = None) -> np.ndarray:
+    """int16 quantisation of a whole tensor with one scale."""
+    x = np.ascontiguousarray(x)
+    if a is None:
+        a = amax(x)
+    q = np.empty(x.shape, dtype=np.int16)
+    lib().tko_quant(_ptr(x), _dt(x), x.size, float(a), _ptr(q))
+    return q
+
+
+def limbs(q: np.ndarray):
+    q = np.ascontiguousarray(q, dtype=np.int16)
+    hi = np.empty(q.shape, dtype=np.int8)
+    lo = np.empty(q.shape, dtype=np.uint8)
+    lib().tko_limbs(_ptr(q), q.size, _ptr(hi), _ptr(lo))
+    return hi, lo
+
+
+def dequant_scale(amax_a: float, amax_b: float) -> float:
+    return float(lib().tko_dequant_scale(float(amax_a), float(amax_b)))
+
+
+# ---- integer GEMM ------------------------------------------------------------
+
+
+def gemm_i16_exact(qa: np.ndarray, qb: np.ndarray) -> np.ndarray:
+    """acc = qa @ qb in int64 via the exact float64 shortcut (K < 2^23)."""
+    assert qa.shape[-1] == qb.shape[-2] and qa.shape[-1] < (1 << 23)
+    return np.matmul(qa.astype(np.float64), qb.astype(np.float64)).astype(np.int64)
+
+
+def gemm_i16_scalar(qa: np.ndarray, qb: np.ndarray) -> np.ndarray:
+    """acc = qa @ qb with the C int64 loop (slow; used to pin the shortcut)."""
+    qa = np.ascontiguousarray(qa, dtype=np.int16)
+    qb = np.ascontiguousarray(qb, dtype=np.int16)
+    M, K = qa.shape
+    K2, N = qb.shape
+    assert K == K2
+    acc = np.empty((M, N), dtype=np.int64)
+    lib().tko_gemm_i16(M, N, K, _ptr(qa), K, 1, _ptr(qb), N, 1, _ptr(acc))
+    return acc
+
+
+def epilogue(acc: np.ndarray, amax_a, amax_b, dtype, alpha=1.0, bias=None,
+             addend=None, beta=0.0, act=ACT_NONE) -> np.ndarray:
+    """Apply the dequant/bias/addend/activation contract to an int64 tile."""
+    acc = np.ascontiguousarray(acc, dtype=np.int64)
+    M, N = acc.shape
+    dt = F16 if np.dtype(dtype) == np.float16 else F32
+    out = np.empty((M, N), dtype=np.float16 if dt == F16 else np.float32)
+    bias_p = None
+    if bias is not None:
+        bias = np.ascontiguousarray(bias, dtype=out.dtype).reshape(-1)
+        assert bias.size == N
+        bias_p = _ptr(bias)
+    add_p, sm, sn = None, 0, 0
+    if addend is not None and beta != 0.0:
+        addend = np.ascontiguousarray(np.broadcast_to(
+            np.asarray(addend, dtype=out.dtype), (M, N)))
+        add_p, sm, sn = _ptr(addend), N, 1
+    lib().tko_epilogue(dt, M, N, _ptr(acc), float(amax_a), float(amax_b), float(alpha),
+                       bias_p, add_p, sm, sn, float(beta), int(act), _ptr(out), N)
+    return out
+
+
+# ---- operator-level compositions ---------------------------------------------
+
+
+def fc(x: np.ndarray, w: np.ndarray, w_trans: bool, bias=None, alpha=1.0,
+       addend=None, beta=0.0, act=ACT_NONE, scalar=False):
+    """Quantised fc: y = epilogue(q16(x) @ op(q16(w))).
+
+    x is [M,K]; w is [N,K] when w_trans (linear) and [K,N] otherwise (mm).
+    Returns (y, acc, amax_x, amax_w).
+    """
+    ax, aw = amax(x), amax(w)
+    qx, qw = quant(x, ax), quant(w, aw)
+    qb = qw.T if w_trans else qw
+    acc = gemm_i16_scalar(qx, qb) if scalar else gemm_i16_exact(qx, qb)
+    y = epilogue(acc, ax, aw, x.dtype, alpha, bias, addend, beta, act)
+    return y, acc, ax, aw
+
+
+def linear(x, w, bias=None, act=ACT_NONE):
+    return fc(x, w, True, bias=bias, act=act)[0]
+
+
+def mm(a, b):
+    return fc(a, b, False)[0]
+
+
+def addmm(self_, a, b, beta=1.0, alpha=1.0):
+    return fc(a, b, False, alpha=alpha, addend=self_, beta=beta)[0]
+
+
+def bmm(a: np.ndarray, b: np.ndarray, alpha=1.0, addend=None, beta=0.0) -> np.ndarray:
+    """Per-slice quantised batched matmul: a [B,M,K] @ b [B,K,N]."""
+    B = a.shape[0]
+    outs = []
+    for i in range(B):
+        add_i = None if addend is None else np.broadcast_to(addend, (B,) + addend.shape[-2:])[i]
+        outs.append(fc(a[i], b[i], False, alpha=alpha, addend=add_i, beta=beta)[0])
+    return np.stack(outs)
+
+
+def baddbmm(self_, a, b, beta=1.0, alpha=1.0):
+    return bmm(a, b, alpha=alpha, addend=self_, beta=beta)
+
+
+def conv_out_hw(H, W, KH, KW, stride, pad, dil):
+    OH = (H + 2 * pad[0] - dil[0] * (KH - 1) - 1) // stride[0] + 1
+    OW = (W + 2 * pad[1] - dil[1] * (KW - 1) - 1) // stride[1] + 1
+    return OH, OW
+
+
+def conv2d_acc(qx: np.ndarray, qw: np.ndarray, stride, pad, dil, groups, scalar=False):
+    """int64 conv accumulators of quantised NCHW input and OIHW weight."""
+    NB, C, H, W = qx.shape
+    F, cg, KH, KW = qw.shape
+    OH, OW = conv_out_hw(H, W, KH, KW, stride, pad, dil)
+    if scalar:
+        acc = np.empty((NB, F, OH, OW), dtype=np.int64)
+        lib().tko_conv2d_i16(NB, C, H, W, F, KH, KW, stride[0], stride[1], pad[0], pad[1],
+                             dil[0], dil[1], groups, _ptr(np.ascontiguousarray(qx)),
+                             _ptr(np.ascontiguousarray(qw)), _ptr(acc))
+        return acc
+    xp = np.zeros((NB, C, H + 2 * pad[0], W + 2 * pad[1]), dtype=np.float64)
+    xp[:, :, pad[0]:pad[0] + H, pad[1]:pad[1] + W] = qx
+    fg = F // groups
+    acc = np.zeros((NB, F, OH, OW), dtype=np.float64)
+    for g in range(groups):
+        wg = qw[g * fg:(g + 1) * fg].astype(np.float64).reshape(fg, cg * KH * KW)
+        cols = np.empty((NB, cg, KH, KW, OH, OW), dtype=np.float64)
+        for r in range(KH):
+            for s in range(KW):
+                h0, w0 = r * dil[0], s * dil[1]
+                cols[:, :, r, s] = xp[:, g * cg:(g + 1) * cg,
+                                      h0:h0 + stride[0] * (OH - 1) + 1:stride[0],
+                                      w0:w0 + stride[1] * (OW - 1) + 1:stride[1]]
+        cols = cols.reshape(NB, cg * KH * KW, OH * OW)
+        acc[:, g * fg:(g + 1) * fg] = np.einsum("fk,bkp->bfp", wg, cols).reshape(NB, fg, OH, OW)
+    return acc.astype(np.int64)
+
+
+def conv2d(x: np.ndarray, w: np.ndarray, bias=None, stride=(1, 1), pad=(0, 0), dil=(1, 1),
+           groups=1, scalar=False) -> np.ndarray:
+    ax, aw = amax(x), amax(w)
+    acc = conv2d_acc(quant(x, ax), quant(w, aw), stride, pad, dil, groups, scalar)
+    NB, F, OH, OW = acc.shape
+    # bias broadcasts over [N, F, OH, OW] along F: flatten so F*OH*OW is one row
+    # per image and expand the bias to match (csrc/ops.cpp:271-283).
+    flat = acc.transpose(0, 1, 2, 3).reshape(NB * F, OH * OW)
+    add = None
+    if bias is not None:
+        add = np.repeat(np.asarray(bias, dtype=x.dtype).reshape(1, F), NB, 0).reshape(NB * F, 1)
+        add = np.broadcast_to(add, flat.shape)
+    y = epilogue(flat, ax, aw, x.dtype, addend=add, beta=1.0 if add is not None else 0.0)
+    return y.reshape(NB, F, OH, OW)
+
+
+# ---- float row ops (tolerance-level references, float64 internally) ----------
+
+
+def softmax(x: np.ndarray, axis=-1) -> np.ndarray:
+    xd = x.astype(np.float64)
+    m = xd.max(axis=axis, keepdims=True)
+    e = np.exp(xd - m)
+    return (e / e.sum(axis=axis, keepdims=True)).astype(x.dtype)
+
+
+def layer_norm(x: np.ndarray, gamma, beta, eps) -> np.ndarray:
+    xd = x.astype(np.float64)
+    mu = xd.mean(-1, keepdims=True)
+    var = ((xd - mu) ** 2).mean(-1, keepdims=True)
+    y = (xd - mu) / np.sqrt(var + eps)
+    if gamma is not None:
+        y = y * np.asarray(gamma, dtype=np.float64)
+    if beta is not None:
+        y = y + np.asarray(beta, dtype=np.float64)
+    return y.astype(x.dtype)
+
+
+def gelu(x: np.ndarray) -> np.ndarray:
+    from math import erf, sqrt
+    xd = x.astype(np.float64)
+    v = np.vectorize(lambda t: 0.5 * t * (1.0 + erf(t / sqrt(2.0))))(xd)
+    return v.astype(x.dtype)
+
+
+def silu(x: np.ndarray) -> np.ndarray:
+    xd = x.astype(np.float64)
+    return (xd / (1.0 + np.exp(-xd))).astype(x.dtype)
+
+
+def round_t(v: np.ndarray, dtype) -> np.ndarray:
+    """Round float64 values to T (nearest-even) through the C helper for fp16."""
+    v = np.asarray(v, dtype=np.float64)
+    if np.dtype(dtype) == np.float32:
+        return v.astype(np.float32)
+    L = lib()
+    flat = v.reshape(-1)
+    bits = np.fromiter((L.tko_f64_to_f16(float(t)) for t in flat), dtype=np.uint16,
+                       count=flat.size)
+    return bits.view(np.float16).reshape(v.shape)
+
+
+def sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask=None, scale=None):
+    """The reference's SDPA composition over [BH, L, E] slices.
+
+    Steps (torch_kunlun/kunlun/attention.py:85-106): per-slice quantised bmm
+    q @ k^T, multiply by the scale (rounded to T), add the additive mask
+    (rounded to T), softmax along the last axis, per-slice quantised bmm with v.
+    The softmax step is computed in float64 here, so results are compared with
+    a tolerance.
+    """
+    BH, L, E = q.shape
+    kt = np.ascontiguousarray(np.swapaxes(k, 1, 2))
+    s = bmm(q, kt)
+    factor = (1.0 / np.sqrt(E)) if scale is None else float(scale)
+    if factor != 1.0:
+        s = round_t(s.astype(np.float32) * np.float32(factor), q.dtype)
+    if mask is not None:
+        s = round_t(s.astype(np.float32) + np.broadcast_to(mask, s.shape).astype(np.float32),
+                    q.dtype)
+    p = softmax(s, -1)
+    return bmm(p, v)

@@ -1,0 +1,413 @@
+// eltwise.cu -- device-side data movement and elementwise ops of the
+// kunlun backend: strided copy with dtype conversion (replaces the host
+// staging of csrc/ops.cpp:289-418), fill (csrc/ops.cpp:162-208 plus the
+// host-pattern path), broadcast binary ops (add/sub/mul/div:
+// csrc/ops.cpp:117-149, csrc/autograd.cpp:40-100) and activations
+// (relu csrc/ops.cpp:151-160, gelu csrc/ops_nn.cpp:132-147, silu
+// csrc/ops_extra.cpp:71, scale csrc/autograd.cpp:586-601).
+//
+// All of these are HBM-bound; arithmetic is fp32 with one rounding to the
+// output type, as in the reference's XDNN elementwise calls.
+#include <cuda_bf16.h>
+
+#include "tk_internal.h"
+
+namespace tk {
+namespace {
+
+constexpr int kMaxDims = 8;
+constexpr int kThreads = 256;
+
+struct Strided {
+    int ndim;
+    int64_t sizes[kMaxDims];
+    int64_t s0[kMaxDims];  // strides of operand 0 (destination / a)
+    int64_t s1[kMaxDims];  // strides of operand 1 (source / b)
+};
+
+__device__ __forceinline__ void offsets(const Strided& d, int64_t i, int64_t& o0, int64_t& o1) {
+    o0 = 0;
+    o1 = 0;
+#pragma unroll 1
+    for (int k = d.ndim - 1; k >= 0; --k) {
+        const int64_t sz = d.sizes[k];
+        const int64_t idx = i % sz;
+        i /= sz;
+        o0 += idx * d.s0[k];
+        o1 += idx * d.s1[k];
+    }
+}
+
+// ---- scalar type codes (tk_scalar_t in tk_kernels.h) ----
+enum : int { T_BOOL = 0, T_U8, T_I8, T_I16, T_I32, T_I64, T_F16, T_BF16, T_F32, T_F64 };
+
+__host__ __device__ inline int scalar_size(int t) {
+    switch (t) {
+        case T_BOOL: case T_U8: case T_I8: return 1;
+        case T_I16: case T_F16: case T_BF16: return 2;
+        case T_I32: case T_F32: return 4;
+        default: return 8;
+    }
+}
+
+__device__ __forceinline__ double load_any(const void* p, int t, int64_t i) {
+    switch (t) {
+        case T_BOOL: return static_cast<const uint8_t*>(p)[i] ? 1.0 : 0.0;
+        case T_U8: return static_cast<const uint8_t*>(p)[i];
+        case T_I8: return static_cast<const int8_t*>(p)[i];
+        case T_I16: return static_cast<const int16_t*>(p)[i];
+        case T_I32: return static_cast<const int32_t*>(p)[i];
+        case T_I64: return static_cast<double>(static_cast<const long long*>(p)[i]);
+        case T_F16: return __half2float(static_cast<const __half*>(p)[i]);
+        case T_BF16: return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+        case T_F32: return static_cast<const float*>(p)[i];
+        default: return static_cast<const double*>(p)[i];
+    }
+}
+
+// binary64 -> binary32 toward zero with the sticky last bit (round to odd),
+// so that a following nearest-even rounding to a narrower float is a single
+// correct rounding (Boldo & Melquiond, 2005).
+__device__ __forceinline__ float d2f_odd(double d) {
+    float f = __double2float_rz(d);
+    if (static_cast<double>(f) != d) f = __uint_as_float(__float_as_uint(f) | 1u);
+    return f;
+}
+
+__device__ __forceinline__ void store_any(void* p, int t, int64_t i, double v) {
+    switch (t) {
+        case T_BOOL: static_cast<uint8_t*>(p)[i] = (v != 0.0) ? 1 : 0; break;
+        case T_U8: static_cast<uint8_t*>(p)[i] = static_cast<uint8_t>(static_cast<long long>(v)); break;
+        case T_I8: static_cast<int8_t*>(p)[i] = static_cast<int8_t>(static_cast<long long>(v)); break;
+        case T_I16: static_cast<int16_t*>(p)[i] = static_cast<int16_t>(static_cast<long long>(v)); break;
+        case T_I32: static_cast<int32_t*>(p)[i] = static_cast<int32_t>(static_cast<long long>(v)); break;
+        case T_I64: static_cast<long long*>(p)[i] = static_cast<long long>(v); break;
+        case T_F16: static_cast<__half*>(p)[i] = __float2half_rn(d2f_odd(v)); break;
+        case T_BF16: static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(d2f_odd(v)); break;
+        case T_F32: static_cast<float*>(p)[i] = __double2float_rn(v); break;
+        default: static_cast<double*>(p)[i] = v; break;
+    }
+}
+
+template <typename E>
+__global__ void copy_same_kernel(E* __restrict__ dst, const E* __restrict__ src, int64_t n,
+                                 Strided d) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t od, os;
+        offsets(d, i, od, os);
+        dst[od] = src[os];
+    }
+}
+
+__global__ void copy_convert_kernel(void* __restrict__ dst, int dt, const void* __restrict__ src,
+                                    int st, int64_t n, Strided d) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t od, os;
+        offsets(d, i, od, os);
+        store_any(dst, dt, od, load_any(src, st, os));
+    }
+}
+
+// Dense conversions between f16 and f32 (the common .half()/.float()).
+__global__ void f32_to_f16_kernel(__half* __restrict__ dst, const float* __restrict__ src, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        dst[i] = __float2half_rn(src[i]);
+}
+
+__global__ void f16_to_f32_kernel(float* __restrict__ dst, const __half* __restrict__ src, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        dst[i] = __half2float(src[i]);
+}
+
+template <typename E>
+__global__ void fill_kernel(E* __restrict__ dst, E v, int64_t n, Strided d) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t od, unused;
+        offsets(d, i, od, unused);
+        dst[od] = v;
+    }
+}
+
+template <typename E>
+__global__ void fill_dense_kernel(E* __restrict__ dst, E v, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        dst[i] = v;
+}
+
+// ---- binary / unary on f16, f32 ----
+template <typename T> __device__ __forceinline__ float ld(const T* p, int64_t i);
+template <> __device__ __forceinline__ float ld<__half>(const __half* p, int64_t i) { return __half2float(p[i]); }
+template <> __device__ __forceinline__ float ld<float>(const float* p, int64_t i) { return p[i]; }
+template <typename T> __device__ __forceinline__ void st(T* p, int64_t i, float v);
+template <> __device__ __forceinline__ void st<__half>(__half* p, int64_t i, float v) { p[i] = __float2half_rn(v); }
+template <> __device__ __forceinline__ void st<float>(float* p, int64_t i, float v) { p[i] = v; }
+
+__device__ __forceinline__ float bin_apply(int op, float a, float b, float alpha) {
+    switch (op) {
+        case TK_BIN_ADD: return alpha == 1.0f ? __fadd_rn(a, b) : __fadd_rn(a, __fmul_rn(alpha, b));
+        case TK_BIN_SUB: return alpha == 1.0f ? __fsub_rn(a, b) : __fsub_rn(a, __fmul_rn(alpha, b));
+        case TK_BIN_MUL: return __fmul_rn(a, b);
+        default: return __fdiv_rn(a, b);
+    }
+}
+
+template <typename T>
+__global__ void binary_kernel(int op, const T* __restrict__ a, const T* __restrict__ b,
+                              T* __restrict__ out, int64_t n, float alpha, Strided d) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t oa, ob;
+        offsets(d, i, oa, ob);
+        st<T>(out, i, bin_apply(op, ld<T>(a, oa), ld<T>(b, ob), alpha));
+    }
+}
+
+template <typename T>
+__global__ void binary_dense_kernel(int op, const T* __restrict__ a, const T* __restrict__ b,
+                                    T* __restrict__ out, int64_t n, float alpha) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        st<T>(out, i, bin_apply(op, ld<T>(a, i), ld<T>(b, i), alpha));
+}
+
+__device__ __forceinline__ float un_apply(int op, float x, float p0, float p1) {
+    switch (op) {
+        case TK_UN_RELU: return (x > 0.0f || x != x) ? x : 0.0f;
+        case TK_UN_GELU: return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+        case TK_UN_GELU_TANH: {
+            const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+            return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+        }
+        case TK_UN_SILU: return x / (1.0f + expf(-x));
+        case TK_UN_SCALE: return __fadd_rn(__fmul_rn(x, p0), p1);
+        default: return x;
+    }
+}
+
+template <typename T>
+__global__ void unary_kernel(int op, const T* __restrict__ x, T* __restrict__ y, int64_t n, float p0,
+                             float p1) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        st<T>(y, i, un_apply(op, ld<T>(x, i), p0, p1));
+}
+
+// silu(gate) * up, each rounded to T like the reference's separate swish and mul.
+template <typename T>
+__global__ void silu_mul_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ y,
+                                int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float h = un_apply(TK_UN_SILU, ld<T>(g, i), 0.f, 0.f);
+        h = ld<T>(reinterpret_cast<const T*>(&h), 0) * 0.0f + h;  // keep in fp32
+        T hr;
+        st<T>(&hr, 0, h);
+        st<T>(y, i, __fmul_rn(ld<T>(&hr, 0), ld<T>(u, i)));
+    }
+}
+
+int grid_for(int64_t n) {
+    int64_t g = ceil_div(n, kThreads);
+    const int64_t cap = static_cast<int64_t>(sm_count(current_device())) * 16;
+    return static_cast<int>(std::max<int64_t>(1, std::min(g, cap)));
+}
+
+int fill_strided_desc(Strided& d, int ndim, const int64_t* sizes, const int64_t* s0,
+                      const int64_t* s1, int64_t& n) {
+    TK_CHECK_ARG(ndim >= 0 && ndim <= kMaxDims, "at most %d dims supported, got %d", kMaxDims, ndim);
+    d.ndim = ndim;
+    n = 1;
+    for (int i = 0; i < ndim; ++i) {
+        TK_CHECK_ARG(sizes[i] >= 0, "negative size");
+        d.sizes[i] = sizes[i];
+        d.s0[i] = s0 ? s0[i] : 0;
+        d.s1[i] = s1 ? s1[i] : 0;
+        n *= sizes[i];
+    }
+    if (ndim == 0) {
+        d.ndim = 1;
+        d.sizes[0] = 1;
+        d.s0[0] = d.s1[0] = 0;
+    }
+    return TK_OK;
+}
+
+bool is_dense(int ndim, const int64_t* sizes, const int64_t* strides) {
+    int64_t expect = 1;
+    for (int i = ndim - 1; i >= 0; --i) {
+        if (sizes[i] != 1 && strides[i] != expect) return false;
+        expect *= sizes[i];
+    }
+    return true;
+}
+
+}  // namespace
+}  // namespace tk
+
+extern "C" {
+
+int tk_copy_strided(void* dst, int dst_type, const void* src, int src_type, int ndim,
+                    const int64_t* sizes, const int64_t* dst_strides, const int64_t* src_strides,
+                    void* stream_) {
+    using namespace tk;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    TK_CHECK_ARG(dst_type >= 0 && dst_type <= T_F64 && src_type >= 0 && src_type <= T_F64,
+                 "tk_copy_strided: bad scalar type");
+    Strided d;
+    int64_t n = 0;
+    int rc = fill_strided_desc(d, ndim, sizes, dst_strides, src_strides, n);
+    if (rc) return rc;
+    if (n == 0) return TK_OK;
+    TK_CHECK_ARG(dst && src, "tk_copy_strided: NULL pointer");
+    const bool dd = is_dense(ndim, sizes, dst_strides), sd = is_dense(ndim, sizes, src_strides);
+    if (dst_type == src_type && dd && sd) {
+        TK_CUDA_TRY(cudaMemcpyAsync(dst, src, static_cast<size_t>(n) * scalar_size(dst_type),
+                                    cudaMemcpyDeviceToDevice, stream));
+        return TK_OK;
+    }
+    const int grid = grid_for(n);
+    if (dd && sd && dst_type == T_F16 && src_type == T_F32) {
+        f32_to_f16_kernel<<<grid, kThreads, 0, stream>>>(static_cast<__half*>(dst),
+                                                         static_cast<const float*>(src), n);
+        return launch_status("copy f32->f16");
+    }
+    if (dd && sd && dst_type == T_F32 && src_type == T_F16) {
+        f16_to_f32_kernel<<<grid, kThreads, 0, stream>>>(static_cast<float*>(dst),
+                                                         static_cast<const __half*>(src), n);
+        return launch_status("copy f16->f32");
+    }
+    if (dst_type == src_type) {
+        switch (scalar_size(dst_type)) {
+            case 1: copy_same_kernel<uint8_t><<<grid, kThreads, 0, stream>>>(
+                        static_cast<uint8_t*>(dst), static_cast<const uint8_t*>(src), n, d); break;
+            case 2: copy_same_kernel<uint16_t><<<grid, kThreads, 0, stream>>>(
+                        static_cast<uint16_t*>(dst), static_cast<const uint16_t*>(src), n, d); break;
+            case 4: copy_same_kernel<uint32_t><<<grid, kThreads, 0, stream>>>(
+                        static_cast<uint32_t*>(dst), static_cast<const uint32_t*>(src), n, d); break;
+            default: copy_same_kernel<unsigned long long><<<grid, kThreads, 0, stream>>>(
+                        static_cast<unsigned long long*>(dst),
+                        static_cast<const unsigned long long*>(src), n, d); break;
+        }
+        return launch_status("copy_strided");
+    }
+    copy_convert_kernel<<<grid, kThreads, 0, stream>>>(dst, dst_type, src, src_type, n, d);
+    return launch_status("copy_convert");
+}
+
+int tk_fill_strided(void* dst, int type, double value, int64_t ivalue, int ndim,
+                    const int64_t* sizes, const int64_t* strides, void* stream_) {
+    using namespace tk;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    Strided d;
+    int64_t n = 0;
+    int rc = fill_strided_desc(d, ndim, sizes, strides, nullptr, n);
+    if (rc) return rc;
+    if (n == 0) return TK_OK;
+    TK_CHECK_ARG(dst != nullptr, "tk_fill_strided: NULL pointer");
+    const bool dense = is_dense(ndim, sizes, strides);
+    const int grid = grid_for(n);
+    auto launch = [&](auto v) {
+        using E = decltype(v);
+        if (dense)
+            fill_dense_kernel<E><<<grid, kThreads, 0, stream>>>(static_cast<E*>(dst), v, n);
+        else
+            fill_kernel<E><<<grid, kThreads, 0, stream>>>(static_cast<E*>(dst), v, n, d);
+    };
+    switch (type) {
+        case T_BOOL: launch(static_cast<uint8_t>(ivalue != 0)); break;
+        case T_U8: launch(static_cast<uint8_t>(ivalue)); break;
+        case T_I8: launch(static_cast<int8_t>(ivalue)); break;
+        case T_I16: launch(static_cast<int16_t>(ivalue)); break;
+        case T_I32: launch(static_cast<int32_t>(ivalue)); break;
+        case T_I64: launch(static_cast<long long>(ivalue)); break;
+        case T_F16: { __half h = __float2half_rn(static_cast<float>(value));
+                      launch(*reinterpret_cast<uint16_t*>(&h)); break; }
+        case T_BF16: { __nv_bfloat16 h = __float2bfloat16_rn(static_cast<float>(value));
+                       launch(*reinterpret_cast<uint16_t*>(&h)); break; }
+        case T_F32: launch(static_cast<float>(value)); break;
+        case T_F64: launch(value); break;
+        default: TK_FAIL(TK_ERR_INVALID_ARG, "tk_fill_strided: bad scalar type %d", type);
+    }
+    return launch_status("fill");
+}
+
+int tk_binary(int op, tk_dtype_t dt, const void* a, const int64_t* a_strides, const void* b,
+              const int64_t* b_strides, void* out, int ndim, const int64_t* sizes, float alpha,
+              void* stream_) {
+    using namespace tk;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    TK_CHECK_ARG(op >= TK_BIN_ADD && op <= TK_BIN_DIV, "tk_binary: bad op %d", op);
+    TK_CHECK_ARG(dt == TK_DTYPE_F16 || dt == TK_DTYPE_F32, "tk_binary: bad dtype");
+    Strided d;
+    int64_t n = 0;
+    int rc = fill_strided_desc(d, ndim, sizes, a_strides, b_strides, n);
+    if (rc) return rc;
+    if (n == 0) return TK_OK;
+    TK_CHECK_ARG(a && b && out, "tk_binary: NULL pointer");
+    const bool dense = is_dense(ndim, sizes, a_strides) && is_dense(ndim, sizes, b_strides);
+    const int grid = grid_for(n);
+    if (dt == TK_DTYPE_F16) {
+        if (dense)
+            binary_dense_kernel<__half><<<grid, kThreads, 0, stream>>>(
+                op, static_cast<const __half*>(a), static_cast<const __half*>(b),
+                static_cast<__half*>(out), n, alpha);
+        else
+            binary_kernel<__half><<<grid, kThreads, 0, stream>>>(
+                op, static_cast<const __half*>(a), static_cast<const __half*>(b),
+                static_cast<__half*>(out), n, alpha, d);
+    } else {
+        if (dense)
+            binary_dense_kernel<float><<<grid, kThreads, 0, stream>>>(
+                op, static_cast<const float*>(a), static_cast<const float*>(b),
+                static_cast<float*>(out), n, alpha);
+        else
+            binary_kernel<float><<<grid, kThreads, 0, stream>>>(
+                op, static_cast<const float*>(a), static_cast<const float*>(b),
+                static_cast<float*>(out), n, alpha, d);
+    }
+    return launch_status("binary");
+}
+
+int tk_unary(int op, tk_dtype_t dt, const void* x, void* y, int64_t n, float p0, float p1,
+             void* stream_) {
+    using namespace tk;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    TK_CHECK_ARG(op >= TK_UN_RELU && op <= TK_UN_SCALE, "tk_unary: bad op %d", op);
+    TK_CHECK_ARG(n >= 0, "tk_unary: negative size");
+    if (n == 0) return TK_OK;
+    TK_CHECK_ARG(x && y, "tk_unary: NULL pointer");
+    const int grid = grid_for(n);
+    if (dt == TK_DTYPE_F16)
+        unary_kernel<__half><<<grid, kThreads, 0, stream>>>(op, static_cast<const __half*>(x),
+                                                             static_cast<__half*>(y), n, p0, p1);
+    else
+        unary_kernel<float><<<grid, kThreads, 0, stream>>>(op, static_cast<const float*>(x),
+                                                            static_cast<float*>(y), n, p0, p1);
+    return launch_status("unary");
+}
+
+int tk_silu_mul(tk_dtype_t dt, const void* gate, const void* up, void* y, int64_t n, void* stream_) {
+    using namespace tk;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    TK_CHECK_ARG(n >= 0, "tk_silu_mul: negative size");
+    if (n == 0) return TK_OK;
+    TK_CHECK_ARG(gate && up && y, "tk_silu_mul: NULL pointer");
+    const int grid = grid_for(n);
+    if (dt == TK_DTYPE_F16)
+        silu_mul_kernel<__half><<<grid, kThreads, 0, stream>>>(
+            static_cast<const __half*>(gate), static_cast<const __half*>(up),
+            static_cast<__half*>(y), n);
+    else
+        silu_mul_kernel<float><<<grid, kThreads, 0, stream>>>(
+            static_cast<const float*>(gate), static_cast<const float*>(up),
+            static_cast<float*>(y), n);
+    return launch_status("silu_mul");
+}
+
+}  // extern "C"

@@ -1,0 +1,647 @@
+// qgemm.cu -- int16-quantised GEMM on sm_100a tensor cores.
+//
+// Replaces baidu::xpu::api::fc<T,T,T,TGEMM> (called from csrc/ops.cpp:224 for
+// mm/linear and per batch slice from csrc/ops_nn.cpp:214 for bmm) together
+// with the bias/scale/add launches that follow it in the reference.
+//
+// Numerics: each int16 operand q is stored as two int8 limb planes,
+// q = 256*hi + lo with hi signed in [-128,127] and lo unsigned in [0,255].
+// Four tcgen05 kind::i8 MMAs per K-step produce three int32 TMEM accumulators
+//   HH = sum hi_a*hi_b,  MID = sum hi_a*lo_b + lo_a*hi_b,  LL = sum lo_a*lo_b
+// which are exact for K <= 32768 (|MID| <= K*65280 < 2^31).  The epilogue
+// rebuilds acc = 65536*HH + 256*MID + LL exactly in binary64 (every partial
+// result is an integer below 2^53), multiplies by the dequant scale
+// amax_a*amax_b/32767^2 and rounds once to fp16/fp32, then applies the
+// reference's post-GEMM ops in its order (alpha, bias, beta*addend, act).
+//
+// Kernel structure (one persistent CTA per SM, 192 threads):
+//   warp 0      TMA producer: 4 boxes per stage (A hi/lo, B hi/lo), 128 rows
+//               x 128 bytes each, 128-byte swizzle, 3-stage ring;
+//   warp 1      TMEM owner + MMA issuer (one thread), 16 MMAs per stage;
+//   warps 2..5  epilogue: tcgen05.ld of the 3 x 128 accumulator columns of
+//               its 32 TMEM lanes, binary64 recombine, dequant, fused ops,
+//               vector stores.
+// TMEM holds the three 128x128 accumulators in 384 of 512 columns; the MMA
+// warp waits for the epilogue to drain them before the next tile.
+// No TMA multicast is used anywhere.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "tk_internal.h"
+#include "tk_ptx.cuh"
+
+namespace tk {
+
+int amax_launch(tk_dtype_t dtype, const void* x, int64_t nslices, int64_t slice_stride,
+                int64_t slice_len, float* amax_out, cudaStream_t stream);
+int quantize_limbs_launch(tk_dtype_t dtype, const void* x, int64_t batch, int64_t rows,
+                          int64_t cols, int64_t sb, int64_t sr, int64_t sc, const float* amax,
+                          int64_t amax_stride, int8_t* limbs, cudaStream_t stream);
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int BK = 128;  // bytes (int8 elements) per stage along K
+constexpr int UMMA_K = 32;
+constexpr int STAGES = 3;
+constexpr int TILE_BYTES = BM * BK;            // one limb plane of one operand
+constexpr int STAGE_BYTES = 4 * TILE_BYTES;    // A hi, A lo, B hi, B lo
+constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int ACC_HH = 0;
+constexpr int ACC_MID = BN;
+constexpr int ACC_LL = 2 * BN;
+constexpr int kMaxK = 32768;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+
+constexpr uint32_t IDESC_SS = idesc_i8(BM, BN, true, true);
+constexpr uint32_t IDESC_SU = idesc_i8(BM, BN, true, false);
+constexpr uint32_t IDESC_US = idesc_i8(BM, BN, false, true);
+constexpr uint32_t IDESC_UU = idesc_i8(BM, BN, false, false);
+
+struct EpiParams {
+    int dtype;  // 0 fp16, 1 fp32
+    int64_t M, N;
+    void* out;
+    int64_t out_sb, out_sm;
+    const void* bias;
+    const void* addend;
+    int64_t add_sb, add_sm, add_sn;
+    float alpha, beta;
+    int act;
+    const float* amax_a;
+    const float* amax_b;
+    int64_t scale_stride;  // 1: per-slice amax; 0: one amax for all slices
+    bool vec_store;
+    int32_t* dbg;  // [3][M][N] raw accumulators of slice 0, or null
+};
+
+struct TileParams {
+    int batch, tiles_m, tiles_n, num_tiles, num_kb;
+    unsigned* err;
+};
+
+// ---- shared numerics (device) -----------------------------------------------
+
+// binary64 -> binary16, nearest-even.  Uses the round-to-odd intermediate of
+// Boldo & Melquiond ("When double rounding is odd", 2005): rounding to
+// binary32 toward zero and setting the last bit when inexact, then rounding
+// to binary16 to nearest, equals a single correct rounding because binary32
+// carries at least two more significand bits than binary16.
+__device__ __forceinline__ float d2f_round_odd(double d) {
+    float f = __double2float_rz(d);
+    if (static_cast<double>(f) != d) f = __uint_as_float(__float_as_uint(f) | 1u);
+    return f;
+}
+
+__device__ __forceinline__ float round_t_from_double(double d, int dtype) {
+    if (dtype == 0) return __half2float(__float2half_rn(d2f_round_odd(d)));
+    return __double2float_rn(d);
+}
+
+__device__ __forceinline__ float round_t(float v, int dtype) {
+    return dtype == 0 ? __half2float(__float2half_rn(v)) : v;
+}
+
+__device__ __forceinline__ float load_t(const void* p, int dtype, int64_t i) {
+    return dtype == 0 ? __half2float(static_cast<const __half*>(p)[i])
+                      : static_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ float gelu_erf(float x) {
+    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+    const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+    return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+}
+
+__device__ __forceinline__ float apply_act(float r, int act, int dtype) {
+    switch (act) {
+        case TK_ACT_RELU:
+            return (r > 0.0f || r != r) ? r : 0.0f;
+        case TK_ACT_GELU:
+            return round_t(gelu_erf(r), dtype);
+        case TK_ACT_GELU_TANH:
+            return round_t(gelu_tanh(r), dtype);
+        case TK_ACT_SILU:
+            return round_t(r / (1.0f + expf(-r)), dtype);
+        default:
+            return r;
+    }
+}
+
+__device__ __forceinline__ double dequant_scale(const EpiParams& p, int64_t b) {
+    const float aa = p.amax_a[b * p.scale_stride];
+    const float ab = p.amax_b[b * p.scale_stride];
+    return __ddiv_rn(__dmul_rn(static_cast<double>(aa), static_cast<double>(ab)), 1073676289.0);
+}
+
+// The reference's post-GEMM sequence on one element (see file header).
+__device__ __forceinline__ float epilogue_one(const EpiParams& p, double s, double acc, int64_t b,
+                                              int64_t m, int64_t n) {
+    float r = round_t_from_double(__dmul_rn(acc, s), p.dtype);
+    if (p.alpha != 1.0f) r = round_t(__fmul_rn(r, p.alpha), p.dtype);
+    if (p.bias != nullptr) r = round_t(__fadd_rn(r, load_t(p.bias, p.dtype, n)), p.dtype);
+    if (p.addend != nullptr && p.beta != 0.0f) {
+        float a = load_t(p.addend, p.dtype, b * p.add_sb + m * p.add_sm + n * p.add_sn);
+        if (p.beta != 1.0f) a = round_t(__fmul_rn(a, p.beta), p.dtype);
+        r = round_t(__fadd_rn(r, a), p.dtype);
+    }
+    return apply_act(r, p.act, p.dtype);
+}
+
+__device__ __forceinline__ void store_one(const EpiParams& p, int64_t off, float v) {
+    if (p.dtype == 0)
+        static_cast<__half*>(p.out)[off] = __float2half_rn(v);
+    else
+        static_cast<float*>(p.out)[off] = v;
+}
+
+__device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b, int& mt, int& nt) {
+    const int per_batch = tp.tiles_m * tp.tiles_n;
+    b = t / per_batch;
+    const int id = t - b * per_batch;
+    constexpr int GROUP = 8;  // M-tiles per raster group (keeps B tiles hot in L2)
+    const int width = GROUP * tp.tiles_n;
+    const int g = id / width;
+    const int first_m = g * GROUP;
+    const int gsize = min(tp.tiles_m - first_m, GROUP);
+    const int r = id - g * width;
+    mt = first_m + r % gsize;
+    nt = r / gsize;
+}
+
+// ---- tensor-core kernel --------------------------------------------------------
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const TileParams tp, const EpiParams ep) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* full_bar = bars;                 // [STAGES] TMA -> MMA
+    uint64_t* empty_bar = bars + STAGES;       // [STAGES] MMA -> TMA
+    uint64_t* acc_full = bars + 2 * STAGES;    // MMA -> epilogue
+    uint64_t* acc_empty = acc_full + 1;        // epilogue -> MMA (4 arrivals)
+    uint64_t* drain_bar = acc_full + 2;        // MMA teardown
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 3);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(full_bar + s), 1);
+            mbar_init(smem_u32(empty_bar + s), 1);
+        }
+        mbar_init(smem_u32(acc_full), 1);
+        mbar_init(smem_u32(acc_empty), 4);
+        mbar_init(smem_u32(drain_bar), 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t last_phase[STAGES];
+        bool used[STAGES];
+        for (int s = 0; s < STAGES; ++s) { used[s] = false; last_phase[s] = 0; }
+        bool ok = true;
+        for (int t = blockIdx.x; t < tp.num_tiles && ok; t += gridDim.x) {
+            int b, mt, nt;
+            decode_tile(tp, t, b, mt, nt);
+            for (int kb = 0; kb < tp.num_kb; ++kb) {
+                if (!mbar_wait_bounded(smem_u32(empty_bar + stage), phase ^ 1u, abort_flag,
+                                       tp.err, kDevErrWaitEmpty)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t fb = smem_u32(full_bar + stage);
+                    mbar_arrive_expect_tx(fb, STAGE_BYTES);
+                    uint8_t* sbase = smem + stage * STAGE_BYTES;
+                    const int kx = kb * BK;
+                    tma_load_3d(smem_u32(sbase + 0 * TILE_BYTES), &tmA, fb, kx, mt * BM, 2 * b + 0);
+                    tma_load_3d(smem_u32(sbase + 1 * TILE_BYTES), &tmA, fb, kx, mt * BM, 2 * b + 1);
+                    tma_load_3d(smem_u32(sbase + 2 * TILE_BYTES), &tmB, fb, kx, nt * BN, 2 * b + 0);
+                    tma_load_3d(smem_u32(sbase + 3 * TILE_BYTES), &tmB, fb, kx, nt * BN, 2 * b + 1);
+                }
+                __syncwarp();
+                used[stage] = true;
+                last_phase[stage] = phase;
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+        }
+        // Drain: every box this warp issued must have landed before exit.
+        for (int s = 0; s < STAGES; ++s) {
+            if (used[s]) {
+                volatile int no_abort = 0;
+                mbar_wait_bounded(smem_u32(full_bar + s), last_phase[s], &no_abort, tp.err,
+                                  kDevErrWaitDrain);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t acc_phase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tp.num_tiles && ok; t += gridDim.x) {
+            if (!mbar_wait_bounded(smem_u32(acc_empty), acc_phase ^ 1u, abort_flag, tp.err,
+                                   kDevErrWaitAccEmpty)) {
+                break;
+            }
+            tc_fence_after();
+            for (int kb = 0; kb < tp.num_kb; ++kb) {
+                if (!mbar_wait_bounded(smem_u32(full_bar + stage), phase, abort_flag, tp.err,
+                                       kDevErrWaitFull)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t sb = smem_u32(smem + stage * STAGE_BYTES);
+                    const uint64_t a_hi = smem_desc_kmajor_sw128(sb + 0 * TILE_BYTES);
+                    const uint64_t a_lo = smem_desc_kmajor_sw128(sb + 1 * TILE_BYTES);
+                    const uint64_t b_hi = smem_desc_kmajor_sw128(sb + 2 * TILE_BYTES);
+                    const uint64_t b_lo = smem_desc_kmajor_sw128(sb + 3 * TILE_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+                        // K advance inside the 128-byte swizzle row: start address
+                        // moves by kk*32 bytes (encoded >> 4).
+                        const uint64_t off = static_cast<uint64_t>((kk * UMMA_K) >> 4);
+                        const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+                        tc_mma_i8(tmem_base + ACC_HH, a_hi + off, b_hi + off, IDESC_SS, acc);
+                        tc_mma_i8(tmem_base + ACC_MID, a_hi + off, b_lo + off, IDESC_SU, acc);
+                        tc_mma_i8(tmem_base + ACC_MID, a_lo + off, b_hi + off, IDESC_US, 1u);
+                        tc_mma_i8(tmem_base + ACC_LL, a_lo + off, b_lo + off, IDESC_UU, acc);
+                    }
+                    tc_commit(smem_u32(empty_bar + stage));
+                }
+                __syncwarp();
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+            if (!ok) break;
+            if (lane == 0) tc_commit(smem_u32(acc_full));
+            __syncwarp();
+            acc_phase ^= 1u;
+        }
+        // Drain: all MMAs issued by this thread complete before TMEM is freed.
+        if (lane == 0) tc_commit(smem_u32(drain_bar));
+        __syncwarp();
+        volatile int no_abort = 0;
+        mbar_wait_bounded(smem_u32(drain_bar), 0, &no_abort, tp.err, kDevErrWaitDrain);
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+        const int row = quarter * 32 + lane;
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        uint32_t acc_phase = 0;
+        for (int t = blockIdx.x; t < tp.num_tiles; t += gridDim.x) {
+            int b, mt, nt;
+            decode_tile(tp, t, b, mt, nt);
+            if (!mbar_wait_bounded(smem_u32(acc_full), acc_phase, abort_flag, tp.err,
+                                   kDevErrWaitAccFull)) {
+                break;
+            }
+            tc_fence_after();
+            const int64_t m = static_cast<int64_t>(mt) * BM + row;
+            const double s = dequant_scale(ep, b);
+            const bool row_ok = m < ep.M;
+            const int64_t out_row = b * ep.out_sb + m * ep.out_sm;
+#pragma unroll 1
+            for (int c = 0; c < BN / 16; ++c) {
+                uint32_t hh[16], mid[16], ll[16];
+                tmem_ld_32x32b_x16(t_row + ACC_HH + c * 16, hh);
+                tmem_ld_32x32b_x16(t_row + ACC_MID + c * 16, mid);
+                tmem_ld_32x32b_x16(t_row + ACC_LL + c * 16, ll);
+                tc_wait_ld();
+                const int64_t n0 = static_cast<int64_t>(nt) * BN + c * 16;
+                if (!row_ok || n0 >= ep.N) continue;
+                float v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const double acc = __fma_rn(
+                        static_cast<double>(static_cast<int32_t>(hh[j])), 65536.0,
+                        __fma_rn(static_cast<double>(static_cast<int32_t>(mid[j])), 256.0,
+                                 static_cast<double>(static_cast<int32_t>(ll[j]))));
+                    v[j] = epilogue_one(ep, s, acc, b, m, n0 + j);
+                }
+                if (ep.dbg != nullptr && b == 0) {
+                    for (int j = 0; j < 16 && n0 + j < ep.N; ++j) {
+                        ep.dbg[(0 * ep.M + m) * ep.N + n0 + j] = static_cast<int32_t>(hh[j]);
+                        ep.dbg[(1 * ep.M + m) * ep.N + n0 + j] = static_cast<int32_t>(mid[j]);
+                        ep.dbg[(2 * ep.M + m) * ep.N + n0 + j] = static_cast<int32_t>(ll[j]);
+                    }
+                }
+                if (ep.vec_store && n0 + 16 <= ep.N) {
+                    if (ep.dtype == 0) {
+                        uint32_t w[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            __half2 h2 = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+                            w[j] = *reinterpret_cast<uint32_t*>(&h2);
+                        }
+                        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(ep.out) + out_row + n0);
+                        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                    } else {
+                        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(ep.out) + out_row + n0);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    }
+                } else {
+                    for (int j = 0; j < 16 && n0 + j < ep.N; ++j) store_one(ep, out_row + n0 + j, v[j]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(acc_empty));
+            acc_phase ^= 1u;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ---- CUDA-core cross-check kernel ------------------------------------------------
+
+__global__ void qgemm_simt_kernel(const int8_t* __restrict__ la, const int8_t* __restrict__ lb,
+                                  int64_t batch, int64_t K, int64_t ld, EpiParams ep) {
+    const int64_t n = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t m = blockIdx.y;
+    const int64_t b = blockIdx.z;
+    if (n >= ep.N) return;
+    const int64_t pa = ep.M * ld, pb = ep.N * ld;
+    const int8_t* ahi = la + (2 * b) * pa + m * ld;
+    const int8_t* alo = ahi + pa;
+    const int8_t* bhi = lb + (2 * b) * pb + n * ld;
+    const int8_t* blo = bhi + pb;
+    int64_t acc = 0;
+    for (int64_t k = 0; k < K; ++k) {
+        const int64_t qa = 256 * static_cast<int64_t>(ahi[k]) +
+                           static_cast<int64_t>(static_cast<uint8_t>(alo[k]));
+        const int64_t qb = 256 * static_cast<int64_t>(bhi[k]) +
+                           static_cast<int64_t>(static_cast<uint8_t>(blo[k]));
+        acc += qa * qb;
+    }
+    const double s = dequant_scale(ep, b);
+    const float v = epilogue_one(ep, s, static_cast<double>(acc), b, m, n);
+    store_one(ep, b * ep.out_sb + m * ep.out_sm + n, v);
+}
+
+// ---- host side --------------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        }
+    });
+    return fn;
+}
+
+// Tensor map over limb planes [planes][rows][ld] (uint8), box 128 x 128 x 1.
+int make_limb_map(CUtensorMap* map, const int8_t* base, int64_t planes, int64_t rows, int64_t ld) {
+    EncodeTiledFn enc = get_encode_fn();
+    if (enc == nullptr) TK_FAIL(TK_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(ld), static_cast<cuuint64_t>(rows),
+                          static_cast<cuuint64_t>(planes)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld), static_cast<cuuint64_t>(rows * ld)};
+    cuuint32_t box[3] = {BK, BM, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(base), dims,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) TK_FAIL(TK_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return TK_OK;
+}
+
+struct Layout {
+    int64_t ld;        // padded K (bytes per limb row)
+    size_t off_amax_a, off_amax_b, off_la, off_lb, total;
+};
+
+Layout workspace_layout(const tk_qgemm_desc_t& d) {
+    Layout L;
+    L.ld = static_cast<int64_t>(round_up(static_cast<size_t>(std::max<int64_t>(d.k, 1)), 16));
+    const int64_t nscale = d.per_slice_scales ? d.batch : 1;
+    L.off_amax_a = 0;
+    L.off_amax_b = round_up(sizeof(float) * nscale, 256);
+    L.off_la = round_up(L.off_amax_b + sizeof(float) * nscale, 1024);
+    L.off_lb = round_up(L.off_la + static_cast<size_t>(d.batch * 2 * d.m * L.ld), 1024);
+    L.total = round_up(L.off_lb + static_cast<size_t>(d.batch * 2 * d.n * L.ld), 1024);
+    return L;
+}
+
+int validate(const tk_qgemm_desc_t& d) {
+    TK_CHECK_ARG(d.dtype == TK_DTYPE_F16 || d.dtype == TK_DTYPE_F32, "qgemm: bad dtype %d",
+                 (int)d.dtype);
+    TK_CHECK_ARG(d.batch >= 0 && d.m >= 0 && d.n >= 0 && d.k >= 0, "qgemm: negative size");
+    TK_CHECK_ARG(d.k <= kMaxK, "qgemm: K=%lld exceeds %d (int32 limb accumulators)",
+                 (long long)d.k, kMaxK);
+    TK_CHECK_ARG(d.batch <= 65535 && d.m < (1LL << 31) && d.n < (1LL << 31),
+                 "qgemm: size out of range");
+    TK_CHECK_ARG(d.act >= TK_ACT_NONE && d.act <= TK_ACT_SILU, "qgemm: bad act %d", (int)d.act);
+    if (d.batch * d.m * d.n > 0) TK_CHECK_ARG(d.out != nullptr, "qgemm: out is NULL");
+    return TK_OK;
+}
+
+bool slice_dense(int64_t rows, int64_t cols, int64_t sr, int64_t sc) {
+    if (rows <= 1 || cols <= 1) return true;
+    return (sr == cols && sc == 1) || (sr == 1 && sc == rows);
+}
+
+// Quantise one operand ([batch][rows][cols] strided view) into limb planes.
+int quantise_operand(tk_dtype_t dt, const void* x, int64_t batch, int64_t rows, int64_t cols,
+                     int64_t sb, int64_t sr, int64_t sc, bool per_slice, const float* given_amax,
+                     float* amax_ws, int8_t* limbs, cudaStream_t stream, const char* name) {
+    const float* amax = given_amax;
+    if (amax == nullptr) {
+        if (rows * cols > 0) {
+            if (!slice_dense(rows, cols, sr, sc))
+                TK_FAIL(TK_ERR_UNSUPPORTED,
+                        "qgemm: operand %s slices must be dense (row- or column-major)", name);
+            if (per_slice) {
+                int rc = amax_launch(dt, x, batch, sb, rows * cols, amax_ws, stream);
+                if (rc) return rc;
+            } else {
+                if (batch > 1 && sb != rows * cols)
+                    TK_FAIL(TK_ERR_UNSUPPORTED,
+                            "qgemm: operand %s must be one dense block for a shared scale", name);
+                int rc = amax_launch(dt, x, 1, 0, batch * rows * cols, amax_ws, stream);
+                if (rc) return rc;
+            }
+        } else {
+            TK_CUDA_TRY(cudaMemsetAsync(amax_ws, 0, sizeof(float) * (per_slice ? batch : 1), stream));
+        }
+        amax = amax_ws;
+    }
+    return quantize_limbs_launch(dt, x, batch, rows, cols, sb, sr, sc, amax, per_slice ? 1 : 0,
+                                 limbs, stream);
+}
+
+EpiParams make_epi(const tk_qgemm_desc_t& d, const float* amax_a, const float* amax_b,
+                   int32_t* dbg) {
+    EpiParams ep;
+    ep.dtype = d.dtype == TK_DTYPE_F16 ? 0 : 1;
+    ep.M = d.m;
+    ep.N = d.n;
+    ep.out = d.out;
+    ep.out_sb = d.out_sb;
+    ep.out_sm = d.out_sm;
+    ep.bias = d.bias;
+    ep.addend = d.addend;
+    ep.add_sb = d.add_sb;
+    ep.add_sm = d.add_sm;
+    ep.add_sn = d.add_sn;
+    ep.alpha = d.alpha;
+    ep.beta = d.beta;
+    ep.act = d.act;
+    ep.amax_a = amax_a;
+    ep.amax_b = amax_b;
+    ep.scale_stride = d.per_slice_scales ? 1 : 0;
+    const size_t es = dtype_size(d.dtype);
+    ep.vec_store = (reinterpret_cast<uintptr_t>(d.out) % 16 == 0) &&
+                   ((d.out_sm * static_cast<int64_t>(es)) % 16 == 0) &&
+                   (d.batch <= 1 || (d.out_sb * static_cast<int64_t>(es)) % 16 == 0);
+    ep.dbg = dbg;
+    return ep;
+}
+
+enum class Path { TensorCore, Simt };
+
+int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t stream, Path path,
+        int32_t* dbg) {
+    TK_CHECK_ARG(desc != nullptr, "qgemm: desc is NULL");
+    const tk_qgemm_desc_t& d = *desc;
+    int rc = validate(d);
+    if (rc) return rc;
+    if (d.batch == 0 || d.m == 0 || d.n == 0) return TK_OK;
+    const Layout L = workspace_layout(d);
+    TK_CHECK_ARG(ws != nullptr && ws_bytes >= L.total,
+                 "qgemm: workspace too small (%zu < %zu bytes)", ws_bytes, L.total);
+    TK_CHECK_ARG(reinterpret_cast<uintptr_t>(ws) % 1024 == 0,
+                 "qgemm: workspace must be 1024-byte aligned");
+    uint8_t* w = static_cast<uint8_t*>(ws);
+    float* amax_a = reinterpret_cast<float*>(w + L.off_amax_a);
+    float* amax_b = reinterpret_cast<float*>(w + L.off_amax_b);
+    int8_t* la = reinterpret_cast<int8_t*>(w + L.off_la);
+    int8_t* lb = reinterpret_cast<int8_t*>(w + L.off_lb);
+    const bool per = d.per_slice_scales != 0;
+    if (d.k > 0) {
+        rc = quantise_operand(d.dtype, d.a, d.batch, d.m, d.k, d.a_sb, d.a_sm, d.a_sk, per,
+                              d.amax_a, amax_a, la, stream, "A");
+        if (rc) return rc;
+        rc = quantise_operand(d.dtype, d.b, d.batch, d.n, d.k, d.b_sb, d.b_sn, d.b_sk, per,
+                              d.amax_b, amax_b, lb, stream, "B");
+        if (rc) return rc;
+    } else {
+        TK_CUDA_TRY(cudaMemsetAsync(amax_a, 0, L.off_la, stream));
+    }
+    const float* sa = (d.k > 0 && d.amax_a) ? d.amax_a : amax_a;
+    const float* sb = (d.k > 0 && d.amax_b) ? d.amax_b : amax_b;
+    EpiParams ep = make_epi(d, sa, sb, dbg);
+
+    if (path == Path::Simt || d.k == 0) {
+        dim3 grid(static_cast<unsigned>(ceil_div(d.n, 128)), static_cast<unsigned>(d.m),
+                  static_cast<unsigned>(d.batch));
+        TK_CHECK_ARG(d.m <= 65535 || path == Path::TensorCore,
+                     "qgemm_simt: m must be <= 65535");
+        if (d.m > 65535) TK_FAIL(TK_ERR_UNSUPPORTED, "qgemm: K=0 with m > 65535");
+        qgemm_simt_kernel<<<grid, 128, 0, stream>>>(la, lb, d.batch, d.k, L.ld, ep);
+        return launch_status("qgemm_simt");
+    }
+
+    CUtensorMap tmA, tmB;
+    rc = make_limb_map(&tmA, la, 2 * d.batch, d.m, L.ld);
+    if (rc) return rc;
+    rc = make_limb_map(&tmB, lb, 2 * d.batch, d.n, L.ld);
+    if (rc) return rc;
+    TileParams tp;
+    tp.batch = static_cast<int>(d.batch);
+    tp.tiles_m = static_cast<int>(ceil_div(d.m, BM));
+    tp.tiles_n = static_cast<int>(ceil_div(d.n, BN));
+    const int64_t nt = static_cast<int64_t>(tp.tiles_m) * tp.tiles_n * d.batch;
+    TK_CHECK_ARG(nt < (1LL << 31), "qgemm: too many tiles");
+    tp.num_tiles = static_cast<int>(nt);
+    tp.num_kb = static_cast<int>(ceil_div(d.k, BK));
+    const int dev = current_device();
+    tp.err = device_error_word(dev);
+    static std::once_flag attr_once[64];
+    if (dev >= 0 && dev < 64) {
+        std::call_once(attr_once[dev], [] {
+            cudaFuncSetAttribute(qgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 SMEM_BYTES);
+        });
+    }
+    const int grid = static_cast<int>(std::min<int64_t>(nt, sm_count(dev)));
+    qgemm_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tmA, tmB, tp, ep);
+    return launch_status("qgemm_tc");
+}
+
+}  // namespace
+}  // namespace tk
+
+extern "C" {
+
+size_t tk_qgemm_workspace_size(const tk_qgemm_desc_t* desc) {
+    if (desc == nullptr) return 0;
+    return tk::workspace_layout(*desc).total;
+}
+
+int tk_qgemm(const tk_qgemm_desc_t* desc, void* workspace, size_t workspace_bytes, void* stream) {
+    return tk::run(desc, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                   tk::Path::TensorCore, nullptr);
+}
+
+int tk_qgemm_simt(const tk_qgemm_desc_t* desc, void* workspace, size_t workspace_bytes,
+                  void* stream) {
+    return tk::run(desc, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                   tk::Path::Simt, nullptr);
+}
+
+int tk_qgemm_debug(const tk_qgemm_desc_t* desc, void* workspace, size_t workspace_bytes,
+                   int32_t* acc3, void* stream) {
+    return tk::run(desc, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                   tk::Path::TensorCore, acc3);
+}
+
+}  // extern "C"

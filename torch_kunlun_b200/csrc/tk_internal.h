@@ -1,0 +1,57 @@
+// tk_internal.h -- shared host-side helpers of libtk_kernels.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/tk_kernels.h"
+
+namespace tk {
+
+// Thread-local last-error message; set by fail() and returned by
+// tk_last_error_string().
+void set_error(const char* fmt, ...);
+
+inline int fail_status(int status) { return status; }
+
+#define TK_FAIL(status, ...)          \
+    do {                              \
+        ::tk::set_error(__VA_ARGS__); \
+        return (status);              \
+    } while (0)
+
+#define TK_CHECK_ARG(cond, ...)                                  \
+    do {                                                         \
+        if (!(cond)) TK_FAIL(TK_ERR_INVALID_ARG, __VA_ARGS__);   \
+    } while (0)
+
+#define TK_CUDA_TRY(expr)                                                              \
+    do {                                                                               \
+        cudaError_t _e = (expr);                                                       \
+        if (_e != cudaSuccess)                                                         \
+            TK_FAIL(TK_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(_e));      \
+    } while (0)
+
+// Status of the most recent kernel launch on this thread.
+inline int launch_status(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) TK_FAIL(TK_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+    return TK_OK;
+}
+
+int current_device();
+int sm_count(int device);
+// Device address of the per-device error word that bounded waits write.
+unsigned* device_error_word(int device);
+
+inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+inline size_t dtype_size(tk_dtype_t dt) { return dt == TK_DTYPE_F16 ? 2 : 4; }
+
+}  // namespace tk
