@@ -133,6 +133,17 @@ TK_API size_t tk_qgemm_workspace_size(const tk_qgemm_desc_t* desc);
 TK_API int tk_qgemm(const tk_qgemm_desc_t* desc, void* workspace, size_t workspace_bytes,
              void* stream);
 
+/* The GEMM and epilogue alone, on operands already quantised by
+ * tk_quantize_limbs (layout [batch][2][rows][round_up(k,16)]) with the amax
+ * values they were quantised with (one per slice when per_slice_scales, else
+ * one per operand).  desc->a and desc->b are ignored.  Lets a caller keep the
+ * quantised form of an operand that does not change between calls (weights)
+ * -- XDNN's fc accepts precomputed max pointers for the same purpose
+ * (csrc/ops.cpp:227 passes them as null). */
+TK_API int tk_qgemm_from_limbs(const tk_qgemm_desc_t* desc, const int8_t* a_limbs,
+                               const int8_t* b_limbs, const float* amax_a, const float* amax_b,
+                               void* stream);
+
 /* Same contract computed by a plain CUDA-core kernel (one output per thread).
  * Used to cross-check the tensor-core path on the device; not fast. */
 TK_API int tk_qgemm_simt(const tk_qgemm_desc_t* desc, void* workspace, size_t workspace_bytes,
@@ -143,6 +154,52 @@ TK_API int tk_qgemm_simt(const tk_qgemm_desc_t* desc, void* workspace, size_t wo
  * ([3][m][n], int32) in addition to out. */
 TK_API int tk_qgemm_debug(const tk_qgemm_desc_t* desc, void* workspace, size_t workspace_bytes,
                    int32_t* acc3, void* stream);
+
+/* ---- data movement and elementwise ops -----------------------------------
+ * Scalar type codes of tk_copy_strided / tk_fill_strided. */
+typedef enum {
+    TK_T_BOOL = 0, TK_T_U8 = 1, TK_T_I8 = 2, TK_T_I16 = 3, TK_T_I32 = 4, TK_T_I64 = 5,
+    TK_T_F16 = 6, TK_T_BF16 = 7, TK_T_F32 = 8, TK_T_F64 = 9
+} tk_scalar_t;
+
+/* dst[i] = convert(src[i]) over an ndim <= 8 strided index space.  Replaces
+ * the host-staged copy_ / materialize_private_contiguous of the reference
+ * (csrc/ops.cpp:289-418), which copies non-contiguous views through CPU
+ * memory; conversion is by value (float -> int truncates). */
+TK_API int tk_copy_strided(void* dst, int dst_type, const void* src, int src_type, int ndim,
+                           const int64_t* sizes, const int64_t* dst_strides,
+                           const int64_t* src_strides, void* stream);
+
+/* Fill a strided view with one value (float types use `value`, integer types
+ * `ivalue`).  Replaces xdnn::constant and the host-pattern fill of
+ * csrc/ops.cpp:162-208. */
+TK_API int tk_fill_strided(void* dst, int type, double value, int64_t ivalue, int ndim,
+                           const int64_t* sizes, const int64_t* strides, void* stream);
+
+typedef enum { TK_BIN_ADD = 0, TK_BIN_SUB = 1, TK_BIN_MUL = 2, TK_BIN_DIV = 3 } tk_binop_t;
+
+/* out[i] = a[i] op (alpha * b[i]) (alpha applies to add/sub) computed in fp32
+ * and rounded once, over a broadcast index space (strides 0 broadcast); out
+ * is contiguous.  Replaces xdnn add/broadcast_add/sub/mul
+ * (csrc/ops.cpp:117-149, csrc/autograd.cpp:40-100). */
+TK_API int tk_binary(int op, tk_dtype_t dtype, const void* a, const int64_t* a_strides,
+                     const void* b, const int64_t* b_strides, void* out, int ndim,
+                     const int64_t* sizes, float alpha, void* stream);
+
+typedef enum {
+    TK_UN_RELU = 0, TK_UN_GELU = 1, TK_UN_GELU_TANH = 2, TK_UN_SILU = 3, TK_UN_SCALE = 4
+} tk_unop_t;
+
+/* y[i] = op(x[i]) on n contiguous elements; TK_UN_SCALE is x*p0 + p1.
+ * Replaces xdnn relu (csrc/ops.cpp:151-160), gelu / approximate_gelu
+ * (csrc/ops_nn.cpp:132-147), swish (csrc/ops_extra.cpp:71) and scale
+ * (csrc/autograd.cpp:586-601). */
+TK_API int tk_unary(int op, tk_dtype_t dtype, const void* x, void* y, int64_t n, float p0,
+                    float p1, void* stream);
+
+/* y = T(silu(gate)) * up, rounded like the reference's swish followed by mul. */
+TK_API int tk_silu_mul(tk_dtype_t dtype, const void* gate, const void* up, void* y, int64_t n,
+                       void* stream);
 
 #ifdef __cplusplus
 }

@@ -23,7 +23,8 @@ ACT = {"none": 0, "relu": 1, "gelu": 2, "gelu_tanh": 3, "silu": 4}
 EXPORTED = [
     "tk_abi_version", "tk_last_error_string", "tk_device_error", "tk_amax",
     "tk_quantize_limbs", "tk_qgemm_workspace_size", "tk_qgemm", "tk_qgemm_simt",
-    "tk_qgemm_debug",
+    "tk_qgemm_debug", "tk_qgemm_from_limbs", "tk_copy_strided", "tk_fill_strided",
+    "tk_binary", "tk_unary", "tk_silu_mul",
 ]
 
 
@@ -71,6 +72,7 @@ def lib() -> ctypes.CDLL:
         L.tk_qgemm_workspace_size.restype = ctypes.c_size_t
         for name in ("tk_qgemm", "tk_qgemm_simt"):
             getattr(L, name).argtypes = [ctypes.POINTER(QGemmDesc), vp, ctypes.c_size_t, vp]
+        L.tk_qgemm_from_limbs.argtypes = [ctypes.POINTER(QGemmDesc), vp, vp, vp, vp, vp]
         L.tk_qgemm_debug.argtypes = [ctypes.POINTER(QGemmDesc), vp, ctypes.c_size_t, vp, vp]
         _lib = L
     return _lib

@@ -204,9 +204,8 @@ __global__ void silu_mul_kernel(const T* __restrict__ g, const T* __restrict__ u
                                 int64_t n) {
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        float h = un_apply(TK_UN_SILU, ld<T>(g, i), 0.f, 0.f);
-        h = ld<T>(reinterpret_cast<const T*>(&h), 0) * 0.0f + h;  // keep in fp32
-        T hr;
+        const float h = un_apply(TK_UN_SILU, ld<T>(g, i), 0.f, 0.f);
+        T hr;  // silu output rounded to T, as the reference stores it
         st<T>(&hr, 0, h);
         st<T>(y, i, __fmul_rn(ld<T>(&hr, 0), ld<T>(u, i)));
     }

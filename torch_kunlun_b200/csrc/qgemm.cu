@@ -49,7 +49,8 @@ constexpr int UMMA_K = 32;
 constexpr int STAGES = 3;
 constexpr int TILE_BYTES = BM * BK;            // one limb plane of one operand
 constexpr int STAGE_BYTES = 4 * TILE_BYTES;    // A hi, A lo, B hi, B lo
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_EPI_WARPS = 8;  // two warps per TMEM lane quarter, 64 columns each
+constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
 constexpr int TMEM_COLS = 512;
 constexpr int ACC_HH = 0;
 constexpr int ACC_MID = BN;
@@ -76,6 +77,7 @@ struct EpiParams {
     const float* amax_b;
     int64_t scale_stride;  // 1: per-slice amax; 0: one amax for all slices
     bool vec_store;
+    bool bias_vec;  // bias is 16-byte aligned: vector loads per 16-column chunk
     int32_t* dbg;  // [3][M][N] raw accumulators of slice 0, or null
 };
 
@@ -135,6 +137,25 @@ __device__ __forceinline__ float apply_act(float r, int act, int dtype) {
     }
 }
 
+template <int ACT>
+__device__ __forceinline__ float act_t(float r, int dtype) {
+    if constexpr (ACT == TK_ACT_NONE) {
+        return r;
+    } else if constexpr (ACT == TK_ACT_RELU) {
+        return (r > 0.0f || r != r) ? r : 0.0f;
+    } else {
+        return apply_act(r, ACT, dtype);
+    }
+}
+
+// Integer recombination of the three limb accumulators, exact in int64:
+// acc = 65536*HH + 256*MID + LL (|acc| <= 2^46 for K <= 32768).
+__device__ __forceinline__ long long recombine(uint32_t hh, uint32_t mid, uint32_t ll) {
+    return (static_cast<long long>(static_cast<int32_t>(hh)) << 16) +
+           (static_cast<long long>(static_cast<int32_t>(mid)) << 8) +
+           static_cast<long long>(static_cast<int32_t>(ll));
+}
+
 __device__ __forceinline__ double dequant_scale(const EpiParams& p, int64_t b) {
     const float aa = p.amax_a[b * p.scale_stride];
     const float ab = p.amax_b[b * p.scale_stride];
@@ -178,6 +199,7 @@ __device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b,
 
 // ---- tensor-core kernel --------------------------------------------------------
 
+template <int DT, int ACT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const TileParams tp, const EpiParams ep) {
@@ -202,7 +224,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             mbar_init(smem_u32(empty_bar + s), 1);
         }
         mbar_init(smem_u32(acc_full), 1);
-        mbar_init(smem_u32(acc_empty), 4);
+        mbar_init(smem_u32(acc_empty), NUM_EPI_WARPS);
         mbar_init(smem_u32(drain_bar), 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -311,10 +333,17 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         volatile int no_abort = 0;
         mbar_wait_bounded(smem_u32(drain_bar), 0, &no_abort, tp.err, kDevErrWaitDrain);
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
-        const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+        // ---------------- epilogue (warps 2..9) ----------------
+        // Warp w reads TMEM lane quarter (w % 4) -- the hardware restricts a
+        // warp to lanes [32*(w%4), 32*(w%4)+32) -- and columns
+        // [64*half, 64*half + 64) of each accumulator.
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
         const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        const bool has_bias = ep.bias != nullptr;
+        const bool has_add = ep.addend != nullptr && ep.beta != 0.0f;
+        const bool has_alpha = ep.alpha != 1.0f;
         uint32_t acc_phase = 0;
         for (int t = blockIdx.x; t < tp.num_tiles; t += gridDim.x) {
             int b, mt, nt;
@@ -329,7 +358,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             const bool row_ok = m < ep.M;
             const int64_t out_row = b * ep.out_sb + m * ep.out_sm;
 #pragma unroll 1
-            for (int c = 0; c < BN / 16; ++c) {
+            for (int cc = 0; cc < BN / 32; ++cc) {
+                const int c = half * (BN / 32) + cc;  // 16-column chunk index
                 uint32_t hh[16], mid[16], ll[16];
                 tmem_ld_32x32b_x16(t_row + ACC_HH + c * 16, hh);
                 tmem_ld_32x32b_x16(t_row + ACC_MID + c * 16, mid);
@@ -337,14 +367,62 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 tc_wait_ld();
                 const int64_t n0 = static_cast<int64_t>(nt) * BN + c * 16;
                 if (!row_ok || n0 >= ep.N) continue;
+                const bool full = n0 + 16 <= ep.N;
                 float v[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const double acc = __fma_rn(
-                        static_cast<double>(static_cast<int32_t>(hh[j])), 65536.0,
-                        __fma_rn(static_cast<double>(static_cast<int32_t>(mid[j])), 256.0,
-                                 static_cast<double>(static_cast<int32_t>(ll[j]))));
-                    v[j] = epilogue_one(ep, s, acc, b, m, n0 + j);
+                for (int j = 0; j < 16; ++j)
+                    v[j] = round_t_from_double(
+                        __dmul_rn(static_cast<double>(recombine(hh[j], mid[j], ll[j])), s), DT);
+                if (has_alpha) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = round_t(__fmul_rn(v[j], ep.alpha), DT);
+                }
+                if (has_bias) {
+                    float bv[16];
+                    if (full && ep.bias_vec) {
+                        // 16 consecutive bias values with 128-bit loads (the
+                        // same addresses for the whole warp: one broadcast).
+                        if constexpr (DT == 0) {
+                            const uint4* src = reinterpret_cast<const uint4*>(
+                                static_cast<const __half*>(ep.bias) + n0);
+                            uint4 q[2] = {__ldg(src), __ldg(src + 1)};
+                            const __half2* h2 = reinterpret_cast<const __half2*>(q);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                const float2 f = __half22float2(h2[j]);
+                                bv[2 * j] = f.x;
+                                bv[2 * j + 1] = f.y;
+                            }
+                        } else {
+                            const float4* src = reinterpret_cast<const float4*>(
+                                static_cast<const float*>(ep.bias) + n0);
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const float4 f = __ldg(src + j);
+                                bv[4 * j] = f.x; bv[4 * j + 1] = f.y;
+                                bv[4 * j + 2] = f.z; bv[4 * j + 3] = f.w;
+                            }
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            bv[j] = (n0 + j < ep.N) ? load_t(ep.bias, DT, n0 + j) : 0.0f;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = round_t(__fadd_rn(v[j], bv[j]), DT);
+                }
+                if (has_add) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        if (!full && n0 + j >= ep.N) continue;
+                        float a = load_t(ep.addend, DT, b * ep.add_sb + m * ep.add_sm + (n0 + j) * ep.add_sn);
+                        if (ep.beta != 1.0f) a = round_t(__fmul_rn(a, ep.beta), DT);
+                        v[j] = round_t(__fadd_rn(v[j], a), DT);
+                    }
+                }
+                if constexpr (ACT != TK_ACT_NONE) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = act_t<ACT>(v[j], DT);
                 }
                 if (ep.dbg != nullptr && b == 0) {
                     for (int j = 0; j < 16 && n0 + j < ep.N; ++j) {
@@ -353,8 +431,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                         ep.dbg[(2 * ep.M + m) * ep.N + n0 + j] = static_cast<int32_t>(ll[j]);
                     }
                 }
-                if (ep.vec_store && n0 + 16 <= ep.N) {
-                    if (ep.dtype == 0) {
+                if (ep.vec_store && full) {
+                    if constexpr (DT == 0) {
                         uint32_t w[8];
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
@@ -371,7 +449,9 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                             dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
                     }
                 } else {
-                    for (int j = 0; j < 16 && n0 + j < ep.N; ++j) store_one(ep, out_row + n0 + j, v[j]);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (full || n0 + j < ep.N) store_one(ep, out_row + n0 + j, v[j]);
                 }
             }
             tc_fence_before();
@@ -542,11 +622,69 @@ EpiParams make_epi(const tk_qgemm_desc_t& d, const float* amax_a, const float* a
     ep.vec_store = (reinterpret_cast<uintptr_t>(d.out) % 16 == 0) &&
                    ((d.out_sm * static_cast<int64_t>(es)) % 16 == 0) &&
                    (d.batch <= 1 || (d.out_sb * static_cast<int64_t>(es)) % 16 == 0);
+    ep.bias_vec = d.bias != nullptr && reinterpret_cast<uintptr_t>(d.bias) % 16 == 0;
     ep.dbg = dbg;
     return ep;
 }
 
 enum class Path { TensorCore, Simt };
+
+template <int DT, int ACT>
+int launch_one(int dev, int grid, const CUtensorMap& tmA, const CUtensorMap& tmB,
+               const TileParams& tp, const EpiParams& ep, cudaStream_t stream) {
+    static std::once_flag attr_once[64];
+    if (dev >= 0 && dev < 64) {
+        std::call_once(attr_once[dev], [] {
+            cudaFuncSetAttribute(qgemm_tc_kernel<DT, ACT>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        });
+    }
+    qgemm_tc_kernel<DT, ACT><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tmA, tmB, tp, ep);
+    return TK_OK;
+}
+
+template <int DT>
+int dispatch_act(int act, int dev, int grid, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                 const TileParams& tp, const EpiParams& ep, cudaStream_t stream) {
+    switch (act) {
+        case TK_ACT_NONE: return launch_one<DT, TK_ACT_NONE>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_RELU: return launch_one<DT, TK_ACT_RELU>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_GELU: return launch_one<DT, TK_ACT_GELU>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_GELU_TANH: return launch_one<DT, TK_ACT_GELU_TANH>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_SILU: return launch_one<DT, TK_ACT_SILU>(dev, grid, tmA, tmB, tp, ep, stream);
+        default: TK_FAIL(TK_ERR_INVALID_ARG, "qgemm: bad act %d", act);
+    }
+}
+
+int dispatch_tc(int dt, int act, int dev, int grid, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                const TileParams& tp, const EpiParams& ep, cudaStream_t stream) {
+    return dt == 0 ? dispatch_act<0>(act, dev, grid, tmA, tmB, tp, ep, stream)
+                   : dispatch_act<1>(act, dev, grid, tmA, tmB, tp, ep, stream);
+}
+
+int launch_tc(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb, int64_t ld,
+              const EpiParams& ep, cudaStream_t stream) {
+    CUtensorMap tmA, tmB;
+    int rc = make_limb_map(&tmA, la, 2 * d.batch, d.m, ld);
+    if (rc) return rc;
+    rc = make_limb_map(&tmB, lb, 2 * d.batch, d.n, ld);
+    if (rc) return rc;
+    TileParams tp;
+    tp.batch = static_cast<int>(d.batch);
+    tp.tiles_m = static_cast<int>(ceil_div(d.m, BM));
+    tp.tiles_n = static_cast<int>(ceil_div(d.n, BN));
+    const int64_t nt = static_cast<int64_t>(tp.tiles_m) * tp.tiles_n * d.batch;
+    TK_CHECK_ARG(nt < (1LL << 31), "qgemm: too many tiles");
+    tp.num_tiles = static_cast<int>(nt);
+    tp.num_kb = static_cast<int>(ceil_div(d.k, BK));
+    const int dev = current_device();
+    tp.err = device_error_word(dev);
+    const int grid = static_cast<int>(std::min<int64_t>(nt, sm_count(dev)));
+    int rc2 = dispatch_tc(d.dtype == TK_DTYPE_F16 ? 0 : 1, static_cast<int>(d.act), dev, grid,
+                          tmA, tmB, tp, ep, stream);
+    if (rc2) return rc2;
+    return launch_status("qgemm_tc");
+}
 
 int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t stream, Path path,
         int32_t* dbg) {
@@ -590,31 +728,7 @@ int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t str
         return launch_status("qgemm_simt");
     }
 
-    CUtensorMap tmA, tmB;
-    rc = make_limb_map(&tmA, la, 2 * d.batch, d.m, L.ld);
-    if (rc) return rc;
-    rc = make_limb_map(&tmB, lb, 2 * d.batch, d.n, L.ld);
-    if (rc) return rc;
-    TileParams tp;
-    tp.batch = static_cast<int>(d.batch);
-    tp.tiles_m = static_cast<int>(ceil_div(d.m, BM));
-    tp.tiles_n = static_cast<int>(ceil_div(d.n, BN));
-    const int64_t nt = static_cast<int64_t>(tp.tiles_m) * tp.tiles_n * d.batch;
-    TK_CHECK_ARG(nt < (1LL << 31), "qgemm: too many tiles");
-    tp.num_tiles = static_cast<int>(nt);
-    tp.num_kb = static_cast<int>(ceil_div(d.k, BK));
-    const int dev = current_device();
-    tp.err = device_error_word(dev);
-    static std::once_flag attr_once[64];
-    if (dev >= 0 && dev < 64) {
-        std::call_once(attr_once[dev], [] {
-            cudaFuncSetAttribute(qgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 SMEM_BYTES);
-        });
-    }
-    const int grid = static_cast<int>(std::min<int64_t>(nt, sm_count(dev)));
-    qgemm_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tmA, tmB, tp, ep);
-    return launch_status("qgemm_tc");
+    return launch_tc(d, la, lb, L.ld, ep, stream);
 }
 
 }  // namespace
@@ -636,6 +750,24 @@ int tk_qgemm_simt(const tk_qgemm_desc_t* desc, void* workspace, size_t workspace
                   void* stream) {
     return tk::run(desc, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
                    tk::Path::Simt, nullptr);
+}
+
+int tk_qgemm_from_limbs(const tk_qgemm_desc_t* desc, const int8_t* a_limbs, const int8_t* b_limbs,
+                        const float* amax_a, const float* amax_b, void* stream) {
+    using namespace tk;
+    TK_CHECK_ARG(desc != nullptr, "qgemm_from_limbs: desc is NULL");
+    const tk_qgemm_desc_t& d = *desc;
+    int rc = validate(d);
+    if (rc) return rc;
+    if (d.batch == 0 || d.m == 0 || d.n == 0) return TK_OK;
+    TK_CHECK_ARG(d.k > 0, "qgemm_from_limbs: K must be positive");
+    TK_CHECK_ARG(a_limbs && b_limbs && amax_a && amax_b, "qgemm_from_limbs: NULL pointer");
+    TK_CHECK_ARG(reinterpret_cast<uintptr_t>(a_limbs) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(b_limbs) % 16 == 0,
+                 "qgemm_from_limbs: limb planes must be 16-byte aligned");
+    const int64_t ld = static_cast<int64_t>(round_up(static_cast<size_t>(d.k), 16));
+    EpiParams ep = make_epi(d, amax_a, amax_b, nullptr);
+    return launch_tc(d, a_limbs, b_limbs, ld, ep, static_cast<cudaStream_t>(stream));
 }
 
 int tk_qgemm_debug(const tk_qgemm_desc_t* desc, void* workspace, size_t workspace_bytes,
