@@ -155,6 +155,44 @@ TK_API int tk_qgemm_simt(const tk_qgemm_desc_t* desc, void* workspace, size_t wo
 TK_API int tk_qgemm_debug(const tk_qgemm_desc_t* desc, void* workspace, size_t workspace_bytes,
                    int32_t* acc3, void* stream);
 
+/* ---- quantised conv2d --------------------------------------------------------
+ * Replaces baidu::xpu::api::conv2d<T,T,T,TGEMM> and the bias broadcast_add of
+ * conv2d_impl (csrc/ops.cpp:237-285): NCHW input x [n,c,h,w], OIHW weight
+ * [f, c/groups, kh, kw], optional bias [f], NCHW output [n,f,oh,ow], all
+ * contiguous.  The whole input and the whole weight are quantised with one
+ * scale each; the bias is added after the output is rounded to dtype.
+ * (c/groups)*kh*kw must be <= 32768.
+ */
+typedef struct {
+    tk_dtype_t dtype;
+    int64_t n, c, h, w, f, kh, kw;
+    int64_t stride_h, stride_w, pad_h, pad_w, dil_h, dil_w, groups;
+    const void* x;
+    const void* weight;
+    const void* bias;
+    void* out;
+    const float* amax_x; /* optional precomputed per-tensor amax (device) */
+    const float* amax_w;
+} tk_conv2d_desc_t;
+
+TK_API size_t tk_conv2d_workspace_size(const tk_conv2d_desc_t* desc);
+TK_API int tk_conv2d_q16(const tk_conv2d_desc_t* desc, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* ---- row ops ------------------------------------------------------------------
+ * Softmax over the last dimension of a contiguous [rows, cols] tensor
+ * (xdnn::softmax, csrc/ops_nn.cpp:73-83); out_dtype may be fp32 for fp16
+ * input (aten _softmax half_to_float). */
+TK_API int tk_softmax(tk_dtype_t in_dtype, tk_dtype_t out_dtype, const void* x, void* y,
+                      int64_t rows, int64_t cols, void* stream);
+
+/* LayerNorm over the last `cols` elements of each row, optional gamma/beta of
+ * wdtype, writing fp32 mean and rstd per row when the pointers are non-NULL
+ * (xdnn::layer_norm, csrc/ops_nn.cpp:85-130). */
+TK_API int tk_layer_norm(tk_dtype_t dtype, tk_dtype_t wdtype, const void* x, const void* gamma,
+                         const void* beta, void* y, float* mean, float* rstd, int64_t rows,
+                         int64_t cols, float eps, void* stream);
+
 /* ---- data movement and elementwise ops -----------------------------------
  * Scalar type codes of tk_copy_strided / tk_fill_strided. */
 typedef enum {

@@ -1,0 +1,76 @@
+"""CPU checks of the C ABI boundary: the library loads, exports every entry
+point declared in include/tk_kernels.h, and rejects bad arguments before any
+device work (no GPU is touched)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from torch_kunlun_b200 import _capi as C
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    src = open(os.path.join(ROOT, "include", "tk_kernels.h")).read()
+    return sorted(set(re.findall(r"TK_API\s+[\w\s\*]+?\b(tk_\w+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = C.lib()
+    names = declared_symbols()
+    assert len(names) >= 19
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+    assert set(names) <= set(C.EXPORTED) | set(names)
+
+
+def test_binding_lists_every_declared_symbol():
+    assert set(declared_symbols()) == set(C.EXPORTED)
+
+
+def test_abi_version():
+    assert C.lib().tk_abi_version() == 1
+
+
+def test_qgemm_rejects_large_k_without_touching_the_device():
+    d = C.QGemmDesc()
+    d.dtype = 0
+    d.batch, d.m, d.n, d.k = 1, 4, 4, 40000
+    d.out = 1  # never dereferenced: validation fails first
+    rc = C.lib().tk_qgemm(ctypes.byref(d), None, 0, None)
+    assert rc == 1
+    assert b"exceeds 32768" in C.lib().tk_last_error_string()
+
+
+def test_qgemm_workspace_layout():
+    d = C.QGemmDesc()
+    d.dtype = 0
+    d.batch, d.m, d.n, d.k = 2, 100, 60, 33
+    d.per_slice_scales = 1
+    ws = C.lib().tk_qgemm_workspace_size(ctypes.byref(d))
+    ld = 48  # round_up(33, 16)
+    assert ws >= 2 * 2 * 100 * ld + 2 * 2 * 60 * ld
+    assert ws % 1024 == 0
+
+
+def test_package_registers_kunlun_device_and_bkcl():
+    import torch
+    import torch.distributed as dist
+    import torch_kunlun  # noqa: F401
+    assert torch._C._get_privateuse1_backend_name() == "kunlun"
+    assert hasattr(torch, "kunlun") and hasattr(torch.Tensor, "kunlun")
+    assert "bkcl" in dist.Backend.backend_list
+    assert torch_kunlun.kunlun.Stream is torch.kunlun.Stream
+
+
+def test_cluster_budget_roundtrip_api():
+    import torch_kunlun
+    k = torch_kunlun.kunlun
+    orig = k.cluster_budget()
+    try:
+        assert k.set_cluster_budget(2) == 2
+        assert k.cluster_budget() == 2 and k.sdnn_budget() == 2
+    finally:
+        k.set_cluster_budget(orig)

@@ -23,9 +23,20 @@ CSRC = os.path.join(PKG, "csrc")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
-KERNEL_SOURCES = ["capi.cu", "quant.cu", "qgemm.cu", "eltwise.cu"]
+KERNEL_SOURCES = ["capi.cu", "quant.cu", "qgemm.cu", "eltwise.cu", "rowops.cu", "conv.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 KERNEL_LIB = os.path.join(PKG, "libtk_kernels.so")
+
+
+def _nccl_dir() -> str:
+    import importlib.util
+    spec = importlib.util.find_spec("nvidia.nccl")
+    if spec and spec.submodule_search_locations:
+        return list(spec.submodule_search_locations)[0]
+    return "/usr"
+
+
+NCCL_DIR = _nccl_dir()
 
 
 def _newer(target: str, sources) -> bool:
@@ -59,7 +70,7 @@ def build_kernels(force: bool = False, verbose_ptxas: bool = False) -> str:
         _run(cmd)
         objs.append(o)
     _run([NVCC, *ARCH_FLAGS, "-shared", "-cudart", "shared", "-o", KERNEL_LIB, *objs,
-          "-Xlinker", f"-rpath,{CUDA_HOME}/lib64"])
+          "-Xlinker", "-soname=libtk_kernels.so", "-Xlinker", f"-rpath,{CUDA_HOME}/lib64"])
     return KERNEL_LIB
 
 
@@ -78,13 +89,19 @@ def build_extension(force: bool = False) -> str:
         return target
     build_dir = os.path.join(PKG, "_build", "ext")
     os.makedirs(build_dir, exist_ok=True)
+    # the freshly built module links libtk_kernels.so; make it resolvable for
+    # the import that load() performs (the installed copy finds it via $ORIGIN)
+    import ctypes
+    ctypes.CDLL(KERNEL_LIB, mode=ctypes.RTLD_GLOBAL)
     cpp_extension.load(
         name="_C",
         sources=srcs,
         extra_cflags=["-O2", "-std=c++17", f"-I{os.path.join(ROOT, 'include')}",
-                      f"-I{CUDA_HOME}/include"],
+                      f"-I{NCCL_DIR}/include", f"-I{CUDA_HOME}/include"],
         extra_ldflags=[f"-L{PKG}", "-ltk_kernels", f"-L{CUDA_HOME}/lib64", "-lcudart",
-                       "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{CUDA_HOME}/lib64"],
+                       f"-L{NCCL_DIR}/lib", "-l:libnccl.so.2",
+                       "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{NCCL_DIR}/lib",
+                       f"-Wl,-rpath,{CUDA_HOME}/lib64"],
         build_directory=build_dir,
         with_cuda=False,
         is_python_module=True,

@@ -24,7 +24,8 @@ EXPORTED = [
     "tk_abi_version", "tk_last_error_string", "tk_device_error", "tk_amax",
     "tk_quantize_limbs", "tk_qgemm_workspace_size", "tk_qgemm", "tk_qgemm_simt",
     "tk_qgemm_debug", "tk_qgemm_from_limbs", "tk_copy_strided", "tk_fill_strided",
-    "tk_binary", "tk_unary", "tk_silu_mul",
+    "tk_binary", "tk_unary", "tk_silu_mul", "tk_conv2d_workspace_size", "tk_conv2d_q16",
+    "tk_softmax", "tk_layer_norm",
 ]
 
 

@@ -1,0 +1,278 @@
+// conv.cu -- int16-quantised conv2d (NCHW input, OIHW weight, bias, stride,
+// padding, dilation, groups).
+//
+// Replaces baidu::xpu::api::conv2d<T,T,T,TGEMM> and the bias broadcast_add
+// that follows it (csrc/ops.cpp:237-285).  Per the reference, the whole
+// input and the whole weight are each quantised with one per-tensor scale.
+//
+// Paths:
+//   * groups == C == F/mult (depthwise): a CUDA-core kernel, one output per
+//     thread, exact int64 accumulation of the KHxKW taps.  HBM-bound.
+//   * otherwise a GEMM per (image, group) on the tensor-core limb kernel:
+//     A = the image's input patches [OH*OW, C/g*KH*KW] quantised straight into
+//     limb planes (1x1 stride-1 convolutions read NCHW directly as a
+//     transposed operand; larger kernels gather patches in the same pass),
+//     B = the group's weights [F/g, C/g*KH*KW] (shared by all images), and
+//     the epilogue writes the pixels x channels tile into NCHW.
+#include "tk_internal.h"
+#include "tk_numerics.cuh"
+
+namespace tk {
+
+int amax_launch(tk_dtype_t dtype, const void* x, int64_t nslices, int64_t slice_stride,
+                int64_t slice_len, float* amax_out, cudaStream_t stream);
+int quantize_limbs_launch(tk_dtype_t dtype, const void* x, int64_t batch, int64_t rows,
+                          int64_t cols, int64_t sb, int64_t sr, int64_t sc, const float* amax,
+                          int64_t amax_stride, int8_t* limbs, cudaStream_t stream);
+int qgemm_limbs_ex(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb,
+                   const float* amax_a, const float* amax_b, int b_mod, int64_t out_sn,
+                   int64_t bias_mod, cudaStream_t stream);
+
+namespace {
+
+struct ConvGeom {
+    int64_t N, C, H, W, F, KH, KW, sh, sw, ph, pw, dh, dw, groups, OH, OW;
+};
+
+template <typename T>
+__device__ __forceinline__ float ldx(const T* p, int64_t i);
+template <> __device__ __forceinline__ float ldx<__half>(const __half* p, int64_t i) { return __half2float(p[i]); }
+template <> __device__ __forceinline__ float ldx<float>(const float* p, int64_t i) { return p[i]; }
+
+// Patch gather + quantisation.  Slice b = n*groups + g, row p = oh*OW + ow,
+// column k = (c*KH + r)*KW + s over the group's channels; 4 columns per thread
+// so that both limb planes are written with 32-bit stores.
+template <typename T>
+__global__ void im2col_quant_kernel(const T* __restrict__ x, ConvGeom g, int64_t K, int64_t ld,
+                                    const float* __restrict__ amax, int8_t* __restrict__ limbs) {
+    const int64_t P = g.OH * g.OW;
+    const int64_t k4n = ld / 4;
+    const int64_t total = g.N * g.groups * P * k4n;
+    const float inv = quant_inv(amax[0]);
+    const int64_t cg = g.C / g.groups;
+    const int64_t khw = g.KH * g.KW;
+    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t k4 = idx % k4n;
+        const int64_t rest = idx / k4n;
+        const int64_t p = rest % P;
+        const int64_t b = rest / P;
+        const int64_t n = b / g.groups, grp = b % g.groups;
+        const int64_t oh = p / g.OW, ow = p % g.OW;
+        unsigned hi = 0, lo = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t k = k4 * 4 + j;
+            int q = 0;
+            if (k < K) {
+                const int64_t c = k / khw;
+                const int64_t rs = k - c * khw;
+                const int64_t r = rs / g.KW, s = rs - r * g.KW;
+                const int64_t ih = oh * g.sh - g.ph + r * g.dh;
+                const int64_t iw = ow * g.sw - g.pw + s * g.dw;
+                if (ih >= 0 && ih < g.H && iw >= 0 && iw < g.W) {
+                    const int64_t ci = grp * cg + c;
+                    q = quant_one(ldx<T>(x, ((n * g.C + ci) * g.H + ih) * g.W + iw), inv);
+                }
+            }
+            hi |= (static_cast<unsigned>(q >> 8) & 0xFFu) << (8 * j);
+            lo |= (static_cast<unsigned>(q) & 0xFFu) << (8 * j);
+        }
+        const int64_t plane = P * ld;
+        int8_t* base = limbs + (b * 2) * plane + p * ld + k4 * 4;
+        *reinterpret_cast<unsigned*>(base) = hi;
+        *reinterpret_cast<unsigned*>(base + plane) = lo;
+    }
+}
+
+// Depthwise (one input channel per group): output channel f reads input
+// channel f / mult.  Exact int64 accumulation, then the shared epilogue
+// (dequantise + round, then bias added after rounding).
+template <typename T, int DT>
+__global__ void depthwise_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                 const T* __restrict__ bias, T* __restrict__ out, ConvGeom g,
+                                 const float* __restrict__ amax_x, const float* __restrict__ amax_w) {
+    const int64_t total = g.N * g.F * g.OH * g.OW;
+    const float ax = amax_x[0], aw = amax_w[0];
+    const float invx = quant_inv(ax), invw = quant_inv(aw);
+    const double s = dequant_scale(ax, aw);
+    const int64_t mult = g.F / g.C;
+    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t ow = idx % g.OW;
+        int64_t t = idx / g.OW;
+        const int64_t oh = t % g.OH;
+        t /= g.OH;
+        const int64_t f = t % g.F;
+        const int64_t n = t / g.F;
+        const int64_t c = f / mult;
+        const T* xc = x + (n * g.C + c) * g.H * g.W;
+        const T* wf = w + f * g.KH * g.KW;
+        long long acc = 0;
+        for (int64_t r = 0; r < g.KH; ++r) {
+            const int64_t ih = oh * g.sh - g.ph + r * g.dh;
+            if (ih < 0 || ih >= g.H) continue;
+            for (int64_t sx = 0; sx < g.KW; ++sx) {
+                const int64_t iw = ow * g.sw - g.pw + sx * g.dw;
+                if (iw < 0 || iw >= g.W) continue;
+                acc += static_cast<long long>(quant_one(ldx<T>(xc, ih * g.W + iw), invx)) *
+                       static_cast<long long>(quant_one(ldx<T>(wf, r * g.KW + sx), invw));
+            }
+        }
+        float v = round_t_from_double(__dmul_rn(static_cast<double>(acc), s), DT);
+        if (bias != nullptr) v = round_t(__fadd_rn(v, ldx<T>(bias, f)), DT);
+        store_t(out, DT, idx, v);
+    }
+}
+
+int grid_1d(int64_t n, int threads) {
+    const int64_t g = ceil_div(n, threads);
+    const int64_t cap = static_cast<int64_t>(sm_count(current_device())) * 32;
+    return static_cast<int>(std::max<int64_t>(1, std::min(g, cap)));
+}
+
+int geometry(const tk_conv2d_desc_t& d, ConvGeom& g) {
+    TK_CHECK_ARG(d.dtype == TK_DTYPE_F16 || d.dtype == TK_DTYPE_F32, "conv2d: bad dtype");
+    TK_CHECK_ARG(d.n >= 0 && d.c > 0 && d.h > 0 && d.w > 0 && d.f > 0 && d.kh > 0 && d.kw > 0,
+                 "conv2d: bad shape");
+    TK_CHECK_ARG(d.stride_h > 0 && d.stride_w > 0 && d.dil_h > 0 && d.dil_w > 0 && d.pad_h >= 0 &&
+                     d.pad_w >= 0,
+                 "conv2d: bad stride/padding/dilation");
+    TK_CHECK_ARG(d.groups > 0 && d.c % d.groups == 0 && d.f % d.groups == 0,
+                 "conv2d: channels must be divisible by groups");
+    g = {d.n, d.c, d.h, d.w, d.f, d.kh, d.kw, d.stride_h, d.stride_w, d.pad_h, d.pad_w,
+         d.dil_h, d.dil_w, d.groups, 0, 0};
+    g.OH = (d.h + 2 * d.pad_h - d.dil_h * (d.kh - 1) - 1) / d.stride_h + 1;
+    g.OW = (d.w + 2 * d.pad_w - d.dil_w * (d.kw - 1) - 1) / d.stride_w + 1;
+    TK_CHECK_ARG(g.OH > 0 && g.OW > 0, "conv2d: non-positive output size");
+    return TK_OK;
+}
+
+bool is_depthwise(const ConvGeom& g) { return g.groups == g.C && g.groups > 1; }
+bool is_pointwise(const ConvGeom& g) {
+    return g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0 &&
+           g.groups == 1;
+}
+
+struct ConvLayout {
+    int64_t K, ld;
+    size_t off_amax, off_la, off_lb, total;
+};
+
+ConvLayout conv_layout(const ConvGeom& g) {
+    ConvLayout L;
+    L.K = (g.C / g.groups) * g.KH * g.KW;
+    L.ld = static_cast<int64_t>(round_up(static_cast<size_t>(L.K), 16));
+    const int64_t P = g.OH * g.OW;
+    L.off_amax = 0;
+    L.off_la = 1024;
+    if (is_depthwise(g)) {
+        L.off_lb = L.off_la;
+        L.total = L.off_la;
+        return L;
+    }
+    L.off_lb = round_up(L.off_la + static_cast<size_t>(g.N * g.groups * 2 * P * L.ld), 1024);
+    L.total = round_up(L.off_lb + static_cast<size_t>(g.groups * 2 * (g.F / g.groups) * L.ld), 1024);
+    return L;
+}
+
+}  // namespace
+}  // namespace tk
+
+extern "C" {
+
+size_t tk_conv2d_workspace_size(const tk_conv2d_desc_t* desc) {
+    using namespace tk;
+    if (desc == nullptr) return 0;
+    ConvGeom g;
+    if (geometry(*desc, g) != TK_OK) return 0;
+    return conv_layout(g).total;
+}
+
+int tk_conv2d_q16(const tk_conv2d_desc_t* desc, void* workspace, size_t workspace_bytes,
+                  void* stream_) {
+    using namespace tk;
+    TK_CHECK_ARG(desc != nullptr, "conv2d: desc is NULL");
+    const tk_conv2d_desc_t& d = *desc;
+    ConvGeom g;
+    int rc = geometry(d, g);
+    if (rc) return rc;
+    if (g.N == 0) return TK_OK;
+    TK_CHECK_ARG(d.x && d.weight && d.out, "conv2d: NULL pointer");
+    const ConvLayout L = conv_layout(g);
+    TK_CHECK_ARG(workspace != nullptr && workspace_bytes >= L.total &&
+                     reinterpret_cast<uintptr_t>(workspace) % 1024 == 0,
+                 "conv2d: workspace must be >= %zu bytes and 1024-byte aligned", L.total);
+    TK_CHECK_ARG(L.K <= 32768, "conv2d: C/groups*KH*KW = %lld exceeds 32768", (long long)L.K);
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* amax = reinterpret_cast<float*>(ws + L.off_amax);  // [0] input, [1] weight
+    const float* ax = d.amax_x;
+    const float* aw = d.amax_w;
+    if (ax == nullptr) {
+        rc = amax_launch(d.dtype, d.x, 1, 0, g.N * g.C * g.H * g.W, amax, stream);
+        if (rc) return rc;
+        ax = amax;
+    }
+    if (aw == nullptr) {
+        rc = amax_launch(d.dtype, d.weight, 1, 0, g.F * (g.C / g.groups) * g.KH * g.KW, amax + 1,
+                         stream);
+        if (rc) return rc;
+        aw = amax + 1;
+    }
+    const int64_t P = g.OH * g.OW;
+    if (is_depthwise(g)) {
+        const int64_t total = g.N * g.F * P;
+        const int grid = grid_1d(total, 256);
+        if (d.dtype == TK_DTYPE_F16)
+            depthwise_kernel<__half, 0><<<grid, 256, 0, stream>>>(
+                static_cast<const __half*>(d.x), static_cast<const __half*>(d.weight),
+                static_cast<const __half*>(d.bias), static_cast<__half*>(d.out), g, ax, aw);
+        else
+            depthwise_kernel<float, 1><<<grid, 256, 0, stream>>>(
+                static_cast<const float*>(d.x), static_cast<const float*>(d.weight),
+                static_cast<const float*>(d.bias), static_cast<float*>(d.out), g, ax, aw);
+        return launch_status("conv2d depthwise");
+    }
+    int8_t* la = reinterpret_cast<int8_t*>(ws + L.off_la);  // patches [N*groups][2][P][ld]
+    int8_t* lb = reinterpret_cast<int8_t*>(ws + L.off_lb);  // weights [groups][2][F/g][ld]
+    const int64_t fg = g.F / g.groups;
+    // weights: contiguous OIHW, one [F/g, K] slice per group
+    rc = quantize_limbs_launch(d.dtype, d.weight, g.groups, fg, L.K, fg * L.K, L.K, 1, aw, 0, lb,
+                               stream);
+    if (rc) return rc;
+    if (is_pointwise(g)) {
+        // A[n] = x[n] viewed as [P, C] with strides (1, P): a transposed read.
+        rc = quantize_limbs_launch(d.dtype, d.x, g.N, P, g.C, g.C * P, 1, P, ax, 0, la, stream);
+        if (rc) return rc;
+    } else {
+        const int64_t total = g.N * g.groups * P * (L.ld / 4);
+        const int grid = grid_1d(total, 256);
+        if (d.dtype == TK_DTYPE_F16)
+            im2col_quant_kernel<__half><<<grid, 256, 0, stream>>>(
+                static_cast<const __half*>(d.x), g, L.K, L.ld, ax, la);
+        else
+            im2col_quant_kernel<float><<<grid, 256, 0, stream>>>(
+                static_cast<const float*>(d.x), g, L.K, L.ld, ax, la);
+        rc = launch_status("conv2d im2col");
+        if (rc) return rc;
+    }
+    tk_qgemm_desc_t q = {};
+    q.dtype = d.dtype;
+    q.batch = g.N * g.groups;
+    q.m = P;
+    q.n = fg;
+    q.k = L.K;
+    q.out = d.out;
+    q.out_sb = fg * P;  // slice (n, grp) starts at out[n][grp*fg][0][0]
+    q.out_sm = 1;       // pixels are contiguous in NCHW
+    q.bias = d.bias;
+    q.alpha = 1.0f;
+    q.beta = 0.0f;
+    q.act = TK_ACT_NONE;
+    q.per_slice_scales = 0;
+    return qgemm_limbs_ex(q, la, lb, ax, aw, static_cast<int>(g.groups), /*out_sn=*/P,
+                          /*bias_mod=*/g.groups > 1 ? g.groups : 0, stream);
+}
+
+}  // extern "C"

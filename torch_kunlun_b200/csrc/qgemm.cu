@@ -30,6 +30,7 @@
 #include <mutex>
 
 #include "tk_internal.h"
+#include "tk_numerics.cuh"
 #include "tk_ptx.cuh"
 
 namespace tk {
@@ -67,8 +68,9 @@ struct EpiParams {
     int dtype;  // 0 fp16, 1 fp32
     int64_t M, N;
     void* out;
-    int64_t out_sb, out_sm;
+    int64_t out_sb, out_sm, out_sn;  // out_sn == 1 except for transposed (NCHW) stores
     const void* bias;
+    int64_t bias_mod;  // 0: bias[n]; else bias[(b % bias_mod) * N + n] (grouped conv)
     const void* addend;
     int64_t add_sb, add_sm, add_sn;
     float alpha, beta;
@@ -83,58 +85,14 @@ struct EpiParams {
 
 struct TileParams {
     int batch, tiles_m, tiles_n, num_tiles, num_kb;
+    int b_mod;  // 0: B slice b; else B slice (b % b_mod) (operand shared across images)
     unsigned* err;
 };
 
-// ---- shared numerics (device) -----------------------------------------------
+// ---- numerics (device): tk_numerics.cuh holds the shared contract ----------
 
-// binary64 -> binary16, nearest-even.  Uses the round-to-odd intermediate of
-// Boldo & Melquiond ("When double rounding is odd", 2005): rounding to
-// binary32 toward zero and setting the last bit when inexact, then rounding
-// to binary16 to nearest, equals a single correct rounding because binary32
-// carries at least two more significand bits than binary16.
-__device__ __forceinline__ float d2f_round_odd(double d) {
-    float f = __double2float_rz(d);
-    if (static_cast<double>(f) != d) f = __uint_as_float(__float_as_uint(f) | 1u);
-    return f;
-}
-
-__device__ __forceinline__ float round_t_from_double(double d, int dtype) {
-    if (dtype == 0) return __half2float(__float2half_rn(d2f_round_odd(d)));
-    return __double2float_rn(d);
-}
-
-__device__ __forceinline__ float round_t(float v, int dtype) {
-    return dtype == 0 ? __half2float(__float2half_rn(v)) : v;
-}
-
-__device__ __forceinline__ float load_t(const void* p, int dtype, int64_t i) {
-    return dtype == 0 ? __half2float(static_cast<const __half*>(p)[i])
-                      : static_cast<const float*>(p)[i];
-}
-
-__device__ __forceinline__ float gelu_erf(float x) {
-    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
-}
-
-__device__ __forceinline__ float gelu_tanh(float x) {
-    const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-    return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
-}
-
-__device__ __forceinline__ float apply_act(float r, int act, int dtype) {
-    switch (act) {
-        case TK_ACT_RELU:
-            return (r > 0.0f || r != r) ? r : 0.0f;
-        case TK_ACT_GELU:
-            return round_t(gelu_erf(r), dtype);
-        case TK_ACT_GELU_TANH:
-            return round_t(gelu_tanh(r), dtype);
-        case TK_ACT_SILU:
-            return round_t(r / (1.0f + expf(-r)), dtype);
-        default:
-            return r;
-    }
+__device__ __forceinline__ double epi_scale(const EpiParams& p, int64_t b) {
+    return ::tk::dequant_scale(p.amax_a[b * p.scale_stride], p.amax_b[b * p.scale_stride]);
 }
 
 template <int ACT>
@@ -156,11 +114,6 @@ __device__ __forceinline__ long long recombine(uint32_t hh, uint32_t mid, uint32
            static_cast<long long>(static_cast<int32_t>(ll));
 }
 
-__device__ __forceinline__ double dequant_scale(const EpiParams& p, int64_t b) {
-    const float aa = p.amax_a[b * p.scale_stride];
-    const float ab = p.amax_b[b * p.scale_stride];
-    return __ddiv_rn(__dmul_rn(static_cast<double>(aa), static_cast<double>(ab)), 1073676289.0);
-}
 
 // The reference's post-GEMM sequence on one element (see file header).
 __device__ __forceinline__ float epilogue_one(const EpiParams& p, double s, double acc, int64_t b,
@@ -177,10 +130,7 @@ __device__ __forceinline__ float epilogue_one(const EpiParams& p, double s, doub
 }
 
 __device__ __forceinline__ void store_one(const EpiParams& p, int64_t off, float v) {
-    if (p.dtype == 0)
-        static_cast<__half*>(p.out)[off] = __float2half_rn(v);
-    else
-        static_cast<float*>(p.out)[off] = v;
+    store_t(p.out, p.dtype, off, v);
 }
 
 __device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b, int& mt, int& nt) {
@@ -264,8 +214,9 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     const int kx = kb * BK;
                     tma_load_3d(smem_u32(sbase + 0 * TILE_BYTES), &tmA, fb, kx, mt * BM, 2 * b + 0);
                     tma_load_3d(smem_u32(sbase + 1 * TILE_BYTES), &tmA, fb, kx, mt * BM, 2 * b + 1);
-                    tma_load_3d(smem_u32(sbase + 2 * TILE_BYTES), &tmB, fb, kx, nt * BN, 2 * b + 0);
-                    tma_load_3d(smem_u32(sbase + 3 * TILE_BYTES), &tmB, fb, kx, nt * BN, 2 * b + 1);
+                    const int bb = tp.b_mod ? b % tp.b_mod : b;
+                    tma_load_3d(smem_u32(sbase + 2 * TILE_BYTES), &tmB, fb, kx, nt * BN, 2 * bb + 0);
+                    tma_load_3d(smem_u32(sbase + 3 * TILE_BYTES), &tmB, fb, kx, nt * BN, 2 * bb + 1);
                 }
                 __syncwarp();
                 used[stage] = true;
@@ -354,7 +305,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             }
             tc_fence_after();
             const int64_t m = static_cast<int64_t>(mt) * BM + row;
-            const double s = dequant_scale(ep, b);
+            const double s = epi_scale(ep, b);
             const bool row_ok = m < ep.M;
             const int64_t out_row = b * ep.out_sb + m * ep.out_sm;
 #pragma unroll 1
@@ -379,12 +330,16 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 }
                 if (has_bias) {
                     float bv[16];
+                    const void* bias_base = ep.bias_mod
+                        ? static_cast<const void*>(static_cast<const char*>(ep.bias) +
+                              (b % ep.bias_mod) * ep.N * (DT == 0 ? 2 : 4))
+                        : ep.bias;
                     if (full && ep.bias_vec) {
                         // 16 consecutive bias values with 128-bit loads (the
                         // same addresses for the whole warp: one broadcast).
                         if constexpr (DT == 0) {
                             const uint4* src = reinterpret_cast<const uint4*>(
-                                static_cast<const __half*>(ep.bias) + n0);
+                                static_cast<const __half*>(bias_base) + n0);
                             uint4 q[2] = {__ldg(src), __ldg(src + 1)};
                             const __half2* h2 = reinterpret_cast<const __half2*>(q);
 #pragma unroll
@@ -395,7 +350,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                             }
                         } else {
                             const float4* src = reinterpret_cast<const float4*>(
-                                static_cast<const float*>(ep.bias) + n0);
+                                static_cast<const float*>(bias_base) + n0);
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {
                                 const float4 f = __ldg(src + j);
@@ -406,7 +361,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     } else {
 #pragma unroll
                         for (int j = 0; j < 16; ++j)
-                            bv[j] = (n0 + j < ep.N) ? load_t(ep.bias, DT, n0 + j) : 0.0f;
+                            bv[j] = (n0 + j < ep.N) ? load_t(bias_base, DT, n0 + j) : 0.0f;
                     }
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] = round_t(__fadd_rn(v[j], bv[j]), DT);
@@ -451,7 +406,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 } else {
 #pragma unroll
                     for (int j = 0; j < 16; ++j)
-                        if (full || n0 + j < ep.N) store_one(ep, out_row + n0 + j, v[j]);
+                        if (full || n0 + j < ep.N) store_one(ep, out_row + (n0 + j) * ep.out_sn, v[j]);
                 }
             }
             tc_fence_before();
@@ -490,9 +445,9 @@ __global__ void qgemm_simt_kernel(const int8_t* __restrict__ la, const int8_t* _
                            static_cast<int64_t>(static_cast<uint8_t>(blo[k]));
         acc += qa * qb;
     }
-    const double s = dequant_scale(ep, b);
+    const double s = epi_scale(ep, b);
     const float v = epilogue_one(ep, s, static_cast<double>(acc), b, m, n);
-    store_one(ep, b * ep.out_sb + m * ep.out_sm + n, v);
+    store_one(ep, b * ep.out_sb + m * ep.out_sm + n * ep.out_sn, v);
 }
 
 // ---- host side --------------------------------------------------------------------
@@ -607,7 +562,9 @@ EpiParams make_epi(const tk_qgemm_desc_t& d, const float* amax_a, const float* a
     ep.out = d.out;
     ep.out_sb = d.out_sb;
     ep.out_sm = d.out_sm;
+    ep.out_sn = 1;
     ep.bias = d.bias;
+    ep.bias_mod = 0;
     ep.addend = d.addend;
     ep.add_sb = d.add_sb;
     ep.add_sm = d.add_sm;
@@ -622,7 +579,8 @@ EpiParams make_epi(const tk_qgemm_desc_t& d, const float* amax_a, const float* a
     ep.vec_store = (reinterpret_cast<uintptr_t>(d.out) % 16 == 0) &&
                    ((d.out_sm * static_cast<int64_t>(es)) % 16 == 0) &&
                    (d.batch <= 1 || (d.out_sb * static_cast<int64_t>(es)) % 16 == 0);
-    ep.bias_vec = d.bias != nullptr && reinterpret_cast<uintptr_t>(d.bias) % 16 == 0;
+    ep.bias_vec = d.bias != nullptr && reinterpret_cast<uintptr_t>(d.bias) % 16 == 0 &&
+                  (ep.bias_mod == 0 || (d.n * static_cast<int64_t>(es)) % 16 == 0);
     ep.dbg = dbg;
     return ep;
 }
@@ -663,13 +621,14 @@ int dispatch_tc(int dt, int act, int dev, int grid, const CUtensorMap& tmA, cons
 }
 
 int launch_tc(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb, int64_t ld,
-              const EpiParams& ep, cudaStream_t stream) {
+              const EpiParams& ep, cudaStream_t stream, int b_mod = 0) {
     CUtensorMap tmA, tmB;
     int rc = make_limb_map(&tmA, la, 2 * d.batch, d.m, ld);
     if (rc) return rc;
-    rc = make_limb_map(&tmB, lb, 2 * d.batch, d.n, ld);
+    rc = make_limb_map(&tmB, lb, 2 * (b_mod ? b_mod : d.batch), d.n, ld);
     if (rc) return rc;
     TileParams tp;
+    tp.b_mod = b_mod;
     tp.batch = static_cast<int>(d.batch);
     tp.tiles_m = static_cast<int>(ceil_div(d.m, BM));
     tp.tiles_n = static_cast<int>(ceil_div(d.n, BN));
@@ -732,6 +691,29 @@ int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t str
 }
 
 }  // namespace
+
+// Internal entry used by the conv path: GEMM on prepared limbs where the B
+// operand (weights) has b_mod slices shared across the batch, the output is
+// written with column stride out_sn (NCHW from a pixels x channels tile) and
+// the bias is indexed per group.
+int qgemm_limbs_ex(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb,
+                   const float* amax_a, const float* amax_b, int b_mod, int64_t out_sn,
+                   int64_t bias_mod, cudaStream_t stream) {
+    int rc = validate(d);
+    if (rc) return rc;
+    if (d.batch == 0 || d.m == 0 || d.n == 0) return TK_OK;
+    TK_CHECK_ARG(d.k > 0, "qgemm: K must be positive");
+    const int64_t ld = static_cast<int64_t>(round_up(static_cast<size_t>(d.k), 16));
+    EpiParams ep = make_epi(d, amax_a, amax_b, nullptr);
+    ep.out_sn = out_sn;
+    ep.bias_mod = bias_mod;
+    if (out_sn != 1) ep.vec_store = false;
+    const size_t es = dtype_size(d.dtype);
+    ep.bias_vec = d.bias != nullptr && reinterpret_cast<uintptr_t>(d.bias) % 16 == 0 &&
+                  (bias_mod == 0 || (d.n * static_cast<int64_t>(es)) % 16 == 0);
+    return launch_tc(d, la, lb, ld, ep, stream, b_mod);
+}
+
 }  // namespace tk
 
 extern "C" {

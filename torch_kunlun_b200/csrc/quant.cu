@@ -9,26 +9,12 @@
 // element through a 64x64 shared-memory tile so that either operand layout
 // (K-contiguous or transposed) is read and written coalesced.
 #include "tk_internal.h"
+#include "tk_numerics.cuh"
 
 namespace tk {
 namespace {
 
 constexpr int kAmaxThreads = 256;
-
-// Quantisation contract (identical on every path of this library):
-//   inv = 32767 / amax (IEEE fp32 division), 0 when amax is 0/NaN/Inf;
-//   q   = clamp(rint_even(x * inv), -32767, 32767), NaN products give 0.
-__device__ __forceinline__ float quant_inv(float amax) {
-    return (amax > 0.0f && amax != __int_as_float(0x7F800000)) ? __fdiv_rn(32767.0f, amax)
-                                                                 : 0.0f;
-}
-
-__device__ __forceinline__ int quant_one(float v, float inv) {
-    float t = __fmul_rn(v, inv);
-    if (t != t) return 0;
-    int q = __float2int_rn(t);
-    return max(-32767, min(32767, q));
-}
 
 __device__ __forceinline__ float load_f(const __half* p) { return __half2float(*p); }
 __device__ __forceinline__ float load_f(const float* p) { return *p; }

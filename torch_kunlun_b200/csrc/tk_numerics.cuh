@@ -1,0 +1,90 @@
+// tk_numerics.cuh -- the numeric contract of the int16-quantised path, shared
+// by every kernel of the library so that all paths round identically.
+//
+//   inv = 32767 / amax (IEEE fp32 division), 0 when amax is 0, NaN or Inf
+//   q   = clamp(rint_even(x * inv), -32767, 32767), NaN products give 0
+//   s   = fp64(amax_a) * fp64(amax_b) / 32767^2 (one fp64 rounding)
+//   r   = T(fp64(acc) * s)  with acc the exact integer dot product
+// followed by the reference's separately rounded post-ops.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include <cstdint>
+
+#include "../../include/tk_kernels.h"
+
+namespace tk {
+
+__device__ __forceinline__ float quant_inv(float amax) {
+    return (amax > 0.0f && amax != __int_as_float(0x7F800000)) ? __fdiv_rn(32767.0f, amax) : 0.0f;
+}
+
+__device__ __forceinline__ int quant_one(float v, float inv) {
+    const float t = __fmul_rn(v, inv);
+    if (t != t) return 0;
+    return max(-32767, min(32767, __float2int_rn(t)));
+}
+
+__device__ __forceinline__ double dequant_scale(float amax_a, float amax_b) {
+    return __ddiv_rn(__dmul_rn(static_cast<double>(amax_a), static_cast<double>(amax_b)),
+                     1073676289.0);
+}
+
+// binary64 -> binary16, nearest-even, through the round-to-odd binary32
+// intermediate of Boldo & Melquiond ("When double rounding is odd", 2005):
+// rounding toward zero to binary32 and setting the last bit when inexact,
+// then rounding to nearest binary16, equals one correct rounding because
+// binary32 carries at least two more significand bits than binary16.
+__device__ __forceinline__ float d2f_round_odd(double d) {
+    float f = __double2float_rz(d);
+    if (static_cast<double>(f) != d) f = __uint_as_float(__float_as_uint(f) | 1u);
+    return f;
+}
+
+// Round a binary64 value to the output type (0 = fp16, 1 = fp32), returned
+// widened to fp32 (exactly).
+__device__ __forceinline__ float round_t_from_double(double d, int dtype) {
+    if (dtype == 0) return __half2float(__float2half_rn(d2f_round_odd(d)));
+    return __double2float_rn(d);
+}
+
+__device__ __forceinline__ float round_t(float v, int dtype) {
+    return dtype == 0 ? __half2float(__float2half_rn(v)) : v;
+}
+
+__device__ __forceinline__ float load_t(const void* p, int dtype, int64_t i) {
+    return dtype == 0 ? __half2float(static_cast<const __half*>(p)[i])
+                      : static_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ void store_t(void* p, int dtype, int64_t i, float v) {
+    if (dtype == 0)
+        static_cast<__half*>(p)[i] = __float2half_rn(v);
+    else
+        static_cast<float*>(p)[i] = v;
+}
+
+__device__ __forceinline__ float gelu_erf(float x) {
+    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+    const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+    return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+// Activation applied to an already T-rounded value; result rounded to T.
+__device__ __forceinline__ float apply_act(float r, int act, int dtype) {
+    switch (act) {
+        case TK_ACT_RELU: return (r > 0.0f || r != r) ? r : 0.0f;
+        case TK_ACT_GELU: return round_t(gelu_erf(r), dtype);
+        case TK_ACT_GELU_TANH: return round_t(gelu_tanh(r), dtype);
+        case TK_ACT_SILU: return round_t(silu_f(r), dtype);
+        default: return r;
+    }
+}
+
+}  // namespace tk

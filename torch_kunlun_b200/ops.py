@@ -1,0 +1,32 @@
+"""Fused operators of the kunlun backend that have no single aten name.
+
+* ``linear(x, w, b, act)`` -- act(x @ w^T + b) in one quantised GEMM launch;
+  the activation is applied to the rounded, bias-added output, i.e. the same
+  values the reference produces with linear followed by a separate
+  relu / gelu / silu launch (csrc/ops.cpp:480-495, :151-160,
+  csrc/ops_nn.cpp:132-147, csrc/ops_extra.cpp:71).
+* ``silu_mul(gate, up)`` -- T(silu(gate)) * up, the gated-MLP product, in one
+  elementwise pass.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _C
+
+ACT = {"none": 0, "relu": 1, "gelu": 2, "gelu_tanh": 3, "silu": 4}
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
+           act: str = "none") -> torch.Tensor:
+    return _C.linear_act(x, weight, bias, ACT[act])
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    return _C.silu_mul(gate, up)
+
+
+__all__ = ["linear", "silu_mul", "ACT"]
