@@ -1,0 +1,371 @@
+"""Benchmark of the int16-quantised dense-op path on B200.
+
+Default workload (one GPU): the single int16-quantised linear of torch_kunlun,
+y = x @ W^T + b with x fp16 [2048, 4096] ~ N(0,1), W fp16 [4096, 4096] ~
+N(0,0.02), b fp16 [4096] ~ N(0,0.01) (seed 0), called as
+torch.nn.functional.linear on kunlun tensors: per-tensor max-abs int16
+quantisation of x and W, exact integer MAC, dequantisation and bias.
+A step is one such call.  Metric: effective int16 TOPS = 2*M*N*K / step time.
+
+Arms:
+  default            kunlun device (hand-written sm_100a kernels)
+  --impl reference   the reference path on the host cores: the oracle's CPU
+                     restatement of the quantised fc (oracle/oracle.py)
+
+Multi-GPU (--gpus N under torchrun): the linear does not shard (replicas
+only); every rank runs the same workload on its own GPU, ranks meet at a
+barrier around the timed region and the slowest rank's time is reported;
+value is the aggregate over ranks ("scaling": "weak").
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+M, N, K = 2048, 4096, 4096
+OPS_PER_STEP = 2 * M * N * K
+METRIC = "int16-quant linear effective TOPS/GPU (aggregate over GPUs)"
+WORKLOAD = "int16-quantised linear x[2048,4096] @ W[4096,4096]^T + b, fp16 in/out"
+KERNELS_PER_STEP = 5  # amax(x), amax(W), quantise(x), quantise(W), limb GEMM + epilogue
+
+
+def make_inputs():
+    import torch
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(M, K, generator=g).half()
+    w = (torch.randn(N, K, generator=g) * 0.02).half()
+    b = (torch.randn(N, generator=g) * 0.01).half()
+    return x, w, b
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
+            int(os.environ.get("WORLD_SIZE", "1")))
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"tk_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        try:
+            rows = [l.split(",") for l in open(self.path).read().strip().splitlines() if l.strip()]
+        except Exception:
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def timed_steps(step, steps, warmup, flush, kunlun, stream=None):
+    """Per-step device time with CUDA events on the launching stream; the L2
+    flush between steps is outside the events."""
+    for _ in range(warmup):
+        step()
+        flush()
+    kunlun.synchronize()
+    times = []
+    for _ in range(steps):
+        e0 = kunlun.Event(enable_timing=True)
+        e1 = kunlun.Event(enable_timing=True)
+        e0.record(stream)
+        step()
+        e1.record(stream)
+        flush()
+        times.append((e0, e1))
+    kunlun.synchronize()
+    return [a.elapsed_time(b) for a, b in times]
+
+
+def kernel_breakdown(xd, wd, bd, out, kunlun, flush, iters=10):
+    """Average device time of each kernel of one step, launched through the C
+    ABI on the same stream with the same operands (events per kernel)."""
+    import torch
+    from torch_kunlun_b200 import _capi as C
+    L = C.lib()
+    stream = kunlun.current_stream().stream_id
+    dev = xd.device
+    ld = (K + 15) // 16 * 16
+    la = torch.empty(2 * M * ld, dtype=torch.int8, device=dev)
+    lb = torch.empty(2 * N * ld, dtype=torch.int8, device=dev)
+    amax = torch.empty(2, dtype=torch.float32, device=dev)
+    d = C.QGemmDesc()
+    d.dtype = C.TK_DTYPE_F16
+    d.batch, d.m, d.n, d.k = 1, M, N, K
+    d.out = out.data_ptr()
+    d.out_sb, d.out_sm = M * N, N
+    d.bias = bd.data_ptr()
+    d.alpha, d.beta, d.act, d.per_slice_scales = 1.0, 0.0, 0, 1
+    stages = {
+        "amax": lambda: (C.check(L.tk_amax(0, xd.data_ptr(), 1, 0, M * K, amax.data_ptr(), stream), "amax"),
+                         C.check(L.tk_amax(0, wd.data_ptr(), 1, 0, N * K, amax.data_ptr() + 4, stream), "amax")),
+        "quantise": lambda: (C.check(L.tk_quantize_limbs(0, xd.data_ptr(), 1, M, K, 0, K, 1, amax.data_ptr(), 0,
+                                                         la.data_ptr(), stream), "q"),
+                             C.check(L.tk_quantize_limbs(0, wd.data_ptr(), 1, N, K, 0, K, 1, amax.data_ptr() + 4,
+                                                         0, lb.data_ptr(), stream), "q")),
+        "gemm": lambda: C.check(L.tk_qgemm_from_limbs(ctypes.byref(d), la.data_ptr(), lb.data_ptr(),
+                                                      amax.data_ptr(), amax.data_ptr() + 4, stream), "gemm"),
+    }
+    res = {}
+    for name in ("amax", "quantise", "gemm"):
+        stages["amax"](); stages["quantise"]()
+        ts = timed_steps(stages[name], iters, 3, flush, kunlun)
+        res[name] = sum(ts) / len(ts)
+    return res
+
+
+def measured_int8_peak_tops(torch):
+    """cuBLASLt int8 GEMM (torch._int_mm) at 8192^3, best of 5 (burst)."""
+    n = 8192
+    a = torch.randint(-128, 127, (n, n), dtype=torch.int8, device="cuda")
+    b = torch.randint(-128, 127, (n, n), dtype=torch.int8, device="cuda").t()
+    for _ in range(3):
+        torch._int_mm(a, b)
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(5):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch._int_mm(a, b)
+        e.record()
+        torch.cuda.synchronize()
+        best = min(best, s.elapsed_time(e))
+    del a, b
+    torch.cuda.empty_cache()
+    return 2 * n ** 3 / best / 1e9
+
+
+def ncu_traffic():
+    """dram bytes per GEMM launch from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", "qgemm_linear_2048x4096x4096.md")
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1].strip())
+    except Exception:
+        pass
+    return None
+
+
+def oracle_sample(rows=256, reps=1):
+    """The oracle's CPU restatement of the quantised fc on a row sample of x
+    (all of W): returns (seconds per sample, ops per sample)."""
+    import numpy as np
+    from oracle import oracle as O
+    x, w, b = make_inputs()
+    xs, wn, bn = x[:rows].numpy(), w.numpy(), b.numpy()
+    O.linear(xs[:8, :64].copy(), wn[:16, :64].copy(), None)  # build / warm the library
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.linear(xs, wn, bn)
+    dt = (time.perf_counter() - t0) / reps
+    return dt, 2 * rows * N * K
+
+
+def run_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return 0
+    import numpy as np  # noqa: F401
+    cores = os.cpu_count() or 1
+    rows = 256
+    for _ in range(max(1, args.warmup)):
+        oracle_sample(rows, 1)
+    times = []
+    for _ in range(args.steps):
+        dt, ops = oracle_sample(rows, 1)
+        times.append(dt)
+    ms = 1000 * statistics.mean(times)
+    value = ops / (ms / 1000) / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int16",
+        "data": "synthetic (seeded N(0,1)/N(0,0.02)/N(0,0.01), no dataset)",
+        "config": {"workload": WORKLOAD, "sample": f"x rows 0..{rows} of {M}, all of W",
+                   "parallelism": "replicas only"},
+        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": cores, "kind": "port",
+                         "sample": f"{rows} of {M} rows of x with all of W per step "
+                                   "(oracle: C quantise + exact fp64 BLAS GEMM + C epilogue)"},
+        "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="kunlun", choices=["kunlun", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    args.warmup = max(args.warmup, 3)
+
+    import torch
+    import torch_kunlun  # noqa: F401
+    kunlun = torch_kunlun.kunlun
+
+    rank, local_rank, world = dist_env()
+    kunlun.set_device(local_rank)
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("kunlun", local_rank)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+        pg = dist
+
+    x, w, b = make_inputs()
+    xd, wd, bd = x.to(dev), w.to(dev), b.to(dev)
+    out = torch.empty(M, N, dtype=torch.float16, device=dev)
+    scratch = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
+
+    def flush():
+        scratch.fill_(1)
+
+    def step():
+        torch.nn.functional.linear(xd, wd, bd)
+
+    if pg:
+        pg.barrier()
+    kunlun.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        times = timed_steps(step, args.steps, args.warmup, flush, kunlun)
+    kunlun.synchronize()
+    if pg:
+        pg.barrier()
+    ms = sum(times) / len(times)
+    clock = clocks.summary()
+
+    # end-to-end through the public API with host buffers: pinned H2D of the
+    # step's inputs, the op, D2H of the result, all inside the timed events
+    xh, wh, bh = x.pin_memory(), w.pin_memory(), b.pin_memory()
+    yh = torch.empty(M, N, dtype=torch.float16).pin_memory()
+    xe = torch.empty_like(xd)
+    we = torch.empty_like(wd)
+    be = torch.empty_like(bd)
+
+    def e2e_step():
+        xe.copy_(xh, non_blocking=True)
+        we.copy_(wh, non_blocking=True)
+        be.copy_(bh, non_blocking=True)
+        y = torch.nn.functional.linear(xe, we, be)
+        yh.copy_(y, non_blocking=True)
+
+    e2e_times = timed_steps(e2e_step, args.steps, args.warmup, flush, kunlun)
+    e2e_ms = sum(e2e_times) / len(e2e_times)
+
+    parts = kernel_breakdown(xd, wd, bd, out, kunlun, flush)
+
+    # max over ranks of the timed quantities
+    if pg:
+        t = torch.tensor([ms, e2e_ms, parts["gemm"]], dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms, e2e_ms, gemm_ms = t.tolist()
+    else:
+        gemm_ms = parts["gemm"]
+
+    int8_peak = measured_int8_peak_tops(torch) if rank == 0 else None
+    cpu_base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        reps = []
+        for _ in range(3):
+            dt, ops = oracle_sample(256, 1)
+            reps.append(dt)
+        cpu_base = {"value": ops / statistics.mean(reps) / 1e12, "unit": "TOPS",
+                    "cores": os.cpu_count() or 1, "kind": "port",
+                    "sample": "256 of 2048 rows of x with all of W per call, 3 calls "
+                              "(oracle: C quantise + exact fp64 BLAS GEMM + C epilogue)"}
+
+    if rank == 0:
+        value = world * OPS_PER_STEP / (ms / 1000) / 1e12
+        achieved = OPS_PER_STEP / (gemm_ms / 1000) / 1e12
+        peak = int8_peak / 4.0
+        line = {
+            "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int16",
+            "data": "synthetic (seeded N(0,1)/N(0,0.02)/N(0,0.01), no dataset)",
+            "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "parallelism":
+                       "replicas only" if world > 1 else "single GPU",
+                       "l2": "flushed between steps (512 MiB device write outside the timed events)",
+                       "step_breakdown_ms": {k: round(v, 4) for k, v in parts.items()}},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TOPS", "frac": achieved / peak,
+                         "traffic": ncu_traffic(),
+                         "kernel": "qgemm_tc_kernel (tcgen05 kind::i8, 4 limb MMAs per int16 MAC)",
+                         "peak_source": f"int8 dense {int8_peak:.0f} TOPS measured live (cuBLASLt "
+                                        "int8 8192^3 via torch._int_mm, burst) / 4 limb MMAs"},
+            "e2e": {"value": world * OPS_PER_STEP / (e2e_ms / 1000) / 1e12, "unit": "TOPS",
+                    "h2d_bytes_per_step": int(xh.nbytes + wh.nbytes + bh.nbytes),
+                    "d2h_bytes_per_step": int(yh.nbytes)},
+            "gpu_launches": KERNELS_PER_STEP * args.steps,
+            "clocks": clock,
+            "cpu_baseline": cpu_base,
+        }
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
