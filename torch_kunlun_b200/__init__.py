@@ -27,7 +27,7 @@ _KERNEL_LIB = os.path.join(_HERE, "libtk_kernels.so")
 if not os.path.exists(_KERNEL_LIB):
     raise ImportError(
         f"torch_kunlun_b200: {_KERNEL_LIB} is missing; build the native libraries with "
-        "`python -m torch_kunlun_b200._build`")
+        "`python torch_kunlun_b200/_build.py`")
 # _C links libtk_kernels.so by soname; load it first so the link resolves
 # wherever the package directory lives.
 _kernels = ctypes.CDLL(_KERNEL_LIB, mode=ctypes.RTLD_GLOBAL)

@@ -6,7 +6,9 @@
   the ``kunlun`` device and calls the C ABI.
 
 Both land next to this file so they travel with the source tree; nothing is
-installed into site-packages.  Run ``python -m torch_kunlun_b200._build``.
+installed into site-packages.  Run it as a script,
+``python torch_kunlun_b200/_build.py [--force]``, so that the package (and a
+possibly stale extension) is not imported while the extension is rebuilt.
 """
 
 from __future__ import annotations
