@@ -117,6 +117,11 @@ void destroy_stream(int device, int64_t id) {
     cudaStreamDestroy(s);
 }
 
+void require_live(int64_t id) {
+    TORCH_CHECK(stream_is_live(stream_handle(id)), "kunlun: stream ", id,
+                " was destroyed or was not created by this backend");
+}
+
 void set_current_stream(int device, int64_t id) {
     if (device < 0) device = current_device();
     if (static_cast<size_t>(device) >= t_current.size()) t_current.resize(device + 1, 0);
@@ -124,11 +129,13 @@ void set_current_stream(int device, int64_t id) {
 }
 
 void synchronize_stream(int device, int64_t id) {
+    require_live(id);
     DeviceRestore g(device);
     check_cuda(cudaStreamSynchronize(stream_handle(id)), "cudaStreamSynchronize");
 }
 
 bool stream_query(int device, int64_t id) {
+    require_live(id);
     DeviceRestore g(device);
     cudaError_t e = cudaStreamQuery(stream_handle(id));
     if (e == cudaErrorNotReady) {
@@ -162,12 +169,14 @@ void event_destroy(int64_t id) {
 }
 
 void event_record(int64_t ev, int device, int64_t stream_id) {
+    require_live(stream_id);
     DeviceRestore g(device);
     check_cuda(cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev), stream_handle(stream_id)),
                "cudaEventRecord");
 }
 
 void stream_wait_event(int device, int64_t stream_id, int64_t ev) {
+    require_live(stream_id);
     DeviceRestore g(device);
     check_cuda(cudaStreamWaitEvent(stream_handle(stream_id), reinterpret_cast<cudaEvent_t>(ev), 0),
                "cudaStreamWaitEvent");

@@ -138,7 +138,10 @@ def _device_index(device) -> int:
 
 
 _PRIVATEUSE1_DEVICE_TYPE = int(torch._C._autograd.DeviceType.PrivateUse1.value)
-_OWNED_STREAMS = set()
+# (device, stream id) -> id() of the one Stream object that owns (and will
+# destroy) the stream; wrappers of the same stream made by current_stream()
+# and friends do not own it.
+_OWNED_STREAMS = {}
 
 
 class Stream(torch.Stream):
@@ -154,7 +157,7 @@ class Stream(torch.Stream):
         raw_id = int(_C.create_stream(index, int(priority))) if owned else int(stream_id)
         obj = super().__new__(cls, raw_id, index, _PRIVATEUSE1_DEVICE_TYPE)
         if owned:
-            _OWNED_STREAMS.add((index, raw_id))
+            _OWNED_STREAMS[(index, raw_id)] = id(obj)
         return obj
 
     def __init__(self, device=None, stream_id=None, priority: int = 0):
@@ -186,8 +189,8 @@ class Stream(torch.Stream):
     def __del__(self):
         try:
             key = (int(self.device_index), int(self.stream_id))
-            if key in _OWNED_STREAMS:
-                _OWNED_STREAMS.discard(key)
+            if _OWNED_STREAMS.get(key) == id(self):
+                del _OWNED_STREAMS[key]
                 _C.destroy_stream(*key)
         except Exception:
             pass
