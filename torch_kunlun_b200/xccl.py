@@ -170,7 +170,10 @@ class ProcessGroupXCCL(dist.ProcessGroup):
     def __init__(self, store, rank: int, size: int, timeout=None, engine_factory=None):
         if store is None:
             raise ValueError("ProcessGroupXCCL requires a c10d Store")
-        super().__init__(store, int(rank), int(size))
+        # torch 2.11 builds Python ProcessGroup subclasses through the
+        # (rank, size) constructor; the store is kept for the id exchange.
+        super().__init__(int(rank), int(size))
+        self._store = store
         self._rank = int(rank)
         self._size = int(size)
         factory = engine_factory or type(self).engine_factory
