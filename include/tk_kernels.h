@@ -144,6 +144,21 @@ TK_API int tk_qgemm_from_limbs(const tk_qgemm_desc_t* desc, const int8_t* a_limb
                                const int8_t* b_limbs, const float* amax_a, const float* amax_b,
                                void* stream);
 
+/* tk_qgemm for callers that cannot allocate device memory (for example a
+ * host application or inference server that owns all device memory, passes
+ * this library only its inputs and outputs, and forbids allocation after
+ * start-up).  No counterpart in the reference: XDNN's fc draws its scratch
+ * from the per-device context the reference creates.  Same contract and
+ * results as tk_qgemm, but the scratch is a fixed 64 MiB array inside the
+ * library's device image (held by every GPU that loads the library until
+ * exit), so the call allocates nothing.  Problems whose
+ * tk_qgemm_workspace_size exceeds 64 MiB - 1 KiB are rejected with
+ * TK_ERR_WORKSPACE.  All calls share the array: calls that overlap on the
+ * GPU race; calls ordered on one stream are safe.  The first call on a
+ * device does a one-time set-up (device address lookup); make it before any
+ * stream capture. */
+TK_API int tk_qgemm_noalloc(const tk_qgemm_desc_t* desc, void* stream);
+
 /* Same contract computed by a plain CUDA-core kernel (one output per thread).
  * Used to cross-check the tensor-core path on the device; not fast. */
 TK_API int tk_qgemm_simt(const tk_qgemm_desc_t* desc, void* workspace, size_t workspace_bytes,

@@ -25,7 +25,7 @@ EXPORTED = [
     "tk_quantize_limbs", "tk_qgemm_workspace_size", "tk_qgemm", "tk_qgemm_simt",
     "tk_qgemm_debug", "tk_qgemm_from_limbs", "tk_copy_strided", "tk_fill_strided",
     "tk_binary", "tk_unary", "tk_silu_mul", "tk_conv2d_workspace_size", "tk_conv2d_q16",
-    "tk_softmax", "tk_layer_norm",
+    "tk_softmax", "tk_layer_norm", "tk_qgemm_noalloc",
 ]
 
 
@@ -61,7 +61,7 @@ def lib() -> ctypes.CDLL:
         if not os.path.exists(LIB_PATH):
             raise RuntimeError(
                 f"torch_kunlun_b200: {LIB_PATH} is missing; build it with "
-                "`python -m torch_kunlun_b200._build` (there is no CPU fallback)")
+                "`python torch_kunlun_b200/_build.py` (there is no CPU fallback)")
         L = ctypes.CDLL(LIB_PATH)
         vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
         L.tk_abi_version.restype = i32
@@ -74,6 +74,7 @@ def lib() -> ctypes.CDLL:
         for name in ("tk_qgemm", "tk_qgemm_simt"):
             getattr(L, name).argtypes = [ctypes.POINTER(QGemmDesc), vp, ctypes.c_size_t, vp]
         L.tk_qgemm_from_limbs.argtypes = [ctypes.POINTER(QGemmDesc), vp, vp, vp, vp, vp]
+        L.tk_qgemm_noalloc.argtypes = [ctypes.POINTER(QGemmDesc), vp]
         L.tk_qgemm_debug.argtypes = [ctypes.POINTER(QGemmDesc), vp, ctypes.c_size_t, vp, vp]
         _lib = L
     return _lib
