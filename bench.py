@@ -25,7 +25,6 @@ import ctypes
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -37,7 +36,7 @@ M, N, K = 2048, 4096, 4096
 OPS_PER_STEP = 2 * M * N * K
 METRIC = "int16-quant linear effective TOPS/GPU (aggregate over GPUs)"
 WORKLOAD = "int16-quantised linear x[2048,4096] @ W[4096,4096]^T + b, fp16 in/out"
-KERNELS_PER_STEP = 5  # amax(x), amax(W), quantise(x), quantise(W), limb GEMM + epilogue
+KERNELS_PER_STEP = 3  # amax of x and W, quantise of x and W, limb GEMM + epilogue
 
 
 def make_inputs():
@@ -55,58 +54,63 @@ def dist_env():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    """SM clock and clock-event (throttle) reasons of one GPU, polled through
+    NVML every 5 ms while the timed region runs.  The GPU is found by UUID so
+    CUDA and NVML device orderings cannot disagree."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.path = os.path.join("/tmp", f"tk_clocks_{os.getpid()}.csv")
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples = []
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(self.cuda_index).uuid)
+            h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
         except Exception:
-            self.proc = None
+            return self
+        self._stop = threading.Event()
+
+        def poll():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                         int(get_reasons(h))))
+                except Exception:
+                    pass
+                self._stop.wait(0.005)
+
+        self._thread = threading.Thread(target=poll, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        try:
-            rows = [l.split(",") for l in open(self.path).read().strip().splitlines() if l.strip()]
-        except Exception:
+        if not self.samples:
             return None
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            r = [c.strip() for c in r]
-            if len(r) < 9:
-                continue
-            try:
-                sm.append(float(r[1]))
-                mx = float(r[2])
-            except ValueError:
-                continue
-            for name, v in zip(names, r[5:9]):
-                if v.lower() == "active":
+        reasons = set()
+        for _, bits in self.samples:
+            for bit, name in self.REASONS.items():
+                if bits & bit:
                     reasons.add(name)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(c for c, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(self.samples), "source": "NVML, 5 ms"}
 
 
 def timed_steps(step, steps, warmup, flush, kunlun, stream=None):
@@ -130,8 +134,9 @@ def timed_steps(step, steps, warmup, flush, kunlun, stream=None):
 
 
 def kernel_breakdown(xd, wd, bd, out, kunlun, flush, iters=10):
-    """Average device time of each kernel of one step, launched through the C
-    ABI on the same stream with the same operands (events per kernel)."""
+    """Average device time of the step's GEMM kernel, launched through the C
+    ABI on the same stream with the same operands, quantised once beforehand
+    (CUDA events around each launch, L2 flushed between launches)."""
     import torch
     from torch_kunlun_b200 import _capi as C
     L = C.lib()
@@ -158,12 +163,10 @@ def kernel_breakdown(xd, wd, bd, out, kunlun, flush, iters=10):
         "gemm": lambda: C.check(L.tk_qgemm_from_limbs(ctypes.byref(d), la.data_ptr(), lb.data_ptr(),
                                                       amax.data_ptr(), amax.data_ptr() + 4, stream), "gemm"),
     }
-    res = {}
-    for name in ("amax", "quantise", "gemm"):
-        stages["amax"](); stages["quantise"]()
-        ts = timed_steps(stages[name], iters, 3, flush, kunlun)
-        res[name] = sum(ts) / len(ts)
-    return res
+    stages["amax"]()
+    stages["quantise"]()
+    ts = timed_steps(stages["gemm"], iters, 3, flush, kunlun)
+    return {"gemm": sum(ts) / len(ts)}
 
 
 def measured_int8_peak_tops(torch):
@@ -248,8 +251,8 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="kunlun", choices=["kunlun", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -286,7 +289,7 @@ def main():
     if pg:
         pg.barrier()
     kunlun.synchronize()
-    with ClockSampler(local_rank) as clocks:
+    with ClockSampler(torch.cuda.current_device()) as clocks:
         times = timed_steps(step, args.steps, args.warmup, flush, kunlun)
     kunlun.synchronize()
     if pg:
@@ -346,7 +349,8 @@ def main():
             "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "parallelism":
                        "replicas only" if world > 1 else "single GPU",
                        "l2": "flushed between steps (512 MiB device write outside the timed events)",
-                       "step_breakdown_ms": {k: round(v, 4) for k, v in parts.items()}},
+                       "step_breakdown_ms": {"gemm": round(gemm_ms, 4),
+                                             "amax_and_quantise": round(ms - gemm_ms, 4)}},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                          "unit": "TOPS", "frac": achieved / peak,
                          "traffic": ncu_traffic(),

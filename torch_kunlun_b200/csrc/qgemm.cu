@@ -524,33 +524,20 @@ bool slice_dense(int64_t rows, int64_t cols, int64_t sr, int64_t sc) {
     return (sr == cols && sc == 1) || (sr == 1 && sc == rows);
 }
 
-// Quantise one operand ([batch][rows][cols] strided view) into limb planes.
-int quantise_operand(tk_dtype_t dt, const void* x, int64_t batch, int64_t rows, int64_t cols,
-                     int64_t sb, int64_t sr, int64_t sc, bool per_slice, const float* given_amax,
-                     float* amax_ws, int8_t* limbs, cudaStream_t stream, const char* name) {
-    const float* amax = given_amax;
-    if (amax == nullptr) {
-        if (rows * cols > 0) {
-            if (!slice_dense(rows, cols, sr, sc))
-                TK_FAIL(TK_ERR_UNSUPPORTED,
-                        "qgemm: operand %s slices must be dense (row- or column-major)", name);
-            if (per_slice) {
-                int rc = amax_launch(dt, x, batch, sb, rows * cols, amax_ws, stream);
-                if (rc) return rc;
-            } else {
-                if (batch > 1 && sb != rows * cols)
-                    TK_FAIL(TK_ERR_UNSUPPORTED,
-                            "qgemm: operand %s must be one dense block for a shared scale", name);
-                int rc = amax_launch(dt, x, 1, 0, batch * rows * cols, amax_ws, stream);
-                if (rc) return rc;
-            }
-        } else {
-            TK_CUDA_TRY(cudaMemsetAsync(amax_ws, 0, sizeof(float) * (per_slice ? batch : 1), stream));
-        }
-        amax = amax_ws;
-    }
-    return quantize_limbs_launch(dt, x, batch, rows, cols, sb, sr, sc, amax, per_slice ? 1 : 0,
-                                 limbs, stream);
+// An operand whose amax is computed by the call must be laid out densely:
+// every slice a row- or column-major block and, for one shared scale, the
+// slices one contiguous block.
+int check_dense(const void* x, int64_t batch, int64_t rows, int64_t cols, int64_t sb, int64_t sr,
+                int64_t sc, bool per_slice, const float* given_amax, const char* name) {
+    if (given_amax != nullptr || rows * cols == 0) return TK_OK;
+    TK_CHECK_ARG(x != nullptr, "qgemm: operand %s is NULL", name);
+    if (!slice_dense(rows, cols, sr, sc))
+        TK_FAIL(TK_ERR_UNSUPPORTED, "qgemm: operand %s slices must be dense (row- or column-major)",
+                name);
+    if (!per_slice && batch > 1 && sb != rows * cols)
+        TK_FAIL(TK_ERR_UNSUPPORTED, "qgemm: operand %s must be one dense block for a shared scale",
+                name);
+    return TK_OK;
 }
 
 EpiParams make_epi(const tk_qgemm_desc_t& d, const float* amax_a, const float* amax_b,
@@ -663,15 +650,20 @@ int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t str
     int8_t* la = reinterpret_cast<int8_t*>(w + L.off_la);
     int8_t* lb = reinterpret_cast<int8_t*>(w + L.off_lb);
     const bool per = d.per_slice_scales != 0;
+    // Both amax slots are cleared with one memset (they are adjacent), then one
+    // launch reduces every amax that was not given and one quantises both
+    // row-contiguous operands.
+    TK_CUDA_TRY(cudaMemsetAsync(amax_a, 0, L.off_la, stream));
     if (d.k > 0) {
-        rc = quantise_operand(d.dtype, d.a, d.batch, d.m, d.k, d.a_sb, d.a_sm, d.a_sk, per,
-                              d.amax_a, amax_a, la, stream, "A");
+        rc = check_dense(d.a, d.batch, d.m, d.k, d.a_sb, d.a_sm, d.a_sk, per, d.amax_a, "A");
         if (rc) return rc;
-        rc = quantise_operand(d.dtype, d.b, d.batch, d.n, d.k, d.b_sb, d.b_sn, d.b_sk, per,
-                              d.amax_b, amax_b, lb, stream, "B");
+        rc = check_dense(d.b, d.batch, d.n, d.k, d.b_sb, d.b_sn, d.b_sk, per, d.amax_b, "B");
         if (rc) return rc;
-    } else {
-        TK_CUDA_TRY(cudaMemsetAsync(amax_a, 0, L.off_la, stream));
+        QuantOperand ops[2] = {
+            {d.a, d.batch, d.m, d.k, d.a_sb, d.a_sm, d.a_sk, per, d.amax_a, amax_a, la},
+            {d.b, d.batch, d.n, d.k, d.b_sb, d.b_sn, d.b_sk, per, d.amax_b, amax_b, lb}};
+        rc = quantise_operands(d.dtype, ops, 2, stream);
+        if (rc) return rc;
     }
     const float* sa = (d.k > 0 && d.amax_a) ? d.amax_a : amax_a;
     const float* sb = (d.k > 0 && d.amax_b) ? d.amax_b : amax_b;

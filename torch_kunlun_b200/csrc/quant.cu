@@ -154,6 +154,185 @@ quant_limbs_kernel(const T* __restrict__ x, int64_t rows, int64_t cols, int64_t 
     }
 }
 
+
+// ---- fused multi-operand paths used by the GEMM ------------------------------
+
+// One amax descriptor: nslices dense ranges of slice_len elements.
+struct AmaxDesc {
+    const void* x;
+    int64_t nslices, slice_stride, slice_len, chunk, chunks;  // chunks per slice
+    unsigned* out;
+    bool vec;
+};
+
+template <typename T>
+__device__ __forceinline__ unsigned amax_range(const T* base, int64_t start, int64_t end, bool vec);
+
+template <>
+__device__ __forceinline__ unsigned amax_range<__half>(const __half* xh, int64_t start, int64_t end,
+                                                       bool vec) {
+    const unsigned short* base = reinterpret_cast<const unsigned short*>(xh);
+    unsigned m2 = 0;
+    int64_t i = start;
+    if (vec) {
+        const int64_t nv = (end - start) / 8;
+        const uint4* pv = reinterpret_cast<const uint4*>(base + start);
+        int64_t j = threadIdx.x;
+        for (; j + 3 * static_cast<int64_t>(blockDim.x) < nv; j += 4 * blockDim.x) {
+            uint4 w[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) w[u] = __ldg(pv + j + u * blockDim.x);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                m2 = __vmaxu2(m2, w[u].x & 0x7FFF7FFFu);
+                m2 = __vmaxu2(m2, w[u].y & 0x7FFF7FFFu);
+                m2 = __vmaxu2(m2, w[u].z & 0x7FFF7FFFu);
+                m2 = __vmaxu2(m2, w[u].w & 0x7FFF7FFFu);
+            }
+        }
+        for (; j < nv; j += blockDim.x) {
+            const uint4 w = __ldg(pv + j);
+            m2 = __vmaxu2(m2, w.x & 0x7FFF7FFFu);
+            m2 = __vmaxu2(m2, w.y & 0x7FFF7FFFu);
+            m2 = __vmaxu2(m2, w.z & 0x7FFF7FFFu);
+            m2 = __vmaxu2(m2, w.w & 0x7FFF7FFFu);
+        }
+        i = start + nv * 8;
+    }
+    for (int64_t j = i + threadIdx.x; j < end; j += blockDim.x)
+        m2 = __vmaxu2(m2, static_cast<unsigned>(base[j] & 0x7FFFu));
+    const unsigned h = max(m2 & 0xFFFFu, m2 >> 16);
+    // widen the fp16 magnitude bits to the fp32 magnitude bits (NaN -> canonical)
+    if ((h & 0x7C00u) == 0x7C00u && (h & 0x3FFu) != 0u) return 0x7FC00000u;
+    return __float_as_uint(__half2float(__ushort_as_half(static_cast<unsigned short>(h)))) & 0x7FFFFFFFu;
+}
+
+template <>
+__device__ __forceinline__ unsigned amax_range<float>(const float* xf, int64_t start, int64_t end,
+                                                      bool vec) {
+    const unsigned* base = reinterpret_cast<const unsigned*>(xf);
+    unsigned m = 0;
+    int64_t i = start;
+    if (vec) {
+        const int64_t nv = (end - start) / 4;
+        const uint4* pv = reinterpret_cast<const uint4*>(base + start);
+        for (int64_t j = threadIdx.x; j < nv; j += blockDim.x) {
+            const uint4 w = __ldg(pv + j);
+            m = max(m, max(max(w.x & 0x7FFFFFFFu, w.y & 0x7FFFFFFFu),
+                           max(w.z & 0x7FFFFFFFu, w.w & 0x7FFFFFFFu)));
+        }
+        i = start + nv * 4;
+    }
+    for (int64_t j = i + threadIdx.x; j < end; j += blockDim.x) m = max(m, base[j] & 0x7FFFFFFFu);
+    return m;
+}
+
+// Blocks [0, blocks0) reduce descriptor d0, the rest d1.  Each block takes one
+// chunk of one slice and folds its maximum into out[slice] with atomicMax on
+// the fp32 magnitude bits (the order of non-negative floats, NaN on top).
+template <typename T>
+__global__ void __launch_bounds__(kAmaxThreads)
+amax_multi_kernel(AmaxDesc d0, AmaxDesc d1, int64_t blocks0) {
+    int64_t b = blockIdx.x;
+    const AmaxDesc& d = b < blocks0 ? d0 : d1;
+    if (b >= blocks0) b -= blocks0;
+    const int64_t slice = b / d.chunks;
+    const int64_t c = b - slice * d.chunks;
+    const int64_t start = c * d.chunk;
+    const int64_t end = min(start + d.chunk, d.slice_len);
+    const T* base = static_cast<const T*>(d.x) + slice * d.slice_stride;
+    unsigned m = amax_range<T>(base, start, end, d.vec);
+    m = block_max_u32(m);
+    if (threadIdx.x == 0 && m != 0u) atomicMax(d.out + slice, m);
+}
+
+// Row-contiguous operand quantised 8 columns per thread: one 128-bit load
+// (two for fp32) and two 64-bit limb stores per step.
+struct QVecDesc {
+    const void* x;
+    int64_t rows, cols, ld, sb, sr;
+    int64_t groups;  // ld / 8
+    int64_t items;   // batch * rows * groups
+    const float* amax;
+    int64_t amax_stride;
+    int8_t* limbs;
+};
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, int64_t n, float (&v)[8]);
+
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, int64_t n, float (&v)[8]) {
+    if (n >= 8) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4*>(p));
+        const __half2* h = reinterpret_cast<const __half2*>(&w);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(h[j]);
+            v[2 * j] = f.x;
+            v[2 * j + 1] = f.y;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = j < n ? __half2float(p[j]) : 0.0f;
+    }
+}
+
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, int64_t n, float (&v)[8]) {
+    if (n >= 8) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = j < n ? p[j] : 0.0f;
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void quant_vec_item(const QVecDesc& d, int64_t i) {
+    const int64_t g = i % d.groups;
+    const int64_t rr = i / d.groups;
+    const int64_t r = rr % d.rows;
+    const int64_t b = rr / d.rows;
+    const int64_t c0 = g * 8;
+    float v[8];
+    const int64_t n = d.cols - c0;
+    if (n > 0) {
+        load8<T>(static_cast<const T*>(d.x) + b * d.sb + r * d.sr + c0, n, v);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+    }
+    const float inv = quant_inv(d.amax[b * d.amax_stride]);
+    unsigned hi0 = 0, hi1 = 0, lo0 = 0, lo1 = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int q = quant_one(v[j], inv);
+        const unsigned h = (static_cast<unsigned>(q >> 8) & 0xFFu) << (8 * (j & 3));
+        const unsigned l = (static_cast<unsigned>(q) & 0xFFu) << (8 * (j & 3));
+        if (j < 4) { hi0 |= h; lo0 |= l; } else { hi1 |= h; lo1 |= l; }
+    }
+    const int64_t plane = d.rows * d.ld;
+    int8_t* dst = d.limbs + (b * 2) * plane + r * d.ld + c0;
+    *reinterpret_cast<uint2*>(dst) = make_uint2(hi0, hi1);
+    *reinterpret_cast<uint2*>(dst + plane) = make_uint2(lo0, lo1);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) quant_vec_kernel(QVecDesc d0, QVecDesc d1) {
+    const int64_t total = d0.items + d1.items;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        if (i < d0.items)
+            quant_vec_item<T>(d0, i);
+        else
+            quant_vec_item<T>(d1, i - d0.items);
+    }
+}
+
 }  // namespace
 
 int amax_launch(tk_dtype_t dtype, const void* x, int64_t nslices, int64_t slice_stride,
@@ -224,6 +403,105 @@ int quantize_limbs_launch(tk_dtype_t dtype, const void* x, int64_t batch, int64_
                 xp, rows, cols, ld, sb, sr, sc, amax, amax_stride, limbs);
     }
     return launch_status("quantize_limbs");
+}
+
+
+bool quant_vec_ok(tk_dtype_t dt, const QuantOperand& o) {
+    const int64_t es = static_cast<int64_t>(dtype_size(dt));
+    if (o.sc != 1 && o.cols > 1) return false;
+    if (reinterpret_cast<uintptr_t>(o.x) % 16 != 0) return false;
+    if ((o.sr * es) % 16 != 0 && o.rows > 1) return false;
+    if ((o.sb * es) % 16 != 0 && o.batch > 1) return false;
+    return true;
+}
+
+// Quantise up to two operands for one GEMM: one launch computes every amax
+// that is not given, one launch quantises every row-contiguous operand, and
+// any transposed operand goes through the shared-memory tile kernel.  The
+// caller has zeroed the amax slots.
+int quantise_operands(tk_dtype_t dt, const QuantOperand* ops, int nops, cudaStream_t stream) {
+    TK_CHECK_ARG(nops >= 1 && nops <= 2, "quantise_operands: 1 or 2 operands");
+    const int dev = current_device();
+    AmaxDesc ad[2] = {};
+    int64_t ablocks[2] = {0, 0};
+    for (int i = 0; i < nops; ++i) {
+        const QuantOperand& o = ops[i];
+        if (o.given_amax != nullptr || o.batch * o.rows * o.cols == 0) continue;
+        AmaxDesc& d = ad[i];
+        d.x = o.x;
+        d.out = reinterpret_cast<unsigned*>(o.amax_out);
+        if (o.per_slice) {
+            d.nslices = o.batch;
+            d.slice_stride = o.sb;
+            d.slice_len = o.rows * o.cols;
+        } else {
+            d.nslices = 1;
+            d.slice_stride = 0;
+            d.slice_len = o.batch * o.rows * o.cols;
+        }
+        const int64_t per_block = static_cast<int64_t>(kAmaxThreads) * 64;
+        int64_t chunks = ceil_div(d.slice_len, per_block);
+        const int64_t want = std::max<int64_t>(1, (8LL * sm_count(dev)) / d.nslices);
+        chunks = std::max<int64_t>(1, std::min(chunks, want));
+        d.chunk = (ceil_div(d.slice_len, chunks) + 7) / 8 * 8;
+        d.chunks = ceil_div(d.slice_len, d.chunk);
+        const size_t es = dtype_size(dt);
+        d.vec = reinterpret_cast<uintptr_t>(o.x) % 16 == 0 &&
+                ((d.slice_stride * static_cast<int64_t>(es)) % 16 == 0);
+        ablocks[i] = d.nslices * d.chunks;
+    }
+    if (ablocks[0] + ablocks[1] > 0) {
+        const AmaxDesc& first = ablocks[0] ? ad[0] : ad[1];
+        const AmaxDesc& second = ablocks[0] ? ad[1] : ad[0];
+        const int64_t b0 = ablocks[0] ? ablocks[0] : ablocks[1];
+        const int64_t total = ablocks[0] + ablocks[1];
+        TK_CHECK_ARG(total < (1LL << 31), "quantise: too many amax blocks");
+        if (dt == TK_DTYPE_F16)
+            amax_multi_kernel<__half><<<static_cast<unsigned>(total), kAmaxThreads, 0, stream>>>(
+                first, second, b0);
+        else
+            amax_multi_kernel<float><<<static_cast<unsigned>(total), kAmaxThreads, 0, stream>>>(
+                first, second, b0);
+        int rc = launch_status("amax");
+        if (rc) return rc;
+    }
+    QVecDesc vd[2] = {};
+    int nvec = 0;
+    for (int i = 0; i < nops; ++i) {
+        const QuantOperand& o = ops[i];
+        const float* amax = o.given_amax ? o.given_amax : o.amax_out;
+        if (o.batch * o.rows == 0) continue;
+        const int64_t ld = static_cast<int64_t>(round_up(static_cast<size_t>(o.cols), 16));
+        if (quant_vec_ok(dt, o)) {
+            QVecDesc& d = vd[nvec++];
+            d.x = o.x;
+            d.rows = o.rows;
+            d.cols = o.cols;
+            d.ld = ld;
+            d.sb = o.sb;
+            d.sr = o.sr;
+            d.groups = ld / 8;
+            d.items = o.batch * o.rows * d.groups;
+            d.amax = amax;
+            d.amax_stride = o.per_slice ? 1 : 0;
+            d.limbs = o.limbs;
+        } else {
+            int rc = quantize_limbs_launch(dt, o.x, o.batch, o.rows, o.cols, o.sb, o.sr, o.sc, amax,
+                                           o.per_slice ? 1 : 0, o.limbs, stream);
+            if (rc) return rc;
+        }
+    }
+    if (nvec > 0) {
+        const int64_t items = vd[0].items + vd[1].items;
+        const int64_t cap = static_cast<int64_t>(sm_count(dev)) * 16;
+        const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min(ceil_div(items, 256), cap)));
+        if (dt == TK_DTYPE_F16)
+            quant_vec_kernel<__half><<<grid, 256, 0, stream>>>(vd[0], vd[1]);
+        else
+            quant_vec_kernel<float><<<grid, 256, 0, stream>>>(vd[0], vd[1]);
+        return launch_status("quantise");
+    }
+    return TK_OK;
 }
 
 }  // namespace tk

@@ -54,4 +54,17 @@ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 inline size_t dtype_size(tk_dtype_t dt) { return dt == TK_DTYPE_F16 ? 2 : 4; }
 
+// One GEMM operand to quantise: a [batch][rows][cols] strided view, one amax
+// per slice (per_slice) or for the whole operand, written to amax_out unless
+// given_amax is set, and limb planes [batch][2][rows][round_up(cols,16)].
+struct QuantOperand {
+    const void* x;
+    int64_t batch, rows, cols, sb, sr, sc;
+    bool per_slice;
+    const float* given_amax;
+    float* amax_out;
+    int8_t* limbs;
+};
+int quantise_operands(tk_dtype_t dt, const QuantOperand* ops, int nops, cudaStream_t stream);
+
 }  // namespace tk
