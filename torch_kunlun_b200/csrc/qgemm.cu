@@ -27,7 +27,10 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cmath>
+#include <cstdlib>
 #include <mutex>
+#include <string>
 
 #include "tk_internal.h"
 #include "tk_numerics.cuh"
@@ -44,25 +47,44 @@ int quantize_limbs_launch(tk_dtype_t dtype, const void* x, int64_t batch, int64_
 namespace {
 
 constexpr int BM = 128;
-constexpr int BN = 128;
 constexpr int BK = 128;  // bytes (int8 elements) per stage along K
 constexpr int UMMA_K = 32;
-constexpr int STAGES = 3;
-constexpr int TILE_BYTES = BM * BK;            // one limb plane of one operand
-constexpr int STAGE_BYTES = 4 * TILE_BYTES;    // A hi, A lo, B hi, B lo
-constexpr int NUM_EPI_WARPS = 8;  // two warps per TMEM lane quarter, 64 columns each
+constexpr int NUM_EPI_WARPS = 8;  // two warps per TMEM lane quarter
 constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
 constexpr int TMEM_COLS = 512;
-constexpr int ACC_HH = 0;
-constexpr int ACC_MID = BN;
-constexpr int ACC_LL = 2 * BN;
 constexpr int kMaxK = 32768;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
 
-constexpr uint32_t IDESC_SS = idesc_i8(BM, BN, true, true);
-constexpr uint32_t IDESC_SU = idesc_i8(BM, BN, true, false);
-constexpr uint32_t IDESC_US = idesc_i8(BM, BN, false, true);
-constexpr uint32_t IDESC_UU = idesc_i8(BM, BN, false, false);
+// Tile configuration: BN columns per tile, a STAGES-deep TMA ring and NBUF
+// accumulator buffers in TMEM (each buffer holds HH, MID and LL, 3*BN
+// columns).  With NBUF = 2 the epilogue of one tile overlaps the MMAs of the
+// next; 2*3*BN <= 512 limits that to BN <= 80.
+template <int BN_, int STAGES_, int NBUF_>
+struct TileCfg {
+    static constexpr int BN = BN_;
+    static constexpr int STAGES = STAGES_;
+    static constexpr int NBUF = NBUF_;
+    static constexpr int A_BYTES = BM * BK;   // one limb plane of the A tile
+    static constexpr int B_BYTES = BN * BK;   // one limb plane of the B tile
+    static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr int BUF_COLS = NBUF == 1 ? 3 * BN : 256;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+    static constexpr uint32_t IDESC_SS = idesc_i8(BM, BN, true, true);
+    static constexpr uint32_t IDESC_SU = idesc_i8(BM, BN, true, false);
+    static constexpr uint32_t IDESC_US = idesc_i8(BM, BN, false, true);
+    static constexpr uint32_t IDESC_UU = idesc_i8(BM, BN, false, false);
+    static_assert(B_BYTES % 1024 == 0, "B tile must be a whole number of swizzle atoms");
+    static_assert(NBUF * BUF_COLS <= TMEM_COLS && 3 * BN <= BUF_COLS, "TMEM budget");
+    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+    static_assert(SMEM <= 232448, "shared memory budget");
+};
+// Measured on B200 (int16-quantised GEMMs, K-major limb operands): 128x160
+// tiles are 5-14% faster than 128x128 once K >= 2048 (less operand traffic
+// per MMA, fewer waves for N = 4096) and slower for short K, where the
+// non-overlapped epilogue dominates.  A double-buffered 128x80 variant
+// (epilogue overlapped with the next tile's MMAs) was 30% slower at 4096^3:
+// operand delivery, not the epilogue, limits these tiles.
+using CfgWide = TileCfg<128, 3, 1>;   // 128x128 tiles, accumulators single-buffered
+using CfgWider = TileCfg<160, 3, 1>;  // 128x160 tiles (480 TMEM columns), single-buffered
 
 struct EpiParams {
     int dtype;  // 0 fp16, 1 fp32
@@ -149,20 +171,27 @@ __device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b,
 
 // ---- tensor-core kernel --------------------------------------------------------
 
-template <int DT, int ACT>
+template <class C, int DT, int ACT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const TileParams tp, const EpiParams ep) {
+    constexpr int STAGES = C::STAGES;
+    constexpr int STAGE_BYTES = C::STAGE_BYTES;
+    constexpr int BN = C::BN;
+    constexpr int NBUF = C::NBUF;
+    constexpr int OFF_ALO = C::A_BYTES;
+    constexpr int OFF_BHI = 2 * C::A_BYTES;
+    constexpr int OFF_BLO = 2 * C::A_BYTES + C::B_BYTES;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
     uint64_t* full_bar = bars;                 // [STAGES] TMA -> MMA
     uint64_t* empty_bar = bars + STAGES;       // [STAGES] MMA -> TMA
-    uint64_t* acc_full = bars + 2 * STAGES;    // MMA -> epilogue
-    uint64_t* acc_empty = acc_full + 1;        // epilogue -> MMA (4 arrivals)
-    uint64_t* drain_bar = acc_full + 2;        // MMA teardown
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 3);
+    uint64_t* acc_full = bars + 2 * STAGES;    // [NBUF] MMA -> epilogue
+    uint64_t* acc_empty = acc_full + NBUF;     // [NBUF] epilogue -> MMA (one arrival per epilogue warp)
+    uint64_t* drain_bar = acc_empty + NBUF;    // MMA teardown
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -173,8 +202,10 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             mbar_init(smem_u32(full_bar + s), 1);
             mbar_init(smem_u32(empty_bar + s), 1);
         }
-        mbar_init(smem_u32(acc_full), 1);
-        mbar_init(smem_u32(acc_empty), NUM_EPI_WARPS);
+        for (int i = 0; i < NBUF; ++i) {
+            mbar_init(smem_u32(acc_full + i), 1);
+            mbar_init(smem_u32(acc_empty + i), NUM_EPI_WARPS);
+        }
         mbar_init(smem_u32(drain_bar), 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -212,11 +243,11 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     mbar_arrive_expect_tx(fb, STAGE_BYTES);
                     uint8_t* sbase = smem + stage * STAGE_BYTES;
                     const int kx = kb * BK;
-                    tma_load_3d(smem_u32(sbase + 0 * TILE_BYTES), &tmA, fb, kx, mt * BM, 2 * b + 0);
-                    tma_load_3d(smem_u32(sbase + 1 * TILE_BYTES), &tmA, fb, kx, mt * BM, 2 * b + 1);
+                    tma_load_3d(smem_u32(sbase), &tmA, fb, kx, mt * BM, 2 * b + 0);
+                    tma_load_3d(smem_u32(sbase + OFF_ALO), &tmA, fb, kx, mt * BM, 2 * b + 1);
                     const int bb = tp.b_mod ? b % tp.b_mod : b;
-                    tma_load_3d(smem_u32(sbase + 2 * TILE_BYTES), &tmB, fb, kx, nt * BN, 2 * bb + 0);
-                    tma_load_3d(smem_u32(sbase + 3 * TILE_BYTES), &tmB, fb, kx, nt * BN, 2 * bb + 1);
+                    tma_load_3d(smem_u32(sbase + OFF_BHI), &tmB, fb, kx, nt * BN, 2 * bb + 0);
+                    tma_load_3d(smem_u32(sbase + OFF_BLO), &tmB, fb, kx, nt * BN, 2 * bb + 1);
                 }
                 __syncwarp();
                 used[stage] = true;
@@ -236,14 +267,19 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         // ---------------- MMA issuer ----------------
         int stage = 0;
         uint32_t phase = 0;
-        uint32_t acc_phase = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < tp.num_tiles && ok; t += gridDim.x) {
-            if (!mbar_wait_bounded(smem_u32(acc_empty), acc_phase ^ 1u, abort_flag, tp.err,
+        int local = 0;  // tiles processed by this CTA
+        for (int t = blockIdx.x; t < tp.num_tiles && ok; t += gridDim.x, ++local) {
+            const int buf = local % NBUF;
+            const uint32_t acc_phase = static_cast<uint32_t>(local / NBUF) & 1u;
+            if (!mbar_wait_bounded(smem_u32(acc_empty + buf), acc_phase ^ 1u, abort_flag, tp.err,
                                    kDevErrWaitAccEmpty)) {
                 break;
             }
             tc_fence_after();
+            const uint32_t acc_hh = tmem_base + buf * C::BUF_COLS;
+            const uint32_t acc_mid = acc_hh + BN;
+            const uint32_t acc_ll = acc_hh + 2 * BN;
             for (int kb = 0; kb < tp.num_kb; ++kb) {
                 if (!mbar_wait_bounded(smem_u32(full_bar + stage), phase, abort_flag, tp.err,
                                        kDevErrWaitFull)) {
@@ -253,20 +289,20 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 tc_fence_after();
                 if (lane == 0) {
                     const uint32_t sb = smem_u32(smem + stage * STAGE_BYTES);
-                    const uint64_t a_hi = smem_desc_kmajor_sw128(sb + 0 * TILE_BYTES);
-                    const uint64_t a_lo = smem_desc_kmajor_sw128(sb + 1 * TILE_BYTES);
-                    const uint64_t b_hi = smem_desc_kmajor_sw128(sb + 2 * TILE_BYTES);
-                    const uint64_t b_lo = smem_desc_kmajor_sw128(sb + 3 * TILE_BYTES);
+                    const uint64_t a_hi = smem_desc_kmajor_sw128(sb);
+                    const uint64_t a_lo = smem_desc_kmajor_sw128(sb + OFF_ALO);
+                    const uint64_t b_hi = smem_desc_kmajor_sw128(sb + OFF_BHI);
+                    const uint64_t b_lo = smem_desc_kmajor_sw128(sb + OFF_BLO);
 #pragma unroll
                     for (int kk = 0; kk < BK / UMMA_K; ++kk) {
                         // K advance inside the 128-byte swizzle row: start address
                         // moves by kk*32 bytes (encoded >> 4).
                         const uint64_t off = static_cast<uint64_t>((kk * UMMA_K) >> 4);
                         const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
-                        tc_mma_i8(tmem_base + ACC_HH, a_hi + off, b_hi + off, IDESC_SS, acc);
-                        tc_mma_i8(tmem_base + ACC_MID, a_hi + off, b_lo + off, IDESC_SU, acc);
-                        tc_mma_i8(tmem_base + ACC_MID, a_lo + off, b_hi + off, IDESC_US, 1u);
-                        tc_mma_i8(tmem_base + ACC_LL, a_lo + off, b_lo + off, IDESC_UU, acc);
+                        tc_mma_i8(acc_hh, a_hi + off, b_hi + off, C::IDESC_SS, acc);
+                        tc_mma_i8(acc_mid, a_hi + off, b_lo + off, C::IDESC_SU, acc);
+                        tc_mma_i8(acc_mid, a_lo + off, b_hi + off, C::IDESC_US, 1u);
+                        tc_mma_i8(acc_ll, a_lo + off, b_lo + off, C::IDESC_UU, acc);
                     }
                     tc_commit(smem_u32(empty_bar + stage));
                 }
@@ -274,9 +310,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 if (++stage == STAGES) { stage = 0; phase ^= 1u; }
             }
             if (!ok) break;
-            if (lane == 0) tc_commit(smem_u32(acc_full));
+            if (lane == 0) tc_commit(smem_u32(acc_full + buf));
             __syncwarp();
-            acc_phase ^= 1u;
         }
         // Drain: all MMAs issued by this thread complete before TMEM is freed.
         if (lane == 0) tc_commit(smem_u32(drain_bar));
@@ -295,26 +330,28 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         const bool has_bias = ep.bias != nullptr;
         const bool has_add = ep.addend != nullptr && ep.beta != 0.0f;
         const bool has_alpha = ep.alpha != 1.0f;
-        uint32_t acc_phase = 0;
-        for (int t = blockIdx.x; t < tp.num_tiles; t += gridDim.x) {
+        int local = 0;
+        for (int t = blockIdx.x; t < tp.num_tiles; t += gridDim.x, ++local) {
             int b, mt, nt;
             decode_tile(tp, t, b, mt, nt);
-            if (!mbar_wait_bounded(smem_u32(acc_full), acc_phase, abort_flag, tp.err,
+            const int buf = local % NBUF;
+            const uint32_t acc_phase = static_cast<uint32_t>(local / NBUF) & 1u;
+            if (!mbar_wait_bounded(smem_u32(acc_full + buf), acc_phase, abort_flag, tp.err,
                                    kDevErrWaitAccFull)) {
                 break;
             }
             tc_fence_after();
+            const uint32_t t_buf = t_row + buf * C::BUF_COLS;
             const int64_t m = static_cast<int64_t>(mt) * BM + row;
             const double s = epi_scale(ep, b);
             const bool row_ok = m < ep.M;
             const int64_t out_row = b * ep.out_sb + m * ep.out_sm;
 #pragma unroll 1
-            for (int cc = 0; cc < BN / 32; ++cc) {
-                const int c = half * (BN / 32) + cc;  // 16-column chunk index
+            for (int c = half; c < BN / 16; c += 2) {  // 16-column chunks, alternating halves
                 uint32_t hh[16], mid[16], ll[16];
-                tmem_ld_32x32b_x16(t_row + ACC_HH + c * 16, hh);
-                tmem_ld_32x32b_x16(t_row + ACC_MID + c * 16, mid);
-                tmem_ld_32x32b_x16(t_row + ACC_LL + c * 16, ll);
+                tmem_ld_32x32b_x16(t_buf + c * 16, hh);
+                tmem_ld_32x32b_x16(t_buf + BN + c * 16, mid);
+                tmem_ld_32x32b_x16(t_buf + 2 * BN + c * 16, ll);
                 tc_wait_ld();
                 const int64_t n0 = static_cast<int64_t>(nt) * BN + c * 16;
                 if (!row_ok || n0 >= ep.N) continue;
@@ -411,8 +448,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(acc_empty));
-            acc_phase ^= 1u;
+            if (lane == 0) mbar_arrive(smem_u32(acc_empty + buf));
         }
     }
 
@@ -473,13 +509,14 @@ EncodeTiledFn get_encode_fn() {
 }
 
 // Tensor map over limb planes [planes][rows][ld] (uint8), box 128 x 128 x 1.
-int make_limb_map(CUtensorMap* map, const int8_t* base, int64_t planes, int64_t rows, int64_t ld) {
+int make_limb_map(CUtensorMap* map, const int8_t* base, int64_t planes, int64_t rows, int64_t ld,
+                  int box_rows) {
     EncodeTiledFn enc = get_encode_fn();
     if (enc == nullptr) TK_FAIL(TK_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     cuuint64_t dims[3] = {static_cast<cuuint64_t>(ld), static_cast<cuuint64_t>(rows),
                           static_cast<cuuint64_t>(planes)};
     cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld), static_cast<cuuint64_t>(rows * ld)};
-    cuuint32_t box[3] = {BK, BM, 1};
+    cuuint32_t box[3] = {BK, static_cast<cuuint32_t>(box_rows), 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(base), dims,
                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -574,51 +611,64 @@ EpiParams make_epi(const tk_qgemm_desc_t& d, const float* amax_a, const float* a
 
 enum class Path { TensorCore, Simt };
 
-template <int DT, int ACT>
+template <class C, int DT, int ACT>
 int launch_one(int dev, int grid, const CUtensorMap& tmA, const CUtensorMap& tmB,
                const TileParams& tp, const EpiParams& ep, cudaStream_t stream) {
     static std::once_flag attr_once[64];
     if (dev >= 0 && dev < 64) {
         std::call_once(attr_once[dev], [] {
-            cudaFuncSetAttribute(qgemm_tc_kernel<DT, ACT>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+            cudaFuncSetAttribute(qgemm_tc_kernel<C, DT, ACT>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         });
     }
-    qgemm_tc_kernel<DT, ACT><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tmA, tmB, tp, ep);
+    qgemm_tc_kernel<C, DT, ACT><<<grid, NUM_THREADS, C::SMEM, stream>>>(tmA, tmB, tp, ep);
     return TK_OK;
 }
 
-template <int DT>
+template <class C, int DT>
 int dispatch_act(int act, int dev, int grid, const CUtensorMap& tmA, const CUtensorMap& tmB,
                  const TileParams& tp, const EpiParams& ep, cudaStream_t stream) {
     switch (act) {
-        case TK_ACT_NONE: return launch_one<DT, TK_ACT_NONE>(dev, grid, tmA, tmB, tp, ep, stream);
-        case TK_ACT_RELU: return launch_one<DT, TK_ACT_RELU>(dev, grid, tmA, tmB, tp, ep, stream);
-        case TK_ACT_GELU: return launch_one<DT, TK_ACT_GELU>(dev, grid, tmA, tmB, tp, ep, stream);
-        case TK_ACT_GELU_TANH: return launch_one<DT, TK_ACT_GELU_TANH>(dev, grid, tmA, tmB, tp, ep, stream);
-        case TK_ACT_SILU: return launch_one<DT, TK_ACT_SILU>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_NONE: return launch_one<C, DT, TK_ACT_NONE>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_RELU: return launch_one<C, DT, TK_ACT_RELU>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_GELU: return launch_one<C, DT, TK_ACT_GELU>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_GELU_TANH:
+            return launch_one<C, DT, TK_ACT_GELU_TANH>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_SILU: return launch_one<C, DT, TK_ACT_SILU>(dev, grid, tmA, tmB, tp, ep, stream);
         default: TK_FAIL(TK_ERR_INVALID_ARG, "qgemm: bad act %d", act);
     }
 }
 
-int dispatch_tc(int dt, int act, int dev, int grid, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                const TileParams& tp, const EpiParams& ep, cudaStream_t stream) {
-    return dt == 0 ? dispatch_act<0>(act, dev, grid, tmA, tmB, tp, ep, stream)
-                   : dispatch_act<1>(act, dev, grid, tmA, tmB, tp, ep, stream);
+// Tile configuration for a problem: 128x160 tiles for K >= 2048, else
+// 128x128.  TK_QGEMM_TILE=wide|wider forces one (a tuning override).
+enum class TileChoice { Wide, Wider };
+
+TileChoice choose_tiles(const tk_qgemm_desc_t& d) {
+    static const int forced = [] {
+        const char* v = std::getenv("TK_QGEMM_TILE");
+        if (v == nullptr) return 0;
+        if (std::string(v) == "wide") return 1;
+        if (std::string(v) == "wider") return 2;
+        return 0;
+    }();
+    if (forced == 1) return TileChoice::Wide;
+    if (forced == 2) return TileChoice::Wider;
+    return d.k >= 2048 ? TileChoice::Wider : TileChoice::Wide;
 }
 
-int launch_tc(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb, int64_t ld,
-              const EpiParams& ep, cudaStream_t stream, int b_mod = 0) {
+template <class C>
+int launch_cfg(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb, int64_t ld,
+               const EpiParams& ep, cudaStream_t stream, int b_mod) {
     CUtensorMap tmA, tmB;
-    int rc = make_limb_map(&tmA, la, 2 * d.batch, d.m, ld);
+    int rc = make_limb_map(&tmA, la, 2 * d.batch, d.m, ld, BM);
     if (rc) return rc;
-    rc = make_limb_map(&tmB, lb, 2 * (b_mod ? b_mod : d.batch), d.n, ld);
+    rc = make_limb_map(&tmB, lb, 2 * (b_mod ? b_mod : d.batch), d.n, ld, C::BN);
     if (rc) return rc;
     TileParams tp;
     tp.b_mod = b_mod;
     tp.batch = static_cast<int>(d.batch);
     tp.tiles_m = static_cast<int>(ceil_div(d.m, BM));
-    tp.tiles_n = static_cast<int>(ceil_div(d.n, BN));
+    tp.tiles_n = static_cast<int>(ceil_div(d.n, C::BN));
     const int64_t nt = static_cast<int64_t>(tp.tiles_m) * tp.tiles_n * d.batch;
     TK_CHECK_ARG(nt < (1LL << 31), "qgemm: too many tiles");
     tp.num_tiles = static_cast<int>(nt);
@@ -626,10 +676,18 @@ int launch_tc(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb, int6
     const int dev = current_device();
     tp.err = device_error_word(dev);
     const int grid = static_cast<int>(std::min<int64_t>(nt, sm_count(dev)));
-    int rc2 = dispatch_tc(d.dtype == TK_DTYPE_F16 ? 0 : 1, static_cast<int>(d.act), dev, grid,
-                          tmA, tmB, tp, ep, stream);
-    if (rc2) return rc2;
+    rc = d.dtype == TK_DTYPE_F16
+             ? dispatch_act<C, 0>(static_cast<int>(d.act), dev, grid, tmA, tmB, tp, ep, stream)
+             : dispatch_act<C, 1>(static_cast<int>(d.act), dev, grid, tmA, tmB, tp, ep, stream);
+    if (rc) return rc;
     return launch_status("qgemm_tc");
+}
+
+int launch_tc(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb, int64_t ld,
+              const EpiParams& ep, cudaStream_t stream, int b_mod = 0) {
+    if (choose_tiles(d) == TileChoice::Wider)
+        return launch_cfg<CfgWider>(d, la, lb, ld, ep, stream, b_mod);
+    return launch_cfg<CfgWide>(d, la, lb, ld, ep, stream, b_mod);
 }
 
 int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t stream, Path path,

@@ -291,46 +291,48 @@ __device__ __forceinline__ void load8<float>(const float* p, int64_t n, float (&
     }
 }
 
+// One warp per row: lanes walk the row's 8-column groups (a warp moves 512 B
+// of fp16 per step), eight rows per block.  Rows [0, rows0) belong to d0.
 template <typename T>
-__device__ __forceinline__ void quant_vec_item(const QVecDesc& d, int64_t i) {
-    const int64_t g = i % d.groups;
-    const int64_t rr = i / d.groups;
-    const int64_t r = rr % d.rows;
-    const int64_t b = rr / d.rows;
-    const int64_t c0 = g * 8;
-    float v[8];
-    const int64_t n = d.cols - c0;
-    if (n > 0) {
-        load8<T>(static_cast<const T*>(d.x) + b * d.sb + r * d.sr + c0, n, v);
-    } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = 0.0f;
-    }
+__device__ __forceinline__ void quant_vec_row(const QVecDesc& d, int64_t row) {
+    const int64_t b = row / d.rows;
+    const int64_t r = row - b * d.rows;
     const float inv = quant_inv(d.amax[b * d.amax_stride]);
-    unsigned hi0 = 0, hi1 = 0, lo0 = 0, lo1 = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const int q = quant_one(v[j], inv);
-        const unsigned h = (static_cast<unsigned>(q >> 8) & 0xFFu) << (8 * (j & 3));
-        const unsigned l = (static_cast<unsigned>(q) & 0xFFu) << (8 * (j & 3));
-        if (j < 4) { hi0 |= h; lo0 |= l; } else { hi1 |= h; lo1 |= l; }
-    }
+    const T* src = static_cast<const T*>(d.x) + b * d.sb + r * d.sr;
     const int64_t plane = d.rows * d.ld;
-    int8_t* dst = d.limbs + (b * 2) * plane + r * d.ld + c0;
-    *reinterpret_cast<uint2*>(dst) = make_uint2(hi0, hi1);
-    *reinterpret_cast<uint2*>(dst + plane) = make_uint2(lo0, lo1);
+    int8_t* dst = d.limbs + (b * 2) * plane + r * d.ld;
+    for (int64_t g = threadIdx.x; g < d.groups; g += 32) {
+        const int64_t c0 = g * 8;
+        float v[8];
+        const int64_t n = d.cols - c0;
+        if (n > 0) {
+            load8<T>(src + c0, n, v);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+        }
+        unsigned hi0 = 0, hi1 = 0, lo0 = 0, lo1 = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int q = quant_one(v[j], inv);
+            const unsigned h = (static_cast<unsigned>(q >> 8) & 0xFFu) << (8 * (j & 3));
+            const unsigned l = (static_cast<unsigned>(q) & 0xFFu) << (8 * (j & 3));
+            if (j < 4) { hi0 |= h; lo0 |= l; } else { hi1 |= h; lo1 |= l; }
+        }
+        *reinterpret_cast<uint2*>(dst + c0) = make_uint2(hi0, hi1);
+        *reinterpret_cast<uint2*>(dst + plane + c0) = make_uint2(lo0, lo1);
+    }
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256) quant_vec_kernel(QVecDesc d0, QVecDesc d1) {
-    const int64_t total = d0.items + d1.items;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        if (i < d0.items)
-            quant_vec_item<T>(d0, i);
-        else
-            quant_vec_item<T>(d1, i - d0.items);
-    }
+__global__ void __launch_bounds__(256) quant_vec_kernel(QVecDesc d0, QVecDesc d1, int64_t rows0,
+                                                        int64_t rows_total) {
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + threadIdx.y;
+    if (row >= rows_total) return;
+    if (row < rows0)
+        quant_vec_row<T>(d0, row);
+    else
+        quant_vec_row<T>(d1, row - rows0);
 }
 
 }  // namespace
@@ -492,13 +494,17 @@ int quantise_operands(tk_dtype_t dt, const QuantOperand* ops, int nops, cudaStre
         }
     }
     if (nvec > 0) {
-        const int64_t items = vd[0].items + vd[1].items;
-        const int64_t cap = static_cast<int64_t>(sm_count(dev)) * 16;
-        const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min(ceil_div(items, 256), cap)));
+        const int64_t rows0 = vd[0].items / vd[0].groups;
+        const int64_t rows1 = nvec > 1 ? vd[1].items / vd[1].groups : 0;
+        const int64_t blocks = ceil_div(rows0 + rows1, 8);
+        TK_CHECK_ARG(blocks < (1LL << 31), "quantise: too many rows");
+        const dim3 block(32, 8);
         if (dt == TK_DTYPE_F16)
-            quant_vec_kernel<__half><<<grid, 256, 0, stream>>>(vd[0], vd[1]);
+            quant_vec_kernel<__half><<<static_cast<unsigned>(blocks), block, 0, stream>>>(
+                vd[0], vd[1], rows0, rows0 + rows1);
         else
-            quant_vec_kernel<float><<<grid, 256, 0, stream>>>(vd[0], vd[1]);
+            quant_vec_kernel<float><<<static_cast<unsigned>(blocks), block, 0, stream>>>(
+                vd[0], vd[1], rows0, rows0 + rows1);
         return launch_status("quantise");
     }
     return TK_OK;
