@@ -291,36 +291,60 @@ __device__ __forceinline__ void load8<float>(const float* p, int64_t n, float (&
     }
 }
 
+// Quantise 8 values and pack their limbs: lo bytes and hi bytes of the int16
+// codes into one 8-byte word each.  The clamp of quant_one is not needed
+// here: with inv = RN(32767/amax) and |v| <= amax, |RN(v*inv)| <= 32767.004,
+// so the rounded code never leaves [-32767, 32767]; a NaN product (possible
+// only when amax itself is not finite) is mapped to 0 as in quant_one.
+__device__ __forceinline__ void quant8_pack(const float (&v)[8], float inv, uint2& hi, uint2& lo) {
+    int q[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float t = __fmul_rn(v[j], inv);
+        q[j] = (t == t) ? __float2int_rn(t) : 0;
+    }
+    // byte 0 of each code is its lo limb, byte 1 its (two's-complement) hi limb
+    lo.x = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
+    lo.y = __byte_perm(__byte_perm(q[4], q[5], 0x0040), __byte_perm(q[6], q[7], 0x0040), 0x5410);
+    hi.x = __byte_perm(__byte_perm(q[0], q[1], 0x0051), __byte_perm(q[2], q[3], 0x0051), 0x5410);
+    hi.y = __byte_perm(__byte_perm(q[4], q[5], 0x0051), __byte_perm(q[6], q[7], 0x0051), 0x5410);
+}
+
 // One warp per row: lanes walk the row's 8-column groups (a warp moves 512 B
 // of fp16 per step), eight rows per block.  Rows [0, rows0) belong to d0.
 template <typename T>
-__device__ __forceinline__ void quant_vec_row(const QVecDesc& d, int64_t row) {
+__device__ __forceinline__ void quant_vec_row(const QVecDesc& d, int64_t row, int lane) {
     const int64_t b = row / d.rows;
     const int64_t r = row - b * d.rows;
     const float inv = quant_inv(d.amax[b * d.amax_stride]);
     const T* src = static_cast<const T*>(d.x) + b * d.sb + r * d.sr;
     const int64_t plane = d.rows * d.ld;
     int8_t* dst = d.limbs + (b * 2) * plane + r * d.ld;
-    for (int64_t g = threadIdx.x; g < d.groups; g += 32) {
-        const int64_t c0 = g * 8;
-        float v[8];
-        const int64_t n = d.cols - c0;
-        if (n > 0) {
-            load8<T>(src + c0, n, v);
-        } else {
+    // Four groups per lane per step: their loads are issued before any is
+    // used, so a warp keeps 4 x 512 B in flight instead of one.
+    for (int64_t g0 = lane; g0 < d.groups; g0 += 128) {
+        float v[4][8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = 0.0f;
-        }
-        unsigned hi0 = 0, hi1 = 0, lo0 = 0, lo1 = 0;
+        for (int u = 0; u < 4; ++u) {
+            const int64_t c0 = (g0 + 32 * u) * 8;
+            const int64_t n = d.cols - c0;
+            if (g0 + 32 * u < d.groups && n > 0) {
+                load8<T>(src + c0, n, v[u]);
+            } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int q = quant_one(v[j], inv);
-            const unsigned h = (static_cast<unsigned>(q >> 8) & 0xFFu) << (8 * (j & 3));
-            const unsigned l = (static_cast<unsigned>(q) & 0xFFu) << (8 * (j & 3));
-            if (j < 4) { hi0 |= h; lo0 |= l; } else { hi1 |= h; lo1 |= l; }
+                for (int j = 0; j < 8; ++j) v[u][j] = 0.0f;
+            }
         }
-        *reinterpret_cast<uint2*>(dst + c0) = make_uint2(hi0, hi1);
-        *reinterpret_cast<uint2*>(dst + plane + c0) = make_uint2(lo0, lo1);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t g = g0 + 32 * u;
+            if (g >= d.groups) break;
+            uint2 hi, lo;
+            quant8_pack(v[u], inv, hi, lo);
+            const int64_t c0 = g * 8;
+            *reinterpret_cast<uint2*>(dst + c0) = hi;
+            *reinterpret_cast<uint2*>(dst + plane + c0) = lo;
+        }
     }
 }
 
@@ -330,9 +354,9 @@ __global__ void __launch_bounds__(256) quant_vec_kernel(QVecDesc d0, QVecDesc d1
     const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + threadIdx.y;
     if (row >= rows_total) return;
     if (row < rows0)
-        quant_vec_row<T>(d0, row);
+        quant_vec_row<T>(d0, row, threadIdx.x);
     else
-        quant_vec_row<T>(d1, row - rows0);
+        quant_vec_row<T>(d1, row - rows0, threadIdx.x);
 }
 
 }  // namespace
