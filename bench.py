@@ -48,6 +48,13 @@ def make_inputs():
     return x, w, b
 
 
+TP_T, TP_H, TP_F = 16384, 8192, 28672
+TP_OPS_PER_STEP = 3 * 2 * TP_T * TP_H * TP_F
+TP_METRIC = "int16-quant TP-MLP effective TOPS (aggregate over GPUs)"
+TP_WORKLOAD = ("tensor-parallel SiLU-gated MLP, x[16384,8192], gate/up [8192,28672] column-split, "
+               "down [28672,8192] row-split, partial sums all-reduced over bkcl (NCCL)")
+
+
 def dist_env():
     return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
             int(os.environ.get("WORLD_SIZE", "1")))
@@ -255,7 +262,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="kunlun", choices=["kunlun", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="linear", choices=["linear", "tp_mlp"])
+    ap.add_argument("--reduce", default="allreduce", choices=["allreduce", "reduce_scatter"])
     args = ap.parse_args()
+    if args.workload == "tp_mlp" and args.impl != "reference":
+        return run_tp_mlp(args)
     if args.impl == "reference":
         return run_reference(args)
     args.warmup = max(args.warmup, 3)
@@ -368,6 +379,71 @@ def main():
     if pg:
         pg.barrier()
         pg.destroy_process_group()
+    return 0
+
+
+def run_tp_mlp(args):
+    """Tensor-parallel MLP (strong scaling: the whole MLP is split over the
+    ranks).  Inputs are larger than L2, so no flush is needed."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    import torch_kunlun  # noqa: F401
+    from torch_kunlun_b200 import tp
+    kunlun = torch_kunlun.kunlun
+    rank, local_rank, world = dist_env()
+    kunlun.set_device(local_rank)
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("kunlun", local_rank)
+    if world > 1:
+        dist.init_process_group("bkcl", timeout=datetime.timedelta(seconds=300))
+    fr = TP_F // world
+
+    def randn_dev(shape, seed, scale):
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        t = (torch.randn(shape, generator=g, device="cuda") * scale).half()
+        out = torch.empty(shape, dtype=torch.float16, device=dev)
+        out.copy_(t)
+        return out
+
+    x = randn_dev((TP_T, TP_H), 0, 1.0)
+    wg = randn_dev((fr, TP_H), 1000 + rank, 0.02)
+    wu = randn_dev((fr, TP_H), 2000 + rank, 0.02)
+    wd = randn_dev((TP_H, fr), 3000 + rank, 0.02)
+    torch.cuda.synchronize()
+    comm = kunlun.Stream(dev)
+
+    def step():
+        tp.tp_mlp_forward(x, wg, wu, wd, reduce=args.reduce, chunks=4, comm_stream=comm)
+
+    if world > 1:
+        dist.barrier()
+    kunlun.synchronize()
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        times = timed_steps(step, args.steps, args.warmup, lambda: None, kunlun)
+    kunlun.synchronize()
+    ms = sum(times) / len(times)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float32).to(dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.cpu().item())
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": TP_METRIC, "value": TP_OPS_PER_STEP / (ms / 1000) / 1e12, "unit": "TOPS",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int16",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, no dataset)",
+            "config": {"workload": TP_WORKLOAD, "T": TP_T, "H": TP_H, "F": TP_F,
+                       "parallelism": f"tp{world}", "reduce": args.reduce,
+                       "overlap": "down projection in 4 row blocks, each block's all-reduce on a "
+                                  "second stream", "l2": "inputs larger than L2"},
+            "gpu_launches": None, "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
     return 0
 
 

@@ -36,6 +36,7 @@ from . import _C  # noqa: E402,F401  (registers PrivateUse1, allocator, guard, h
 from . import kunlun  # noqa: E402
 from . import xccl  # noqa: E402
 from . import ops  # noqa: E402
+from . import tp  # noqa: E402
 
 __version__ = "0.1.0"
 
@@ -48,4 +49,4 @@ if not hasattr(torch.Tensor, "kunlun"):
 
 scaled_dot_product_attention = kunlun.scaled_dot_product_attention
 
-__all__ = ["kunlun", "xccl", "ops", "scaled_dot_product_attention"]
+__all__ = ["kunlun", "xccl", "ops", "tp", "scaled_dot_product_attention"]

@@ -98,6 +98,12 @@ void xccl_barrier(int device);
 at::Tensor linear_act(const at::Tensor& input, const at::Tensor& weight,
                       const std::optional<at::Tensor>& bias, int64_t act);
 at::Tensor silu_mul(const at::Tensor& gate, const at::Tensor& up);
+at::Tensor amax(const at::Tensor& x);
+at::Tensor linear_scaled(const at::Tensor& input, const at::Tensor& weight,
+                         const std::optional<at::Tensor>& bias, int64_t act,
+                         const std::optional<at::Tensor>& amax_x,
+                         const std::optional<at::Tensor>& amax_w,
+                         const std::optional<at::Tensor>& out);
 at::Tensor sdpa(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                 const std::optional<at::Tensor>& mask, bool is_causal, std::optional<double> scale);
 

@@ -89,6 +89,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("linear_act", &linear_act, py::arg("input"), py::arg("weight"),
           py::arg("bias") = py::none(), py::arg("act") = 0);
     m.def("silu_mul", &silu_mul);
+    m.def("amax", &amax);
+    m.def("linear_scaled", &linear_scaled, py::arg("input"), py::arg("weight"),
+          py::arg("bias") = py::none(), py::arg("act") = 0, py::arg("amax_x") = py::none(),
+          py::arg("amax_w") = py::none(), py::arg("out") = py::none());
     m.def("sdpa", &sdpa, py::arg("query"), py::arg("key"), py::arg("value"),
           py::arg("attn_mask") = py::none(), py::arg("is_causal") = false,
           py::arg("scale") = py::none());

@@ -150,6 +150,19 @@ at::Tensor& copy_impl(at::Tensor& self, const at::Tensor& src, bool non_blocking
                 self.sizes());
     const bool self_dev = self.device().type() == c10::DeviceType::PrivateUse1;
     const bool src_dev = src.device().type() == c10::DeviceType::PrivateUse1;
+    if (self_dev && src.device().is_cuda() && src.device().index() == self.device().index()) {
+        // torch.cuda memory of the same GPU: an ordinary device copy on the
+        // kunlun stream once the cuda stream's pending work is done.
+        const int d = self.device().index();
+        DeviceScope g(d);
+        check_cuda(cudaStreamSynchronize(nullptr), "cudaStreamSynchronize(cuda src)");
+        at::Tensor sc = src.contiguous();
+        at::Tensor view = at::from_blob(sc.data_ptr(), sc.sizes(), sc.strides(),
+                                        self.options().dtype(sc.scalar_type()));
+        device_copy(self, view);
+        check_cuda(cudaStreamSynchronize(current_stream(d)), "cudaStreamSynchronize(kunlun)");
+        return self;
+    }
     if (self_dev && src_dev) {
         if (self.device() == src.device()) {
             if (self.is_same(src)) return self;

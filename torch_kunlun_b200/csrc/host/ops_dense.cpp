@@ -52,7 +52,8 @@ at::Tensor dense_slices(const at::Tensor& t, bool whole_block) {
 // out [B,M,N] with unit stride along N.
 void run_qgemm(const at::Tensor& a_in, const at::Tensor& b_in, at::Tensor& out,
                const std::optional<at::Tensor>& bias, const at::Tensor* addend, double alpha,
-               double beta, int act, bool per_slice) {
+               double beta, int act, bool per_slice, const float* amax_a = nullptr,
+               const float* amax_b = nullptr) {
     const int dev = out.device().index();
     DeviceScope g(dev);
     const bool whole = !per_slice;
@@ -100,6 +101,8 @@ void run_qgemm(const at::Tensor& a_in, const at::Tensor& b_in, at::Tensor& out,
     d.beta = static_cast<float>(beta);
     d.act = static_cast<tk_act_t>(act);
     d.per_slice_scales = per_slice ? 1 : 0;
+    d.amax_a = amax_a;
+    d.amax_b = amax_b;
     const size_t ws_bytes = tk_qgemm_workspace_size(&d);
     at::Tensor ws = workspace(ws_bytes, out.device());
     check_tk(tk_qgemm(&d, aligned_base(ws), ws_bytes, current_stream(dev)), "tk_qgemm");
@@ -263,6 +266,56 @@ at::Tensor linear_act(const at::Tensor& input, const at::Tensor& weight,
                   static_cast<int>(act), true);
     }
     return out.view(out_shape);
+}
+
+// max |x| over the whole tensor as a 1-element fp32 kunlun tensor (the
+// per-tensor quantisation scale source).
+at::Tensor amax(const at::Tensor& x_in) {
+    TORCH_CHECK(x_in.device().type() == c10::DeviceType::PrivateUse1, "kunlun amax: kunlun tensor");
+    at::Tensor x = x_in.contiguous();
+    at::Tensor out = at::empty({1}, x.options().dtype(at::kFloat));
+    const int dev = x.device().index();
+    DeviceScope g(dev);
+    check_tk(tk_amax(tk_dtype(x.scalar_type()), x.data_ptr(), 1, 0, x.numel(),
+                     out.data_ptr<float>(), current_stream(dev)),
+             "tk_amax");
+    return out;
+}
+
+// act(x @ W^T + b) with the per-tensor scales given (1-element fp32 tensors
+// from amax(); None computes that operand's amax).  Splitting x into row
+// blocks and passing the whole tensor's amax gives exactly the values of
+// one unsplit call.
+at::Tensor linear_scaled(const at::Tensor& input, const at::Tensor& weight,
+                         const std::optional<at::Tensor>& bias, int64_t act,
+                         const std::optional<at::Tensor>& amax_x,
+                         const std::optional<at::Tensor>& amax_w,
+                         const std::optional<at::Tensor>& out_opt) {
+    TORCH_CHECK(input.dim() == 2 && weight.dim() == 2, "kunlun linear_scaled: 2-D operands");
+    check_operand(weight, input, "linear_scaled");
+    TORCH_CHECK(weight.size(1) == input.size(1), "kunlun linear_scaled: in_features mismatch");
+    auto scale_ptr = [&](const std::optional<at::Tensor>& t) -> const float* {
+        if (!t.has_value() || !t->defined()) return nullptr;
+        TORCH_CHECK(t->scalar_type() == at::kFloat && t->numel() >= 1 && t->device() == input.device(),
+                    "kunlun linear_scaled: scales must be fp32 kunlun tensors");
+        return t->data_ptr<float>();
+    };
+    at::Tensor out;
+    if (out_opt.has_value() && out_opt->defined()) {
+        out = *out_opt;  // e.g. a row block of a larger output
+        TORCH_CHECK(out.dim() == 2 && out.size(0) == input.size(0) && out.size(1) == weight.size(0) &&
+                        out.stride(1) == 1 && out.scalar_type() == input.scalar_type() &&
+                        out.device() == input.device(),
+                    "kunlun linear_scaled: out must be a row-major [M, N] block of the input dtype");
+    } else {
+        out = at::empty({input.size(0), weight.size(0)}, input.options());
+    }
+    if (out.numel() > 0) {
+        at::Tensor o3 = out.unsqueeze(0);
+        run_qgemm(input.unsqueeze(0), weight.unsqueeze(0), o3, bias, nullptr, 1.0, 0.0,
+                  static_cast<int>(act), true, scale_ptr(amax_x), scale_ptr(amax_w));
+    }
+    return out;
 }
 
 namespace {

@@ -29,4 +29,18 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     return _C.silu_mul(gate, up)
 
 
-__all__ = ["linear", "silu_mul", "ACT"]
+def amax(x: torch.Tensor) -> torch.Tensor:
+    """max |x| as a 1-element fp32 tensor on x's device (the per-tensor scale)."""
+    return _C.amax(x)
+
+
+def linear_scaled(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                  act: str = "none", amax_x: Optional[torch.Tensor] = None,
+                  amax_w: Optional[torch.Tensor] = None,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``linear`` with given per-tensor scales; row blocks of x with the whole
+    x's amax reproduce one unsplit call exactly."""
+    return _C.linear_scaled(x, weight, bias, ACT[act], amax_x, amax_w, out)
+
+
+__all__ = ["linear", "silu_mul", "amax", "linear_scaled", "ACT"]
