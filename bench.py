@@ -55,6 +55,68 @@ TP_WORKLOAD = ("tensor-parallel SiLU-gated MLP, x[16384,8192], gate/up [8192,286
                "down [28672,8192] row-split, partial sums all-reduced over bkcl (NCCL)")
 
 
+BERT_B, BERT_L, BERT_H, BERT_HEADS, BERT_F, BERT_TAIL = 32, 512, 768, 12, 3072, 64
+BERT_WORKLOAD = ("BERT-base encoder block forward: hidden 768, 12 heads x 64, FFN 3072 gelu, "
+                 "post-LN eps 1e-12, batch 32 x seq 512 fp16, additive mask on the last 64 keys")
+
+
+def bert_inputs():
+    """Seeded block input [32, 512, 768] ~N(0,1), weights ~N(0,0.02), mask."""
+    import torch
+    from torch_kunlun_b200 import encoder
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(BERT_B, BERT_L, BERT_H, generator=g).half()
+    w = encoder.init_weights(BERT_H, BERT_F, generator=g)
+    mask = encoder.padding_mask(BERT_B, BERT_L, BERT_TAIL)
+    return x, w, mask
+
+
+def bert_cpu_baseline(batch=1, reps=3):
+    """torch CPU aten fp32 eager encoder block on `batch` sequences (all host
+    threads): tokens/s."""
+    import torch
+    import torch.nn.functional as F
+    x, w, mask = bert_inputs()
+    x, mask = x[:batch].float(), mask[:batch].float()
+    f = {k: v.float() for k, v in vars(w).items()}
+    torch.set_num_threads(os.cpu_count() or 1)
+    B, L, H, E = batch, BERT_L, BERT_H, BERT_H // BERT_HEADS
+
+    def block():
+        x2 = x.reshape(B * L, H)
+        qkv = F.linear(x2, f["w_qkv"], f["b_qkv"]).view(B, L, 3, BERT_HEADS, E).permute(2, 0, 3, 1, 4)
+        ctx = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], attn_mask=mask)
+        ctx = ctx.transpose(1, 2).reshape(B * L, H)
+        h = F.layer_norm(x2 + F.linear(ctx, f["w_o"], f["b_o"]), (H,), f["ln1_w"], f["ln1_b"], 1e-12)
+        g = F.gelu(F.linear(h, f["w_1"], f["b_1"]))
+        return F.layer_norm(h + F.linear(g, f["w_2"], f["b_2"]), (H,), f["ln2_w"], f["ln2_b"], 1e-12)
+
+    block()
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        block()
+        ts.append(time.perf_counter() - t0)
+    return B * L / statistics.median(ts), torch.get_num_threads()
+
+
+def bert_measure(dev, kunlun, steps, warmup, flush):
+    """Device time per encoder block forward (CUDA events) and tokens/s."""
+    from torch_kunlun_b200 import encoder
+    x, w, mask = bert_inputs()
+    xd, wd, md = x.to(dev), w.to(dev), mask.to(dev)
+
+    def step():
+        encoder.encoder_block(xd, wd, md, heads=BERT_HEADS, eps=1e-12)
+
+    times = timed_steps(step, steps, warmup, flush, kunlun)
+    ms = sum(times) / len(times)
+    macs = encoder.encoder_block_macs(BERT_B, BERT_L, BERT_H, BERT_F)
+    return {"tokens_per_s": BERT_B * BERT_L / (ms / 1000), "ms_per_block": ms,
+            "effective_tops": 2 * macs / (ms / 1000) / 1e12, "steps": steps, "warmup": warmup,
+            "workload": BERT_WORKLOAD}
+
+
 def dist_env():
     return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
             int(os.environ.get("WORLD_SIZE", "1")))
@@ -262,7 +324,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="kunlun", choices=["kunlun", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="linear", choices=["linear", "tp_mlp"])
+    ap.add_argument("--no-bert", action="store_true", help="skip the encoder-block measurement")
+    ap.add_argument("--workload", default="linear", choices=["linear", "tp_mlp", "bert"])
     ap.add_argument("--reduce", default="allreduce", choices=["allreduce", "reduce_scatter"])
     args = ap.parse_args()
     if args.workload == "tp_mlp" and args.impl != "reference":
@@ -270,6 +333,8 @@ def main():
     if args.impl == "reference":
         return run_reference(args)
     args.warmup = max(args.warmup, 3)
+    if args.workload == "bert":
+        return run_bert(args)
 
     import torch
     import torch_kunlun  # noqa: F401
@@ -327,12 +392,19 @@ def main():
     e2e_ms = sum(e2e_times) / len(e2e_times)
 
     parts = kernel_breakdown(xd, wd, bd, out, kunlun, flush)
+    bert = None
+    if not args.no_bert:
+        bert = bert_measure(dev, kunlun, max(5, args.steps // 10), args.warmup, flush)
 
     # max over ranks of the timed quantities
     if pg:
-        t = torch.tensor([ms, e2e_ms, parts["gemm"]], dtype=torch.float64)
+        t = torch.tensor([ms, e2e_ms, parts["gemm"], bert["ms_per_block"] if bert else 0.0],
+                         dtype=torch.float64)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        ms, e2e_ms, gemm_ms = t.tolist()
+        ms, e2e_ms, gemm_ms, bert_ms = t.tolist()
+        if bert:
+            bert["ms_per_block"] = bert_ms
+            bert["tokens_per_s"] = world * BERT_B * BERT_L / (bert_ms / 1000)
     else:
         gemm_ms = parts["gemm"]
 
@@ -347,6 +419,11 @@ def main():
                     "cores": os.cpu_count() or 1, "kind": "port",
                     "sample": "256 of 2048 rows of x with all of W per call, 3 calls "
                               "(oracle: C quantise + exact fp64 BLAS GEMM + C epilogue)"}
+        if bert:
+            tps, threads = bert_cpu_baseline()
+            bert["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads,
+                                    "kind": "torch CPU aten fp32 eager",
+                                    "sample": "1 of 32 sequences (512 tokens), median of 3"}
 
     if rank == 0:
         value = world * OPS_PER_STEP / (ms / 1000) / 1e12
@@ -374,11 +451,33 @@ def main():
             "gpu_launches": KERNELS_PER_STEP * args.steps,
             "clocks": clock,
             "cpu_baseline": cpu_base,
+            "bert_block": bert,
         }
         print(json.dumps(line), flush=True)
     if pg:
         pg.barrier()
         pg.destroy_process_group()
+    return 0
+
+
+def run_bert(args):
+    """Encoder block alone on one GPU (tokens/s)."""
+    import torch
+    import torch_kunlun  # noqa: F401
+    kunlun = torch_kunlun.kunlun
+    dev = torch.device("kunlun", 0)
+    scratch = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        r = bert_measure(dev, kunlun, args.steps, args.warmup, lambda: scratch.fill_(1))
+    line = {"metric": "BERT-block tokens/s", "value": r["tokens_per_s"], "unit": "tokens/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": r["ms_per_block"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int16",
+            "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, no dataset)",
+            "config": {"workload": BERT_WORKLOAD, "parallelism": "single GPU",
+                       "l2": "flushed between steps (512 MiB device write outside the timed events)"},
+            "effective_tops": r["effective_tops"], "clocks": clocks.summary()}
+    print(json.dumps(line), flush=True)
     return 0
 
 

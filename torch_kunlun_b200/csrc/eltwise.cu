@@ -89,6 +89,25 @@ __device__ __forceinline__ void store_any(void* p, int t, int64_t i, double v) {
     }
 }
 
+// 32-bit index variant for index spaces below 2^31 elements.
+template <typename E>
+__global__ void copy_same_kernel32(E* __restrict__ dst, const E* __restrict__ src, int n,
+                                   Strided d) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        int rem = i;
+        long long od = 0, os = 0;
+#pragma unroll 1
+        for (int k = d.ndim - 1; k >= 0; --k) {
+            const int sz = static_cast<int>(d.sizes[k]);
+            const int idx = rem % sz;
+            rem /= sz;
+            od += idx * d.s0[k];
+            os += idx * d.s1[k];
+        }
+        dst[od] = src[os];
+    }
+}
+
 template <typename E>
 __global__ void copy_same_kernel(E* __restrict__ dst, const E* __restrict__ src, int64_t n,
                                  Strided d) {
@@ -246,6 +265,76 @@ bool is_dense(int ndim, const int64_t* sizes, const int64_t* strides) {
     return true;
 }
 
+// Merge adjacent dims that are contiguous in both operands, drop size-1 dims.
+void collapse(Strided& d) {
+    Strided o;
+    o.ndim = 0;
+    for (int k = 0; k < d.ndim; ++k) {
+        if (d.sizes[k] == 1) continue;
+        if (o.ndim > 0) {
+            const int j = o.ndim - 1;
+            if (o.s0[j] == d.sizes[k] * d.s0[k] && o.s1[j] == d.sizes[k] * d.s1[k]) {
+                o.sizes[j] *= d.sizes[k];
+                o.s0[j] = d.s0[k];
+                o.s1[j] = d.s1[k];
+                continue;
+            }
+        }
+        o.sizes[o.ndim] = d.sizes[k];
+        o.s0[o.ndim] = d.s0[k];
+        o.s1[o.ndim] = d.s1[k];
+        ++o.ndim;
+    }
+    if (o.ndim == 0) {
+        o.ndim = 1;
+        o.sizes[0] = 1;
+        o.s0[0] = o.s1[0] = 0;
+    }
+    d = o;
+}
+
+// Same-dtype strided copy: collapsed dims, 16-byte vectors along a shared
+// contiguous innermost dim when alignment allows, 32-bit indexing when the
+// index space fits.
+int copy_same_fast(void* dst, const void* src, int es, Strided d, cudaStream_t stream) {
+    collapse(d);
+    const int last = d.ndim - 1;
+    const int vec = 16 / es;
+    bool v16 = d.s0[last] == 1 && d.s1[last] == 1 && d.sizes[last] % vec == 0 &&
+               reinterpret_cast<uintptr_t>(dst) % 16 == 0 && reinterpret_cast<uintptr_t>(src) % 16 == 0;
+    for (int k = 0; k < last && v16; ++k) v16 = d.s0[k] % vec == 0 && d.s1[k] % vec == 0;
+    int e = es;
+    if (v16) {
+        d.sizes[last] /= vec;
+        for (int k = 0; k < last; ++k) {
+            d.s0[k] /= vec;
+            d.s1[k] /= vec;
+        }
+        e = 16;
+    }
+    int64_t n = 1;
+    for (int k = 0; k < d.ndim; ++k) n *= d.sizes[k];
+    const int grid = grid_for(n);
+    const bool small = n < (1LL << 31);
+    auto go = [&](auto tag) {
+        using E = decltype(tag);
+        if (small)
+            copy_same_kernel32<E><<<grid, kThreads, 0, stream>>>(
+                static_cast<E*>(dst), static_cast<const E*>(src), static_cast<int>(n), d);
+        else
+            copy_same_kernel<E><<<grid, kThreads, 0, stream>>>(static_cast<E*>(dst),
+                                                                static_cast<const E*>(src), n, d);
+    };
+    switch (e) {
+        case 1: go(uint8_t{}); break;
+        case 2: go(uint16_t{}); break;
+        case 4: go(uint32_t{}); break;
+        case 8: go(static_cast<unsigned long long>(0)); break;
+        default: go(uint4{}); break;
+    }
+    return launch_status("copy_strided");
+}
+
 }  // namespace
 }  // namespace tk
 
@@ -281,20 +370,7 @@ int tk_copy_strided(void* dst, int dst_type, const void* src, int src_type, int 
                                                          static_cast<const __half*>(src), n);
         return launch_status("copy f16->f32");
     }
-    if (dst_type == src_type) {
-        switch (scalar_size(dst_type)) {
-            case 1: copy_same_kernel<uint8_t><<<grid, kThreads, 0, stream>>>(
-                        static_cast<uint8_t*>(dst), static_cast<const uint8_t*>(src), n, d); break;
-            case 2: copy_same_kernel<uint16_t><<<grid, kThreads, 0, stream>>>(
-                        static_cast<uint16_t*>(dst), static_cast<const uint16_t*>(src), n, d); break;
-            case 4: copy_same_kernel<uint32_t><<<grid, kThreads, 0, stream>>>(
-                        static_cast<uint32_t*>(dst), static_cast<const uint32_t*>(src), n, d); break;
-            default: copy_same_kernel<unsigned long long><<<grid, kThreads, 0, stream>>>(
-                        static_cast<unsigned long long*>(dst),
-                        static_cast<const unsigned long long*>(src), n, d); break;
-        }
-        return launch_status("copy_strided");
-    }
+    if (dst_type == src_type) return copy_same_fast(dst, src, scalar_size(dst_type), d, stream);
     copy_convert_kernel<<<grid, kThreads, 0, stream>>>(dst, dst_type, src, src_type, n, d);
     return launch_status("copy_convert");
 }

@@ -96,7 +96,8 @@ void xccl_barrier(int device);
 
 // ---- fused ops exposed to Python ----
 at::Tensor linear_act(const at::Tensor& input, const at::Tensor& weight,
-                      const std::optional<at::Tensor>& bias, int64_t act);
+                      const std::optional<at::Tensor>& bias, int64_t act,
+                      const std::optional<at::Tensor>& residual);
 at::Tensor silu_mul(const at::Tensor& gate, const at::Tensor& up);
 at::Tensor amax(const at::Tensor& x);
 at::Tensor linear_scaled(const at::Tensor& input, const at::Tensor& weight,

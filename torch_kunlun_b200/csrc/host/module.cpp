@@ -87,7 +87,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("xccl_barrier", &xccl_barrier);
 
     m.def("linear_act", &linear_act, py::arg("input"), py::arg("weight"),
-          py::arg("bias") = py::none(), py::arg("act") = 0);
+          py::arg("bias") = py::none(), py::arg("act") = 0, py::arg("residual") = py::none());
     m.def("silu_mul", &silu_mul);
     m.def("amax", &amax);
     m.def("linear_scaled", &linear_scaled, py::arg("input"), py::arg("weight"),

@@ -249,7 +249,8 @@ at::Tensor convolution_overrideable(const at::Tensor& input, const at::Tensor& w
 
 // y = act(x @ W^T + b) for x [..., K], W [N, K] in one call.
 at::Tensor linear_act(const at::Tensor& input, const at::Tensor& weight,
-                      const std::optional<at::Tensor>& bias, int64_t act) {
+                      const std::optional<at::Tensor>& bias, int64_t act,
+                      const std::optional<at::Tensor>& residual) {
     TORCH_CHECK(input.dim() >= 1 && weight.dim() == 2, "kunlun linear: bad ranks");
     check_operand(weight, input, "linear");
     const int64_t K = input.size(-1);
@@ -262,8 +263,14 @@ at::Tensor linear_act(const at::Tensor& input, const at::Tensor& weight,
     at::Tensor out = at::empty({x2.size(0), N}, input.options());
     if (out.numel() > 0) {
         at::Tensor o3 = out.unsqueeze(0);
-        run_qgemm(x2.unsqueeze(0), weight.unsqueeze(0), o3, bias, nullptr, 1.0, 0.0,
-                  static_cast<int>(act), true);
+        at::Tensor r3;
+        if (residual.has_value() && residual->defined()) {
+            TORCH_CHECK(residual->numel() == out.numel() && residual->size(-1) == N,
+                        "kunlun linear: residual shape mismatch");
+            r3 = residual->reshape({1, x2.size(0), N});
+        }
+        run_qgemm(x2.unsqueeze(0), weight.unsqueeze(0), o3, bias, r3.defined() ? &r3 : nullptr,
+                  1.0, r3.defined() ? 1.0 : 0.0, static_cast<int>(act), true);
     }
     return out.view(out_shape);
 }
@@ -322,7 +329,7 @@ namespace {
 
 at::Tensor linear_fwd(const at::Tensor& input, const at::Tensor& weight,
                       const std::optional<at::Tensor>& bias) {
-    return linear_act(input, weight, bias, TK_ACT_NONE);
+    return linear_act(input, weight, bias, TK_ACT_NONE, std::nullopt);
 }
 
 // Autograd entry for linear: without gradients the fused kernel runs below

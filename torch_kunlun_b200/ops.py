@@ -21,8 +21,11 @@ ACT = {"none": 0, "relu": 1, "gelu": 2, "gelu_tanh": 3, "silu": 4}
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
-           act: str = "none") -> torch.Tensor:
-    return _C.linear_act(x, weight, bias, ACT[act])
+           act: str = "none", residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """act(x @ w^T + b) [+ residual]: with a residual the epilogue adds it
+    after the bias (rounded to T), giving the values of linear followed by a
+    separate add (csrc/ops.cpp:480-495 then csrc/ops.cpp:117-149)."""
+    return _C.linear_act(x, weight, bias, ACT[act], residual)
 
 
 def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
