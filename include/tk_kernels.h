@@ -194,6 +194,40 @@ TK_API size_t tk_conv2d_workspace_size(const tk_conv2d_desc_t* desc);
 TK_API int tk_conv2d_q16(const tk_conv2d_desc_t* desc, void* workspace, size_t workspace_bytes,
                          void* stream);
 
+/* ---- fused scaled-dot-product attention -------------------------------------
+ * out = softmax(T(T(T(q k^T) * scale) + mask)) v over [batch, heads] slices,
+ * with the reference's composition semantics
+ * (torch_kunlun/kunlun/attention.py:36-107, csrc/ops_nn.cpp:199-221): per-slice
+ * max-abs int16 quantisation of q, k, v and of the softmax output P, exact
+ * integer MAC, dequantisation, every intermediate rounded to T where the
+ * reference writes a T tensor.  The causal mask adds -1e4 above the diagonal
+ * and the additive mask (type T, any broadcast strides) is added after it as
+ * a separately rounded add.  The [L, S] scores never reach HBM: a statistics
+ * pass (row max and sum of exponentials, the slice's max probability) and an
+ * output pass recompute them on the tensor cores.
+ * Limits: e <= 128, s <= 32768.  Strides are in elements over
+ * (batch, heads, row, column); mask strides may be 0 (broadcast). */
+typedef struct {
+    tk_dtype_t dtype;
+    int64_t batch, heads, l, s, e, ev;
+    const void* q;
+    int64_t q_strides[4];
+    const void* k;
+    int64_t k_strides[4];
+    const void* v;
+    int64_t v_strides[4];
+    void* out;
+    int64_t out_strides[4];
+    const void* mask; /* NULL = none */
+    int64_t mask_strides[4];
+    int causal;
+    float scale; /* multiplier of q k^T; the reference passes 1/sqrt(e) */
+} tk_sdpa_desc_t;
+
+TK_API size_t tk_sdpa_workspace_size(const tk_sdpa_desc_t* desc);
+TK_API int tk_sdpa_q16(const tk_sdpa_desc_t* desc, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
 /* ---- row ops ------------------------------------------------------------------
  * Softmax over the last dimension of a contiguous [rows, cols] tensor
  * (xdnn::softmax, csrc/ops_nn.cpp:73-83); out_dtype may be fp32 for fp16

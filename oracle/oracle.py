@@ -314,7 +314,7 @@ def round_t(v: np.ndarray, dtype) -> np.ndarray:
     return bits.view(np.float16).reshape(v.shape)
 
 
-def sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask=None, scale=None):
+def sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask=None, scale=None, causal=False):
     """The reference's SDPA composition over [BH, L, E] slices.
 
     Steps (torch_kunlun/kunlun/attention.py:85-106): per-slice quantised bmm
@@ -329,6 +329,12 @@ def sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask=None, scale=None):
     factor = (1.0 / np.sqrt(E)) if scale is None else float(scale)
     if factor != 1.0:
         s = round_t(s.astype(np.float32) * np.float32(factor), q.dtype)
+    if causal:
+        # -1e4 strictly above the diagonal, added as its own rounded step
+        # (torch_kunlun/kunlun/attention.py:89-95)
+        S = k.shape[1]
+        tri = np.triu(np.full((L, S), -1.0e4, dtype=np.float32), 1)
+        s = round_t(s.astype(np.float32) + tri, q.dtype)
     if mask is not None:
         s = round_t(s.astype(np.float32) + np.broadcast_to(mask, s.shape).astype(np.float32),
                     q.dtype)

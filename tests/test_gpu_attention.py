@@ -1,0 +1,142 @@
+"""Fused scaled-dot-product attention (tk_sdpa_q16) against the oracle's
+restatement of the reference composition (torch_kunlun/kunlun/attention.py:
+per-slice quantised q k^T, scale, causal / additive mask, softmax, per-slice
+quantised P v) and against the backend's own composed path.
+
+The scores and both products are integer-exact; softmax is the one
+floating-point reduction (its fp16 output may differ by an ulp from the
+float64 oracle, and the second quantised product carries that), so outputs
+are compared at a stated absolute tolerance relative to max|v|."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+torch_kunlun = pytest.importorskip("torch_kunlun")
+kunlun = torch_kunlun.kunlun
+from oracle import oracle as O  # noqa: E402
+from torch_kunlun_b200 import _C  # noqa: E402
+
+DEV = "kunlun"
+
+
+def rnd(shape, seed, dtype=torch.float16, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(shape, generator=g) * scale).to(dtype)
+
+
+def oracle_sdpa(q, k, v, mask=None, causal=False, scale=None):
+    """q, k, v CPU [B, H, L, E]; mask broadcastable to [B, H, L, S]."""
+    B, H, L, E = q.shape
+    S, Ev = k.shape[2], v.shape[3]
+    m3 = None
+    if mask is not None:
+        m3 = mask.to(q.dtype).expand(B, H, L, S).reshape(B * H, L, S).numpy()
+    out = O.sdpa(q.reshape(B * H, L, E).numpy(), k.reshape(B * H, S, E).numpy(),
+                 v.reshape(B * H, S, Ev).numpy(), mask=m3, scale=scale, causal=causal)
+    return torch.from_numpy(out.astype(np.float32)).reshape(B, H, L, Ev)
+
+
+def check(got, want, v, tol=2e-2):
+    err = (got.float() - want).abs().max().item()
+    assert err <= tol * max(1.0, v.abs().max().item()), err
+
+
+CASES = [
+    # B, H, L, S, E, Ev
+    (1, 2, 128, 128, 64, 64),
+    (2, 3, 100, 77, 40, 24),     # ragged rows, keys and head dims
+    (1, 2, 200, 300, 128, 128),  # two limb chunks, two output tiles
+    (2, 1, 64, 512, 64, 96),
+    (1, 1, 1, 1, 8, 8),
+]
+
+
+@pytest.mark.parametrize("B,H,L,S,E,Ev", CASES)
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_fused_matches_oracle(B, H, L, S, E, Ev, dtype):
+    q, k, v = rnd((B, H, L, E), 1, dtype), rnd((B, H, S, E), 2, dtype), rnd((B, H, S, Ev), 3, dtype)
+    out = kunlun.scaled_dot_product_attention(q.to(DEV), k.to(DEV), v.to(DEV)).cpu()
+    assert out.shape == (B, H, L, Ev) and out.dtype == dtype
+    check(out, oracle_sdpa(q, k, v), v)
+
+
+@pytest.mark.parametrize("mask_shape", ["2d", "3d_batch", "4d_keys", "4d_full", "bool"])
+def test_fused_masks_match_oracle(mask_shape):
+    B, H, L, S, E = 2, 3, 96, 160, 64
+    q, k, v = rnd((B, H, L, E), 4), rnd((B, H, S, E), 5), rnd((B, H, S, E), 6)
+    g = torch.Generator().manual_seed(7)
+    if mask_shape == "2d":
+        mask = (torch.randn(L, S, generator=g) * 2).half()
+    elif mask_shape == "3d_batch":
+        mask = (torch.randn(B, L, S, generator=g) * 2).half()
+    elif mask_shape == "4d_keys":
+        mask = torch.zeros(B, 1, 1, S, dtype=torch.float16)
+        mask[..., S - 40:] = -1e4
+    elif mask_shape == "4d_full":
+        mask = (torch.randn(B, H, L, S, generator=g) * 2).half()
+    else:
+        mask = torch.rand(L, S, generator=g) < 0.3
+    out = kunlun.scaled_dot_product_attention(q.to(DEV), k.to(DEV), v.to(DEV),
+                                              attn_mask=mask.to(DEV)).cpu()
+    om = mask
+    if mask.dtype == torch.bool:
+        om = mask.half() * -1e4
+    if mask_shape == "3d_batch":
+        om = mask.unsqueeze(1)
+    check(out, oracle_sdpa(q, k, v, mask=om), v)
+
+
+def test_fused_causal_scale_and_mask():
+    B, H, L, S, E = 1, 4, 130, 130, 64
+    q, k, v = rnd((B, H, L, E), 8), rnd((B, H, S, E), 9), rnd((B, H, S, E), 10)
+    mask = torch.zeros(B, 1, 1, S, dtype=torch.float16)
+    mask[..., :5] = -1e4
+    out = kunlun.scaled_dot_product_attention(q.to(DEV), k.to(DEV), v.to(DEV), attn_mask=mask.to(DEV),
+                                              is_causal=True, scale=0.3).cpu()
+    check(out, oracle_sdpa(q, k, v, mask=mask, causal=True, scale=0.3), v)
+    out2 = kunlun.scaled_dot_product_attention(q.to(DEV), k.to(DEV), v.to(DEV), is_causal=True).cpu()
+    check(out2, oracle_sdpa(q, k, v, causal=True), v)
+
+
+def test_fused_equals_composed_path():
+    B, H, L, S, E = 2, 4, 256, 256, 64
+    q, k, v = rnd((B, H, L, E), 11), rnd((B, H, S, E), 12), rnd((B, H, S, E), 13)
+    mask = torch.zeros(B, 1, 1, S, dtype=torch.float16)
+    mask[..., S - 32:] = -1e4
+    args = (q.to(DEV), k.to(DEV), v.to(DEV), mask.to(DEV), False, None)
+    fused = _C.sdpa(*args, fused=True).cpu().float()
+    composed = _C.sdpa(*args, fused=False).cpu().float()
+    # both are the reference composition; only the softmax sum order differs
+    assert (fused - composed).abs().max().item() < 2e-2
+
+
+def test_fused_reads_strided_head_views():
+    """Head-split views of a packed [B, L, 3, H, E] projection give the same
+    result as contiguous copies, and the output's heads merge with a view."""
+    B, L, H, E = 2, 192, 4, 64
+    qkv = rnd((B, L, 3, H, E), 14)
+    view = qkv.to(DEV).permute(2, 0, 3, 1, 4)
+    out_v = kunlun.scaled_dot_product_attention(view[0], view[1], view[2])
+    cont = qkv.permute(2, 0, 3, 1, 4).contiguous()
+    out_c = kunlun.scaled_dot_product_attention(cont[0].to(DEV), cont[1].to(DEV), cont[2].to(DEV))
+    assert torch.equal(out_v.cpu(), out_c.cpu())
+    merged = out_v.transpose(1, 2)
+    assert merged.is_contiguous()  # [B, L, H, E] storage: no copy to merge heads
+    ref = torch.nn.functional.scaled_dot_product_attention(cont[0].float(), cont[1].float(),
+                                                           cont[2].float())
+    assert torch.allclose(out_v.cpu().float(), ref, atol=3e-2, rtol=3e-2)
+
+
+def test_fused_large_magnitudes_and_zero_slice():
+    B, H, L, S, E = 1, 2, 64, 64, 32
+    q = rnd((B, H, L, E), 15, scale=30.0)
+    k = rnd((B, H, S, E), 16, scale=30.0)
+    v = rnd((B, H, S, E), 17)
+    v[:, 1] = 0.0  # a zero slice: amax 0, quantisation to zero
+    out = kunlun.scaled_dot_product_attention(q.to(DEV), k.to(DEV), v.to(DEV)).cpu()
+    assert torch.all(out[:, 1] == 0)
+    check(out, oracle_sdpa(q, k, v), v)

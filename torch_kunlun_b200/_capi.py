@@ -25,7 +25,7 @@ EXPORTED = [
     "tk_quantize_limbs", "tk_qgemm_workspace_size", "tk_qgemm", "tk_qgemm_simt",
     "tk_qgemm_debug", "tk_qgemm_from_limbs", "tk_copy_strided", "tk_fill_strided",
     "tk_binary", "tk_unary", "tk_silu_mul", "tk_conv2d_workspace_size", "tk_conv2d_q16",
-    "tk_softmax", "tk_layer_norm", "tk_qgemm_noalloc",
+    "tk_softmax", "tk_layer_norm", "tk_qgemm_noalloc", "tk_sdpa_workspace_size", "tk_sdpa_q16",
 ]
 
 
@@ -55,6 +55,22 @@ class QGemmDesc(ctypes.Structure):
 _lib = None
 
 
+class SdpaDesc(ctypes.Structure):
+    """Mirror of tk_sdpa_desc_t."""
+    _fields_ = [
+        ("dtype", ctypes.c_int),
+        ("batch", ctypes.c_int64), ("heads", ctypes.c_int64), ("l", ctypes.c_int64),
+        ("s", ctypes.c_int64), ("e", ctypes.c_int64), ("ev", ctypes.c_int64),
+        ("q", ctypes.c_void_p), ("q_strides", ctypes.c_int64 * 4),
+        ("k", ctypes.c_void_p), ("k_strides", ctypes.c_int64 * 4),
+        ("v", ctypes.c_void_p), ("v_strides", ctypes.c_int64 * 4),
+        ("out", ctypes.c_void_p), ("out_strides", ctypes.c_int64 * 4),
+        ("mask", ctypes.c_void_p), ("mask_strides", ctypes.c_int64 * 4),
+        ("causal", ctypes.c_int),
+        ("scale", ctypes.c_float),
+    ]
+
+
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
@@ -70,6 +86,9 @@ def lib() -> ctypes.CDLL:
         L.tk_amax.argtypes = [i32, vp, i64, i64, i64, vp, vp]
         L.tk_quantize_limbs.argtypes = [i32, vp, i64, i64, i64, i64, i64, i64, vp, i64, vp, vp]
         L.tk_qgemm_workspace_size.argtypes = [ctypes.POINTER(QGemmDesc)]
+        L.tk_sdpa_workspace_size.argtypes = [ctypes.POINTER(SdpaDesc)]
+        L.tk_sdpa_workspace_size.restype = ctypes.c_size_t
+        L.tk_sdpa_q16.argtypes = [ctypes.POINTER(SdpaDesc), vp, ctypes.c_size_t, vp]
         L.tk_qgemm_workspace_size.restype = ctypes.c_size_t
         for name in ("tk_qgemm", "tk_qgemm_simt"):
             getattr(L, name).argtypes = [ctypes.POINTER(QGemmDesc), vp, ctypes.c_size_t, vp]

@@ -1,0 +1,1141 @@
+// attention.cu -- fused scaled-dot-product attention on sm_100a tensor cores
+// with the reference's int16-quantised composition semantics.
+//
+// The reference computes attention as separate launches
+// (torch_kunlun/kunlun/attention.py:36-107): a per-slice quantised bmm
+// q @ k^T (csrc/ops_nn.cpp:199-221), mul.Scalar by the scale, add of the
+// causal / additive mask, softmax (csrc/ops_nn.cpp:73-83) and a per-slice
+// quantised bmm with v, each a kernel writing and re-reading [L, S] tensors.
+// Here three kernels do the same arithmetic:
+//
+//   attn_quant_kernel   per (batch, head) slice of q, k, v: max-abs, then
+//                       int16 quantisation into int8 limb rows laid out for
+//                       the tensor cores (v transposed); zeroes the slice's
+//                       probability amax.
+//   attn_stats_kernel   S = q k^T on the tensor cores (three limb
+//                       accumulators in TMEM); on the CUDA cores the exact
+//                       dequantised, scaled, masked scores (each step rounded
+//                       to T as the reference's separate launches round),
+//                       written once as T, the row max and sum of
+//                       exponentials, and the slice's largest probability --
+//                       the per-slice amax with which the reference's second
+//                       bmm quantises P.
+//   attn_out_kernel     reads the scores back by TMA, forms
+//                       P = T(exp(s - m) / l), quantises it with the slice
+//                       scale into shared memory as limb tiles and
+//                       accumulates P v on the tensor cores; the epilogue
+//                       dequantises O and stores it through its strides.
+// Compared with the composition, the softmax pass, the probability tensor
+// (written, read for its amax, read again to quantise) and its limb planes
+// never reach HBM, and the score epilogue runs once.
+//
+// Limb layout ("64-interleaved"): an int16 row of 64*G values is stored as G
+// chunks of 128 bytes, chunk g = [hi of values 64g..64g+63 | lo of the same],
+// hi = q >> 8 (signed), lo = q & 255 (unsigned).  A 128-byte chunk is one
+// 128B-swizzle row, so a tile of chunk rows is loaded by TMA with
+// SWIZZLE_128B and consumed by tcgen05.mma kind::i8 through K-major
+// descriptors: the hi part is K sub-blocks 0..1 (32 bytes each), the lo part
+// sub-blocks 2..3.  Per 32-byte sub-block pair four MMAs produce
+//   HH += hi*hi,  MID += hi*lo + lo*hi,  LL += lo*lo
+// which recombine exactly as 65536*HH + 256*MID + LL.
+//
+// CTA roles of both tensor-core kernels (320 threads, one CTA per SM,
+// persistent over 128-row query tiles):
+//   warp 0      TMA producer (4-stage ring);
+//   warp 1      TMEM owner and MMA issuer;
+//   warps 2..9  CUDA-core work: warp w owns TMEM lane quarter w % 4 (32
+//               query rows) and one half (32 keys) of each 64-key tile.
+// Every wait is bounded (error word + abort flag); no TMA multicast is used.
+#include <cuda.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "tk_internal.h"
+#include "tk_numerics.cuh"
+#include "tk_ptx.cuh"
+
+namespace tk {
+namespace {
+
+constexpr int BM = 128;              // query rows per tile
+constexpr int BKEY = 64;             // keys per tile
+constexpr int EVT = 64;              // value columns per output tile
+constexpr int STAGES = 4;
+constexpr int NUM_SOFT_WARPS = 8;
+constexpr int NUM_THREADS = 64 + 32 * NUM_SOFT_WARPS;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t COL_S = 0;        // S: HH, MID, LL at +0, +64, +128
+constexpr uint32_t COL_O = 256;      // O: HH, MID, LL at +256, +320, +384
+constexpr int Q_CHUNK = BM * 128;    // bytes of one 128-row chunk tile
+constexpr int K_CHUNK = BKEY * 128;
+constexpr int V_TILE = EVT * 128;
+constexpr int P_TILE = BM * 128;
+constexpr float kMaskedValue = -1.0e4f;  // the reference's causal fill
+
+constexpr uint32_t IDESC_SS = idesc_i8(BM, 64, true, true);
+constexpr uint32_t IDESC_SU = idesc_i8(BM, 64, true, false);
+constexpr uint32_t IDESC_US = idesc_i8(BM, 64, false, true);
+constexpr uint32_t IDESC_UU = idesc_i8(BM, 64, false, false);
+
+// Shared memory of the statistics kernel.
+template <int G>
+struct StatsSmem {
+    static constexpr int STAGE_BYTES = G * K_CHUNK;
+    static constexpr int OFF_Q = 0;
+    static constexpr int OFF_STAGE = OFF_Q + G * Q_CHUNK;
+    static constexpr int OFF_RED = OFF_STAGE + STAGES * STAGE_BYTES;  // float[2][2][BM]
+    static constexpr int OFF_BAR = OFF_RED + 4 * BM * 4;
+    static constexpr int NUM_BARS = 2 * STAGES + 7;
+    static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+    static constexpr int ALLOC = OFF_MISC + 16 + 1024;  // + slack for 1024-byte alignment
+};
+
+// Shared memory of the output kernel.
+template <int DT>
+struct OutSmem {
+    static constexpr int S_BYTES = BM * BKEY * (DT == 0 ? 2 : 4);
+    static constexpr int STAGE_BYTES = S_BYTES + V_TILE;
+    static constexpr int OFF_STAGE = 0;
+    static constexpr int OFF_P = OFF_STAGE + STAGES * STAGE_BYTES;
+    static constexpr int OFF_BAR = OFF_P + 2 * P_TILE;
+    static constexpr int NUM_BARS = 2 * STAGES + 7;
+    static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+    static constexpr int ALLOC = OFF_MISC + 16 + 1024;
+};
+
+struct AttnParams {
+    int B, H, L, S, Ev;
+    int64_t Spad;   // keys per score row in the workspace (multiple of 64)
+    int n_kt;       // key tiles of 64
+    int m_tiles;    // query tiles of 128 per slice
+    int ev_tiles;   // output column tiles of 64 (1 in the statistics kernel)
+    int tiles;      // work items
+    const float* amax;       // [3][B*H]: q, k, v
+    unsigned* amax_p;        // [B*H] float bits of the slice's max probability
+    float* row_max;          // [B*H*L]
+    float* row_inv;          // [B*H*L] 1 / sum of exponentials
+    void* scores;            // [B*H][L][Spad] T
+    void* out;
+    int64_t os[4];
+    int out_vec;             // 16-byte vector stores of 32 consecutive columns
+    const void* mask;
+    int mask_vec;            // mask rows contiguous and 16-byte aligned: vector loads
+    int64_t ms[4];
+    int causal;
+    float scale;
+    unsigned* err;
+};
+
+__device__ __forceinline__ void decode(const AttnParams& p, int tile, int& bh, int& mt, int& evh) {
+    evh = tile % p.ev_tiles;
+    const int r = tile / p.ev_tiles;
+    mt = r % p.m_tiles;
+    bh = r / p.m_tiles;
+}
+
+// exp(x) as 2^(x log2 e) on the special-function unit.  Both kernels use the
+// same function, so the largest probability found by the statistics kernel
+// is exactly the one the output kernel quantises.
+__device__ __forceinline__ float exp_fast(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
+    return y;
+}
+
+// 32 consecutive scores j0..j0+31 of query row i in the reference
+// composition: the exact limb dot product, T(acc * s_qk), T(. * scale), the
+// causal -1e4 and the additive mask, each rounded to T; padding keys
+// (j >= S) become -inf.  The conditions are uniform per call, so each step is
+// a branch-free loop over the 32 elements.
+template <int DT>
+__device__ __forceinline__ void scores32(const uint32_t (&hh)[32], const uint32_t (&mid)[32],
+                                         const uint32_t (&ll)[32], double sqk, const AttnParams& p,
+                                         int64_t i, int64_t j0, const void* mask_row, float (&s)[32]) {
+#pragma unroll
+    for (int c = 0; c < 32; ++c)
+        s[c] = round_t_from_double(__dmul_rn(limb_acc_to_double(hh[c], mid[c], ll[c]), sqk), DT);
+    if (p.scale != 1.0f) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) s[c] = round_t(__fmul_rn(s[c], p.scale), DT);
+    }
+    if (p.causal && j0 + 31 > i) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+            const float t = round_t(__fadd_rn(s[c], kMaskedValue), DT);
+            s[c] = (j0 + c > i) ? t : s[c];
+        }
+    }
+    const bool full = j0 + 32 <= p.S;
+    if (mask_row != nullptr) {
+        float mv[32];
+        if (full && p.mask_vec) {
+            if constexpr (DT == 0) {
+                const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __half*>(mask_row) + j0);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint4 u = __ldg(src + k);
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = __half22float2(h2[e]);
+                        mv[8 * k + 2 * e] = f.x;
+                        mv[8 * k + 2 * e + 1] = f.y;
+                    }
+                }
+            } else {
+                const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(mask_row) + j0);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const float4 f = __ldg(src + k);
+                    mv[4 * k] = f.x; mv[4 * k + 1] = f.y; mv[4 * k + 2] = f.z; mv[4 * k + 3] = f.w;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                const int64_t j = j0 + c < p.S ? j0 + c : p.S - 1;  // clamped: padding keys are overwritten below
+                mv[c] = DT == 0 ? __half2float(__ldg(static_cast<const __half*>(mask_row) + j * p.ms[3]))
+                                : __ldg(static_cast<const float*>(mask_row) + j * p.ms[3]);
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 32; ++c) s[c] = round_t(__fadd_rn(s[c], mv[c]), DT);
+    }
+    if (!full) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) s[c] = (j0 + c < p.S) ? s[c] : -INFINITY;
+    }
+}
+
+template <int DT>
+__device__ __forceinline__ void store_row32(void* base, const float (&v)[32]) {
+    if constexpr (DT == 0) {
+        uint4* dst = static_cast<uint4*>(base);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            uint32_t w[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                __half2 h2 = __floats2half2_rn(v[8 * c + 2 * k], v[8 * c + 2 * k + 1]);
+                w[k] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+            dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    } else {
+        float4* dst = static_cast<float4*>(base);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) dst[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+    }
+}
+
+// ---- statistics kernel: scores, row max / sum, slice max probability ---------
+
+template <int G, int DT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+attn_stats_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const AttnParams p) {
+    using L = StatsSmem<G>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+    uint64_t* stage_full = bars;
+    uint64_t* stage_empty = bars + STAGES;
+    uint64_t* q_full = bars + 2 * STAGES;
+    uint64_t* q_empty = q_full + 1;
+    uint64_t* s_full = q_full + 2;
+    uint64_t* s_empty = q_full + 3;
+    uint64_t* c_full = q_full + 4;   // [2] second-half partials published
+    uint64_t* drain_bar = q_full + 6;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* red = reinterpret_cast<float*>(smem + L::OFF_RED);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(stage_full + s), 1);
+            mbar_init(smem_u32(stage_empty + s), 1);
+        }
+        mbar_init(smem_u32(q_full), 1);
+        mbar_init(smem_u32(q_empty), 1);
+        mbar_init(smem_u32(s_full), 1);
+        mbar_init(smem_u32(s_empty), NUM_SOFT_WARPS);
+        mbar_init(smem_u32(c_full), NUM_SOFT_WARPS / 2);
+        mbar_init(smem_u32(c_full + 1), NUM_SOFT_WARPS / 2);
+        mbar_init(smem_u32(drain_bar), 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer: Q once per tile, K per key tile ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t last_phase[STAGES];
+        bool used[STAGES];
+        for (int s = 0; s < STAGES; ++s) { used[s] = false; last_phase[s] = 0; }
+        int q_loads = 0;
+        bool ok = true;
+        int lt = 0;
+        for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, ++lt) {
+            int bh, mt, evh;
+            decode(p, tile, bh, mt, evh);
+            if (!mbar_wait_bounded(smem_u32(q_empty), (static_cast<uint32_t>(lt) & 1u) ^ 1u,
+                                   abort_flag, p.err, kDevErrWaitEmpty))
+                break;
+            if (lane == 0) {
+                const uint32_t fb = smem_u32(q_full);
+                mbar_arrive_expect_tx(fb, G * Q_CHUNK);
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                    tma_load_3d(smem_u32(smem + L::OFF_Q + g * Q_CHUNK), &tmQ, fb, g * 128, mt * BM, bh);
+            }
+            __syncwarp();
+            ++q_loads;
+            for (int t = 0; t < p.n_kt; ++t) {
+                if (!mbar_wait_bounded(smem_u32(stage_empty + stage), phase ^ 1u, abort_flag,
+                                       p.err, kDevErrWaitEmpty)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t fb = smem_u32(stage_full + stage);
+                    uint8_t* sb = smem + L::OFF_STAGE + stage * L::STAGE_BYTES;
+                    mbar_arrive_expect_tx(fb, G * K_CHUNK);
+#pragma unroll
+                    for (int g = 0; g < G; ++g)
+                        tma_load_3d(smem_u32(sb + g * K_CHUNK), &tmK, fb, g * 128, t * BKEY, bh);
+                }
+                __syncwarp();
+                used[stage] = true;
+                last_phase[stage] = phase;
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+        }
+        volatile int no_abort = 0;
+        for (int s = 0; s < STAGES; ++s)
+            if (used[s])
+                mbar_wait_bounded(smem_u32(stage_full + s), last_phase[s], &no_abort, p.err,
+                                  kDevErrWaitDrain);
+        if (q_loads > 0)
+            mbar_wait_bounded(smem_u32(q_full), static_cast<uint32_t>(q_loads - 1) & 1u, &no_abort,
+                              p.err, kDevErrWaitDrain);
+    } else if (warp == 1) {
+        // ---------------- MMA issuer: S = Q K^T per key tile ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t n_s = 0;
+        bool ok = true;
+        int lt = 0;
+        const uint32_t s_hh = tmem_base + COL_S, s_mid = s_hh + 64, s_ll = s_hh + 128;
+        const uint32_t q_base = smem_u32(smem + L::OFF_Q);
+        for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, ++lt) {
+            if (!mbar_wait_bounded(smem_u32(q_full), static_cast<uint32_t>(lt) & 1u, abort_flag,
+                                   p.err, kDevErrWaitFull))
+                break;
+            for (int t = 0; t < p.n_kt; ++t) {
+                if (!mbar_wait_bounded(smem_u32(stage_full + stage), phase, abort_flag, p.err,
+                                       kDevErrWaitFull) ||
+                    !mbar_wait_bounded(smem_u32(s_empty), (n_s & 1u) ^ 1u, abort_flag, p.err,
+                                       kDevErrWaitAccEmpty)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t kb = smem_u32(smem + L::OFF_STAGE + stage * L::STAGE_BYTES);
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        const uint64_t a0 = smem_desc_kmajor_sw128(q_base + g * Q_CHUNK);
+                        const uint64_t b0 = smem_desc_kmajor_sw128(kb + g * K_CHUNK);
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const uint64_t hi = static_cast<uint64_t>((u * 32) >> 4);
+                            const uint64_t lo = static_cast<uint64_t>((64 + u * 32) >> 4);
+                            const uint32_t acc = (g > 0 || u > 0) ? 1u : 0u;
+                            tc_mma_i8(s_hh, a0 + hi, b0 + hi, IDESC_SS, acc);
+                            tc_mma_i8(s_mid, a0 + hi, b0 + lo, IDESC_SU, acc);
+                            tc_mma_i8(s_mid, a0 + lo, b0 + hi, IDESC_US, 1u);
+                            tc_mma_i8(s_ll, a0 + lo, b0 + lo, IDESC_UU, acc);
+                        }
+                    }
+                    tc_commit(smem_u32(s_full));
+                    tc_commit(smem_u32(stage_empty + stage));
+                }
+                __syncwarp();
+                ++n_s;
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+            if (!ok) break;
+            if (lane == 0) tc_commit(smem_u32(q_empty));
+            __syncwarp();
+        }
+        if (lane == 0) tc_commit(smem_u32(drain_bar));
+        __syncwarp();
+        volatile int no_abort = 0;
+        mbar_wait_bounded(smem_u32(drain_bar), 0, &no_abort, p.err, kDevErrWaitDrain);
+    } else {
+        // ---------------- scores and statistics (warps 2..9) ----------------
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row = quarter * 32 + lane;
+        const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        const int BH = p.B * p.H;
+        constexpr int ES = DT == 0 ? 2 : 4;
+        uint32_t n_s = 0;
+        int lt = 0;
+        for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++lt) {
+            int bh, mt, evh;
+            decode(p, tile, bh, mt, evh);
+            const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+            const int64_t i = static_cast<int64_t>(mt) * BM + row;
+            const bool row_ok = i < p.L;
+            const double sqk = dequant_scale(__ldg(p.amax + bh), __ldg(p.amax + BH + bh));
+            const void* mask_row = nullptr;
+            if (p.mask != nullptr && row_ok)
+                mask_row = static_cast<const char*>(p.mask) + (b * p.ms[0] + h * p.ms[1] + i * p.ms[2]) * ES;
+            char* srow = static_cast<char*>(p.scores) + ((static_cast<int64_t>(bh) * p.L + i) * p.Spad) * ES;
+            float m_run = -INFINITY, l_run = 0.0f;
+            bool ok = true;
+            for (int t = 0; t < p.n_kt; ++t) {
+                if (!mbar_wait_bounded(smem_u32(s_full), n_s & 1u, abort_flag, p.err,
+                                       kDevErrWaitAccFull)) {
+                    ok = false;
+                    break;
+                }
+                ++n_s;
+                tc_fence_after();
+                uint32_t hh[32], mid[32], ll[32];
+                const uint32_t col = COL_S + 32 * half;
+                tmem_ld_32x32b_x32(t_lane + col, hh);
+                tmem_ld_32x32b_x32(t_lane + col + 64, mid);
+                tmem_ld_32x32b_x32(t_lane + col + 128, ll);
+                tc_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(s_empty));
+                const int64_t j0 = static_cast<int64_t>(t) * BKEY + 32 * half;
+                float s[32];
+                scores32<DT>(hh, mid, ll, sqk, p, i, j0, mask_row, s);
+                if (row_ok) store_row32<DT>(srow + j0 * ES, s);
+                float tmax = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < 32; ++c) tmax = fmaxf(tmax, s[c]);
+                const float m_new = fmaxf(m_run, tmax);
+                if (m_new != -INFINITY) {
+                    if (m_run != -INFINITY && m_new != m_run) l_run *= exp_fast(m_run - m_new);
+                    m_run = m_new;
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) acc += exp_fast(s[c] - m_run);
+                    l_run += acc;
+                }
+            }
+            if (!ok) break;
+            // Combine the two key halves of each row.  The second-half warps
+            // publish their partials in buffer lt & 1, rewritten two work
+            // items later -- by then the first-half warps have read it (they
+            // release the next item's first S tile only after this combine).
+            const int rb = lt & 1;
+            float* rm = red + rb * 2 * BM;
+            if (half == 1) {
+                rm[row] = m_run;
+                rm[BM + row] = l_run;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(c_full + rb));
+            } else {
+                if (!mbar_wait_bounded(smem_u32(c_full + rb), (static_cast<uint32_t>(lt) >> 1) & 1u,
+                                       abort_flag, p.err, kDevErrWaitFull))
+                    break;
+                const float m1 = rm[row], l1 = rm[BM + row];
+                const float m = fmaxf(m_run, m1);
+                float l = 0.0f;
+                if (m_run != -INFINITY) l += l_run * exp_fast(m_run - m);
+                if (m1 != -INFINITY) l += l1 * exp_fast(m1 - m);
+                const float inv = 1.0f / l;
+                unsigned bits = 0;
+                if (row_ok) {
+                    p.row_max[static_cast<int64_t>(bh) * p.L + i] = m;
+                    p.row_inv[static_cast<int64_t>(bh) * p.L + i] = inv;
+                    // the row's largest probability, T(exp(0) / l)
+                    if (m != -INFINITY) bits = __float_as_uint(round_t(exp_fast(0.0f) * inv, DT));
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, o));
+                if (lane == 0 && bits != 0) atomicMax(p.amax_p + bh, bits);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ---- output kernel: P = softmax(scores), quantised, O = P V -------------------
+
+template <int DT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+attn_out_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmV,
+                const AttnParams p) {
+    using L = OutSmem<DT>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+    uint64_t* stage_full = bars;
+    uint64_t* stage_empty = bars + STAGES;
+    uint64_t* p_full = bars + 2 * STAGES;  // [2]
+    uint64_t* p_empty = p_full + 2;        // [2]
+    uint64_t* o_full = p_full + 4;
+    uint64_t* o_empty = p_full + 5;
+    uint64_t* drain_bar = p_full + 6;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(stage_full + s), 1);
+            mbar_init(smem_u32(stage_empty + s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(p_full + b), NUM_SOFT_WARPS);
+            mbar_init(smem_u32(p_empty + b), 1);
+        }
+        mbar_init(smem_u32(o_full), 1);
+        mbar_init(smem_u32(o_empty), NUM_SOFT_WARPS);
+        mbar_init(smem_u32(drain_bar), 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmS);
+        tma_prefetch_desc(&tmV);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer: score tile + V^T tile per key tile ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t last_phase[STAGES];
+        bool used[STAGES];
+        for (int s = 0; s < STAGES; ++s) { used[s] = false; last_phase[s] = 0; }
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
+            int bh, mt, evh;
+            decode(p, tile, bh, mt, evh);
+            for (int t = 0; t < p.n_kt; ++t) {
+                if (!mbar_wait_bounded(smem_u32(stage_empty + stage), phase ^ 1u, abort_flag,
+                                       p.err, kDevErrWaitEmpty)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t fb = smem_u32(stage_full + stage);
+                    uint8_t* sb = smem + L::OFF_STAGE + stage * L::STAGE_BYTES;
+                    mbar_arrive_expect_tx(fb, L::STAGE_BYTES);
+                    tma_load_3d(smem_u32(sb), &tmS, fb, t * BKEY, mt * BM, bh);
+                    if (DT == 1)  // fp32 scores: a second 32-key box of 128-byte rows
+                        tma_load_3d(smem_u32(sb + L::S_BYTES / 2), &tmS, fb, t * BKEY + 32, mt * BM, bh);
+                    tma_load_3d(smem_u32(sb + L::S_BYTES), &tmV, fb, t * 128, evh * EVT, bh);
+                }
+                __syncwarp();
+                used[stage] = true;
+                last_phase[stage] = phase;
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+        }
+        volatile int no_abort = 0;
+        for (int s = 0; s < STAGES; ++s)
+            if (used[s])
+                mbar_wait_bounded(smem_u32(stage_full + s), last_phase[s], &no_abort, p.err,
+                                  kDevErrWaitDrain);
+    } else if (warp == 1) {
+        // ---------------- MMA issuer: O += P V per key tile ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t n_p = 0;
+        bool ok = true;
+        int lt = 0;
+        const uint32_t o_hh = tmem_base + COL_O, o_mid = o_hh + 64, o_ll = o_hh + 128;
+        for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, ++lt) {
+            for (int t = 0; t < p.n_kt; ++t) {
+                const uint32_t buf = n_p & 1u;
+                if (!mbar_wait_bounded(smem_u32(p_full + buf), (n_p >> 1) & 1u, abort_flag, p.err,
+                                       kDevErrWaitFull) ||
+                    !mbar_wait_bounded(smem_u32(stage_full + stage), phase, abort_flag, p.err,
+                                       kDevErrWaitFull) ||
+                    (t == 0 && !mbar_wait_bounded(smem_u32(o_empty), (static_cast<uint32_t>(lt) & 1u) ^ 1u,
+                                                  abort_flag, p.err, kDevErrWaitAccEmpty))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint64_t a0 = smem_desc_kmajor_sw128(smem_u32(smem + L::OFF_P + buf * P_TILE));
+                    const uint64_t b0 = smem_desc_kmajor_sw128(
+                        smem_u32(smem + L::OFF_STAGE + stage * L::STAGE_BYTES + L::S_BYTES));
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const uint64_t hi = static_cast<uint64_t>((u * 32) >> 4);
+                        const uint64_t lo = static_cast<uint64_t>((64 + u * 32) >> 4);
+                        const uint32_t acc = (t > 0 || u > 0) ? 1u : 0u;
+                        tc_mma_i8(o_hh, a0 + hi, b0 + hi, IDESC_SS, acc);
+                        tc_mma_i8(o_mid, a0 + hi, b0 + lo, IDESC_SU, acc);
+                        tc_mma_i8(o_mid, a0 + lo, b0 + hi, IDESC_US, 1u);
+                        tc_mma_i8(o_ll, a0 + lo, b0 + lo, IDESC_UU, acc);
+                    }
+                    tc_commit(smem_u32(p_empty + buf));
+                    tc_commit(smem_u32(stage_empty + stage));
+                    if (t == p.n_kt - 1) tc_commit(smem_u32(o_full));
+                }
+                __syncwarp();
+                ++n_p;
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+        }
+        if (lane == 0) tc_commit(smem_u32(drain_bar));
+        __syncwarp();
+        volatile int no_abort = 0;
+        mbar_wait_bounded(smem_u32(drain_bar), 0, &no_abort, p.err, kDevErrWaitDrain);
+    } else {
+        // ---------------- probabilities and output epilogue (warps 2..9) ----------------
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row = quarter * 32 + lane;
+        const int sw = row & 7;
+        const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        const int BH = p.B * p.H;
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t n_p = 0;
+        int lt = 0;
+        for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++lt) {
+            int bh, mt, evh;
+            decode(p, tile, bh, mt, evh);
+            const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+            const int64_t i = static_cast<int64_t>(mt) * BM + row;
+            const bool row_ok = i < p.L;
+            // rows past L quantise to 0 (their scores are TMA zero fill)
+            const float inv_p = row_ok ? quant_inv(__uint_as_float(p.amax_p[bh])) : 0.0f;
+            float m_i = 0.0f, inv_i = 0.0f;
+            if (row_ok) {
+                m_i = p.row_max[static_cast<int64_t>(bh) * p.L + i];
+                inv_i = p.row_inv[static_cast<int64_t>(bh) * p.L + i];
+            }
+            bool ok = true;
+            for (int t = 0; t < p.n_kt; ++t) {
+                if (!mbar_wait_bounded(smem_u32(stage_full + stage), phase, abort_flag, p.err,
+                                       kDevErrWaitFull)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* sb = smem + L::OFF_STAGE + stage * L::STAGE_BYTES;
+                float s[32];
+                if constexpr (DT == 0) {
+                    // the row's 128-byte line, 16-byte chunks swizzled by row & 7
+                    const uint8_t* line = sb + row * 128;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint4 u = *reinterpret_cast<const uint4*>(line + (((4 * half + k) ^ sw) << 4));
+                        const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 f = __half22float2(h2[e]);
+                            s[8 * k + 2 * e] = f.x;
+                            s[8 * k + 2 * e + 1] = f.y;
+                        }
+                    }
+                } else {
+                    const uint8_t* line = sb + half * (L::S_BYTES / 2) + row * 128;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const float4 f = *reinterpret_cast<const float4*>(line + ((k ^ sw) << 4));
+                        s[4 * k] = f.x;
+                        s[4 * k + 1] = f.y;
+                        s[4 * k + 2] = f.z;
+                        s[4 * k + 3] = f.w;
+                    }
+                }
+                // P = T(exp(s - m) / l), quantised with the slice scale: the
+                // probabilities are >= 0, so q is in [0, 32767] and the hi
+                // limb in [0, 127].
+                uint32_t hw[8], lw[8];
+#pragma unroll
+                for (int w = 0; w < 8; ++w) {
+                    uint32_t hv = 0, lv = 0;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float pr = round_t(exp_fast(s[4 * w + k] - m_i) * inv_i, DT);
+                        const int q = quant_one(pr, inv_p);
+                        hv |= static_cast<uint32_t>(q >> 8) << (8 * k);
+                        lv |= static_cast<uint32_t>(q & 0xFF) << (8 * k);
+                    }
+                    hw[w] = hv;
+                    lw[w] = lv;
+                }
+                const uint32_t buf = n_p & 1u;
+                if (!mbar_wait_bounded(smem_u32(p_empty + buf), ((n_p >> 1) & 1u) ^ 1u, abort_flag,
+                                       p.err, kDevErrWaitEmpty)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* prow = smem + L::OFF_P + buf * P_TILE + row * 128;
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    const int ch = 2 * half + k;  // 16-key chunk of the hi part
+                    *reinterpret_cast<uint4*>(prow + ((ch ^ sw) << 4)) =
+                        make_uint4(hw[4 * k], hw[4 * k + 1], hw[4 * k + 2], hw[4 * k + 3]);
+                    *reinterpret_cast<uint4*>(prow + (((ch + 4) ^ sw) << 4)) =
+                        make_uint4(lw[4 * k], lw[4 * k + 1], lw[4 * k + 2], lw[4 * k + 3]);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(p_full + buf));
+                ++n_p;
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+            if (!ok) break;
+            if (!mbar_wait_bounded(smem_u32(o_full), static_cast<uint32_t>(lt) & 1u, abort_flag, p.err,
+                                   kDevErrWaitAccFull))
+                break;
+            tc_fence_after();
+            uint32_t hh[32], mid[32], ll[32];
+            const uint32_t col = COL_O + 32 * half;
+            tmem_ld_32x32b_x32(t_lane + col, hh);
+            tmem_ld_32x32b_x32(t_lane + col + 64, mid);
+            tmem_ld_32x32b_x32(t_lane + col + 128, ll);
+            tc_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(o_empty));
+            if (row_ok) {
+                const double spv = dequant_scale(__uint_as_float(p.amax_p[bh]), __ldg(p.amax + 2 * BH + bh));
+                const int64_t e0 = static_cast<int64_t>(evh) * EVT + 32 * half;
+                const int64_t obase = b * p.os[0] + h * p.os[1] + i * p.os[2];
+                float o[32];
+#pragma unroll
+                for (int c = 0; c < 32; ++c)
+                    o[c] = round_t_from_double(__dmul_rn(limb_acc_to_double(hh[c], mid[c], ll[c]), spv), DT);
+                if (p.out_vec && e0 + 32 <= p.Ev) {
+                    store_row32<DT>(static_cast<char*>(p.out) + (obase + e0) * (DT == 0 ? 2 : 4), o);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c)
+                        if (e0 + c < p.Ev) store_t(p.out, DT, obase + (e0 + c) * p.os[3], o[c]);
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ---- quantisation of q, k, v into limb rows ---------------------------------
+
+struct QuantParams {
+    const void* src[3];
+    int64_t st[3][4];
+    int rows[3], cols[3];
+    int H, BH;
+    int vec[3];         // columns contiguous, 16-byte aligned rows: vector loads
+    float* amax;        // [3][BH]
+    unsigned* amax_p;   // [BH], zeroed here
+    uint8_t* dst[3];
+    int64_t ld[3];      // bytes per limb row
+    int64_t slice[3];   // bytes per slice
+};
+
+constexpr int QT_THREADS = 256;
+constexpr int QT_MAX_EV = 256;
+
+template <typename T> __device__ __forceinline__ float ldx(const T* p, int64_t i);
+template <> __device__ __forceinline__ float ldx<__half>(const __half* p, int64_t i) { return __half2float(__ldg(p + i)); }
+template <> __device__ __forceinline__ float ldx<float>(const float* p, int64_t i) { return __ldg(p + i); }
+
+// 8 consecutive elements from a 16-byte aligned address.
+__device__ __forceinline__ void ld8(const __half* p, float* v) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(h2[e]);
+        v[2 * e] = f.x;
+        v[2 * e + 1] = f.y;
+    }
+}
+__device__ __forceinline__ void ld8(const float* p, float* v) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ void pack16(const int (&q)[16], uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        h[w] = 0;
+        l[w] = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            h[w] |= static_cast<uint32_t>((q[4 * w + k] >> 8) & 0xFF) << (8 * k);
+            l[w] |= static_cast<uint32_t>(q[4 * w + k] & 0xFF) << (8 * k);
+        }
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(QT_THREADS)
+attn_quant_kernel(QuantParams p) {
+    __shared__ unsigned red[QT_THREADS / 32];
+    __shared__ int16_t tile[BKEY][QT_MAX_EV + 2];
+    const int bh = blockIdx.x, z = blockIdx.y;
+    const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+    const T* x = static_cast<const T*>(p.src[z]) + b * p.st[z][0] + h * p.st[z][1];
+    const int64_t sr = p.st[z][2], sc = p.st[z][3];
+    const int rows = p.rows[z], cols = p.cols[z];
+    const bool vec = p.vec[z] != 0;
+
+    unsigned mx = 0;  // max of |x| bit patterns: NaN dominates, then Inf
+    if (vec) {
+        const int pcs = cols / 8;
+        for (int it = threadIdx.x; it < rows * pcs; it += QT_THREADS) {
+            const int r = it / pcs, pc = it - (it / pcs) * pcs;
+            float v[8];
+            ld8(x + r * sr + pc * 8, v);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) mx = max(mx, __float_as_uint(fabsf(v[e])));
+        }
+    } else {
+        for (int it = threadIdx.x; it < rows * cols; it += QT_THREADS) {
+            const int r = it / cols, c = it - (it / cols) * cols;
+            mx = max(mx, __float_as_uint(fabsf(ldx<T>(x, r * sr + c * sc))));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = 0;
+#pragma unroll
+    for (int w = 0; w < QT_THREADS / 32; ++w) mx = max(mx, red[w]);
+    const float amax = __uint_as_float(mx);
+    if (threadIdx.x == 0) {
+        p.amax[z * p.BH + bh] = amax;
+        if (z == 0) p.amax_p[bh] = 0u;
+    }
+    const float inv = quant_inv(amax);
+    uint8_t* out = p.dst[z] + bh * p.slice[z];
+    const int64_t ld = p.ld[z];
+
+    if (z < 2) {
+        // rows x (ld / 2) values in 16-value pieces: hi at g*128 + c%64, lo at +64
+        const int pieces = static_cast<int>(ld / 32);
+        for (int it = threadIdx.x; it < rows * pieces; it += QT_THREADS) {
+            const int r = it / pieces, pc = it - (it / pieces) * pieces;
+            const int c0 = pc * 16;
+            int q[16];
+            if (vec && c0 + 16 <= cols) {
+                float v[16];
+                ld8(x + r * sr + c0, v);
+                ld8(x + r * sr + c0 + 8, v + 8);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) q[e] = quant_one(v[e], inv);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    q[e] = (c0 + e < cols) ? quant_one(ldx<T>(x, r * sr + (c0 + e) * sc), inv) : 0;
+            }
+            uint4 hi, lo;
+            pack16(q, hi, lo);
+            uint8_t* dst = out + r * ld + (c0 / 64) * 128 + (c0 % 64);
+            *reinterpret_cast<uint4*>(dst) = hi;
+            *reinterpret_cast<uint4*>(dst + 64) = lo;
+        }
+    } else {
+        // v^T: row e holds, per key tile kt, [hi of keys 64kt.. | lo of the same]
+        const int n_kt = static_cast<int>(ld / 128);
+        for (int kt = 0; kt < n_kt; ++kt) {
+            if (vec) {
+                const int pcs = cols / 8;
+                for (int it = threadIdx.x; it < BKEY * pcs; it += QT_THREADS) {
+                    const int kk = it / pcs, pc = it - (it / pcs) * pcs;
+                    const int j = kt * BKEY + kk;
+                    float v[8];
+                    if (j < rows) {
+                        ld8(x + j * sr + pc * 8, v);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) v[e] = 0.0f;
+                    }
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) tile[kk][pc * 8 + e] = static_cast<int16_t>(quant_one(v[e], inv));
+                }
+            } else {
+                for (int it = threadIdx.x; it < BKEY * cols; it += QT_THREADS) {
+                    const int kk = it / cols, e = it - (it / cols) * cols;
+                    const int j = kt * BKEY + kk;
+                    tile[kk][e] = static_cast<int16_t>(j < rows ? quant_one(ldx<T>(x, j * sr + e * sc), inv) : 0);
+                }
+            }
+            __syncthreads();
+            for (int it = threadIdx.x; it < cols * 4; it += QT_THREADS) {
+                const int e = it >> 2, pc = it & 3;
+                int q[16];
+#pragma unroll
+                for (int k = 0; k < 16; ++k) q[k] = tile[pc * 16 + k][e];
+                uint4 hi, lo;
+                pack16(q, hi, lo);
+                uint8_t* dst = out + e * ld + kt * 128 + pc * 16;
+                *reinterpret_cast<uint4*>(dst) = hi;
+                *reinterpret_cast<uint4*>(dst + 64) = lo;
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// ---- host side ---------------------------------------------------------------
+
+struct Layout {
+    int G;
+    int64_t BH, Spad, ldq, ldv;
+    size_t off_amax, off_amax_p, off_max, off_inv, off_q, off_k, off_v, off_s, total;
+};
+
+Layout layout_of(const tk_sdpa_desc_t& d) {
+    Layout l;
+    l.G = static_cast<int>(ceil_div(d.e, 64));
+    l.BH = d.batch * d.heads;
+    l.Spad = static_cast<int64_t>(round_up(static_cast<size_t>(d.s), BKEY));
+    l.ldq = 128 * l.G;
+    l.ldv = 2 * l.Spad;
+    const size_t es = dtype_size(d.dtype);
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = o;
+        o = round_up(o + bytes, 1024);
+        return at;
+    };
+    l.off_amax = take(3 * l.BH * sizeof(float));
+    l.off_amax_p = take(l.BH * sizeof(unsigned));
+    l.off_max = take(l.BH * d.l * sizeof(float));
+    l.off_inv = take(l.BH * d.l * sizeof(float));
+    l.off_q = take(static_cast<size_t>(l.BH * d.l * l.ldq));
+    l.off_k = take(static_cast<size_t>(l.BH * d.s * l.ldq));
+    l.off_v = take(static_cast<size_t>(l.BH * d.ev * l.ldv));
+    l.off_s = take(static_cast<size_t>(l.BH * d.l * l.Spad) * es);
+    l.total = o + 1024;  // base alignment slack
+    return l;
+}
+
+int validate(const tk_sdpa_desc_t* d) {
+    TK_CHECK_ARG(d != nullptr, "tk_sdpa_q16: NULL descriptor");
+    TK_CHECK_ARG(d->dtype == TK_DTYPE_F16 || d->dtype == TK_DTYPE_F32, "tk_sdpa_q16: bad dtype");
+    TK_CHECK_ARG(d->batch >= 0 && d->heads >= 0 && d->l >= 0 && d->s >= 0 && d->e >= 0 && d->ev >= 0,
+                 "tk_sdpa_q16: negative size");
+    if (d->e > 128) TK_FAIL(TK_ERR_UNSUPPORTED, "tk_sdpa_q16: head dim %lld > 128", (long long)d->e);
+    if (d->ev > QT_MAX_EV)
+        TK_FAIL(TK_ERR_UNSUPPORTED, "tk_sdpa_q16: value dim %lld > %d", (long long)d->ev, QT_MAX_EV);
+    if (d->s > 32768)
+        TK_FAIL(TK_ERR_UNSUPPORTED, "tk_sdpa_q16: %lld keys exceed the exact int32 limb sums (32768)",
+                (long long)d->s);
+    TK_CHECK_ARG(d->batch * d->heads < (1LL << 31) && d->l < (1LL << 31), "tk_sdpa_q16: too large");
+    return TK_OK;
+}
+
+int make_map(CUtensorMap* map, CUtensorMapDataType type, size_t esize, const void* base, int64_t d0,
+             int64_t d1, int64_t d2, uint32_t box0, uint32_t box1) {
+    EncodeTiledFn enc = tensor_map_encoder();
+    if (enc == nullptr) TK_FAIL(TK_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1),
+                          static_cast<cuuint64_t>(d2)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(d0 * esize), static_cast<cuuint64_t>(d0 * d1 * esize)};
+    cuuint32_t box[3] = {box0, box1, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, type, 3, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) TK_FAIL(TK_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return TK_OK;
+}
+
+// One attribute call per kernel instantiation and device (the template is
+// keyed by the kernel itself, not its signature, which several share).
+template <auto Kernel>
+int set_smem(int bytes, int dev) {
+    static std::once_flag once[64];
+    static cudaError_t err[64];
+    const int slot = std::min(dev, 63);
+    std::call_once(once[slot], [&] {
+        err[slot] = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    });
+    if (err[slot] != cudaSuccess)
+        TK_FAIL(TK_ERR_CUDA, "attention smem attribute: %s", cudaGetErrorString(err[slot]));
+    return TK_OK;
+}
+
+template <int G, int DT>
+int run_attention(const CUtensorMap& tq, const CUtensorMap& tk_, const CUtensorMap& ts,
+                  const CUtensorMap& tv, AttnParams p, int ev_tiles, int dev, cudaStream_t stream) {
+    const int sms = sm_count(dev);
+    p.ev_tiles = 1;
+    p.tiles = p.B * p.H * p.m_tiles;
+    int rc = set_smem<attn_stats_kernel<G, DT>>(StatsSmem<G>::ALLOC, dev);
+    if (rc) return rc;
+    attn_stats_kernel<G, DT><<<std::min(p.tiles, sms), NUM_THREADS, StatsSmem<G>::ALLOC, stream>>>(tq, tk_, p);
+    rc = launch_status("attention statistics");
+    if (rc) return rc;
+    p.ev_tiles = ev_tiles;
+    p.tiles = p.B * p.H * p.m_tiles * ev_tiles;
+    rc = set_smem<attn_out_kernel<DT>>(OutSmem<DT>::ALLOC, dev);
+    if (rc) return rc;
+    attn_out_kernel<DT><<<std::min(p.tiles, sms), NUM_THREADS, OutSmem<DT>::ALLOC, stream>>>(ts, tv, p);
+    return launch_status("attention output");
+}
+
+// Innermost stride 1 and every other stride and the base 16-byte aligned, so
+// runs of `cols` (a multiple of 8) elements load and store as vectors.
+bool vec_ok(const void* ptr, const int64_t* st, int64_t cols, size_t es) {
+    const int64_t v = static_cast<int64_t>(16 / es);
+    return st[3] == 1 && cols % 8 == 0 && reinterpret_cast<uintptr_t>(ptr) % 16 == 0 &&
+           st[0] % v == 0 && st[1] % v == 0 && st[2] % v == 0;
+}
+
+}  // namespace
+}  // namespace tk
+
+extern "C" {
+
+size_t tk_sdpa_workspace_size(const tk_sdpa_desc_t* desc) {
+    if (tk::validate(desc) != TK_OK) return 0;
+    return tk::layout_of(*desc).total;
+}
+
+int tk_sdpa_q16(const tk_sdpa_desc_t* desc, void* workspace, size_t workspace_bytes, void* stream_) {
+    using namespace tk;
+    int rc = validate(desc);
+    if (rc) return rc;
+    const tk_sdpa_desc_t& d = *desc;
+    if (d.batch == 0 || d.heads == 0 || d.l == 0 || d.ev == 0) return TK_OK;
+    TK_CHECK_ARG(d.s > 0 && d.e > 0, "tk_sdpa_q16: empty key or head dimension");
+    TK_CHECK_ARG(d.q && d.k && d.v && d.out, "tk_sdpa_q16: NULL tensor");
+    const Layout l = layout_of(d);
+    if (workspace == nullptr || workspace_bytes < l.total)
+        TK_FAIL(TK_ERR_WORKSPACE, "tk_sdpa_q16: workspace of %zu bytes, %zu needed", workspace_bytes,
+                l.total);
+    uint8_t* ws = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(workspace) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    const int dev = current_device();
+    const size_t es = dtype_size(d.dtype);
+
+    QuantParams qp;
+    const void* srcs[3] = {d.q, d.k, d.v};
+    const int64_t* strs[3] = {d.q_strides, d.k_strides, d.v_strides};
+    const int64_t rows[3] = {d.l, d.s, d.s}, cols[3] = {d.e, d.e, d.ev};
+    uint8_t* dsts[3] = {ws + l.off_q, ws + l.off_k, ws + l.off_v};
+    const int64_t lds[3] = {l.ldq, l.ldq, l.ldv};
+    const int64_t slices[3] = {d.l * l.ldq, d.s * l.ldq, d.ev * l.ldv};
+    for (int z = 0; z < 3; ++z) {
+        qp.src[z] = srcs[z];
+        for (int a = 0; a < 4; ++a) qp.st[z][a] = strs[z][a];
+        qp.rows[z] = static_cast<int>(rows[z]);
+        qp.cols[z] = static_cast<int>(cols[z]);
+        qp.vec[z] = vec_ok(srcs[z], strs[z], cols[z], es) ? 1 : 0;
+        qp.dst[z] = dsts[z];
+        qp.ld[z] = lds[z];
+        qp.slice[z] = slices[z];
+    }
+    qp.H = static_cast<int>(d.heads);
+    qp.BH = static_cast<int>(l.BH);
+    qp.amax = reinterpret_cast<float*>(ws + l.off_amax);
+    qp.amax_p = reinterpret_cast<unsigned*>(ws + l.off_amax_p);
+    const dim3 qgrid(static_cast<unsigned>(l.BH), 3);
+    if (d.dtype == TK_DTYPE_F16)
+        attn_quant_kernel<__half><<<qgrid, QT_THREADS, 0, stream>>>(qp);
+    else
+        attn_quant_kernel<float><<<qgrid, QT_THREADS, 0, stream>>>(qp);
+    rc = launch_status("attention quantise");
+    if (rc) return rc;
+
+    const CUtensorMapDataType stype =
+        d.dtype == TK_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    CUtensorMap tq, tk_, tv, ts;
+    rc = make_map(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + l.off_q, l.ldq, d.l, l.BH, 128, BM);
+    if (!rc) rc = make_map(&tk_, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + l.off_k, l.ldq, d.s, l.BH, 128, BKEY);
+    if (!rc) rc = make_map(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + l.off_v, l.ldv, d.ev, l.BH, 128, EVT);
+    if (!rc)
+        rc = make_map(&ts, stype, es, ws + l.off_s, l.Spad, d.l, l.BH, static_cast<uint32_t>(128 / es), BM);
+    if (rc) return rc;
+
+    AttnParams p;
+    p.B = static_cast<int>(d.batch);
+    p.H = static_cast<int>(d.heads);
+    p.L = static_cast<int>(d.l);
+    p.S = static_cast<int>(d.s);
+    p.Ev = static_cast<int>(d.ev);
+    p.Spad = l.Spad;
+    p.n_kt = static_cast<int>(ceil_div(d.s, BKEY));
+    p.m_tiles = static_cast<int>(ceil_div(d.l, BM));
+    p.amax = qp.amax;
+    p.amax_p = qp.amax_p;
+    p.row_max = reinterpret_cast<float*>(ws + l.off_max);
+    p.row_inv = reinterpret_cast<float*>(ws + l.off_inv);
+    p.scores = ws + l.off_s;
+    p.out = d.out;
+    for (int a = 0; a < 4; ++a) {
+        p.os[a] = d.out_strides[a];
+        p.ms[a] = d.mask_strides[a];
+    }
+    p.out_vec = vec_ok(d.out, d.out_strides, 32, es) ? 1 : 0;
+    p.mask = d.mask;
+    p.mask_vec = d.mask != nullptr && vec_ok(d.mask, d.mask_strides, 32, es) ? 1 : 0;
+    p.causal = d.causal ? 1 : 0;
+    p.scale = d.scale;
+    p.err = device_error_word(dev);
+    const int ev_tiles = static_cast<int>(ceil_div(d.ev, EVT));
+    TK_CHECK_ARG(l.BH * p.m_tiles * ev_tiles < (1LL << 31), "tk_sdpa_q16: too many tiles");
+    if (l.G == 1)
+        return d.dtype == TK_DTYPE_F16 ? run_attention<1, 0>(tq, tk_, ts, tv, p, ev_tiles, dev, stream)
+                                       : run_attention<1, 1>(tq, tk_, ts, tv, p, ev_tiles, dev, stream);
+    return d.dtype == TK_DTYPE_F16 ? run_attention<2, 0>(tq, tk_, ts, tv, p, ev_tiles, dev, stream)
+                                   : run_attention<2, 1>(tq, tk_, ts, tv, p, ev_tiles, dev, stream);
+}
+
+}  // extern "C"

@@ -106,6 +106,7 @@ at::Tensor linear_scaled(const at::Tensor& input, const at::Tensor& weight,
                          const std::optional<at::Tensor>& amax_w,
                          const std::optional<at::Tensor>& out);
 at::Tensor sdpa(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
-                const std::optional<at::Tensor>& mask, bool is_causal, std::optional<double> scale);
+                const std::optional<at::Tensor>& mask, bool is_causal, std::optional<double> scale,
+                bool fused);
 
 }  // namespace torch_kunlun

@@ -95,6 +95,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("amax_w") = py::none(), py::arg("out") = py::none());
     m.def("sdpa", &sdpa, py::arg("query"), py::arg("key"), py::arg("value"),
           py::arg("attn_mask") = py::none(), py::arg("is_causal") = false,
-          py::arg("scale") = py::none());
+          py::arg("scale") = py::none(), py::arg("fused") = true);
     m.def("abi_version", [] { return tk_abi_version(); });
 }

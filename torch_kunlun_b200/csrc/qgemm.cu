@@ -85,6 +85,8 @@ struct TileCfg {
 // operand delivery, not the epilogue, limits these tiles.
 using CfgWide = TileCfg<128, 3, 1>;   // 128x128 tiles, accumulators single-buffered
 using CfgWider = TileCfg<160, 3, 1>;  // 128x160 tiles (480 TMEM columns), single-buffered
+using CfgOverlap64 = TileCfg<64, 4, 2>;  // 128x64 tiles, epilogue overlapped with the next tile
+using CfgOverlap80 = TileCfg<80, 4, 2>;  // 128x80 tiles, epilogue overlapped with the next tile
 
 struct EpiParams {
     int dtype;  // 0 fp16, 1 fp32
@@ -128,13 +130,6 @@ __device__ __forceinline__ float act_t(float r, int dtype) {
     }
 }
 
-// Integer recombination of the three limb accumulators, exact in int64:
-// acc = 65536*HH + 256*MID + LL (|acc| <= 2^46 for K <= 32768).
-__device__ __forceinline__ long long recombine(uint32_t hh, uint32_t mid, uint32_t ll) {
-    return (static_cast<long long>(static_cast<int32_t>(hh)) << 16) +
-           (static_cast<long long>(static_cast<int32_t>(mid)) << 8) +
-           static_cast<long long>(static_cast<int32_t>(ll));
-}
 
 
 // The reference's post-GEMM sequence on one element (see file header).
@@ -359,8 +354,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 float v[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
-                    v[j] = round_t_from_double(
-                        __dmul_rn(static_cast<double>(recombine(hh[j], mid[j], ll[j])), s), DT);
+                    v[j] = round_t_from_double(__dmul_rn(limb_acc_to_double(hh[j], mid[j], ll[j]), s), DT);
                 if (has_alpha) {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] = round_t(__fmul_rn(v[j], ep.alpha), DT);
@@ -487,11 +481,6 @@ __global__ void qgemm_simt_kernel(const int8_t* __restrict__ la, const int8_t* _
 }
 
 // ---- host side --------------------------------------------------------------------
-
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 EncodeTiledFn get_encode_fn() {
     static EncodeTiledFn fn = nullptr;
@@ -641,7 +630,7 @@ int dispatch_act(int act, int dev, int grid, const CUtensorMap& tmA, const CUten
 
 // Tile configuration for a problem: 128x160 tiles for K >= 2048, else
 // 128x128.  TK_QGEMM_TILE=wide|wider forces one (a tuning override).
-enum class TileChoice { Wide, Wider };
+enum class TileChoice { Wide, Wider, Overlap64, Overlap80 };
 
 TileChoice choose_tiles(const tk_qgemm_desc_t& d) {
     static const int forced = [] {
@@ -649,10 +638,14 @@ TileChoice choose_tiles(const tk_qgemm_desc_t& d) {
         if (v == nullptr) return 0;
         if (std::string(v) == "wide") return 1;
         if (std::string(v) == "wider") return 2;
+        if (std::string(v) == "overlap64") return 3;
+        if (std::string(v) == "overlap80") return 4;
         return 0;
     }();
     if (forced == 1) return TileChoice::Wide;
     if (forced == 2) return TileChoice::Wider;
+    if (forced == 3) return TileChoice::Overlap64;
+    if (forced == 4) return TileChoice::Overlap80;
     return d.k >= 2048 ? TileChoice::Wider : TileChoice::Wide;
 }
 
@@ -685,9 +678,12 @@ int launch_cfg(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb, int
 
 int launch_tc(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb, int64_t ld,
               const EpiParams& ep, cudaStream_t stream, int b_mod = 0) {
-    if (choose_tiles(d) == TileChoice::Wider)
-        return launch_cfg<CfgWider>(d, la, lb, ld, ep, stream, b_mod);
-    return launch_cfg<CfgWide>(d, la, lb, ld, ep, stream, b_mod);
+    switch (choose_tiles(d)) {
+        case TileChoice::Wider: return launch_cfg<CfgWider>(d, la, lb, ld, ep, stream, b_mod);
+        case TileChoice::Overlap64: return launch_cfg<CfgOverlap64>(d, la, lb, ld, ep, stream, b_mod);
+        case TileChoice::Overlap80: return launch_cfg<CfgOverlap80>(d, la, lb, ld, ep, stream, b_mod);
+        default: return launch_cfg<CfgWide>(d, la, lb, ld, ep, stream, b_mod);
+    }
 }
 
 int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t stream, Path path,
@@ -741,6 +737,8 @@ int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t str
 }
 
 }  // namespace
+
+EncodeTiledFn tensor_map_encoder() { return get_encode_fn(); }
 
 // Internal entry used by the conv path: GEMM on prepared limbs where the B
 // operand (weights) has b_mod slices shared across the batch, the output is

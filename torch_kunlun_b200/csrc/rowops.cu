@@ -20,6 +20,51 @@ template <typename T> __device__ __forceinline__ void stf(T* p, int64_t i, float
 template <> __device__ __forceinline__ void stf<__half>(__half* p, int64_t i, float v) { p[i] = __float2half_rn(v); }
 template <> __device__ __forceinline__ void stf<float>(float* p, int64_t i, float v) { p[i] = v; }
 
+// N consecutive elements (N * sizeof(T) a multiple of 16 bytes, p 16-byte
+// aligned) loaded / stored with 128-bit accesses.
+template <int N>
+__device__ __forceinline__ void ldv(const __half* p, float (&o)[N]) {
+#pragma unroll
+    for (int c = 0; c < N / 8; ++c) {
+        const uint4 u = *reinterpret_cast<const uint4*>(p + 8 * c);
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const float2 f = __half22float2(h[t]);
+            o[8 * c + 2 * t] = f.x;
+            o[8 * c + 2 * t + 1] = f.y;
+        }
+    }
+}
+template <int N>
+__device__ __forceinline__ void ldv(const float* p, float (&o)[N]) {
+#pragma unroll
+    for (int c = 0; c < N / 4; ++c) {
+        const float4 f = *reinterpret_cast<const float4*>(p + 4 * c);
+        o[4 * c] = f.x;
+        o[4 * c + 1] = f.y;
+        o[4 * c + 2] = f.z;
+        o[4 * c + 3] = f.w;
+    }
+}
+template <int N>
+__device__ __forceinline__ void stv(__half* p, const float (&v)[N]) {
+#pragma unroll
+    for (int c = 0; c < N / 8; ++c) {
+        uint4 u;
+        __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) h[t] = __floats2half2_rn(v[8 * c + 2 * t], v[8 * c + 2 * t + 1]);
+        *reinterpret_cast<uint4*>(p + 8 * c) = u;
+    }
+}
+template <int N>
+__device__ __forceinline__ void stv(float* p, const float (&v)[N]) {
+#pragma unroll
+    for (int c = 0; c < N / 4; ++c)
+        *reinterpret_cast<float4*>(p + 4 * c) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -32,7 +77,7 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // One warp per row; each lane holds PER columns: lane l owns columns
-// l*VEC + j*32*VEC + t (t < VEC) so that loads are 128-bit and coalesced.
+// l*VEC + j*32*VEC + t (t < VEC), loaded and stored as 128-bit vectors.
 template <typename TI, typename TO, int PER>
 __global__ void softmax_warp_kernel(const TI* __restrict__ x, TO* __restrict__ y, int64_t rows,
                                     int cols) {
@@ -46,11 +91,17 @@ __global__ void softmax_warp_kernel(const TI* __restrict__ x, TO* __restrict__ y
 #pragma unroll
     for (int j = 0; j < PER / VEC; ++j) {
         const int c0 = (j * 32 + lane) * VEC;
+        float t[VEC];
+        if (c0 < cols) {  // cols is a multiple of VEC on this path
+            ldv<VEC>(xr + c0, t);
+        } else {
 #pragma unroll
-        for (int t = 0; t < VEC; ++t) {
-            const int c = c0 + t;
-            v[j * VEC + t] = c < cols ? ldf<TI>(xr, c) : -INFINITY;
-            m = fmaxf(m, v[j * VEC + t]);
+            for (int i = 0; i < VEC; ++i) t[i] = -INFINITY;
+        }
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+            v[j * VEC + i] = t[i];
+            m = fmaxf(m, t[i]);
         }
     }
     m = warp_max(m);
@@ -66,9 +117,12 @@ __global__ void softmax_warp_kernel(const TI* __restrict__ x, TO* __restrict__ y
 #pragma unroll
     for (int j = 0; j < PER / VEC; ++j) {
         const int c0 = (j * 32 + lane) * VEC;
+        if (c0 < cols) {
+            float o[VEC];
 #pragma unroll
-        for (int t = 0; t < VEC; ++t)
-            if (c0 + t < cols) stf<TO>(yr, c0 + t, v[j * VEC + t] * inv);
+            for (int i = 0; i < VEC; ++i) o[i] = v[j * VEC + i] * inv;
+            stv<VEC>(yr + c0, o);
+        }
     }
 }
 
@@ -122,11 +176,17 @@ __global__ void layer_norm_warp_kernel(const T* __restrict__ x, const TW* __rest
 #pragma unroll
     for (int j = 0; j < PER / VEC; ++j) {
         const int c0 = (j * 32 + lane) * VEC;
+        float t[VEC];
+        if (c0 < cols) {  // cols is a multiple of VEC on this path
+            ldv<VEC>(xr + c0, t);
+        } else {
 #pragma unroll
-        for (int t = 0; t < VEC; ++t) {
-            const int c = c0 + t;
-            v[j * VEC + t] = c < cols ? ldf<T>(xr, c) : 0.f;
-            s += v[j * VEC + t];
+            for (int i = 0; i < VEC; ++i) t[i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+            v[j * VEC + i] = t[i];
+            s += t[i];
         }
     }
     const float mean = warp_sum(s) / cols;
@@ -136,7 +196,7 @@ __global__ void layer_norm_warp_kernel(const T* __restrict__ x, const TW* __rest
         const int c0 = (j * 32 + lane) * VEC;
 #pragma unroll
         for (int t = 0; t < VEC; ++t) {
-            const float d = (c0 + t < cols) ? v[j * VEC + t] - mean : 0.f;
+            const float d = (c0 < cols) ? v[j * VEC + t] - mean : 0.f;
             q += d * d;
         }
     }
@@ -146,15 +206,21 @@ __global__ void layer_norm_warp_kernel(const T* __restrict__ x, const TW* __rest
 #pragma unroll
     for (int j = 0; j < PER / VEC; ++j) {
         const int c0 = (j * 32 + lane) * VEC;
+        if (c0 < cols) {
+            float o[VEC], g[VEC], b[VEC];
 #pragma unroll
-        for (int t = 0; t < VEC; ++t) {
-            const int c = c0 + t;
-            if (c < cols) {
-                float o = (v[j * VEC + t] - mean) * rstd;
-                if (gamma) o = o * ldf<TW>(gamma, c);
-                if (beta) o = o + ldf<TW>(beta, c);
-                stf<T>(yr, c, o);
+            for (int t = 0; t < VEC; ++t) o[t] = (v[j * VEC + t] - mean) * rstd;
+            if (gamma) {
+                ldv<VEC>(gamma + c0, g);
+#pragma unroll
+                for (int t = 0; t < VEC; ++t) o[t] = o[t] * g[t];
             }
+            if (beta) {
+                ldv<VEC>(beta + c0, b);
+#pragma unroll
+                for (int t = 0; t < VEC; ++t) o[t] = o[t] + b[t];
+            }
+            stv<VEC>(yr + c0, o);
         }
     }
     if (lane == 0) {
@@ -209,7 +275,8 @@ int softmax_launch(const void* x, void* y, int64_t rows, int64_t cols, cudaStrea
     const TI* xp = static_cast<const TI*>(x);
     TO* yp = static_cast<TO*>(y);
     constexpr int VEC = 16 / sizeof(TI);
-    if (cols <= kRegCols && (cols % VEC) == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0) {
+    if (cols <= kRegCols && (cols % VEC) == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+        reinterpret_cast<uintptr_t>(y) % 16 == 0 && (cols * sizeof(TO)) % 16 == 0) {
         const int warps = 8;
         const unsigned grid = static_cast<unsigned>(ceil_div(rows, warps));
         const int per = static_cast<int>(round_up(static_cast<size_t>(ceil_div(cols, 32)), VEC));
@@ -234,7 +301,9 @@ int layer_norm_launch(const void* x, const void* g, const void* b, void* y, floa
     const TW* gp = static_cast<const TW*>(g);
     const TW* bp = static_cast<const TW*>(b);
     constexpr int VEC = 16 / sizeof(T);
-    if (cols <= kRegCols && (cols % VEC) == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0) {
+    if (cols <= kRegCols && (cols % VEC) == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+        reinterpret_cast<uintptr_t>(y) % 16 == 0 && reinterpret_cast<uintptr_t>(g) % 16 == 0 &&
+        reinterpret_cast<uintptr_t>(b) % 16 == 0) {
         const int warps = 8;
         const unsigned grid = static_cast<unsigned>(ceil_div(rows, warps));
         const int per = static_cast<int>(round_up(static_cast<size_t>(ceil_div(cols, 32)), VEC));

@@ -1,6 +1,7 @@
 // tk_internal.h -- shared host-side helpers of libtk_kernels.so.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 
@@ -66,5 +67,13 @@ struct QuantOperand {
     int8_t* limbs;
 };
 int quantise_operands(tk_dtype_t dt, const QuantOperand* ops, int nops, cudaStream_t stream);
+
+// cuTensorMapEncodeTiled, resolved once through the runtime's driver entry
+// point query (NULL when unavailable).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn tensor_map_encoder();
 
 }  // namespace tk

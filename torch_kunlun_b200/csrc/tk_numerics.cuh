@@ -22,8 +22,8 @@ __device__ __forceinline__ float quant_inv(float amax) {
 
 __device__ __forceinline__ int quant_one(float v, float inv) {
     const float t = __fmul_rn(v, inv);
-    if (t != t) return 0;
-    return max(-32767, min(32767, __float2int_rn(t)));
+    const int q = max(-32767, min(32767, __float2int_rn(t)));
+    return t == t ? q : 0;  // a select, so loops over elements stay branch-free
 }
 
 __device__ __forceinline__ double dequant_scale(float amax_a, float amax_b) {
@@ -31,21 +31,20 @@ __device__ __forceinline__ double dequant_scale(float amax_a, float amax_b) {
                      1073676289.0);
 }
 
-// binary64 -> binary16, nearest-even, through the round-to-odd binary32
-// intermediate of Boldo & Melquiond ("When double rounding is odd", 2005):
-// rounding toward zero to binary32 and setting the last bit when inexact,
-// then rounding to nearest binary16, equals one correct rounding because
-// binary32 carries at least two more significand bits than binary16.
-__device__ __forceinline__ float d2f_round_odd(double d) {
-    float f = __double2float_rz(d);
-    if (static_cast<double>(f) != d) f = __uint_as_float(__float_as_uint(f) | 1u);
-    return f;
+// The exact integer 65536*hh + 256*mid + ll of three int32 limb accumulators
+// as binary64, without a conversion instruction: for |acc| < 2^51 the bit
+// pattern of 1.5 * 2^52 plus acc is the binary64 value 1.5 * 2^52 + acc.
+__device__ __forceinline__ double limb_acc_to_double(uint32_t hh, uint32_t mid, uint32_t ll) {
+    const long long acc = (static_cast<long long>(static_cast<int32_t>(hh)) << 16) +
+                          (static_cast<long long>(static_cast<int32_t>(mid)) << 8) +
+                          static_cast<long long>(static_cast<int32_t>(ll));
+    return __longlong_as_double(acc + 0x4338000000000000LL) - 6755399441055744.0;
 }
 
 // Round a binary64 value to the output type (0 = fp16, 1 = fp32), returned
 // widened to fp32 (exactly).
 __device__ __forceinline__ float round_t_from_double(double d, int dtype) {
-    if (dtype == 0) return __half2float(__float2half_rn(d2f_round_odd(d)));
+    if (dtype == 0) return __half2float(__double2half(d));  // one nearest-even rounding
     return __double2float_rn(d);
 }
 
