@@ -117,6 +117,115 @@ def bert_measure(dev, kunlun, steps, warmup, flush):
             "workload": BERT_WORKLOAD}
 
 
+BMM_B, BMM_M, BMM_E = 64, 512, 128
+BMM_OPS = 2 * (2 * BMM_B * BMM_M * BMM_M * BMM_E)
+CONV_CASES = [  # (name, C, F, H, k, pad, groups, bias)
+    ("1x1 256->64 @56", 256, 64, 56, 1, 0, 1, False),
+    ("3x3 64->64 @56 pad1", 64, 64, 56, 3, 1, 1, False),
+    ("3x3 256->256 @14 pad1 +bias", 256, 256, 14, 3, 1, 1, True),
+    ("3x3 depthwise g=512 @7 pad1", 512, 512, 7, 3, 1, 512, False),
+]
+CONV_N = 64
+
+
+def bmm_measure(dev, kunlun, flush, steps=20, warmup=3):
+    """Attention-score batched matmuls: S = A @ B, P = softmax(S), O = P @ V
+    for A [64,512,128], B [64,128,512], V [64,512,128] ~N(0,1), fp16 and fp32;
+    composed from the quantised bmm and softmax ops, and the same three steps
+    through the fused attention kernels (scale 1, no mask)."""
+    import torch
+    out = {}
+    for dt, name in ((torch.float16, "fp16"), (torch.float32, "fp32")):
+        g = torch.Generator().manual_seed(0)
+        a = torch.randn(BMM_B, BMM_M, BMM_E, generator=g).to(dt).to(dev)
+        b = torch.randn(BMM_B, BMM_E, BMM_M, generator=g).to(dt).to(dev)
+        v = torch.randn(BMM_B, BMM_M, BMM_E, generator=g).to(dt).to(dev)
+        kt = b.transpose(1, 2)
+
+        def composed():
+            torch.bmm(torch.softmax(torch.bmm(a, b), -1), v)
+
+        def fused():
+            torch_kunlun_sdpa(a, kt, v, scale=1.0)
+
+        for label, fn in (("composed", composed), ("fused", fused)):
+            ts = timed_steps(fn, steps, warmup, flush, kunlun)
+            ms = sum(ts) / len(ts)
+            out[f"{name}_{label}"] = {"ms": ms, "tops": BMM_OPS / (ms / 1000) / 1e12}
+    return out
+
+
+def torch_kunlun_sdpa(q, k, v, scale):
+    import torch_kunlun
+    return torch_kunlun.scaled_dot_product_attention(q, k, v, scale=scale)
+
+
+def conv_inputs(case, seed=0):
+    import torch
+    name, C, F, H, k, pad, groups, has_bias = case
+    g = torch.Generator().manual_seed(seed)
+    x = torch.relu(torch.randn(CONV_N, C, H, H, generator=g)).half()
+    fan_in = (C // groups) * k * k
+    w = (torch.randn(F, C // groups, k, k, generator=g) * (2.0 / fan_in) ** 0.5).half()
+    bias = (torch.randn(F, generator=g) * 0.01).half() if has_bias else None
+    return x, w, bias
+
+
+def conv_ops(case):
+    name, C, F, H, k, pad, groups, has_bias = case
+    OH = H + 2 * pad - k + 1
+    return 2 * CONV_N * OH * OH * F * (C // groups) * k * k
+
+
+def conv_measure(dev, kunlun, flush, steps=20, warmup=3):
+    """ResNet-50-stage conv2d shapes at batch 64 (NCHW fp16, Kaiming-normal
+    weights, ReLU(N(0,1)) inputs): device time per conv, TOPS, and for the
+    depthwise case the HBM bytes it must move."""
+    import torch
+    import torch.nn.functional as F
+    res = {}
+    for case in CONV_CASES:
+        name, C, Fo, H, k, pad, groups, has_bias = case
+        x, w, b = conv_inputs(case)
+        xd, wd = x.to(dev), w.to(dev)
+        bd = b.to(dev) if b is not None else None
+
+        def fn():
+            F.conv2d(xd, wd, bd, padding=pad, groups=groups)
+
+        ts = timed_steps(fn, steps, warmup, flush, kunlun)
+        ms = sum(ts) / len(ts)
+        OH = H + 2 * pad - k + 1
+        r = {"ms": ms, "tops": conv_ops(case) / (ms / 1000) / 1e12}
+        if groups > 1:
+            nbytes = (x.numel() + CONV_N * Fo * OH * OH + w.numel()) * 2
+            r["gbs"] = nbytes / (ms / 1000) / 1e9
+        res[name] = r
+    return res
+
+
+def conv_cpu_baseline():
+    """torch CPU aten fp32 conv2d on 4 of the 64 images per case (all host
+    threads): TOPS."""
+    import torch
+    import torch.nn.functional as F
+    torch.set_num_threads(os.cpu_count() or 1)
+    res = {}
+    for case in CONV_CASES:
+        name, C, Fo, H, k, pad, groups, has_bias = case
+        x, w, b = conv_inputs(case)
+        x4 = x[:4].float()
+        wf = w.float()
+        bf = b.float() if b is not None else None
+        F.conv2d(x4, wf, bf, padding=pad, groups=groups)
+        t0 = time.perf_counter()
+        for _ in range(3):
+            F.conv2d(x4, wf, bf, padding=pad, groups=groups)
+        dt = (time.perf_counter() - t0) / 3
+        res[name] = conv_ops(case) * 4 / CONV_N / dt / 1e12
+    return res
+
+
 def dist_env():
     return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
             int(os.environ.get("WORLD_SIZE", "1")))
@@ -325,6 +434,7 @@ def main():
     ap.add_argument("--impl", default="kunlun", choices=["kunlun", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-bert", action="store_true", help="skip the encoder-block measurement")
+    ap.add_argument("--no-extra", action="store_true", help="skip the bmm and conv measurements")
     ap.add_argument("--workload", default="linear", choices=["linear", "tp_mlp", "bert"])
     ap.add_argument("--reduce", default="allreduce", choices=["allreduce", "reduce_scatter"])
     args = ap.parse_args()
@@ -395,6 +505,10 @@ def main():
     bert = None
     if not args.no_bert:
         bert = bert_measure(dev, kunlun, max(5, args.steps // 10), args.warmup, flush)
+    bmm = conv = None
+    if not args.no_extra:
+        bmm = bmm_measure(dev, kunlun, flush)
+        conv = conv_measure(dev, kunlun, flush)
 
     # max over ranks of the timed quantities
     if pg:
@@ -424,6 +538,10 @@ def main():
             bert["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads,
                                     "kind": "torch CPU aten fp32 eager",
                                     "sample": "1 of 32 sequences (512 tokens), median of 3"}
+        if conv:
+            cb = conv_cpu_baseline()
+            for name, v in cb.items():
+                conv[name]["cpu_baseline_tops"] = v
 
     if rank == 0:
         value = world * OPS_PER_STEP / (ms / 1000) / 1e12
@@ -452,6 +570,13 @@ def main():
             "clocks": clock,
             "cpu_baseline": cpu_base,
             "bert_block": bert,
+            "bmm_attention_scores": None if bmm is None else {
+                "workload": "S = A[64,512,128] @ B[64,128,512], P = softmax(S), O = P @ V[64,512,128]",
+                "ops_per_step": BMM_OPS, **bmm},
+            "conv_resnet50": None if conv is None else {
+                "workload": "conv2d NCHW fp16 batch 64, Kaiming-normal weights, ReLU(N(0,1)) inputs",
+                "cpu_baseline": "torch CPU aten fp32 on 4 of 64 images, all host threads",
+                **conv},
         }
         print(json.dumps(line), flush=True)
     if pg:

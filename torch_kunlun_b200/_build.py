@@ -25,7 +25,7 @@ CSRC = os.path.join(PKG, "csrc")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
-KERNEL_SOURCES = ["capi.cu", "quant.cu", "qgemm.cu", "eltwise.cu", "rowops.cu", "conv.cu", "noalloc.cu", "attention.cu"]
+KERNEL_SOURCES = ["capi.cu", "quant.cu", "qgemm.cu", "eltwise.cu", "rowops.cu", "conv.cu", "noalloc.cu", "attention.cu", "conv_tc.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 KERNEL_LIB = os.path.join(PKG, "libtk_kernels.so")
 

@@ -8,6 +8,8 @@
 // Paths:
 //   * groups == C == F/mult (depthwise): a CUDA-core kernel, one output per
 //     thread, exact int64 accumulation of the KHxKW taps.  HBM-bound.
+//   * groups == 1, stride 1: implicit GEMM on the tensor cores (conv_tc.cu),
+//     no patch matrix in HBM.
 //   * otherwise a GEMM per (image, group) on the tensor-core limb kernel:
 //     A = the image's input patches [OH*OW, C/g*KH*KW] quantised straight into
 //     limb planes (1x1 stride-1 convolutions read NCHW directly as a
@@ -27,6 +29,11 @@ int quantize_limbs_launch(tk_dtype_t dtype, const void* x, int64_t batch, int64_
 int qgemm_limbs_ex(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb,
                    const float* amax_a, const float* amax_b, int b_mod, int64_t out_sn,
                    int64_t bias_mod, cudaStream_t stream);
+size_t conv_tc_workspace(int64_t N, int64_t C, int64_t H, int64_t W, int64_t F, int64_t KH, int64_t KW);
+int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, void* out, int64_t N,
+            int64_t C, int64_t H, int64_t W, int64_t F, int64_t KH, int64_t KW, int64_t ph, int64_t pw,
+            int64_t dh, int64_t dw, int64_t OH, int64_t OW, const float* amax_x, const float* amax_w,
+            uint8_t* ws, cudaStream_t stream);
 
 namespace {
 
@@ -125,6 +132,110 @@ __global__ void depthwise_kernel(const T* __restrict__ x, const T* __restrict__ 
     }
 }
 
+// Depthwise on small planes: one warp per output plane (n, f).  The warp
+// quantises its input plane (channel f / mult) into shared memory with
+// coalesced loads, then each lane produces outputs along the row with exact
+// int64 accumulation of the taps; stores are coalesced along ow.
+constexpr int kDwPlaneMax = 1024;  // input elements per plane held in shared memory
+constexpr int kDwWarps = 8;
+
+template <typename T, int DT>
+__global__ void __launch_bounds__(32 * kDwWarps)
+depthwise_plane_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ bias,
+                       T* __restrict__ out, ConvGeom g, const float* __restrict__ amax_x,
+                       const float* __restrict__ amax_w) {
+    __shared__ int16_t plane[kDwWarps][kDwPlaneMax];
+    __shared__ int wq[kDwWarps][64];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t pl = static_cast<int64_t>(blockIdx.x) * kDwWarps + warp;  // n * F + f
+    if (pl >= g.N * g.F) return;
+    const int64_t f = pl % g.F, n = pl / g.F;
+    const int64_t c = f / (g.F / g.C);
+    const float ax = __ldg(amax_x), aw = __ldg(amax_w);
+    const float invx = quant_inv(ax), invw = quant_inv(aw);
+    const double s = dequant_scale(ax, aw);
+    const int HW = static_cast<int>(g.H * g.W);
+    const T* xp = x + (n * g.C + c) * HW;
+    for (int i = lane; i < HW; i += 32) plane[warp][i] = static_cast<int16_t>(quant_one(ldx<T>(xp, i), invx));
+    const int taps = static_cast<int>(g.KH * g.KW);
+    for (int i = lane; i < taps; i += 32) wq[warp][i] = quant_one(ldx<T>(w, f * taps + i), invw);
+    __syncwarp();
+    float bv = 0.0f;
+    if (bias != nullptr) bv = ldx<T>(bias, f);
+    const int OHW = static_cast<int>(g.OH * g.OW);
+    T* op = out + pl * OHW;
+    for (int o = lane; o < OHW; o += 32) {
+        const int oh = o / static_cast<int>(g.OW), ow = o - oh * static_cast<int>(g.OW);
+        long long acc = 0;
+        for (int r = 0; r < g.KH; ++r) {
+            const int ih = oh * static_cast<int>(g.sh) - static_cast<int>(g.ph) + r * static_cast<int>(g.dh);
+            if (ih < 0 || ih >= g.H) continue;
+            for (int q = 0; q < g.KW; ++q) {
+                const int iw = ow * static_cast<int>(g.sw) - static_cast<int>(g.pw) + q * static_cast<int>(g.dw);
+                if (iw < 0 || iw >= g.W) continue;
+                acc += static_cast<long long>(plane[warp][ih * g.W + iw]) * wq[warp][r * g.KW + q];
+            }
+        }
+        float v = round_t_from_double(__dmul_rn(static_cast<double>(acc), s), DT);
+        if (bias != nullptr) v = round_t(__fadd_rn(v, bv), DT);
+        store_t(op, DT, o, v);
+    }
+}
+
+// Depthwise with one output channel per input channel (multiplier 1) on
+// small planes: a block takes a run of whole planes, which is one contiguous
+// span of the NCHW input and of the output.  It quantises the span into
+// shared memory with coalesced loads, then threads produce consecutive
+// outputs (coalesced stores), each with exact int64 accumulation of the taps.
+constexpr int kDwFlatElems = 4096;  // input elements per block in shared memory
+
+template <typename T, int DT>
+__global__ void __launch_bounds__(256)
+depthwise_flat_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ bias,
+                      T* __restrict__ out, ConvGeom g, int planes_per_block,
+                      const float* __restrict__ amax_x, const float* __restrict__ amax_w) {
+    __shared__ int16_t xs[kDwFlatElems];
+    __shared__ int wsq[kDwFlatElems / 4];
+    const int HW = static_cast<int>(g.H * g.W), OHW = static_cast<int>(g.OH * g.OW);
+    const int taps = static_cast<int>(g.KH * g.KW);
+    const int64_t planes = g.N * g.C;
+    const int64_t pl0 = static_cast<int64_t>(blockIdx.x) * planes_per_block;
+    const int np = static_cast<int>(min(static_cast<int64_t>(planes_per_block), planes - pl0));
+    const float ax = __ldg(amax_x), aw = __ldg(amax_w);
+    const float invx = quant_inv(ax), invw = quant_inv(aw);
+    const double s = dequant_scale(ax, aw);
+    const T* xb = x + pl0 * HW;
+    for (int i = threadIdx.x; i < np * HW; i += blockDim.x)
+        xs[i] = static_cast<int16_t>(quant_one(ldx<T>(xb, i), invx));
+    for (int i = threadIdx.x; i < np * taps; i += blockDim.x) {
+        const int pp = i / taps, tp = i - (i / taps) * taps;
+        const int64_t c = (pl0 + pp) % g.C;
+        wsq[i] = quant_one(ldx<T>(w, c * taps + tp), invw);
+    }
+    __syncthreads();
+    T* ob = out + pl0 * OHW;
+    const int OW = static_cast<int>(g.OW);
+    for (int o = threadIdx.x; o < np * OHW; o += blockDim.x) {
+        const int pp = o / OHW, rem = o - (o / OHW) * OHW;
+        const int oh = rem / OW, ow = rem - (rem / OW) * OW;
+        const int16_t* xp = xs + pp * HW;
+        const int* wp = wsq + pp * taps;
+        long long acc = 0;
+        for (int r = 0; r < g.KH; ++r) {
+            const int ih = oh * static_cast<int>(g.sh) - static_cast<int>(g.ph) + r * static_cast<int>(g.dh);
+            if (ih < 0 || ih >= g.H) continue;
+            for (int q = 0; q < g.KW; ++q) {
+                const int iw = ow * static_cast<int>(g.sw) - static_cast<int>(g.pw) + q * static_cast<int>(g.dw);
+                if (iw < 0 || iw >= g.W) continue;
+                acc += static_cast<long long>(xp[ih * g.W + iw]) * wp[r * g.KW + q];
+            }
+        }
+        float v = round_t_from_double(__dmul_rn(static_cast<double>(acc), s), DT);
+        if (bias != nullptr) v = round_t(__fadd_rn(v, ldx<T>(bias, (pl0 + pp) % g.C)), DT);
+        store_t(ob, DT, o, v);
+    }
+}
+
 int grid_1d(int64_t n, int threads) {
     const int64_t g = ceil_div(n, threads);
     const int64_t cap = static_cast<int64_t>(sm_count(current_device())) * 32;
@@ -149,6 +260,12 @@ int geometry(const tk_conv2d_desc_t& d, ConvGeom& g) {
 }
 
 bool is_depthwise(const ConvGeom& g) { return g.groups == g.C && g.groups > 1; }
+// Implicit GEMM on the tensor cores: one group, unit stride (any padding and
+// dilation), and per-tap channel depth within the exact-accumulation limit.
+bool is_implicit(const ConvGeom& g) {
+    return g.groups == 1 && g.sh == 1 && g.sw == 1 && round_up(g.C, 64) * g.KH * g.KW <= 32768 &&
+           g.N * g.H < (1LL << 31);
+}
 bool is_pointwise(const ConvGeom& g) {
     return g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0 &&
            g.groups == 1;
@@ -169,6 +286,11 @@ ConvLayout conv_layout(const ConvGeom& g) {
     if (is_depthwise(g)) {
         L.off_lb = L.off_la;
         L.total = L.off_la;
+        return L;
+    }
+    if (is_implicit(g)) {
+        L.off_lb = L.off_la;
+        L.total = L.off_la + conv_tc_workspace(g.N, g.C, g.H, g.W, g.F, g.KH, g.KW);
         return L;
     }
     L.off_lb = round_up(L.off_la + static_cast<size_t>(g.N * g.groups * 2 * P * L.ld), 1024);
@@ -221,6 +343,35 @@ int tk_conv2d_q16(const tk_conv2d_desc_t* desc, void* workspace, size_t workspac
         aw = amax + 1;
     }
     const int64_t P = g.OH * g.OW;
+    if (is_depthwise(g) && g.F == g.C && g.H * g.W <= kDwFlatElems / 2 &&
+        g.KH * g.KW * (kDwFlatElems / (g.H * g.W)) <= kDwFlatElems / 4) {
+        const int ppb = static_cast<int>(kDwFlatElems / (g.H * g.W));
+        const int64_t blocks = ceil_div(g.N * g.C, ppb);
+        TK_CHECK_ARG(blocks < (1LL << 31), "conv2d: too many planes");
+        if (d.dtype == TK_DTYPE_F16)
+            depthwise_flat_kernel<__half, 0><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+                static_cast<const __half*>(d.x), static_cast<const __half*>(d.weight),
+                static_cast<const __half*>(d.bias), static_cast<__half*>(d.out), g, ppb, ax, aw);
+        else
+            depthwise_flat_kernel<float, 1><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+                static_cast<const float*>(d.x), static_cast<const float*>(d.weight),
+                static_cast<const float*>(d.bias), static_cast<float*>(d.out), g, ppb, ax, aw);
+        return launch_status("conv2d depthwise");
+    }
+    if (is_depthwise(g) && g.H * g.W <= kDwPlaneMax && g.KH * g.KW <= 64) {
+        const int64_t planes = g.N * g.F;
+        TK_CHECK_ARG(ceil_div(planes, kDwWarps) < (1LL << 31), "conv2d: too many planes");
+        const unsigned grid = static_cast<unsigned>(ceil_div(planes, kDwWarps));
+        if (d.dtype == TK_DTYPE_F16)
+            depthwise_plane_kernel<__half, 0><<<grid, 32 * kDwWarps, 0, stream>>>(
+                static_cast<const __half*>(d.x), static_cast<const __half*>(d.weight),
+                static_cast<const __half*>(d.bias), static_cast<__half*>(d.out), g, ax, aw);
+        else
+            depthwise_plane_kernel<float, 1><<<grid, 32 * kDwWarps, 0, stream>>>(
+                static_cast<const float*>(d.x), static_cast<const float*>(d.weight),
+                static_cast<const float*>(d.bias), static_cast<float*>(d.out), g, ax, aw);
+        return launch_status("conv2d depthwise");
+    }
     if (is_depthwise(g)) {
         const int64_t total = g.N * g.F * P;
         const int grid = grid_1d(total, 256);
@@ -234,6 +385,9 @@ int tk_conv2d_q16(const tk_conv2d_desc_t* desc, void* workspace, size_t workspac
                 static_cast<const float*>(d.bias), static_cast<float*>(d.out), g, ax, aw);
         return launch_status("conv2d depthwise");
     }
+    if (is_implicit(g))
+        return conv_tc(d.dtype, d.x, d.weight, d.bias, d.out, g.N, g.C, g.H, g.W, g.F, g.KH, g.KW,
+                       g.ph, g.pw, g.dh, g.dw, g.OH, g.OW, ax, aw, ws + L.off_la, stream);
     int8_t* la = reinterpret_cast<int8_t*>(ws + L.off_la);  // patches [N*groups][2][P][ld]
     int8_t* lb = reinterpret_cast<int8_t*>(ws + L.off_lb);  // weights [groups][2][F/g][ld]
     const int64_t fg = g.F / g.groups;

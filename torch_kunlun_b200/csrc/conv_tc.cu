@@ -1,0 +1,540 @@
+// conv_tc.cu -- implicit-GEMM int16-quantised conv2d on sm_100a tensor cores.
+//
+// Replaces baidu::xpu::api::conv2d<T,T,T,TGEMM> plus the bias broadcast_add
+// of conv2d_impl (csrc/ops.cpp:237-285) for groups == 1, stride 1 (any
+// padding and dilation).  Semantics are those of the explicit path in
+// conv.cu: one max-abs scale for the whole input and one for the whole
+// weight, exact integer MAC, T(acc * s), then the bias added and rounded.
+//
+// Data flow (no patch matrix in HBM):
+//   x_limbs_kernel   NCHW input -> quantised NHWC limb rows: per pixel, per
+//                    group of 64 channels, 128 bytes [hi of the 64 | lo of
+//                    the 64] (hi = q >> 8 signed, lo = q & 255 unsigned);
+//   w_limbs_kernel   OIHW weight -> [F][KH][KW][channel groups] limb rows of
+//                    the same 128-byte form;
+//   conv_tc_kernel   one CTA per SM, persistent over output tiles of
+//                    TH x TW pixels of one image x BN filters.  Each K step
+//                    is one (tap, 64-channel group): a 4-D TMA box
+//                    {128 B, TW, TH, 1} at (group, ow0 + kw*dw - pw,
+//                    oh0 + kh*dh - ph, n) gathers the shifted input window
+//                    (out-of-range rows and columns -- the padding -- load as
+//                    zero), a 2-D box brings the BN filters' rows, and four
+//                    tcgen05 kind::i8 MMAs per 32-byte sub-block build the
+//                    HH / MID / LL accumulators in TMEM.  Sixteen epilogue
+//                    warps recombine exactly, dequantise, add the bias and
+//                    store NCHW: lanes are consecutive pixels, so every
+//                    store instruction is coalesced along the output row.
+// The 128-row MMA covers TH*TW <= 128 pixels (TW = min(OW, 128)); rows past
+// TH*TW hold stale shared memory and are never stored.  With BN = 64 the
+// accumulators are double-buffered so the epilogue of one tile overlaps the
+// MMAs of the next.  Every wait is bounded; no TMA multicast is used.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "tk_internal.h"
+#include "tk_numerics.cuh"
+#include "tk_ptx.cuh"
+
+namespace tk {
+namespace {
+
+constexpr int BM = 128;
+constexpr int KB = 128;  // bytes per K step: one 64-channel group, both limbs
+constexpr int NUM_EPI_WARPS = 16;  // four per TMEM lane quarter
+constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr int A_BYTES = BM * KB;
+
+// K steps are small (one 64-channel group, 8 MMAs), so the ring is deep to
+// keep enough TMA bytes in flight to cover L2 latency.
+template <int BN_, int NBUF_, int STAGES_>
+struct ConvCfg {
+    static constexpr int BN = BN_;
+    static constexpr int NBUF = NBUF_;
+    static constexpr int STAGES = STAGES_;
+    static constexpr int B_BYTES = BN * KB;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int BUF_COLS = NBUF == 1 ? 3 * BN : 256;
+    static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+    static constexpr int SMEM = OFF_BAR + 256 + 1024;
+    static constexpr uint32_t IDESC_SS = idesc_i8(BM, BN, true, true);
+    static constexpr uint32_t IDESC_SU = idesc_i8(BM, BN, true, false);
+    static constexpr uint32_t IDESC_US = idesc_i8(BM, BN, false, true);
+    static constexpr uint32_t IDESC_UU = idesc_i8(BM, BN, false, false);
+    static_assert(NBUF * BUF_COLS <= TMEM_COLS && 3 * BN <= BUF_COLS, "TMEM budget");
+};
+using ConvNarrow = ConvCfg<64, 2, 8>;
+using ConvWide = ConvCfg<128, 1, 6>;
+
+struct ConvTcParams {
+    int N, F, OH, OW, KH, KW, ph, pw, dh, dw, Cg;
+    int TH, TW, tiles_h, tiles_w, tiles_f, tiles;
+    int num_kb;
+    const float* amax_x;
+    const float* amax_w;
+    const void* bias;
+    void* out;
+    unsigned* err;
+};
+
+__device__ __forceinline__ void decode(const ConvTcParams& p, int t, int& n, int& oh0, int& ow0, int& fb) {
+    fb = t % p.tiles_f;
+    int r = t / p.tiles_f;
+    const int tw = r % p.tiles_w;
+    r /= p.tiles_w;
+    const int th = r % p.tiles_h;
+    n = r / p.tiles_h;
+    oh0 = th * p.TH;
+    ow0 = tw * p.TW;
+}
+
+template <class C, int DT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+               const ConvTcParams p) {
+    constexpr int BN = C::BN;
+    constexpr int NBUF = C::NBUF;
+    constexpr int STAGES = C::STAGES;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+    uint64_t* full_bar = bars;
+    uint64_t* empty_bar = bars + STAGES;
+    uint64_t* acc_full = bars + 2 * STAGES;
+    uint64_t* acc_empty = acc_full + NBUF;
+    uint64_t* drain_bar = acc_empty + NBUF;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(full_bar + s), 1);
+            mbar_init(smem_u32(empty_bar + s), 1);
+        }
+        for (int b = 0; b < NBUF; ++b) {
+            mbar_init(smem_u32(acc_full + b), 1);
+            mbar_init(smem_u32(acc_empty + b), NUM_EPI_WARPS);
+        }
+        mbar_init(smem_u32(drain_bar), 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmX);
+        tma_prefetch_desc(&tmW);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t a_bytes = static_cast<uint32_t>(p.TH * p.TW * KB);
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t last_phase[STAGES];
+        bool used[STAGES];
+        for (int s = 0; s < STAGES; ++s) { used[s] = false; last_phase[s] = 0; }
+        bool ok = true;
+        for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+            int n, oh0, ow0, fb;
+            decode(p, t, n, oh0, ow0, fb);
+            int cg = 0, kw = 0, kh = 0;
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                if (!mbar_wait_bounded(smem_u32(empty_bar + stage), phase ^ 1u, abort_flag, p.err,
+                                       kDevErrWaitEmpty)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t fbar = smem_u32(full_bar + stage);
+                    uint8_t* sb = smem + stage * C::STAGE_BYTES;
+                    mbar_arrive_expect_tx(fbar, a_bytes + C::B_BYTES);
+                    tma_load_4d(smem_u32(sb), &tmX, fbar, cg * KB, ow0 + kw * p.dw - p.pw,
+                                oh0 + kh * p.dh - p.ph, n);
+                    tma_load_3d(smem_u32(sb + A_BYTES), &tmW, fbar, kb * KB, fb * BN, 0);
+                }
+                __syncwarp();
+                used[stage] = true;
+                last_phase[stage] = phase;
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                if (++cg == p.Cg) {
+                    cg = 0;
+                    if (++kw == p.KW) { kw = 0; ++kh; }
+                }
+            }
+        }
+        volatile int no_abort = 0;
+        for (int s = 0; s < STAGES; ++s)
+            if (used[s])
+                mbar_wait_bounded(smem_u32(full_bar + s), last_phase[s], &no_abort, p.err, kDevErrWaitDrain);
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        int local = 0;
+        for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++local) {
+            const int buf = local % NBUF;
+            const uint32_t acc_phase = static_cast<uint32_t>(local / NBUF) & 1u;
+            if (!mbar_wait_bounded(smem_u32(acc_empty + buf), acc_phase ^ 1u, abort_flag, p.err,
+                                   kDevErrWaitAccEmpty))
+                break;
+            tc_fence_after();
+            const uint32_t acc_hh = tmem_base + buf * C::BUF_COLS;
+            const uint32_t acc_mid = acc_hh + BN;
+            const uint32_t acc_ll = acc_hh + 2 * BN;
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                if (!mbar_wait_bounded(smem_u32(full_bar + stage), phase, abort_flag, p.err,
+                                       kDevErrWaitFull)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t sb = smem_u32(smem + stage * C::STAGE_BYTES);
+                    const uint64_t a0 = smem_desc_kmajor_sw128(sb);
+                    const uint64_t b0 = smem_desc_kmajor_sw128(sb + A_BYTES);
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const uint64_t hi = static_cast<uint64_t>((u * 32) >> 4);
+                        const uint64_t lo = static_cast<uint64_t>((64 + u * 32) >> 4);
+                        const uint32_t acc = (kb > 0 || u > 0) ? 1u : 0u;
+                        tc_mma_i8(acc_hh, a0 + hi, b0 + hi, C::IDESC_SS, acc);
+                        tc_mma_i8(acc_mid, a0 + hi, b0 + lo, C::IDESC_SU, acc);
+                        tc_mma_i8(acc_mid, a0 + lo, b0 + hi, C::IDESC_US, 1u);
+                        tc_mma_i8(acc_ll, a0 + lo, b0 + lo, C::IDESC_UU, acc);
+                    }
+                    tc_commit(smem_u32(empty_bar + stage));
+                }
+                __syncwarp();
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+            if (!ok) break;
+            if (lane == 0) tc_commit(smem_u32(acc_full + buf));
+            __syncwarp();
+        }
+        if (lane == 0) tc_commit(smem_u32(drain_bar));
+        __syncwarp();
+        volatile int no_abort = 0;
+        mbar_wait_bounded(smem_u32(drain_bar), 0, &no_abort, p.err, kDevErrWaitDrain);
+    } else {
+        // ---------------- epilogue (warps 2..9) ----------------
+        const int quarter = warp & 3;
+        const int sub = (warp - 2) >> 2;  // which quarter of the BN columns
+        const int row = quarter * 32 + lane;
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        const double s = dequant_scale(__ldg(p.amax_x), __ldg(p.amax_w));
+        const int64_t plane = static_cast<int64_t>(p.OH) * p.OW;
+        const int th = row / p.TW, tw = row - (row / p.TW) * p.TW;
+        constexpr int ES = DT == 0 ? 2 : 4;
+        int local = 0;
+        for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++local) {
+            int n, oh0, ow0, fb;
+            decode(p, t, n, oh0, ow0, fb);
+            const int buf = local % NBUF;
+            const uint32_t acc_phase = static_cast<uint32_t>(local / NBUF) & 1u;
+            if (!mbar_wait_bounded(smem_u32(acc_full + buf), acc_phase, abort_flag, p.err,
+                                   kDevErrWaitAccFull))
+                break;
+            tc_fence_after();
+            const uint32_t t_buf = t_row + buf * C::BUF_COLS;
+            const int oh = oh0 + th, ow = ow0 + tw;
+            const bool pix_ok = row < p.TH * p.TW && oh < p.OH && ow < p.OW;
+            const int64_t pix = static_cast<int64_t>(oh) * p.OW + ow;
+#pragma unroll 1
+            for (int c = sub * (BN / 64); c < (sub + 1) * (BN / 64); ++c) {  // 16-column blocks
+                uint32_t hh[16], mid[16], ll[16];
+                tmem_ld_32x32b_x16(t_buf + c * 16, hh);
+                tmem_ld_32x32b_x16(t_buf + BN + c * 16, mid);
+                tmem_ld_32x32b_x16(t_buf + 2 * BN + c * 16, ll);
+                tc_wait_ld();
+                const int f0 = fb * BN + c * 16;
+                if (!pix_ok || f0 >= p.F) continue;
+                // column f of this pixel sits plane elements after column f - 1
+                char* o = static_cast<char*>(p.out) + ((static_cast<int64_t>(n) * p.F + f0) * plane + pix) * ES;
+                const int64_t step = plane * ES;
+                const int nf = min(16, p.F - f0);
+                if constexpr (DT == 0) {
+                    // T(acc * s) rounds once from binary64 to binary16; the bias
+                    // add in binary16 equals the binary32 add rounded to binary16
+                    // (binary32 carries more than 2*11 + 2 significand bits).
+                    __half bv[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) bv[j] = __ushort_as_half(0);
+                    if (p.bias != nullptr) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (j < nf) bv[j] = static_cast<const __half*>(p.bias)[f0 + j];
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        __half h = __double2half(__dmul_rn(limb_acc_to_double(hh[j], mid[j], ll[j]), s));
+                        if (p.bias != nullptr) h = __hadd(h, bv[j]);
+                        if (j < nf) *reinterpret_cast<__half*>(o + j * step) = h;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        if (j < nf) {
+                            float v = __double2float_rn(__dmul_rn(limb_acc_to_double(hh[j], mid[j], ll[j]), s));
+                            if (p.bias != nullptr) v = __fadd_rn(v, static_cast<const float*>(p.bias)[f0 + j]);
+                            *reinterpret_cast<float*>(o + j * step) = v;
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(acc_empty + buf));
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ---- operand quantisation into 128-byte limb rows ---------------------------
+
+constexpr int XQ_W = 128;   // pixels per block pass
+constexpr int XQ_THREADS = 256;
+
+__device__ __forceinline__ int64_t ceil_div_dev(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+template <typename T> __device__ __forceinline__ float ldt(const T* p, int64_t i);
+template <> __device__ __forceinline__ float ldt<__half>(const __half* p, int64_t i) { return __half2float(__ldg(p + i)); }
+template <> __device__ __forceinline__ float ldt<float>(const float* p, int64_t i) { return __ldg(p + i); }
+
+__device__ __forceinline__ void pack16(const int16_t* q, int stride, uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        h[w] = 0;
+        l[w] = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int v = q[(4 * w + k) * stride];
+            h[w] |= static_cast<uint32_t>((v >> 8) & 0xFF) << (8 * k);
+            l[w] |= static_cast<uint32_t>(v & 0xFF) << (8 * k);
+        }
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// One block per (image, 128-pixel run of the flattened H*W plane, 64-channel
+// group): the 64 x 128 tile is read along the pixels (contiguous in NCHW,
+// 16-byte vectors when aligned), quantised into shared memory and written as
+// each pixel's 128-byte limb row of that channel group (NHWC order).
+template <typename T>
+__global__ void __launch_bounds__(XQ_THREADS)
+x_limbs_kernel(const T* __restrict__ x, int C, int64_t HW, int Cg, int vec,
+               const float* __restrict__ amax, uint8_t* __restrict__ xl) {
+    __shared__ int16_t q[64][XQ_W + 2];
+    const int64_t runs = ceil_div_dev(HW, XQ_W);
+    const int g = blockIdx.x % Cg;
+    const int64_t r = blockIdx.x / Cg;
+    const int64_t p0 = (r % runs) * XQ_W;
+    const int64_t n = r / runs;
+    const int pn = static_cast<int>(HW - p0 < XQ_W ? HW - p0 : XQ_W);
+    const float inv = quant_inv(__ldg(amax));
+    const T* xs = x + (n * C + g * 64) * HW + p0;
+    constexpr int V = 16 / sizeof(T);
+    if (vec) {
+        // V consecutive pixels per thread; HW and p0 are multiples of V
+        for (int it = threadIdx.x; it < 64 * (XQ_W / V); it += XQ_THREADS) {
+            const int cc = it / (XQ_W / V), pv = (it - cc * (XQ_W / V)) * V;
+            float v[V];
+            if (g * 64 + cc < C && pv < pn) {
+                if constexpr (sizeof(T) == 2) {
+                    const uint4 u = __ldg(reinterpret_cast<const uint4*>(xs + cc * HW + pv));
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = __half22float2(h2[e]);
+                        v[2 * e] = f.x;
+                        v[2 * e + 1] = f.y;
+                    }
+                } else {
+                    const float4 f = __ldg(reinterpret_cast<const float4*>(xs + cc * HW + pv));
+                    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < V; ++e) v[e] = 0.0f;
+            }
+#pragma unroll
+            for (int e = 0; e < V; ++e) q[cc][pv + e] = static_cast<int16_t>(quant_one(v[e], inv));
+        }
+    } else {
+        for (int it = threadIdx.x; it < 64 * XQ_W; it += XQ_THREADS) {
+            const int cc = it / XQ_W, pp = it - (it / XQ_W) * XQ_W;
+            int v = 0;
+            if (g * 64 + cc < C && pp < pn) v = quant_one(ldt<T>(xs, cc * HW + pp), inv);
+            q[cc][pp] = static_cast<int16_t>(v);
+        }
+    }
+    __syncthreads();
+    uint8_t* out = xl + ((n * HW + p0) * Cg + g) * 128;
+    for (int it = threadIdx.x; it < pn * 4; it += XQ_THREADS) {
+        const int pp = it >> 2, pc = it & 3;
+        uint4 hi, lo;
+        pack16(&q[pc * 16][pp], XQ_W + 2, hi, lo);
+        uint8_t* dst = out + static_cast<int64_t>(pp) * (Cg * 128) + pc * 16;
+        *reinterpret_cast<uint4*>(dst) = hi;
+        *reinterpret_cast<uint4*>(dst + 64) = lo;
+    }
+}
+
+// Weight limb rows [F][KH][KW][Cg][128 B]: thread per (f, tap, group, 16-channel piece).
+template <typename T>
+__global__ void w_limbs_kernel(const T* __restrict__ w, int F, int C, int KH, int KW, int Cg,
+                               const float* __restrict__ amax, uint8_t* __restrict__ wl) {
+    const int taps = KH * KW;
+    const int64_t total = static_cast<int64_t>(F) * taps * Cg * 4;
+    const float inv = quant_inv(__ldg(amax));
+    for (int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < total;
+         it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int pc = static_cast<int>(it & 3);
+        int64_t r = it >> 2;
+        const int g = static_cast<int>(r % Cg);
+        r /= Cg;
+        const int tap = static_cast<int>(r % taps);
+        const int f = static_cast<int>(r / taps);
+        int16_t q[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const int c = g * 64 + pc * 16 + k;
+            q[k] = static_cast<int16_t>(c < C ? quant_one(ldt<T>(w, (static_cast<int64_t>(f) * C + c) * taps + tap), inv) : 0);
+        }
+        uint4 hi, lo;
+        pack16(q, 1, hi, lo);
+        uint8_t* dst = wl + ((static_cast<int64_t>(f) * taps + tap) * Cg + g) * 128 + pc * 16;
+        *reinterpret_cast<uint4*>(dst) = hi;
+        *reinterpret_cast<uint4*>(dst + 64) = lo;
+    }
+}
+
+template <class C, int DT>
+int launch_conv(const CUtensorMap& tx, const CUtensorMap& tw, const ConvTcParams& p, int dev,
+                cudaStream_t stream) {
+    static std::once_flag once[64];
+    static cudaError_t err[64];
+    const int slot = std::min(dev, 63);
+    std::call_once(once[slot], [&] {
+        err[slot] = cudaFuncSetAttribute(conv_tc_kernel<C, DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM);
+    });
+    if (err[slot] != cudaSuccess) TK_FAIL(TK_ERR_CUDA, "conv smem attribute: %s", cudaGetErrorString(err[slot]));
+    const int grid = std::min(p.tiles, sm_count(dev));
+    conv_tc_kernel<C, DT><<<grid, NUM_THREADS, C::SMEM, stream>>>(tx, tw, p);
+    return launch_status("conv2d implicit GEMM");
+}
+
+}  // namespace
+
+// Workspace bytes of the implicit-GEMM path (limb rows of x and w).
+size_t conv_tc_workspace(int64_t N, int64_t C, int64_t H, int64_t W, int64_t F, int64_t KH, int64_t KW) {
+    const int64_t Cg = ceil_div(C, 64);
+    return round_up(static_cast<size_t>(N * H * W * Cg * 128), 1024) +
+           round_up(static_cast<size_t>(F * KH * KW * Cg * 128), 1024);
+}
+
+// Implicit-GEMM conv2d for groups == 1 and stride 1; `ws` is 1024-aligned
+// with conv_tc_workspace(...) bytes; amax_x / amax_w are device scalars.
+int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, void* out, int64_t N,
+            int64_t C, int64_t H, int64_t W, int64_t F, int64_t KH, int64_t KW, int64_t ph, int64_t pw,
+            int64_t dh, int64_t dw, int64_t OH, int64_t OW, const float* amax_x, const float* amax_w,
+            uint8_t* ws, cudaStream_t stream) {
+    const int dev = current_device();
+    const int64_t Cg = ceil_div(C, 64);
+    uint8_t* xl = ws;
+    uint8_t* wl = ws + round_up(static_cast<size_t>(N * H * W * Cg * 128), 1024);
+    const int64_t runs = ceil_div(H * W, XQ_W);
+    TK_CHECK_ARG(N * runs * Cg < (1LL << 31), "conv2d: input too large");
+    const unsigned xgrid = static_cast<unsigned>(N * runs * Cg);
+    const size_t es = dtype_size(dtype);
+    const int xvec = ((H * W) % static_cast<int64_t>(16 / es) == 0 &&
+                      reinterpret_cast<uintptr_t>(x) % 16 == 0) ? 1 : 0;
+    if (dtype == TK_DTYPE_F16) {
+        x_limbs_kernel<__half><<<xgrid, XQ_THREADS, 0, stream>>>(
+            static_cast<const __half*>(x), (int)C, H * W, (int)Cg, xvec, amax_x, xl);
+        w_limbs_kernel<__half><<<std::max<int64_t>(1, std::min<int64_t>(ceil_div(F * KH * KW * Cg * 4, 256), 4096)), 256, 0,
+                                 stream>>>(static_cast<const __half*>(w), (int)F, (int)C, (int)KH, (int)KW, (int)Cg,
+                                           amax_w, wl);
+    } else {
+        x_limbs_kernel<float><<<xgrid, XQ_THREADS, 0, stream>>>(
+            static_cast<const float*>(x), (int)C, H * W, (int)Cg, xvec, amax_x, xl);
+        w_limbs_kernel<float><<<std::max<int64_t>(1, std::min<int64_t>(ceil_div(F * KH * KW * Cg * 4, 256), 4096)), 256, 0,
+                                stream>>>(static_cast<const float*>(w), (int)F, (int)C, (int)KH, (int)KW, (int)Cg,
+                                          amax_w, wl);
+    }
+    int rc = launch_status("conv2d limbs");
+    if (rc) return rc;
+
+    ConvTcParams p;
+    p.N = (int)N; p.F = (int)F; p.OH = (int)OH; p.OW = (int)OW; p.KH = (int)KH; p.KW = (int)KW;
+    p.ph = (int)ph; p.pw = (int)pw; p.dh = (int)dh; p.dw = (int)dw; p.Cg = (int)Cg;
+    p.TW = static_cast<int>(std::min<int64_t>(OW, BM));
+    p.TH = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(BM / p.TW, OH)));
+    p.tiles_h = static_cast<int>(ceil_div(OH, p.TH));
+    p.tiles_w = static_cast<int>(ceil_div(OW, p.TW));
+    const bool narrow = F <= 64;
+    const int BN = narrow ? ConvNarrow::BN : ConvWide::BN;
+    p.tiles_f = static_cast<int>(ceil_div(F, BN));
+    const int64_t tiles = N * p.tiles_h * p.tiles_w * p.tiles_f;
+    TK_CHECK_ARG(tiles < (1LL << 31), "conv2d: too many tiles");
+    p.tiles = static_cast<int>(tiles);
+    p.num_kb = static_cast<int>(KH * KW * Cg);
+    p.amax_x = amax_x;
+    p.amax_w = amax_w;
+    p.bias = bias;
+    p.out = out;
+    p.err = device_error_word(dev);
+
+    EncodeTiledFn enc = tensor_map_encoder();
+    if (enc == nullptr) TK_FAIL(TK_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    CUtensorMap tx, tw;
+    {
+        const uint64_t row = static_cast<uint64_t>(Cg) * 128;
+        cuuint64_t dims[4] = {row, static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H),
+                              static_cast<cuuint64_t>(N)};
+        cuuint64_t strides[3] = {row, row * W, row * W * H};
+        cuuint32_t box[4] = {128, static_cast<cuuint32_t>(p.TW), static_cast<cuuint32_t>(p.TH), 1};
+        cuuint32_t estr[4] = {1, 1, 1, 1};
+        CUresult r = enc(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, xl, dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) TK_FAIL(TK_ERR_CUDA, "conv2d input tensor map failed (%d)", (int)r);
+    }
+    {
+        const uint64_t row = static_cast<uint64_t>(KH * KW * Cg) * 128;
+        cuuint64_t dims[3] = {row, static_cast<cuuint64_t>(F), 1};
+        cuuint64_t strides[2] = {row, row * F};
+        cuuint32_t box[3] = {128, static_cast<cuuint32_t>(BN), 1};
+        cuuint32_t estr[3] = {1, 1, 1};
+        CUresult r = enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, wl, dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) TK_FAIL(TK_ERR_CUDA, "conv2d weight tensor map failed (%d)", (int)r);
+    }
+    if (narrow)
+        return dtype == TK_DTYPE_F16 ? launch_conv<ConvNarrow, 0>(tx, tw, p, dev, stream)
+                                     : launch_conv<ConvNarrow, 1>(tx, tw, p, dev, stream);
+    return dtype == TK_DTYPE_F16 ? launch_conv<ConvWide, 0>(tx, tw, p, dev, stream)
+                                 : launch_conv<ConvWide, 1>(tx, tw, p, dev, stream);
+}
+
+}  // namespace tk

@@ -114,6 +114,17 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
         : "memory");
 }
 
+// 4-D tiled load (no multicast); c0 innermost, a multiple of 16 bytes.  Other
+// coordinates may be negative or past the end: those elements read as zero.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint32_t bar,
+                                            int c0, int c1, int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
 // ---- tcgen05 ------------------------------------------------------------------
 
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
