@@ -104,6 +104,7 @@ struct EpiParams {
     int64_t scale_stride;  // 1: per-slice amax; 0: one amax for all slices
     bool vec_store;
     bool bias_vec;  // bias is 16-byte aligned: vector loads per 16-column chunk
+    bool add_vec;   // addend rows contiguous and 16-byte aligned: vector loads
     int32_t* dbg;  // [3][M][N] raw accumulators of slice 0, or null
 };
 
@@ -325,6 +326,10 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         const bool has_bias = ep.bias != nullptr;
         const bool has_add = ep.addend != nullptr && ep.beta != 0.0f;
         const bool has_alpha = ep.alpha != 1.0f;
+        const bool fast_ok = ep.vec_store && !has_alpha && ep.dbg == nullptr &&
+                             (!has_bias || (ep.bias_vec && ep.bias_mod == 0)) &&
+                             (!has_add || (ep.add_vec && ep.beta == 1.0f));
+        const void* bias_base = ep.bias;
         int local = 0;
         for (int t = blockIdx.x; t < tp.num_tiles; t += gridDim.x, ++local) {
             int b, mt, nt;
@@ -343,14 +348,65 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             const int64_t out_row = b * ep.out_sb + m * ep.out_sm;
 #pragma unroll 1
             for (int c = half; c < BN / 16; c += 2) {  // 16-column chunks, alternating halves
+                const int64_t n0 = static_cast<int64_t>(nt) * BN + c * 16;
+                const bool full = n0 + 16 <= ep.N;
+                // fp16 fast path: whole chunk, no alpha, vector bias / addend / store
+                const bool fast = DT == 0 && fast_ok && row_ok && full;
+                uint4 add_q[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+                if (fast && has_add) {  // issued before the TMEM loads to hide its latency
+                    const uint4* src = reinterpret_cast<const uint4*>(
+                        static_cast<const __half*>(ep.addend) + b * ep.add_sb + m * ep.add_sm + n0);
+                    add_q[0] = __ldg(src);
+                    add_q[1] = __ldg(src + 1);
+                }
                 uint32_t hh[16], mid[16], ll[16];
                 tmem_ld_32x32b_x16(t_buf + c * 16, hh);
                 tmem_ld_32x32b_x16(t_buf + BN + c * 16, mid);
                 tmem_ld_32x32b_x16(t_buf + 2 * BN + c * 16, ll);
                 tc_wait_ld();
-                const int64_t n0 = static_cast<int64_t>(nt) * BN + c * 16;
                 if (!row_ok || n0 >= ep.N) continue;
-                const bool full = n0 + 16 <= ep.N;
+                if constexpr (DT == 0) {
+                    if (fast) {
+                        // One binary64 -> binary16 rounding, then the bias and
+                        // addend in binary16: each add of two binary16 values
+                        // rounded once equals the binary32 add rounded to
+                        // binary16 (binary32 has more than 2*11 + 2 bits).
+                        __half2 hv[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            hv[j] = __halves2half2(
+                                __double2half(__dmul_rn(limb_acc_to_double(hh[2 * j], mid[2 * j], ll[2 * j]), s)),
+                                __double2half(__dmul_rn(limb_acc_to_double(hh[2 * j + 1], mid[2 * j + 1], ll[2 * j + 1]), s)));
+                        if (has_bias) {
+                            const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __half*>(bias_base) + n0);
+                            const uint4 q0 = __ldg(src), q1 = __ldg(src + 1);
+                            const __half2* b0 = reinterpret_cast<const __half2*>(&q0);
+                            const __half2* b1 = reinterpret_cast<const __half2*>(&q1);
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                hv[j] = __hadd2(hv[j], b0[j]);
+                                hv[4 + j] = __hadd2(hv[4 + j], b1[j]);
+                            }
+                        }
+                        if (has_add) {
+                            const __half2* a2 = reinterpret_cast<const __half2*>(add_q);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) hv[j] = __hadd2(hv[j], a2[j]);
+                        }
+                        if constexpr (ACT != TK_ACT_NONE) {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                const float2 f = __half22float2(hv[j]);
+                                hv[j] = __floats2half2_rn(act_t<ACT>(f.x, DT), act_t<ACT>(f.y, DT));
+                            }
+                        }
+                        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(ep.out) + out_row + n0);
+                        const uint4* w = reinterpret_cast<const uint4*>(hv);
+                        dst[0] = w[0];
+                        dst[1] = w[1];
+                        continue;
+                    }
+                }
                 float v[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
@@ -594,6 +650,9 @@ EpiParams make_epi(const tk_qgemm_desc_t& d, const float* amax_a, const float* a
                    (d.batch <= 1 || (d.out_sb * static_cast<int64_t>(es)) % 16 == 0);
     ep.bias_vec = d.bias != nullptr && reinterpret_cast<uintptr_t>(d.bias) % 16 == 0 &&
                   (ep.bias_mod == 0 || (d.n * static_cast<int64_t>(es)) % 16 == 0);
+    ep.add_vec = d.addend != nullptr && reinterpret_cast<uintptr_t>(d.addend) % 16 == 0 &&
+                 d.add_sn == 1 && (d.add_sm * static_cast<int64_t>(es)) % 16 == 0 &&
+                 (d.add_sb * static_cast<int64_t>(es)) % 16 == 0;
     ep.dbg = dbg;
     return ep;
 }
