@@ -248,6 +248,8 @@ amax_multi_kernel(AmaxDesc d0, AmaxDesc d1, int64_t blocks0) {
 
 // Row-contiguous operand quantised 8 columns per thread: one 128-bit load
 // (two for fp32) and two 64-bit limb stores per step.
+__device__ __forceinline__ int64_t ceil_div_dev(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
 struct QVecDesc {
     const void* x;
     int64_t rows, cols, ld, sb, sr;
@@ -310,25 +312,63 @@ __device__ __forceinline__ void quant8_pack(const float (&v)[8], float inv, uint
     hi.y = __byte_perm(__byte_perm(q[4], q[5], 0x0051), __byte_perm(q[6], q[7], 0x0051), 0x5410);
 }
 
-// One warp per row: lanes walk the row's 8-column groups (a warp moves 512 B
-// of fp16 per step), eight rows per block.  Rows [0, rows0) belong to d0.
+// One warp quantises one segment of kSegGroups 8-column groups of a row:
+// each lane issues its four 128-bit loads before using any of them, and the
+// small segments give a fine-grained, balanced grid.
+constexpr int kSegGroups = 128;
+
 template <typename T>
-__device__ __forceinline__ void quant_vec_row(const QVecDesc& d, int64_t row, int lane) {
+__device__ __forceinline__ void quant_vec_segment(const QVecDesc& d, int64_t row, int64_t seg, int lane) {
     const int64_t b = row / d.rows;
     const int64_t r = row - b * d.rows;
     const float inv = quant_inv(d.amax[b * d.amax_stride]);
     const T* src = static_cast<const T*>(d.x) + b * d.sb + r * d.sr;
     const int64_t plane = d.rows * d.ld;
     int8_t* dst = d.limbs + (b * 2) * plane + r * d.ld;
-    // Four groups per lane per step: their loads are issued before any is
-    // used, so a warp keeps 4 x 512 B in flight instead of one.
-    for (int64_t g0 = lane; g0 < d.groups; g0 += 128) {
-        float v[4][8];
+    const int64_t g0 = seg * kSegGroups + lane;
+    if constexpr (sizeof(T) == 2) {
+        // keep the four loads as raw 128-bit words (16 registers) until used
+        uint4 w[4];
+        bool part[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int64_t c0 = (g0 + 32 * u) * 8;
             const int64_t n = d.cols - c0;
-            if (g0 + 32 * u < d.groups && n > 0) {
+            part[u] = n > 0 && n < 8;
+            w[u] = (g0 + 32 * u < d.groups && n >= 8) ? __ldg(reinterpret_cast<const uint4*>(src + c0))
+                                                      : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t g = g0 + 32 * u;
+            if (g < d.groups) {
+                const int64_t c0 = g * 8;
+                float v[8];
+                if (part[u]) {
+                    load8<T>(src + c0, d.cols - c0, v);
+                } else {
+                    const __half2* h = reinterpret_cast<const __half2*>(&w[u]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 f = __half22float2(h[j]);
+                        v[2 * j] = f.x;
+                        v[2 * j + 1] = f.y;
+                    }
+                }
+                uint2 hi, lo;
+                quant8_pack(v, inv, hi, lo);
+                *reinterpret_cast<uint2*>(dst + c0) = hi;
+                *reinterpret_cast<uint2*>(dst + plane + c0) = lo;
+            }
+        }
+    } else {
+        float v[4][8];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t g = g0 + 32 * u;
+            const int64_t c0 = g * 8;
+            const int64_t n = d.cols - c0;
+            if (g < d.groups && n > 0) {
                 load8<T>(src + c0, n, v[u]);
             } else {
 #pragma unroll
@@ -338,25 +378,28 @@ __device__ __forceinline__ void quant_vec_row(const QVecDesc& d, int64_t row, in
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int64_t g = g0 + 32 * u;
-            if (g >= d.groups) break;
-            uint2 hi, lo;
-            quant8_pack(v[u], inv, hi, lo);
-            const int64_t c0 = g * 8;
-            *reinterpret_cast<uint2*>(dst + c0) = hi;
-            *reinterpret_cast<uint2*>(dst + plane + c0) = lo;
+            if (g < d.groups) {
+                uint2 hi, lo;
+                quant8_pack(v[u], inv, hi, lo);
+                const int64_t c0 = g * 8;
+                *reinterpret_cast<uint2*>(dst + c0) = hi;
+                *reinterpret_cast<uint2*>(dst + plane + c0) = lo;
+            }
         }
     }
 }
 
+// Warp items [0, items0) are (row, segment) pairs of d0, the rest of d1.
 template <typename T>
-__global__ void __launch_bounds__(256) quant_vec_kernel(QVecDesc d0, QVecDesc d1, int64_t rows0,
-                                                        int64_t rows_total) {
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + threadIdx.y;
-    if (row >= rows_total) return;
-    if (row < rows0)
-        quant_vec_row<T>(d0, row, threadIdx.x);
-    else
-        quant_vec_row<T>(d1, row - rows0, threadIdx.x);
+__global__ void __launch_bounds__(256) quant_vec_kernel(QVecDesc d0, QVecDesc d1, int64_t items0,
+                                                        int64_t items_total) {
+    const int64_t item = static_cast<int64_t>(blockIdx.x) * 8 + threadIdx.y;
+    if (item >= items_total) return;
+    const bool first = item < items0;
+    const QVecDesc& d = first ? d0 : d1;
+    const int64_t it = first ? item : item - items0;
+    const int64_t segs = ceil_div_dev(d.groups, kSegGroups);
+    quant_vec_segment<T>(d, it / segs, it - (it / segs) * segs, threadIdx.x);
 }
 
 }  // namespace
@@ -518,17 +561,20 @@ int quantise_operands(tk_dtype_t dt, const QuantOperand* ops, int nops, cudaStre
         }
     }
     if (nvec > 0) {
-        const int64_t rows0 = vd[0].items / vd[0].groups;
-        const int64_t rows1 = nvec > 1 ? vd[1].items / vd[1].groups : 0;
-        const int64_t blocks = ceil_div(rows0 + rows1, 8);
+        auto warp_items = [](const QVecDesc& d) {
+            return d.items / d.groups * ceil_div(d.groups, kSegGroups);  // rows x segments
+        };
+        const int64_t items0 = warp_items(vd[0]);
+        const int64_t items1 = nvec > 1 ? warp_items(vd[1]) : 0;
+        const int64_t blocks = ceil_div(items0 + items1, 8);
         TK_CHECK_ARG(blocks < (1LL << 31), "quantise: too many rows");
         const dim3 block(32, 8);
         if (dt == TK_DTYPE_F16)
             quant_vec_kernel<__half><<<static_cast<unsigned>(blocks), block, 0, stream>>>(
-                vd[0], vd[1], rows0, rows0 + rows1);
+                vd[0], vd[1], items0, items0 + items1);
         else
             quant_vec_kernel<float><<<static_cast<unsigned>(blocks), block, 0, stream>>>(
-                vd[0], vd[1], rows0, rows0 + rows1);
+                vd[0], vd[1], items0, items0 + items1);
         return launch_status("quantise");
     }
     return TK_OK;
