@@ -43,8 +43,8 @@
 // persistent over 128-row query tiles):
 //   warp 0      TMA producer (4-stage ring);
 //   warp 1      TMEM owner and MMA issuer;
-//   warps 2..9  CUDA-core work: warp w owns TMEM lane quarter w % 4 (32
-//               query rows) and one half (32 keys) of each 64-key tile.
+//   warps 2..17 CUDA-core work: warp w owns TMEM lane quarter w % 4 (32
+//               query rows) and one quarter (16 keys) of each 64-key tile.
 // Every wait is bounded (error word + abort flag); no TMA multicast is used.
 #include <cuda.h>
 
@@ -63,8 +63,10 @@ constexpr int BM = 128;              // query rows per tile
 constexpr int BKEY = 64;             // keys per tile
 constexpr int EVT = 64;              // value columns per output tile
 constexpr int STAGES = 4;
-constexpr int NUM_SOFT_WARPS = 8;
+constexpr int NUM_SOFT_WARPS = 16;                  // four per TMEM lane quarter
 constexpr int NUM_THREADS = 64 + 32 * NUM_SOFT_WARPS;
+constexpr int SUBS = NUM_SOFT_WARPS / 4;             // warps sharing a lane quarter
+constexpr int CW = 64 / SUBS;                        // key (or value) columns per warp
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t COL_S = 0;        // S: HH, MID, LL at +0, +64, +128
 constexpr uint32_t COL_O = 256;      // O: HH, MID, LL at +256, +320, +384
@@ -85,8 +87,8 @@ struct StatsSmem {
     static constexpr int STAGE_BYTES = G * K_CHUNK;
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_STAGE = OFF_Q + G * Q_CHUNK;
-    static constexpr int OFF_RED = OFF_STAGE + STAGES * STAGE_BYTES;  // float[2][2][BM]
-    static constexpr int OFF_BAR = OFF_RED + 4 * BM * 4;
+    static constexpr int OFF_RED = OFF_STAGE + STAGES * STAGE_BYTES;  // float[2][SUBS][2][BM]
+    static constexpr int OFF_BAR = OFF_RED + 2 * SUBS * 2 * BM * 4;
     static constexpr int NUM_BARS = 2 * STAGES + 7;
     static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
     static constexpr int ALLOC = OFF_MISC + 16 + 1024;  // + slack for 1024-byte alignment
@@ -144,37 +146,37 @@ __device__ __forceinline__ float exp_fast(float x) {
     return y;
 }
 
-// 32 consecutive scores j0..j0+31 of query row i in the reference
+// N consecutive scores j0..j0+N-1 of query row i in the reference
 // composition: the exact limb dot product, T(acc * s_qk), T(. * scale), the
 // causal -1e4 and the additive mask, each rounded to T; padding keys
 // (j >= S) become -inf.  The conditions are uniform per call, so each step is
 // a branch-free loop over the 32 elements.
-template <int DT>
-__device__ __forceinline__ void scores32(const uint32_t (&hh)[32], const uint32_t (&mid)[32],
-                                         const uint32_t (&ll)[32], double sqk, const AttnParams& p,
-                                         int64_t i, int64_t j0, const void* mask_row, float (&s)[32]) {
+template <int DT, int N>
+__device__ __forceinline__ void scores_n(const uint32_t (&hh)[N], const uint32_t (&mid)[N],
+                                         const uint32_t (&ll)[N], double sqk, const AttnParams& p,
+                                         int64_t i, int64_t j0, const void* mask_row, float (&s)[N]) {
 #pragma unroll
-    for (int c = 0; c < 32; ++c)
+    for (int c = 0; c < N; ++c)
         s[c] = round_t_from_double(__dmul_rn(limb_acc_to_double(hh[c], mid[c], ll[c]), sqk), DT);
     if (p.scale != 1.0f) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) s[c] = round_t(__fmul_rn(s[c], p.scale), DT);
+        for (int c = 0; c < N; ++c) s[c] = round_t(__fmul_rn(s[c], p.scale), DT);
     }
-    if (p.causal && j0 + 31 > i) {
+    if (p.causal && j0 + N - 1 > i) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
+        for (int c = 0; c < N; ++c) {
             const float t = round_t(__fadd_rn(s[c], kMaskedValue), DT);
             s[c] = (j0 + c > i) ? t : s[c];
         }
     }
-    const bool full = j0 + 32 <= p.S;
+    const bool full = j0 + N <= p.S;
     if (mask_row != nullptr) {
-        float mv[32];
+        float mv[N];
         if (full && p.mask_vec) {
             if constexpr (DT == 0) {
                 const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __half*>(mask_row) + j0);
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
+                for (int k = 0; k < N / 8; ++k) {
                     const uint4 u = __ldg(src + k);
                     const __half2* h2 = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
@@ -187,34 +189,34 @@ __device__ __forceinline__ void scores32(const uint32_t (&hh)[32], const uint32_
             } else {
                 const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(mask_row) + j0);
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
+                for (int k = 0; k < N / 4; ++k) {
                     const float4 f = __ldg(src + k);
                     mv[4 * k] = f.x; mv[4 * k + 1] = f.y; mv[4 * k + 2] = f.z; mv[4 * k + 3] = f.w;
                 }
             }
         } else {
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
+            for (int c = 0; c < N; ++c) {
                 const int64_t j = j0 + c < p.S ? j0 + c : p.S - 1;  // clamped: padding keys are overwritten below
                 mv[c] = DT == 0 ? __half2float(__ldg(static_cast<const __half*>(mask_row) + j * p.ms[3]))
                                 : __ldg(static_cast<const float*>(mask_row) + j * p.ms[3]);
             }
         }
 #pragma unroll
-        for (int c = 0; c < 32; ++c) s[c] = round_t(__fadd_rn(s[c], mv[c]), DT);
+        for (int c = 0; c < N; ++c) s[c] = round_t(__fadd_rn(s[c], mv[c]), DT);
     }
     if (!full) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) s[c] = (j0 + c < p.S) ? s[c] : -INFINITY;
+        for (int c = 0; c < N; ++c) s[c] = (j0 + c < p.S) ? s[c] : -INFINITY;
     }
 }
 
-template <int DT>
-__device__ __forceinline__ void store_row32(void* base, const float (&v)[32]) {
+template <int DT, int N>
+__device__ __forceinline__ void store_row_n(void* base, const float (&v)[N]) {
     if constexpr (DT == 0) {
         uint4* dst = static_cast<uint4*>(base);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < N / 8; ++c) {
             uint32_t w[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -226,8 +228,15 @@ __device__ __forceinline__ void store_row32(void* base, const float (&v)[32]) {
     } else {
         float4* dst = static_cast<float4*>(base);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) dst[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+        for (int c = 0; c < N / 4; ++c) dst[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
     }
+}
+
+// N (16 or 32) consecutive TMEM columns of this warp's 32 lanes.
+template <int N>
+__device__ __forceinline__ void tmem_ld_cw(uint32_t taddr, uint32_t (&r)[N]) {
+    if constexpr (N == 16) tmem_ld_32x32b_x16(taddr, r);
+    else tmem_ld_32x32b_x32(taddr, r);
 }
 
 // ---- statistics kernel: scores, row max / sum, slice max probability ---------
@@ -247,7 +256,7 @@ attn_stats_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
     uint64_t* q_empty = q_full + 1;
     uint64_t* s_full = q_full + 2;
     uint64_t* s_empty = q_full + 3;
-    uint64_t* c_full = q_full + 4;   // [2] second-half partials published
+    uint64_t* c_full = q_full + 4;   // [2] partials of the other key quarters published
     uint64_t* drain_bar = q_full + 6;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -265,8 +274,8 @@ attn_stats_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
         mbar_init(smem_u32(q_empty), 1);
         mbar_init(smem_u32(s_full), 1);
         mbar_init(smem_u32(s_empty), NUM_SOFT_WARPS);
-        mbar_init(smem_u32(c_full), NUM_SOFT_WARPS / 2);
-        mbar_init(smem_u32(c_full + 1), NUM_SOFT_WARPS / 2);
+        mbar_init(smem_u32(c_full), NUM_SOFT_WARPS - 4);
+        mbar_init(smem_u32(c_full + 1), NUM_SOFT_WARPS - 4);
         mbar_init(smem_u32(drain_bar), 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -390,9 +399,9 @@ attn_stats_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
         volatile int no_abort = 0;
         mbar_wait_bounded(smem_u32(drain_bar), 0, &no_abort, p.err, kDevErrWaitDrain);
     } else {
-        // ---------------- scores and statistics (warps 2..9) ----------------
+        // ---------------- scores and statistics (warps 2..17) ----------------
         const int quarter = warp & 3;
-        const int half = (warp - 2) >> 2;
+        const int sub = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
         const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
         const int BH = p.B * p.H;
@@ -420,53 +429,59 @@ attn_stats_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
                 }
                 ++n_s;
                 tc_fence_after();
-                uint32_t hh[32], mid[32], ll[32];
-                const uint32_t col = COL_S + 32 * half;
-                tmem_ld_32x32b_x32(t_lane + col, hh);
-                tmem_ld_32x32b_x32(t_lane + col + 64, mid);
-                tmem_ld_32x32b_x32(t_lane + col + 128, ll);
+                uint32_t hh[CW], mid[CW], ll[CW];
+                const uint32_t col = COL_S + CW * sub;
+                tmem_ld_cw(t_lane + col, hh);
+                tmem_ld_cw(t_lane + col + 64, mid);
+                tmem_ld_cw(t_lane + col + 128, ll);
                 tc_wait_ld();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(s_empty));
-                const int64_t j0 = static_cast<int64_t>(t) * BKEY + 32 * half;
-                float s[32];
-                scores32<DT>(hh, mid, ll, sqk, p, i, j0, mask_row, s);
-                if (row_ok) store_row32<DT>(srow + j0 * ES, s);
+                const int64_t j0 = static_cast<int64_t>(t) * BKEY + CW * sub;
+                float s[CW];
+                scores_n<DT, CW>(hh, mid, ll, sqk, p, i, j0, mask_row, s);
+                if (row_ok) store_row_n<DT, CW>(srow + j0 * ES, s);
                 float tmax = -INFINITY;
 #pragma unroll
-                for (int c = 0; c < 32; ++c) tmax = fmaxf(tmax, s[c]);
+                for (int c = 0; c < CW; ++c) tmax = fmaxf(tmax, s[c]);
                 const float m_new = fmaxf(m_run, tmax);
                 if (m_new != -INFINITY) {
                     if (m_run != -INFINITY && m_new != m_run) l_run *= exp_fast(m_run - m_new);
                     m_run = m_new;
                     float acc = 0.0f;
 #pragma unroll
-                    for (int c = 0; c < 32; ++c) acc += exp_fast(s[c] - m_run);
+                    for (int c = 0; c < CW; ++c) acc += exp_fast(s[c] - m_run);
                     l_run += acc;
                 }
             }
             if (!ok) break;
-            // Combine the two key halves of each row.  The second-half warps
-            // publish their partials in buffer lt & 1, rewritten two work
-            // items later -- by then the first-half warps have read it (they
-            // release the next item's first S tile only after this combine).
+            // Combine the key quarters of each row.  The warps of quarters
+            // 1..SUBS-1 publish their partials in buffer lt & 1, rewritten two
+            // work items later -- by then the quarter-0 warps have read it
+            // (they release the next item's first S tile only after this
+            // combine).
             const int rb = lt & 1;
-            float* rm = red + rb * 2 * BM;
-            if (half == 1) {
-                rm[row] = m_run;
-                rm[BM + row] = l_run;
+            float* rm = red + rb * SUBS * 2 * BM;
+            if (sub > 0) {
+                rm[(sub * 2) * BM + row] = m_run;
+                rm[(sub * 2 + 1) * BM + row] = l_run;
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(c_full + rb));
             } else {
                 if (!mbar_wait_bounded(smem_u32(c_full + rb), (static_cast<uint32_t>(lt) >> 1) & 1u,
                                        abort_flag, p.err, kDevErrWaitFull))
                     break;
-                const float m1 = rm[row], l1 = rm[BM + row];
-                const float m = fmaxf(m_run, m1);
+                float m = m_run;
+#pragma unroll
+                for (int q = 1; q < SUBS; ++q) m = fmaxf(m, rm[(q * 2) * BM + row]);
                 float l = 0.0f;
                 if (m_run != -INFINITY) l += l_run * exp_fast(m_run - m);
-                if (m1 != -INFINITY) l += l1 * exp_fast(m1 - m);
+#pragma unroll
+                for (int q = 1; q < SUBS; ++q) {
+                    const float mq = rm[(q * 2) * BM + row], lq = rm[(q * 2 + 1) * BM + row];
+                    if (mq != -INFINITY) l += lq * exp_fast(mq - m);
+                }
                 const float inv = 1.0f / l;
                 unsigned bits = 0;
                 if (row_ok) {
@@ -626,9 +641,9 @@ attn_out_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__
         volatile int no_abort = 0;
         mbar_wait_bounded(smem_u32(drain_bar), 0, &no_abort, p.err, kDevErrWaitDrain);
     } else {
-        // ---------------- probabilities and output epilogue (warps 2..9) ----------------
+        // ---------------- probabilities and output epilogue (warps 2..17) ----------------
         const int quarter = warp & 3;
-        const int half = (warp - 2) >> 2;
+        const int sub = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
         const int sw = row & 7;
         const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -658,13 +673,13 @@ attn_out_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__
                     break;
                 }
                 const uint8_t* sb = smem + L::OFF_STAGE + stage * L::STAGE_BYTES;
-                float s[32];
+                float s[CW];
                 if constexpr (DT == 0) {
                     // the row's 128-byte line, 16-byte chunks swizzled by row & 7
                     const uint8_t* line = sb + row * 128;
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const uint4 u = *reinterpret_cast<const uint4*>(line + (((4 * half + k) ^ sw) << 4));
+                    for (int k = 0; k < CW / 8; ++k) {
+                        const uint4 u = *reinterpret_cast<const uint4*>(line + ((((CW / 8) * sub + k) ^ sw) << 4));
                         const __half2* h2 = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
@@ -674,10 +689,13 @@ attn_out_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__
                         }
                     }
                 } else {
-                    const uint8_t* line = sb + half * (L::S_BYTES / 2) + row * 128;
+                    // keys 32h..32h+31 are box h; within its 128-byte line,
+                    // key 32h + c is float c
+                    const int kb = CW * sub;
+                    const uint8_t* line = sb + (kb / 32) * (L::S_BYTES / 2) + row * 128;
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const float4 f = *reinterpret_cast<const float4*>(line + ((k ^ sw) << 4));
+                    for (int k = 0; k < CW / 4; ++k) {
+                        const float4 f = *reinterpret_cast<const float4*>(line + ((((kb % 32) / 4 + k) ^ sw) << 4));
                         s[4 * k] = f.x;
                         s[4 * k + 1] = f.y;
                         s[4 * k + 2] = f.z;
@@ -687,9 +705,9 @@ attn_out_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__
                 // P = T(exp(s - m) / l), quantised with the slice scale: the
                 // probabilities are >= 0, so q is in [0, 32767] and the hi
                 // limb in [0, 127].
-                uint32_t hw[8], lw[8];
+                uint32_t hw[CW / 4], lw[CW / 4];
 #pragma unroll
-                for (int w = 0; w < 8; ++w) {
+                for (int w = 0; w < CW / 4; ++w) {
                     uint32_t hv = 0, lv = 0;
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
@@ -709,8 +727,8 @@ attn_out_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__
                 }
                 uint8_t* prow = smem + L::OFF_P + buf * P_TILE + row * 128;
 #pragma unroll
-                for (int k = 0; k < 2; ++k) {
-                    const int ch = 2 * half + k;  // 16-key chunk of the hi part
+                for (int k = 0; k < CW / 16; ++k) {
+                    const int ch = (CW / 16) * sub + k;  // 16-key chunk of the hi part
                     *reinterpret_cast<uint4*>(prow + ((ch ^ sw) << 4)) =
                         make_uint4(hw[4 * k], hw[4 * k + 1], hw[4 * k + 2], hw[4 * k + 3]);
                     *reinterpret_cast<uint4*>(prow + (((ch + 4) ^ sw) << 4)) =
@@ -727,28 +745,28 @@ attn_out_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__
                                    kDevErrWaitAccFull))
                 break;
             tc_fence_after();
-            uint32_t hh[32], mid[32], ll[32];
-            const uint32_t col = COL_O + 32 * half;
-            tmem_ld_32x32b_x32(t_lane + col, hh);
-            tmem_ld_32x32b_x32(t_lane + col + 64, mid);
-            tmem_ld_32x32b_x32(t_lane + col + 128, ll);
+            uint32_t hh[CW], mid[CW], ll[CW];
+            const uint32_t col = COL_O + CW * sub;
+            tmem_ld_cw(t_lane + col, hh);
+            tmem_ld_cw(t_lane + col + 64, mid);
+            tmem_ld_cw(t_lane + col + 128, ll);
             tc_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(o_empty));
             if (row_ok) {
                 const double spv = dequant_scale(__uint_as_float(p.amax_p[bh]), __ldg(p.amax + 2 * BH + bh));
-                const int64_t e0 = static_cast<int64_t>(evh) * EVT + 32 * half;
+                const int64_t e0 = static_cast<int64_t>(evh) * EVT + CW * sub;
                 const int64_t obase = b * p.os[0] + h * p.os[1] + i * p.os[2];
-                float o[32];
+                float o[CW];
 #pragma unroll
-                for (int c = 0; c < 32; ++c)
+                for (int c = 0; c < CW; ++c)
                     o[c] = round_t_from_double(__dmul_rn(limb_acc_to_double(hh[c], mid[c], ll[c]), spv), DT);
-                if (p.out_vec && e0 + 32 <= p.Ev) {
-                    store_row32<DT>(static_cast<char*>(p.out) + (obase + e0) * (DT == 0 ? 2 : 4), o);
+                if (p.out_vec && e0 + CW <= p.Ev) {
+                    store_row_n<DT, CW>(static_cast<char*>(p.out) + (obase + e0) * (DT == 0 ? 2 : 4), o);
                 } else {
 #pragma unroll
-                    for (int c = 0; c < 32; ++c)
+                    for (int c = 0; c < CW; ++c)
                         if (e0 + c < p.Ev) store_t(p.out, DT, obase + (e0 + c) * p.os[3], o[c]);
                 }
             }
@@ -1123,9 +1141,9 @@ int tk_sdpa_q16(const tk_sdpa_desc_t* desc, void* workspace, size_t workspace_by
         p.os[a] = d.out_strides[a];
         p.ms[a] = d.mask_strides[a];
     }
-    p.out_vec = vec_ok(d.out, d.out_strides, 32, es) ? 1 : 0;
+    p.out_vec = vec_ok(d.out, d.out_strides, CW, es) ? 1 : 0;
     p.mask = d.mask;
-    p.mask_vec = d.mask != nullptr && vec_ok(d.mask, d.mask_strides, 32, es) ? 1 : 0;
+    p.mask_vec = d.mask != nullptr && vec_ok(d.mask, d.mask_strides, CW, es) ? 1 : 0;
     p.causal = d.causal ? 1 : 0;
     p.scale = d.scale;
     p.err = device_error_word(dev);

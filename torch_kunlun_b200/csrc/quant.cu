@@ -510,7 +510,9 @@ int quantise_operands(tk_dtype_t dt, const QuantOperand* ops, int nops, cudaStre
         }
         const int64_t per_block = static_cast<int64_t>(kAmaxThreads) * 64;
         int64_t chunks = ceil_div(d.slice_len, per_block);
-        const int64_t want = std::max<int64_t>(1, (8LL * sm_count(dev)) / d.nslices);
+        // two blocks per SM per operand: fat blocks keep many loads in flight
+        // and few atomics land on the shared maximum
+        const int64_t want = std::max<int64_t>(1, (2LL * sm_count(dev)) / d.nslices);
         chunks = std::max<int64_t>(1, std::min(chunks, want));
         d.chunk = (ceil_div(d.slice_len, chunks) + 7) / 8 * 8;
         d.chunks = ceil_div(d.slice_len, d.chunk);
