@@ -127,6 +127,7 @@ struct AttnParams {
     int64_t ms[4];
     int causal;
     float scale;
+    int scale_h;             // scale is exactly a binary16 number
     unsigned* err;
 };
 
@@ -208,6 +209,74 @@ __device__ __forceinline__ void scores_n(const uint32_t (&hh)[N], const uint32_t
     if (!full) {
 #pragma unroll
         for (int c = 0; c < N; ++c) s[c] = (j0 + c < p.S) ? s[c] : -INFINITY;
+    }
+}
+
+// The binary16 form of scores_n: after the one binary64 -> binary16
+// rounding every step is a packed binary16 operation.  A binary16 product or
+// sum of two binary16 values rounded once equals the binary32 operation
+// rounded to binary16 (products are exact in binary32; for sums binary32
+// carries more than 2*11 + 2 significand bits), so the scale (when it is a
+// binary16 number), the causal -1e4 and the mask need no conversions.
+template <int N>
+__device__ __forceinline__ void scores_h(const uint32_t (&hh)[N], const uint32_t (&mid)[N],
+                                         const uint32_t (&ll)[N], double sqk, const AttnParams& p,
+                                         int64_t i, int64_t j0, const void* mask_row, __half2 (&sh)[N / 2]) {
+#pragma unroll
+    for (int j = 0; j < N / 2; ++j)
+        sh[j] = __halves2half2(
+            __double2half(__dmul_rn(limb_acc_to_double(hh[2 * j], mid[2 * j], ll[2 * j]), sqk)),
+            __double2half(__dmul_rn(limb_acc_to_double(hh[2 * j + 1], mid[2 * j + 1], ll[2 * j + 1]), sqk)));
+    if (p.scale != 1.0f) {
+        if (p.scale_h) {
+            const __half2 sc = __float2half2_rn(p.scale);
+#pragma unroll
+            for (int j = 0; j < N / 2; ++j) sh[j] = __hmul2(sh[j], sc);
+        } else {
+#pragma unroll
+            for (int j = 0; j < N / 2; ++j) {
+                const float2 f = __half22float2(sh[j]);
+                sh[j] = __floats2half2_rn(__fmul_rn(f.x, p.scale), __fmul_rn(f.y, p.scale));
+            }
+        }
+    }
+    if (p.causal && j0 + N - 1 > i) {
+        const __half2 neg = __float2half2_rn(kMaskedValue);
+#pragma unroll
+        for (int j = 0; j < N / 2; ++j) {
+            const __half2 t = __hadd2(sh[j], neg);
+            sh[j] = __halves2half2(j0 + 2 * j > i ? __low2half(t) : __low2half(sh[j]),
+                                   j0 + 2 * j + 1 > i ? __high2half(t) : __high2half(sh[j]));
+        }
+    }
+    const bool full = j0 + N <= p.S;
+    if (mask_row != nullptr) {
+        if (full && p.mask_vec) {
+            const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __half*>(mask_row) + j0);
+#pragma unroll
+            for (int k = 0; k < N / 8; ++k) {
+                const uint4 u = __ldg(src + k);
+                const __half2* m2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) sh[4 * k + e] = __hadd2(sh[4 * k + e], m2[e]);
+            }
+        } else {
+            const __half* mh = static_cast<const __half*>(mask_row);
+#pragma unroll
+            for (int j = 0; j < N / 2; ++j) {
+                // clamped: padding keys are overwritten below
+                const int64_t ja = j0 + 2 * j < p.S ? j0 + 2 * j : p.S - 1;
+                const int64_t jb = j0 + 2 * j + 1 < p.S ? j0 + 2 * j + 1 : p.S - 1;
+                sh[j] = __hadd2(sh[j], __halves2half2(__ldg(mh + ja * p.ms[3]), __ldg(mh + jb * p.ms[3])));
+            }
+        }
+    }
+    if (!full) {
+        const __half ninf = __ushort_as_half(0xFC00);
+#pragma unroll
+        for (int j = 0; j < N / 2; ++j)
+            sh[j] = __halves2half2(j0 + 2 * j < p.S ? __low2half(sh[j]) : ninf,
+                                   j0 + 2 * j + 1 < p.S ? __high2half(sh[j]) : ninf);
     }
 }
 
@@ -440,8 +509,25 @@ attn_stats_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
                 if (lane == 0) mbar_arrive(smem_u32(s_empty));
                 const int64_t j0 = static_cast<int64_t>(t) * BKEY + CW * sub;
                 float s[CW];
-                scores_n<DT, CW>(hh, mid, ll, sqk, p, i, j0, mask_row, s);
-                if (row_ok) store_row_n<DT, CW>(srow + j0 * ES, s);
+                if constexpr (DT == 0) {
+                    __half2 sh[CW / 2];
+                    scores_h<CW>(hh, mid, ll, sqk, p, i, j0, mask_row, sh);
+                    if (row_ok) {
+                        uint4* dst = reinterpret_cast<uint4*>(srow + j0 * ES);
+                        const uint4* src = reinterpret_cast<const uint4*>(sh);
+#pragma unroll
+                        for (int k = 0; k < CW / 8; ++k) dst[k] = src[k];
+                    }
+#pragma unroll
+                    for (int j = 0; j < CW / 2; ++j) {
+                        const float2 f = __half22float2(sh[j]);
+                        s[2 * j] = f.x;
+                        s[2 * j + 1] = f.y;
+                    }
+                } else {
+                    scores_n<DT, CW>(hh, mid, ll, sqk, p, i, j0, mask_row, s);
+                    if (row_ok) store_row_n<DT, CW>(srow + j0 * ES, s);
+                }
                 float tmax = -INFINITY;
 #pragma unroll
                 for (int c = 0; c < CW; ++c) tmax = fmaxf(tmax, s[c]);
@@ -1146,6 +1232,7 @@ int tk_sdpa_q16(const tk_sdpa_desc_t* desc, void* workspace, size_t workspace_by
     p.mask_vec = d.mask != nullptr && vec_ok(d.mask, d.mask_strides, CW, es) ? 1 : 0;
     p.causal = d.causal ? 1 : 0;
     p.scale = d.scale;
+    p.scale_h = __half2float(__float2half_rn(d.scale)) == d.scale ? 1 : 0;
     p.err = device_error_word(dev);
     const int ev_tiles = static_cast<int>(ceil_div(d.ev, EVT));
     TK_CHECK_ARG(l.BH * p.m_tiles * ev_tiles < (1LL << 31), "tk_sdpa_q16: too many tiles");
