@@ -194,6 +194,14 @@ TK_API size_t tk_conv2d_workspace_size(const tk_conv2d_desc_t* desc);
 TK_API int tk_conv2d_q16(const tk_conv2d_desc_t* desc, void* workspace, size_t workspace_bytes,
                          void* stream);
 
+/* ---- reduction ---------------------------------------------------------------
+ * out[o][i] = sum_r x[o][r][i] over a contiguous [outer, red, inner] tensor,
+ * accumulated in fp32 in a fixed order (deterministic) and rounded once to
+ * out_dtype (fp16 input may produce fp32 output).  Replaces xdnn::reduce_sum
+ * of the bias gradients (csrc/autograd.cpp:407-412) and of sum over dims. */
+TK_API int tk_reduce_sum(tk_dtype_t in_dtype, tk_dtype_t out_dtype, const void* x, int64_t outer,
+                         int64_t red, int64_t inner, void* out, void* stream);
+
 /* ---- fused scaled-dot-product attention -------------------------------------
  * out = softmax(T(T(T(q k^T) * scale) + mask)) v over [batch, heads] slices,
  * with the reference's composition semantics
@@ -263,7 +271,13 @@ TK_API int tk_copy_strided(void* dst, int dst_type, const void* src, int src_typ
 TK_API int tk_fill_strided(void* dst, int type, double value, int64_t ivalue, int ndim,
                            const int64_t* sizes, const int64_t* strides, void* stream);
 
-typedef enum { TK_BIN_ADD = 0, TK_BIN_SUB = 1, TK_BIN_MUL = 2, TK_BIN_DIV = 3 } tk_binop_t;
+typedef enum {
+    TK_BIN_ADD = 0,
+    TK_BIN_SUB = 1,
+    TK_BIN_MUL = 2,
+    TK_BIN_DIV = 3,
+    TK_BIN_THRESHOLD_BACKWARD = 4 /* out = b > alpha ? a : 0 (relu_grad, csrc/autograd.cpp:320-335) */
+} tk_binop_t;
 
 /* out[i] = a[i] op (alpha * b[i]) (alpha applies to add/sub) computed in fp32
  * and rounded once, over a broadcast index space (strides 0 broadcast); out

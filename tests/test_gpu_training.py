@@ -1,0 +1,111 @@
+"""Backward through the quantised dense ops (the next row of the hot path):
+torch's autograd formulas for mm / addmm / linear / bmm run their gradient
+products on the same int16-quantised GEMM, so the input and weight gradients
+are bit-exact against the oracle's quantised product of the same operands;
+the bias gradient is a deterministic fp32 sum.  Plus the reference's own
+training test (tests/test_training.py:17-39: MLP + ReLU + MSE + SGD, loss
+must decrease) and the ops it needs (threshold_backward, sum, mse_loss)."""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+torch_kunlun = pytest.importorskip("torch_kunlun")
+kunlun = torch_kunlun.kunlun
+from oracle import oracle as O  # noqa: E402
+from tests._qgemm_helpers import assert_bits_equal  # noqa: E402
+
+DEV = "kunlun"
+
+
+def rnd(shape, seed, scale=1.0, dtype=torch.float16):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(shape, generator=g) * scale).to(dtype)
+
+
+def test_linear_backward_uses_the_quantised_gemm():
+    x, w, b = rnd((96, 64), 1), rnd((48, 64), 2, 0.05), rnd((48,), 3, 0.05)
+    gy = rnd((96, 48), 4)
+    xd = x.to(DEV).requires_grad_()
+    wd = w.to(DEV).requires_grad_()
+    bd = b.to(DEV).requires_grad_()
+    y = F.linear(xd, wd, bd)
+    y.backward(gy.to(DEV))
+    # dX = dY @ W and dW = dY^T @ X, each one quantised product (per-tensor scales)
+    assert_bits_equal(xd.grad.cpu().numpy(), O.mm(gy.numpy(), w.numpy()), "grad_input")
+    assert_bits_equal(wd.grad.cpu().numpy(),
+                      O.mm(np.ascontiguousarray(gy.numpy().T), x.numpy()), "grad_weight")
+    want_b = gy.double().sum(0)
+    assert torch.allclose(bd.grad.cpu().double(), want_b, atol=2e-2, rtol=2e-3)
+
+
+def test_mm_and_bmm_backward():
+    a, b = rnd((40, 72), 5), rnd((72, 24), 6, 0.1)
+    ad, bd = a.to(DEV).requires_grad_(), b.to(DEV).requires_grad_()
+    g = rnd((40, 24), 7)
+    (ad @ bd).backward(g.to(DEV))
+    assert_bits_equal(ad.grad.cpu().numpy(), O.mm(g.numpy(), np.ascontiguousarray(b.numpy().T)), "mm dA")
+    assert_bits_equal(bd.grad.cpu().numpy(), O.mm(np.ascontiguousarray(a.numpy().T), g.numpy()), "mm dB")
+    A, B = rnd((3, 16, 32), 8), rnd((3, 32, 8), 9, 0.2)
+    Ad, Bd = A.to(DEV).requires_grad_(), B.to(DEV).requires_grad_()
+    G = rnd((3, 16, 8), 10)
+    torch.bmm(Ad, Bd).backward(G.to(DEV))
+    want = O.bmm(G.numpy(), np.ascontiguousarray(np.swapaxes(B.numpy(), 1, 2)))
+    assert_bits_equal(Ad.grad.cpu().numpy(), want, "bmm dA")
+
+
+@pytest.mark.parametrize("dims,keepdim", [((0,), False), ((1,), True), ((0, 2), False), (None, False),
+                                          ((-1,), False), ((1, 2), True)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_sum_over_dims(dims, keepdim, dtype):
+    x = rnd((5, 7, 33), 11, dtype=dtype)
+    xd = x.to(DEV)
+    got = (xd.sum() if dims is None else xd.sum(dim=dims, keepdim=keepdim)).cpu()
+    want = x.double().sum() if dims is None else x.double().sum(dim=dims, keepdim=keepdim)
+    assert got.shape == want.shape and got.dtype == dtype
+    tol = 5e-3 if dtype == torch.float16 else 1e-5
+    assert torch.allclose(got.double(), want, atol=tol * 10, rtol=tol)
+    f32 = xd.sum(dim=0, dtype=torch.float32).cpu() if dtype == torch.float16 else None
+    if f32 is not None:
+        assert f32.dtype == torch.float32
+        assert torch.allclose(f32.double(), x.double().sum(0), atol=1e-4, rtol=1e-5)
+
+
+def test_relu_and_mse_backward():
+    x, t = rnd((32, 16), 12), rnd((32, 16), 13)
+    xd = x.to(DEV).requires_grad_()
+    loss = F.mse_loss(torch.relu(xd), t.to(DEV))
+    loss.backward()
+    xr = x.float().requires_grad_()
+    lr = F.mse_loss(torch.relu(xr), t.float())
+    lr.backward()
+    assert abs(loss.cpu().item() - lr.item()) < 2e-3 * max(1.0, lr.item())
+    assert torch.allclose(xd.grad.cpu().float(), xr.grad, atol=1e-4, rtol=1e-2)
+    for red in ("sum", "none"):
+        got = F.mse_loss(xd.detach(), t.to(DEV), reduction=red).cpu().float()
+        want = F.mse_loss(x.float(), t.float(), reduction=red)
+        assert torch.allclose(got, want, atol=5e-2, rtol=3e-3)
+
+
+def test_mlp_mse_sgd_training():
+    """The reference's tests/test_training.py:17-39 on the kunlun device."""
+    torch.manual_seed(0)
+    model = torch.nn.Sequential(
+        torch.nn.Linear(8, 16),
+        torch.nn.ReLU(),
+        torch.nn.Linear(16, 1),
+    ).half().to(DEV)
+    opt = torch.optim.SGD(model.parameters(), lr=0.05, foreach=False)
+    loss_fn = torch.nn.MSELoss()
+    x = torch.randn(32, 8, dtype=torch.float16).to(DEV)
+    target = torch.randn(32, 1, dtype=torch.float16).to(DEV)
+    losses = []
+    for _ in range(20):
+        opt.zero_grad()
+        loss = loss_fn(model(x), target)
+        loss.backward()
+        opt.step()
+        losses.append(float(loss.detach().cpu().item()))
+    assert losses[-1] < losses[0], f"loss did not decrease: {losses[0]} -> {losses[-1]}"

@@ -10,6 +10,8 @@
 // output type, as in the reference's XDNN elementwise calls.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "tk_internal.h"
 
 namespace tk {
@@ -172,6 +174,7 @@ __device__ __forceinline__ float bin_apply(int op, float a, float b, float alpha
         case TK_BIN_ADD: return alpha == 1.0f ? __fadd_rn(a, b) : __fadd_rn(a, __fmul_rn(alpha, b));
         case TK_BIN_SUB: return alpha == 1.0f ? __fsub_rn(a, b) : __fsub_rn(a, __fmul_rn(alpha, b));
         case TK_BIN_MUL: return __fmul_rn(a, b);
+        case TK_BIN_THRESHOLD_BACKWARD: return b > alpha ? a : 0.0f;
         default: return __fdiv_rn(a, b);
     }
 }
@@ -263,6 +266,74 @@ bool is_dense(int ndim, const int64_t* sizes, const int64_t* strides) {
         expect *= sizes[i];
     }
     return true;
+}
+
+// ---- sum over the middle dim of [outer, red, inner] --------------------------
+
+template <typename TI, typename TO>
+__device__ __forceinline__ void store_sum(TO* p, int64_t i, float v);
+template <> __device__ __forceinline__ void store_sum<__half, __half>(__half* p, int64_t i, float v) { p[i] = __float2half_rn(v); }
+template <> __device__ __forceinline__ void store_sum<__half, float>(float* p, int64_t i, float v) { p[i] = v; }
+template <> __device__ __forceinline__ void store_sum<float, float>(float* p, int64_t i, float v) { p[i] = v; }
+
+// inner > 1: a 32 x 8 block covers 32 consecutive inner columns of one outer
+// index; thread row ty sums red indices ty, ty + 8, ... (coalesced along the
+// columns), then the 8 partials are added in a fixed order.
+template <typename TI, typename TO>
+__global__ void reduce_cols_kernel(const TI* __restrict__ x, TO* __restrict__ out, int64_t red,
+                                   int64_t inner) {
+    __shared__ float part[8][33];
+    const int64_t o = blockIdx.y;
+    const int64_t col = static_cast<int64_t>(blockIdx.x) * 32 + threadIdx.x;
+    float acc = 0.0f;
+    if (col < inner) {
+        const TI* xp = x + o * red * inner + col;
+        for (int64_t r = threadIdx.y; r < red; r += 8) acc += ld<TI>(xp, r * inner);
+    }
+    part[threadIdx.y][threadIdx.x] = acc;
+    __syncthreads();
+    if (threadIdx.y == 0 && col < inner) {
+        float s = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s += part[k][threadIdx.x];
+        store_sum<TI, TO>(out, o * inner + col, s);
+    }
+}
+
+// inner == 1: one warp per row, lane-strided partials, shuffle tree.
+template <typename TI, typename TO>
+__global__ void reduce_rows_kernel(const TI* __restrict__ x, TO* __restrict__ out, int64_t rows,
+                                   int64_t red) {
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + threadIdx.y;
+    if (row >= rows) return;
+    const TI* xp = x + row * red;
+    float acc = 0.0f;
+    for (int64_t r = threadIdx.x; r < red; r += 32) acc += ld<TI>(xp, r);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (threadIdx.x == 0) store_sum<TI, TO>(out, row, acc);
+}
+
+template <typename TI, typename TO>
+int reduce_launch(const void* x, int64_t outer, int64_t red, int64_t inner, void* out,
+                  cudaStream_t stream) {
+    const dim3 block(32, 8);
+    if (inner == 1) {
+        const int64_t blocks = ceil_div(outer, 8);
+        TK_CHECK_ARG(blocks < (1LL << 31), "tk_reduce_sum: too many rows");
+        reduce_rows_kernel<TI, TO><<<static_cast<unsigned>(blocks), block, 0, stream>>>(
+            static_cast<const TI*>(x), static_cast<TO*>(out), outer, red);
+    } else {
+        TK_CHECK_ARG(ceil_div(inner, 32) < (1LL << 31), "tk_reduce_sum: inner extent too large");
+        for (int64_t o0 = 0; o0 < outer; o0 += 65535) {  // grid.y is limited to 65535
+            const int64_t no = std::min<int64_t>(65535, outer - o0);
+            const dim3 grid(static_cast<unsigned>(ceil_div(inner, 32)), static_cast<unsigned>(no));
+            reduce_cols_kernel<TI, TO><<<grid, block, 0, stream>>>(
+                static_cast<const TI*>(x) + o0 * red * inner, static_cast<TO*>(out) + o0 * inner, red,
+                inner);
+        }
+    }
+    return launch_status("reduce_sum");
 }
 
 // Merge adjacent dims that are contiguous in both operands, drop size-1 dims.
@@ -417,7 +488,7 @@ int tk_binary(int op, tk_dtype_t dt, const void* a, const int64_t* a_strides, co
               void* stream_) {
     using namespace tk;
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-    TK_CHECK_ARG(op >= TK_BIN_ADD && op <= TK_BIN_DIV, "tk_binary: bad op %d", op);
+    TK_CHECK_ARG(op >= TK_BIN_ADD && op <= TK_BIN_THRESHOLD_BACKWARD, "tk_binary: bad op %d", op);
     TK_CHECK_ARG(dt == TK_DTYPE_F16 || dt == TK_DTYPE_F32, "tk_binary: bad dtype");
     Strided d;
     int64_t n = 0;
@@ -447,6 +518,22 @@ int tk_binary(int op, tk_dtype_t dt, const void* a, const int64_t* a_strides, co
                 static_cast<float*>(out), n, alpha, d);
     }
     return launch_status("binary");
+}
+
+int tk_reduce_sum(tk_dtype_t in_dtype, tk_dtype_t out_dtype, const void* x, int64_t outer,
+                  int64_t red, int64_t inner, void* out, void* stream_) {
+    using namespace tk;
+    TK_CHECK_ARG(outer >= 0 && red >= 0 && inner >= 0, "tk_reduce_sum: negative size");
+    if (outer == 0 || inner == 0) return TK_OK;
+    TK_CHECK_ARG(x && out, "tk_reduce_sum: NULL pointer");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    if (in_dtype == TK_DTYPE_F16 && out_dtype == TK_DTYPE_F16)
+        return reduce_launch<__half, __half>(x, outer, red, inner, out, stream);
+    if (in_dtype == TK_DTYPE_F16 && out_dtype == TK_DTYPE_F32)
+        return reduce_launch<__half, float>(x, outer, red, inner, out, stream);
+    if (in_dtype == TK_DTYPE_F32 && out_dtype == TK_DTYPE_F32)
+        return reduce_launch<float, float>(x, outer, red, inner, out, stream);
+    TK_FAIL(TK_ERR_UNSUPPORTED, "tk_reduce_sum: unsupported dtype combination");
 }
 
 int tk_unary(int op, tk_dtype_t dt, const void* x, void* y, int64_t n, float p0, float p1,

@@ -8,6 +8,7 @@
 // attention composition of torch_kunlun/kunlun/attention.py:36-107.
 #include <torch/library.h>
 
+#include <algorithm>
 #include <cmath>
 
 #include "kunlun.h"
@@ -183,6 +184,96 @@ at::Tensor& mul_(at::Tensor& self, const at::Tensor& other) {
     return self;
 }
 
+// ---- backward support: relu gradient, sums, MSE loss --------------------------
+
+// relu's backward (torch's threshold_backward): grad where self > threshold.
+at::Tensor threshold_backward(const at::Tensor& grad_output, const at::Tensor& self,
+                              const at::Scalar& threshold) {
+    return binary(grad_output, self, TK_BIN_THRESHOLD_BACKWARD, threshold.toDouble());
+}
+
+// Sum over `dims` (all when empty) in fp32 with one rounding to the output
+// dtype (fp16 input may sum into fp32).  Reduced dims that form one block of
+// the shape are summed in place; otherwise they are moved last first.
+at::Tensor sum_dim(const at::Tensor& self, at::OptionalIntArrayRef dim, bool keepdim,
+                   std::optional<at::ScalarType> dtype) {
+    const at::ScalarType in_t = self.scalar_type();
+    const at::ScalarType out_t = dtype.value_or(in_t);
+    TORCH_CHECK((in_t == at::kHalf && (out_t == at::kHalf || out_t == at::kFloat)) ||
+                    (in_t == at::kFloat && out_t == at::kFloat),
+                "kunlun sum supports float16 -> float16/float32 and float32 -> float32, got ", in_t,
+                " -> ", out_t);
+    const int64_t nd = self.dim();
+    std::vector<bool> red(std::max<int64_t>(nd, 1), false);
+    if (!dim.has_value() || dim->empty()) {
+        std::fill(red.begin(), red.end(), true);
+    } else {
+        for (int64_t d : *dim) red[c10::maybe_wrap_dim(d, std::max<int64_t>(nd, 1))] = true;
+    }
+    std::vector<int64_t> out_shape, kept_dims, red_dims;
+    for (int64_t d = 0; d < nd; ++d) {
+        if (red[d]) {
+            red_dims.push_back(d);
+            if (keepdim) out_shape.push_back(1);
+        } else {
+            kept_dims.push_back(d);
+            out_shape.push_back(self.size(d));
+        }
+    }
+    at::Tensor out = at::empty(out_shape, self.options().dtype(out_t));
+    if (out.numel() == 0) return out;
+    at::Tensor x;
+    int64_t outer = 1, rcount = 1, inner = 1;
+    const bool block = red_dims.empty() || red_dims.back() - red_dims.front() + 1 ==
+                                               static_cast<int64_t>(red_dims.size());
+    if (nd == 0) {
+        x = self.reshape({1});
+    } else if (block) {
+        x = self.contiguous();
+        const int64_t lo = red_dims.empty() ? nd : red_dims.front();
+        const int64_t hi = red_dims.empty() ? nd - 1 : red_dims.back();
+        for (int64_t d = 0; d < lo; ++d) outer *= self.size(d);
+        for (int64_t d = lo; d <= hi; ++d) rcount *= self.size(d);
+        for (int64_t d = hi + 1; d < nd; ++d) inner *= self.size(d);
+    } else {
+        std::vector<int64_t> perm(kept_dims);
+        perm.insert(perm.end(), red_dims.begin(), red_dims.end());
+        x = self.permute(perm).contiguous();
+        for (int64_t d : kept_dims) outer *= self.size(d);
+        for (int64_t d : red_dims) rcount *= self.size(d);
+    }
+    if (rcount == 0) return out.zero_();
+    const int dev = self.device().index();
+    DeviceScope g(dev);
+    check_tk(tk_reduce_sum(tk_dtype(in_t), tk_dtype(out_t), x.data_ptr(), outer, rcount, inner,
+                           out.data_ptr(), current_stream(dev)),
+             "tk_reduce_sum");
+    return out;
+}
+
+at::Tensor sum_all(const at::Tensor& self, std::optional<at::ScalarType> dtype) {
+    return sum_dim(self, std::nullopt, false, dtype);
+}
+
+// MSE loss with the reference's reduction codes (0 none, 1 mean, 2 sum): the
+// difference and its square rounded to T, the reduction summed in fp32.
+at::Tensor mse_loss(const at::Tensor& self, const at::Tensor& target, int64_t reduction) {
+    at::Tensor d = binary(self, target, TK_BIN_SUB, 1.0);
+    at::Tensor sq = binary(d, d, TK_BIN_MUL, 1.0);
+    if (reduction == 0) return sq;
+    at::Tensor s = sum_dim(sq, std::nullopt, false, at::kFloat);
+    if (reduction == 1) s = unary(s, TK_UN_SCALE, static_cast<float>(1.0 / std::max<int64_t>(1, sq.numel())), 0.f);
+    return s.to(self.scalar_type());
+}
+
+at::Tensor mse_loss_backward(const at::Tensor& grad_output, const at::Tensor& self,
+                             const at::Tensor& target, int64_t reduction) {
+    const double norm = reduction == 1 ? 2.0 / std::max<int64_t>(1, self.numel()) : 2.0;
+    at::Tensor d = binary(self, target, TK_BIN_SUB, 1.0);
+    at::Tensor g = binary(d, grad_output, TK_BIN_MUL, 1.0);
+    return unary(g, TK_UN_SCALE, static_cast<float>(norm), 0.f);
+}
+
 }  // namespace
 
 at::Tensor silu_mul(const at::Tensor& gate, const at::Tensor& up) {
@@ -215,4 +306,9 @@ TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
     m.impl("mul.Scalar", TORCH_FN(torch_kunlun::mul_scalar));
     m.impl("add_.Tensor", TORCH_FN(torch_kunlun::add_));
     m.impl("mul_.Tensor", TORCH_FN(torch_kunlun::mul_));
+    m.impl("threshold_backward", TORCH_FN(torch_kunlun::threshold_backward));
+    m.impl("sum.dim_IntList", TORCH_FN(torch_kunlun::sum_dim));
+    m.impl("sum", TORCH_FN(torch_kunlun::sum_all));
+    m.impl("mse_loss", TORCH_FN(torch_kunlun::mse_loss));
+    m.impl("mse_loss_backward", TORCH_FN(torch_kunlun::mse_loss_backward));
 }
