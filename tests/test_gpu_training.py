@@ -109,3 +109,69 @@ def test_mlp_mse_sgd_training():
         opt.step()
         losses.append(float(loss.detach().cpu().item()))
     assert losses[-1] < losses[0], f"loss did not decrease: {losses[0]} -> {losses[-1]}"
+
+
+def _ones_like(x):
+    out = torch.empty_like(x)
+    out.fill_(1.0)
+    return out
+
+
+def test_conv2d_backward_reference_case():
+    """The reference's tests/test_autograd_nn.py:20-40."""
+    x = torch.randn(1, 2, 5, 5, dtype=torch.float16)
+    w = torch.randn(3, 2, 3, 3, dtype=torch.float16)
+    b = torch.randn(3, dtype=torch.float16)
+    xr, wr, br = x.clone().requires_grad_(), w.clone().requires_grad_(), b.clone().requires_grad_()
+    ref = F.conv2d(xr, wr, br, padding=1)
+    ref.backward(_ones_like(ref))
+    xk = x.clone().to(DEV).requires_grad_()
+    wk = w.clone().to(DEV).requires_grad_()
+    bk = b.clone().to(DEV).requires_grad_()
+    out = F.conv2d(xk, wk, bk, padding=1)
+    out.backward(_ones_like(out))
+    kunlun.synchronize()
+    assert torch.allclose(out.cpu(), ref.detach(), atol=5e-2, rtol=5e-2)
+    assert torch.allclose(xk.grad.cpu(), xr.grad, atol=5e-2, rtol=5e-2)
+    assert torch.allclose(wk.grad.cpu(), wr.grad, atol=5e-2, rtol=5e-2)
+    assert torch.allclose(bk.grad.cpu(), br.grad, atol=5e-2, rtol=5e-2)
+
+
+def test_conv2d_backward_is_quantised_conv():
+    """grad_input and grad_weight are themselves quantised convolutions of the
+    contract: bit-exact against the oracle on the same operands."""
+    N, C, H, F_, k, pad = 2, 6, 9, 5, 3, 1
+    x = rnd((N, C, H, H), 20)
+    w = rnd((F_, C, k, k), 21, 0.2)
+    gy = rnd((N, F_, H, H), 22)
+    xk = x.to(DEV).requires_grad_()
+    wk = w.to(DEV).requires_grad_()
+    F.conv2d(xk, wk, padding=pad).backward(gy.to(DEV))
+    wt = np.ascontiguousarray(np.flip(np.swapaxes(w.numpy(), 0, 1), (2, 3)))
+    want_gi = O.conv2d(gy.numpy(), wt, None, (1, 1), (k - 1 - pad, k - 1 - pad), (1, 1), 1)
+    assert_bits_equal(xk.grad.cpu().numpy(), want_gi, "conv grad_input")
+    xt = np.ascontiguousarray(np.swapaxes(x.numpy(), 0, 1)).astype(np.float32)
+    gt = np.ascontiguousarray(np.swapaxes(gy.numpy(), 0, 1)).astype(np.float32)
+    gw = O.conv2d(xt, gt, None, (1, 1), (pad, pad), (1, 1), 1)[:, :, :k, :k]
+    want_gw = np.ascontiguousarray(np.swapaxes(gw, 0, 1)).astype(np.float16)
+    assert_bits_equal(wk.grad.cpu().numpy(), want_gw, "conv grad_weight")
+
+
+@pytest.mark.parametrize("stride,groups,dil", [(2, 1, 1), (1, 2, 1), (2, 2, 1), (1, 1, 2)])
+def test_conv2d_backward_strided_grouped(stride, groups, dil):
+    x = rnd((2, 4, 11, 10), 23)
+    w = rnd((6, 4 // groups, 3, 3), 24, 0.3)
+    b = rnd((6,), 25, 0.1)
+    gy = None
+    xr, wr, br = x.float().requires_grad_(), w.float().requires_grad_(), b.float().requires_grad_()
+    ref = F.conv2d(xr, wr, br, stride=stride, padding=1, dilation=dil, groups=groups)
+    gy = rnd(tuple(ref.shape), 26)
+    ref.backward(gy.float())
+    xk = x.to(DEV).requires_grad_()
+    wk = w.to(DEV).requires_grad_()
+    bk = b.to(DEV).requires_grad_()
+    out = F.conv2d(xk, wk, bk, stride=stride, padding=1, dilation=dil, groups=groups)
+    out.backward(gy.to(DEV))
+    for got, want in ((xk.grad, xr.grad), (wk.grad, wr.grad), (bk.grad, br.grad)):
+        scale = max(1.0, want.abs().max().item())
+        assert (got.cpu().float() - want).abs().max().item() <= 2e-2 * scale

@@ -177,7 +177,8 @@ std::vector<int64_t> pair_of(at::IntArrayRef v, int64_t dflt) {
 
 at::Tensor conv2d_impl(const at::Tensor& input, const at::Tensor& weight,
                        const std::optional<at::Tensor>& bias, at::IntArrayRef stride,
-                       at::IntArrayRef padding, at::IntArrayRef dilation, int64_t groups) {
+                       at::IntArrayRef padding, at::IntArrayRef dilation, int64_t groups,
+                       const float* amax_x = nullptr, const float* amax_w = nullptr) {
     check_operand(weight, input, "conv2d");
     const bool batched = input.dim() == 4;
     TORCH_CHECK((input.dim() == 4 || input.dim() == 3) && weight.dim() == 4,
@@ -217,6 +218,8 @@ at::Tensor conv2d_impl(const at::Tensor& input, const at::Tensor& weight,
     d.x = x.data_ptr();
     d.weight = w.data_ptr();
     d.out = out.data_ptr();
+    d.amax_x = amax_x;
+    d.amax_w = amax_w;
     const int dev = x.device().index();
     DeviceScope g(dev);
     if (out.numel() > 0) {
@@ -243,6 +246,97 @@ at::Tensor convolution_overrideable(const at::Tensor& input, const at::Tensor& w
     TORCH_CHECK(!transposed, "kunlun: transposed convolution is not implemented");
     TORCH_CHECK(input.dim() == 4 || input.dim() == 3, "kunlun: only 2-D convolution is implemented");
     return conv2d_impl(input, weight, bias, stride, padding, dilation, groups);
+}
+
+// w [A, B, KH, KW] with both spatial axes reversed, as a device strided copy
+// that reads the source with negative strides from its last tap.
+at::Tensor flip_hw(const at::Tensor& w_in) {
+    at::Tensor w = w_in.contiguous();
+    at::Tensor out = at::empty(w.sizes(), w.options());
+    if (w.numel() == 0) return out;
+    const int64_t sizes[4] = {w.size(0), w.size(1), w.size(2), w.size(3)};
+    const int64_t dst[4] = {w.stride(0), w.stride(1), w.stride(2), w.stride(3)};
+    const int64_t src[4] = {w.stride(0), w.stride(1), -w.stride(2), -w.stride(3)};
+    const int64_t last = (w.size(2) - 1) * w.stride(2) + (w.size(3) - 1) * w.stride(3);
+    const int dev = w.device().index();
+    DeviceScope g(dev);
+    const int t = tk_scalar_code(w.scalar_type());
+    check_tk(tk_copy_strided(out.data_ptr(), t,
+                             static_cast<const char*>(w.data_ptr()) + last * w.element_size(), t, 4,
+                             sizes, dst, src, current_stream(dev)),
+             "tk_copy_strided");
+    return out;
+}
+
+// Gradients of the quantised conv2d (the reference's conv2d_grad,
+// csrc/autograd.cpp:621-682), each a quantised convolution of the same
+// contract with one per-tensor scale per operand:
+//   grad_input  = correlation of the zero-inserted (stride), padded grad_output
+//                 with the spatially flipped, in/out-swapped weight;
+//   grad_weight = per group, the correlation of the input with grad_output,
+//                 both with batch and channels swapped (the batch is the
+//                 reduction), scales from the whole input and the whole
+//                 grad_output; reductions longer than the exact limb limit
+//                 (32768) are split over the batch and the fp32 chunk results
+//                 summed before the one rounding to the input dtype;
+//   grad_bias   = sum of grad_output over batch and pixels (fp32, one rounding).
+std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable(
+    const at::Tensor& grad_output, const at::Tensor& input, const at::Tensor& weight,
+    at::IntArrayRef stride, at::IntArrayRef padding, at::IntArrayRef dilation, bool transposed,
+    at::IntArrayRef output_padding, int64_t groups, std::array<bool, 3> output_mask) {
+    TORCH_CHECK(!transposed, "kunlun: transposed convolution backward is not implemented");
+    TORCH_CHECK(input.dim() == 4 && weight.dim() == 4 && grad_output.dim() == 4,
+                "kunlun conv2d backward expects NCHW tensors");
+    const auto s = pair_of(stride, 1), p = pair_of(padding, 0), dl = pair_of(dilation, 1);
+    const int64_t N = input.size(0), C = input.size(1), H = input.size(2), W = input.size(3);
+    const int64_t F = weight.size(0), Cg = weight.size(1), KH = weight.size(2), KW = weight.size(3);
+    const int64_t Fg = F / groups;
+    const int64_t OH = grad_output.size(2), OW = grad_output.size(3);
+    at::Tensor g = grad_output.contiguous();
+    at::Tensor gi, gw, gb;
+    if (output_mask[0]) {
+        const int64_t ph = dl[0] * (KH - 1) - p[0], pw = dl[1] * (KW - 1) - p[1];
+        TORCH_CHECK(ph >= 0 && pw >= 0,
+                    "kunlun conv2d backward: padding larger than the dilated kernel is not supported");
+        // rows / columns of the input that the forward's last window did not reach
+        const int64_t eh = (H + 2 * p[0] - dl[0] * (KH - 1) - 1) % s[0];
+        const int64_t ew = (W + 2 * p[1] - dl[1] * (KW - 1) - 1) % s[1];
+        at::Tensor gz = g;
+        if (s[0] > 1 || s[1] > 1 || eh > 0 || ew > 0) {
+            gz = at::zeros({N, F, (OH - 1) * s[0] + 1 + eh, (OW - 1) * s[1] + 1 + ew}, g.options());
+            gz.slice(2, 0, (OH - 1) * s[0] + 1, s[0]).slice(3, 0, (OW - 1) * s[1] + 1, s[1]).copy_(g);
+        }
+        at::Tensor wt = flip_hw(weight.view({groups, Fg, Cg, KH, KW}).transpose(1, 2).reshape({C, Fg, KH, KW}));
+        const int64_t pad[2] = {ph, pw}, one[2] = {1, 1};
+        gi = conv2d_impl(gz, wt, std::nullopt, one, pad, dilation, groups);
+    }
+    if (output_mask[1]) {
+        at::Tensor ax = torch_kunlun::amax(input), ag = torch_kunlun::amax(g);
+        std::vector<at::Tensor> per_group;
+        for (int64_t gr = 0; gr < groups; ++gr) {
+            // [Cg, N, H, W] and [Fg, N, OH, OW]: batch as channels, reduced over
+            at::Tensor xt = input.slice(1, gr * Cg, (gr + 1) * Cg).transpose(0, 1);
+            at::Tensor gt = g.slice(1, gr * Fg, (gr + 1) * Fg).transpose(0, 1);
+            const int64_t per_image = OH * OW;
+            const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(N, 32768 / per_image));
+            TORCH_CHECK(per_image <= 32768, "kunlun conv2d backward: output plane exceeds 32768 pixels");
+            at::Tensor acc;
+            for (int64_t n0 = 0; n0 < N; n0 += chunk) {
+                const int64_t n1 = std::min(N, n0 + chunk);
+                at::Tensor xc = xt.slice(1, n0, n1).to(at::kFloat).contiguous();
+                at::Tensor gc = gt.slice(1, n0, n1).to(at::kFloat).contiguous();
+                at::Tensor r = conv2d_impl(xc, gc, std::nullopt, dilation, padding, stride, 1,
+                                           ax.data_ptr<float>(), ag.data_ptr<float>());
+                r = r.slice(2, 0, KH).slice(3, 0, KW);  // [Cg, Fg, KH, KW]
+                acc = acc.defined() ? at::add(acc, r) : r;
+            }
+            per_group.push_back(acc.transpose(0, 1));
+        }
+        gw = at::empty(weight.sizes(), weight.options());
+        for (int64_t gr = 0; gr < groups; ++gr) gw.slice(0, gr * Fg, (gr + 1) * Fg).copy_(per_group[gr]);
+    }
+    if (output_mask[2]) gb = at::sum(g, {0, 2, 3});
+    return {gi, gw, gb};
 }
 
 }  // namespace
@@ -345,6 +439,25 @@ at::Tensor linear_autograd(const at::Tensor& input, const at::Tensor& weight,
     return linear_fwd(input, weight, bias);
 }
 
+// conv2d under autograd: with gradients required, route through
+// aten::convolution, whose backward is convolution_backward_overrideable.
+at::Tensor conv2d_autograd(const at::Tensor& input, const at::Tensor& weight,
+                           const std::optional<at::Tensor>& bias, at::IntArrayRef stride,
+                           at::IntArrayRef padding, at::IntArrayRef dilation, int64_t groups) {
+    const bool needs_grad = at::GradMode::is_enabled() &&
+                            (input.requires_grad() || weight.requires_grad() ||
+                             (bias.has_value() && bias->defined() && bias->requires_grad()));
+    if (needs_grad) {
+        const bool batched = input.dim() == 4;
+        at::Tensor x = batched ? input : input.unsqueeze(0);
+        const int64_t zero[2] = {0, 0};
+        at::Tensor out = at::convolution(x, weight, bias, stride, padding, dilation, false, zero, groups);
+        return batched ? out : out.squeeze(0);
+    }
+    at::AutoDispatchBelowADInplaceOrView guard;
+    return conv2d_impl(input, weight, bias, stride, padding, dilation, groups);
+}
+
 }  // namespace
 }  // namespace torch_kunlun
 
@@ -356,8 +469,11 @@ TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
     m.impl("linear", TORCH_FN(torch_kunlun::linear_fwd));
     m.impl("conv2d", TORCH_FN(torch_kunlun::conv2d));
     m.impl("convolution_overrideable", TORCH_FN(torch_kunlun::convolution_overrideable));
+    m.impl("convolution_backward_overrideable",
+           TORCH_FN(torch_kunlun::convolution_backward_overrideable));
 }
 
 TORCH_LIBRARY_IMPL(aten, AutogradPrivateUse1, m) {
     m.impl("linear", TORCH_FN(torch_kunlun::linear_autograd));
+    m.impl("conv2d", TORCH_FN(torch_kunlun::conv2d_autograd));
 }
