@@ -29,7 +29,8 @@ int quantize_limbs_launch(tk_dtype_t dtype, const void* x, int64_t batch, int64_
 int qgemm_limbs_ex(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb,
                    const float* amax_a, const float* amax_b, int b_mod, int64_t out_sn,
                    int64_t bias_mod, cudaStream_t stream);
-size_t conv_tc_workspace(int64_t N, int64_t C, int64_t H, int64_t W, int64_t F, int64_t KH, int64_t KW);
+size_t conv_tc_workspace(int64_t N, int64_t C, int64_t H, int64_t W, int64_t F, int64_t KH, int64_t KW,
+                         int64_t ph, int64_t pw);
 int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, void* out, int64_t N,
             int64_t C, int64_t H, int64_t W, int64_t F, int64_t KH, int64_t KW, int64_t ph, int64_t pw,
             int64_t dh, int64_t dw, int64_t OH, int64_t OW, const float* amax_x, const float* amax_w,
@@ -290,7 +291,7 @@ ConvLayout conv_layout(const ConvGeom& g) {
     }
     if (is_implicit(g)) {
         L.off_lb = L.off_la;
-        L.total = L.off_la + conv_tc_workspace(g.N, g.C, g.H, g.W, g.F, g.KH, g.KW);
+        L.total = L.off_la + conv_tc_workspace(g.N, g.C, g.H, g.W, g.F, g.KH, g.KW, g.ph, g.pw);
         return L;
     }
     L.off_lb = round_up(L.off_la + static_cast<size_t>(g.N * g.groups * 2 * P * L.ld), 1024);
