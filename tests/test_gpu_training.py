@@ -175,3 +175,25 @@ def test_conv2d_backward_strided_grouped(stride, groups, dil):
     for got, want in ((xk.grad, xr.grad), (wk.grad, wr.grad), (bk.grad, br.grad)):
         scale = max(1.0, want.abs().max().item())
         assert (got.cpu().float() - want).abs().max().item() <= 2e-2 * scale
+
+
+def test_cat_out_variants_and_inplace_division():
+    """Ops the data-parallel reducer and coalesced broadcast run on the device:
+    cat (flatten of a bucket), mul.out into a strided bucket view with a
+    wrapped scalar, div_ / sub_ in place."""
+    a, b, c = rnd((3, 5), 30), rnd((2, 5), 31), rnd((4, 5), 32, dtype=torch.float32)
+    got = torch.cat([a.to(DEV), b.to(DEV), torch.empty(0, dtype=torch.float16).to(DEV), c.to(DEV)]).cpu()
+    assert torch.equal(got, torch.cat([a.float(), b.float(), c]))
+    got1 = torch.cat([a.to(DEV), a.to(DEV)], dim=1).cpu()
+    assert torch.equal(got1, torch.cat([a, a], dim=1))
+    bucket = torch.zeros(40, dtype=torch.float16).to(DEV)
+    view = bucket.narrow(0, 5, 15).view(3, 5)
+    torch.mul(a.to(DEV), 0.5, out=view)
+    want = torch.zeros(40, dtype=torch.float16)
+    want[5:20] = (a.float() * 0.5).half().reshape(-1)
+    assert torch.equal(bucket.cpu(), want)
+    x = a.to(DEV)
+    x.div_(4)
+    assert torch.equal(x.cpu(), (a.float() * 0.25).half())
+    x.sub_(b[:1].to(DEV), alpha=2)
+    assert torch.allclose(x.cpu().float(), (a.float() * 0.25).half().float() - 2 * b[:1].float(), atol=2e-3)

@@ -121,3 +121,71 @@ def test_bkcl_backend_registered_for_kunlun():
     import torch_kunlun  # noqa: F401
     assert "bkcl" in dist.Backend.backend_list
     assert dist.Backend.default_device_backend_map.get("kunlun") == "bkcl"
+
+
+def _ddp_worker(rank, world, port, q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        _GLOO[0] = dist.group.WORLD
+        from torch_kunlun_b200 import xccl
+        store = dist.TCPStore("127.0.0.1", port + 1, world, rank == 0)
+        pg = xccl.ProcessGroupXCCL(store, rank, world, engine_factory=GlooEngine)
+        torch.manual_seed(100 + rank)  # different initial weights on every rank
+        model = torch.nn.Sequential(torch.nn.Linear(8, 16), torch.nn.ReLU(), torch.nn.Linear(16, 1))
+        ddp = torch.nn.parallel.DistributedDataParallel(model, process_group=pg, bucket_cap_mb=0.0001)
+        # construction broadcast rank 0's parameters (coalesced broadcast)
+        torch.manual_seed(100)
+        want0 = torch.nn.Sequential(torch.nn.Linear(8, 16), torch.nn.ReLU(), torch.nn.Linear(16, 1))
+        for p, w in zip(model.parameters(), want0.parameters()):
+            assert torch.equal(p.detach(), w.detach())
+        ref = [p.detach().clone().requires_grad_() for p in model.parameters()]
+        opt = torch.optim.SGD(model.parameters(), lr=0.1)
+        for step in range(3):
+            g = torch.Generator().manual_seed(10 * step + rank)
+            x, t = torch.randn(4, 8, generator=g), torch.randn(4, 1, generator=g)
+            opt.zero_grad()
+            torch.nn.functional.mse_loss(ddp(x), t).backward()
+            # every rank's local gradient, gathered, averaged: DDP's result
+            for p in ref:
+                p.grad = None
+            h = torch.relu(x @ ref[0].t() + ref[1])
+            torch.nn.functional.mse_loss(h @ ref[2].t() + ref[3], t).backward()
+            for p, r in zip(model.parameters(), ref):
+                parts = [torch.empty_like(r.grad) for _ in range(world)]
+                dist.all_gather(parts, r.grad, group=_GLOO[0])
+                want = sum(parts) / world
+                assert torch.allclose(p.grad, want, atol=1e-6, rtol=1e-5), (step, p.grad, want)
+            opt.step()
+            with torch.no_grad():
+                for p, r in zip(model.parameters(), ref):
+                    r.copy_(p)
+        flat = torch.cat([p.detach().reshape(-1) for p in model.parameters()])
+        every = [torch.empty_like(flat) for _ in range(world)]
+        dist.all_gather(every, flat, group=_GLOO[0])
+        assert all(torch.equal(every[0], e) for e in every)
+        q.put((rank, "ok"))
+    except Exception:  # pragma: no cover - reported to the parent
+        import traceback
+        q.put((rank, traceback.format_exc()[-1500:]))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_ddp_over_the_bkcl_process_group_on_two_gloo_ranks():
+    """DistributedDataParallel driving ProcessGroupXCCL (reference
+    torch_kunlun/xccl.py:158-213): the coalesced parameter broadcast at
+    construction, per-bucket gradient allreduce through Work futures, and
+    identical parameters on every rank after the optimizer steps."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ddp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=180) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert results == {0: "ok", 1: "ok"}, results

@@ -313,6 +313,52 @@ void record_stream(at::Tensor& self, c10::Stream stream) {
     record_data_ptr_on_stream(self.storage().data_ptr(), stream);
 }
 
+// Concatenation along `dim`: each input is a device copy into its slice of
+// the output (converting to the promoted dtype).  Legacy 1-D empty inputs
+// are skipped as in aten.  Used by DDP's coalesced broadcast
+// (flatten_dense_tensors) and by user code.
+at::Tensor cat(const at::ITensorListRef& tensors, int64_t dim) {
+    std::vector<at::Tensor> ts;
+    for (const at::Tensor& t : tensors) ts.push_back(t);
+    TORCH_CHECK(!ts.empty(), "kunlun cat: expected a non-empty list of tensors");
+    auto skip = [](const at::Tensor& t) { return t.dim() == 1 && t.size(0) == 0; };
+    const at::Tensor* ref = nullptr;
+    at::ScalarType rt = ts[0].scalar_type();
+    bool first = true;
+    for (const at::Tensor& t : ts) {
+        TORCH_CHECK(t.device().type() == c10::DeviceType::PrivateUse1, "kunlun cat: tensor on ",
+                    t.device());
+        rt = first ? t.scalar_type() : c10::promoteTypes(rt, t.scalar_type());
+        first = false;
+        if (!skip(t) && ref == nullptr) ref = &t;
+    }
+    if (ref == nullptr) return at::empty({0}, ts[0].options().dtype(rt));
+    const int64_t nd = ref->dim();
+    TORCH_CHECK(nd > 0, "kunlun cat: zero-dimensional tensor cannot be concatenated");
+    dim = c10::maybe_wrap_dim(dim, nd);
+    std::vector<int64_t> shape = ref->sizes().vec();
+    int64_t total = 0;
+    for (const at::Tensor& t : ts) {
+        if (skip(t)) continue;
+        TORCH_CHECK(t.dim() == nd, "kunlun cat: tensors must have the same number of dimensions");
+        for (int64_t d = 0; d < nd; ++d)
+            TORCH_CHECK(d == dim || t.size(d) == shape[d], "kunlun cat: sizes of tensors must match except in dimension ",
+                        dim);
+        TORCH_CHECK(t.device() == ref->device(), "kunlun cat: tensors on different devices");
+        total += t.size(dim);
+    }
+    shape[dim] = total;
+    at::Tensor out = at::empty(shape, ref->options().dtype(rt));
+    int64_t off = 0;
+    for (const at::Tensor& t : ts) {
+        if (skip(t) || t.size(dim) == 0) continue;
+        at::Tensor slice = out.narrow(dim, off, t.size(dim));
+        device_copy(slice, t);
+        off += t.size(dim);
+    }
+    return out;
+}
+
 }  // namespace
 }  // namespace torch_kunlun
 
@@ -331,4 +377,5 @@ TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
     m.impl("clone", TORCH_FN(torch_kunlun::clone));
     m.impl("fill_.Scalar", TORCH_FN(torch_kunlun::fill_impl));
     m.impl("zero_", TORCH_FN(torch_kunlun::zero_impl));
+    m.impl("cat", TORCH_FN(torch_kunlun::cat));
 }

@@ -135,8 +135,13 @@ at::Tensor binary(const at::Tensor& a_in, const at::Tensor& b_in, int op, double
             case TK_BIN_SUB:
                 if (b_scalar) return unary(x, TK_UN_SCALE, 1.f, static_cast<float>(-alpha * v));
                 return unary(x, TK_UN_SCALE, static_cast<float>(-alpha), static_cast<float>(v));
+            case TK_BIN_DIV:
+                // tensor / scalar multiplies by the reciprocal, as torch's CUDA
+                // division by a CPU scalar does
+                if (b_scalar) return unary(x, TK_UN_SCALE, static_cast<float>(1.0 / v), 0.f);
+                break;  // scalar / tensor: the tensor path
             default:
-                break;  // division by / of a scalar: fall through to the tensor path
+                break;
         }
     }
     at::Tensor a = is_kunlun(a_in) ? a_in : a_in.to(b_in.device());
@@ -182,6 +187,35 @@ at::Tensor& add_(at::Tensor& self, const at::Tensor& other, const at::Scalar& al
 at::Tensor& mul_(at::Tensor& self, const at::Tensor& other) {
     self.copy_(binary(self, other, TK_BIN_MUL, 1.0));
     return self;
+}
+at::Tensor& sub_(at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha) {
+    self.copy_(binary(self, other, TK_BIN_SUB, alpha.toDouble()));
+    return self;
+}
+at::Tensor& div_(at::Tensor& self, const at::Tensor& other) {
+    self.copy_(binary(self, other, TK_BIN_DIV, 1.0));
+    return self;
+}
+
+// out= variants write through copy_, so `out` may be any strided view (DDP's
+// reducer multiplies each gradient by 1/world_size straight into its bucket
+// view: at::mul_out(bucket_view, grad, wrapped_scalar)).
+at::Tensor& out_result(at::Tensor& out, const at::Tensor& r) {
+    if (!out.sizes().equals(r.sizes())) {
+        TORCH_CHECK(out.numel() == 0 || out.is_contiguous(), "kunlun out=: cannot resize a non-contiguous output");
+        out.resize_(r.sizes());
+    }
+    out.copy_(r);
+    return out;
+}
+at::Tensor& mul_out(const at::Tensor& self, const at::Tensor& other, at::Tensor& out) {
+    return out_result(out, binary(self, other, TK_BIN_MUL, 1.0));
+}
+at::Tensor& add_out(const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha, at::Tensor& out) {
+    return out_result(out, binary(self, other, TK_BIN_ADD, alpha.toDouble()));
+}
+at::Tensor& div_out(const at::Tensor& self, const at::Tensor& other, at::Tensor& out) {
+    return out_result(out, binary(self, other, TK_BIN_DIV, 1.0));
 }
 
 // ---- backward support: relu gradient, sums, MSE loss --------------------------
@@ -306,6 +340,11 @@ TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
     m.impl("mul.Scalar", TORCH_FN(torch_kunlun::mul_scalar));
     m.impl("add_.Tensor", TORCH_FN(torch_kunlun::add_));
     m.impl("mul_.Tensor", TORCH_FN(torch_kunlun::mul_));
+    m.impl("sub_.Tensor", TORCH_FN(torch_kunlun::sub_));
+    m.impl("div_.Tensor", TORCH_FN(torch_kunlun::div_));
+    m.impl("mul.out", TORCH_FN(torch_kunlun::mul_out));
+    m.impl("add.out", TORCH_FN(torch_kunlun::add_out));
+    m.impl("div.out", TORCH_FN(torch_kunlun::div_out));
     m.impl("threshold_backward", TORCH_FN(torch_kunlun::threshold_backward));
     m.impl("sum.dim_IntList", TORCH_FN(torch_kunlun::sum_dim));
     m.impl("sum", TORCH_FN(torch_kunlun::sum_all));

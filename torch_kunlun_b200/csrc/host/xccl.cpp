@@ -60,10 +60,14 @@ ncclDataType_t to_nccl(at::ScalarType t) {
         case at::kFloat: return ncclFloat32;
         case at::kHalf: return ncclFloat16;
         case at::kBFloat16: return ncclBfloat16;
+        case at::kDouble: return ncclFloat64;
         case at::kInt: return ncclInt32;
+        case at::kLong: return ncclInt64;
+        case at::kChar: return ncclInt8;
+        case at::kByte:
+        case at::kBool: return ncclUint8;
         default:
-            TORCH_CHECK(false, "kunlun xccl unsupported dtype ", t,
-                        " (float32/float16/bfloat16/int32 collectives only)");
+            TORCH_CHECK(false, "kunlun xccl unsupported dtype ", t);
     }
 }
 
