@@ -194,6 +194,29 @@ TK_API size_t tk_conv2d_workspace_size(const tk_conv2d_desc_t* desc);
 TK_API int tk_conv2d_q16(const tk_conv2d_desc_t* desc, void* workspace, size_t workspace_bytes,
                          void* stream);
 
+/* ---- quantised conv3d --------------------------------------------------------
+ * Replaces baidu::xpu::api::conv3d<T,T,T,TGEMM> and the bias add of conv3d
+ * (csrc/ops_nn_extra.cpp:88-121) with the conv2d contract above: NCDHW input
+ * [n,c,d,h,w], OIDHW weight [f, c/groups, kd, kh, kw], optional bias [f],
+ * NCDHW output, one scale per tensor, bias added after rounding.
+ * (c/groups)*kd*kh*kw must be <= 32768.  tk_conv2d_q16 is this call with
+ * d = kd = 1. */
+typedef struct {
+    tk_dtype_t dtype;
+    int64_t n, c, d, h, w, f, kd, kh, kw;
+    int64_t stride_d, stride_h, stride_w, pad_d, pad_h, pad_w, dil_d, dil_h, dil_w, groups;
+    const void* x;
+    const void* weight;
+    const void* bias;
+    void* out;
+    const float* amax_x; /* optional precomputed per-tensor amax (device) */
+    const float* amax_w;
+} tk_conv3d_desc_t;
+
+TK_API size_t tk_conv3d_workspace_size(const tk_conv3d_desc_t* desc);
+TK_API int tk_conv3d_q16(const tk_conv3d_desc_t* desc, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
 /* ---- reduction ---------------------------------------------------------------
  * out[o][i] = sum_r x[o][r][i] over a contiguous [outer, red, inner] tensor,
  * accumulated in fp32 in a fixed order (deterministic) and rounded once to

@@ -268,6 +268,99 @@ def conv2d(x: np.ndarray, w: np.ndarray, bias=None, stride=(1, 1), pad=(0, 0), d
     return y.reshape(NB, F, OH, OW)
 
 
+def convnd_acc(qx: np.ndarray, qw: np.ndarray, stride, pad, dil, groups) -> np.ndarray:
+    """int64 accumulators of a quantised convolution with any number of
+    spatial axes (NC... input, OI... weight): the conv2d gather above per
+    kernel tap, float64 sums of integers below 2^53 (exact)."""
+    import itertools
+    k = qx.ndim - 2
+    NB, C = qx.shape[:2]
+    F, cg = qw.shape[:2]
+    ks = qw.shape[2:]
+    outs = [(qx.shape[2 + i] + 2 * pad[i] - dil[i] * (ks[i] - 1) - 1) // stride[i] + 1 for i in range(k)]
+    xp = np.zeros((NB, C) + tuple(qx.shape[2 + i] + 2 * pad[i] for i in range(k)), dtype=np.float64)
+    xp[(slice(None), slice(None)) + tuple(slice(pad[i], pad[i] + qx.shape[2 + i]) for i in range(k))] = qx
+    fg = F // groups
+    acc = np.zeros((NB, F) + tuple(outs), dtype=np.float64)
+    for g in range(groups):
+        xs = xp[:, g * cg:(g + 1) * cg]
+        for tap in itertools.product(*[range(t) for t in ks]):
+            sl = tuple(slice(tap[i] * dil[i], tap[i] * dil[i] + stride[i] * (outs[i] - 1) + 1, stride[i])
+                       for i in range(k))
+            win = xs[(slice(None), slice(None)) + sl]                      # [NB, cg, O...]
+            wt = qw[(slice(g * fg, (g + 1) * fg), slice(None)) + tap].astype(np.float64)  # [fg, cg]
+            acc[:, g * fg:(g + 1) * fg] += np.einsum("fc,nc...->nf...", wt, win)
+    return acc.astype(np.int64)
+
+
+def _conv_epilogue(acc, x, ax, aw, bias):
+    NB, F = acc.shape[:2]
+    flat = acc.reshape(NB * F, -1)
+    add = None
+    if bias is not None:
+        add = np.repeat(np.asarray(bias, dtype=x.dtype).reshape(1, F), NB, 0).reshape(NB * F, 1)
+        add = np.broadcast_to(add, flat.shape)
+    y = epilogue(flat, ax, aw, x.dtype, addend=add, beta=1.0 if add is not None else 0.0)
+    return y.reshape(acc.shape)
+
+
+def conv3d(x: np.ndarray, w: np.ndarray, bias=None, stride=(1, 1, 1), pad=(0, 0, 0), dil=(1, 1, 1),
+           groups=1) -> np.ndarray:
+    """conv3d with the conv2d contract (csrc/ops_nn_extra.cpp:88-121: xdnn
+    conv3d with TGEMM = int16 and null maxptrs, then a separately rounded bias
+    add)."""
+    ax, aw = amax(x), amax(w)
+    acc = convnd_acc(quant(x, ax), quant(w, aw), stride, pad, dil, groups)
+    return _conv_epilogue(acc, x, ax, aw, bias)
+
+
+def conv1d(x: np.ndarray, w: np.ndarray, bias=None, stride=1, pad=0, dil=1, groups=1) -> np.ndarray:
+    """conv1d as conv2d on [N, C, 1, L] (csrc/ops_nn_extra.cpp:70-86)."""
+    y = conv2d(x[:, :, None, :], w[:, :, None, :], bias, (1, stride), (0, pad), (1, dil), groups)
+    return y[:, :, 0, :]
+
+
+def conv_transpose_acc(qx: np.ndarray, qw: np.ndarray, stride, pad, out_pad, dil, groups) -> np.ndarray:
+    """int64 accumulators of a transposed convolution by its definition: input
+    element i scatters x[i] * w[tap] to output position i*stride - pad +
+    tap*dil (weight [C_in, C_out/groups, K...])."""
+    import itertools
+    k = qx.ndim - 2
+    NB, Cin = qx.shape[:2]
+    cog = qw.shape[1]
+    ks = qw.shape[2:]
+    cig = Cin // groups
+    ins = qx.shape[2:]
+    outs = [(ins[i] - 1) * stride[i] - 2 * pad[i] + dil[i] * (ks[i] - 1) + 1 + out_pad[i] for i in range(k)]
+    full = [(ins[i] - 1) * stride[i] + dil[i] * (ks[i] - 1) + 1 + out_pad[i] for i in range(k)]
+    acc = np.zeros((NB, cog * groups) + tuple(full), dtype=np.float64)
+    for g in range(groups):
+        xs = qx[:, g * cig:(g + 1) * cig].astype(np.float64)
+        for tap in itertools.product(*[range(t) for t in ks]):
+            wt = qw[(slice(g * cig, (g + 1) * cig), slice(None)) + tap].astype(np.float64)  # [cig, cog]
+            contrib = np.einsum("nc...,co->no...", xs, wt)
+            sl = tuple(slice(tap[i] * dil[i], tap[i] * dil[i] + stride[i] * (ins[i] - 1) + 1, stride[i])
+                       for i in range(k))
+            acc[(slice(None), slice(g * cog, (g + 1) * cog)) + sl] += contrib
+    crop = tuple(slice(pad[i], pad[i] + outs[i]) for i in range(k))
+    return acc[(slice(None), slice(None)) + crop].astype(np.int64)
+
+
+def conv_transpose(x: np.ndarray, w: np.ndarray, bias=None, stride=None, pad=None, out_pad=None, dil=None,
+                   groups=1) -> np.ndarray:
+    """Transposed convolution (csrc/ops_nn_extra.cpp:123-159: xdnn
+    conv2d_transpose with TGEMM = int16, null maxptrs, then the bias add) with
+    the conv2d contract: one scale per tensor, exact sum, one rounding."""
+    k = x.ndim - 2
+    stride = stride or (1,) * k
+    pad = pad or (0,) * k
+    out_pad = out_pad or (0,) * k
+    dil = dil or (1,) * k
+    ax, aw = amax(x), amax(w)
+    acc = conv_transpose_acc(quant(x, ax), quant(w, aw), stride, pad, out_pad, dil, groups)
+    return _conv_epilogue(acc, x, ax, aw, bias)
+
+
 # ---- float row ops (tolerance-level references, float64 internally) ----------
 
 

@@ -118,3 +118,33 @@ def test_conv_fast_matches_scalar():
         a = O.conv2d_acc(qx, qw, stride, pad, dil, groups, scalar=False)
         b = O.conv2d_acc(qx, qw, stride, pad, dil, groups, scalar=True)
         assert np.array_equal(a, b)
+
+
+def test_nd_and_transposed_conv_accumulators_match_exact_float64_convs():
+    """The oracle's N-d gather and its scatter definition of the transposed
+    convolution against torch's CPU float64 convolutions of the same integer
+    codes (exact: every partial sum is an integer below 2^53)."""
+    import torch
+    import torch.nn.functional as F
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((2, 4, 5, 6, 7)).astype(np.float16)
+    w = rng.standard_normal((6, 2, 2, 3, 2)).astype(np.float16)
+    qx, qw = O.quant(x), O.quant(w)
+    want = F.conv3d(torch.tensor(qx, dtype=torch.float64), torch.tensor(qw, dtype=torch.float64),
+                    stride=(1, 2, 1), padding=(1, 0, 1), dilation=(2, 1, 1), groups=2).numpy()
+    assert np.array_equal(O.convnd_acc(qx, qw, (1, 2, 1), (1, 0, 1), (2, 1, 1), 2), want.astype(np.int64))
+    x2 = rng.standard_normal((2, 4, 7, 6)).astype(np.float16)
+    q2 = O.quant(x2)
+    w2 = O.quant(rng.standard_normal((6, 2, 3, 3)).astype(np.float16))
+    assert np.array_equal(O.convnd_acc(q2, w2, (2, 1), (1, 1), (1, 2), 2),
+                          O.conv2d_acc(q2, w2, (2, 1), (1, 1), (1, 2), 2))
+    wt = O.quant(rng.standard_normal((4, 3, 3, 3)).astype(np.float16))
+    for s, p, op, d in [((2, 2), (1, 1), (1, 1), (1, 1)), ((2, 3), (2, 0), (0, 2), (2, 1))]:
+        want = F.conv_transpose2d(torch.tensor(q2, dtype=torch.float64), torch.tensor(wt, dtype=torch.float64),
+                                  stride=s, padding=p, output_padding=op, groups=2, dilation=d).numpy()
+        assert np.array_equal(O.conv_transpose_acc(q2, wt, s, p, op, d, 2), want.astype(np.int64))
+    x1 = rng.standard_normal((2, 3, 9)).astype(np.float16)
+    w1 = rng.standard_normal((4, 3, 3)).astype(np.float16)
+    y1 = O.conv1d(x1, w1, None, 2, 1, 1, 1)
+    y2 = O.conv2d(x1[:, :, None, :], w1[:, :, None, :], None, (1, 2), (0, 1), (1, 1), 1)[:, :, 0, :]
+    assert np.array_equal(y1.view(np.uint16), y2.view(np.uint16))

@@ -1,21 +1,23 @@
-// conv.cu -- int16-quantised conv2d (NCHW input, OIHW weight, bias, stride,
-// padding, dilation, groups).
+// conv.cu -- int16-quantised conv2d and conv3d (NC[D]HW input, OI[D]HW
+// weight, bias, stride, padding, dilation, groups).
 //
 // Replaces baidu::xpu::api::conv2d<T,T,T,TGEMM> and the bias broadcast_add
-// that follows it (csrc/ops.cpp:237-285).  Per the reference, the whole
-// input and the whole weight are each quantised with one per-tensor scale.
+// that follows it (csrc/ops.cpp:237-285), and xdnn conv3d + add
+// (csrc/ops_nn_extra.cpp:88-121).  Per the reference, the whole input and the
+// whole weight are each quantised with one per-tensor scale.  A 2-D
+// convolution is handled as the 3-D one with D = KD = 1.
 //
 // Paths:
-//   * groups == C == F/mult (depthwise): a CUDA-core kernel, one output per
-//     thread, exact int64 accumulation of the KHxKW taps.  HBM-bound.
+//   * 2-D, groups == C == F/mult (depthwise): a CUDA-core kernel, one output
+//     per thread, exact int64 accumulation of the KHxKW taps.  HBM-bound.
 //   * groups == 1, stride 1: implicit GEMM on the tensor cores (conv_tc.cu),
 //     no patch matrix in HBM.
 //   * otherwise a GEMM per (image, group) on the tensor-core limb kernel:
-//     A = the image's input patches [OH*OW, C/g*KH*KW] quantised straight into
-//     limb planes (1x1 stride-1 convolutions read NCHW directly as a
-//     transposed operand; larger kernels gather patches in the same pass),
-//     B = the group's weights [F/g, C/g*KH*KW] (shared by all images), and
-//     the epilogue writes the pixels x channels tile into NCHW.
+//     A = the image's input patches [OD*OH*OW, C/g*KD*KH*KW] quantised
+//     straight into limb planes (1x1 stride-1 convolutions read NCHW
+//     directly as a transposed operand; larger kernels gather patches in the
+//     same pass), B = the group's weights [F/g, C/g*KD*KH*KW] (shared by all
+//     images), and the epilogue writes the pixels x channels tile into NCHW.
 #include "tk_internal.h"
 #include "tk_numerics.cuh"
 
@@ -29,17 +31,18 @@ int quantize_limbs_launch(tk_dtype_t dtype, const void* x, int64_t batch, int64_
 int qgemm_limbs_ex(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb,
                    const float* amax_a, const float* amax_b, int b_mod, int64_t out_sn,
                    int64_t bias_mod, cudaStream_t stream);
-size_t conv_tc_workspace(int64_t N, int64_t C, int64_t H, int64_t W, int64_t F, int64_t KH, int64_t KW,
-                         int64_t ph, int64_t pw);
+size_t conv_tc_workspace(int64_t N, int64_t C, int64_t D, int64_t H, int64_t W, int64_t F, int64_t KD,
+                         int64_t KH, int64_t KW, int64_t ph, int64_t pw);
 int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, void* out, int64_t N,
-            int64_t C, int64_t H, int64_t W, int64_t F, int64_t KH, int64_t KW, int64_t ph, int64_t pw,
-            int64_t dh, int64_t dw, int64_t OH, int64_t OW, const float* amax_x, const float* amax_w,
-            uint8_t* ws, cudaStream_t stream);
+            int64_t C, int64_t D, int64_t H, int64_t W, int64_t F, int64_t KD, int64_t KH, int64_t KW,
+            int64_t pd, int64_t ph, int64_t pw, int64_t dd, int64_t dh, int64_t dw, int64_t OD, int64_t OH,
+            int64_t OW, const float* amax_x, const float* amax_w, uint8_t* ws, cudaStream_t stream);
 
 namespace {
 
 struct ConvGeom {
     int64_t N, C, H, W, F, KH, KW, sh, sw, ph, pw, dh, dw, groups, OH, OW;
+    int64_t D, KD, sd, pd, dd, OD;  // depth (1, 1, 1, 0, 1, 1 for 2-D)
 };
 
 template <typename T>
@@ -47,18 +50,20 @@ __device__ __forceinline__ float ldx(const T* p, int64_t i);
 template <> __device__ __forceinline__ float ldx<__half>(const __half* p, int64_t i) { return __half2float(p[i]); }
 template <> __device__ __forceinline__ float ldx<float>(const float* p, int64_t i) { return p[i]; }
 
-// Patch gather + quantisation.  Slice b = n*groups + g, row p = oh*OW + ow,
-// column k = (c*KH + r)*KW + s over the group's channels; 4 columns per thread
-// so that both limb planes are written with 32-bit stores.
+// Patch gather + quantisation.  Slice b = n*groups + g, row
+// p = (od*OH + oh)*OW + ow, column k = ((c*KD + t)*KH + r)*KW + s over the
+// group's channels; 4 columns per thread so that both limb planes are written
+// with 32-bit stores.
 template <typename T>
 __global__ void im2col_quant_kernel(const T* __restrict__ x, ConvGeom g, int64_t K, int64_t ld,
                                     const float* __restrict__ amax, int8_t* __restrict__ limbs) {
-    const int64_t P = g.OH * g.OW;
+    const int64_t P = g.OD * g.OH * g.OW;
     const int64_t k4n = ld / 4;
     const int64_t total = g.N * g.groups * P * k4n;
     const float inv = quant_inv(amax[0]);
     const int64_t cg = g.C / g.groups;
     const int64_t khw = g.KH * g.KW;
+    const int64_t kdhw = g.KD * khw;
     for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
          idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int64_t k4 = idx % k4n;
@@ -66,21 +71,23 @@ __global__ void im2col_quant_kernel(const T* __restrict__ x, ConvGeom g, int64_t
         const int64_t p = rest % P;
         const int64_t b = rest / P;
         const int64_t n = b / g.groups, grp = b % g.groups;
-        const int64_t oh = p / g.OW, ow = p % g.OW;
+        const int64_t ow = p % g.OW, oh = (p / g.OW) % g.OH, od = p / (g.OW * g.OH);
         unsigned hi = 0, lo = 0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int64_t k = k4 * 4 + j;
             int q = 0;
             if (k < K) {
-                const int64_t c = k / khw;
-                const int64_t rs = k - c * khw;
+                const int64_t c = k / kdhw;
+                const int64_t trs = k - c * kdhw;
+                const int64_t t = trs / khw, rs = trs - t * khw;
                 const int64_t r = rs / g.KW, s = rs - r * g.KW;
+                const int64_t id = od * g.sd - g.pd + t * g.dd;
                 const int64_t ih = oh * g.sh - g.ph + r * g.dh;
                 const int64_t iw = ow * g.sw - g.pw + s * g.dw;
-                if (ih >= 0 && ih < g.H && iw >= 0 && iw < g.W) {
+                if (id >= 0 && id < g.D && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W) {
                     const int64_t ci = grp * cg + c;
-                    q = quant_one(ldx<T>(x, ((n * g.C + ci) * g.H + ih) * g.W + iw), inv);
+                    q = quant_one(ldx<T>(x, (((n * g.C + ci) * g.D + id) * g.H + ih) * g.W + iw), inv);
                 }
             }
             hi |= (static_cast<unsigned>(q >> 8) & 0xFFu) << (8 * j);
@@ -243,33 +250,50 @@ int grid_1d(int64_t n, int threads) {
     return static_cast<int>(std::max<int64_t>(1, std::min(g, cap)));
 }
 
-int geometry(const tk_conv2d_desc_t& d, ConvGeom& g) {
-    TK_CHECK_ARG(d.dtype == TK_DTYPE_F16 || d.dtype == TK_DTYPE_F32, "conv2d: bad dtype");
-    TK_CHECK_ARG(d.n >= 0 && d.c > 0 && d.h > 0 && d.w > 0 && d.f > 0 && d.kh > 0 && d.kw > 0,
-                 "conv2d: bad shape");
-    TK_CHECK_ARG(d.stride_h > 0 && d.stride_w > 0 && d.dil_h > 0 && d.dil_w > 0 && d.pad_h >= 0 &&
-                     d.pad_w >= 0,
-                 "conv2d: bad stride/padding/dilation");
+int geometry(const tk_conv3d_desc_t& d, ConvGeom& g) {
+    TK_CHECK_ARG(d.dtype == TK_DTYPE_F16 || d.dtype == TK_DTYPE_F32, "conv: bad dtype");
+    TK_CHECK_ARG(d.n >= 0 && d.c > 0 && d.d > 0 && d.h > 0 && d.w > 0 && d.f > 0 && d.kd > 0 &&
+                     d.kh > 0 && d.kw > 0,
+                 "conv: bad shape");
+    TK_CHECK_ARG(d.stride_d > 0 && d.stride_h > 0 && d.stride_w > 0 && d.dil_d > 0 && d.dil_h > 0 &&
+                     d.dil_w > 0 && d.pad_d >= 0 && d.pad_h >= 0 && d.pad_w >= 0,
+                 "conv: bad stride/padding/dilation");
     TK_CHECK_ARG(d.groups > 0 && d.c % d.groups == 0 && d.f % d.groups == 0,
-                 "conv2d: channels must be divisible by groups");
+                 "conv: channels must be divisible by groups");
     g = {d.n, d.c, d.h, d.w, d.f, d.kh, d.kw, d.stride_h, d.stride_w, d.pad_h, d.pad_w,
-         d.dil_h, d.dil_w, d.groups, 0, 0};
+         d.dil_h, d.dil_w, d.groups, 0, 0, d.d, d.kd, d.stride_d, d.pad_d, d.dil_d, 0};
+    g.OD = (d.d + 2 * d.pad_d - d.dil_d * (d.kd - 1) - 1) / d.stride_d + 1;
     g.OH = (d.h + 2 * d.pad_h - d.dil_h * (d.kh - 1) - 1) / d.stride_h + 1;
     g.OW = (d.w + 2 * d.pad_w - d.dil_w * (d.kw - 1) - 1) / d.stride_w + 1;
-    TK_CHECK_ARG(g.OH > 0 && g.OW > 0, "conv2d: non-positive output size");
+    TK_CHECK_ARG(g.OD > 0 && g.OH > 0 && g.OW > 0, "conv: non-positive output size");
     return TK_OK;
 }
 
-bool is_depthwise(const ConvGeom& g) { return g.groups == g.C && g.groups > 1; }
+tk_conv3d_desc_t as_3d(const tk_conv2d_desc_t& d) {
+    tk_conv3d_desc_t e = {};
+    e.dtype = d.dtype;
+    e.n = d.n; e.c = d.c; e.d = 1; e.h = d.h; e.w = d.w;
+    e.f = d.f; e.kd = 1; e.kh = d.kh; e.kw = d.kw;
+    e.stride_d = 1; e.stride_h = d.stride_h; e.stride_w = d.stride_w;
+    e.pad_d = 0; e.pad_h = d.pad_h; e.pad_w = d.pad_w;
+    e.dil_d = 1; e.dil_h = d.dil_h; e.dil_w = d.dil_w;
+    e.groups = d.groups;
+    e.x = d.x; e.weight = d.weight; e.bias = d.bias; e.out = d.out;
+    e.amax_x = d.amax_x; e.amax_w = d.amax_w;
+    return e;
+}
+
+bool is_2d(const ConvGeom& g) { return g.D == 1 && g.KD == 1 && g.pd == 0; }
+bool is_depthwise(const ConvGeom& g) { return is_2d(g) && g.groups == g.C && g.groups > 1; }
 // Implicit GEMM on the tensor cores: one group, unit stride (any padding and
 // dilation), and per-tap channel depth within the exact-accumulation limit.
 bool is_implicit(const ConvGeom& g) {
-    return g.groups == 1 && g.sh == 1 && g.sw == 1 && round_up(g.C, 64) * g.KH * g.KW <= 32768 &&
-           g.N * g.H < (1LL << 31);
+    return g.groups == 1 && g.sd == 1 && g.sh == 1 && g.sw == 1 &&
+           round_up(g.C, 64) * g.KD * g.KH * g.KW <= 32768 && g.N * g.D * g.H < (1LL << 31);
 }
 bool is_pointwise(const ConvGeom& g) {
-    return g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0 &&
-           g.groups == 1;
+    return g.KD == 1 && g.KH == 1 && g.KW == 1 && g.sd == 1 && g.sh == 1 && g.sw == 1 && g.pd == 0 &&
+           g.ph == 0 && g.pw == 0 && g.groups == 1;
 }
 
 struct ConvLayout {
@@ -279,9 +303,9 @@ struct ConvLayout {
 
 ConvLayout conv_layout(const ConvGeom& g) {
     ConvLayout L;
-    L.K = (g.C / g.groups) * g.KH * g.KW;
+    L.K = (g.C / g.groups) * g.KD * g.KH * g.KW;
     L.ld = static_cast<int64_t>(round_up(static_cast<size_t>(L.K), 16));
-    const int64_t P = g.OH * g.OW;
+    const int64_t P = g.OD * g.OH * g.OW;
     L.off_amax = 0;
     L.off_la = 1024;
     if (is_depthwise(g)) {
@@ -291,7 +315,7 @@ ConvLayout conv_layout(const ConvGeom& g) {
     }
     if (is_implicit(g)) {
         L.off_lb = L.off_la;
-        L.total = L.off_la + conv_tc_workspace(g.N, g.C, g.H, g.W, g.F, g.KH, g.KW, g.ph, g.pw);
+        L.total = L.off_la + conv_tc_workspace(g.N, g.C, g.D, g.H, g.W, g.F, g.KD, g.KH, g.KW, g.ph, g.pw);
         return L;
     }
     L.off_lb = round_up(L.off_la + static_cast<size_t>(g.N * g.groups * 2 * P * L.ld), 1024);
@@ -304,7 +328,7 @@ ConvLayout conv_layout(const ConvGeom& g) {
 
 extern "C" {
 
-size_t tk_conv2d_workspace_size(const tk_conv2d_desc_t* desc) {
+size_t tk_conv3d_workspace_size(const tk_conv3d_desc_t* desc) {
     using namespace tk;
     if (desc == nullptr) return 0;
     ConvGeom g;
@@ -312,38 +336,52 @@ size_t tk_conv2d_workspace_size(const tk_conv2d_desc_t* desc) {
     return conv_layout(g).total;
 }
 
+size_t tk_conv2d_workspace_size(const tk_conv2d_desc_t* desc) {
+    if (desc == nullptr) return 0;
+    const tk_conv3d_desc_t e = tk::as_3d(*desc);
+    return tk_conv3d_workspace_size(&e);
+}
+
 int tk_conv2d_q16(const tk_conv2d_desc_t* desc, void* workspace, size_t workspace_bytes,
-                  void* stream_) {
+                  void* stream) {
     using namespace tk;
     TK_CHECK_ARG(desc != nullptr, "conv2d: desc is NULL");
-    const tk_conv2d_desc_t& d = *desc;
+    const tk_conv3d_desc_t e = as_3d(*desc);
+    return tk_conv3d_q16(&e, workspace, workspace_bytes, stream);
+}
+
+int tk_conv3d_q16(const tk_conv3d_desc_t* desc, void* workspace, size_t workspace_bytes,
+                  void* stream_) {
+    using namespace tk;
+    TK_CHECK_ARG(desc != nullptr, "conv: desc is NULL");
+    const tk_conv3d_desc_t& d = *desc;
     ConvGeom g;
     int rc = geometry(d, g);
     if (rc) return rc;
     if (g.N == 0) return TK_OK;
-    TK_CHECK_ARG(d.x && d.weight && d.out, "conv2d: NULL pointer");
+    TK_CHECK_ARG(d.x && d.weight && d.out, "conv: NULL pointer");
     const ConvLayout L = conv_layout(g);
     TK_CHECK_ARG(workspace != nullptr && workspace_bytes >= L.total &&
                      reinterpret_cast<uintptr_t>(workspace) % 1024 == 0,
-                 "conv2d: workspace must be >= %zu bytes and 1024-byte aligned", L.total);
-    TK_CHECK_ARG(L.K <= 32768, "conv2d: C/groups*KH*KW = %lld exceeds 32768", (long long)L.K);
+                 "conv: workspace must be >= %zu bytes and 1024-byte aligned", L.total);
+    TK_CHECK_ARG(L.K <= 32768, "conv: C/groups*KD*KH*KW = %lld exceeds 32768", (long long)L.K);
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     float* amax = reinterpret_cast<float*>(ws + L.off_amax);  // [0] input, [1] weight
     const float* ax = d.amax_x;
     const float* aw = d.amax_w;
     if (ax == nullptr) {
-        rc = amax_launch(d.dtype, d.x, 1, 0, g.N * g.C * g.H * g.W, amax, stream);
+        rc = amax_launch(d.dtype, d.x, 1, 0, g.N * g.C * g.D * g.H * g.W, amax, stream);
         if (rc) return rc;
         ax = amax;
     }
     if (aw == nullptr) {
-        rc = amax_launch(d.dtype, d.weight, 1, 0, g.F * (g.C / g.groups) * g.KH * g.KW, amax + 1,
+        rc = amax_launch(d.dtype, d.weight, 1, 0, g.F * (g.C / g.groups) * g.KD * g.KH * g.KW, amax + 1,
                          stream);
         if (rc) return rc;
         aw = amax + 1;
     }
-    const int64_t P = g.OH * g.OW;
+    const int64_t P = g.OD * g.OH * g.OW;
     if (is_depthwise(g) && g.F == g.C && g.H * g.W <= kDwFlatElems / 2 &&
         g.KH * g.KW * (kDwFlatElems / (g.H * g.W)) <= kDwFlatElems / 4) {
         const int ppb = static_cast<int>(kDwFlatElems / (g.H * g.W));
@@ -387,12 +425,13 @@ int tk_conv2d_q16(const tk_conv2d_desc_t* desc, void* workspace, size_t workspac
         return launch_status("conv2d depthwise");
     }
     if (is_implicit(g))
-        return conv_tc(d.dtype, d.x, d.weight, d.bias, d.out, g.N, g.C, g.H, g.W, g.F, g.KH, g.KW,
-                       g.ph, g.pw, g.dh, g.dw, g.OH, g.OW, ax, aw, ws + L.off_la, stream);
+        return conv_tc(d.dtype, d.x, d.weight, d.bias, d.out, g.N, g.C, g.D, g.H, g.W, g.F, g.KD, g.KH,
+                       g.KW, g.pd, g.ph, g.pw, g.dd, g.dh, g.dw, g.OD, g.OH, g.OW, ax, aw, ws + L.off_la,
+                       stream);
     int8_t* la = reinterpret_cast<int8_t*>(ws + L.off_la);  // patches [N*groups][2][P][ld]
     int8_t* lb = reinterpret_cast<int8_t*>(ws + L.off_lb);  // weights [groups][2][F/g][ld]
     const int64_t fg = g.F / g.groups;
-    // weights: contiguous OIHW, one [F/g, K] slice per group
+    // weights: contiguous OI[D]HW, one [F/g, K] slice per group
     rc = quantize_limbs_launch(d.dtype, d.weight, g.groups, fg, L.K, fg * L.K, L.K, 1, aw, 0, lb,
                                stream);
     if (rc) return rc;

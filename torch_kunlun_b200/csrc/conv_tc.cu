@@ -1,22 +1,25 @@
-// conv_tc.cu -- implicit-GEMM int16-quantised conv2d on sm_100a tensor cores.
+// conv_tc.cu -- implicit-GEMM int16-quantised conv2d / conv3d on sm_100a
+// tensor cores.
 //
 // Replaces baidu::xpu::api::conv2d<T,T,T,TGEMM> plus the bias broadcast_add
-// of conv2d_impl (csrc/ops.cpp:237-285) for groups == 1, stride 1 (any
-// padding and dilation).  Semantics are those of the explicit path in
+// of conv2d_impl (csrc/ops.cpp:237-285), and xdnn conv3d of conv3d
+// (csrc/ops_nn_extra.cpp:88-121), for groups == 1, stride 1 (any padding and
+// dilation).  A 2-D convolution is the 3-D one with D = KD = 1.  Semantics are those of the explicit path in
 // conv.cu: one max-abs scale for the whole input and one for the whole
 // weight, exact integer MAC, T(acc * s), then the bias added and rounded.
 //
 // Data flow (no patch matrix in HBM):
-//   x_limbs_kernel   NCHW input -> quantised NHWC limb rows: per pixel, per
+//   x_limbs_kernel   NC(D)HW input -> quantised N(D)HWC limb rows: per pixel, per
 //                    group of 64 channels, 128 bytes [hi of the 64 | lo of
 //                    the 64] (hi = q >> 8 signed, lo = q & 255 unsigned);
-//   w_limbs_kernel   OIHW weight -> [F][KH][KW][channel groups] limb rows of
+//   w_limbs_kernel   OI(D)HW weight -> [F][KD][KH][KW][channel groups] limb rows of
 //                    the same 128-byte form;
 //   conv_tc_kernel   one CTA per SM, persistent over output tiles of
-//                    TH x TW pixels of one image x BN filters.  Each K step
-//                    is one (tap, 64-channel group): a 4-D TMA box
-//                    {128 B, TW, TH, 1} at (group, ow0 + kw*dw - pw,
-//                    oh0 + kh*dh - ph, n) gathers the shifted input window
+//                    TH x TW pixels of one (image, output depth) x BN
+//                    filters.  Each K step is one (tap, 64-channel group):
+//                    a 5-D TMA box {128 B, TW, TH, 1, 1} at (group,
+//                    ow0 + kw*dw - pw, oh0 + kh*dh - ph, od + kd*dd - pd, n)
+//                    gathers the shifted input window
 //                    (out-of-range rows and columns -- the padding -- load as
 //                    zero), a 2-D box brings the BN filters' rows, and four
 //                    tcgen05 kind::i8 MMAs per 32-byte sub-block build the
@@ -76,7 +79,7 @@ using ConvNarrow = ConvCfg<64, 2, 8>;
 using ConvWide = ConvCfg<128, 1, 6>;
 
 struct ConvTcParams {
-    int N, F, OH, OW, KH, KW, ph, pw, dh, dw, Cg;
+    int N, F, OD, OH, OW, KD, KH, KW, pd, ph, pw, dd, dh, dw, Cg;
     int TH, TW, tiles_h, tiles_w, tiles_f, tiles;
     int num_kb;
     const float* amax_x;
@@ -86,13 +89,16 @@ struct ConvTcParams {
     unsigned* err;
 };
 
-__device__ __forceinline__ void decode(const ConvTcParams& p, int t, int& n, int& oh0, int& ow0, int& fb) {
+__device__ __forceinline__ void decode(const ConvTcParams& p, int t, int& n, int& od, int& oh0, int& ow0,
+                                       int& fb) {
     fb = t % p.tiles_f;
     int r = t / p.tiles_f;
     const int tw = r % p.tiles_w;
     r /= p.tiles_w;
     const int th = r % p.tiles_h;
-    n = r / p.tiles_h;
+    r /= p.tiles_h;
+    od = r % p.OD;
+    n = r / p.OD;
     oh0 = th * p.TH;
     ow0 = tw * p.TW;
 }
@@ -152,9 +158,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
         for (int s = 0; s < STAGES; ++s) { used[s] = false; last_phase[s] = 0; }
         bool ok = true;
         for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
-            int n, oh0, ow0, fb;
-            decode(p, t, n, oh0, ow0, fb);
-            int cg = 0, kw = 0, kh = 0;
+            int n, od, oh0, ow0, fb;
+            decode(p, t, n, od, oh0, ow0, fb);
+            int cg = 0, kw = 0, kh = 0, kd = 0;
             for (int kb = 0; kb < p.num_kb; ++kb) {
                 if (!mbar_wait_bounded(smem_u32(empty_bar + stage), phase ^ 1u, abort_flag, p.err,
                                        kDevErrWaitEmpty)) {
@@ -165,8 +171,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
                     const uint32_t fbar = smem_u32(full_bar + stage);
                     uint8_t* sb = smem + stage * C::STAGE_BYTES;
                     mbar_arrive_expect_tx(fbar, a_bytes + C::B_BYTES);
-                    tma_load_4d(smem_u32(sb), &tmX, fbar, cg * KB, ow0 + kw * p.dw - p.pw,
-                                oh0 + kh * p.dh - p.ph, n);
+                    tma_load_5d(smem_u32(sb), &tmX, fbar, cg * KB, ow0 + kw * p.dw - p.pw,
+                                oh0 + kh * p.dh - p.ph, od + kd * p.dd - p.pd, n);
                     tma_load_3d(smem_u32(sb + A_BYTES), &tmW, fbar, kb * KB, fb * BN, 0);
                 }
                 __syncwarp();
@@ -175,7 +181,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
                 if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 if (++cg == p.Cg) {
                     cg = 0;
-                    if (++kw == p.KW) { kw = 0; ++kh; }
+                    if (++kw == p.KW) {
+                        kw = 0;
+                        if (++kh == p.KH) { kh = 0; ++kd; }
+                    }
                 }
             }
         }
@@ -240,13 +249,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
         const int row = quarter * 32 + lane;
         const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
         const double s = dequant_scale(__ldg(p.amax_x), __ldg(p.amax_w));
-        const int64_t plane = static_cast<int64_t>(p.OH) * p.OW;
+        const int64_t plane = static_cast<int64_t>(p.OD) * p.OH * p.OW;
         const int th = row / p.TW, tw = row - (row / p.TW) * p.TW;
         constexpr int ES = DT == 0 ? 2 : 4;
         int local = 0;
         for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++local) {
-            int n, oh0, ow0, fb;
-            decode(p, t, n, oh0, ow0, fb);
+            int n, od, oh0, ow0, fb;
+            decode(p, t, n, od, oh0, ow0, fb);
             const int buf = local % NBUF;
             const uint32_t acc_phase = static_cast<uint32_t>(local / NBUF) & 1u;
             if (!mbar_wait_bounded(smem_u32(acc_full + buf), acc_phase, abort_flag, p.err,
@@ -256,7 +265,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
             const uint32_t t_buf = t_row + buf * C::BUF_COLS;
             const int oh = oh0 + th, ow = ow0 + tw;
             const bool pix_ok = row < p.TH * p.TW && oh < p.OH && ow < p.OW;
-            const int64_t pix = static_cast<int64_t>(oh) * p.OW + ow;
+            const int64_t pix = (static_cast<int64_t>(od) * p.OH + oh) * p.OW + ow;
 #pragma unroll 1
             for (int c = sub * (BN / 64); c < (sub + 1) * (BN / 64); ++c) {  // 16-column blocks
                 uint32_t hh[16], mid[16], ll[16];
@@ -791,19 +800,20 @@ bool window_fits(int64_t KH, int64_t KW, int64_t dh, int64_t dw, int64_t Wp) {
 
 // Workspace bytes of the implicit-GEMM path (limb rows of the zero-padded x
 // and of w).
-size_t conv_tc_workspace(int64_t N, int64_t C, int64_t H, int64_t W, int64_t F, int64_t KH, int64_t KW,
-                         int64_t ph, int64_t pw) {
+size_t conv_tc_workspace(int64_t N, int64_t C, int64_t D, int64_t H, int64_t W, int64_t F, int64_t KD,
+                         int64_t KH, int64_t KW, int64_t ph, int64_t pw) {
     const int64_t Cg = ceil_div(C, 64);
-    return round_up(static_cast<size_t>(N * (H + 2 * ph) * (W + 2 * pw) * Cg * 128), 1024) +
-           round_up(static_cast<size_t>(F * KH * KW * Cg * 128), 1024);
+    return round_up(static_cast<size_t>(N * D * (H + 2 * ph) * (W + 2 * pw) * Cg * 128), 1024) +
+           round_up(static_cast<size_t>(F * KD * KH * KW * Cg * 128), 1024);
 }
 
-// Implicit-GEMM conv2d for groups == 1 and stride 1; `ws` is 1024-aligned
-// with conv_tc_workspace(...) bytes; amax_x / amax_w are device scalars.
+// Implicit-GEMM conv (2-D with D = KD = 1, or 3-D) for groups == 1 and
+// stride 1; `ws` is 1024-aligned with conv_tc_workspace(...) bytes;
+// amax_x / amax_w are device scalars.
 int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, void* out, int64_t N,
-            int64_t C, int64_t H, int64_t W, int64_t F, int64_t KH, int64_t KW, int64_t ph, int64_t pw,
-            int64_t dh, int64_t dw, int64_t OH, int64_t OW, const float* amax_x, const float* amax_w,
-            uint8_t* ws, cudaStream_t stream) {
+            int64_t C, int64_t D, int64_t H, int64_t W, int64_t F, int64_t KD, int64_t KH, int64_t KW,
+            int64_t pd, int64_t ph, int64_t pw, int64_t dd, int64_t dh, int64_t dw, int64_t OD, int64_t OH,
+            int64_t OW, const float* amax_x, const float* amax_w, uint8_t* ws, cudaStream_t stream) {
     const int dev = current_device();
     const int64_t Cg = ceil_div(C, 64);
     const int64_t Hp = H + 2 * ph, Wp = W + 2 * pw;
@@ -811,33 +821,37 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
     // Window variant for up to 64 filters and a real halo.  A 1x1 filter has
     // no halo, and with 128-filter tiles the per-tap ring measured faster
     // (3x3 256->256 @14, batch 64: 77 vs 83 us).
-    const bool win = F <= 64 && KH * KW > 1 && window_fits(KH, KW, dh, dw, Wp) &&
+    const bool win = D == 1 && KD == 1 && F <= 64 && KH * KW > 1 && window_fits(KH, KW, dh, dw, Wp) &&
                      N * Hp * Wp < (1LL << 31);
-    const int64_t sh = win ? Hp : H, sw = win ? Wp : W;  // stored plane
+    // stored rows per image: the padded plane (window variant, D == 1) or the
+    // unpadded volume D*H*W (as D*H rows of W pixels)
+    const int64_t sh = win ? Hp : D * H, sw = win ? Wp : W;
     const size_t x_bytes = static_cast<size_t>(N * sh * sw * Cg * 128);
     uint8_t* xl = ws;
     uint8_t* wl = ws + round_up(x_bytes, 1024);
     if (win && (ph > 0 || pw > 0)) TK_CUDA_TRY(cudaMemsetAsync(xl, 0, x_bytes, stream));
-    const int64_t runs = ceil_div(H * W, XQ_W);
-    TK_CHECK_ARG(N * runs * Cg < (1LL << 31) && H * W < (1LL << 31), "conv2d: input too large");
+    const int64_t DHW = D * H * W;  // the image's flattened volume (rows of limbs)
+    const int64_t runs = ceil_div(DHW, XQ_W);
+    TK_CHECK_ARG(N * runs * Cg < (1LL << 31) && DHW < (1LL << 31), "conv: input too large");
     const unsigned xgrid = static_cast<unsigned>(N * runs * Cg);
     const size_t es = dtype_size(dtype);
-    const int xvec = ((H * W) % static_cast<int64_t>(16 / es) == 0 &&
+    const int xvec = (DHW % static_cast<int64_t>(16 / es) == 0 &&
                       reinterpret_cast<uintptr_t>(x) % 16 == 0) ? 1 : 0;
     const int oph = win ? static_cast<int>(ph) : 0, opw = win ? static_cast<int>(pw) : 0;
-    const unsigned wgrid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(F * KH * KW * Cg * 4, 256), 4096)));
+    const int64_t taps = KD * KH * KW;
+    const unsigned wgrid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(F * taps * Cg * 4, 256), 4096)));
     if (dtype == TK_DTYPE_F16) {
         x_limbs_kernel<__half><<<xgrid, XQ_THREADS, 0, stream>>>(
-            static_cast<const __half*>(x), (int)C, H * W, (int)W, oph, opw, (int)sh, (int)sw, (int)Cg, xvec,
+            static_cast<const __half*>(x), (int)C, DHW, (int)W, oph, opw, (int)sh, (int)sw, (int)Cg, xvec,
             amax_x, xl);
-        w_limbs_kernel<__half><<<wgrid, 256, 0, stream>>>(static_cast<const __half*>(w), (int)F, (int)C, (int)KH,
-                                                          (int)KW, (int)Cg, amax_w, wl);
+        w_limbs_kernel<__half><<<wgrid, 256, 0, stream>>>(static_cast<const __half*>(w), (int)F, (int)C,
+                                                          (int)(KD * KH), (int)KW, (int)Cg, amax_w, wl);
     } else {
         x_limbs_kernel<float><<<xgrid, XQ_THREADS, 0, stream>>>(
-            static_cast<const float*>(x), (int)C, H * W, (int)W, oph, opw, (int)sh, (int)sw, (int)Cg, xvec,
+            static_cast<const float*>(x), (int)C, DHW, (int)W, oph, opw, (int)sh, (int)sw, (int)Cg, xvec,
             amax_x, xl);
-        w_limbs_kernel<float><<<wgrid, 256, 0, stream>>>(static_cast<const float*>(w), (int)F, (int)C, (int)KH,
-                                                         (int)KW, (int)Cg, amax_w, wl);
+        w_limbs_kernel<float><<<wgrid, 256, 0, stream>>>(static_cast<const float*>(w), (int)F, (int)C,
+                                                         (int)(KD * KH), (int)KW, (int)Cg, amax_w, wl);
     }
     int rc = launch_status("conv2d limbs");
     if (rc) return rc;
@@ -848,7 +862,7 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
     const int BN = narrow ? ConvNarrow::BN : ConvWide::BN;
     CUtensorMap tx, tw;
     {
-        const uint64_t row = static_cast<uint64_t>(KH * KW * Cg) * 128;
+        const uint64_t row = static_cast<uint64_t>(taps * Cg) * 128;
         cuuint64_t dims[3] = {row, static_cast<cuuint64_t>(F), 1};
         cuuint64_t strides[2] = {row, row * F};
         cuuint32_t box[3] = {128, static_cast<cuuint32_t>(BN), 1};
@@ -900,17 +914,19 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
     }
 
     ConvTcParams p;
-    p.N = (int)N; p.F = (int)F; p.OH = (int)OH; p.OW = (int)OW; p.KH = (int)KH; p.KW = (int)KW;
-    p.ph = (int)ph; p.pw = (int)pw; p.dh = (int)dh; p.dw = (int)dw; p.Cg = (int)Cg;
+    p.N = (int)N; p.F = (int)F; p.OD = (int)OD; p.OH = (int)OH; p.OW = (int)OW;
+    p.KD = (int)KD; p.KH = (int)KH; p.KW = (int)KW;
+    p.pd = (int)pd; p.ph = (int)ph; p.pw = (int)pw; p.dd = (int)dd; p.dh = (int)dh; p.dw = (int)dw;
+    p.Cg = (int)Cg;
     p.TW = static_cast<int>(std::min<int64_t>(OW, BM));
     p.TH = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(BM / p.TW, OH)));
     p.tiles_h = static_cast<int>(ceil_div(OH, p.TH));
     p.tiles_w = static_cast<int>(ceil_div(OW, p.TW));
     p.tiles_f = static_cast<int>(tiles_f);
-    const int64_t tiles = N * p.tiles_h * p.tiles_w * p.tiles_f;
-    TK_CHECK_ARG(tiles < (1LL << 31), "conv2d: too many tiles");
+    const int64_t tiles = N * OD * p.tiles_h * p.tiles_w * p.tiles_f;
+    TK_CHECK_ARG(tiles < (1LL << 31), "conv: too many tiles");
     p.tiles = static_cast<int>(tiles);
-    p.num_kb = static_cast<int>(KH * KW * Cg);
+    p.num_kb = static_cast<int>(taps * Cg);
     p.amax_x = amax_x;
     p.amax_w = amax_w;
     p.bias = bias;
@@ -918,12 +934,12 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
     p.err = device_error_word(dev);
     {
         const uint64_t row = static_cast<uint64_t>(Cg) * 128;
-        cuuint64_t dims[4] = {row, static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H),
-                              static_cast<cuuint64_t>(N)};
-        cuuint64_t strides[3] = {row, row * W, row * W * H};
-        cuuint32_t box[4] = {128, static_cast<cuuint32_t>(p.TW), static_cast<cuuint32_t>(p.TH), 1};
-        cuuint32_t estr[4] = {1, 1, 1, 1};
-        CUresult r = enc(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, xl, dims, strides, box, estr,
+        cuuint64_t dims[5] = {row, static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H),
+                              static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(N)};
+        cuuint64_t strides[4] = {row, row * W, row * W * H, row * W * H * D};
+        cuuint32_t box[5] = {128, static_cast<cuuint32_t>(p.TW), static_cast<cuuint32_t>(p.TH), 1, 1};
+        cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+        CUresult r = enc(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, xl, dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) TK_FAIL(TK_ERR_CUDA, "conv2d input tensor map failed (%d)", (int)r);

@@ -168,51 +168,66 @@ at::Tensor baddbmm(const at::Tensor& self, const at::Tensor& batch1, const at::T
     return out;
 }
 
-std::vector<int64_t> pair_of(at::IntArrayRef v, int64_t dflt) {
-    if (v.empty()) return {dflt, dflt};
-    if (v.size() == 1) return {v[0], v[0]};
-    TORCH_CHECK(v.size() == 2, "kunlun conv2d expects 1 or 2 element arrays");
-    return {v[0], v[1]};
+// Per-axis convolution parameter: [v] broadcasts, [] takes the default.
+std::vector<int64_t> axis_param(at::IntArrayRef v, int64_t k, int64_t dflt, const char* what) {
+    if (v.empty()) return std::vector<int64_t>(k, dflt);
+    if (v.size() == 1) return std::vector<int64_t>(k, v[0]);
+    TORCH_CHECK(static_cast<int64_t>(v.size()) == k, "kunlun conv: ", what, " needs 1 or ", k, " values");
+    return v.vec();
 }
 
-at::Tensor conv2d_impl(const at::Tensor& input, const at::Tensor& weight,
-                       const std::optional<at::Tensor>& bias, at::IntArrayRef stride,
-                       at::IntArrayRef padding, at::IntArrayRef dilation, int64_t groups,
-                       const float* amax_x = nullptr, const float* amax_w = nullptr) {
-    check_operand(weight, input, "conv2d");
-    const bool batched = input.dim() == 4;
-    TORCH_CHECK((input.dim() == 4 || input.dim() == 3) && weight.dim() == 4,
-                "kunlun conv2d requires NCHW (or CHW) input and OIHW weight");
+// Quantised 2-D or 3-D convolution (NCHW / NCDHW, a CHW input is one
+// image): one tk_conv3d_q16 call, a 2-D convolution being the 3-D one with
+// depth 1.  amax_x / amax_w override the per-tensor scales (device fp32).
+at::Tensor conv_impl(const at::Tensor& input, const at::Tensor& weight,
+                     const std::optional<at::Tensor>& bias, at::IntArrayRef stride,
+                     at::IntArrayRef padding, at::IntArrayRef dilation, int64_t groups,
+                     const float* amax_x = nullptr, const float* amax_w = nullptr) {
+    check_operand(weight, input, "conv");
+    const int64_t k = weight.dim() - 2;
+    TORCH_CHECK((k == 2 || k == 3) && (input.dim() == k + 2 || (k == 2 && input.dim() == 3)),
+                "kunlun conv requires NCHW (or CHW) input with OIHW weight, or NCDHW with OIDHW");
+    const bool batched = input.dim() == k + 2;
     at::Tensor x = (batched ? input : input.unsqueeze(0)).contiguous();
     at::Tensor w = weight.contiguous();
-    const auto s = pair_of(stride, 1), p = pair_of(padding, 0), dl = pair_of(dilation, 1);
-    tk_conv2d_desc_t d = {};
+    const auto s = axis_param(stride, k, 1, "stride"), p = axis_param(padding, k, 0, "padding"),
+               dl = axis_param(dilation, k, 1, "dilation");
+    const int64_t o = k == 3 ? 0 : 1;  // 2-D: the depth axis is absent
+    tk_conv3d_desc_t d = {};
     d.dtype = tk_dtype(x.scalar_type());
     d.n = x.size(0);
     d.c = x.size(1);
-    d.h = x.size(2);
-    d.w = x.size(3);
+    d.d = k == 3 ? x.size(2) : 1;
+    d.h = x.size(3 - o);
+    d.w = x.size(4 - o);
     d.f = w.size(0);
-    d.kh = w.size(2);
-    d.kw = w.size(3);
-    d.stride_h = s[0];
-    d.stride_w = s[1];
-    d.pad_h = p[0];
-    d.pad_w = p[1];
-    d.dil_h = dl[0];
-    d.dil_w = dl[1];
+    d.kd = k == 3 ? w.size(2) : 1;
+    d.kh = w.size(3 - o);
+    d.kw = w.size(4 - o);
+    d.stride_d = k == 3 ? s[0] : 1;
+    d.stride_h = s[1 - o];
+    d.stride_w = s[2 - o];
+    d.pad_d = k == 3 ? p[0] : 0;
+    d.pad_h = p[1 - o];
+    d.pad_w = p[2 - o];
+    d.dil_d = k == 3 ? dl[0] : 1;
+    d.dil_h = dl[1 - o];
+    d.dil_w = dl[2 - o];
     d.groups = groups;
     TORCH_CHECK(groups > 0 && d.c % groups == 0 && w.size(1) == d.c / groups,
-                "kunlun conv2d: weight/input channel mismatch");
-    const int64_t oh = (d.h + 2 * d.pad_h - d.dil_h * (d.kh - 1) - 1) / d.stride_h + 1;
-    const int64_t ow = (d.w + 2 * d.pad_w - d.dil_w * (d.kw - 1) - 1) / d.stride_w + 1;
-    TORCH_CHECK(oh > 0 && ow > 0, "kunlun conv2d produced non-positive output shape");
-    at::Tensor out = at::empty({d.n, d.f, oh, ow}, x.options());
+                "kunlun conv: weight/input channel mismatch");
+    std::vector<int64_t> shape = {d.n, d.f};
+    for (int64_t i = 0; i < k; ++i) {
+        const int64_t o_i = (x.size(2 + i) + 2 * p[i] - dl[i] * (w.size(2 + i) - 1) - 1) / s[i] + 1;
+        TORCH_CHECK(o_i > 0, "kunlun conv produced non-positive output shape");
+        shape.push_back(o_i);
+    }
+    at::Tensor out = at::empty(shape, x.options());
     at::Tensor b;
     if (bias.has_value() && bias->defined()) {
         b = bias->contiguous();
-        check_operand(b, x, "conv2d bias");
-        TORCH_CHECK(b.numel() == d.f, "kunlun conv2d bias size mismatch");
+        check_operand(b, x, "conv bias");
+        TORCH_CHECK(b.numel() == d.f, "kunlun conv bias size mismatch");
         d.bias = b.data_ptr();
     }
     d.x = x.data_ptr();
@@ -223,9 +238,9 @@ at::Tensor conv2d_impl(const at::Tensor& input, const at::Tensor& weight,
     const int dev = x.device().index();
     DeviceScope g(dev);
     if (out.numel() > 0) {
-        const size_t ws_bytes = tk_conv2d_workspace_size(&d);
+        const size_t ws_bytes = tk_conv3d_workspace_size(&d);
         at::Tensor ws = workspace(ws_bytes, x.device());
-        check_tk(tk_conv2d_q16(&d, aligned_base(ws), ws_bytes, current_stream(dev)), "tk_conv2d_q16");
+        check_tk(tk_conv3d_q16(&d, aligned_base(ws), ws_bytes, current_stream(dev)), "tk_conv3d_q16");
     }
     return batched ? out : out.squeeze(0);
 }
@@ -233,109 +248,204 @@ at::Tensor conv2d_impl(const at::Tensor& input, const at::Tensor& weight,
 at::Tensor conv2d(const at::Tensor& input, const at::Tensor& weight,
                   const std::optional<at::Tensor>& bias, at::IntArrayRef stride,
                   at::IntArrayRef padding, at::IntArrayRef dilation, int64_t groups) {
-    return conv2d_impl(input, weight, bias, stride, padding, dilation, groups);
+    TORCH_CHECK(weight.dim() == 4, "kunlun conv2d requires an OIHW weight");
+    return conv_impl(input, weight, bias, stride, padding, dilation, groups);
+}
+
+// w [A, B, K...] with every spatial axis reversed, as a device strided copy
+// that reads the source with negative strides from its last tap.
+at::Tensor flip_spatial(const at::Tensor& w_in) {
+    at::Tensor w = w_in.contiguous();
+    at::Tensor out = at::empty(w.sizes(), w.options());
+    if (w.numel() == 0) return out;
+    const int64_t nd = w.dim();
+    std::vector<int64_t> sizes = w.sizes().vec(), dst = w.strides().vec(), src = dst;
+    int64_t last = 0;
+    for (int64_t i = 2; i < nd; ++i) {
+        src[i] = -dst[i];
+        last += (sizes[i] - 1) * dst[i];
+    }
+    const int dev = w.device().index();
+    DeviceScope g(dev);
+    const int t = tk_scalar_code(w.scalar_type());
+    check_tk(tk_copy_strided(out.data_ptr(), t,
+                             static_cast<const char*>(w.data_ptr()) + last * w.element_size(), t,
+                             static_cast<int>(nd), sizes.data(), dst.data(), src.data(), current_stream(dev)),
+             "tk_copy_strided");
+    return out;
+}
+
+// Correlation of the zero-inserted (stride), padded g [N, F, O...] with the
+// spatially flipped, in/out-swapped weight [F, C/groups, K...]: the input
+// gradient of conv(x, weight) for an x of spatial size `in_size`, and equally
+// the transposed convolution of g (the reference's conv2d_grad and
+// conv2d_transpose, csrc/autograd.cpp:621-682, csrc/ops_nn_extra.cpp:123-159).
+// One quantised convolution: inserting zeros changes neither operand's
+// max-abs, so every output keeps one exact sum and one rounding.  A padding
+// wider than the dilated kernel is a crop of the result.
+at::Tensor conv_input_grad(const at::Tensor& g_in, const at::Tensor& weight, const std::vector<int64_t>& in_size,
+                           const std::vector<int64_t>& s, const std::vector<int64_t>& p,
+                           const std::vector<int64_t>& dl, int64_t groups,
+                           const std::optional<at::Tensor>& bias = std::nullopt) {
+    const int64_t k = weight.dim() - 2;
+    at::Tensor g = g_in.contiguous();
+    const int64_t N = g.size(0), F = weight.size(0), Cg = weight.size(1), Fg = F / groups, C = Cg * groups;
+    std::vector<int64_t> zsize = {N, F}, pad(k), crop(k), ones(k, 1);
+    bool spread = false;
+    for (int64_t i = 0; i < k; ++i) {
+        const int64_t K = weight.size(2 + i), O = g.size(2 + i);
+        const int64_t e = in_size[i] + 2 * p[i] - dl[i] * (K - 1) - 1 - (O - 1) * s[i];
+        TORCH_CHECK(e >= 0, "kunlun conv input gradient: inconsistent sizes");
+        zsize.push_back((O - 1) * s[i] + 1 + e);
+        spread = spread || s[i] > 1 || e > 0;
+        const int64_t pi = dl[i] * (K - 1) - p[i];
+        pad[i] = std::max<int64_t>(pi, 0);
+        crop[i] = std::max<int64_t>(-pi, 0);
+    }
+    at::Tensor gz = g;
+    if (spread) {
+        gz = at::zeros(zsize, g.options());
+        at::Tensor view = gz;
+        for (int64_t i = 0; i < k; ++i) view = view.slice(2 + i, 0, (g.size(2 + i) - 1) * s[i] + 1, s[i]);
+        view.copy_(g);
+    }
+    std::vector<int64_t> wv = {groups, Fg, Cg}, wr = {C, Fg};
+    for (int64_t i = 0; i < k; ++i) {
+        wv.push_back(weight.size(2 + i));
+        wr.push_back(weight.size(2 + i));
+    }
+    at::Tensor wt = flip_spatial(weight.contiguous().view(wv).transpose(1, 2).reshape(wr));
+    at::Tensor r = conv_impl(gz, wt, bias, ones, pad, dl, groups);
+    bool cropped = false;
+    for (int64_t i = 0; i < k; ++i)
+        if (crop[i] > 0) {
+            r = r.narrow(2 + i, crop[i], in_size[i]);
+            cropped = true;
+        }
+    return cropped ? r.contiguous() : r;
+}
+
+// Gradient of conv(x, weight) with respect to the weight [F, C/groups, K...]:
+// per group, the correlation of x and g with batch and channels swapped (the
+// batch is the reduction), scales from the whole x and the whole g.
+// Reductions longer than the exact limb limit (32768) are split over the
+// batch and the fp32 chunk results summed before the one rounding to the
+// input dtype.
+at::Tensor conv_weight_grad(const at::Tensor& x, const at::Tensor& g_in, at::IntArrayRef w_size,
+                            const std::vector<int64_t>& s, const std::vector<int64_t>& p,
+                            const std::vector<int64_t>& dl, int64_t groups) {
+    const int64_t k = static_cast<int64_t>(w_size.size()) - 2;
+    at::Tensor g = g_in.contiguous();
+    const int64_t N = x.size(0), Cg = w_size[1], F = w_size[0], Fg = F / groups;
+    int64_t per_image = 1;
+    for (int64_t i = 0; i < k; ++i) per_image *= g.size(2 + i);
+    TORCH_CHECK(per_image <= 32768, "kunlun conv weight gradient: output volume exceeds 32768 elements");
+    const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(N, 32768 / per_image));
+    at::Tensor ax = torch_kunlun::amax(x), ag = torch_kunlun::amax(g);
+    at::Tensor gw = at::empty(w_size, x.options());
+    for (int64_t gr = 0; gr < groups; ++gr) {
+        // [Cg, N, S...] and [Fg, N, O...]: batch as channels, reduced over
+        at::Tensor xt = x.slice(1, gr * Cg, (gr + 1) * Cg).transpose(0, 1);
+        at::Tensor gt = g.slice(1, gr * Fg, (gr + 1) * Fg).transpose(0, 1);
+        at::Tensor acc;
+        for (int64_t n0 = 0; n0 < N; n0 += chunk) {
+            const int64_t n1 = std::min(N, n0 + chunk);
+            at::Tensor xc = xt.slice(1, n0, n1).to(at::kFloat).contiguous();
+            at::Tensor gc = gt.slice(1, n0, n1).to(at::kFloat).contiguous();
+            at::Tensor r = conv_impl(xc, gc, std::nullopt, dl, p, s, 1, ax.data_ptr<float>(), ag.data_ptr<float>());
+            for (int64_t i = 0; i < k; ++i) r = r.slice(2 + i, 0, w_size[2 + i]);  // [Cg, Fg, K...]
+            acc = acc.defined() ? at::add(acc, r) : r;
+        }
+        gw.slice(0, gr * Fg, (gr + 1) * Fg).copy_(acc.transpose(0, 1));
+    }
+    return gw;
+}
+
+std::vector<int64_t> reduce_dims_for_bias(const at::Tensor& g) {
+    std::vector<int64_t> dims = {0};
+    for (int64_t i = 2; i < g.dim(); ++i) dims.push_back(i);
+    return dims;
 }
 
 // aten::convolution_overrideable is where aten::convolution sends backends
-// that are not built in (F.conv2d on a kunlun tensor with autograd active).
+// that are not built in: conv1d / conv2d / conv3d and their transposed forms
+// on kunlun tensors.  conv1d is conv2d on [N, C, 1, L] as in the reference
+// (csrc/ops_nn_extra.cpp:70-86); a transposed convolution is the
+// correlation of the zero-inserted input with the flipped weight.
 at::Tensor convolution_overrideable(const at::Tensor& input, const at::Tensor& weight,
                                     const std::optional<at::Tensor>& bias, at::IntArrayRef stride,
                                     at::IntArrayRef padding, at::IntArrayRef dilation,
                                     bool transposed, at::IntArrayRef output_padding,
                                     int64_t groups) {
-    TORCH_CHECK(!transposed, "kunlun: transposed convolution is not implemented");
-    TORCH_CHECK(input.dim() == 4 || input.dim() == 3, "kunlun: only 2-D convolution is implemented");
-    return conv2d_impl(input, weight, bias, stride, padding, dilation, groups);
+    const int64_t k = weight.dim() - 2;
+    TORCH_CHECK(k >= 1 && k <= 3 && input.dim() == weight.dim(),
+                "kunlun: convolution needs batched 1-D, 2-D or 3-D operands");
+    if (k == 1) {
+        const auto s = axis_param(stride, 1, 1, "stride"), p = axis_param(padding, 1, 0, "padding"),
+                   dl = axis_param(dilation, 1, 1, "dilation"),
+                   op = axis_param(output_padding, 1, 0, "output_padding");
+        const int64_t s2[2] = {1, s[0]}, p2[2] = {0, p[0]}, d2[2] = {1, dl[0]}, o2[2] = {0, op[0]};
+        return torch_kunlun::convolution_overrideable(input.unsqueeze(2), weight.unsqueeze(2), bias, s2, p2, d2,
+                                                      transposed, o2, groups)
+            .squeeze(2);
+    }
+    if (!transposed) return conv_impl(input, weight, bias, stride, padding, dilation, groups);
+    const auto s = axis_param(stride, k, 1, "stride"), p = axis_param(padding, k, 0, "padding"),
+               dl = axis_param(dilation, k, 1, "dilation"),
+               op = axis_param(output_padding, k, 0, "output_padding");
+    check_operand(weight, input, "conv_transpose");
+    TORCH_CHECK(groups > 0 && input.size(1) == weight.size(0) && weight.size(0) % groups == 0,
+                "kunlun conv_transpose: weight/input channel mismatch");
+    std::vector<int64_t> out_size(k);
+    for (int64_t i = 0; i < k; ++i) {
+        TORCH_CHECK(op[i] >= 0 && (op[i] < s[i] || op[i] < dl[i]), "kunlun conv_transpose: bad output_padding");
+        out_size[i] = (input.size(2 + i) - 1) * s[i] - 2 * p[i] + dl[i] * (weight.size(2 + i) - 1) + 1 + op[i];
+        TORCH_CHECK(out_size[i] > 0, "kunlun conv_transpose produced non-positive output shape");
+    }
+    return conv_input_grad(input, weight, out_size, s, p, dl, groups, bias);
 }
 
-// w [A, B, KH, KW] with both spatial axes reversed, as a device strided copy
-// that reads the source with negative strides from its last tap.
-at::Tensor flip_hw(const at::Tensor& w_in) {
-    at::Tensor w = w_in.contiguous();
-    at::Tensor out = at::empty(w.sizes(), w.options());
-    if (w.numel() == 0) return out;
-    const int64_t sizes[4] = {w.size(0), w.size(1), w.size(2), w.size(3)};
-    const int64_t dst[4] = {w.stride(0), w.stride(1), w.stride(2), w.stride(3)};
-    const int64_t src[4] = {w.stride(0), w.stride(1), -w.stride(2), -w.stride(3)};
-    const int64_t last = (w.size(2) - 1) * w.stride(2) + (w.size(3) - 1) * w.stride(3);
-    const int dev = w.device().index();
-    DeviceScope g(dev);
-    const int t = tk_scalar_code(w.scalar_type());
-    check_tk(tk_copy_strided(out.data_ptr(), t,
-                             static_cast<const char*>(w.data_ptr()) + last * w.element_size(), t, 4,
-                             sizes, dst, src, current_stream(dev)),
-             "tk_copy_strided");
-    return out;
-}
-
-// Gradients of the quantised conv2d (the reference's conv2d_grad,
-// csrc/autograd.cpp:621-682), each a quantised convolution of the same
-// contract with one per-tensor scale per operand:
-//   grad_input  = correlation of the zero-inserted (stride), padded grad_output
-//                 with the spatially flipped, in/out-swapped weight;
-//   grad_weight = per group, the correlation of the input with grad_output,
-//                 both with batch and channels swapped (the batch is the
-//                 reduction), scales from the whole input and the whole
-//                 grad_output; reductions longer than the exact limb limit
-//                 (32768) are split over the batch and the fp32 chunk results
-//                 summed before the one rounding to the input dtype;
-//   grad_bias   = sum of grad_output over batch and pixels (fp32, one rounding).
+// Gradients of the quantised convolutions (the reference's conv2d_grad,
+// csrc/autograd.cpp:621-682, and the conv3d / conv_transpose2d backward of
+// csrc/autograd_nn_extra.cpp), each a quantised convolution of the same
+// contract with one per-tensor scale per operand; the bias gradient is a sum
+// of grad_output over batch and pixels (fp32, one rounding).
+//   forward conv:       grad_input  = conv_input_grad(grad_output, weight)
+//                       grad_weight = conv_weight_grad(input, grad_output)
+//   transposed conv:    grad_input  = conv(grad_output, weight)
+//                       grad_weight = conv_weight_grad(grad_output, input)
 std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable(
     const at::Tensor& grad_output, const at::Tensor& input, const at::Tensor& weight,
     at::IntArrayRef stride, at::IntArrayRef padding, at::IntArrayRef dilation, bool transposed,
     at::IntArrayRef output_padding, int64_t groups, std::array<bool, 3> output_mask) {
-    TORCH_CHECK(!transposed, "kunlun: transposed convolution backward is not implemented");
-    TORCH_CHECK(input.dim() == 4 && weight.dim() == 4 && grad_output.dim() == 4,
-                "kunlun conv2d backward expects NCHW tensors");
-    const auto s = pair_of(stride, 1), p = pair_of(padding, 0), dl = pair_of(dilation, 1);
-    const int64_t N = input.size(0), C = input.size(1), H = input.size(2), W = input.size(3);
-    const int64_t F = weight.size(0), Cg = weight.size(1), KH = weight.size(2), KW = weight.size(3);
-    const int64_t Fg = F / groups;
-    const int64_t OH = grad_output.size(2), OW = grad_output.size(3);
-    at::Tensor g = grad_output.contiguous();
+    const int64_t k = weight.dim() - 2;
+    TORCH_CHECK(k >= 1 && k <= 3 && input.dim() == weight.dim() && grad_output.dim() == weight.dim(),
+                "kunlun convolution backward expects batched 1-D, 2-D or 3-D tensors");
+    if (k == 1) {
+        const auto s = axis_param(stride, 1, 1, "stride"), p = axis_param(padding, 1, 0, "padding"),
+                   dl = axis_param(dilation, 1, 1, "dilation"),
+                   op = axis_param(output_padding, 1, 0, "output_padding");
+        const int64_t s2[2] = {1, s[0]}, p2[2] = {0, p[0]}, d2[2] = {1, dl[0]}, o2[2] = {0, op[0]};
+        auto r = torch_kunlun::convolution_backward_overrideable(grad_output.unsqueeze(2), input.unsqueeze(2),
+                                                                 weight.unsqueeze(2), s2, p2, d2, transposed, o2,
+                                                                 groups, output_mask);
+        auto sq = [](const at::Tensor& t) { return t.defined() && t.dim() > 2 ? t.squeeze(2) : t; };
+        return std::make_tuple(sq(std::get<0>(r)), sq(std::get<1>(r)), std::get<2>(r));
+    }
+    const auto s = axis_param(stride, k, 1, "stride"), p = axis_param(padding, k, 0, "padding"),
+               dl = axis_param(dilation, k, 1, "dilation");
     at::Tensor gi, gw, gb;
-    if (output_mask[0]) {
-        const int64_t ph = dl[0] * (KH - 1) - p[0], pw = dl[1] * (KW - 1) - p[1];
-        TORCH_CHECK(ph >= 0 && pw >= 0,
-                    "kunlun conv2d backward: padding larger than the dilated kernel is not supported");
-        // rows / columns of the input that the forward's last window did not reach
-        const int64_t eh = (H + 2 * p[0] - dl[0] * (KH - 1) - 1) % s[0];
-        const int64_t ew = (W + 2 * p[1] - dl[1] * (KW - 1) - 1) % s[1];
-        at::Tensor gz = g;
-        if (s[0] > 1 || s[1] > 1 || eh > 0 || ew > 0) {
-            gz = at::zeros({N, F, (OH - 1) * s[0] + 1 + eh, (OW - 1) * s[1] + 1 + ew}, g.options());
-            gz.slice(2, 0, (OH - 1) * s[0] + 1, s[0]).slice(3, 0, (OW - 1) * s[1] + 1, s[1]).copy_(g);
+    if (!transposed) {
+        if (output_mask[0]) {
+            std::vector<int64_t> in_size(input.sizes().begin() + 2, input.sizes().end());
+            gi = conv_input_grad(grad_output, weight, in_size, s, p, dl, groups);
         }
-        at::Tensor wt = flip_hw(weight.view({groups, Fg, Cg, KH, KW}).transpose(1, 2).reshape({C, Fg, KH, KW}));
-        const int64_t pad[2] = {ph, pw}, one[2] = {1, 1};
-        gi = conv2d_impl(gz, wt, std::nullopt, one, pad, dilation, groups);
+        if (output_mask[1]) gw = conv_weight_grad(input, grad_output, weight.sizes(), s, p, dl, groups);
+    } else {
+        if (output_mask[0]) gi = conv_impl(grad_output.contiguous(), weight, std::nullopt, s, p, dl, groups);
+        if (output_mask[1]) gw = conv_weight_grad(grad_output, input, weight.sizes(), s, p, dl, groups);
     }
-    if (output_mask[1]) {
-        at::Tensor ax = torch_kunlun::amax(input), ag = torch_kunlun::amax(g);
-        std::vector<at::Tensor> per_group;
-        for (int64_t gr = 0; gr < groups; ++gr) {
-            // [Cg, N, H, W] and [Fg, N, OH, OW]: batch as channels, reduced over
-            at::Tensor xt = input.slice(1, gr * Cg, (gr + 1) * Cg).transpose(0, 1);
-            at::Tensor gt = g.slice(1, gr * Fg, (gr + 1) * Fg).transpose(0, 1);
-            const int64_t per_image = OH * OW;
-            const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(N, 32768 / per_image));
-            TORCH_CHECK(per_image <= 32768, "kunlun conv2d backward: output plane exceeds 32768 pixels");
-            at::Tensor acc;
-            for (int64_t n0 = 0; n0 < N; n0 += chunk) {
-                const int64_t n1 = std::min(N, n0 + chunk);
-                at::Tensor xc = xt.slice(1, n0, n1).to(at::kFloat).contiguous();
-                at::Tensor gc = gt.slice(1, n0, n1).to(at::kFloat).contiguous();
-                at::Tensor r = conv2d_impl(xc, gc, std::nullopt, dilation, padding, stride, 1,
-                                           ax.data_ptr<float>(), ag.data_ptr<float>());
-                r = r.slice(2, 0, KH).slice(3, 0, KW);  // [Cg, Fg, KH, KW]
-                acc = acc.defined() ? at::add(acc, r) : r;
-            }
-            per_group.push_back(acc.transpose(0, 1));
-        }
-        gw = at::empty(weight.sizes(), weight.options());
-        for (int64_t gr = 0; gr < groups; ++gr) gw.slice(0, gr * Fg, (gr + 1) * Fg).copy_(per_group[gr]);
-    }
-    if (output_mask[2]) gb = at::sum(g, {0, 2, 3});
+    if (output_mask[2]) gb = at::sum(grad_output, reduce_dims_for_bias(grad_output));
     return {gi, gw, gb};
 }
 
@@ -455,7 +565,7 @@ at::Tensor conv2d_autograd(const at::Tensor& input, const at::Tensor& weight,
         return batched ? out : out.squeeze(0);
     }
     at::AutoDispatchBelowADInplaceOrView guard;
-    return conv2d_impl(input, weight, bias, stride, padding, dilation, groups);
+    return torch_kunlun::conv2d(input, weight, bias, stride, padding, dilation, groups);
 }
 
 }  // namespace
