@@ -165,6 +165,27 @@ struct AmaxDesc {
     bool vec;
 };
 
+__device__ __forceinline__ uint4 ldg_nc_v4(const uint4* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// max(m, |a|) over the four fp16 pairs of w, as 16-bit magnitudes.
+__device__ __forceinline__ unsigned fold_abs_max_h2x4(unsigned m, const uint4& w) {
+    asm volatile(
+        "{\n\t.reg .b32 t;\n\t"
+        "and.b32 t, %1, 0x7FFF7FFF;\n\tmax.u16x2 %0, %0, t;\n\t"
+        "and.b32 t, %2, 0x7FFF7FFF;\n\tmax.u16x2 %0, %0, t;\n\t"
+        "and.b32 t, %3, 0x7FFF7FFF;\n\tmax.u16x2 %0, %0, t;\n\t"
+        "and.b32 t, %4, 0x7FFF7FFF;\n\tmax.u16x2 %0, %0, t;\n\t}"
+        : "+r"(m)
+        : "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w));
+    return m;
+}
+
 template <typename T>
 __device__ __forceinline__ unsigned amax_range(const T* base, int64_t start, int64_t end, bool vec);
 
@@ -178,17 +199,14 @@ __device__ __forceinline__ unsigned amax_range<__half>(const __half* xh, int64_t
         const int64_t nv = (end - start) / 8;
         const uint4* pv = reinterpret_cast<const uint4*>(base + start);
         int64_t j = threadIdx.x;
-        for (; j + 3 * static_cast<int64_t>(blockDim.x) < nv; j += 4 * blockDim.x) {
-            uint4 w[4];
+        for (; j + 7 * static_cast<int64_t>(blockDim.x) < nv; j += 8 * blockDim.x) {
+            uint4 w[8];
+            // loads and folds are volatile, so the eight 128-bit loads are
+            // all issued (in flight together) before the first fold
 #pragma unroll
-            for (int u = 0; u < 4; ++u) w[u] = __ldg(pv + j + u * blockDim.x);
+            for (int u = 0; u < 8; ++u) w[u] = ldg_nc_v4(pv + j + u * blockDim.x);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                m2 = __vmaxu2(m2, w[u].x & 0x7FFF7FFFu);
-                m2 = __vmaxu2(m2, w[u].y & 0x7FFF7FFFu);
-                m2 = __vmaxu2(m2, w[u].z & 0x7FFF7FFFu);
-                m2 = __vmaxu2(m2, w[u].w & 0x7FFF7FFFu);
-            }
+            for (int u = 0; u < 8; ++u) m2 = fold_abs_max_h2x4(m2, w[u]);
         }
         for (; j < nv; j += blockDim.x) {
             const uint4 w = __ldg(pv + j);
@@ -293,23 +311,63 @@ __device__ __forceinline__ void load8<float>(const float* p, int64_t n, float (&
     }
 }
 
-// Quantise 8 values and pack their limbs: lo bytes and hi bytes of the int16
-// codes into one 8-byte word each.  The clamp of quant_one is not needed
-// here: with inv = RN(32767/amax) and |v| <= amax, |RN(v*inv)| <= 32767.004,
-// so the rounded code never leaves [-32767, 32767]; a NaN product (possible
-// only when amax itself is not finite) is mapped to 0 as in quant_one.
-__device__ __forceinline__ void quant8_pack(const float (&v)[8], float inv, uint2& hi, uint2& lo) {
-    int q[8];
+// Codes of 8 values by magic-number rounding (the classic float-to-int
+// conversion by adding 1.5 * 2^23): for |t| < 2^22 the binary32 sum
+// t + 1.5 * 2^23 rounds t to the nearest integer, ties to even (the rounding
+// of every binary32 add), and holds that integer in two's complement in the
+// low bits of its significand; the low 16 bits of the sum's bit pattern are
+// the int16 code.  t = RN(v * inv) is the same binary32 product quant_one
+// rounds, so the codes are identical -- provided the product is rounded
+// before the add: a fused multiply-add would round v * inv + 1.5 * 2^23
+// once and break ties of RN(v * inv) (e.g. v = amax / 2 gives
+// RN(v * inv) = 16383.5, code 16384, while the exact product lies just below
+// the tie).  The products run two lanes per instruction; the adds are
+// __fadd_rn, which the compiler never contracts into a multiply-add.
+// Requires inv > 0 and |v| <= amax, which bounds |t| by 32767.004 (the
+// inv == 0 case is handled by the caller: every code is 0).
+__device__ __forceinline__ uint64_t f32x2_mul_add_magic(uint64_t v2, uint64_t inv2) {
+    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+    uint64_t t;
+    asm volatile("mul.rn.f32x2 %0, %1, %2;" : "=l"(t) : "l"(v2), "l"(inv2));
+    const float lo = __fadd_rn(__uint_as_float(static_cast<unsigned>(t)), kMagic);
+    const float hi = __fadd_rn(__uint_as_float(static_cast<unsigned>(t >> 32)), kMagic);
+    return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
+}
+
+__device__ __forceinline__ uint64_t pack_f32x2(float a, float b) {
+    return static_cast<uint64_t>(__float_as_uint(a)) | (static_cast<uint64_t>(__float_as_uint(b)) << 32);
+}
+
+// r[j]: bit patterns whose low 16 bits are the codes -> hi / lo limb words.
+__device__ __forceinline__ void pack_codes8(const uint64_t (&r)[4], uint2& hi, uint2& lo) {
+    unsigned p[4];  // two codes per word: code_2i | code_2i+1 << 16
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const float t = __fmul_rn(v[j], inv);
-        q[j] = (t == t) ? __float2int_rn(t) : 0;
+    for (int j = 0; j < 4; ++j)
+        p[j] = __byte_perm(static_cast<unsigned>(r[j]), static_cast<unsigned>(r[j] >> 32), 0x5410);
+    lo.x = __byte_perm(p[0], p[1], 0x6420);
+    hi.x = __byte_perm(p[0], p[1], 0x7531);
+    lo.y = __byte_perm(p[2], p[3], 0x6420);
+    hi.y = __byte_perm(p[2], p[3], 0x7531);
+}
+
+__device__ __forceinline__ void quant8_magic(const float (&v)[8], float inv, uint2& hi, uint2& lo) {
+    const uint64_t inv2 = pack_f32x2(inv, inv);
+    uint64_t r[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) r[j] = f32x2_mul_add_magic(pack_f32x2(v[2 * j], v[2 * j + 1]), inv2);
+    pack_codes8(r, hi, lo);
+}
+
+__device__ __forceinline__ void quant8_magic_h(const uint4& w, float inv, uint2& hi, uint2& lo) {
+    const uint64_t inv2 = pack_f32x2(inv, inv);
+    const __half2* h = reinterpret_cast<const __half2*>(&w);
+    uint64_t r[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h[j]);
+        r[j] = f32x2_mul_add_magic(pack_f32x2(f.x, f.y), inv2);
     }
-    // byte 0 of each code is its lo limb, byte 1 its (two's-complement) hi limb
-    lo.x = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
-    lo.y = __byte_perm(__byte_perm(q[4], q[5], 0x0040), __byte_perm(q[6], q[7], 0x0040), 0x5410);
-    hi.x = __byte_perm(__byte_perm(q[0], q[1], 0x0051), __byte_perm(q[2], q[3], 0x0051), 0x5410);
-    hi.y = __byte_perm(__byte_perm(q[4], q[5], 0x0051), __byte_perm(q[6], q[7], 0x0051), 0x5410);
+    pack_codes8(r, hi, lo);
 }
 
 // One warp quantises one segment of kSegGroups 8-column groups of a row:
@@ -326,6 +384,17 @@ __device__ __forceinline__ void quant_vec_segment(const QVecDesc& d, int64_t row
     const int64_t plane = d.rows * d.ld;
     int8_t* dst = d.limbs + (b * 2) * plane + r * d.ld;
     const int64_t g0 = seg * kSegGroups + lane;
+    if (inv == 0.0f) {  // amax 0 or not finite: every code is 0
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t g = g0 + 32 * u;
+            if (g < d.groups) {
+                *reinterpret_cast<uint2*>(dst + g * 8) = make_uint2(0, 0);
+                *reinterpret_cast<uint2*>(dst + plane + g * 8) = make_uint2(0, 0);
+            }
+        }
+        return;
+    }
     if constexpr (sizeof(T) == 2) {
         // keep the four loads as raw 128-bit words (16 registers) until used
         uint4 w[4];
@@ -343,20 +412,14 @@ __device__ __forceinline__ void quant_vec_segment(const QVecDesc& d, int64_t row
             const int64_t g = g0 + 32 * u;
             if (g < d.groups) {
                 const int64_t c0 = g * 8;
-                float v[8];
-                if (part[u]) {
-                    load8<T>(src + c0, d.cols - c0, v);
-                } else {
-                    const __half2* h = reinterpret_cast<const __half2*>(&w[u]);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float2 f = __half22float2(h[j]);
-                        v[2 * j] = f.x;
-                        v[2 * j + 1] = f.y;
-                    }
-                }
                 uint2 hi, lo;
-                quant8_pack(v, inv, hi, lo);
+                if (part[u]) {
+                    float v[8];
+                    load8<T>(src + c0, d.cols - c0, v);
+                    quant8_magic(v, inv, hi, lo);
+                } else {
+                    quant8_magic_h(w[u], inv, hi, lo);
+                }
                 *reinterpret_cast<uint2*>(dst + c0) = hi;
                 *reinterpret_cast<uint2*>(dst + plane + c0) = lo;
             }
@@ -380,7 +443,7 @@ __device__ __forceinline__ void quant_vec_segment(const QVecDesc& d, int64_t row
             const int64_t g = g0 + 32 * u;
             if (g < d.groups) {
                 uint2 hi, lo;
-                quant8_pack(v[u], inv, hi, lo);
+                quant8_magic(v[u], inv, hi, lo);
                 const int64_t c0 = g * 8;
                 *reinterpret_cast<uint2*>(dst + c0) = hi;
                 *reinterpret_cast<uint2*>(dst + plane + c0) = lo;
@@ -493,6 +556,13 @@ int quantise_operands(tk_dtype_t dt, const QuantOperand* ops, int nops, cudaStre
     const int dev = current_device();
     AmaxDesc ad[2] = {};
     int64_t ablocks[2] = {0, 0};
+    // one chunk size for every operand: about eight blocks per SM in all,
+    // so the larger operand gets proportionally more blocks
+    int64_t amax_elems = 0;
+    for (int i = 0; i < nops; ++i)
+        if (ops[i].given_amax == nullptr) amax_elems += ops[i].batch * ops[i].rows * ops[i].cols;
+    const int64_t chunk_goal = std::max<int64_t>(static_cast<int64_t>(kAmaxThreads) * 64,
+                                                 ceil_div(amax_elems, 8LL * sm_count(dev)));
     for (int i = 0; i < nops; ++i) {
         const QuantOperand& o = ops[i];
         if (o.given_amax != nullptr || o.batch * o.rows * o.cols == 0) continue;
@@ -508,12 +578,7 @@ int quantise_operands(tk_dtype_t dt, const QuantOperand* ops, int nops, cudaStre
             d.slice_stride = 0;
             d.slice_len = o.batch * o.rows * o.cols;
         }
-        const int64_t per_block = static_cast<int64_t>(kAmaxThreads) * 64;
-        int64_t chunks = ceil_div(d.slice_len, per_block);
-        // two blocks per SM per operand: fat blocks keep many loads in flight
-        // and few atomics land on the shared maximum
-        const int64_t want = std::max<int64_t>(1, (2LL * sm_count(dev)) / d.nslices);
-        chunks = std::max<int64_t>(1, std::min(chunks, want));
+        const int64_t chunks = std::max<int64_t>(1, ceil_div(d.slice_len, chunk_goal));
         d.chunk = (ceil_div(d.slice_len, chunks) + 7) / 8 * 8;
         d.chunks = ceil_div(d.slice_len, d.chunk);
         const size_t es = dtype_size(dt);
