@@ -436,7 +436,7 @@ def main():
     ap.add_argument("--no-bert", action="store_true", help="skip the encoder-block measurement")
     ap.add_argument("--no-extra", action="store_true", help="skip the bmm and conv measurements")
     ap.add_argument("--workload", default="linear", choices=["linear", "tp_mlp", "bert"])
-    ap.add_argument("--reduce", default="allreduce", choices=["allreduce", "reduce_scatter"])
+    ap.add_argument("--reduce", default="allreduce", choices=["allreduce", "reduce_scatter", "peer", "peer_fused"])
     args = ap.parse_args()
     if args.workload == "tp_mlp" and args.impl != "reference":
         return run_tp_mlp(args)
@@ -661,14 +661,25 @@ def run_tp_mlp(args):
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, no dataset)",
             "config": {"workload": TP_WORKLOAD, "T": TP_T, "H": TP_H, "F": TP_F,
                        "parallelism": f"tp{world}", "reduce": args.reduce,
-                       "overlap": "down projection in 4 row blocks, each block's all-reduce on a "
-                                  "second stream", "l2": "inputs larger than L2"},
+                       "overlap": OVERLAP[args.reduce], "l2": "inputs larger than L2"},
             "gpu_launches": None, "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        tp.release_peer_buffers()
         dist.destroy_process_group()
     return 0
+
+
+OVERLAP = {
+    "allreduce": "down projection in 4 row blocks, each block's all-reduce on a second stream",
+    "reduce_scatter": "none: one GEMM, then the bkcl reduce-scatter",
+    "peer": "down projection one owner's row block at a time; each finished block is copied by a copy "
+            "engine into its owner's buffer (CUDA IPC, NVLink) while the next block computes; a "
+            "one-element all-reduce as the barrier, then each rank sums its slots",
+    "peer_fused": "the down GEMM's epilogue stores each tile into the owning rank's buffer over NVLink "
+                  "(CUDA IPC), a one-element all-reduce as the barrier, then each rank sums its slots",
+}
 
 
 if __name__ == "__main__":

@@ -159,6 +159,19 @@ TK_API int tk_qgemm_from_limbs(const tk_qgemm_desc_t* desc, const int8_t* a_limb
  * stream capture. */
 TK_API int tk_qgemm_noalloc(const tk_qgemm_desc_t* desc, void* stream);
 
+/* tk_qgemm (batch 1) with the output rows scattered over destination buffers:
+ * rows [q*rows_per_dest, (q+1)*rows_per_dest) are stored at row_dest[q]
+ * (row stride out_sm, local row m - q*rows_per_dest) and out is ignored.
+ * row_dest entries are device pointers valid on the calling GPU, typically
+ * other GPUs' buffers opened through CUDA IPC: a row-parallel linear writes
+ * each row block straight into the rank that owns it over NVLink while the
+ * GEMM runs, and that rank sums its slots with tk_reduce_sum.  Replaces the
+ * fc + bkcl reduce_scatter pair of a row-parallel linear (csrc/ops.cpp:210-230,
+ * csrc/xccl.cpp:111-163).  1 <= ndest <= 8, m == ndest * rows_per_dest. */
+TK_API int tk_qgemm_scatter_rows(const tk_qgemm_desc_t* desc, void* const* row_dest, int ndest,
+                                 int64_t rows_per_dest, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
 /* Same contract computed by a plain CUDA-core kernel (one output per thread).
  * Used to cross-check the tensor-core path on the device; not fast. */
 TK_API int tk_qgemm_simt(const tk_qgemm_desc_t* desc, void* workspace, size_t workspace_bytes,

@@ -106,6 +106,19 @@ def _rank_main(rank, world, port, q):
         ys = tp.tp_mlp_forward(x, wgs, wus, wds, reduce="reduce_scatter")
         rows = want[rank * T // world:(rank + 1) * T // world]
         assert torch.allclose(ys.cpu().float(), rows, atol=1e-3, rtol=2 ** -9)
+        # peer reduction: every rank's partial stored into the owner's buffer by
+        # the GEMM epilogue over NVLink, summed in rank order in fp32, one rounding
+        mine = p[:, rank * T // world:(rank + 1) * T // world]
+        acc = torch.zeros_like(mine[0])
+        for r in range(world):
+            acc = acc + mine[r]
+        want_peer = acc.half()
+        for mode in ("peer", "peer_fused", "peer"):  # both alternating buffers, and reuse
+            yp = tp.tp_mlp_forward(x, wgs, wus, wds, reduce=mode)
+            assert torch.equal(yp.cpu().view(torch.int16), want_peer.view(torch.int16)), mode
+        if world == 2:  # one add of two binary16 values: NCCL's sum rounds the same way
+            assert torch.equal(yp.cpu().view(torch.int16), ys.cpu().view(torch.int16))
+        tp.release_peer_buffers()
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, "ok"))

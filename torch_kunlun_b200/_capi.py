@@ -26,7 +26,7 @@ EXPORTED = [
     "tk_qgemm_debug", "tk_qgemm_from_limbs", "tk_copy_strided", "tk_fill_strided",
     "tk_binary", "tk_unary", "tk_silu_mul", "tk_conv2d_workspace_size", "tk_conv2d_q16",
     "tk_softmax", "tk_layer_norm", "tk_qgemm_noalloc", "tk_sdpa_workspace_size", "tk_sdpa_q16",
-    "tk_reduce_sum", "tk_conv3d_workspace_size", "tk_conv3d_q16",
+    "tk_reduce_sum", "tk_conv3d_workspace_size", "tk_conv3d_q16", "tk_qgemm_scatter_rows",
 ]
 
 

@@ -300,6 +300,61 @@ __global__ void reduce_cols_kernel(const TI* __restrict__ x, TO* __restrict__ ou
     }
 }
 
+// outer == 1, red <= 8, inner a multiple of 8 with 16-byte aligned rows (the
+// slots of a row-block exchange): 8 consecutive columns per thread, all red
+// loads in flight, slots added in index order from 0 -- the same additions and
+// rounding as reduce_cols_kernel, at HBM speed.
+template <typename T> __device__ __forceinline__ void ld8f(const T* p, float (&v)[8]);
+template <> __device__ __forceinline__ void ld8f<__half>(const __half* p, float (&v)[8]) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h[j]);
+        v[2 * j] = f.x;
+        v[2 * j + 1] = f.y;
+    }
+}
+template <> __device__ __forceinline__ void ld8f<float>(const float* p, float (&v)[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <typename T> __device__ __forceinline__ void st8f(T* p, const float (&v)[8]);
+template <> __device__ __forceinline__ void st8f<__half>(__half* p, const float (&v)[8]) {
+    uint4 u;
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+}
+template <> __device__ __forceinline__ void st8f<float>(float* p, const float (&v)[8]) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+template <typename TI, typename TO>
+__global__ void __launch_bounds__(256) sum_slots_kernel(const TI* __restrict__ x, TO* __restrict__ out, int red,
+                                                        int64_t inner) {
+    const int64_t n8 = inner / 8;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < n8;
+         i += static_cast<int64_t>(gridDim.x) * 256) {
+        float v[8][8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+            if (r < red) ld8f<TI>(x + r * inner + i * 8, v[r]);
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+            if (r < red) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[j] += v[r][j];
+            }
+        st8f<TO>(out + i * 8, acc);
+    }
+}
+
 // inner == 1: one warp per row, lane-strided partials, shuffle tree.
 template <typename TI, typename TO>
 __global__ void reduce_rows_kernel(const TI* __restrict__ x, TO* __restrict__ out, int64_t rows,
@@ -318,6 +373,15 @@ template <typename TI, typename TO>
 int reduce_launch(const void* x, int64_t outer, int64_t red, int64_t inner, void* out,
                   cudaStream_t stream) {
     const dim3 block(32, 8);
+    if (outer == 1 && red >= 1 && red <= 8 && inner % 8 == 0 &&
+        reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+        (inner * static_cast<int64_t>(sizeof(TI))) % 16 == 0) {
+        const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(inner / 8, 256),
+                                                                      8LL * sm_count(current_device())));
+        sum_slots_kernel<TI, TO><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            static_cast<const TI*>(x), static_cast<TO*>(out), static_cast<int>(red), inner);
+        return launch_status("reduce_sum");
+    }
     if (inner == 1) {
         const int64_t blocks = ceil_div(outer, 8);
         TK_CHECK_ARG(blocks < (1LL << 31), "tk_reduce_sum: too many rows");

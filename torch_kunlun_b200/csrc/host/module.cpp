@@ -32,6 +32,10 @@ py::dict device_properties(int device) {
 
 }  // namespace
 
+namespace torch_kunlun {
+void register_peer(pybind11::module& m);
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     using namespace torch_kunlun;
     m.def("device_count", &device_count);
@@ -97,4 +101,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("attn_mask") = py::none(), py::arg("is_causal") = false,
           py::arg("scale") = py::none(), py::arg("fused") = true);
     m.def("abi_version", [] { return tk_abi_version(); });
+    torch_kunlun::register_peer(m);
 }

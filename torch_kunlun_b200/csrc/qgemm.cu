@@ -88,6 +88,8 @@ using CfgWider = TileCfg<160, 3, 1>;  // 128x160 tiles (480 TMEM columns), singl
 using CfgOverlap64 = TileCfg<64, 4, 2>;  // 128x64 tiles, epilogue overlapped with the next tile
 using CfgOverlap80 = TileCfg<80, 4, 2>;  // 128x80 tiles, epilogue overlapped with the next tile
 
+constexpr int kMaxRowDests = 8;
+
 struct EpiParams {
     int dtype;  // 0 fp16, 1 fp32
     int64_t M, N;
@@ -106,7 +108,24 @@ struct EpiParams {
     bool bias_vec;  // bias is 16-byte aligned: vector loads per 16-column chunk
     bool add_vec;   // addend rows contiguous and 16-byte aligned: vector loads
     int32_t* dbg;  // [3][M][N] raw accumulators of slice 0, or null
+    // Row scatter (batch 1): rows [q*R, (q+1)*R) go to row_dest[q] at local
+    // row m - q*R (row stride out_sm) instead of out; R = row_dest_rows > 0.
+    // The destinations may be other GPUs' memory (CUDA IPC over NVLink).
+    void* row_dest[kMaxRowDests];
+    int64_t row_dest_rows;
+    int row_dest_n;
 };
+
+// Destination buffer and element offset of row m's first column.
+__device__ __forceinline__ void* row_out(const EpiParams& p, int64_t b, int64_t m, int64_t& row_off) {
+    if (p.row_dest_rows > 0) {
+        const int64_t q = min(m / p.row_dest_rows, static_cast<int64_t>(p.row_dest_n - 1));
+        row_off = (m - q * p.row_dest_rows) * p.out_sm;
+        return p.row_dest[q];
+    }
+    row_off = b * p.out_sb + m * p.out_sm;
+    return p.out;
+}
 
 struct TileParams {
     int batch, tiles_m, tiles_n, num_tiles, num_kb;
@@ -147,9 +166,6 @@ __device__ __forceinline__ float epilogue_one(const EpiParams& p, double s, doub
     return apply_act(r, p.act, p.dtype);
 }
 
-__device__ __forceinline__ void store_one(const EpiParams& p, int64_t off, float v) {
-    store_t(p.out, p.dtype, off, v);
-}
 
 __device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b, int& mt, int& nt) {
     const int per_batch = tp.tiles_m * tp.tiles_n;
@@ -345,7 +361,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             const int64_t m = static_cast<int64_t>(mt) * BM + row;
             const double s = epi_scale(ep, b);
             const bool row_ok = m < ep.M;
-            const int64_t out_row = b * ep.out_sb + m * ep.out_sm;
+            int64_t out_row;
+            void* const obase = row_out(ep, b, m, out_row);
 #pragma unroll 1
             for (int c = half; c < BN / 16; c += 2) {  // 16-column chunks, alternating halves
                 const int64_t n0 = static_cast<int64_t>(nt) * BN + c * 16;
@@ -400,7 +417,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                                 hv[j] = __floats2half2_rn(act_t<ACT>(f.x, DT), act_t<ACT>(f.y, DT));
                             }
                         }
-                        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(ep.out) + out_row + n0);
+                        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(obase) + out_row + n0);
                         const uint4* w = reinterpret_cast<const uint4*>(hv);
                         dst[0] = w[0];
                         dst[1] = w[1];
@@ -481,11 +498,11 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                             __half2 h2 = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
                             w[j] = *reinterpret_cast<uint32_t*>(&h2);
                         }
-                        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(ep.out) + out_row + n0);
+                        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(obase) + out_row + n0);
                         dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
                         dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
                     } else {
-                        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(ep.out) + out_row + n0);
+                        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(obase) + out_row + n0);
 #pragma unroll
                         for (int j = 0; j < 4; ++j)
                             dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
@@ -493,13 +510,16 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 } else {
 #pragma unroll
                     for (int j = 0; j < 16; ++j)
-                        if (full || n0 + j < ep.N) store_one(ep, out_row + (n0 + j) * ep.out_sn, v[j]);
+                        if (full || n0 + j < ep.N) store_t(obase, ep.dtype, out_row + (n0 + j) * ep.out_sn, v[j]);
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(acc_empty + buf));
         }
+        // stores into other GPUs' memory are ordered before anything this
+        // GPU does after the kernel
+        if (ep.row_dest_rows > 0) __threadfence_system();
     }
 
     tc_fence_before();
@@ -533,7 +553,9 @@ __global__ void qgemm_simt_kernel(const int8_t* __restrict__ la, const int8_t* _
     }
     const double s = epi_scale(ep, b);
     const float v = epilogue_one(ep, s, static_cast<double>(acc), b, m, n);
-    store_one(ep, b * ep.out_sb + m * ep.out_sm + n * ep.out_sn, v);
+    int64_t row_off;
+    void* base = row_out(ep, b, m, row_off);
+    store_t(base, ep.dtype, row_off + n * ep.out_sn, v);
 }
 
 // ---- host side --------------------------------------------------------------------
@@ -654,8 +676,18 @@ EpiParams make_epi(const tk_qgemm_desc_t& d, const float* amax_a, const float* a
                  d.add_sn == 1 && (d.add_sm * static_cast<int64_t>(es)) % 16 == 0 &&
                  (d.add_sb * static_cast<int64_t>(es)) % 16 == 0;
     ep.dbg = dbg;
+    for (int i = 0; i < kMaxRowDests; ++i) ep.row_dest[i] = nullptr;
+    ep.row_dest_rows = 0;
+    ep.row_dest_n = 0;
     return ep;
 }
+
+// Rows scattered over destination buffers (tk_qgemm_scatter_rows).
+struct RowScatter {
+    void* const* dest;
+    int n;
+    int64_t rows;
+};
 
 enum class Path { TensorCore, Simt };
 
@@ -746,10 +778,15 @@ int launch_tc(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb, int6
 }
 
 int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t stream, Path path,
-        int32_t* dbg) {
+        int32_t* dbg, const RowScatter* scatter = nullptr) {
     TK_CHECK_ARG(desc != nullptr, "qgemm: desc is NULL");
     const tk_qgemm_desc_t& d = *desc;
-    int rc = validate(d);
+    int rc = scatter ? TK_OK : validate(d);
+    if (scatter) {
+        tk_qgemm_desc_t v = d;
+        v.out = scatter->n > 0 ? scatter->dest[0] : nullptr;  // validated below per destination
+        rc = validate(v);
+    }
     if (rc) return rc;
     if (d.batch == 0 || d.m == 0 || d.n == 0) return TK_OK;
     const Layout L = workspace_layout(d);
@@ -781,6 +818,18 @@ int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t str
     const float* sa = (d.k > 0 && d.amax_a) ? d.amax_a : amax_a;
     const float* sb = (d.k > 0 && d.amax_b) ? d.amax_b : amax_b;
     EpiParams ep = make_epi(d, sa, sb, dbg);
+    if (scatter) {
+        const size_t es = dtype_size(d.dtype);
+        bool vec = (d.out_sm * static_cast<int64_t>(es)) % 16 == 0;
+        for (int i = 0; i < scatter->n; ++i) {
+            ep.row_dest[i] = scatter->dest[i];
+            vec = vec && reinterpret_cast<uintptr_t>(scatter->dest[i]) % 16 == 0;
+        }
+        ep.row_dest_rows = scatter->rows;
+        ep.row_dest_n = scatter->n;
+        ep.out = nullptr;
+        ep.vec_store = vec;
+    }
 
     if (path == Path::Simt || d.k == 0) {
         dim3 grid(static_cast<unsigned>(ceil_div(d.n, 128)), static_cast<unsigned>(d.m),
@@ -863,6 +912,24 @@ int tk_qgemm_debug(const tk_qgemm_desc_t* desc, void* workspace, size_t workspac
                    int32_t* acc3, void* stream) {
     return tk::run(desc, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
                    tk::Path::TensorCore, acc3);
+}
+
+int tk_qgemm_scatter_rows(const tk_qgemm_desc_t* desc, void* const* row_dest, int ndest,
+                          int64_t rows_per_dest, void* workspace, size_t workspace_bytes, void* stream) {
+    using namespace tk;
+    TK_CHECK_ARG(desc != nullptr && row_dest != nullptr, "qgemm_scatter_rows: NULL argument");
+    TK_CHECK_ARG(ndest >= 1 && ndest <= kMaxRowDests, "qgemm_scatter_rows: 1..%d destinations",
+                 kMaxRowDests);
+    TK_CHECK_ARG(desc->batch == 1, "qgemm_scatter_rows: batch must be 1");
+    TK_CHECK_ARG(rows_per_dest > 0 && rows_per_dest * ndest == desc->m,
+                 "qgemm_scatter_rows: m (%lld) must equal ndest * rows_per_dest",
+                 (long long)desc->m);
+    TK_CHECK_ARG(desc->out_sm >= desc->n, "qgemm_scatter_rows: out_sm must be >= n");
+    for (int i = 0; i < ndest; ++i)
+        TK_CHECK_ARG(row_dest[i] != nullptr, "qgemm_scatter_rows: destination %d is NULL", i);
+    const RowScatter sc = {row_dest, ndest, rows_per_dest};
+    return run(desc, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), Path::TensorCore,
+               nullptr, &sc);
 }
 
 }  // extern "C"

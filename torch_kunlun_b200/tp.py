@@ -9,10 +9,24 @@ are summed by an all-reduce (or reduce-scattered by rows).  Every rank
 quantises its own shards with their own per-tensor scales, as separate
 per-rank linear calls of the reference would.
 
-Overlap: the down projection is computed in row blocks, each block's
-all-reduce running on a communication stream while the next block is
-computed.  All blocks use the whole activation's and weight's amax, so the
-values equal those of one unsplit call.
+Reductions of the partial sums:
+
+- ``"allreduce"``: the down projection is computed in row blocks, each
+  block's all-reduce running on a communication stream while the next block
+  is computed.  All blocks use the whole activation's and weight's amax, so
+  the values equal those of one unsplit call.
+- ``"reduce_scatter"``: one GEMM, then the bkcl reduce-scatter by rows.
+- ``"peer"``: receive buffers shared through CUDA IPC; the down projection
+  runs one row block (one owner's rows) at a time, starting with the next
+  rank's rows, and each finished block is copied into slot r of its owner's
+  buffer by a copy engine over NVLink while the next block computes; the
+  owner's own block is computed last, straight into its slot.  After a
+  one-element all-reduce as a barrier each rank sums its slots in rank order
+  in fp32 and rounds once.  Returns this rank's rows, like
+  ``"reduce_scatter"``.
+- ``"peer_fused"``: the same exchange from one GEMM whose epilogue stores
+  every output tile straight into the owner's buffer over NVLink
+  (tk_qgemm_scatter_rows).  Same values as ``"peer"``.
 """
 
 from __future__ import annotations
@@ -27,6 +41,125 @@ from . import _C, kunlun, ops
 
 def _world(group) -> int:
     return dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+
+
+class PeerRowExchange:
+    """Receive buffers for one row-parallel output shape, shared by the ranks
+    of one node through CUDA IPC.  Rank q's buffer holds one [rows, cols]
+    slot per source rank; rank r's GEMM writes slot r of every owner.  Two
+    buffers alternate between calls: a rank may run the next call's GEMM
+    while another rank still sums the previous call's slots, and the barrier
+    of the call in between keeps the call after that from overwriting them."""
+
+    _count = 0
+
+    def __init__(self, rows: int, cols: int, dtype: torch.dtype, device: torch.device, group=None):
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.group = group
+        self.rows, self.cols, self.dtype = rows, cols, dtype
+        self.device = int(device.index or 0)
+        es = torch.tensor([], dtype=dtype).element_size()
+        slot_bytes = rows * cols * es
+        store = dist.distributed_c10d._get_default_store()
+        PeerRowExchange._count += 1  # the same sequence on every rank
+        tag = f"tk_peer_rows/{PeerRowExchange._count}/{rows}x{cols}/{dtype}"
+        self._owned, self._opened = [], []
+        self.dests, self.local = [], []
+        for b in range(2):
+            ptr, handle = _C.peer_alloc(self.world * slot_bytes, self.device)
+            self._owned.append(ptr)
+            store.set(f"{tag}/{b}/{self.rank}", handle)
+            self.local.append(_C.tensor_at(ptr, [self.world, rows, cols], dtype, self.device))
+        for b in range(2):
+            bases = []
+            for q in range(self.world):
+                if q == self.rank:
+                    bases.append(self._owned[b])
+                else:
+                    peer = _C.peer_open(store.get(f"{tag}/{b}/{q}"), self.device)
+                    self._opened.append(peer)
+                    bases.append(peer)
+            self.dests.append([base + self.rank * slot_bytes for base in bases])
+        self.flag = torch.zeros(1, dtype=torch.float32, device=device)
+        self._next = 0
+        dist.barrier(group=group)  # every rank has opened every buffer
+
+    def forward_fused(self, h: torch.Tensor, w: torch.Tensor, ah: torch.Tensor,
+                      aw: torch.Tensor) -> torch.Tensor:
+        b = self._next
+        self._next ^= 1
+        _C.linear_scatter_rows(h, w, ah, aw, self.dests[b], self.rows)
+        # stream-ordered barrier: every rank's GEMM has stored its slots
+        dist.all_reduce(self.flag, group=self.group)
+        return _C.sum_slots(self.local[b])
+
+    def forward(self, h: torch.Tensor, w: torch.Tensor, ah: torch.Tensor, aw: torch.Tensor,
+                copy_stream: Optional[kunlun.Stream] = None) -> torch.Tensor:
+        b = self._next
+        self._next ^= 1
+        R, P, me = self.rows, self.world, self.rank
+        compute = kunlun.current_stream(h.device)
+        copy = copy_stream if copy_stream is not None else self._copy_stream(h.device)
+        if not hasattr(self, "_stage"):
+            self._stage = [torch.empty(R, self.cols, dtype=self.dtype, device=h.device) for _ in range(2)]
+            self._stage_free = [None, None]
+        es = self._stage[0].element_size()
+        for i in range(1, P + 1):
+            q = (me + i) % P
+            rows = h[q * R:(q + 1) * R]
+            if q == me:
+                _C.linear_scaled(rows, w, None, 0, ah, aw, self.local[b][me])
+                break
+            s = i % 2
+            if self._stage_free[s] is not None:
+                compute.wait_event(self._stage_free[s])
+            _C.linear_scaled(rows, w, None, 0, ah, aw, self._stage[s])
+            done = kunlun.Event(device=h.device)
+            done.record(compute)
+            with kunlun.stream(copy):
+                copy.wait_event(done)
+                _C.copy_bytes(self.dests[b][q], self._stage[s].data_ptr(), R * self.cols * es)
+                freed = kunlun.Event(device=h.device)
+                freed.record(copy)
+            self._stage_free[s] = freed
+        compute.wait_stream(copy)
+        # stream-ordered barrier: every rank's blocks have landed in their slots
+        dist.all_reduce(self.flag, group=self.group)
+        return _C.sum_slots(self.local[b])
+
+    def _copy_stream(self, device):
+        if not hasattr(self, "_copy"):
+            self._copy = kunlun.Stream(device)
+        return self._copy
+
+    def close(self):
+        kunlun.synchronize()
+        for p in self._opened:
+            _C.peer_release(p)
+        self._opened = []
+        dist.barrier(group=self.group)  # no rank still maps our buffers
+        for p in self._owned:
+            _C.peer_release(p)
+        self._owned = []
+
+
+_EXCHANGES = {}
+
+
+def peer_exchange(rows: int, cols: int, dtype: torch.dtype, device: torch.device, group=None) -> PeerRowExchange:
+    key = (rows, cols, dtype, int(device.index or 0), id(group))
+    ex = _EXCHANGES.get(key)
+    if ex is None:
+        ex = _EXCHANGES[key] = PeerRowExchange(rows, cols, dtype, device, group)
+    return ex
+
+
+def release_peer_buffers():
+    """Unmap and free every exchange buffer (collective: all ranks call it)."""
+    for key in sorted(_EXCHANGES, key=str):
+        _EXCHANGES[key].close()
+    _EXCHANGES.clear()
 
 
 def tp_mlp_forward(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
@@ -49,6 +182,13 @@ def tp_mlp_forward(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
     world = _world(group)
     if world == 1:
         return _C.linear_scaled(h, w_down, None, 0, ah, aw)
+    if reduce in ("peer", "peer_fused"):
+        if T % world:
+            raise ValueError("peer reduction needs T divisible by the world size")
+        ex = peer_exchange(T // world, H, x.dtype, x.device, group)
+        if reduce == "peer_fused":
+            return ex.forward_fused(h, w_down, ah, aw)
+        return ex.forward(h, w_down, ah, aw, comm_stream)
     if reduce == "reduce_scatter":
         if T % world:
             raise ValueError("reduce_scatter needs T divisible by the world size")
@@ -75,4 +215,4 @@ def tp_mlp_forward(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
     return out
 
 
-__all__ = ["tp_mlp_forward"]
+__all__ = ["tp_mlp_forward", "PeerRowExchange", "peer_exchange", "release_peer_buffers"]
