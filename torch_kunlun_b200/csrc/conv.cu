@@ -25,6 +25,8 @@ namespace tk {
 
 int amax_launch(tk_dtype_t dtype, const void* x, int64_t nslices, int64_t slice_stride,
                 int64_t slice_len, float* amax_out, cudaStream_t stream);
+int amax_pair_launch(tk_dtype_t dtype, const void* x, int64_t nx, const void* w, int64_t nw, float* out,
+                     cudaStream_t stream);
 int quantize_limbs_launch(tk_dtype_t dtype, const void* x, int64_t batch, int64_t rows,
                           int64_t cols, int64_t sb, int64_t sr, int64_t sc, const float* amax,
                           int64_t amax_stride, int8_t* limbs, cudaStream_t stream);
@@ -370,6 +372,13 @@ int tk_conv3d_q16(const tk_conv3d_desc_t* desc, void* workspace, size_t workspac
     float* amax = reinterpret_cast<float*>(ws + L.off_amax);  // [0] input, [1] weight
     const float* ax = d.amax_x;
     const float* aw = d.amax_w;
+    if (ax == nullptr && aw == nullptr) {  // both scales in one launch
+        rc = amax_pair_launch(d.dtype, d.x, g.N * g.C * g.D * g.H * g.W, d.weight,
+                              g.F * (g.C / g.groups) * g.KD * g.KH * g.KW, amax, stream);
+        if (rc) return rc;
+        ax = amax;
+        aw = amax + 1;
+    }
     if (ax == nullptr) {
         rc = amax_launch(d.dtype, d.x, 1, 0, g.N * g.C * g.D * g.H * g.W, amax, stream);
         if (rc) return rc;

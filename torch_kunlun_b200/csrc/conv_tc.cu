@@ -729,30 +729,72 @@ x_limbs_kernel(const T* __restrict__ x, int C, int64_t HW, int W, int ph, int pw
     }
 }
 
-// Weight limb rows [F][KH][KW][Cg][128 B]: thread per (f, tap, group, 16-channel piece).
-template <typename T>
-__global__ void w_limbs_kernel(const T* __restrict__ w, int F, int C, int KH, int KW, int Cg,
-                               const float* __restrict__ amax, uint8_t* __restrict__ wl) {
-    const int taps = KH * KW;
-    const int64_t total = static_cast<int64_t>(F) * taps * Cg * 4;
-    const float inv = quant_inv(__ldg(amax));
+// Zero the padding ring of the zero-padded limb planes [N][Hp][Wp][Cg*128]
+// (x_limbs_kernel writes the interior): thread per 16-byte piece of a ring
+// position; the ring of one image is ph full rows at the top and bottom and
+// pw columns at both ends of the H rows between.
+__global__ void zero_ring_kernel(uint8_t* __restrict__ xl, int64_t N, int H, int W, int ph, int pw, int Cg) {
+    const int Hp = H + 2 * ph, Wp = W + 2 * pw;
+    const int64_t ring = static_cast<int64_t>(Hp) * Wp - static_cast<int64_t>(H) * W;
+    const int pieces = Cg * 8;
+    const int64_t total = N * ring * pieces;
     for (int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < total;
          it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int pc = static_cast<int>(it & 3);
-        int64_t r = it >> 2;
-        const int g = static_cast<int>(r % Cg);
-        r /= Cg;
-        const int tap = static_cast<int>(r % taps);
-        const int f = static_cast<int>(r / taps);
-        int16_t q[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            const int c = g * 64 + pc * 16 + k;
-            q[k] = static_cast<int16_t>(c < C ? quant_one(ldt<T>(w, (static_cast<int64_t>(f) * C + c) * taps + tap), inv) : 0);
+        const int piece = static_cast<int>(it % pieces);
+        const int64_t r = it / pieces;
+        const int64_t n = r / ring;
+        int64_t i = r - n * ring;
+        int hp, wp;
+        const int64_t band = static_cast<int64_t>(ph) * Wp;
+        if (i < band) {
+            hp = static_cast<int>(i / Wp);
+            wp = static_cast<int>(i % Wp);
+        } else if (i < 2 * band) {
+            i -= band;
+            hp = H + ph + static_cast<int>(i / Wp);
+            wp = static_cast<int>(i % Wp);
+        } else {
+            i -= 2 * band;
+            const int k = static_cast<int>(i % (2 * pw));
+            hp = ph + static_cast<int>(i / (2 * pw));
+            wp = k < pw ? k : W + k;
         }
+        uint8_t* dst = xl + ((n * Hp + hp) * Wp + wp) * static_cast<int64_t>(Cg) * 128 + piece * 16;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+    }
+}
+
+// Weight limb rows [F][taps][Cg][128 B].  One block per (filter, 64-channel
+// group, run of WQ_TAPS taps): the 64 x WQ_TAPS codes are read with the taps
+// contiguous (OI[D]HW order), quantised into shared memory, and each thread
+// packs the 16-channel hi and lo pieces of one tap's row.
+constexpr int WQ_TAPS = 32;
+
+template <typename T>
+__global__ void __launch_bounds__(128)
+w_limbs_kernel(const T* __restrict__ w, int F, int C, int taps, int Cg, const float* __restrict__ amax,
+               uint8_t* __restrict__ wl) {
+    __shared__ int16_t q[64][WQ_TAPS + 2];
+    const int runs = (taps + WQ_TAPS - 1) / WQ_TAPS;
+    const int run = blockIdx.x % runs;
+    const int g = (blockIdx.x / runs) % Cg;
+    const int f = blockIdx.x / (runs * Cg);
+    const int t0 = run * WQ_TAPS;
+    const int nt = min(WQ_TAPS, taps - t0);
+    const float inv = quant_inv(__ldg(amax));
+    for (int it = threadIdx.x; it < 64 * WQ_TAPS; it += 128) {
+        const int cc = it / WQ_TAPS, t = it - (it / WQ_TAPS) * WQ_TAPS;
+        const int c = g * 64 + cc;
+        int v = 0;
+        if (c < C && t < nt) v = quant_one(ldt<T>(w, (static_cast<int64_t>(f) * C + c) * taps + t0 + t), inv);
+        q[cc][t] = static_cast<int16_t>(v);
+    }
+    __syncthreads();
+    for (int it = threadIdx.x; it < nt * 4; it += 128) {
+        const int t = it >> 2, pc = it & 3;
         uint4 hi, lo;
-        pack16(q, 1, hi, lo);
-        uint8_t* dst = wl + ((static_cast<int64_t>(f) * taps + tap) * Cg + g) * 128 + pc * 16;
+        pack16(&q[pc * 16][t], WQ_TAPS + 2, hi, lo);
+        uint8_t* dst = wl + ((static_cast<int64_t>(f) * taps + t0 + t) * Cg + g) * 128 + pc * 16;
         *reinterpret_cast<uint4*>(dst) = hi;
         *reinterpret_cast<uint4*>(dst + 64) = lo;
     }
@@ -829,7 +871,13 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
     const size_t x_bytes = static_cast<size_t>(N * sh * sw * Cg * 128);
     uint8_t* xl = ws;
     uint8_t* wl = ws + round_up(x_bytes, 1024);
-    if (win && (ph > 0 || pw > 0)) TK_CUDA_TRY(cudaMemsetAsync(xl, 0, x_bytes, stream));
+    if (win && (ph > 0 || pw > 0)) {
+        const int64_t ring = Hp * Wp - H * W;
+        const int64_t total = N * ring * Cg * 8;
+        const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), 8LL * sm_count(dev)));
+        zero_ring_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(xl, N, (int)H, (int)W, (int)ph, (int)pw,
+                                                                           (int)Cg);
+    }
     const int64_t DHW = D * H * W;  // the image's flattened volume (rows of limbs)
     const int64_t runs = ceil_div(DHW, XQ_W);
     TK_CHECK_ARG(N * runs * Cg < (1LL << 31) && DHW < (1LL << 31), "conv: input too large");
@@ -839,19 +887,21 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
                       reinterpret_cast<uintptr_t>(x) % 16 == 0) ? 1 : 0;
     const int oph = win ? static_cast<int>(ph) : 0, opw = win ? static_cast<int>(pw) : 0;
     const int64_t taps = KD * KH * KW;
-    const unsigned wgrid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(F * taps * Cg * 4, 256), 4096)));
+    const int64_t wblocks = F * Cg * ceil_div(taps, WQ_TAPS);
+    TK_CHECK_ARG(wblocks < (1LL << 31), "conv: weight too large");
+    const unsigned wgrid = static_cast<unsigned>(wblocks);
     if (dtype == TK_DTYPE_F16) {
         x_limbs_kernel<__half><<<xgrid, XQ_THREADS, 0, stream>>>(
             static_cast<const __half*>(x), (int)C, DHW, (int)W, oph, opw, (int)sh, (int)sw, (int)Cg, xvec,
             amax_x, xl);
-        w_limbs_kernel<__half><<<wgrid, 256, 0, stream>>>(static_cast<const __half*>(w), (int)F, (int)C,
-                                                          (int)(KD * KH), (int)KW, (int)Cg, amax_w, wl);
+        w_limbs_kernel<__half><<<wgrid, 128, 0, stream>>>(static_cast<const __half*>(w), (int)F, (int)C,
+                                                          (int)taps, (int)Cg, amax_w, wl);
     } else {
         x_limbs_kernel<float><<<xgrid, XQ_THREADS, 0, stream>>>(
             static_cast<const float*>(x), (int)C, DHW, (int)W, oph, opw, (int)sh, (int)sw, (int)Cg, xvec,
             amax_x, xl);
-        w_limbs_kernel<float><<<wgrid, 256, 0, stream>>>(static_cast<const float*>(w), (int)F, (int)C,
-                                                         (int)(KD * KH), (int)KW, (int)Cg, amax_w, wl);
+        w_limbs_kernel<float><<<wgrid, 128, 0, stream>>>(static_cast<const float*>(w), (int)F, (int)C,
+                                                         (int)taps, (int)Cg, amax_w, wl);
     }
     int rc = launch_status("conv2d limbs");
     if (rc) return rc;

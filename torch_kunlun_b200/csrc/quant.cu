@@ -501,6 +501,48 @@ int amax_launch(tk_dtype_t dtype, const void* x, int64_t nslices, int64_t slice_
     return launch_status("amax");
 }
 
+// max |x| of two whole tensors in one launch (out[0] for x, out[1] for w):
+// one memset of both slots, one amax_multi_kernel with a chunk size shared by
+// both operands.
+int amax_pair_launch(tk_dtype_t dtype, const void* x, int64_t nx, const void* w, int64_t nw, float* out,
+                     cudaStream_t stream) {
+    TK_CHECK_ARG(nx >= 0 && nw >= 0 && out != nullptr, "amax_pair: bad arguments");
+    TK_CUDA_TRY(cudaMemsetAsync(out, 0, 2 * sizeof(float), stream));
+    const int dev = current_device();
+    const int64_t chunk_goal = std::max<int64_t>(static_cast<int64_t>(kAmaxThreads) * 64,
+                                                 ceil_div(nx + nw, 8LL * sm_count(dev)));
+    AmaxDesc ad[2] = {};
+    int64_t blocks[2] = {0, 0};
+    const void* src[2] = {x, w};
+    const int64_t len[2] = {nx, nw};
+    for (int i = 0; i < 2; ++i) {
+        if (len[i] == 0) continue;
+        TK_CHECK_ARG(src[i] != nullptr, "amax_pair: NULL operand");
+        AmaxDesc& d = ad[i];
+        d.x = src[i];
+        d.out = reinterpret_cast<unsigned*>(out + i);
+        d.nslices = 1;
+        d.slice_stride = 0;
+        d.slice_len = len[i];
+        const int64_t chunks = std::max<int64_t>(1, ceil_div(len[i], chunk_goal));
+        d.chunk = (ceil_div(len[i], chunks) + 7) / 8 * 8;
+        d.chunks = ceil_div(len[i], d.chunk);
+        d.vec = reinterpret_cast<uintptr_t>(src[i]) % 16 == 0;
+        blocks[i] = d.chunks;
+    }
+    const int64_t total = blocks[0] + blocks[1];
+    if (total == 0) return TK_OK;
+    TK_CHECK_ARG(total < (1LL << 31), "amax_pair: too many blocks");
+    const AmaxDesc& first = blocks[0] ? ad[0] : ad[1];
+    const AmaxDesc& second = blocks[0] ? ad[1] : ad[0];
+    const int64_t b0 = blocks[0] ? blocks[0] : blocks[1];
+    if (dtype == TK_DTYPE_F16)
+        amax_multi_kernel<__half><<<static_cast<unsigned>(total), kAmaxThreads, 0, stream>>>(first, second, b0);
+    else
+        amax_multi_kernel<float><<<static_cast<unsigned>(total), kAmaxThreads, 0, stream>>>(first, second, b0);
+    return launch_status("amax");
+}
+
 int quantize_limbs_launch(tk_dtype_t dtype, const void* x, int64_t batch, int64_t rows,
                           int64_t cols, int64_t sb, int64_t sr, int64_t sc, const float* amax,
                           int64_t amax_stride, int8_t* limbs, cudaStream_t stream) {
