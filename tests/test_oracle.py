@@ -148,3 +148,35 @@ def test_nd_and_transposed_conv_accumulators_match_exact_float64_convs():
     y1 = O.conv1d(x1, w1, None, 2, 1, 1, 1)
     y2 = O.conv2d(x1[:, :, None, :], w1[:, :, None, :], None, (1, 2), (0, 1), (1, 1), 1)[:, :, 0, :]
     assert np.array_equal(y1.view(np.uint16), y2.view(np.uint16))
+
+
+def test_sampled_recomputation_equals_the_whole_oracle():
+    """The full-size GPU tests check sampled outputs: scales of the whole
+    operands, codes of the sampled rows / receptive fields only, exact int64
+    dots, the oracle epilogue.  On a small case that equals the whole
+    oracle's output at the same positions."""
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((40, 72)).astype(np.float16)
+    w = (rng.standard_normal((50, 72)) * 0.02).astype(np.float16)
+    b = (rng.standard_normal(50) * 0.01).astype(np.float16)
+    full = O.linear(x, w, b)
+    ax, aw = O.amax(x), O.amax(w)
+    rows, cols = np.array([0, 7, 39]), np.array([0, 3, 20, 49])
+    acc = O.quant(x[rows], ax).astype(np.int64) @ O.quant(w[cols], aw).astype(np.int64).T
+    got = O.epilogue(acc, ax, aw, np.float16, bias=b[cols])
+    assert np.array_equal(got.view(np.uint16), full[np.ix_(rows, cols)].view(np.uint16))
+    xc = np.maximum(rng.standard_normal((2, 5, 7, 7)), 0).astype(np.float16)
+    wc = (rng.standard_normal((4, 5, 3, 3)) * 0.3).astype(np.float16)
+    fullc = O.conv2d(xc, wc, None, (1, 1), (1, 1), (1, 1), 1)
+    axc, awc = O.amax(xc), O.amax(wc)
+    qw = O.quant(wc, awc).astype(np.int64).reshape(4, -1)
+    for n, oh, ow in [(0, 0, 0), (1, 6, 6), (1, 3, 0)]:
+        xp = np.zeros((5, 3, 3), dtype=np.float16)
+        for r in range(3):
+            for s in range(3):
+                ih, iw = oh - 1 + r, ow - 1 + s
+                if 0 <= ih < 7 and 0 <= iw < 7:
+                    xp[:, r, s] = xc[n, :, ih, iw]
+        acc = (qw @ O.quant(xp, axc).astype(np.int64).reshape(-1))[None]
+        got = O.epilogue(acc, axc, awc, np.float16)[0]
+        assert np.array_equal(got.view(np.uint16), fullc[n, :, oh, ow].view(np.uint16))
