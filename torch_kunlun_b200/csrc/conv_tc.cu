@@ -41,6 +41,8 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "tk_internal.h"
@@ -630,6 +632,228 @@ conv_win_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__
     }
 }
 
+// ---- stacked-limb window variant: two wide MMAs per K sub-block -------------
+//
+// For up to 64 filters the four limb products per 32-channel sub-block
+// (hi*hi, hi*lo, lo*hi, lo*lo) are four N = 64 MMAs that each re-read their
+// 4 KB A tile for 262K MACs.  Here both weight limbs are stacked along N in
+// one unsigned operand -- rows 0-63 the hi limbs offset to u8 (b_hi + 128),
+// rows 64-127 the lo limbs, rows 128-143 all ones -- so each sub-block is two
+// N = 144 MMAs: acc1 = a_hi x stack, acc2 = a_lo x stack.  With
+// S_hi = sum a_hi and S_lo = sum a_lo (the ones columns):
+//   HH  = acc1[f] - 128 S_hi
+//   MID = acc1[64 + f] + acc2[f] - 128 S_lo
+//   LL  = acc2[64 + f]
+// all exact in 32-bit two's complement (every true value fits; |acc2| <=
+// 255 * 255 * 32768 < 2^31).  Two K steps (tap, group) share one 128-byte
+// weight row: step 2p + h sits at byte 64 h of pair p's 144-row tile.  The
+// whole stacked filter block stays resident; the epilogue copies the
+// accumulators out of TMEM and releases them before its arithmetic, so the
+// single accumulator buffer (288 of 512 columns) overlaps the next tile.
+
+constexpr int STK_N = 144;
+constexpr int STK_TILE = STK_N * KB;             // bytes per pair of K steps
+constexpr int STK_MAX_PAIRS = kResWeightBytes / STK_TILE;
+constexpr int STK_OFF_B = 2 * WIN_BYTES;
+constexpr int STK_OFF_BAR = STK_OFF_B + STK_MAX_PAIRS * STK_TILE;
+constexpr int STK_SMEM = STK_OFF_BAR + 256 + 1024;
+constexpr uint32_t STK_IDESC_SU = idesc_i8(BM, STK_N, true, false);
+constexpr uint32_t STK_IDESC_UU = idesc_i8(BM, STK_N, false, false);
+static_assert(STK_TILE % 1024 == 0, "stacked tiles keep the 1024-byte swizzle alignment");
+
+template <int DT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+conv_stk_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                const ConvWinParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STK_OFF_BAR);
+    uint64_t* a_full = bars;
+    uint64_t* a_empty = bars + 2;
+    uint64_t* acc_full = bars + 4;
+    uint64_t* acc_empty = bars + 5;
+    uint64_t* drain_bar = bars + 6;
+    uint64_t* w_full = bars + 7;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nkb = p.taps * p.Cg;
+    const int npairs = (nkb + 1) / 2;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(smem_u32(a_full + i), 1);
+            mbar_init(smem_u32(a_empty + i), 1);
+        }
+        mbar_init(smem_u32(acc_full), 1);
+        mbar_init(smem_u32(acc_empty), NUM_EPI_WARPS);
+        mbar_init(smem_u32(drain_bar), 1);
+        mbar_init(smem_u32(w_full), 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmX);
+        tma_prefetch_desc(&tmW);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int64_t plane = static_cast<int64_t>(p.Hp) * p.Wp;
+
+    if (warp == 0) {
+        // ---------------- TMA producer: stacked weights once, a window per channel group ----------------
+        int ab = 0;
+        uint32_t aph = 0;
+        uint32_t a_last[2] = {0, 0};
+        bool a_used[2] = {false, false};
+        bool ok = true;
+        if (lane == 0) {
+            const uint32_t fbar = smem_u32(w_full);
+            mbar_arrive_expect_tx(fbar, static_cast<uint32_t>(npairs * STK_TILE));
+            for (int q = 0; q < npairs; ++q)
+                tma_load_3d(smem_u32(smem + STK_OFF_B + q * STK_TILE), &tmW, fbar, 0, q * STK_N, 0);
+        }
+        __syncwarp();
+        for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+            const int pt = t % p.pos_tiles;
+            const int n = t / p.pos_tiles;
+            const int row0 = static_cast<int>(n * plane) + pt * BM;
+            for (int g = 0; g < p.Cg && ok; ++g) {
+                if (!mbar_wait_bounded(smem_u32(a_empty + ab), aph ^ 1u, abort_flag, p.err, kDevErrWaitEmpty)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t fbar = smem_u32(a_full + ab);
+                    mbar_arrive_expect_tx(fbar, static_cast<uint32_t>(p.win_rows * KB));
+                    tma_load_3d(smem_u32(smem + ab * WIN_BYTES), &tmX, fbar, g * KB, row0, 0);
+                }
+                __syncwarp();
+                a_used[ab] = true;
+                a_last[ab] = aph;
+                if (++ab == 2) { ab = 0; aph ^= 1u; }
+            }
+        }
+        volatile int no_abort = 0;
+        mbar_wait_bounded(smem_u32(w_full), 0, &no_abort, p.err, kDevErrWaitDrain);
+        for (int i = 0; i < 2; ++i)
+            if (a_used[i]) mbar_wait_bounded(smem_u32(a_full + i), a_last[i], &no_abort, p.err, kDevErrWaitDrain);
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        int ab = 0;
+        uint32_t aph = 0;
+        bool ok = mbar_wait_bounded(smem_u32(w_full), 0, abort_flag, p.err, kDevErrWaitFull);
+        int local = 0;
+        const uint32_t acc1 = tmem_base, acc2 = tmem_base + STK_N;
+        for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++local) {
+            if (!mbar_wait_bounded(smem_u32(acc_empty), (static_cast<uint32_t>(local) & 1u) ^ 1u, abort_flag,
+                                   p.err, kDevErrWaitAccEmpty))
+                break;
+            tc_fence_after();
+            for (int g = 0; g < p.Cg && ok; ++g) {
+                if (!mbar_wait_bounded(smem_u32(a_full + ab), aph, abort_flag, p.err, kDevErrWaitFull)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t win = smem_u32(smem + ab * WIN_BYTES);
+                if (lane == 0) {
+                    for (int tap = 0; tap < p.taps; ++tap) {
+                        const int kb = tap * p.Cg + g;
+                        const uint32_t a_row = win + static_cast<uint32_t>(p.tap_off[tap]) * KB;
+                        const uint32_t b_row = smem_u32(smem + STK_OFF_B + (kb >> 1) * STK_TILE) + (kb & 1) * 64;
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const uint64_t a_hi = smem_desc_kmajor_sw128(a_row + u * 32);
+                            const uint64_t a_lo = smem_desc_kmajor_sw128(a_row + 64 + u * 32);
+                            const uint64_t b = smem_desc_kmajor_sw128(b_row + u * 32);
+                            const uint32_t acc = (g > 0 || tap > 0 || u > 0) ? 1u : 0u;
+                            tc_mma_i8(acc1, a_hi, b, STK_IDESC_SU, acc);
+                            tc_mma_i8(acc2, a_lo, b, STK_IDESC_UU, acc);
+                        }
+                    }
+                    tc_commit(smem_u32(a_empty + ab));
+                }
+                __syncwarp();
+                if (++ab == 2) { ab = 0; aph ^= 1u; }
+            }
+            if (!ok) break;
+            if (lane == 0) tc_commit(smem_u32(acc_full));
+            __syncwarp();
+        }
+        if (lane == 0) tc_commit(smem_u32(drain_bar));
+        __syncwarp();
+        volatile int no_abort = 0;
+        mbar_wait_bounded(smem_u32(drain_bar), 0, &no_abort, p.err, kDevErrWaitDrain);
+    } else {
+        // ---------------- epilogue (warps 2..17): 16 filters of 32 positions each ----------------
+        const int quarter = warp & 3;
+        const int sub = (warp - 2) >> 2;
+        const int row = quarter * 32 + lane;
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        const double s = dequant_scale(__ldg(p.amax_x), __ldg(p.amax_w));
+        const int64_t oplane = static_cast<int64_t>(p.OH) * p.OW;
+        constexpr int ES = DT == 0 ? 2 : 4;
+        const int f0 = sub * 16;
+        int local = 0;
+        for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++local) {
+            const int pt = t % p.pos_tiles;
+            const int n = t / p.pos_tiles;
+            if (!mbar_wait_bounded(smem_u32(acc_full), static_cast<uint32_t>(local) & 1u, abort_flag, p.err,
+                                   kDevErrWaitAccFull))
+                break;
+            tc_fence_after();
+            uint32_t h1[16], m1[16], m2[16], l2[16], s_hi, s_lo;
+            tmem_ld_32x32b_x16(t_row + f0, h1);
+            tmem_ld_32x32b_x16(t_row + 64 + f0, m1);
+            tmem_ld_32x32b_x16(t_row + STK_N + f0, m2);
+            tmem_ld_32x32b_x16(t_row + STK_N + 64 + f0, l2);
+            tmem_ld_32x32b_x1(t_row + 128, s_hi);
+            tmem_ld_32x32b_x1(t_row + STK_N + 128, s_lo);
+            tc_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(acc_empty));  // TMEM free for the next tile
+            const int pos = pt * BM + row;
+            const int oh = pos / p.Wp, ow = pos - (pos / p.Wp) * p.Wp;
+            if (oh >= p.OH || ow >= p.OW || f0 >= p.F) continue;
+            const int64_t pix = static_cast<int64_t>(oh) * p.OW + ow;
+            char* o = static_cast<char*>(p.out) + ((static_cast<int64_t>(n) * p.F + f0) * oplane + pix) * ES;
+            const int64_t step = oplane * ES;
+            const int nf = min(16, p.F - f0);
+            const uint32_t c_hi = 128u * s_hi, c_lo = 128u * s_lo;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const uint32_t hh = h1[j] - c_hi;
+                const uint32_t mid = m1[j] + m2[j] - c_lo;
+                const double v = __dmul_rn(limb_acc_to_double(hh, mid, l2[j]), s);
+                if constexpr (DT == 0) {
+                    __half h = __double2half(v);
+                    if (p.bias != nullptr) h = __hadd(h, static_cast<const __half*>(p.bias)[f0 + j < p.F ? f0 + j : 0]);
+                    if (j < nf) *reinterpret_cast<__half*>(o + j * step) = h;
+                } else {
+                    float r = __double2float_rn(v);
+                    if (p.bias != nullptr) r = __fadd_rn(r, static_cast<const float*>(p.bias)[f0 + j < p.F ? f0 + j : 0]);
+                    if (j < nf) *reinterpret_cast<float*>(o + j * step) = r;
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
 // ---- operand quantisation into 128-byte limb rows ---------------------------
 
 constexpr int XQ_W = 128;   // pixels per block pass
@@ -764,6 +988,47 @@ __global__ void zero_ring_kernel(uint8_t* __restrict__ xl, int64_t N, int H, int
     }
 }
 
+// Stacked weight tiles for conv_stk_kernel: [pairs][144 rows][128 B]; byte
+// 64 h + c of row n in pair p belongs to K step kb = 2p + h (tap kb / Cg,
+// channel group kb % Cg, channel c of the group): rows 0-63 hold
+// (q >> 8) + 128 of filter n, rows 64-127 q & 255 of filter n - 64, rows
+// 128-143 ones.  Thread per 16-byte piece.
+template <typename T>
+__global__ void w_stack_kernel(const T* __restrict__ w, int F, int C, int taps, int Cg, int npairs,
+                               const float* __restrict__ amax, uint8_t* __restrict__ ws) {
+    const int64_t total = static_cast<int64_t>(npairs) * STK_N * 8;
+    const float inv = quant_inv(__ldg(amax));
+    const int nkb = taps * Cg;
+    for (int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < total;
+         it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int piece = static_cast<int>(it & 7);  // 16-byte piece of the 128-byte row
+        const int64_t r = it >> 3;
+        const int n = static_cast<int>(r % STK_N);
+        const int pair = static_cast<int>(r / STK_N);
+        const int h = piece >> 2, pc = piece & 3;
+        const int kb = 2 * pair + h;
+        uint8_t b[16];
+        if (n >= 128) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) b[j] = 1;
+        } else {
+            const int f = n & 63;
+            const int tap = kb / Cg, g = kb - (kb / Cg) * Cg;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int c = g * 64 + pc * 16 + j;
+                int q = 0;
+                if (kb < nkb && f < F && c < C)
+                    q = quant_one(ldt<T>(w, (static_cast<int64_t>(f) * C + c) * taps + tap), inv);
+                b[j] = static_cast<uint8_t>(n < 64 ? ((q >> 8) + 128) & 0xFF : q & 0xFF);
+            }
+        }
+        uint4 v;
+        memcpy(&v, b, 16);
+        *reinterpret_cast<uint4*>(ws + r * KB + piece * 16) = v;
+    }
+}
+
 // Weight limb rows [F][taps][Cg][128 B].  One block per (filter, 64-channel
 // group, run of WQ_TAPS taps): the 64 x WQ_TAPS codes are read with the taps
 // contiguous (OI[D]HW order), quantised into shared memory, and each thread
@@ -832,6 +1097,21 @@ int launch_win(const CUtensorMap& tx, const CUtensorMap& tw, const ConvWinParams
     return launch_status("conv2d window implicit GEMM");
 }
 
+template <int DT>
+int launch_stk(const CUtensorMap& tx, const CUtensorMap& tw, const ConvWinParams& p, int dev, cudaStream_t stream) {
+    static std::once_flag once[64];
+    static cudaError_t err[64];
+    const int slot = std::min(dev, 63);
+    std::call_once(once[slot], [&] {
+        err[slot] = cudaFuncSetAttribute(conv_stk_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, STK_SMEM);
+    });
+    if (err[slot] != cudaSuccess) TK_FAIL(TK_ERR_CUDA, "conv smem attribute: %s", cudaGetErrorString(err[slot]));
+    TK_CHECK_ARG(p.tiles_f == 1, "conv stacked kernel: at most 64 filters");
+    const int grid = std::min(p.tiles, sm_count(dev));
+    conv_stk_kernel<DT><<<grid, NUM_THREADS, STK_SMEM, stream>>>(tx, tw, p);
+    return launch_status("conv2d stacked window implicit GEMM");
+}
+
 // The window variant applies when one window of 128 + max tap offset rows
 // fits a TMA box.
 bool window_fits(int64_t KH, int64_t KW, int64_t dh, int64_t dw, int64_t Wp) {
@@ -845,8 +1125,10 @@ bool window_fits(int64_t KH, int64_t KW, int64_t dh, int64_t dw, int64_t Wp) {
 size_t conv_tc_workspace(int64_t N, int64_t C, int64_t D, int64_t H, int64_t W, int64_t F, int64_t KD,
                          int64_t KH, int64_t KW, int64_t ph, int64_t pw) {
     const int64_t Cg = ceil_div(C, 64);
+    const int64_t nkb = KD * KH * KW * Cg;
+    const int64_t w_bytes = std::max<int64_t>(F * nkb * 128, ceil_div(nkb, 2) * STK_TILE);
     return round_up(static_cast<size_t>(N * D * (H + 2 * ph) * (W + 2 * pw) * Cg * 128), 1024) +
-           round_up(static_cast<size_t>(F * KD * KH * KW * Cg * 128), 1024);
+           round_up(static_cast<size_t>(w_bytes), 1024);
 }
 
 // Implicit-GEMM conv (2-D with D = KD = 1, or 3-D) for groups == 1 and
@@ -887,21 +1169,38 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
                       reinterpret_cast<uintptr_t>(x) % 16 == 0) ? 1 : 0;
     const int oph = win ? static_cast<int>(ph) : 0, opw = win ? static_cast<int>(pw) : 0;
     const int64_t taps = KD * KH * KW;
+    // stacked-limb window kernel when the stacked filter block stays resident
+    // (TK_CONV_STACKED=0 selects the four-MMA window kernel instead)
+    static const bool stacked_on = [] {
+        const char* v = std::getenv("TK_CONV_STACKED");
+        return v == nullptr || v[0] != '0';
+    }();
+    const int64_t npairs = ceil_div(taps * Cg, 2);
+    const bool stk = win && stacked_on && npairs <= STK_MAX_PAIRS;
     const int64_t wblocks = F * Cg * ceil_div(taps, WQ_TAPS);
     TK_CHECK_ARG(wblocks < (1LL << 31), "conv: weight too large");
     const unsigned wgrid = static_cast<unsigned>(wblocks);
+    const unsigned sgrid = static_cast<unsigned>(ceil_div(npairs * STK_N * 8, 256));
     if (dtype == TK_DTYPE_F16) {
         x_limbs_kernel<__half><<<xgrid, XQ_THREADS, 0, stream>>>(
             static_cast<const __half*>(x), (int)C, DHW, (int)W, oph, opw, (int)sh, (int)sw, (int)Cg, xvec,
             amax_x, xl);
-        w_limbs_kernel<__half><<<wgrid, 128, 0, stream>>>(static_cast<const __half*>(w), (int)F, (int)C,
-                                                          (int)taps, (int)Cg, amax_w, wl);
+        if (stk)
+            w_stack_kernel<__half><<<sgrid, 256, 0, stream>>>(static_cast<const __half*>(w), (int)F, (int)C,
+                                                              (int)taps, (int)Cg, (int)npairs, amax_w, wl);
+        else
+            w_limbs_kernel<__half><<<wgrid, 128, 0, stream>>>(static_cast<const __half*>(w), (int)F, (int)C,
+                                                              (int)taps, (int)Cg, amax_w, wl);
     } else {
         x_limbs_kernel<float><<<xgrid, XQ_THREADS, 0, stream>>>(
             static_cast<const float*>(x), (int)C, DHW, (int)W, oph, opw, (int)sh, (int)sw, (int)Cg, xvec,
             amax_x, xl);
-        w_limbs_kernel<float><<<wgrid, 128, 0, stream>>>(static_cast<const float*>(w), (int)F, (int)C,
-                                                         (int)taps, (int)Cg, amax_w, wl);
+        if (stk)
+            w_stack_kernel<float><<<sgrid, 256, 0, stream>>>(static_cast<const float*>(w), (int)F, (int)C,
+                                                             (int)taps, (int)Cg, (int)npairs, amax_w, wl);
+        else
+            w_limbs_kernel<float><<<wgrid, 128, 0, stream>>>(static_cast<const float*>(w), (int)F, (int)C,
+                                                             (int)taps, (int)Cg, amax_w, wl);
     }
     int rc = launch_status("conv2d limbs");
     if (rc) return rc;
@@ -911,7 +1210,18 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
     const bool narrow = F <= 64;
     const int BN = narrow ? ConvNarrow::BN : ConvWide::BN;
     CUtensorMap tx, tw;
-    {
+    if (stk) {
+        // [pairs * 144 rows][128 B], one 144-row box per pair of K steps
+        const uint64_t rows = static_cast<uint64_t>(npairs * STK_N);
+        cuuint64_t dims[3] = {128, rows, 1};
+        cuuint64_t strides[2] = {128, 128 * rows};
+        cuuint32_t box[3] = {128, static_cast<cuuint32_t>(STK_N), 1};
+        cuuint32_t estr[3] = {1, 1, 1};
+        CUresult r = enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, wl, dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) TK_FAIL(TK_ERR_CUDA, "conv2d stacked weight tensor map failed (%d)", (int)r);
+    } else {
         const uint64_t row = static_cast<uint64_t>(taps * Cg) * 128;
         cuuint64_t dims[3] = {row, static_cast<cuuint64_t>(F), 1};
         cuuint64_t strides[2] = {row, row * F};
@@ -956,6 +1266,8 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) TK_FAIL(TK_ERR_CUDA, "conv2d window tensor map failed (%d)", (int)r);
+        if (stk) return dtype == TK_DTYPE_F16 ? launch_stk<0>(tx, tw, q, dev, stream)
+                                              : launch_stk<1>(tx, tw, q, dev, stream);
         if (KH * KW * Cg * WinResident::B_BYTES <= kResWeightBytes)
             return dtype == TK_DTYPE_F16 ? launch_win<WinResident, 0>(tx, tw, q, dev, stream)
                                          : launch_win<WinResident, 1>(tx, tw, q, dev, stream);
