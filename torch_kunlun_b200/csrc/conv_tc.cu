@@ -1141,12 +1141,20 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
     const int dev = current_device();
     const int64_t Cg = ceil_div(C, 64);
     const int64_t Hp = H + 2 * ph, Wp = W + 2 * pw;
-    // window variant: input stored zero-padded, one window per channel group
-    // Window variant for up to 64 filters and a real halo.  A 1x1 filter has
-    // no halo, and with 128-filter tiles the per-tap ring measured faster
-    // (3x3 256->256 @14, batch 64: 77 vs 83 us).
-    const bool win = D == 1 && KD == 1 && F <= 64 && KH * KW > 1 && window_fits(KH, KW, dh, dw, Wp) &&
-                     N * Hp * Wp < (1LL << 31);
+    // Window variant (input stored zero-padded, one window per channel group)
+    // for up to 64 filters.  With 128-filter tiles the per-tap ring measured
+    // faster (3x3 256->256 @14, batch 64: 77 vs 83 us).  A 1x1 filter has no
+    // halo: it takes the window path only with the stacked-limb MMAs, which
+    // halve its MMA count; the four-MMA window kernel was slower than the
+    // per-tap kernel there.
+    static const bool stacked_on = [] {
+        const char* v = std::getenv("TK_CONV_STACKED");
+        return v == nullptr || v[0] != '0';
+    }();
+    const int64_t npairs = ceil_div(KD * KH * KW * Cg, 2);
+    const bool stk_fits = stacked_on && npairs <= STK_MAX_PAIRS;
+    const bool win = D == 1 && KD == 1 && F <= 64 && (KH * KW > 1 || stk_fits) &&
+                     window_fits(KH, KW, dh, dw, Wp) && N * Hp * Wp < (1LL << 31);
     // stored rows per image: the padded plane (window variant, D == 1) or the
     // unpadded volume D*H*W (as D*H rows of W pixels)
     const int64_t sh = win ? Hp : D * H, sw = win ? Wp : W;
@@ -1170,13 +1178,8 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
     const int oph = win ? static_cast<int>(ph) : 0, opw = win ? static_cast<int>(pw) : 0;
     const int64_t taps = KD * KH * KW;
     // stacked-limb window kernel when the stacked filter block stays resident
-    // (TK_CONV_STACKED=0 selects the four-MMA window kernel instead)
-    static const bool stacked_on = [] {
-        const char* v = std::getenv("TK_CONV_STACKED");
-        return v == nullptr || v[0] != '0';
-    }();
-    const int64_t npairs = ceil_div(taps * Cg, 2);
-    const bool stk = win && stacked_on && npairs <= STK_MAX_PAIRS;
+    // (TK_CONV_STACKED=0 selects the four-MMA kernels instead)
+    const bool stk = win && stk_fits;
     const int64_t wblocks = F * Cg * ceil_div(taps, WQ_TAPS);
     TK_CHECK_ARG(wblocks < (1LL << 31), "conv: weight too large");
     const unsigned wgrid = static_cast<unsigned>(wblocks);
