@@ -882,15 +882,26 @@ __device__ __forceinline__ void pack16(const int16_t* q, int stride, uint4& hi, 
     lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-// One block per (image, 128-pixel run of the flattened H*W plane, 64-channel
-// group): the 64 x 128 tile is read along the pixels (contiguous in NCHW,
-// 16-byte vectors when aligned), quantised into shared memory and written as
-// each pixel's 128-byte limb row of that channel group (NHWC order).
+// One block per (image, 128-pixel run of the flattened D*H*W volume, 64-channel
+// group).  Thread (cc4, pg) reads 4 channels x 8 consecutive pixels (16-byte
+// vectors along the pixels when aligned) and forms their codes by
+// magic-number rounding: RN(v * inv) + 1.5 * 2^23 as two unfused binary32
+// operations holds RN(v * inv) rounded to the nearest integer (ties to even)
+// in its low significand bits, so the low 16 bits are the int16 code that
+// quant_one gives (|RN(v * inv)| <= 32767.004 since |v| <= amax; inv == 0
+// makes every code 0).  Byte permutes turn 4 channels' codes of one pixel
+// into a hi word and a lo word, stored into the pixel's 128-byte shared row
+// [hi of 64 channels | lo of 64 channels] -- the output row itself -- which
+// phase 2 copies out with 16-byte stores.  A warp covers 8 pixel groups x 4
+// channel quads (coalesced 128-byte loads per channel); the row's eight
+// 16-byte chunks are XOR-swizzled by the pixel group, so each of its stores
+// hits 32 different banks.
 template <typename T>
 __global__ void __launch_bounds__(XQ_THREADS)
 x_limbs_kernel(const T* __restrict__ x, int C, int64_t HW, int W, int ph, int pw, int Hp, int Wp,
                int Cg, int vec, const float* __restrict__ amax, uint8_t* __restrict__ xl) {
-    __shared__ int16_t q[64][XQ_W + 2];
+    static_assert(XQ_THREADS == 256 && XQ_W == 128, "16 channel quads x 16 pixel groups of 8");
+    __shared__ __align__(16) uint32_t rows[XQ_W][32];
     const int64_t runs = ceil_div_dev(HW, XQ_W);
     const int g = blockIdx.x % Cg;
     const int64_t r = blockIdx.x / Cg;
@@ -899,15 +910,21 @@ x_limbs_kernel(const T* __restrict__ x, int C, int64_t HW, int W, int ph, int pw
     const int pn = static_cast<int>(HW - p0 < XQ_W ? HW - p0 : XQ_W);
     const float inv = quant_inv(__ldg(amax));
     const T* xs = x + (n * C + g * 64) * HW + p0;
-    constexpr int V = 16 / sizeof(T);
-    if (vec) {
-        // V consecutive pixels per thread; HW and p0 are multiples of V
-        for (int it = threadIdx.x; it < 64 * (XQ_W / V); it += XQ_THREADS) {
-            const int cc = it / (XQ_W / V), pv = (it - cc * (XQ_W / V)) * V;
-            float v[V];
-            if (g * 64 + cc < C && pv < pn) {
+    const int pg = (threadIdx.x & 7) + 8 * (threadIdx.x >> 7);
+    const int cc4 = (threadIdx.x >> 3) & 15;
+    const int pbase = pg * 8;
+    uint32_t code[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int cl = cc4 * 4 + i;
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = 0.0f;
+        if (g * 64 + cl < C && pbase < pn && inv != 0.0f) {
+            const T* src = xs + static_cast<int64_t>(cl) * HW + pbase;
+            if (vec && pbase + 8 <= pn) {
                 if constexpr (sizeof(T) == 2) {
-                    const uint4 u = __ldg(reinterpret_cast<const uint4*>(xs + cc * HW + pv));
+                    const uint4 u = __ldg(reinterpret_cast<const uint4*>(src));
                     const __half2* h2 = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
@@ -916,40 +933,43 @@ x_limbs_kernel(const T* __restrict__ x, int C, int64_t HW, int W, int ph, int pw
                         v[2 * e + 1] = f.y;
                     }
                 } else {
-                    const float4 f = __ldg(reinterpret_cast<const float4*>(xs + cc * HW + pv));
-                    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+                    const float4 f0 = __ldg(reinterpret_cast<const float4*>(src));
+                    const float4 f1 = __ldg(reinterpret_cast<const float4*>(src) + 1);
+                    v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+                    v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
                 }
             } else {
 #pragma unroll
-                for (int e = 0; e < V; ++e) v[e] = 0.0f;
+                for (int e = 0; e < 8; ++e)
+                    if (pbase + e < pn) v[e] = ldt<T>(src, e);
             }
+        }
 #pragma unroll
-            for (int e = 0; e < V; ++e) q[cc][pv + e] = static_cast<int16_t>(quant_one(v[e], inv));
-        }
-    } else {
-        for (int it = threadIdx.x; it < 64 * XQ_W; it += XQ_THREADS) {
-            const int cc = it / XQ_W, pp = it - (it / XQ_W) * XQ_W;
-            int v = 0;
-            if (g * 64 + cc < C && pp < pn) v = quant_one(ldt<T>(xs, cc * HW + pp), inv);
-            q[cc][pp] = static_cast<int16_t>(v);
-        }
+        for (int e = 0; e < 8; ++e) code[i][e] = __float_as_uint(__fadd_rn(__fmul_rn(v[e], inv), 12582912.0f));
+    }
+    const int swz = pg & 7;  // chunk swizzle of this pixel group's rows
+    const int hi_w = 4 * ((cc4 >> 2) ^ swz) + (cc4 & 3);
+    const int lo_w = 4 * ((4 + (cc4 >> 2)) ^ swz) + (cc4 & 3);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const uint32_t p01 = __byte_perm(code[0][e], code[1][e], 0x5410);
+        const uint32_t p23 = __byte_perm(code[2][e], code[3][e], 0x5410);
+        rows[pbase + e][hi_w] = __byte_perm(p01, p23, 0x7531);
+        rows[pbase + e][lo_w] = __byte_perm(p01, p23, 0x6420);
     }
     __syncthreads();
-    // pixel (h, w) is row (h + ph) * Wp + (w + pw) of the image's padded plane
+    // pixel (h, w) of the plane is row (h + ph) * Wp + (w + pw) of the image's padded plane
     uint8_t* out = xl + (n * Hp * Wp * Cg + g) * static_cast<int64_t>(128);
-    for (int it = threadIdx.x; it < pn * 4; it += XQ_THREADS) {
-        const int pp = it >> 2, pc = it & 3;
+    for (int it = threadIdx.x; it < pn * 8; it += XQ_THREADS) {
+        const int pp = it >> 3, ch = it & 7;
         const int pix = static_cast<int>(p0) + pp;  // HW < 2^31
         int64_t prow = pix;
         if (ph | pw) {
             const int h = pix / W, w = pix - (pix / W) * W;
             prow = static_cast<int64_t>(h + ph) * Wp + (w + pw);
         }
-        uint4 hi, lo;
-        pack16(&q[pc * 16][pp], XQ_W + 2, hi, lo);
-        uint8_t* dst = out + prow * (Cg * 128) + pc * 16;
-        *reinterpret_cast<uint4*>(dst) = hi;
-        *reinterpret_cast<uint4*>(dst + 64) = lo;
+        *reinterpret_cast<uint4*>(out + prow * (Cg * 128) + ch * 16) =
+            *reinterpret_cast<const uint4*>(&rows[pp][4 * (ch ^ ((pp >> 3) & 7))]);
     }
 }
 
