@@ -791,19 +791,15 @@ attn_out_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__
                 // P = T(exp(s - m) / l), quantised with the slice scale: the
                 // probabilities are >= 0, so q is in [0, 32767] and the hi
                 // limb in [0, 127].
+                // (pr <= max P, so quant_code_bits gives quant_one's code)
                 uint32_t hw[CW / 4], lw[CW / 4];
 #pragma unroll
                 for (int w = 0; w < CW / 4; ++w) {
-                    uint32_t hv = 0, lv = 0;
+                    uint32_t r[4];
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const float pr = round_t(exp_fast(s[4 * w + k] - m_i) * inv_i, DT);
-                        const int q = quant_one(pr, inv_p);
-                        hv |= static_cast<uint32_t>(q >> 8) << (8 * k);
-                        lv |= static_cast<uint32_t>(q & 0xFF) << (8 * k);
-                    }
-                    hw[w] = hv;
-                    lw[w] = lv;
+                    for (int k = 0; k < 4; ++k)
+                        r[k] = quant_code_bits(round_t(exp_fast(s[4 * w + k] - m_i) * inv_i, DT), inv_p);
+                    pack_codes4(r[0], r[1], r[2], r[3], hw[w], lw[w]);
                 }
                 const uint32_t buf = n_p & 1u;
                 if (!mbar_wait_bounded(smem_u32(p_empty + buf), ((n_p >> 1) & 1u) ^ 1u, abort_flag,
@@ -973,20 +969,27 @@ attn_quant_kernel(QuantParams p) {
         for (int it = threadIdx.x; it < rows * pieces; it += QT_THREADS) {
             const int r = it / pieces, pc = it - (it / pieces) * pieces;
             const int c0 = pc * 16;
-            int q[16];
-            if (vec && c0 + 16 <= cols) {
-                float v[16];
-                ld8(x + r * sr + c0, v);
-                ld8(x + r * sr + c0 + 8, v + 8);
+            float v[16];
 #pragma unroll
-                for (int e = 0; e < 16; ++e) q[e] = quant_one(v[e], inv);
-            } else {
+            for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+            if (inv != 0.0f) {  // inv == 0 (amax 0 or not finite): every code is 0
+                if (vec && c0 + 16 <= cols) {
+                    ld8(x + r * sr + c0, v);
+                    ld8(x + r * sr + c0 + 8, v + 8);
+                } else {
 #pragma unroll
-                for (int e = 0; e < 16; ++e)
-                    q[e] = (c0 + e < cols) ? quant_one(ldx<T>(x, r * sr + (c0 + e) * sc), inv) : 0;
+                    for (int e = 0; e < 16; ++e)
+                        if (c0 + e < cols) v[e] = ldx<T>(x, r * sr + (c0 + e) * sc);
+                }
             }
+            uint32_t cb[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) cb[e] = quant_code_bits(v[e], inv);
             uint4 hi, lo;
-            pack16(q, hi, lo);
+            pack_codes4(cb[0], cb[1], cb[2], cb[3], hi.x, lo.x);
+            pack_codes4(cb[4], cb[5], cb[6], cb[7], hi.y, lo.y);
+            pack_codes4(cb[8], cb[9], cb[10], cb[11], hi.z, lo.z);
+            pack_codes4(cb[12], cb[13], cb[14], cb[15], hi.w, lo.w);
             uint8_t* dst = out + r * ld + (c0 / 64) * 128 + (c0 % 64);
             *reinterpret_cast<uint4*>(dst) = hi;
             *reinterpret_cast<uint4*>(dst + 64) = lo;
@@ -1008,7 +1011,9 @@ attn_quant_kernel(QuantParams p) {
                         for (int e = 0; e < 8; ++e) v[e] = 0.0f;
                     }
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) tile[kk][pc * 8 + e] = static_cast<int16_t>(quant_one(v[e], inv));
+                    for (int e = 0; e < 8; ++e)
+                        tile[kk][pc * 8 + e] =
+                            inv != 0.0f ? static_cast<int16_t>(quant_code_bits(v[e], inv) & 0xFFFFu) : int16_t(0);
                 }
             } else {
                 for (int it = threadIdx.x; it < BKEY * cols; it += QT_THREADS) {

@@ -20,6 +20,25 @@ __device__ __forceinline__ float quant_inv(float amax) {
     return (amax > 0.0f && amax != __int_as_float(0x7F800000)) ? __fdiv_rn(32767.0f, amax) : 0.0f;
 }
 
+// The int16 code of quant_one(v, inv) in the low 16 bits of the result, for
+// inv > 0 and |v| <= amax (so |RN(v * inv)| <= 32767.004): RN(v * inv) +
+// 1.5 * 2^23, as two binary32 operations the compiler never fuses, rounds
+// RN(v * inv) to the nearest integer (ties to even, like __float2int_rn) and
+// holds it in two's complement in the low significand bits (magic-number
+// rounding) -- no float-to-int conversion on the special-function pipe.
+// With inv == 0 and finite v the code is 0 as well.
+__device__ __forceinline__ uint32_t quant_code_bits(float v, float inv) {
+    return __float_as_uint(__fadd_rn(__fmul_rn(v, inv), 12582912.0f));
+}
+
+// hi and lo limb bytes of four codes (low 16 bits of r0..r3), code i in byte i.
+__device__ __forceinline__ void pack_codes4(uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3,
+                                            uint32_t& hi, uint32_t& lo) {
+    const uint32_t p01 = __byte_perm(r0, r1, 0x5410), p23 = __byte_perm(r2, r3, 0x5410);
+    lo = __byte_perm(p01, p23, 0x6420);
+    hi = __byte_perm(p01, p23, 0x7531);
+}
+
 __device__ __forceinline__ int quant_one(float v, float inv) {
     const float t = __fmul_rn(v, inv);
     const int q = max(-32767, min(32767, __float2int_rn(t)));
