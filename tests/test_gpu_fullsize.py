@@ -111,3 +111,22 @@ def test_sdpa_bert_size_with_padding_mask():
                       mask=m3, scale=1.0 / math.sqrt(64))[0]
         err = np.abs(out[bb, hh].float().numpy() - want.astype(np.float32)).max()
         assert err <= 2e-2 * max(1.0, float(v[bb, hh].abs().max())), (bb, hh, err)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_linear_and_mm_against_torch_cpu_within_the_stated_bound(dtype):
+    """Against torch's CPU aten (fp32 arithmetic on the same inputs) the
+    quantised path stays within max-abs error 2^-10 * max|A| * max|B| * K, for
+    fp16 and for fp32 inputs: the cfg1 linear whole, and an mm."""
+    g = torch.Generator().manual_seed(50)
+    x = torch.randn(2048, 4096, generator=g).to(dtype)
+    w = (torch.randn(4096, 4096, generator=g) * 0.02).to(dtype)
+    b = (torch.randn(4096, generator=g) * 0.01).to(dtype)
+    got = F.linear(x.to(DEV), w.to(DEV), b.to(DEV)).cpu().float()
+    ref = F.linear(x.float(), w.float(), b.float())
+    bound = 2 ** -10 * x.abs().max().item() * w.abs().max().item() * 4096
+    assert (got - ref).abs().max().item() <= bound
+    a, c = torch.randn(300, 1000, generator=g).to(dtype), torch.randn(1000, 200, generator=g).to(dtype)
+    got = (a.to(DEV) @ c.to(DEV)).cpu().float()
+    ref = a.float() @ c.float()
+    assert (got - ref).abs().max().item() <= 2 ** -10 * a.abs().max().item() * c.abs().max().item() * 1000
