@@ -48,7 +48,7 @@ def test_linear_cfg1_2048x4096x4096():
     _linear_case(2048, 4096, 4096, 0)
 
 
-def test_linear_north_star_4096_cubed():
+def test_linear_4096_cubed():
     _linear_case(4096, 4096, 4096, 10)
 
 
