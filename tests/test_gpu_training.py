@@ -197,3 +197,21 @@ def test_cat_out_variants_and_inplace_division():
     assert torch.equal(x.cpu(), (a.float() * 0.25).half())
     x.sub_(b[:1].to(DEV), alpha=2)
     assert torch.allclose(x.cpu().float(), (a.float() * 0.25).half().float() - 2 * b[:1].float(), atol=2e-3)
+
+
+@pytest.mark.parametrize("H,stride,pad,dil", [(200, 1, 1, 1), (401, 2, 1, 1), (190, 1, 2, 2)])
+def test_conv2d_weight_grad_large_image(H, stride, pad, dil):
+    """One image's output plane longer than the exact limb limit (32768
+    terms): the weight gradient is summed over blocks of output rows."""
+    x = rnd((1, 2, H, H), 70)
+    w = rnd((3, 2, 3, 3), 71, 0.3)
+    xr, wr = x.float().requires_grad_(), w.float().requires_grad_()
+    ref = F.conv2d(xr, wr, stride=stride, padding=pad, dilation=dil)
+    gy = rnd(tuple(ref.shape), 72)
+    ref.backward(gy.float())
+    xk, wk = x.to(DEV).requires_grad_(), w.to(DEV).requires_grad_()
+    F.conv2d(xk, wk, stride=stride, padding=pad, dilation=dil).backward(gy.to(DEV))
+    scale = max(1.0, wr.grad.abs().max().item())
+    assert (wk.grad.cpu().float() - wr.grad).abs().max().item() <= 2e-2 * scale
+    scale = max(1.0, xr.grad.abs().max().item())
+    assert (xk.grad.cpu().float() - xr.grad).abs().max().item() <= 2e-2 * scale

@@ -328,8 +328,11 @@ at::Tensor conv_input_grad(const at::Tensor& g_in, const at::Tensor& weight, con
 // Gradient of conv(x, weight) with respect to the weight [F, C/groups, K...]:
 // per group, the correlation of x and g with batch and channels swapped (the
 // batch is the reduction), scales from the whole x and the whole g.
-// Reductions longer than the exact limb limit (32768) are split over the
-// batch and the fp32 chunk results summed before the one rounding to the
+// Reductions longer than the exact limb limit (32768 terms) are split -- over
+// the batch, and when one image's output volume is longer than that, also
+// over blocks of output rows along the first spatial axis (each block reads
+// the input rows it covers, zero-filled outside the image) -- and the fp32
+// chunk results are summed in a fixed order before the one rounding to the
 // input dtype.
 at::Tensor conv_weight_grad(const at::Tensor& x, const at::Tensor& g_in, at::IntArrayRef w_size,
                             const std::vector<int64_t>& s, const std::vector<int64_t>& p,
@@ -337,12 +340,17 @@ at::Tensor conv_weight_grad(const at::Tensor& x, const at::Tensor& g_in, at::Int
     const int64_t k = static_cast<int64_t>(w_size.size()) - 2;
     at::Tensor g = g_in.contiguous();
     const int64_t N = x.size(0), Cg = w_size[1], F = w_size[0], Fg = F / groups;
-    int64_t per_image = 1;
+    int64_t per_image = 1, rest = 1;  // rest: output elements per row of the first spatial axis
     for (int64_t i = 0; i < k; ++i) per_image *= g.size(2 + i);
-    TORCH_CHECK(per_image <= 32768, "kunlun conv weight gradient: output volume exceeds 32768 elements");
-    const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(N, 32768 / per_image));
+    for (int64_t i = 1; i < k; ++i) rest *= g.size(2 + i);
+    const int64_t O0 = g.size(2), H0 = x.size(2), K0 = w_size[2];
+    TORCH_CHECK(rest <= 32768, "kunlun conv weight gradient: one output row holds more than 32768 elements");
+    const int64_t chunk = per_image <= 32768 ? std::max<int64_t>(1, std::min<int64_t>(N, 32768 / per_image)) : 1;
+    const int64_t rows = per_image <= 32768 ? O0 : std::max<int64_t>(1, 32768 / rest);
     at::Tensor ax = torch_kunlun::amax(x), ag = torch_kunlun::amax(g);
     at::Tensor gw = at::empty(w_size, x.options());
+    std::vector<int64_t> p_rows(p);
+    p_rows[0] = 0;  // row blocks carry their own zero rows
     for (int64_t gr = 0; gr < groups; ++gr) {
         // [Cg, N, S...] and [Fg, N, O...]: batch as channels, reduced over
         at::Tensor xt = x.slice(1, gr * Cg, (gr + 1) * Cg).transpose(0, 1);
@@ -350,11 +358,29 @@ at::Tensor conv_weight_grad(const at::Tensor& x, const at::Tensor& g_in, at::Int
         at::Tensor acc;
         for (int64_t n0 = 0; n0 < N; n0 += chunk) {
             const int64_t n1 = std::min(N, n0 + chunk);
-            at::Tensor xc = xt.slice(1, n0, n1).to(at::kFloat).contiguous();
-            at::Tensor gc = gt.slice(1, n0, n1).to(at::kFloat).contiguous();
-            at::Tensor r = conv_impl(xc, gc, std::nullopt, dl, p, s, 1, ax.data_ptr<float>(), ag.data_ptr<float>());
-            for (int64_t i = 0; i < k; ++i) r = r.slice(2 + i, 0, w_size[2 + i]);  // [Cg, Fg, K...]
-            acc = acc.defined() ? at::add(acc, r) : r;
+            for (int64_t o0 = 0; o0 < O0; o0 += rows) {
+                const int64_t o1 = std::min(O0, o0 + rows);
+                at::Tensor gc = gt.slice(1, n0, n1).slice(2, o0, o1).to(at::kFloat).contiguous();
+                at::Tensor xc;
+                const std::vector<int64_t>* pad = &p;
+                if (o0 == 0 && o1 == O0) {
+                    xc = xt.slice(1, n0, n1).to(at::kFloat).contiguous();
+                } else {
+                    // input rows [i0, i1) feed output rows [o0, o1); outside the image they are zero
+                    const int64_t i0 = o0 * s[0] - p[0];
+                    const int64_t i1 = (o1 - 1) * s[0] - p[0] + dl[0] * (K0 - 1) + 1;
+                    std::vector<int64_t> shape = {Cg, n1 - n0, i1 - i0};
+                    for (int64_t i = 1; i < k; ++i) shape.push_back(x.size(2 + i));
+                    xc = at::zeros(shape, x.options().dtype(at::kFloat));
+                    const int64_t a = std::max<int64_t>(i0, 0), b = std::min<int64_t>(i1, H0);
+                    if (b > a) xc.slice(2, a - i0, b - i0).copy_(xt.slice(1, n0, n1).slice(2, a, b));
+                    pad = &p_rows;
+                }
+                at::Tensor r = conv_impl(xc, gc, std::nullopt, dl, *pad, s, 1, ax.data_ptr<float>(),
+                                         ag.data_ptr<float>());
+                for (int64_t i = 0; i < k; ++i) r = r.slice(2 + i, 0, w_size[2 + i]);  // [Cg, Fg, K...]
+                acc = acc.defined() ? at::add(acc, r) : r;
+            }
         }
         gw.slice(0, gr * Fg, (gr + 1) * Fg).copy_(acc.transpose(0, 1));
     }
