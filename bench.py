@@ -487,7 +487,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-bert", action="store_true", help="skip the encoder-block measurement")
     ap.add_argument("--no-extra", action="store_true", help="skip the bmm and conv measurements")
-    ap.add_argument("--workload", default="linear", choices=["linear", "tp_mlp", "bert"])
+    ap.add_argument("--workload", default="linear", choices=["linear", "tp_mlp", "bert", "rowops"])
     ap.add_argument("--reduce", default="allreduce", choices=["allreduce", "reduce_scatter", "peer", "peer_fused"])
     args = ap.parse_args()
     if args.workload == "tp_mlp" and args.impl != "reference":
@@ -495,6 +495,8 @@ def main():
     if args.impl == "reference":
         return run_reference(args)
     args.warmup = max(args.warmup, 3)
+    if args.workload == "rowops" and args.impl != "reference":
+        return run_rowops(args)
     if args.workload == "bert":
         return run_bert(args)
 
@@ -649,6 +651,51 @@ def run_bert(args):
                        "l2": "flushed between steps (512 MiB device write outside the timed events)"},
             "effective_tops": r["effective_tops"], "clocks": clocks.summary()}
     print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_rowops(args):
+    """The HBM-bound kernels on their benchmark shapes: softmax over
+    [64, 512, 512] fp16 (the cfg2 scores), layer_norm over [16384, 768] fp16
+    (cfg4), and the cfg1 operands' amax + quantise (one F.linear, whose two
+    quantise launches a profiler separates).  Algorithmic bytes: 2 + 2 B per
+    element for softmax and layer_norm (plus gamma / beta), 2 B read (amax) +
+    2 B read + 2 B written (limbs) per element for the quantise."""
+    import torch
+    import torch_kunlun  # noqa: F401
+    kunlun = torch_kunlun.kunlun
+    dev = torch.device("kunlun", 0)
+    scratch = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush = lambda: scratch.fill_(1)  # noqa: E731
+    g = torch.Generator().manual_seed(0)
+    s = torch.randn(64, 512, 512, generator=g).half().to(dev)
+    h = torch.randn(16384, 768, generator=g).half().to(dev)
+    gamma = (1 + 0.1 * torch.randn(768, generator=g)).half().to(dev)
+    beta = (0.1 * torch.randn(768, generator=g)).half().to(dev)
+    x = torch.randn(M, K, generator=g).half().to(dev)
+    w = (torch.randn(N, K, generator=g) * 0.02).half().to(dev)
+    out = {}
+    for name, fn, nbytes in (
+            ("softmax_64x512x512", lambda: torch.softmax(s, -1), 4 * s.numel()),
+            ("layer_norm_16384x768", lambda: torch.nn.functional.layer_norm(h, (768,), gamma, beta, 1e-12),
+             4 * h.numel() + 4 * 768)):
+        ts = timed_steps(fn, args.steps, args.warmup, flush, kunlun)
+        ms = sum(ts) / len(ts)
+        out[name] = {"ms": ms, "gbs": nbytes / (ms / 1000) / 1e9, "bytes": nbytes}
+    torch.nn.functional.linear(x, w)  # the quantise launches, for a profiler
+    kunlun.synchronize()
+    peak = None
+    try:
+        with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")) as f:
+            peak = json.load(f).get("hbm_gbs")
+    except (OSError, ValueError):
+        pass
+    for v in out.values():
+        v["frac_of_8tbs"] = v["gbs"] / 8000.0
+        if peak:
+            v["frac_of_measured"] = v["gbs"] / peak
+    print(json.dumps({"workload": "rowops", "steps": args.steps, "warmup": args.warmup,
+                      "l2": "flushed between steps", "hbm_peak_measured_gbs": peak, **out}), flush=True)
     return 0
 
 
