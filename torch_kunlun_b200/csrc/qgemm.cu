@@ -14,15 +14,18 @@
 // amax_a*amax_b/32767^2 and rounds once to fp16/fp32, then applies the
 // reference's post-GEMM ops in its order (alpha, bias, beta*addend, act).
 //
-// Kernel structure (one persistent CTA per SM, 192 threads):
+// Kernel structure (one persistent CTA per SM, 320 threads):
 //   warp 0      TMA producer: 4 boxes per stage (A hi/lo, B hi/lo), 128 rows
 //               x 128 bytes each, 128-byte swizzle, 3-stage ring;
 //   warp 1      TMEM owner + MMA issuer (one thread), 16 MMAs per stage;
-//   warps 2..5  epilogue: tcgen05.ld of the 3 x 128 accumulator columns of
+//   warps 2..9  epilogue, two per TMEM lane quarter taking alternate
+//               16-column chunks: tcgen05.ld of the three accumulators of
 //               its 32 TMEM lanes, binary64 recombine, dequant, fused ops,
 //               vector stores.
-// TMEM holds the three 128x128 accumulators in 384 of 512 columns; the MMA
-// warp waits for the epilogue to drain them before the next tile.
+// Tiles are 128x128 (K < 2048) or 128x160; the three accumulators fill 384
+// or 480 of the 512 TMEM columns, so the MMA warp waits for the epilogue to
+// drain them before the next tile (the 128x64 / 128x80 overlap variants
+// double-buffer them instead).
 // No TMA multicast is used anywhere.
 #include <cuda.h>
 
