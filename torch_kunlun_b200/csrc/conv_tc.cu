@@ -650,16 +650,20 @@ conv_win_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__
 // whole stacked filter block stays resident; the epilogue copies the
 // accumulators out of TMEM and releases them before its arithmetic, so the
 // single accumulator buffer (288 of 512 columns) overlaps the next tile.
+// Four input windows are in flight, so 1x1 convolutions with several channel
+// groups (one 16 KB window each) keep enough TMA bytes outstanding.
 
 constexpr int STK_N = 144;
 constexpr int STK_TILE = STK_N * KB;             // bytes per pair of K steps
 constexpr int STK_MAX_PAIRS = kResWeightBytes / STK_TILE;
-constexpr int STK_OFF_B = 2 * WIN_BYTES;
+constexpr int STK_NWIN = 4;                     // input windows in flight
+constexpr int STK_OFF_B = STK_NWIN * WIN_BYTES;
 constexpr int STK_OFF_BAR = STK_OFF_B + STK_MAX_PAIRS * STK_TILE;
 constexpr int STK_SMEM = STK_OFF_BAR + 256 + 1024;
 constexpr uint32_t STK_IDESC_SU = idesc_i8(BM, STK_N, true, false);
 constexpr uint32_t STK_IDESC_UU = idesc_i8(BM, STK_N, false, false);
 static_assert(STK_TILE % 1024 == 0, "stacked tiles keep the 1024-byte swizzle alignment");
+static_assert(STK_SMEM <= 227 * 1024, "stacked kernel fits the shared-memory limit of one CTA");
 
 template <int DT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -670,12 +674,12 @@ conv_stk_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STK_OFF_BAR);
     uint64_t* a_full = bars;
-    uint64_t* a_empty = bars + 2;
-    uint64_t* acc_full = bars + 4;
-    uint64_t* acc_empty = bars + 5;
-    uint64_t* drain_bar = bars + 6;
-    uint64_t* w_full = bars + 7;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+    uint64_t* a_empty = bars + STK_NWIN;
+    uint64_t* acc_full = bars + 2 * STK_NWIN;
+    uint64_t* acc_empty = acc_full + 1;
+    uint64_t* drain_bar = acc_full + 2;
+    uint64_t* w_full = acc_full + 3;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 4);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -683,7 +687,7 @@ conv_stk_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__
     const int nkb = p.taps * p.Cg;
     const int npairs = (nkb + 1) / 2;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < STK_NWIN; ++i) {
             mbar_init(smem_u32(a_full + i), 1);
             mbar_init(smem_u32(a_empty + i), 1);
         }
@@ -710,8 +714,9 @@ conv_stk_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__
         // ---------------- TMA producer: stacked weights once, a window per channel group ----------------
         int ab = 0;
         uint32_t aph = 0;
-        uint32_t a_last[2] = {0, 0};
-        bool a_used[2] = {false, false};
+        uint32_t a_last[STK_NWIN];
+        bool a_used[STK_NWIN];
+        for (int i = 0; i < STK_NWIN; ++i) { a_last[i] = 0; a_used[i] = false; }
         bool ok = true;
         if (lane == 0) {
             const uint32_t fbar = smem_u32(w_full);
@@ -737,12 +742,12 @@ conv_stk_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__
                 __syncwarp();
                 a_used[ab] = true;
                 a_last[ab] = aph;
-                if (++ab == 2) { ab = 0; aph ^= 1u; }
+                if (++ab == STK_NWIN) { ab = 0; aph ^= 1u; }
             }
         }
         volatile int no_abort = 0;
         mbar_wait_bounded(smem_u32(w_full), 0, &no_abort, p.err, kDevErrWaitDrain);
-        for (int i = 0; i < 2; ++i)
+        for (int i = 0; i < STK_NWIN; ++i)
             if (a_used[i]) mbar_wait_bounded(smem_u32(a_full + i), a_last[i], &no_abort, p.err, kDevErrWaitDrain);
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
@@ -781,7 +786,7 @@ conv_stk_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__
                     tc_commit(smem_u32(a_empty + ab));
                 }
                 __syncwarp();
-                if (++ab == 2) { ab = 0; aph ^= 1u; }
+                if (++ab == STK_NWIN) { ab = 0; aph ^= 1u; }
             }
             if (!ok) break;
             if (lane == 0) tc_commit(smem_u32(acc_full));
