@@ -8,6 +8,8 @@
 // packed-halves max; quantisation reads 2 B and writes 2 B (two limbs) per
 // element through a 64x64 shared-memory tile so that either operand layout
 // (K-contiguous or transposed) is read and written coalesced.
+#include <mutex>
+
 #include "tk_internal.h"
 #include "tk_numerics.cuh"
 
@@ -501,6 +503,23 @@ int amax_launch(tk_dtype_t dtype, const void* x, int64_t nslices, int64_t slice_
     return launch_status("amax");
 }
 
+// Blocks of amax_multi_kernel that are resident at once on the device: the
+// amax passes size their chunks so that all blocks run in one wave (a second,
+// partial wave left most SMs idle at the end).
+int amax_wave_blocks(tk_dtype_t dtype, int dev) {
+    static std::once_flag once[2];
+    static int per_sm[2] = {0, 0};
+    const int t = dtype == TK_DTYPE_F16 ? 0 : 1;
+    std::call_once(once[t], [&] {
+        int n = 0;
+        const cudaError_t e = t == 0
+            ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, amax_multi_kernel<__half>, kAmaxThreads, 0)
+            : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, amax_multi_kernel<float>, kAmaxThreads, 0);
+        per_sm[t] = (e == cudaSuccess && n > 0) ? n : 4;
+    });
+    return per_sm[t] * sm_count(dev);
+}
+
 // max |x| of two whole tensors in one launch (out[0] for x, out[1] for w):
 // one memset of both slots, one amax_multi_kernel with a chunk size shared by
 // both operands.
@@ -510,7 +529,7 @@ int amax_pair_launch(tk_dtype_t dtype, const void* x, int64_t nx, const void* w,
     TK_CUDA_TRY(cudaMemsetAsync(out, 0, 2 * sizeof(float), stream));
     const int dev = current_device();
     const int64_t chunk_goal = std::max<int64_t>(static_cast<int64_t>(kAmaxThreads) * 64,
-                                                 ceil_div(nx + nw, 8LL * sm_count(dev)));
+                                                 ceil_div(nx + nw, amax_wave_blocks(dtype, dev) - 2));
     AmaxDesc ad[2] = {};
     int64_t blocks[2] = {0, 0};
     const void* src[2] = {x, w};
@@ -598,13 +617,14 @@ int quantise_operands(tk_dtype_t dt, const QuantOperand* ops, int nops, cudaStre
     const int dev = current_device();
     AmaxDesc ad[2] = {};
     int64_t ablocks[2] = {0, 0};
-    // one chunk size for every operand: about eight blocks per SM in all,
-    // so the larger operand gets proportionally more blocks
+    // one chunk size for every operand, all blocks in one resident wave, so
+    // the larger operand gets proportionally more blocks (each operand's last
+    // chunk may be short: two blocks of slack)
     int64_t amax_elems = 0;
     for (int i = 0; i < nops; ++i)
         if (ops[i].given_amax == nullptr) amax_elems += ops[i].batch * ops[i].rows * ops[i].cols;
     const int64_t chunk_goal = std::max<int64_t>(static_cast<int64_t>(kAmaxThreads) * 64,
-                                                 ceil_div(amax_elems, 8LL * sm_count(dev)));
+                                                 ceil_div(amax_elems, amax_wave_blocks(dt, dev) - 2));
     for (int i = 0; i < nops; ++i) {
         const QuantOperand& o = ops[i];
         if (o.given_amax != nullptr || o.batch * o.rows * o.cols == 0) continue;
