@@ -11,7 +11,8 @@
  *     cudaStream_t (NULL = legacy default stream of the current device);
  *   - work is enqueued asynchronously on `stream`; nothing synchronises;
  *   - element strides are in elements, not bytes;
- *   - functions are reentrant and keep no per-call global state.
+ *   - functions are reentrant and keep no per-call global state, except
+ *     tk_qgemm_noalloc, whose scratch is one array shared by all its calls.
  *
  * Each function names the reference interface it replaces: the reference
  * calls Baidu XDNN (baidu::xpu::api::*) from the files cited.
@@ -105,7 +106,9 @@ TK_API int tk_quantize_limbs(tk_dtype_t dtype, const void* x, int64_t batch, int
  * multiply by alpha and round; if bias add bias[n] and round; if addend and
  * beta != 0 add beta*addend (addend element (b,m,n) at
  * addend[b*add_sb + m*add_sm + n*add_sn], strides may be 0 to broadcast) and
- * round; apply act.  K must be <= 32768.
+ * round; apply act.  K is any size: reductions longer than 32768 (and long
+ * reductions with few output tiles) are split into chunks whose exact int64
+ * sums are added in the workspace before the one dequantising rounding.
  */
 typedef struct {
     tk_dtype_t dtype;
@@ -139,7 +142,8 @@ TK_API int tk_qgemm(const tk_qgemm_desc_t* desc, void* workspace, size_t workspa
  * one per operand).  desc->a and desc->b are ignored.  Lets a caller keep the
  * quantised form of an operand that does not change between calls (weights)
  * -- XDNN's fc accepts precomputed max pointers for the same purpose
- * (csrc/ops.cpp:227 passes them as null). */
+ * (csrc/ops.cpp:227 passes them as null).  K must be <= 32768 (no workspace
+ * for a split reduction). */
 TK_API int tk_qgemm_from_limbs(const tk_qgemm_desc_t* desc, const int8_t* a_limbs,
                                const int8_t* b_limbs, const float* amax_a, const float* amax_b,
                                void* stream);
@@ -156,7 +160,9 @@ TK_API int tk_qgemm_from_limbs(const tk_qgemm_desc_t* desc, const int8_t* a_limb
  * TK_ERR_WORKSPACE.  All calls share the array: calls that overlap on the
  * GPU race; calls ordered on one stream are safe.  The first call on a
  * device does a one-time set-up (device address lookup); make it before any
- * stream capture. */
+ * stream capture.  `stream` must belong to the current device (the scratch
+ * used is the current device's); a stream of another device is rejected with
+ * TK_ERR_INVALID_ARG, as are descriptors tk_qgemm rejects. */
 TK_API int tk_qgemm_noalloc(const tk_qgemm_desc_t* desc, void* stream);
 
 /* tk_qgemm (batch 1) with the output rows scattered over destination buffers:
@@ -229,6 +235,32 @@ typedef struct {
 TK_API size_t tk_conv3d_workspace_size(const tk_conv3d_desc_t* desc);
 TK_API int tk_conv3d_q16(const tk_conv3d_desc_t* desc, void* workspace, size_t workspace_bytes,
                          void* stream);
+
+/* ---- convolution weight gradient --------------------------------------------
+ * Replaces the weight-gradient half of conv2d_grad (csrc/autograd.cpp:621-682)
+ * and of the conv3d / conv_transpose2d backward
+ * (csrc/autograd_nn_extra.cpp:427-690) under the same contract as the forward
+ * convolution: x (NCDHW [n,c,d,h,w]) and grad_out ([n,f,od,oh,ow], the
+ * forward's output shape) are each quantised with one per-tensor scale, and
+ *   grad_weight[f][c][t][r][s] = T( scale * sum_{n,od,oh,ow} q(grad_out)[n][f][od][oh][ow]
+ *                                  * q(x)[n][g*C/groups + c][od*sd + t*dd - pd][oh*sh + r*dh - ph][ow*sw + s*dw - pw] )
+ * (zero outside the input, f in group g), an exact integer sum of any length
+ * rounded once.  grad_weight is contiguous [f, c/groups, kd, kh, kw].  A 2-D
+ * convolution is d = kd = 1. */
+typedef struct {
+    tk_dtype_t dtype;
+    int64_t n, c, d, h, w, f, kd, kh, kw;
+    int64_t stride_d, stride_h, stride_w, pad_d, pad_h, pad_w, dil_d, dil_h, dil_w, groups;
+    const void* x;        /* forward input [n, c, d, h, w] */
+    const void* grad_out; /* gradient of the forward output [n, f, od, oh, ow] */
+    void* grad_weight;    /* [f, c/groups, kd, kh, kw] */
+    const float* amax_x;  /* optional precomputed per-tensor amax (device) */
+    const float* amax_g;
+} tk_conv3d_wgrad_desc_t;
+
+TK_API size_t tk_conv3d_wgrad_workspace_size(const tk_conv3d_wgrad_desc_t* desc);
+TK_API int tk_conv3d_wgrad_q16(const tk_conv3d_wgrad_desc_t* desc, void* workspace,
+                               size_t workspace_bytes, void* stream);
 
 /* ---- reduction ---------------------------------------------------------------
  * out[o][i] = sum_r x[o][r][i] over a contiguous [outer, red, inner] tensor,

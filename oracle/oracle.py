@@ -361,6 +361,48 @@ def conv_transpose(x: np.ndarray, w: np.ndarray, bias=None, stride=None, pad=Non
     return _conv_epilogue(acc, x, ax, aw, bias)
 
 
+def conv_weight_grad_acc(qx: np.ndarray, qg: np.ndarray, w_shape, stride, pad, dil, groups) -> np.ndarray:
+    """int64 accumulators of the weight gradient of a convolution with any
+    number of spatial axes: acc[f][c][tap] = sum over images and output
+    positions o of qg[n][f][o] * qx[n][g*cg + c][o*stride + tap*dil - pad]
+    (zero outside the input), per kernel tap as float64 sums of integers below
+    2^53 (exact)."""
+    import itertools
+    k = qx.ndim - 2
+    NB, C = qx.shape[:2]
+    F, cg = w_shape[:2]
+    ks = tuple(w_shape[2:])
+    outs = qg.shape[2:]
+    xp = np.zeros((NB, C) + tuple(qx.shape[2 + i] + 2 * pad[i] for i in range(k)), dtype=np.float64)
+    xp[(slice(None), slice(None)) + tuple(slice(pad[i], pad[i] + qx.shape[2 + i]) for i in range(k))] = qx
+    fg = F // groups
+    acc = np.zeros((F, cg) + ks, dtype=np.float64)
+    gd = qg.astype(np.float64)
+    for g in range(groups):
+        xs = xp[:, g * cg:(g + 1) * cg]
+        gs = gd[:, g * fg:(g + 1) * fg]
+        for tap in itertools.product(*[range(t) for t in ks]):
+            sl = tuple(slice(tap[i] * dil[i], tap[i] * dil[i] + stride[i] * (outs[i] - 1) + 1, stride[i])
+                       for i in range(k))
+            win = xs[(slice(None), slice(None)) + sl]                      # [NB, cg, O...]
+            acc[(slice(g * fg, (g + 1) * fg), slice(None)) + tap] = np.einsum(
+                "nfp,ncp->fc", gs.reshape(NB, fg, -1), win.reshape(NB, cg, -1))
+    return acc.astype(np.int64)
+
+
+def conv_weight_grad(x: np.ndarray, grad_out: np.ndarray, w_shape, stride, pad, dil,
+                     groups=1) -> np.ndarray:
+    """Weight gradient of the quantised convolution: the weight half of the
+    reference's conv2d_grad (csrc/autograd.cpp:621-682) under the forward's
+    contract -- x and grad_out each quantised with one per-tensor scale, the
+    exact integer sum over every image and output pixel, one dequantising
+    rounding to T."""
+    ax, ag = amax(x), amax(grad_out)
+    acc = conv_weight_grad_acc(quant(x, ax), quant(grad_out, ag), w_shape, stride, pad, dil, groups)
+    y = epilogue(acc.reshape(acc.shape[0], -1), ax, ag, x.dtype)
+    return y.reshape(acc.shape)
+
+
 # ---- float row ops (tolerance-level references, float64 internally) ----------
 
 

@@ -34,14 +34,27 @@ def test_abi_version():
     assert C.lib().tk_abi_version() == 1
 
 
-def test_qgemm_rejects_large_k_without_touching_the_device():
+def test_qgemm_long_k_reserves_int64_accumulators():
+    # K > 32768 is split: the workspace adds one int64 sum per output
     d = C.QGemmDesc()
     d.dtype = 0
-    d.batch, d.m, d.n, d.k = 1, 4, 4, 40000
+    d.batch, d.m, d.n, d.k = 1, 40, 30, 40000
+    ws = C.lib().tk_qgemm_workspace_size(ctypes.byref(d))
+    assert ws >= 2 * 40 * 40000 + 2 * 30 * 40000 + 8 * 40 * 30
+    d.k = 1 << 31
     d.out = 1  # never dereferenced: validation fails first
-    rc = C.lib().tk_qgemm(ctypes.byref(d), None, 0, None)
-    assert rc == 1
-    assert b"exceeds 32768" in C.lib().tk_last_error_string()
+    assert C.lib().tk_qgemm(ctypes.byref(d), None, 0, None) == 1
+    assert b"out of range" in C.lib().tk_last_error_string()
+
+
+def test_noalloc_validates_the_descriptor_before_sizing_its_scratch():
+    d = C.QGemmDesc()
+    d.dtype = 0
+    d.batch, d.m, d.n, d.k = 1, -4, 4, 64
+    d.out = 1  # never dereferenced: validation fails first
+    rc = C.lib().tk_qgemm_noalloc(ctypes.byref(d), None)
+    assert rc == 1  # TK_ERR_INVALID_ARG, not TK_ERR_WORKSPACE
+    assert b"negative size" in C.lib().tk_last_error_string()
 
 
 def test_qgemm_workspace_layout():

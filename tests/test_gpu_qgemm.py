@@ -143,11 +143,59 @@ def test_edge_values():
     assert_bits_equal(qgemm(a, w).cpu().numpy(), oracle_qgemm(a, w), "extreme K")
 
 
-def test_k_limit_rejected():
-    a = torch.zeros((1, 4, 32769), dtype=torch.float16, device="cuda")
-    w = torch.zeros((1, 4, 32769), dtype=torch.float16, device="cuda")
-    with pytest.raises(RuntimeError, match="exceeds"):
-        qgemm(a, w)
+@pytest.mark.parametrize("M,N,K", [(130, 70, 40000), (64, 200, 65536), (33, 17, 131072)])
+def test_long_k_split_bit_exact(M, N, K):
+    # K > 32768: the reduction is split into exact int32-limb chunks whose
+    # int64 sums are added in a workspace, then dequantised once
+    a = _rand((1, M, K), torch.float16, 70)
+    w = _rand((1, N, K), torch.float16, 71, 0.02)
+    bias = _rand((N,), torch.float16, 72, 0.01)
+    got = qgemm(a, w, bias=bias)
+    assert_bits_equal(got.cpu().numpy(), oracle_qgemm(a, w, bias=bias), f"K={K}")
+
+
+def test_long_k_split_mm_layout_and_epilogue():
+    # [K, N] operand (transposed quantiser), alpha, beta * addend, relu
+    a = _rand((1, 96, 70000), torch.float16, 73)
+    b_kn = _rand((1, 70000, 40), torch.float16, 74)
+    add = _rand((1, 96, 40), torch.float16, 75)
+    got = qgemm(a, b_kn.transpose(1, 2), addend=add, alpha=0.75, beta=-1.5, act="relu")
+    want = oracle_qgemm(a, b_kn.transpose(1, 2), addend=add, alpha=0.75, beta=-1.5, act="relu")
+    assert_bits_equal(got.cpu().numpy(), want, "split mm epilogue")
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_long_k_split_batched_per_slice(dtype):
+    a = _rand((3, 100, 40000), dtype, 76)
+    w = _rand((3, 50, 40000), dtype, 77)
+    assert_bits_equal(qgemm(a, w).cpu().numpy(), oracle_qgemm(a, w), "split bmm")
+
+
+def test_few_tiles_long_k_split_equals_unsplit_result():
+    # 4 output tiles with K = 8192: the reduction is spread over K chunks to
+    # occupy the SMs; the int64 sums make it identical to the oracle
+    a = _rand((1, 256, 8192), torch.float16, 78)
+    w = _rand((1, 256, 8192), torch.float16, 79)
+    got = qgemm(a, w)
+    assert_bits_equal(got.cpu().numpy(), oracle_qgemm(a, w), "few-tile split")
+    simt = qgemm(a, w, path="simt")
+    assert torch.equal(got.view(torch.int16), simt.view(torch.int16))
+
+
+def test_linear_weight_gradient_over_131072_tokens():
+    # the weight gradient of a linear reduces over the tokens: K = 131072
+    import torch_kunlun  # noqa: F401
+    g = torch.Generator().manual_seed(80)
+    x = torch.randn(131072, 64, generator=g).half()
+    w = (torch.randn(32, 64, generator=g) * 0.02).half()
+    gy = (torch.randn(131072, 32, generator=g) * 0.1).half()
+    xd = x.to("kunlun:0").requires_grad_(True)
+    wd = w.to("kunlun:0").requires_grad_(True)
+    y = torch.nn.functional.linear(xd, wd)
+    y.backward(gy.to("kunlun:0"))
+    got = wd.grad.cpu().numpy()
+    want = O.mm(x.numpy().T.copy(), gy.numpy()).T  # (x^T g)^T, one scale per operand
+    assert_bits_equal(got, want, "linear wgrad K=131072")
 
 
 def test_mid_accumulator_worst_case():
@@ -161,3 +209,30 @@ def test_mid_accumulator_worst_case():
     q = O.quant(np.array([v, 1.0], np.float32))
     assert q[0] == -32513
     assert_bits_equal(got.cpu().numpy(), oracle_qgemm(a, w), "worst-case MID")
+
+
+def test_supplied_amax_below_max_clamps_like_the_oracle():
+    # A caller-supplied amax below max|x| scales some values past the code
+    # range: they clamp to +-32767 (and +-inf with it), NaN gives code 0,
+    # exactly as the oracle's quantiser.
+    import torch_kunlun  # noqa: F401
+    from torch_kunlun_b200 import ops
+    g = torch.Generator().manual_seed(91)
+    x = torch.randn(130, 520, generator=g).half()
+    w = (torch.randn(200, 520, generator=g) * 0.02).half()
+    x[3, 7] = float("inf")
+    x[5, 9] = float("-inf")
+    x[8, 1] = float("nan")
+    finite = x[torch.isfinite(x)]
+    ax = np.float32(0.5 * float(finite.abs().max()))
+    xd, wd = x.to("kunlun:0"), w.to("kunlun:0")
+    ax_t = torch.tensor([ax], dtype=torch.float32).to("kunlun:0")
+    got = ops.linear_scaled(xd, wd, amax_x=ax_t).cpu().numpy()
+    xn, wn = x.numpy(), w.numpy()
+    aw = O.amax(wn)
+    qx = O.quant(xn, ax)
+    assert qx[3, 7] == 32767 and qx[5, 9] == -32767 and qx[8, 1] == 0
+    assert (qx == 32767).sum() > 10 and (qx == -32767).sum() > 10
+    acc = O.gemm_i16_exact(qx, O.quant(wn, aw).T)
+    want = O.epilogue(acc, ax, aw, np.float16)
+    assert_bits_equal(got, want, "linear_scaled with amax_x = max|x| / 2")

@@ -150,10 +150,7 @@ def test_conv2d_backward_is_quantised_conv():
     wt = np.ascontiguousarray(np.flip(np.swapaxes(w.numpy(), 0, 1), (2, 3)))
     want_gi = O.conv2d(gy.numpy(), wt, None, (1, 1), (k - 1 - pad, k - 1 - pad), (1, 1), 1)
     assert_bits_equal(xk.grad.cpu().numpy(), want_gi, "conv grad_input")
-    xt = np.ascontiguousarray(np.swapaxes(x.numpy(), 0, 1)).astype(np.float32)
-    gt = np.ascontiguousarray(np.swapaxes(gy.numpy(), 0, 1)).astype(np.float32)
-    gw = O.conv2d(xt, gt, None, (1, 1), (pad, pad), (1, 1), 1)[:, :, :k, :k]
-    want_gw = np.ascontiguousarray(np.swapaxes(gw, 0, 1)).astype(np.float16)
+    want_gw = O.conv_weight_grad(x.numpy(), gy.numpy(), w.shape, (1, 1), (pad, pad), (1, 1), 1)
     assert_bits_equal(wk.grad.cpu().numpy(), want_gw, "conv grad_weight")
 
 
@@ -175,6 +172,9 @@ def test_conv2d_backward_strided_grouped(stride, groups, dil):
     for got, want in ((xk.grad, xr.grad), (wk.grad, wr.grad), (bk.grad, br.grad)):
         scale = max(1.0, want.abs().max().item())
         assert (got.cpu().float() - want).abs().max().item() <= 2e-2 * scale
+    # the weight gradient is one exact quantised sum: bit-exact against the oracle
+    want_gw = O.conv_weight_grad(x.numpy(), gy.numpy(), w.shape, (stride, stride), (1, 1), (dil, dil), groups)
+    assert_bits_equal(wk.grad.cpu().numpy(), want_gw, "strided/grouped grad_weight")
 
 
 def test_cat_out_variants_and_inplace_division():
@@ -202,7 +202,8 @@ def test_cat_out_variants_and_inplace_division():
 @pytest.mark.parametrize("H,stride,pad,dil", [(200, 1, 1, 1), (401, 2, 1, 1), (190, 1, 2, 2)])
 def test_conv2d_weight_grad_large_image(H, stride, pad, dil):
     """One image's output plane longer than the exact limb limit (32768
-    terms): the weight gradient is summed over blocks of output rows."""
+    terms): the reduction is split into exact chunks whose int64 sums are
+    added before the one rounding, so the weight gradient stays bit-exact."""
     x = rnd((1, 2, H, H), 70)
     w = rnd((3, 2, 3, 3), 71, 0.3)
     xr, wr = x.float().requires_grad_(), w.float().requires_grad_()
@@ -213,5 +214,62 @@ def test_conv2d_weight_grad_large_image(H, stride, pad, dil):
     F.conv2d(xk, wk, stride=stride, padding=pad, dilation=dil).backward(gy.to(DEV))
     scale = max(1.0, wr.grad.abs().max().item())
     assert (wk.grad.cpu().float() - wr.grad).abs().max().item() <= 2e-2 * scale
+    want_gw = O.conv_weight_grad(x.numpy(), gy.numpy(), w.shape, (stride, stride), (pad, pad), (dil, dil), 1)
+    assert_bits_equal(wk.grad.cpu().numpy(), want_gw, f"grad_weight H={H}")
     scale = max(1.0, xr.grad.abs().max().item())
     assert (xk.grad.cpu().float() - xr.grad).abs().max().item() <= 2e-2 * scale
+
+
+def _wgrad_capi(x, gy, w_shape, stride, pad, dil, groups):
+    """tk_conv3d_wgrad_q16 through the C ABI on torch.cuda memory (2-D shapes
+    are passed with depth 1)."""
+    import ctypes
+    from torch_kunlun_b200 import _capi as C
+    x5 = x if x.dim() == 5 else x.unsqueeze(2)
+    g5 = gy if gy.dim() == 5 else gy.unsqueeze(2)
+    ws = tuple(w_shape) if len(w_shape) == 5 else (w_shape[0], w_shape[1], 1) + tuple(w_shape[2:])
+    st = tuple(stride) if len(stride) == 3 else (1,) + tuple(stride)
+    pd = tuple(pad) if len(pad) == 3 else (0,) + tuple(pad)
+    dl = tuple(dil) if len(dil) == 3 else (1,) + tuple(dil)
+    xd, gd = x5.contiguous().cuda(), g5.contiguous().cuda()
+    out = torch.full(w_shape, float("nan"), dtype=x.dtype, device="cuda")
+    d = C.ConvWgradDesc()
+    d.dtype = C.TK_DTYPE_F16 if x.dtype == torch.float16 else C.TK_DTYPE_F32
+    d.n, d.c, d.d, d.h, d.w = x5.shape
+    d.f, _, d.kd, d.kh, d.kw = ws
+    d.stride_d, d.stride_h, d.stride_w = st
+    d.pad_d, d.pad_h, d.pad_w = pd
+    d.dil_d, d.dil_h, d.dil_w = dl
+    d.groups = groups
+    d.x, d.grad_out, d.grad_weight = xd.data_ptr(), gd.data_ptr(), out.data_ptr()
+    L = C.lib()
+    nbytes = L.tk_conv3d_wgrad_workspace_size(ctypes.byref(d))
+    assert nbytes > 0
+    buf = torch.empty(nbytes + 1024, dtype=torch.uint8, device="cuda")
+    base = (buf.data_ptr() + 1023) // 1024 * 1024
+    C.check(L.tk_conv3d_wgrad_q16(ctypes.byref(d), base, nbytes, torch.cuda.current_stream().cuda_stream),
+            "tk_conv3d_wgrad_q16")
+    torch.cuda.synchronize()
+    assert C.device_error(0) == 0
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("case", [
+    # (x shape, F, kernel, stride, pad, dil, groups, dtype)
+    ((4, 64, 20, 20), 64, (3, 3), (1, 1), (1, 1), (1, 1), 1, torch.float16),
+    ((3, 32, 15, 17), 48, (1, 1), (1, 1), (0, 0), (1, 1), 1, torch.float16),
+    ((2, 12, 13, 11), 8, (3, 2), (2, 1), (1, 0), (1, 2), 4, torch.float32),
+    ((4, 16, 7, 7), 16, (3, 3), (1, 1), (1, 1), (1, 1), 16, torch.float16),      # depthwise
+    ((1, 3, 230, 150), 5, (5, 5), (1, 1), (2, 2), (1, 1), 1, torch.float16),     # P = 34500 > 32768
+    ((2, 4, 6, 9, 8), 6, (3, 1, 3), (1, 2, 1), (1, 0, 1), (1, 1, 1), 2, torch.float16),  # 3-D
+])
+def test_conv_weight_grad_capi_bit_exact(case):
+    xs, F_, ks, st, pd, dl, groups, dt = case
+    x = torch.relu(rnd(xs, 40, dtype=torch.float32)).to(dt)
+    k = len(ks)
+    outs = [(xs[2 + i] + 2 * pd[i] - dl[i] * (ks[i] - 1) - 1) // st[i] + 1 for i in range(k)]
+    gy = rnd((xs[0], F_) + tuple(outs), 41, dtype=torch.float32).to(dt)
+    w_shape = (F_, xs[1] // groups) + tuple(ks)
+    got = _wgrad_capi(x, gy, w_shape, st, pd, dl, groups)
+    want = O.conv_weight_grad(x.numpy(), gy.numpy(), w_shape, st, pd, dl, groups)
+    assert_bits_equal(got, want, f"wgrad {case}")

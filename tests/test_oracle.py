@@ -180,3 +180,44 @@ def test_sampled_recomputation_equals_the_whole_oracle():
         acc = (qw @ O.quant(xp, axc).astype(np.int64).reshape(-1))[None]
         got = O.epilogue(acc, axc, awc, np.float16)[0]
         assert np.array_equal(got.view(np.uint16), fullc[n, :, oh, ow].view(np.uint16))
+
+
+def test_conv_weight_grad_accumulators_match_loops_and_float64_convs():
+    """The oracle's weight-gradient accumulators against a scalar loop over the
+    definition (2-D, strided, padded, dilated, grouped) and against torch's
+    CPU float64 conv weight gradients of the same integer codes (exact)."""
+    import torch
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((2, 4, 7, 6)).astype(np.float16)
+    stride, pad, dil, groups = (2, 1), (1, 2), (1, 2), 2
+    w_shape = (6, 2, 3, 2)
+    OH = (7 + 2 - 2 - 1) // 2 + 1
+    OW = (6 + 4 - 2 - 1) // 1 + 1
+    g = rng.standard_normal((2, 6, OH, OW)).astype(np.float16)
+    qx, qg = O.quant(x).astype(np.int64), O.quant(g).astype(np.int64)
+    acc = O.conv_weight_grad_acc(qx, qg, w_shape, stride, pad, dil, groups)
+    want = np.zeros(w_shape, dtype=np.int64)
+    for f in range(6):
+        grp = f // 3
+        for c in range(2):
+            for r in range(3):
+                for s in range(2):
+                    t = 0
+                    for n in range(2):
+                        for oh in range(OH):
+                            for ow in range(OW):
+                                ih, iw = oh * stride[0] - pad[0] + r * dil[0], ow * stride[1] - pad[1] + s * dil[1]
+                                if 0 <= ih < 7 and 0 <= iw < 6:
+                                    t += qg[n, f, oh, ow] * qx[n, grp * 2 + c, ih, iw]
+                    want[f, c, r, s] = t
+    assert np.array_equal(acc, want)
+    tw = torch.nn.grad.conv2d_weight(torch.tensor(qx, dtype=torch.float64), w_shape,
+                                     torch.tensor(qg, dtype=torch.float64), stride, pad, dil, groups)
+    assert np.array_equal(acc, tw.numpy().astype(np.int64))
+    x3 = rng.standard_normal((2, 3, 4, 5, 6)).astype(np.float16)
+    g3 = rng.standard_normal((2, 4, 2, 5, 6)).astype(np.float16)
+    q3, qg3 = O.quant(x3), O.quant(g3)
+    acc3 = O.conv_weight_grad_acc(q3, qg3, (4, 3, 3, 1, 3), (2, 1, 1), (1, 0, 1), (1, 1, 1), 1)
+    tw3 = torch.nn.grad.conv3d_weight(torch.tensor(q3, dtype=torch.float64), (4, 3, 3, 1, 3),
+                                      torch.tensor(qg3, dtype=torch.float64), (2, 1, 1), (1, 0, 1), (1, 1, 1), 1)
+    assert np.array_equal(acc3, tw3.numpy().astype(np.int64))

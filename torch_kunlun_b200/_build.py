@@ -61,16 +61,24 @@ def build_kernels(force: bool = False, verbose_ptxas: bool = False) -> str:
         return KERNEL_LIB
     objdir = os.path.join(PKG, "_build")
     os.makedirs(objdir, exist_ok=True)
-    objs = []
+    headers = glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h")) + \
+        [os.path.join(ROOT, "include", "tk_kernels.h")]
+    objs, cmds = [], []
     for s in srcs:
         o = os.path.join(objdir, os.path.basename(s) + ".o")
+        objs.append(o)
+        if not force and _newer(o, [s] + headers):
+            continue  # object is newer than its source and every shared header
         cmd = [NVCC, *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
                "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr",
                "-I", os.path.join(ROOT, "include"), "-c", s, "-o", o]
         if verbose_ptxas:
             cmd.insert(1, "-Xptxas=-v")
-        _run(cmd)
-        objs.append(o)
+        cmds.append(cmd)
+    # the translation units are independent: compile them concurrently
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as ex:
+        list(ex.map(_run, cmds))
     _run([NVCC, *ARCH_FLAGS, "-shared", "-cudart", "shared", "-o", KERNEL_LIB, *objs,
           "-Xlinker", "-soname=libtk_kernels.so", "-Xlinker", f"-rpath,{CUDA_HOME}/lib64"])
     return KERNEL_LIB

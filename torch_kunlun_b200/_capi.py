@@ -27,6 +27,7 @@ EXPORTED = [
     "tk_binary", "tk_unary", "tk_silu_mul", "tk_conv2d_workspace_size", "tk_conv2d_q16",
     "tk_softmax", "tk_layer_norm", "tk_qgemm_noalloc", "tk_sdpa_workspace_size", "tk_sdpa_q16",
     "tk_reduce_sum", "tk_conv3d_workspace_size", "tk_conv3d_q16", "tk_qgemm_scatter_rows",
+    "tk_conv3d_wgrad_workspace_size", "tk_conv3d_wgrad_q16",
 ]
 
 
@@ -72,6 +73,16 @@ class SdpaDesc(ctypes.Structure):
     ]
 
 
+class ConvWgradDesc(ctypes.Structure):
+    """Mirror of tk_conv3d_wgrad_desc_t."""
+    _fields_ = [("dtype", ctypes.c_int)] + [
+        (n, ctypes.c_int64) for n in (
+            "n", "c", "d", "h", "w", "f", "kd", "kh", "kw", "stride_d", "stride_h", "stride_w",
+            "pad_d", "pad_h", "pad_w", "dil_d", "dil_h", "dil_w", "groups")] + [
+        ("x", ctypes.c_void_p), ("grad_out", ctypes.c_void_p), ("grad_weight", ctypes.c_void_p),
+        ("amax_x", ctypes.c_void_p), ("amax_g", ctypes.c_void_p)]
+
+
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
@@ -96,6 +107,9 @@ def lib() -> ctypes.CDLL:
         L.tk_qgemm_from_limbs.argtypes = [ctypes.POINTER(QGemmDesc), vp, vp, vp, vp, vp]
         L.tk_qgemm_noalloc.argtypes = [ctypes.POINTER(QGemmDesc), vp]
         L.tk_qgemm_debug.argtypes = [ctypes.POINTER(QGemmDesc), vp, ctypes.c_size_t, vp, vp]
+        L.tk_conv3d_wgrad_workspace_size.argtypes = [ctypes.POINTER(ConvWgradDesc)]
+        L.tk_conv3d_wgrad_workspace_size.restype = ctypes.c_size_t
+        L.tk_conv3d_wgrad_q16.argtypes = [ctypes.POINTER(ConvWgradDesc), vp, ctypes.c_size_t, vp]
         _lib = L
     return _lib
 

@@ -33,6 +33,10 @@ int quantize_limbs_launch(tk_dtype_t dtype, const void* x, int64_t batch, int64_
 int qgemm_limbs_ex(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb,
                    const float* amax_a, const float* amax_b, int b_mod, int64_t out_sn,
                    int64_t bias_mod, cudaStream_t stream);
+int qgemm_limbs_acc64(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb,
+                      unsigned long long* acc64, int acc_mod, cudaStream_t stream);
+int qgemm_acc64_finish(const tk_qgemm_desc_t& d, const long long* acc64, int64_t slices,
+                       const float* amax_a, const float* amax_b, int64_t out_sn, cudaStream_t stream);
 size_t conv_tc_workspace(int64_t N, int64_t C, int64_t D, int64_t H, int64_t W, int64_t F, int64_t KD,
                          int64_t KH, int64_t KW, int64_t ph, int64_t pw);
 int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, void* out, int64_t N,
@@ -99,6 +103,59 @@ __global__ void im2col_quant_kernel(const T* __restrict__ x, ConvGeom g, int64_t
         int8_t* base = limbs + (b * 2) * plane + p * ld + k4 * 4;
         *reinterpret_cast<unsigned*>(base) = hi;
         *reinterpret_cast<unsigned*>(base + plane) = lo;
+    }
+}
+
+// Transposed patch gather + quantisation for the weight gradient.  Slice
+// b = (n - n0)*groups + g of images [n0, n0 + nimg), row
+// m = ((c*KD + t)*KH + r)*KW + s over the group's channels, column
+// p = (od*OH + oh)*OW + ow (the reduction axis): x at the input position
+// that output pixel p reads through tap (t, r, s), zero in the padding.
+// 8 columns per thread, written as one 8-byte word per limb plane; columns
+// [P, ld) are zero.
+template <typename T>
+__global__ void im2col_t_quant_kernel(const T* __restrict__ x, ConvGeom g, int64_t n0, int64_t nimg,
+                                      int64_t M, int64_t ld, const float* __restrict__ amax,
+                                      int8_t* __restrict__ limbs) {
+    const int64_t P = g.OD * g.OH * g.OW;
+    const int64_t p8n = ld / 8;
+    const int64_t total = nimg * g.groups * M * p8n;
+    const float inv = quant_inv(amax[0]);
+    const int64_t cg = g.C / g.groups;
+    const int64_t khw = g.KH * g.KW;
+    const int64_t kdhw = g.KD * khw;
+    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t p8 = idx % p8n;
+        const int64_t rest = idx / p8n;
+        const int64_t m = rest % M;
+        const int64_t b = rest / M;
+        const int64_t n = n0 + b / g.groups, grp = b % g.groups;
+        const int64_t c = m / kdhw;
+        const int64_t trs = m - c * kdhw;
+        const int64_t t = trs / khw, rs = trs - t * khw;
+        const int64_t r = rs / g.KW, sx = rs - r * g.KW;
+        const T* xc = x + (n * g.C + grp * cg + c) * g.D * g.H * g.W;
+        unsigned hi[2] = {0u, 0u}, lo[2] = {0u, 0u};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int64_t p = p8 * 8 + j;
+            int q = 0;
+            if (p < P) {
+                const int64_t ow = p % g.OW, oh = (p / g.OW) % g.OH, od = p / (g.OW * g.OH);
+                const int64_t id = od * g.sd - g.pd + t * g.dd;
+                const int64_t ih = oh * g.sh - g.ph + r * g.dh;
+                const int64_t iw = ow * g.sw - g.pw + sx * g.dw;
+                if (id >= 0 && id < g.D && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W)
+                    q = quant_one(ldx<T>(xc, (id * g.H + ih) * g.W + iw), inv);
+            }
+            hi[j >> 2] |= (static_cast<unsigned>(q >> 8) & 0xFFu) << (8 * (j & 3));
+            lo[j >> 2] |= (static_cast<unsigned>(q) & 0xFFu) << (8 * (j & 3));
+        }
+        const int64_t plane = M * ld;
+        int8_t* base = limbs + (b * 2) * plane + m * ld + p8 * 8;
+        *reinterpret_cast<uint2*>(base) = make_uint2(hi[0], hi[1]);
+        *reinterpret_cast<uint2*>(base + plane) = make_uint2(lo[0], lo[1]);
     }
 }
 
@@ -325,10 +382,144 @@ ConvLayout conv_layout(const ConvGeom& g) {
     return L;
 }
 
+// ---- weight gradient ----------------------------------------------------------
+
+// Geometry of a weight-gradient descriptor (the forward convolution's).
+int wgrad_geometry(const tk_conv3d_wgrad_desc_t& d, ConvGeom& g) {
+    tk_conv3d_desc_t f = {};
+    f.dtype = d.dtype;
+    f.n = d.n; f.c = d.c; f.d = d.d; f.h = d.h; f.w = d.w;
+    f.f = d.f; f.kd = d.kd; f.kh = d.kh; f.kw = d.kw;
+    f.stride_d = d.stride_d; f.stride_h = d.stride_h; f.stride_w = d.stride_w;
+    f.pad_d = d.pad_d; f.pad_h = d.pad_h; f.pad_w = d.pad_w;
+    f.dil_d = d.dil_d; f.dil_h = d.dil_h; f.dil_w = d.dil_w;
+    f.groups = d.groups;
+    return geometry(f, g);
+}
+
+constexpr size_t kWgradPatchBudget = 512ull << 20;  // bytes of patch limbs per GEMM launch
+
+struct WgradLayout {
+    int64_t M, P, ld, nchunk;
+    size_t off_amax, off_acc, off_lb, off_la, total;
+};
+
+// [amax x, amax g] | acc64 [groups][M][F/g] | dy limbs [N*groups][2][F/g][ld]
+// | patch limbs of nchunk images [nchunk*groups][2][M][ld]
+WgradLayout wgrad_layout(const ConvGeom& g) {
+    WgradLayout L;
+    L.M = (g.C / g.groups) * g.KD * g.KH * g.KW;
+    L.P = g.OD * g.OH * g.OW;
+    L.ld = static_cast<int64_t>(round_up(static_cast<size_t>(L.P), 16));
+    const int64_t fg = g.F / g.groups;
+    const int64_t per_image = g.groups * 2 * L.M * L.ld;
+    L.nchunk = std::max<int64_t>(1, std::min<int64_t>(g.N, static_cast<int64_t>(kWgradPatchBudget) / per_image));
+    L.nchunk = std::max<int64_t>(1, std::min<int64_t>(L.nchunk, 65535 / g.groups));
+    L.off_amax = 0;
+    L.off_acc = 1024;
+    L.off_lb = round_up(L.off_acc + sizeof(int64_t) * static_cast<size_t>(g.groups * L.M * fg), 1024);
+    L.off_la = round_up(L.off_lb + static_cast<size_t>(g.N * g.groups * 2 * fg * L.ld), 1024);
+    L.total = round_up(L.off_la + static_cast<size_t>(L.nchunk * per_image), 1024);
+    return L;
+}
+
 }  // namespace
 }  // namespace tk
 
 extern "C" {
+
+size_t tk_conv3d_wgrad_workspace_size(const tk_conv3d_wgrad_desc_t* desc) {
+    using namespace tk;
+    if (desc == nullptr) return 0;
+    ConvGeom g;
+    if (wgrad_geometry(*desc, g) != TK_OK || g.N == 0) return 0;
+    return wgrad_layout(g).total;
+}
+
+int tk_conv3d_wgrad_q16(const tk_conv3d_wgrad_desc_t* desc, void* workspace, size_t workspace_bytes,
+                        void* stream_) {
+    using namespace tk;
+    TK_CHECK_ARG(desc != nullptr, "conv wgrad: desc is NULL");
+    const tk_conv3d_wgrad_desc_t& d = *desc;
+    ConvGeom g;
+    int rc = wgrad_geometry(d, g);
+    if (rc) return rc;
+    TK_CHECK_ARG(d.grad_weight != nullptr, "conv wgrad: grad_weight is NULL");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    const int64_t fg = g.F / g.groups, cg = g.C / g.groups;
+    const int64_t wnum = g.F * cg * g.KD * g.KH * g.KW;
+    if (g.N == 0) {  // empty reduction: every gradient is T(0 * scale) = 0
+        TK_CUDA_TRY(cudaMemsetAsync(d.grad_weight, 0, wnum * dtype_size(d.dtype), stream));
+        return TK_OK;
+    }
+    TK_CHECK_ARG(d.x != nullptr && d.grad_out != nullptr, "conv wgrad: NULL pointer");
+    const WgradLayout L = wgrad_layout(g);
+    TK_CHECK_ARG(workspace != nullptr && workspace_bytes >= L.total &&
+                     reinterpret_cast<uintptr_t>(workspace) % 1024 == 0,
+                 "conv wgrad: workspace must be >= %zu bytes and 1024-byte aligned", L.total);
+    TK_CHECK_ARG(g.N * g.groups <= 65535, "conv wgrad: n * groups must be <= 65535");
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* amax = reinterpret_cast<float*>(ws + L.off_amax);
+    const int64_t xnum = g.N * g.C * g.D * g.H * g.W, gnum = g.N * g.F * L.P;
+    const float* ax = d.amax_x;
+    const float* ag = d.amax_g;
+    if (ax == nullptr && ag == nullptr) {
+        rc = amax_pair_launch(d.dtype, d.x, xnum, d.grad_out, gnum, amax, stream);
+        if (rc) return rc;
+        ax = amax;
+        ag = amax + 1;
+    }
+    if (ax == nullptr) {
+        rc = amax_launch(d.dtype, d.x, 1, 0, xnum, amax, stream);
+        if (rc) return rc;
+        ax = amax;
+    }
+    if (ag == nullptr) {
+        rc = amax_launch(d.dtype, d.grad_out, 1, 0, gnum, amax + 1, stream);
+        if (rc) return rc;
+        ag = amax + 1;
+    }
+    auto* acc64 = reinterpret_cast<unsigned long long*>(ws + L.off_acc);
+    int8_t* lb = reinterpret_cast<int8_t*>(ws + L.off_lb);
+    int8_t* la = reinterpret_cast<int8_t*>(ws + L.off_la);
+    TK_CUDA_TRY(cudaMemsetAsync(acc64, 0, sizeof(int64_t) * static_cast<size_t>(g.groups * L.M * fg), stream));
+    // B: grad_out as N*groups slices [F/g, P] (row-contiguous), one scale
+    rc = quantize_limbs_launch(d.dtype, d.grad_out, g.N * g.groups, fg, L.P, fg * L.P, L.P, 1, ag, 0, lb,
+                               stream);
+    if (rc) return rc;
+    tk_qgemm_desc_t q = {};
+    q.dtype = d.dtype;
+    q.m = L.M;
+    q.n = fg;
+    q.k = L.P;
+    q.out = d.grad_weight;
+    q.alpha = 1.0f;
+    q.act = TK_ACT_NONE;
+    q.per_slice_scales = 0;
+    for (int64_t n0 = 0; n0 < g.N; n0 += L.nchunk) {
+        const int64_t nimg = std::min(L.nchunk, g.N - n0);
+        const int64_t total = nimg * g.groups * L.M * (L.ld / 8);
+        const int grid = grid_1d(total, 256);
+        if (d.dtype == TK_DTYPE_F16)
+            im2col_t_quant_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half*>(d.x), g, n0, nimg,
+                                                                    L.M, L.ld, ax, la);
+        else
+            im2col_t_quant_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(d.x), g, n0, nimg,
+                                                                   L.M, L.ld, ax, la);
+        rc = launch_status("conv wgrad patches");
+        if (rc) return rc;
+        q.batch = nimg * g.groups;
+        rc = qgemm_limbs_acc64(q, la, lb + n0 * g.groups * 2 * fg * L.ld, acc64, static_cast<int>(g.groups),
+                               stream);
+        if (rc) return rc;
+    }
+    // grad_weight[grp*F/g + f][c][t][r][s] = epilogue(acc64[grp][(c,t,r,s)][f])
+    q.batch = g.groups;
+    q.out_sb = fg * L.M;
+    q.out_sm = 1;
+    return qgemm_acc64_finish(q, reinterpret_cast<const long long*>(acc64), g.groups, ax, ag, /*out_sn=*/L.M,
+                              stream);
+}
 
 size_t tk_conv3d_workspace_size(const tk_conv3d_desc_t* desc) {
     using namespace tk;

@@ -893,8 +893,8 @@ __device__ __forceinline__ void pack16(const int16_t* q, int stride, uint4& hi, 
 // magic-number rounding: RN(v * inv) + 1.5 * 2^23 as two unfused binary32
 // operations holds RN(v * inv) rounded to the nearest integer (ties to even)
 // in its low significand bits, so the low 16 bits are the int16 code that
-// quant_one gives (|RN(v * inv)| <= 32767.004 since |v| <= amax; inv == 0
-// makes every code 0).  Byte permutes turn 4 channels' codes of one pixel
+// quant_one gives (the scaled value is clamped to the code range first, as
+// the amax may be supplied by the caller; inv == 0 makes every code 0).  Byte permutes turn 4 channels' codes of one pixel
 // into a hi word and a lo word, stored into the pixel's 128-byte shared row
 // [hi of 64 channels | lo of 64 channels] -- the output row itself -- which
 // phase 2 copies out with 16-byte stores.  A warp covers 8 pixel groups x 4
@@ -950,7 +950,7 @@ x_limbs_kernel(const T* __restrict__ x, int C, int64_t HW, int W, int ph, int pw
             }
         }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) code[i][e] = __float_as_uint(__fadd_rn(__fmul_rn(v[e], inv), 12582912.0f));
+        for (int e = 0; e < 8; ++e) code[i][e] = quant_code_bits_clamped(v[e], inv);
     }
     const int swz = pg & 7;  // chunk swizzle of this pixel group's rows
     const int hi_w = 4 * ((cc4 >> 2) ^ swz) + (cc4 & 3);
@@ -1172,12 +1172,8 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
     // halo: it takes the window path only with the stacked-limb MMAs, which
     // halve its MMA count; the four-MMA window kernel was slower than the
     // per-tap kernel there.
-    static const bool stacked_on = [] {
-        const char* v = std::getenv("TK_CONV_STACKED");
-        return v == nullptr || v[0] != '0';
-    }();
     const int64_t npairs = ceil_div(KD * KH * KW * Cg, 2);
-    const bool stk_fits = stacked_on && npairs <= STK_MAX_PAIRS;
+    const bool stk_fits = npairs <= STK_MAX_PAIRS;
     const bool win = D == 1 && KD == 1 && F <= 64 && (KH * KW > 1 || stk_fits) &&
                      window_fits(KH, KW, dh, dw, Wp) && N * Hp * Wp < (1LL << 31);
     // stored rows per image: the padded plane (window variant, D == 1) or the
@@ -1203,7 +1199,7 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
     const int oph = win ? static_cast<int>(ph) : 0, opw = win ? static_cast<int>(pw) : 0;
     const int64_t taps = KD * KH * KW;
     // stacked-limb window kernel when the stacked filter block stays resident
-    // (TK_CONV_STACKED=0 selects the four-MMA kernels instead)
+    // (the four-MMA window kernel otherwise)
     const bool stk = win && stk_fits;
     const int64_t wblocks = F * Cg * ceil_div(taps, WQ_TAPS);
     TK_CHECK_ARG(wblocks < (1LL << 31), "conv: weight too large");

@@ -326,64 +326,52 @@ at::Tensor conv_input_grad(const at::Tensor& g_in, const at::Tensor& weight, con
 }
 
 // Gradient of conv(x, weight) with respect to the weight [F, C/groups, K...]:
-// per group, the correlation of x and g with batch and channels swapped (the
-// batch is the reduction), scales from the whole x and the whole g.
-// Reductions longer than the exact limb limit (32768 terms) are split -- over
-// the batch, and when one image's output volume is longer than that, also
-// over blocks of output rows along the first spatial axis (each block reads
-// the input rows it covers, zero-filled outside the image) -- and the fp32
-// chunk results are summed in a fixed order before the one rounding to the
-// input dtype.
-at::Tensor conv_weight_grad(const at::Tensor& x, const at::Tensor& g_in, at::IntArrayRef w_size,
+// one tk_conv3d_wgrad_q16 call (a 2-D convolution being the 3-D one with
+// depth 1).  Every gradient element is one exact integer sum over all images
+// and output pixels of the quantised grad_output and input, with one scale
+// per whole tensor, rounded once -- the weight-gradient half of the
+// reference's conv2d_grad (csrc/autograd.cpp:621-682) under the forward's
+// contract.
+at::Tensor conv_weight_grad(const at::Tensor& x_in, const at::Tensor& g_in, at::IntArrayRef w_size,
                             const std::vector<int64_t>& s, const std::vector<int64_t>& p,
                             const std::vector<int64_t>& dl, int64_t groups) {
     const int64_t k = static_cast<int64_t>(w_size.size()) - 2;
-    at::Tensor g = g_in.contiguous();
-    const int64_t N = x.size(0), Cg = w_size[1], F = w_size[0], Fg = F / groups;
-    int64_t per_image = 1, rest = 1;  // rest: output elements per row of the first spatial axis
-    for (int64_t i = 0; i < k; ++i) per_image *= g.size(2 + i);
-    for (int64_t i = 1; i < k; ++i) rest *= g.size(2 + i);
-    const int64_t O0 = g.size(2), H0 = x.size(2), K0 = w_size[2];
-    TORCH_CHECK(rest <= 32768, "kunlun conv weight gradient: one output row holds more than 32768 elements");
-    const int64_t chunk = per_image <= 32768 ? std::max<int64_t>(1, std::min<int64_t>(N, 32768 / per_image)) : 1;
-    const int64_t rows = per_image <= 32768 ? O0 : std::max<int64_t>(1, 32768 / rest);
-    at::Tensor ax = torch_kunlun::amax(x), ag = torch_kunlun::amax(g);
+    TORCH_CHECK(k == 2 || k == 3, "kunlun conv weight gradient: 2-D or 3-D convolutions");
+    check_operand(g_in, x_in, "conv weight gradient");
+    at::Tensor x = x_in.contiguous(), g = g_in.contiguous();
+    const int64_t o = k == 3 ? 0 : 1;  // 2-D: the depth axis is absent
+    tk_conv3d_wgrad_desc_t d = {};
+    d.dtype = tk_dtype(x.scalar_type());
+    d.n = x.size(0);
+    d.c = x.size(1);
+    d.d = k == 3 ? x.size(2) : 1;
+    d.h = x.size(3 - o);
+    d.w = x.size(4 - o);
+    d.f = w_size[0];
+    d.kd = k == 3 ? w_size[2] : 1;
+    d.kh = w_size[3 - o];
+    d.kw = w_size[4 - o];
+    d.stride_d = k == 3 ? s[0] : 1;
+    d.stride_h = s[1 - o];
+    d.stride_w = s[2 - o];
+    d.pad_d = k == 3 ? p[0] : 0;
+    d.pad_h = p[1 - o];
+    d.pad_w = p[2 - o];
+    d.dil_d = k == 3 ? dl[0] : 1;
+    d.dil_h = dl[1 - o];
+    d.dil_w = dl[2 - o];
+    d.groups = groups;
+    TORCH_CHECK(g.size(0) == d.n && g.size(1) == d.f, "kunlun conv weight gradient: grad_output shape mismatch");
     at::Tensor gw = at::empty(w_size, x.options());
-    std::vector<int64_t> p_rows(p);
-    p_rows[0] = 0;  // row blocks carry their own zero rows
-    for (int64_t gr = 0; gr < groups; ++gr) {
-        // [Cg, N, S...] and [Fg, N, O...]: batch as channels, reduced over
-        at::Tensor xt = x.slice(1, gr * Cg, (gr + 1) * Cg).transpose(0, 1);
-        at::Tensor gt = g.slice(1, gr * Fg, (gr + 1) * Fg).transpose(0, 1);
-        at::Tensor acc;
-        for (int64_t n0 = 0; n0 < N; n0 += chunk) {
-            const int64_t n1 = std::min(N, n0 + chunk);
-            for (int64_t o0 = 0; o0 < O0; o0 += rows) {
-                const int64_t o1 = std::min(O0, o0 + rows);
-                at::Tensor gc = gt.slice(1, n0, n1).slice(2, o0, o1).to(at::kFloat).contiguous();
-                at::Tensor xc;
-                const std::vector<int64_t>* pad = &p;
-                if (o0 == 0 && o1 == O0) {
-                    xc = xt.slice(1, n0, n1).to(at::kFloat).contiguous();
-                } else {
-                    // input rows [i0, i1) feed output rows [o0, o1); outside the image they are zero
-                    const int64_t i0 = o0 * s[0] - p[0];
-                    const int64_t i1 = (o1 - 1) * s[0] - p[0] + dl[0] * (K0 - 1) + 1;
-                    std::vector<int64_t> shape = {Cg, n1 - n0, i1 - i0};
-                    for (int64_t i = 1; i < k; ++i) shape.push_back(x.size(2 + i));
-                    xc = at::zeros(shape, x.options().dtype(at::kFloat));
-                    const int64_t a = std::max<int64_t>(i0, 0), b = std::min<int64_t>(i1, H0);
-                    if (b > a) xc.slice(2, a - i0, b - i0).copy_(xt.slice(1, n0, n1).slice(2, a, b));
-                    pad = &p_rows;
-                }
-                at::Tensor r = conv_impl(xc, gc, std::nullopt, dl, *pad, s, 1, ax.data_ptr<float>(),
-                                         ag.data_ptr<float>());
-                for (int64_t i = 0; i < k; ++i) r = r.slice(2 + i, 0, w_size[2 + i]);  // [Cg, Fg, K...]
-                acc = acc.defined() ? at::add(acc, r) : r;
-            }
-        }
-        gw.slice(0, gr * Fg, (gr + 1) * Fg).copy_(acc.transpose(0, 1));
-    }
+    d.x = x.data_ptr();
+    d.grad_out = g.data_ptr();
+    d.grad_weight = gw.data_ptr();
+    const int dev = x.device().index();
+    DeviceScope ds(dev);
+    const size_t ws_bytes = tk_conv3d_wgrad_workspace_size(&d);
+    TORCH_CHECK(ws_bytes > 0 || d.n == 0, "kunlun conv weight gradient: bad geometry");
+    at::Tensor ws = workspace(std::max<size_t>(ws_bytes, 1024), x.device());
+    check_tk(tk_conv3d_wgrad_q16(&d, aligned_base(ws), ws_bytes, current_stream(dev)), "tk_conv3d_wgrad_q16");
     return gw;
 }
 

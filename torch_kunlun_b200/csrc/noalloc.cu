@@ -24,7 +24,10 @@
 //     limb planes are fully rewritten;
 //   * the first call on a device performs a one-time set-up (it looks up the
 //     array's device address with cudaGetSymbolAddress while that device is
-//     current); make that first call before any stream capture.
+//     current); make that first call before any stream capture;
+//   * `stream` must belong to the current device: the scratch used is the
+//     current device's copy, so a stream of another GPU is rejected with
+//     TK_ERR_INVALID_ARG instead of running with another GPU's scratch.
 #include <mutex>
 
 #include "tk_internal.h"
@@ -64,6 +67,9 @@ int scratch_address(int device, void** out) {
 extern "C" int tk_qgemm_noalloc(const tk_qgemm_desc_t* desc, void* stream) {
     using namespace tk;
     TK_CHECK_ARG(desc != nullptr, "tk_qgemm_noalloc: desc is NULL");
+    // the same argument checks as tk_qgemm, before any size arithmetic
+    int rc = qgemm_validate(*desc);
+    if (rc) return rc;
     const size_t need = tk_qgemm_workspace_size(desc);
     // tk_qgemm wants a 1024-byte-aligned workspace; the array is 256-aligned.
     const size_t slack = 1024;
@@ -73,8 +79,16 @@ extern "C" int tk_qgemm_noalloc(const tk_qgemm_desc_t* desc, void* stream) {
                 "holds %zu bytes (%zu usable); use tk_qgemm with a caller workspace",
                 need, kNoAllocScratchBytes, kNoAllocScratchBytes - slack);
     }
+    const int dev = current_device();
+    if (stream != nullptr) {
+        int sdev = -1;
+        TK_CUDA_TRY(cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev));
+        TK_CHECK_ARG(sdev == dev,
+                     "tk_qgemm_noalloc: the stream belongs to device %d but device %d is current; "
+                     "make the stream's device current first", sdev, dev);
+    }
     void* base = nullptr;
-    int rc = scratch_address(current_device(), &base);
+    rc = scratch_address(dev, &base);
     if (rc) return rc;
     const uintptr_t b = reinterpret_cast<uintptr_t>(base);
     void* aligned = reinterpret_cast<void*>((b + 1023) & ~static_cast<uintptr_t>(1023));

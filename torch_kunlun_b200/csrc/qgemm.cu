@@ -14,6 +14,17 @@
 // amax_a*amax_b/32767^2 and rounds once to fp16/fp32, then applies the
 // reference's post-GEMM ops in its order (alpha, bias, beta*addend, act).
 //
+// Longer reductions (the reference's fc takes any K) are split: each output
+// tile's K range is cut into chunks of at most 32768 (kb_per_split blocks),
+// every chunk is its own work unit, and the epilogue adds the chunk's exact
+// int64 sum into an int64 workspace with integer atomics (order-independent,
+// so the result is deterministic).  A finishing kernel then converts each
+// int64 sum to binary64 (round to nearest, as the oracle's conversion),
+// dequantises with the single rounding and applies the post-GEMM ops.  The
+// same mode splits long-K problems with too few output tiles to fill the
+// GPU, and sums over batch slices (acc_mod) for reductions that span them
+// (the weight gradient of a convolution).
+//
 // Kernel structure (one persistent CTA per SM, 320 threads):
 //   warp 0      TMA producer: 4 boxes per stage (A hi/lo, B hi/lo), 128 rows
 //               x 128 bytes each, 128-byte swizzle, 3-stage ring;
@@ -133,6 +144,12 @@ __device__ __forceinline__ void* row_out(const EpiParams& p, int64_t b, int64_t 
 struct TileParams {
     int batch, tiles_m, tiles_n, num_tiles, num_kb;
     int b_mod;  // 0: B slice b; else B slice (b % b_mod) (operand shared across images)
+    // K split: every (slice, tile) is ksplit work units of kb_per_split K
+    // blocks each; with acc64 set the epilogue adds exact int64 sums into
+    // acc64[(slice * M + m) * N + n], slice = acc_mod ? b % acc_mod : b.
+    int ksplit, kb_per_split;
+    unsigned long long* acc64;
+    int acc_mod;
     unsigned* err;
 };
 
@@ -170,8 +187,15 @@ __device__ __forceinline__ float epilogue_one(const EpiParams& p, double s, doub
 }
 
 
-__device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b, int& mt, int& nt) {
+// Work unit t -> (K chunk ks, slice b, M tile mt, N tile nt).  The K chunk
+// varies slowest, so the units running together share K ranges and reuse
+// operand tiles through L2 as the unsplit GEMM does.
+__device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b, int& mt, int& nt,
+                                            int& ks) {
     const int per_batch = tp.tiles_m * tp.tiles_n;
+    const int per_split = per_batch * tp.batch;
+    ks = t / per_split;
+    t -= ks * per_split;
     b = t / per_batch;
     const int id = t - b * per_batch;
     constexpr int GROUP = 8;  // M-tiles per raster group (keeps B tiles hot in L2)
@@ -245,9 +269,11 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         for (int s = 0; s < STAGES; ++s) { used[s] = false; last_phase[s] = 0; }
         bool ok = true;
         for (int t = blockIdx.x; t < tp.num_tiles && ok; t += gridDim.x) {
-            int b, mt, nt;
-            decode_tile(tp, t, b, mt, nt);
-            for (int kb = 0; kb < tp.num_kb; ++kb) {
+            int b, mt, nt, ks;
+            decode_tile(tp, t, b, mt, nt, ks);
+            const int kb0 = ks * tp.kb_per_split;
+            const int kb1 = min(tp.num_kb, kb0 + tp.kb_per_split);
+            for (int kb = kb0; kb < kb1; ++kb) {
                 if (!mbar_wait_bounded(smem_u32(empty_bar + stage), phase ^ 1u, abort_flag,
                                        tp.err, kDevErrWaitEmpty)) {
                     ok = false;
@@ -295,7 +321,11 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             const uint32_t acc_hh = tmem_base + buf * C::BUF_COLS;
             const uint32_t acc_mid = acc_hh + BN;
             const uint32_t acc_ll = acc_hh + 2 * BN;
-            for (int kb = 0; kb < tp.num_kb; ++kb) {
+            int b, mt, nt, ks;
+            decode_tile(tp, t, b, mt, nt, ks);
+            const int kb0 = ks * tp.kb_per_split;
+            const int kb1 = min(tp.num_kb, kb0 + tp.kb_per_split);
+            for (int kb = kb0; kb < kb1; ++kb) {
                 if (!mbar_wait_bounded(smem_u32(full_bar + stage), phase, abort_flag, tp.err,
                                        kDevErrWaitFull)) {
                     ok = false;
@@ -313,7 +343,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                         // K advance inside the 128-byte swizzle row: start address
                         // moves by kk*32 bytes (encoded >> 4).
                         const uint64_t off = static_cast<uint64_t>((kk * UMMA_K) >> 4);
-                        const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+                        const uint32_t acc = (kb > kb0 || kk > 0) ? 1u : 0u;
                         tc_mma_i8(acc_hh, a_hi + off, b_hi + off, C::IDESC_SS, acc);
                         tc_mma_i8(acc_mid, a_hi + off, b_lo + off, C::IDESC_SU, acc);
                         tc_mma_i8(acc_mid, a_lo + off, b_hi + off, C::IDESC_US, 1u);
@@ -351,8 +381,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         const void* bias_base = ep.bias;
         int local = 0;
         for (int t = blockIdx.x; t < tp.num_tiles; t += gridDim.x, ++local) {
-            int b, mt, nt;
-            decode_tile(tp, t, b, mt, nt);
+            int b, mt, nt, ks;
+            decode_tile(tp, t, b, mt, nt, ks);
             const int buf = local % NBUF;
             const uint32_t acc_phase = static_cast<uint32_t>(local / NBUF) & 1u;
             if (!mbar_wait_bounded(smem_u32(acc_full + buf), acc_phase, abort_flag, tp.err,
@@ -362,7 +392,9 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             tc_fence_after();
             const uint32_t t_buf = t_row + buf * C::BUF_COLS;
             const int64_t m = static_cast<int64_t>(mt) * BM + row;
-            const double s = epi_scale(ep, b);
+            // a split reduction's chunks only add integer sums: no scale (the
+            // scale pointers may be unset until the finishing pass)
+            const double s = tp.acc64 != nullptr ? 0.0 : epi_scale(ep, b);
             const bool row_ok = m < ep.M;
             int64_t out_row;
             void* const obase = row_out(ep, b, m, out_row);
@@ -385,6 +417,17 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 tmem_ld_32x32b_x16(t_buf + 2 * BN + c * 16, ll);
                 tc_wait_ld();
                 if (!row_ok || n0 >= ep.N) continue;
+                if (tp.acc64 != nullptr) {
+                    // K chunk of a split reduction: add its exact int64 sums
+                    const int64_t slice = tp.acc_mod ? b % tp.acc_mod : b;
+                    unsigned long long* dst = tp.acc64 + (slice * ep.M + m) * ep.N + n0;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (full || n0 + j < ep.N)
+                            atomicAdd(dst + j, static_cast<unsigned long long>(
+                                                   limb_acc_to_i64(hh[j], mid[j], ll[j])));
+                    continue;
+                }
                 if constexpr (DT == 0) {
                     if (fast) {
                         // One binary64 -> binary16 rounding, then the bias and
@@ -561,6 +604,28 @@ __global__ void qgemm_simt_kernel(const int8_t* __restrict__ la, const int8_t* _
     store_t(base, ep.dtype, row_off + n * ep.out_sn, v);
 }
 
+// The epilogue of a split reduction: acc64 [slices][M][N] holds the exact
+// int64 sums; each is converted to binary64 with one round-to-nearest (exact
+// below 2^53) and goes through the same post-GEMM sequence as the fused
+// epilogue.
+__global__ void qgemm_acc64_finish_kernel(const long long* __restrict__ acc, int64_t slices,
+                                          EpiParams ep) {
+    const int64_t mn = ep.M * ep.N;
+    const int64_t total = slices * mn;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t b = i / mn;
+        const int64_t r = i - b * mn;
+        const int64_t m = r / ep.N;
+        const int64_t n = r - m * ep.N;
+        const double s = epi_scale(ep, b);
+        const float v = epilogue_one(ep, s, __ll2double_rn(acc[i]), b, m, n);
+        int64_t row_off;
+        void* base = row_out(ep, b, m, row_off);
+        store_t(base, ep.dtype, row_off + n * ep.out_sn, v);
+    }
+}
+
 // ---- host side --------------------------------------------------------------------
 
 EncodeTiledFn get_encode_fn() {
@@ -596,9 +661,24 @@ int make_limb_map(CUtensorMap* map, const int8_t* base, int64_t planes, int64_t 
     return TK_OK;
 }
 
+// N-tile width of the tile configuration choose_tiles picks (below).
+int tile_bn(int64_t k) { return k >= 2048 ? CfgWider::BN : CfgWide::BN; }
+
+// Split reductions (see the file header): always for K > 32768, and for
+// K >= 4096 when the problem has at most 64 output tiles (a weight-gradient
+// shape: a small output over a long reduction), which would otherwise leave
+// most SMs idle.  The decision depends on the descriptor alone, so the
+// workspace size is known without a device.
+bool split_k(const tk_qgemm_desc_t& d) {
+    if (d.k > kMaxK) return true;
+    const int64_t tiles = d.batch * ceil_div(d.m, BM) * ceil_div(d.n, tile_bn(d.k));
+    return d.k >= 4096 && tiles <= 64;
+}
+
 struct Layout {
     int64_t ld;        // padded K (bytes per limb row)
-    size_t off_amax_a, off_amax_b, off_la, off_lb, total;
+    size_t off_amax_a, off_amax_b, off_la, off_lb, off_acc, total;
+    bool split;        // acc64 [batch][m][n] int64 sums at off_acc
 };
 
 Layout workspace_layout(const tk_qgemm_desc_t& d) {
@@ -609,7 +689,10 @@ Layout workspace_layout(const tk_qgemm_desc_t& d) {
     L.off_amax_b = round_up(sizeof(float) * nscale, 256);
     L.off_la = round_up(L.off_amax_b + sizeof(float) * nscale, 1024);
     L.off_lb = round_up(L.off_la + static_cast<size_t>(d.batch * 2 * d.m * L.ld), 1024);
-    L.total = round_up(L.off_lb + static_cast<size_t>(d.batch * 2 * d.n * L.ld), 1024);
+    L.off_acc = round_up(L.off_lb + static_cast<size_t>(d.batch * 2 * d.n * L.ld), 1024);
+    L.split = split_k(d);
+    L.total = L.off_acc;
+    if (L.split) L.total = round_up(L.off_acc + sizeof(int64_t) * static_cast<size_t>(d.batch * d.m * d.n), 1024);
     return L;
 }
 
@@ -617,9 +700,7 @@ int validate(const tk_qgemm_desc_t& d) {
     TK_CHECK_ARG(d.dtype == TK_DTYPE_F16 || d.dtype == TK_DTYPE_F32, "qgemm: bad dtype %d",
                  (int)d.dtype);
     TK_CHECK_ARG(d.batch >= 0 && d.m >= 0 && d.n >= 0 && d.k >= 0, "qgemm: negative size");
-    TK_CHECK_ARG(d.k <= kMaxK, "qgemm: K=%lld exceeds %d (int32 limb accumulators)",
-                 (long long)d.k, kMaxK);
-    TK_CHECK_ARG(d.batch <= 65535 && d.m < (1LL << 31) && d.n < (1LL << 31),
+    TK_CHECK_ARG(d.batch <= 65535 && d.m < (1LL << 31) && d.n < (1LL << 31) && d.k < (1LL << 31),
                  "qgemm: size out of range");
     TK_CHECK_ARG(d.act >= TK_ACT_NONE && d.act <= TK_ACT_SILU, "qgemm: bad act %d", (int)d.act);
     if (d.batch * d.m * d.n > 0) TK_CHECK_ARG(d.out != nullptr, "qgemm: out is NULL");
@@ -723,29 +804,24 @@ int dispatch_act(int act, int dev, int grid, const CUtensorMap& tmA, const CUten
 }
 
 // Tile configuration for a problem: 128x160 tiles for K >= 2048, else
-// 128x128.  TK_QGEMM_TILE=wide|wider forces one (a tuning override).
-enum class TileChoice { Wide, Wider, Overlap64, Overlap80 };
+// 128x128.  The double-buffered 128x64 / 128x80 configurations
+// (CfgOverlap64 / CfgOverlap80) measured slower on every benchmark shape and
+// are not selected.
+enum class TileChoice { Wide, Wider };
 
 TileChoice choose_tiles(const tk_qgemm_desc_t& d) {
-    static const int forced = [] {
-        const char* v = std::getenv("TK_QGEMM_TILE");
-        if (v == nullptr) return 0;
-        if (std::string(v) == "wide") return 1;
-        if (std::string(v) == "wider") return 2;
-        if (std::string(v) == "overlap64") return 3;
-        if (std::string(v) == "overlap80") return 4;
-        return 0;
-    }();
-    if (forced == 1) return TileChoice::Wide;
-    if (forced == 2) return TileChoice::Wider;
-    if (forced == 3) return TileChoice::Overlap64;
-    if (forced == 4) return TileChoice::Overlap80;
-    return d.k >= 2048 ? TileChoice::Wider : TileChoice::Wide;
+    return tile_bn(d.k) == CfgWider::BN ? TileChoice::Wider : TileChoice::Wide;
 }
+
+// Where a split reduction adds its int64 sums (acc64 == nullptr: no split).
+struct SplitAcc {
+    unsigned long long* acc64 = nullptr;
+    int acc_mod = 0;
+};
 
 template <class C>
 int launch_cfg(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb, int64_t ld,
-               const EpiParams& ep, cudaStream_t stream, int b_mod) {
+               const EpiParams& ep, cudaStream_t stream, int b_mod, const SplitAcc& sa) {
     CUtensorMap tmA, tmB;
     int rc = make_limb_map(&tmA, la, 2 * d.batch, d.m, ld, BM);
     if (rc) return rc;
@@ -756,11 +832,25 @@ int launch_cfg(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb, int
     tp.batch = static_cast<int>(d.batch);
     tp.tiles_m = static_cast<int>(ceil_div(d.m, BM));
     tp.tiles_n = static_cast<int>(ceil_div(d.n, C::BN));
-    const int64_t nt = static_cast<int64_t>(tp.tiles_m) * tp.tiles_n * d.batch;
-    TK_CHECK_ARG(nt < (1LL << 31), "qgemm: too many tiles");
-    tp.num_tiles = static_cast<int>(nt);
+    const int64_t tiles = static_cast<int64_t>(tp.tiles_m) * tp.tiles_n * d.batch;
     tp.num_kb = static_cast<int>(ceil_div(d.k, BK));
     const int dev = current_device();
+    // K chunks: at most kMaxK / BK blocks each (exact int32 limb sums); with
+    // few tiles, enough chunks of at least 16 blocks to occupy the SMs
+    int ksplit = 1;
+    if (sa.acc64 != nullptr) {
+        ksplit = static_cast<int>(ceil_div(tp.num_kb, kMaxK / BK));
+        const int64_t fill = std::min<int64_t>(ceil_div(sm_count(dev), tiles), tp.num_kb / 16);
+        ksplit = static_cast<int>(std::max<int64_t>(ksplit, fill));
+        ksplit = std::max(ksplit, 1);
+    }
+    tp.kb_per_split = static_cast<int>(ceil_div(tp.num_kb, ksplit));
+    tp.ksplit = static_cast<int>(ceil_div(tp.num_kb, tp.kb_per_split));
+    tp.acc64 = sa.acc64;
+    tp.acc_mod = sa.acc_mod;
+    const int64_t nt = tiles * tp.ksplit;
+    TK_CHECK_ARG(nt < (1LL << 31), "qgemm: too many tiles");
+    tp.num_tiles = static_cast<int>(nt);
     tp.err = device_error_word(dev);
     const int grid = static_cast<int>(std::min<int64_t>(nt, sm_count(dev)));
     rc = d.dtype == TK_DTYPE_F16
@@ -771,13 +861,24 @@ int launch_cfg(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb, int
 }
 
 int launch_tc(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb, int64_t ld,
-              const EpiParams& ep, cudaStream_t stream, int b_mod = 0) {
+              const EpiParams& ep, cudaStream_t stream, int b_mod = 0, const SplitAcc& sa = SplitAcc{}) {
+    if (sa.acc64 == nullptr)
+        TK_CHECK_ARG(d.k <= kMaxK, "qgemm: K=%lld exceeds %d on a path without a split workspace",
+                     (long long)d.k, kMaxK);
     switch (choose_tiles(d)) {
-        case TileChoice::Wider: return launch_cfg<CfgWider>(d, la, lb, ld, ep, stream, b_mod);
-        case TileChoice::Overlap64: return launch_cfg<CfgOverlap64>(d, la, lb, ld, ep, stream, b_mod);
-        case TileChoice::Overlap80: return launch_cfg<CfgOverlap80>(d, la, lb, ld, ep, stream, b_mod);
-        default: return launch_cfg<CfgWide>(d, la, lb, ld, ep, stream, b_mod);
+        case TileChoice::Wider: return launch_cfg<CfgWider>(d, la, lb, ld, ep, stream, b_mod, sa);
+        default: return launch_cfg<CfgWide>(d, la, lb, ld, ep, stream, b_mod, sa);
     }
+}
+
+// The finishing pass of a split reduction over acc64 [slices][M][N].
+int launch_finish(const long long* acc64, int64_t slices, const EpiParams& ep, cudaStream_t stream) {
+    const int64_t total = slices * ep.M * ep.N;
+    if (total == 0) return TK_OK;
+    const int dev = current_device();
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), 8LL * sm_count(dev)));
+    qgemm_acc64_finish_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(acc64, slices, ep);
+    return launch_status("qgemm_finish");
 }
 
 int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t stream, Path path,
@@ -844,12 +945,55 @@ int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t str
         return launch_status("qgemm_simt");
     }
 
+    if (L.split && dbg == nullptr && scatter == nullptr) {
+        SplitAcc sa;
+        sa.acc64 = reinterpret_cast<unsigned long long*>(w + L.off_acc);
+        TK_CUDA_TRY(cudaMemsetAsync(sa.acc64, 0, sizeof(int64_t) * static_cast<size_t>(d.batch * d.m * d.n),
+                                    stream));
+        rc = launch_tc(d, la, lb, L.ld, ep, stream, 0, sa);
+        if (rc) return rc;
+        return launch_finish(reinterpret_cast<const long long*>(sa.acc64), d.batch, ep, stream);
+    }
     return launch_tc(d, la, lb, L.ld, ep, stream);
 }
 
 }  // namespace
 
 EncodeTiledFn tensor_map_encoder() { return get_encode_fn(); }
+
+int qgemm_validate(const tk_qgemm_desc_t& d) { return validate(d); }
+
+// Split-reduction GEMM on prepared limbs that only adds its exact int64 sums
+// into acc64 (slice b % acc_mod, or b when acc_mod is 0); the caller zeroes
+// acc64 once and runs qgemm_acc64_finish after the last contribution.  Used
+// by the convolution weight gradient, whose reduction runs over images and
+// pixels.
+int qgemm_limbs_acc64(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb,
+                      unsigned long long* acc64, int acc_mod, cudaStream_t stream) {
+    int rc = validate(d);
+    if (rc) return rc;
+    if (d.batch == 0 || d.m == 0 || d.n == 0 || d.k == 0) return TK_OK;
+    TK_CHECK_ARG(acc64 != nullptr && la != nullptr && lb != nullptr, "qgemm_acc64: NULL pointer");
+    const int64_t ld = static_cast<int64_t>(round_up(static_cast<size_t>(d.k), 16));
+    EpiParams ep = make_epi(d, nullptr, nullptr, nullptr);
+    SplitAcc sa;
+    sa.acc64 = acc64;
+    sa.acc_mod = acc_mod;
+    return launch_tc(d, la, lb, ld, ep, stream, 0, sa);
+}
+
+// The epilogue of d (dequantise with amax_a / amax_b per tensor, alpha,
+// bias, addend, activation) over acc64 [slices][m][n], output element
+// (b, m, n) at out[b*out_sb + m*out_sm + n*out_sn].
+int qgemm_acc64_finish(const tk_qgemm_desc_t& d, const long long* acc64, int64_t slices,
+                       const float* amax_a, const float* amax_b, int64_t out_sn, cudaStream_t stream) {
+    int rc = validate(d);
+    if (rc) return rc;
+    EpiParams ep = make_epi(d, amax_a, amax_b, nullptr);
+    ep.out_sn = out_sn;
+    ep.scale_stride = 0;
+    return launch_finish(acc64, slices, ep, stream);
+}
 
 // Internal entry used by the conv path: GEMM on prepared limbs where the B
 // operand (weights) has b_mod slices shared across the batch, the output is

@@ -323,16 +323,18 @@ __device__ __forceinline__ void load8<float>(const float* p, int64_t n, float (&
 // before the add: a fused multiply-add would round v * inv + 1.5 * 2^23
 // once and break ties of RN(v * inv) (e.g. v = amax / 2 gives
 // RN(v * inv) = 16383.5, code 16384, while the exact product lies just below
-// the tie).  The products run two lanes per instruction; the adds are
-// __fadd_rn, which the compiler never contracts into a multiply-add.
-// Requires inv > 0 and |v| <= amax, which bounds |t| by 32767.004 (the
-// inv == 0 case is handled by the caller: every code is 0).
+// the tie).  The products run two lanes per instruction; each is then
+// clamped to [-32767, 32767] with NaN mapped to 0 (quant_one's clamp: a
+// caller may supply an amax below max |x|, and an infinite input scales to
+// infinity), and the adds are __fadd_rn, which the compiler never contracts
+// into a multiply-add.  The inv == 0 case is handled by the caller: every
+// code is 0.
 __device__ __forceinline__ uint64_t f32x2_mul_add_magic(uint64_t v2, uint64_t inv2) {
     constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
     uint64_t t;
     asm volatile("mul.rn.f32x2 %0, %1, %2;" : "=l"(t) : "l"(v2), "l"(inv2));
-    const float lo = __fadd_rn(__uint_as_float(static_cast<unsigned>(t)), kMagic);
-    const float hi = __fadd_rn(__uint_as_float(static_cast<unsigned>(t >> 32)), kMagic);
+    const float lo = __fadd_rn(clamp_code_range(__uint_as_float(static_cast<unsigned>(t))), kMagic);
+    const float hi = __fadd_rn(clamp_code_range(__uint_as_float(static_cast<unsigned>(t >> 32))), kMagic);
     return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
 }
 

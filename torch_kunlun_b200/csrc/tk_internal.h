@@ -76,4 +76,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn tensor_map_encoder();
 
+// The argument checks of tk_qgemm (sizes, dtype, activation, output pointer).
+int qgemm_validate(const tk_qgemm_desc_t& d);
+
 }  // namespace tk

@@ -26,9 +26,23 @@ __device__ __forceinline__ float quant_inv(float amax) {
 // RN(v * inv) to the nearest integer (ties to even, like __float2int_rn) and
 // holds it in two's complement in the low significand bits (magic-number
 // rounding) -- no float-to-int conversion on the special-function pipe.
-// With inv == 0 and finite v the code is 0 as well.
+// With inv == 0 and finite v the code is 0 as well.  Only for amax values
+// computed from the operand itself; quant_code_bits_clamped takes any v.
 __device__ __forceinline__ uint32_t quant_code_bits(float v, float inv) {
     return __float_as_uint(__fadd_rn(__fmul_rn(v, inv), 12582912.0f));
+}
+
+// RN(v * inv) limited to the code range [-32767, 32767], NaN mapped to 0:
+// quant_one's clamp, for a scaled value that may lie outside the range (an
+// amax supplied by the caller below max |x|, or an infinite input).
+__device__ __forceinline__ float clamp_code_range(float t) {
+    const float c = fminf(fmaxf(t, -32767.0f), 32767.0f);
+    return t == t ? c : 0.0f;
+}
+
+// quant_code_bits for any v and any inv >= 0: equal to quant_one's code.
+__device__ __forceinline__ uint32_t quant_code_bits_clamped(float v, float inv) {
+    return __float_as_uint(__fadd_rn(clamp_code_range(__fmul_rn(v, inv)), 12582912.0f));
 }
 
 // hi and lo limb bytes of four codes (low 16 bits of r0..r3), code i in byte i.
@@ -50,13 +64,18 @@ __device__ __forceinline__ double dequant_scale(float amax_a, float amax_b) {
                      1073676289.0);
 }
 
-// The exact integer 65536*hh + 256*mid + ll of three int32 limb accumulators
-// as binary64, without a conversion instruction: for |acc| < 2^51 the bit
-// pattern of 1.5 * 2^52 plus acc is the binary64 value 1.5 * 2^52 + acc.
+// The exact integer 65536*hh + 256*mid + ll of three int32 limb accumulators.
+__device__ __forceinline__ long long limb_acc_to_i64(uint32_t hh, uint32_t mid, uint32_t ll) {
+    return (static_cast<long long>(static_cast<int32_t>(hh)) << 16) +
+           (static_cast<long long>(static_cast<int32_t>(mid)) << 8) +
+           static_cast<long long>(static_cast<int32_t>(ll));
+}
+
+// The same integer as binary64, without a conversion instruction: for
+// |acc| < 2^51 the bit pattern of 1.5 * 2^52 plus acc is the binary64 value
+// 1.5 * 2^52 + acc.
 __device__ __forceinline__ double limb_acc_to_double(uint32_t hh, uint32_t mid, uint32_t ll) {
-    const long long acc = (static_cast<long long>(static_cast<int32_t>(hh)) << 16) +
-                          (static_cast<long long>(static_cast<int32_t>(mid)) << 8) +
-                          static_cast<long long>(static_cast<int32_t>(ll));
+    const long long acc = limb_acc_to_i64(hh, mid, ll);
     return __longlong_as_double(acc + 0x4338000000000000LL) - 6755399441055744.0;
 }
 
