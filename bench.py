@@ -1,27 +1,39 @@
-"""Benchmark of the int16-quantised dense-op path on B200.
+"""Benchmark of torch_kunlun's int16-quantised dense-op path on B200.
 
-Default workload (one GPU): the single int16-quantised linear of torch_kunlun,
-y = x @ W^T + b with x fp16 [2048, 4096] ~ N(0,1), W fp16 [4096, 4096] ~
-N(0,0.02), b fp16 [4096] ~ N(0,0.01) (seed 0), called as
-torch.nn.functional.linear on kunlun tensors: per-tensor max-abs int16
-quantisation of x and W, exact integer MAC, dequantisation and bias.
-A step is one such call.  Metric: effective int16 TOPS = 2*M*N*K / step time.
+Headline, at every GPU count (N = 1 included): the tensor-parallel
+SiLU-gated MLP of BASELINE's multi-GPU config -- x fp16 [16384, 8192] ~N(0,1),
+gate/up weights [28672, 8192] split by output rows (column-parallel), down
+weight [8192, 28672] split by input columns (row-parallel), all ~N(0,0.02);
+h = T(silu(x Wg^T)) * (x Wu^T), y = sum over ranks of h_r Wd_r^T, the partial
+sums reduce-scattered through the `bkcl` ProcessGroup (NCCL over NVLink).
+Every linear is the int16-quantised GEMM; each rank quantises its own shards.
+A step is one forward of the whole MLP over the 16384 tokens.  Metric:
+aggregate int16 TOPS = 3 * 2 * 16384 * 8192 * 28672 / step time (strong
+scaling: the total work is fixed, split over N ranks).
+
+Outside the timed region every rank checks parity (`parity` / `parity_ok`):
+its GEMMs bit-exact against the oracle on sampled rows of its own shards,
+the SiLU gate within its stated bound, and its reduced rows against the
+rank-ordered fp32 sum of every rank's partial (bit-exact for the
+deterministic reductions, within the fp16 summation bound for NCCL's).
+
+On the N = 1 line (skipped with --no-extra) the other configs are objects,
+each with its own roofline: the single linear 2048x4096x4096 (cfg1, with its
+own end-to-end number), the 4096^3 linear, the BERT-base encoder block
+(tokens/s and per-op shares), the attention-score bmm chain, the ResNet-50
+convolutions and the HBM-bound row kernels.
 
 Arms:
-  default            kunlun device (hand-written sm_100a kernels)
+  default            the kunlun device (hand-written sm_100a kernels)
   --impl reference   the reference path on the host cores: the oracle's CPU
-                     restatement of the quantised fc (oracle/oracle.py)
-
-Multi-GPU (--gpus N under torchrun): the linear does not shard (replicas
-only); every rank runs the same workload on its own GPU, ranks meet at a
-barrier around the timed region and the slowest rank's time is reported;
-value is the aggregate over ranks ("scaling": "weak").
+                     restatement (oracle/), rank 0 only
 """
 
 from __future__ import annotations
 
 import argparse
 import ctypes
+import datetime
 import json
 import os
 import statistics
@@ -32,91 +44,22 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-M, N, K = 2048, 4096, 4096
-OPS_PER_STEP = 2 * M * N * K
-METRIC = "int16-quant linear effective TOPS/GPU (aggregate over GPUs)"
-WORKLOAD = "int16-quantised linear x[2048,4096] @ W[4096,4096]^T + b, fp16 in/out"
-KERNELS_PER_STEP = 3  # amax of x and W, quantise of x and W, limb GEMM + epilogue
-
-
-def make_inputs():
-    import torch
-    g = torch.Generator().manual_seed(0)
-    x = torch.randn(M, K, generator=g).half()
-    w = (torch.randn(N, K, generator=g) * 0.02).half()
-    b = (torch.randn(N, generator=g) * 0.01).half()
-    return x, w, b
-
+# ---- the tensor-parallel MLP --------------------------------------------------
 
 TP_T, TP_H, TP_F = 16384, 8192, 28672
-TP_OPS_PER_STEP = 3 * 2 * TP_T * TP_H * TP_F
-TP_METRIC = "int16-quant TP-MLP effective TOPS (aggregate over GPUs)"
-TP_WORKLOAD = ("tensor-parallel SiLU-gated MLP, x[16384,8192], gate/up [8192,28672] column-split, "
-               "down [28672,8192] row-split, partial sums all-reduced over bkcl (NCCL)")
+TP_OPS = 3 * 2 * TP_T * TP_H * TP_F
+TP_BLOCK = 512  # weights are drawn in blocks of 512 rows/columns, so shards agree for every N
+METRIC = "int16-quant TP-MLP effective TOPS (aggregate over GPUs)"
+WORKLOAD = ("tensor-parallel SiLU-gated MLP: x[16384,8192] fp16, gate/up [28672,8192] column-parallel, "
+            "down [8192,28672] row-parallel, partial sums reduced over bkcl (NCCL)")
+REF_ROWS = 16  # tokens per reference-arm / cpu_baseline sample
 
+# ---- the single-GPU configs (objects on the N = 1 line) ------------------------
 
+M1, N1, K1 = 2048, 4096, 4096
 BERT_B, BERT_L, BERT_H, BERT_HEADS, BERT_F, BERT_TAIL = 32, 512, 768, 12, 3072, 64
 BERT_WORKLOAD = ("BERT-base encoder block forward: hidden 768, 12 heads x 64, FFN 3072 gelu, "
                  "post-LN eps 1e-12, batch 32 x seq 512 fp16, additive mask on the last 64 keys")
-
-
-def bert_inputs():
-    """Seeded block input [32, 512, 768] ~N(0,1), weights ~N(0,0.02), mask."""
-    import torch
-    from torch_kunlun_b200 import encoder
-    g = torch.Generator().manual_seed(0)
-    x = torch.randn(BERT_B, BERT_L, BERT_H, generator=g).half()
-    w = encoder.init_weights(BERT_H, BERT_F, generator=g)
-    mask = encoder.padding_mask(BERT_B, BERT_L, BERT_TAIL)
-    return x, w, mask
-
-
-def bert_cpu_baseline(batch=1, reps=3):
-    """torch CPU aten fp32 eager encoder block on `batch` sequences (all host
-    threads): tokens/s."""
-    import torch
-    import torch.nn.functional as F
-    x, w, mask = bert_inputs()
-    x, mask = x[:batch].float(), mask[:batch].float()
-    f = {k: v.float() for k, v in vars(w).items()}
-    torch.set_num_threads(os.cpu_count() or 1)
-    B, L, H, E = batch, BERT_L, BERT_H, BERT_H // BERT_HEADS
-
-    def block():
-        x2 = x.reshape(B * L, H)
-        qkv = F.linear(x2, f["w_qkv"], f["b_qkv"]).view(B, L, 3, BERT_HEADS, E).permute(2, 0, 3, 1, 4)
-        ctx = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], attn_mask=mask)
-        ctx = ctx.transpose(1, 2).reshape(B * L, H)
-        h = F.layer_norm(x2 + F.linear(ctx, f["w_o"], f["b_o"]), (H,), f["ln1_w"], f["ln1_b"], 1e-12)
-        g = F.gelu(F.linear(h, f["w_1"], f["b_1"]))
-        return F.layer_norm(h + F.linear(g, f["w_2"], f["b_2"]), (H,), f["ln2_w"], f["ln2_b"], 1e-12)
-
-    block()
-    ts = []
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        block()
-        ts.append(time.perf_counter() - t0)
-    return B * L / statistics.median(ts), torch.get_num_threads()
-
-
-def bert_measure(dev, kunlun, steps, warmup, flush):
-    """Device time per encoder block forward (CUDA events) and tokens/s."""
-    from torch_kunlun_b200 import encoder
-    x, w, mask = bert_inputs()
-    xd, wd, md = x.to(dev), w.to(dev), mask.to(dev)
-
-    def step():
-        encoder.encoder_block(xd, wd, md, heads=BERT_HEADS, eps=1e-12)
-
-    times = timed_steps(step, steps, warmup, flush, kunlun)
-    ms = sum(times) / len(times)
-    macs = encoder.encoder_block_macs(BERT_B, BERT_L, BERT_H, BERT_F)
-    return {"tokens_per_s": BERT_B * BERT_L / (ms / 1000), "ms_per_block": ms,
-            "effective_tops": 2 * macs / (ms / 1000) / 1e12, "steps": steps, "warmup": warmup,
-            "workload": BERT_WORKLOAD}
-
-
 BMM_B, BMM_M, BMM_E = 64, 512, 128
 BMM_OPS = 2 * (2 * BMM_B * BMM_M * BMM_M * BMM_E)
 CONV_CASES = [  # (name, C, F, H, k, pad, groups, bias)
@@ -127,104 +70,59 @@ CONV_CASES = [  # (name, C, F, H, k, pad, groups, bias)
 ]
 CONV_N = 64
 
-
-def bmm_measure(dev, kunlun, flush, steps=20, warmup=3):
-    """Attention-score batched matmuls: S = A @ B, P = softmax(S), O = P @ V
-    for A [64,512,128], B [64,128,512], V [64,512,128] ~N(0,1), fp16 and fp32;
-    composed from the quantised bmm and softmax ops, and the same three steps
-    through the fused attention kernels (scale 1, no mask)."""
-    import torch
-    out = {}
-    for dt, name in ((torch.float16, "fp16"), (torch.float32, "fp32")):
-        g = torch.Generator().manual_seed(0)
-        a = torch.randn(BMM_B, BMM_M, BMM_E, generator=g).to(dt).to(dev)
-        b = torch.randn(BMM_B, BMM_E, BMM_M, generator=g).to(dt).to(dev)
-        v = torch.randn(BMM_B, BMM_M, BMM_E, generator=g).to(dt).to(dev)
-        kt = b.transpose(1, 2)
-
-        def composed():
-            torch.bmm(torch.softmax(torch.bmm(a, b), -1), v)
-
-        def fused():
-            torch_kunlun_sdpa(a, kt, v, scale=1.0)
-
-        for label, fn in (("composed", composed), ("fused", fused)):
-            ts = timed_steps(fn, steps, warmup, flush, kunlun)
-            ms = sum(ts) / len(ts)
-            out[f"{name}_{label}"] = {"ms": ms, "tops": BMM_OPS / (ms / 1000) / 1e12}
-    return out
+PROFILES = os.path.join(ROOT, "profiles")
 
 
-def torch_kunlun_sdpa(q, k, v, scale):
-    import torch_kunlun
-    return torch_kunlun.scaled_dot_product_attention(q, k, v, scale=scale)
+# ---- peaks and roofline objects ------------------------------------------------
+
+def load_peaks():
+    """Roofline denominators.  HBM: the driver's measured copy bandwidth.
+    int16 GEMM: the int8 dense rate (twice the measured bf16 dense rate on
+    B200) divided by the 4 limb MMAs of one int16 MAC, from the burst figure
+    for kernels timed alone and the sustained one for long steps."""
+    d, src = {}, "fallback figures of this pool (MEASURED_PEAKS.json absent)"
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        src = "MEASURED_PEAKS.json (driver-measured)"
+    except (OSError, ValueError):
+        pass
+    bf16 = float(d.get("bf16_tflops") or 1590.0)
+    bf16_s = float(d.get("bf16_tflops_sustained") or 1400.0)
+    return {"hbm_gbs": float(d.get("hbm_gbs") or 6650.0), "bf16_tflops": bf16,
+            "bf16_tflops_sustained": bf16_s, "int16_burst": 2.0 * bf16 / 4.0,
+            "int16_sustained": 2.0 * bf16_s / 4.0, "source": src}
 
 
-def conv_inputs(case, seed=0):
-    import torch
-    name, C, F, H, k, pad, groups, has_bias = case
-    g = torch.Generator().manual_seed(seed)
-    x = torch.relu(torch.randn(CONV_N, C, H, H, generator=g)).half()
-    fan_in = (C // groups) * k * k
-    w = (torch.randn(F, C // groups, k, k, generator=g) * (2.0 / fan_in) ** 0.5).half()
-    bias = (torch.randn(F, generator=g) * 0.01).half() if has_bias else None
-    return x, w, bias
+def roofline(bound, achieved, peak, unit, peak_source, traffic=None, traffic_source=None, **extra):
+    r = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+         "frac": achieved / peak if peak else None, "peak_source": peak_source,
+         "traffic": traffic}
+    if traffic_source:
+        r["traffic_source"] = traffic_source
+    r.update(extra)
+    return r
 
 
-def conv_ops(case):
-    name, C, F, H, k, pad, groups, has_bias = case
-    OH = H + 2 * pad - k + 1
-    return 2 * CONV_N * OH * OH * F * (C // groups) * k * k
+def ncu_traffic(name):
+    """dram bytes per launch recorded in a committed ncu summary, if present."""
+    p = os.path.join(PROFILES, name)
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1].strip()), "profiles/" + name + " (committed ncu summary)"
+    except OSError:
+        pass
+    return None, None
 
 
-def conv_measure(dev, kunlun, flush, steps=20, warmup=3):
-    """ResNet-50-stage conv2d shapes at batch 64 (NCHW fp16, Kaiming-normal
-    weights, ReLU(N(0,1)) inputs): device time per conv, TOPS, and for the
-    depthwise case the HBM bytes it must move."""
-    import torch
-    import torch.nn.functional as F
-    res = {}
-    for case in CONV_CASES:
-        name, C, Fo, H, k, pad, groups, has_bias = case
-        x, w, b = conv_inputs(case)
-        xd, wd = x.to(dev), w.to(dev)
-        bd = b.to(dev) if b is not None else None
-
-        def fn():
-            F.conv2d(xd, wd, bd, padding=pad, groups=groups)
-
-        ts = timed_steps(fn, steps, warmup, flush, kunlun)
-        ms = sum(ts) / len(ts)
-        OH = H + 2 * pad - k + 1
-        r = {"ms": ms, "tops": conv_ops(case) / (ms / 1000) / 1e12}
-        if groups > 1:
-            nbytes = (x.numel() + CONV_N * Fo * OH * OH + w.numel()) * 2
-            r["gbs"] = nbytes / (ms / 1000) / 1e9
-        res[name] = r
-    return res
+def int16_peak_source(peaks, which):
+    bf = peaks["bf16_tflops"] if which == "burst" else peaks["bf16_tflops_sustained"]
+    return (f"2 x {bf:.1f} TF/s bf16 dense ({which}, {peaks['source']}) as the int8 rate, "
+            "/ 4 limb MMAs per int16 MAC")
 
 
-def conv_cpu_baseline():
-    """torch CPU aten fp32 conv2d on 4 of the 64 images per case (all host
-    threads): TOPS."""
-    import torch
-    import torch.nn.functional as F
-    torch.set_num_threads(os.cpu_count() or 1)
-    res = {}
-    for case in CONV_CASES:
-        name, C, Fo, H, k, pad, groups, has_bias = case
-        x, w, b = conv_inputs(case)
-        x4 = x[:4].float()
-        wf = w.float()
-        bf = b.float() if b is not None else None
-        F.conv2d(x4, wf, bf, padding=pad, groups=groups)
-        t0 = time.perf_counter()
-        for _ in range(3):
-            F.conv2d(x4, wf, bf, padding=pad, groups=groups)
-        dt = (time.perf_counter() - t0) / 3
-        res[name] = conv_ops(case) * 4 / CONV_N / dt / 1e12
-    return res
-
+# ---- timing ------------------------------------------------------------------------
 
 def dist_env():
     return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
@@ -291,16 +189,449 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.samples), "source": "NVML, 5 ms"}
 
 
-def e2e_pipelined(xh, wh, bh, yh, dev, kunlun, steps, warmup):
-    """Device time per step of K pipelined end-to-end steps (see the caller)."""
+def device_delay(kunlun, us):
+    """A bounded device-side spin of `us` microseconds on the current kunlun
+    stream (torch's clock-cycle sleep kernel), enqueued outside the timed
+    events: the host then enqueues the next step while the GPU is still busy,
+    so a short step's time is not stretched by host launch latency."""
+    if us <= 0:
+        return
+    import torch
+    s = kunlun.current_stream()
+    ext = torch.cuda.ExternalStream(s.stream_id, device=torch.device("cuda", torch.cuda.current_device()))
+    with torch.cuda.stream(ext):
+        torch.cuda._sleep(int(us * 2000))  # ~2000 cycles per microsecond at the B200 boost clock
+
+
+def timed_steps(step, steps, warmup, flush, kunlun, gate_us=0):
+    """Per-step device time with CUDA events on the launching stream; the L2
+    flush and the host-latency gate between steps are outside the events."""
+    for _ in range(warmup):
+        step()
+        flush()
+    kunlun.synchronize()
+    times = []
+    for _ in range(steps):
+        device_delay(kunlun, gate_us)
+        e0 = kunlun.Event(enable_timing=True)
+        e1 = kunlun.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        flush()
+        times.append((e0, e1))
+    kunlun.synchronize()
+    return [a.elapsed_time(b) for a, b in times]
+
+
+def step_stats(times):
+    return {"mean": sum(times) / len(times), "min": min(times), "median": statistics.median(times),
+            "max": max(times)}
+
+
+# ---- the C-ABI GEMM kernel alone --------------------------------------------------
+
+class LimbGemm:
+    """One int16 GEMM out[M,N] = q(a) q(w)^T launched alone through the C ABI
+    (tk_qgemm_from_limbs) on operands quantised once beforehand: the device
+    time of the GEMM kernel itself, for the roofline."""
+
+    def __init__(self, a, w, out):
+        import torch
+        from torch_kunlun_b200 import _capi as C
+        self.C, self.L = C, C.lib()
+        self.a, self.w, self.out = a, w, out
+        M, K = a.shape
+        N = w.shape[0]
+        ld = (K + 15) // 16 * 16
+        dev = a.device
+        self.la = torch.empty(2 * M * ld, dtype=torch.int8, device=dev)
+        self.lb = torch.empty(2 * N * ld, dtype=torch.int8, device=dev)
+        self.amax = torch.empty(2, dtype=torch.float32, device=dev)
+        d = C.QGemmDesc()
+        d.dtype = C.TK_DTYPE_F16 if a.dtype == torch.float16 else C.TK_DTYPE_F32
+        d.batch, d.m, d.n, d.k = 1, M, N, K
+        d.out = out.data_ptr()
+        d.out_sb, d.out_sm = M * N, out.stride(0)
+        d.alpha, d.beta, d.act, d.per_slice_scales = 1.0, 0.0, 0, 1
+        self.d, self.M, self.N, self.K = d, M, N, K
+
+    def prepare(self, kunlun):
+        C, L = self.C, self.L
+        st = kunlun.current_stream().stream_id
+        dt = self.d.dtype
+        C.check(L.tk_amax(dt, self.a.data_ptr(), 1, 0, self.M * self.K, self.amax.data_ptr(), st), "amax")
+        C.check(L.tk_amax(dt, self.w.data_ptr(), 1, 0, self.N * self.K, self.amax.data_ptr() + 4, st), "amax")
+        C.check(L.tk_quantize_limbs(dt, self.a.data_ptr(), 1, self.M, self.K, 0, self.a.stride(0), 1,
+                                    self.amax.data_ptr(), 0, self.la.data_ptr(), st), "quantise")
+        C.check(L.tk_quantize_limbs(dt, self.w.data_ptr(), 1, self.N, self.K, 0, self.w.stride(0), 1,
+                                    self.amax.data_ptr() + 4, 0, self.lb.data_ptr(), st), "quantise")
+
+    def launch(self, kunlun):
+        st = kunlun.current_stream().stream_id
+        self.C.check(self.L.tk_qgemm_from_limbs(ctypes.byref(self.d), self.la.data_ptr(), self.lb.data_ptr(),
+                                                self.amax.data_ptr(), self.amax.data_ptr() + 4, st),
+                     "tk_qgemm_from_limbs")
+
+    def ms(self, kunlun, flush, iters=10, warmup=3):
+        self.prepare(kunlun)
+        ts = timed_steps(lambda: self.launch(kunlun), iters, warmup, flush, kunlun, gate_us=200)
+        return sum(ts) / len(ts)
+
+    def ops(self):
+        return 2 * self.M * self.N * self.K
+
+
+# ---- tensor-parallel MLP: data -------------------------------------------------------
+
+def _block(shape, seed, scale):
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (torch.randn(shape, generator=g, device="cuda") * scale).half()
+
+
+def tp_inputs(rank, world, dev):
+    """x [T, H] and this rank's shards.  Every weight is drawn in blocks of
+    512 rows (gate, up) or columns (down) with one seed per block, so rank r
+    of N ranks holds exactly rows/columns [r F/N, (r+1) F/N) of the same
+    full weights for every N."""
+    import torch
+    fr = TP_F // world
+    b0, nb = rank * fr // TP_BLOCK, fr // TP_BLOCK
+    x = torch.empty(TP_T, TP_H, dtype=torch.float16, device=dev)
+    for b in range(TP_T // 2048):
+        x[b * 2048:(b + 1) * 2048].copy_(_block((2048, TP_H), 40000 + b, 1.0))
+    wg = torch.empty(fr, TP_H, dtype=torch.float16, device=dev)
+    wu = torch.empty(fr, TP_H, dtype=torch.float16, device=dev)
+    for j in range(nb):
+        wg[j * TP_BLOCK:(j + 1) * TP_BLOCK].copy_(_block((TP_BLOCK, TP_H), 10000 + b0 + j, 0.02))
+        wu[j * TP_BLOCK:(j + 1) * TP_BLOCK].copy_(_block((TP_BLOCK, TP_H), 20000 + b0 + j, 0.02))
+    wd_cols = torch.cat([_block((TP_H, TP_BLOCK), 30000 + b0 + j, 0.02) for j in range(nb)], dim=1)
+    wd = torch.empty(TP_H, fr, dtype=torch.float16, device=dev)
+    wd.copy_(wd_cols.contiguous())
+    del wd_cols
+    torch.cuda.synchronize()
+    return x, wg, wu, wd
+
+
+def rows_owned(mode, rank, world):
+    """Rows of the full output that a rank's result holds: all of them for the
+    all-reduce, its own block [r T/N, (r+1) T/N) otherwise."""
+    if mode == "allreduce" or world == 1:
+        return 0, TP_T
+    return rank * TP_T // world, (rank + 1) * TP_T // world
+
+
+# ---- tensor-parallel MLP: parity --------------------------------------------------
+
+def f16_ulp(a):
+    """Spacing of binary16 at |a| (2^-24 below the normal range)."""
+    import numpy as np
+    a = np.abs(np.asarray(a, dtype=np.float64))
+    e = np.floor(np.log2(np.maximum(a, 2.0 ** -14)))
+    return 2.0 ** (e - 10)
+
+
+def tp_parity(rank, world, x, wg, wu, wd, outs, dist):
+    """Checks of this rank's results against the oracle (see module doc).
+    outs: {mode: the result tensor that mode returned}."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    from torch_kunlun_b200 import ops
+    S = 32
+    r0 = rank * TP_T // world
+    ax = ops.amax(x)
+    gate = ops.linear_scaled(x, wg, amax_x=ax)
+    up = ops.linear_scaled(x, wu, amax_x=ax)
+    h = ops.silu_mul(gate, up)
+    ah, awd = ops.amax(h), ops.amax(wd)
+    res = {"rank": rank}
+    # (1) the column-parallel GEMMs on sampled rows: bit-exact
+    axv = np.float32(ax.cpu().item())
+    xs = x[r0:r0 + S].cpu().numpy()
+    ok = True
+    for name, w, got in (("gate", wg, gate), ("up", wu, up)):
+        wn = w.cpu().numpy()
+        awn = O.amax(wn)
+        want = O.epilogue(O.gemm_i16_strided(O.quant(xs, axv), O.quant(wn, awn).T), axv, awn, np.float16)
+        g = got[r0:r0 + S].cpu().numpy()
+        same = bool(np.array_equal(g.view(np.uint16), want.view(np.uint16)))
+        res[f"{name}_bitexact"] = same
+        ok = ok and same
+    # (2) the SiLU gate: T(T(silu(gate)) * up) against float64 silu, <= 2 ulp16
+    gs, us = gate[r0:r0 + S].cpu().numpy(), up[r0:r0 + S].cpu().numpy()
+    want_h = O.silu_mul(gs, us)
+    hs = h[r0:r0 + S].cpu().numpy()
+    err = np.abs(hs.astype(np.float64) - want_h.astype(np.float64))
+    h_ok = bool(np.all(err <= 2 * f16_ulp(want_h)))
+    res["silu_gate_within_2ulp"] = h_ok
+    res["silu_gate_differing_fraction"] = float(np.mean(hs.view(np.uint16) != want_h.view(np.uint16)))
+    ok = ok and h_ok
+    # (3) this rank's partial of the down projection on sampled rows: bit-exact
+    ahv, awdv = np.float32(ah.cpu().item()), np.float32(awd.cpu().item())
+    partial_s = ops.linear_scaled(h[r0:r0 + S], wd, amax_x=ah, amax_w=awd).cpu().numpy()
+    want_p = O.epilogue(O.gemm_i16_strided(O.quant(hs, ahv), O.quant(wd.cpu().numpy(), awdv).T),
+                        ahv, awdv, np.float16)
+    same = bool(np.array_equal(partial_s.view(np.uint16), want_p.view(np.uint16)))
+    res["down_partial_bitexact"] = same
+    ok = ok and same
+    # (4) the reduced rows against the rank-ordered fp32 sum of every rank's partial
+    S2 = 64
+    if world == 1:
+        for mode, out in outs.items():
+            got = out[:S].cpu().numpy()
+            res[f"reduced_{mode}"] = "bitexact" if np.array_equal(got.view(np.uint16), want_p.view(np.uint16)) \
+                else "FAIL"
+            ok = ok and res[f"reduced_{mode}"] == "bitexact"
+    else:
+        partial = ops.linear_scaled(h, wd, amax_x=ah, amax_w=awd)
+        tp_rows = TP_T // world
+        sample = torch.cat([partial[q * tp_rows:q * tp_rows + S2] for q in range(world)]).contiguous()
+        gathered = torch.empty(world * world * S2, TP_H, dtype=torch.float16, device=x.device)
+        dist.all_gather_into_tensor(gathered, sample)
+        parts = gathered.cpu().numpy().astype(np.float32).reshape(world, world, S2, TP_H)[:, rank]
+        acc = np.zeros((S2, TP_H), dtype=np.float32)
+        for r in range(world):
+            acc = acc + parts[r]
+        want = acc.astype(np.float16)
+        bound = world * 2.0 ** -11 * np.abs(parts.astype(np.float64)).sum(0) + 2.0 ** -24
+        for mode, out in outs.items():
+            o0, _ = rows_owned(mode, rank, world)
+            got = out[r0 - o0:r0 - o0 + S2].cpu().numpy()
+            if np.array_equal(got.view(np.uint16), want.view(np.uint16)):
+                v = "bitexact"
+            elif np.all(np.abs(got.astype(np.float64) - want.astype(np.float64)) <= bound):
+                v = "within_fp16_sum_bound"
+            else:
+                v = "FAIL"
+            res[f"reduced_{mode}"] = v
+            ok = ok and v != "FAIL"
+            if mode.startswith("peer"):  # rank-ordered fp32 sum, one rounding: must be exact
+                ok = ok and v == "bitexact"
+        del partial, sample, gathered
+    res["ok"] = bool(ok)
+    del gate, up, h
+    return res
+
+
+# ---- tensor-parallel MLP: end to end ----------------------------------------------
+
+def tp_e2e(x_host_rows, wg, wu, wd, dev, kunlun, dist, world, mode, steps, warmup, comm):
+    """Steps through the public API with host buffers, pipelined as a serving
+    loop runs them: each rank copies its row block of x from pinned host
+    memory (a copy stream, two buffer sets), the ranks all-gather x over
+    NVLink, run the MLP, and each copies its result rows back to pinned host
+    memory (a third stream).  Device time of the whole loop / steps."""
+    import torch
+    from torch_kunlun_b200 import tp
+    comp = kunlun.current_stream(dev)
+    h2d, d2h = kunlun.Stream(dev), kunlun.Stream(dev)
+    rows = x_host_rows.shape[0]
+    xs = [torch.empty(rows, TP_H, dtype=torch.float16, device=dev) for _ in range(2)]
+    xf = [torch.empty(TP_T, TP_H, dtype=torch.float16, device=dev) for _ in range(2)] if world > 1 else xs
+    o0, o1 = rows_owned(mode, 0, world)
+    out_rows = o1 - o0
+    yh = [torch.empty(out_rows, TP_H, dtype=torch.float16).pin_memory() for _ in range(2)]
+    freed, fetched = [None, None], [None, None]
+
+    def step(i):
+        s = i % 2
+        with kunlun.stream(h2d):
+            if freed[s] is not None:
+                h2d.wait_event(freed[s])
+            xs[s].copy_(x_host_rows, non_blocking=True)
+            arrived = kunlun.Event(device=dev)
+            arrived.record(h2d)
+        comp.wait_event(arrived)
+        if world > 1:
+            dist.all_gather_into_tensor(xf[s], xs[s])
+        y = tp.tp_mlp_forward(xf[s], wg, wu, wd, reduce=mode, chunks=4, comm_stream=comm)
+        done = kunlun.Event(device=dev)
+        done.record(comp)
+        freed[s] = done
+        with kunlun.stream(d2h):
+            d2h.wait_event(done)
+            if fetched[s] is not None:
+                d2h.wait_event(fetched[s])
+            yh[s].copy_(y, non_blocking=True)
+            y.record_stream(d2h)
+            got = kunlun.Event(device=dev)
+            got.record(d2h)
+            fetched[s] = got
+
+    for i in range(warmup):
+        step(i)
+    kunlun.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = kunlun.Event(enable_timing=True), kunlun.Event(enable_timing=True)
+    e0.record(comp)
+    h2d.wait_event(e0)
+    d2h.wait_event(e0)
+    for i in range(steps):
+        step(i)
+    comp.wait_stream(h2d)
+    comp.wait_stream(d2h)
+    e1.record(comp)
+    kunlun.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return ms, int(x_host_rows.nbytes), int(yh[0].nbytes)
+
+
+# Kernel launches of this library per MLP step (counted from the code path):
+# amax(x); gate and up: weight amax + both operands' quantise + GEMM, each;
+# silu_mul; amax(h); amax(down weight); down: quantise + GEMM per row block.
+def tp_launches(mode, world):
+    base = 1 + 3 + 3 + 1 + 1 + 1
+    if world == 1:
+        return base + 2
+    if mode == "allreduce":
+        return base + 4 * 2
+    if mode == "peer":
+        return base + world * 2 + 1  # one GEMM per owner block, then the slot sum
+    if mode == "peer_fused":
+        return base + 2 + 1
+    return base + 2
+
+
+# ---- reference / CPU baseline: the oracle on a token sample ------------------------
+
+def oracle_tp_sample(x_rows, wg, wu, wd):
+    """The oracle's CPU restatement of the MLP on a few tokens with the full
+    (TP = 1) weights: per-tensor quantisation of every operand, exact integer
+    GEMMs, the SiLU gate, the epilogues.  Returns (seconds, int16 ops)."""
+    from oracle import oracle as O
+    t0 = time.perf_counter()
+    gate = O.linear(x_rows, wg)
+    up = O.linear(x_rows, wu)
+    h = O.silu_mul(gate, up)
+    O.linear(h, wd)
+    dt = time.perf_counter() - t0
+    return dt, 3 * 2 * x_rows.shape[0] * TP_H * TP_F
+
+
+def oracle_tp_data(rows=REF_ROWS):
+    """The full (TP = 1) weights and `rows` tokens of x drawn on the host:
+    the same shapes, distributions and 512-row blocks as tp_inputs (the
+    host generator's stream differs from the device's)."""
+    import numpy as np
+    import torch
+
+    def blk(shape, seed, scale):
+        g = torch.Generator().manual_seed(seed)
+        return (torch.randn(shape, generator=g) * scale).half().numpy()
+    nb = TP_F // TP_BLOCK
+    wg = np.concatenate([blk((TP_BLOCK, TP_H), 10000 + j, 0.02) for j in range(nb)])
+    wu = np.concatenate([blk((TP_BLOCK, TP_H), 20000 + j, 0.02) for j in range(nb)])
+    wd = np.ascontiguousarray(np.concatenate([blk((TP_H, TP_BLOCK), 30000 + j, 0.02) for j in range(nb)], 1))
+    x = blk((rows, TP_H), 40000, 1.0)
+    return x, wg, wu, wd
+
+
+def run_reference(args):
+    """The reference path on the host cores: the oracle port of the MLP on
+    16 tokens with all weights per step (rank 0 only; other ranks exit)."""
+    rank, _, world = dist_env()
+    if rank != 0:
+        return 0
+    x, wg, wu, wd = oracle_tp_data(REF_ROWS)
+    from oracle import oracle as O
+    O.linear(x[:2, :64].copy(), wg[:8, :64].copy())  # build / warm the library
+    for _ in range(max(1, args.warmup)):
+        oracle_tp_sample(x, wg, wu, wd)
+    times = []
+    for _ in range(args.steps):
+        dt, ops = oracle_tp_sample(x, wg, wu, wd)
+        times.append(dt)
+    ms = 1000 * statistics.mean(times)
+    value = ops / (ms / 1000) / 1e12
+    cores = threads_used()
+    sample = (f"{REF_ROWS} of {TP_T} tokens through the whole MLP (TP = 1 weights: every weight amaxed and "
+              "quantised per step) -- oracle: threaded C quantise, exact int64 GEMM, C epilogue")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int16",
+        "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, no dataset)",
+        "config": {"workload": WORKLOAD, "sample": sample, "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def threads_used():
+    try:
+        from oracle import oracle as O
+        return int(O.lib().tko_num_threads())
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# ---- the single-GPU objects ----------------------------------------------------
+
+def linear_object(dev, kunlun, flush, peaks, M, N, K, steps, warmup, with_e2e, cpu_sample):
+    """One int16-quantised linear y = x W^T + b through torch.nn.functional.linear
+    (step: amax + quantise + GEMM + epilogue), the GEMM kernel alone, and its
+    roofline against the burst int16 peak."""
+    import torch
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(M, K, generator=g).half()
+    w = (torch.randn(N, K, generator=g) * 0.02).half()
+    b = (torch.randn(N, generator=g) * 0.01).half()
+    xd, wd, bd = x.to(dev), w.to(dev), b.to(dev)
+    ops = 2 * M * N * K
+
+    def step():
+        torch.nn.functional.linear(xd, wd, bd)
+    ts = timed_steps(step, steps, warmup, flush, kunlun, gate_us=300)
+    ms = sum(ts) / len(ts)
+    out = torch.empty(M, N, dtype=torch.float16, device=dev)
+    gemm = LimbGemm(xd, wd, out)
+    gms = gemm.ms(kunlun, flush)
+    traffic, tsrc = ncu_traffic(f"qgemm_linear_{M}x{N}x{K}.md")
+    r = {"workload": f"int16-quantised linear x[{M},{K}] @ W[{N},{K}]^T + b, fp16",
+         "ms_per_step": ms, "tops": ops / (ms / 1000) / 1e12, "gemm_kernel_ms": gms,
+         "step_breakdown_ms": {"gemm": gms, "amax_quantise_and_launches": ms - gms},
+         "roofline": roofline("tensor", ops / (gms / 1000) / 1e12, peaks["int16_burst"], "TOPS",
+                              int16_peak_source(peaks, "burst"), traffic, tsrc,
+                              kernel="qgemm_tc_kernel", ops_per_launch=ops, launch_ms=gms),
+         "l2": "flushed between steps (512 MiB device write outside the timed events)"}
+    if with_e2e:
+        xh, wh, bh = x.pin_memory(), w.pin_memory(), b.pin_memory()
+        yh = [torch.empty(M, N, dtype=torch.float16).pin_memory() for _ in range(2)]
+        e2e_ms = linear_e2e(xh, wh, bh, yh, dev, kunlun, steps, warmup)
+        r["e2e"] = {"value": ops / (e2e_ms / 1000) / 1e12, "unit": "TOPS", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": int(xh.nbytes + wh.nbytes + bh.nbytes),
+                    "d2h_bytes_per_step": int(yh[0].nbytes),
+                    "timing": "pipelined steps (H2D, op, D2H on three streams), device time / steps"}
+    if cpu_sample:
+        from oracle import oracle as O
+        rows = 256
+        xs, wn, bn = x[:rows].numpy(), w.numpy(), b.numpy()
+        O.linear(xs[:8, :64].copy(), wn[:16, :64].copy(), None)
+        reps = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            O.linear(xs, wn, bn)
+            reps.append(time.perf_counter() - t0)
+        r["cpu_baseline"] = {"value": 2 * rows * N * K / statistics.mean(reps) / 1e12, "unit": "TOPS",
+                             "cores": threads_used(), "kind": "port",
+                             "sample": f"{rows} of {M} rows of x with all of W per call, 3 calls"}
+    return r
+
+
+def linear_e2e(xh, wh, bh, yh, dev, kunlun, steps, warmup):
+    """Device time per step of pipelined end-to-end linear calls."""
     import torch
     comp = kunlun.current_stream(dev)
     h2d, d2h = kunlun.Stream(dev), kunlun.Stream(dev)
     xe = [torch.empty(xh.shape, dtype=xh.dtype, device=dev) for _ in range(2)]
     we = [torch.empty(wh.shape, dtype=wh.dtype, device=dev) for _ in range(2)]
     be = [torch.empty(bh.shape, dtype=bh.dtype, device=dev) for _ in range(2)]
-    read = [None, None]   # compute finished reading buffer set s
-    fetched = [None, None]  # D2H of set s finished
+    read, fetched = [None, None], [None, None]
 
     def step(i):
         s = i % 2
@@ -332,7 +663,7 @@ def e2e_pipelined(xh, wh, bh, yh, dev, kunlun, steps, warmup):
     kunlun.synchronize()
     e0, e1 = kunlun.Event(enable_timing=True), kunlun.Event(enable_timing=True)
     e0.record(comp)
-    h2d.wait_event(e0)  # no copy starts before the timed region opens
+    h2d.wait_event(e0)
     d2h.wait_event(e0)
     for i in range(steps):
         step(i)
@@ -343,64 +674,473 @@ def e2e_pipelined(xh, wh, bh, yh, dev, kunlun, steps, warmup):
     return e0.elapsed_time(e1) / steps
 
 
-def timed_steps(step, steps, warmup, flush, kunlun, stream=None):
-    """Per-step device time with CUDA events on the launching stream; the L2
-    flush between steps is outside the events."""
-    for _ in range(warmup):
-        step()
-        flush()
-    kunlun.synchronize()
-    times = []
-    for _ in range(steps):
-        e0 = kunlun.Event(enable_timing=True)
-        e1 = kunlun.Event(enable_timing=True)
-        e0.record(stream)
-        step()
-        e1.record(stream)
-        flush()
-        times.append((e0, e1))
-    kunlun.synchronize()
-    return [a.elapsed_time(b) for a, b in times]
+def bert_inputs():
+    import torch
+    from torch_kunlun_b200 import encoder
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(BERT_B, BERT_L, BERT_H, generator=g).half()
+    w = encoder.init_weights(BERT_H, BERT_F, generator=g)
+    mask = encoder.padding_mask(BERT_B, BERT_L, BERT_TAIL)
+    return x, w, mask
 
 
-def kernel_breakdown(xd, wd, bd, out, kunlun, flush, iters=10):
-    """Average device time of the step's GEMM kernel, launched through the C
-    ABI on the same stream with the same operands, quantised once beforehand
-    (CUDA events around each launch, L2 flushed between launches)."""
+def bert_object(dev, kunlun, flush, peaks, steps, warmup, cpu):
+    """Encoder block forward: tokens/s, and each op's device time and roofline
+    from an instrumented pass (events between the ops of one block)."""
+    import torch
+    import torch.nn.functional as F
+    from torch_kunlun_b200 import encoder, ops
+    from torch_kunlun_b200.kunlun.attention import scaled_dot_product_attention
+    x, w, mask = bert_inputs()
+    xd, wd, md = x.to(dev), w.to(dev), mask.to(dev)
+
+    def block():
+        encoder.encoder_block(xd, wd, md, heads=BERT_HEADS, eps=1e-12)
+    ts = timed_steps(block, steps, warmup, flush, kunlun, gate_us=300)
+    ms = sum(ts) / len(ts)
+    macs = encoder.encoder_block_macs(BERT_B, BERT_L, BERT_H, BERT_F)
+    T, H, E = BERT_B * BERT_L, BERT_H, BERT_H // BERT_HEADS
+
+    def parts():
+        ev = [kunlun.Event(enable_timing=True) for _ in range(8)]
+        ev[0].record()
+        x2 = xd.reshape(T, H)
+        qkv = ops.linear(x2, wd.w_qkv, wd.b_qkv)
+        ev[1].record()
+        q5 = qkv.view(BERT_B, BERT_L, 3, BERT_HEADS, E).permute(2, 0, 3, 1, 4)
+        ctx = scaled_dot_product_attention(q5[0], q5[1], q5[2], attn_mask=md)
+        ev[2].record()
+        ctx = ctx.transpose(1, 2).reshape(T, H)
+        a = ops.linear(ctx, wd.w_o, wd.b_o, residual=x2)
+        ev[3].record()
+        h = F.layer_norm(a, (H,), wd.ln1_w, wd.ln1_b, 1e-12)
+        ev[4].record()
+        f1 = ops.linear(h, wd.w_1, wd.b_1, act="gelu")
+        ev[5].record()
+        f2 = ops.linear(f1, wd.w_2, wd.b_2, residual=h)
+        ev[6].record()
+        F.layer_norm(f2, (H,), wd.ln2_w, wd.ln2_b, 1e-12)
+        ev[7].record()
+        return ev
+    names = ["qkv_linear", "attention", "out_linear_residual", "layer_norm1", "ffn1_linear_gelu",
+             "ffn2_linear_residual", "layer_norm2"]
+    acc = {n: 0.0 for n in names}
+    reps = 5
+    for i in range(reps + 2):
+        device_delay(kunlun, 300)
+        ev = parts()
+        kunlun.synchronize()
+        if i >= 2:
+            for j, n in enumerate(names):
+                acc[n] += ev[j].elapsed_time(ev[j + 1]) / reps
+        flush()
+    total = sum(acc.values())
+    lin_ops = {"qkv_linear": 2 * T * H * 3 * H, "out_linear_residual": 2 * T * H * H,
+               "ffn1_linear_gelu": 2 * T * H * BERT_F, "ffn2_linear_residual": 2 * T * BERT_F * H}
+    per_op = {}
+    for n in names:
+        t = acc[n]
+        o = {"ms": t, "share": t / total}
+        if n in lin_ops:
+            o["roofline"] = roofline("tensor", lin_ops[n] / (t / 1000) / 1e12, peaks["int16_burst"], "TOPS",
+                                     int16_peak_source(peaks, "burst"), ops_per_launch=lin_ops[n],
+                                     note="whole op: amax + quantise + GEMM + fused epilogue")
+        elif n == "attention":
+            aops = 2 * 2 * BERT_B * BERT_HEADS * BERT_L * BERT_L * E
+            o["roofline"] = roofline("tensor", aops / (t / 1000) / 1e12, peaks["int16_burst"], "TOPS",
+                                     int16_peak_source(peaks, "burst"), ops_per_launch=aops,
+                                     note="quantise + statistics + output kernels")
+        else:
+            nbytes = 2 * 2 * T * H + 2 * 2 * H
+            o["roofline"] = roofline("hbm", nbytes / (t / 1000) / 1e9, peaks["hbm_gbs"], "GB/s",
+                                     f"measured copy bandwidth, {peaks['source']}", algorithmic_bytes=nbytes)
+        per_op[n] = o
+    r = {"workload": BERT_WORKLOAD, "tokens_per_s": T / (ms / 1000), "ms_per_block": ms,
+         "effective_tops": 2 * macs / (ms / 1000) / 1e12, "steps": steps, "warmup": warmup,
+         "per_op": per_op, "per_op_source": "instrumented pass, events between the ops (5 blocks)"}
+    if cpu:
+        tps, threads = bert_cpu_baseline()
+        r["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads,
+                             "kind": "torch CPU aten fp32 eager",
+                             "sample": "1 of 32 sequences (512 tokens), median of 3"}
+    return r
+
+
+def bert_cpu_baseline(batch=1, reps=3):
+    """torch CPU aten fp32 eager encoder block on `batch` sequences (all host
+    threads): tokens/s."""
+    import torch
+    import torch.nn.functional as F
+    x, w, mask = bert_inputs()
+    x, mask = x[:batch].float(), mask[:batch].float()
+    f = {k: v.float() for k, v in vars(w).items()}
+    torch.set_num_threads(os.cpu_count() or 1)
+    B, L, H, E = batch, BERT_L, BERT_H, BERT_H // BERT_HEADS
+
+    def block():
+        x2 = x.reshape(B * L, H)
+        qkv = F.linear(x2, f["w_qkv"], f["b_qkv"]).view(B, L, 3, BERT_HEADS, E).permute(2, 0, 3, 1, 4)
+        ctx = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], attn_mask=mask)
+        ctx = ctx.transpose(1, 2).reshape(B * L, H)
+        h = F.layer_norm(x2 + F.linear(ctx, f["w_o"], f["b_o"]), (H,), f["ln1_w"], f["ln1_b"], 1e-12)
+        g = F.gelu(F.linear(h, f["w_1"], f["b_1"]))
+        return F.layer_norm(h + F.linear(g, f["w_2"], f["b_2"]), (H,), f["ln2_w"], f["ln2_b"], 1e-12)
+
+    block()
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        block()
+        ts.append(time.perf_counter() - t0)
+    return B * L / statistics.median(ts), torch.get_num_threads()
+
+
+def bmm_object(dev, kunlun, flush, peaks, steps=20, warmup=3):
+    """Attention-score chain S = A @ B, P = softmax(S), O = P @ V for A
+    [64,512,128], B [64,128,512], V [64,512,128] ~N(0,1), fp16 and fp32:
+    composed from the quantised bmm and softmax ops, and the same chain
+    through the fused attention kernels (scale 1, no mask)."""
+    import torch
+    import torch_kunlun
+    out = {"workload": "S = A[64,512,128] @ B[64,128,512], P = softmax(S), O = P @ V[64,512,128]",
+           "ops_per_step": BMM_OPS}
+    for dt, name in ((torch.float16, "fp16"), (torch.float32, "fp32")):
+        g = torch.Generator().manual_seed(0)
+        a = torch.randn(BMM_B, BMM_M, BMM_E, generator=g).to(dt).to(dev)
+        b = torch.randn(BMM_B, BMM_E, BMM_M, generator=g).to(dt).to(dev)
+        v = torch.randn(BMM_B, BMM_M, BMM_E, generator=g).to(dt).to(dev)
+        kt = b.transpose(1, 2)
+
+        def composed():
+            torch.bmm(torch.softmax(torch.bmm(a, b), -1), v)
+
+        def fused():
+            torch_kunlun.scaled_dot_product_attention(a, kt, v, scale=1.0)
+
+        for label, fn in (("composed", composed), ("fused", fused)):
+            ts = timed_steps(fn, steps, warmup, flush, kunlun, gate_us=300)
+            ms = sum(ts) / len(ts)
+            tops = BMM_OPS / (ms / 1000) / 1e12
+            out[f"{name}_{label}"] = {
+                "ms": ms, "tops": tops,
+                "roofline": roofline("tensor", tops, peaks["int16_burst"], "TOPS", int16_peak_source(peaks, "burst"),
+                                     ops_per_launch=BMM_OPS, note="whole chain, every launch")}
+    return out
+
+
+def conv_inputs(case, seed=0):
+    import torch
+    name, C, F, H, k, pad, groups, has_bias = case
+    g = torch.Generator().manual_seed(seed)
+    x = torch.relu(torch.randn(CONV_N, C, H, H, generator=g)).half()
+    fan_in = (C // groups) * k * k
+    w = (torch.randn(F, C // groups, k, k, generator=g) * (2.0 / fan_in) ** 0.5).half()
+    bias = (torch.randn(F, generator=g) * 0.01).half() if has_bias else None
+    return x, w, bias
+
+
+def conv_ops(case):
+    name, C, F, H, k, pad, groups, has_bias = case
+    OH = H + 2 * pad - k + 1
+    return 2 * CONV_N * OH * OH * F * (C // groups) * k * k
+
+
+def conv_object(dev, kunlun, flush, peaks, cpu, steps=20, warmup=3):
+    """ResNet-50-stage conv2d shapes at batch 64 (NCHW fp16, Kaiming-normal
+    weights, ReLU(N(0,1)) inputs): device time per conv (amax, quantise and
+    the convolution kernels), int16 TOPS, algorithmic HBM bytes, and the
+    roofline of the bound that applies (tensor for the GEMM-shaped
+    convolutions, HBM for the depthwise one)."""
+    import torch.nn.functional as F
+    res = {"workload": "conv2d NCHW fp16 batch 64, Kaiming-normal weights, ReLU(N(0,1)) inputs"}
+    cb = conv_cpu_baseline() if cpu else {}
+    for case in CONV_CASES:
+        name, C, Fo, H, k, pad, groups, has_bias = case
+        x, w, b = conv_inputs(case)
+        xd, wd = x.to(dev), w.to(dev)
+        bd = b.to(dev) if b is not None else None
+
+        def fn():
+            F.conv2d(xd, wd, bd, padding=pad, groups=groups)
+
+        ts = timed_steps(fn, steps, warmup, flush, kunlun, gate_us=300)
+        ms = sum(ts) / len(ts)
+        OH = H + 2 * pad - k + 1
+        ops = conv_ops(case)
+        nbytes = (x.numel() + CONV_N * Fo * OH * OH + w.numel()) * 2 + (Fo * 2 if has_bias else 0)
+        r = {"ms": ms, "tops": ops / (ms / 1000) / 1e12, "ops": ops, "algorithmic_bytes": nbytes,
+             "gbs": nbytes / (ms / 1000) / 1e9}
+        if groups > 1:
+            r["roofline"] = roofline("hbm", r["gbs"], peaks["hbm_gbs"], "GB/s",
+                                     f"measured copy bandwidth, {peaks['source']}", algorithmic_bytes=nbytes)
+        else:
+            r["roofline"] = roofline("tensor", r["tops"], peaks["int16_burst"], "TOPS",
+                                     int16_peak_source(peaks, "burst"), ops_per_launch=ops,
+                                     hbm_frac=r["gbs"] / peaks["hbm_gbs"])
+        if name in cb:
+            r["cpu_baseline_tops"] = cb[name]
+        res[name] = r
+    if cpu:
+        res["cpu_baseline"] = "torch CPU aten fp32 on 4 of 64 images, all host threads"
+    return res
+
+
+def conv_cpu_baseline():
+    import torch
+    import torch.nn.functional as F
+    torch.set_num_threads(os.cpu_count() or 1)
+    res = {}
+    for case in CONV_CASES:
+        name, C, Fo, H, k, pad, groups, has_bias = case
+        x, w, b = conv_inputs(case)
+        x4, wf = x[:4].float(), w.float()
+        bf = b.float() if b is not None else None
+        F.conv2d(x4, wf, bf, padding=pad, groups=groups)
+        t0 = time.perf_counter()
+        for _ in range(3):
+            F.conv2d(x4, wf, bf, padding=pad, groups=groups)
+        dt = (time.perf_counter() - t0) / 3
+        res[name] = conv_ops(case) * 4 / CONV_N / dt / 1e12
+    return res
+
+
+def rowops_object(dev, kunlun, flush, peaks, steps=20, warmup=3):
+    """The HBM-bound kernels on their benchmark shapes: softmax over
+    [64, 512, 512] fp16 (the cfg2 scores) and [384, 512, 512] (BERT's),
+    layer_norm over [16384, 768] fp16, and the cfg1 operands' amax + quantise
+    through the C ABI.  Algorithmic bytes: 2 + 2 per element for softmax and
+    layer_norm (plus gamma / beta), 2 read (amax) + 2 read + 2 written (two
+    limbs) per element for the quantise."""
     import torch
     from torch_kunlun_b200 import _capi as C
+    g = torch.Generator().manual_seed(0)
+    s = torch.randn(64, 512, 512, generator=g).half().to(dev)
+    s4 = torch.randn(384, 512, 512, generator=g).half().to(dev)
+    h = torch.randn(16384, 768, generator=g).half().to(dev)
+    gamma = (1 + 0.1 * torch.randn(768, generator=g)).half().to(dev)
+    beta = (0.1 * torch.randn(768, generator=g)).half().to(dev)
+    x = torch.randn(M1, K1, generator=g).half().to(dev)
+    w = (torch.randn(N1, K1, generator=g) * 0.02).half().to(dev)
     L = C.lib()
-    stream = kunlun.current_stream().stream_id
-    dev = xd.device
-    ld = (K + 15) // 16 * 16
-    la = torch.empty(2 * M * ld, dtype=torch.int8, device=dev)
-    lb = torch.empty(2 * N * ld, dtype=torch.int8, device=dev)
+    ld = (K1 + 15) // 16 * 16
+    la = torch.empty(2 * M1 * ld, dtype=torch.int8, device=dev)
+    lb = torch.empty(2 * N1 * ld, dtype=torch.int8, device=dev)
     amax = torch.empty(2, dtype=torch.float32, device=dev)
-    d = C.QGemmDesc()
-    d.dtype = C.TK_DTYPE_F16
-    d.batch, d.m, d.n, d.k = 1, M, N, K
-    d.out = out.data_ptr()
-    d.out_sb, d.out_sm = M * N, N
-    d.bias = bd.data_ptr()
-    d.alpha, d.beta, d.act, d.per_slice_scales = 1.0, 0.0, 0, 1
-    stages = {
-        "amax": lambda: (C.check(L.tk_amax(0, xd.data_ptr(), 1, 0, M * K, amax.data_ptr(), stream), "amax"),
-                         C.check(L.tk_amax(0, wd.data_ptr(), 1, 0, N * K, amax.data_ptr() + 4, stream), "amax")),
-        "quantise": lambda: (C.check(L.tk_quantize_limbs(0, xd.data_ptr(), 1, M, K, 0, K, 1, amax.data_ptr(), 0,
-                                                         la.data_ptr(), stream), "q"),
-                             C.check(L.tk_quantize_limbs(0, wd.data_ptr(), 1, N, K, 0, K, 1, amax.data_ptr() + 4,
-                                                         0, lb.data_ptr(), stream), "q")),
-        "gemm": lambda: C.check(L.tk_qgemm_from_limbs(ctypes.byref(d), la.data_ptr(), lb.data_ptr(),
-                                                      amax.data_ptr(), amax.data_ptr() + 4, stream), "gemm"),
-    }
-    stages["amax"]()
-    stages["quantise"]()
-    ts = timed_steps(stages["gemm"], iters, 3, flush, kunlun)
-    return {"gemm": sum(ts) / len(ts)}
+
+    def quantise():
+        st = kunlun.current_stream().stream_id
+        C.check(L.tk_amax(0, x.data_ptr(), 1, 0, M1 * K1, amax.data_ptr(), st), "amax")
+        C.check(L.tk_amax(0, w.data_ptr(), 1, 0, N1 * K1, amax.data_ptr() + 4, st), "amax")
+        C.check(L.tk_quantize_limbs(0, x.data_ptr(), 1, M1, K1, 0, K1, 1, amax.data_ptr(), 0,
+                                    la.data_ptr(), st), "q")
+        C.check(L.tk_quantize_limbs(0, w.data_ptr(), 1, N1, K1, 0, K1, 1, amax.data_ptr() + 4, 0,
+                                    lb.data_ptr(), st), "q")
+    out = {}
+    for name, fn, nbytes in (
+            ("softmax_64x512x512", lambda: torch.softmax(s, -1), 4 * s.numel()),
+            ("softmax_384x512x512", lambda: torch.softmax(s4, -1), 4 * s4.numel()),
+            ("layer_norm_16384x768", lambda: torch.nn.functional.layer_norm(h, (768,), gamma, beta, 1e-12),
+             4 * h.numel() + 4 * 768),
+            ("quantise_cfg1_operands", quantise, 6 * (M1 * K1 + N1 * K1))):
+        ts = timed_steps(fn, steps, warmup, flush, kunlun, gate_us=300)
+        ms = sum(ts) / len(ts)
+        gbs = nbytes / (ms / 1000) / 1e9
+        out[name] = {"ms": ms, "gbs": gbs, "algorithmic_bytes": nbytes,
+                     "roofline": roofline("hbm", gbs, peaks["hbm_gbs"], "GB/s",
+                                          f"measured copy bandwidth, {peaks['source']}",
+                                          algorithmic_bytes=nbytes, frac_of_8tbs=gbs / 8000.0)}
+    return out
 
 
-def measured_int8_peak_tops(torch):
-    """cuBLASLt int8 GEMM (torch._int_mm) at 8192^3, best of 5 (burst)."""
+# ---- the headline run ---------------------------------------------------------------
+
+def run_tp(args):
+    import torch
+    import torch.distributed as dist
+    import torch_kunlun  # noqa: F401
+    from torch_kunlun_b200 import tp
+    kunlun = torch_kunlun.kunlun
+    rank, local_rank, world = dist_env()
+    kunlun.set_device(local_rank)
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("kunlun", local_rank)
+    if world > 1:
+        # the communicator's init log (ranks, devices, channels) stays visible
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        dist.init_process_group("bkcl", timeout=datetime.timedelta(seconds=180))
+    peaks = load_peaks()
+    mode = args.reduce if world > 1 else "none"
+    x, wg, wu, wd = tp_inputs(rank, world, dev)
+    comm = kunlun.Stream(dev)
+
+    def step_fn(m):
+        return lambda: tp.tp_mlp_forward(x, wg, wu, wd, reduce=m if world > 1 else "allreduce", chunks=4,
+                                         comm_stream=comm)
+
+    if world > 1:
+        dist.barrier()
+    kunlun.synchronize()
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        times = timed_steps(step_fn(mode), args.steps, args.warmup, lambda: None, kunlun)
+    kunlun.synchronize()
+    if world > 1:
+        dist.barrier()
+    my = step_stats(times)
+
+    # the other reductions, as objects (fewer steps)
+    mode_ms = {}
+    extra_modes = [m for m in ("allreduce", "reduce_scatter", "peer", "peer_fused")
+                   if world > 1 and m != mode and not args.no_extra_modes]
+    for m in extra_modes:
+        ts = timed_steps(step_fn(m), min(args.steps, 10), 2, lambda: None, kunlun)
+        mode_ms[m] = sum(ts) / len(ts)
+
+    # the three GEMM kernels alone, for the roofline
+    gate_out = torch.empty(TP_T, TP_F // world, dtype=torch.float16, device=dev)
+    up_out = torch.empty_like(gate_out)
+    g_ms = LimbGemm(x, wg, gate_out).ms(kunlun, lambda: None, iters=3, warmup=1)
+    u_ms = LimbGemm(x, wu, up_out).ms(kunlun, lambda: None, iters=3, warmup=1)
+    from torch_kunlun_b200 import ops as kops
+    hbuf = kops.silu_mul(gate_out, up_out)  # the step's activation (scales of its own)
+    del gate_out, up_out
+    y_out = torch.empty(TP_T, TP_H, dtype=torch.float16, device=dev)
+    d_ms = LimbGemm(hbuf, wd, y_out).ms(kunlun, lambda: None, iters=3, warmup=1)
+    del hbuf, y_out
+
+    # parity of this rank's results (outside every timed region)
+    outs = {mode: step_fn(mode)()}
+    for m in extra_modes:
+        outs[m] = step_fn(m)()
+    kunlun.synchronize()
+    par = tp_parity(rank, world, x, wg, wu, wd, outs, dist)
+    del outs
+
+    # end to end through the public API with host buffers
+    r0, r1 = rank * TP_T // world, (rank + 1) * TP_T // world
+    x_host = x[r0:r1].cpu().pin_memory()
+    e2e_ms, h2d_b, d2h_b = tp_e2e(x_host, wg, wu, wd, dev, kunlun, dist, world,
+                                  mode if world > 1 else "allreduce", args.steps, args.warmup, comm)
+
+    # gather per-rank figures
+    mine = [my["mean"], my["min"], my["median"], my["max"], e2e_ms, g_ms, u_ms, d_ms,
+            1.0 if par["ok"] else 0.0] + [mode_ms.get(m, 0.0) for m in extra_modes]
+    if world > 1:
+        t = torch.tensor(mine, dtype=torch.float32).to(dev)
+        allr = torch.empty(world * len(mine), dtype=torch.float32, device=dev)
+        dist.all_gather_into_tensor(allr, t)
+        rows = allr.cpu().view(world, len(mine)).tolist()
+    else:
+        rows = [mine]
+    # every rank's parity record travels through the store
+    pars = [par]
+    if world > 1:
+        store = dist.distributed_c10d._get_default_store()
+        store.set(f"bench_parity/{rank}", json.dumps(par))
+        dist.barrier()
+        pars = [json.loads(store.get(f"bench_parity/{r}").decode()) for r in range(world)]
+
+    cpu_base = None
+    extras = {}
+    if rank == 0 and world == 1:
+        kunlun.synchronize()
+        del x
+        if not args.no_cpu_baseline:
+            xr, wgr, wur, wdr = oracle_tp_data(REF_ROWS)
+            oracle_tp_sample(xr[:2], wgr, wur, wdr)  # warm
+            reps = [oracle_tp_sample(xr, wgr, wur, wdr) for _ in range(2)]
+            cpu_base = {"value": reps[0][1] / statistics.mean(r[0] for r in reps) / 1e12, "unit": "TOPS",
+                        "cores": threads_used(), "kind": "port",
+                        "sample": f"{REF_ROWS} of {TP_T} tokens through the whole MLP with all (TP = 1) "
+                                  "weights, 2 calls (oracle: threaded C quantise, exact int64 GEMM, C epilogue)"}
+            del xr, wgr, wur, wdr
+        if not args.no_extra:
+            del wg, wu, wd
+            kunlun.empty_cache()
+            extras = single_gpu_objects(dev, kunlun, peaks, args)
+
+    if rank == 0:
+        ms = max(r[0] for r in rows)
+        e2e = max(r[4] for r in rows)
+        gemm_ms = [max(r[5] for r in rows), max(r[6] for r in rows), max(r[7] for r in rows)]
+        gemm_ops = 3 * 2 * TP_T * TP_H * (TP_F // world)
+        achieved = gemm_ops / (sum(gemm_ms) / 1000) / 1e12
+        peak = peaks["int16_burst"]  # the GEMM kernels are timed alone
+        line = {
+            "metric": METRIC, "value": TP_OPS / (ms / 1000) / 1e12, "unit": "TOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int16",
+            "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights in 512-row blocks, no dataset)",
+            "config": {"workload": WORKLOAD, "T": TP_T, "H": TP_H, "F": TP_F, "parallelism": f"tp{world}",
+                       "reduce": mode, "overlap": OVERLAP.get(mode, "none (one GPU)"),
+                       "l2": "inputs (x 256 MiB, weights 1.4 GiB over the ranks) larger than L2"},
+            "roofline": roofline("tensor", achieved, peak, "TOPS", int16_peak_source(peaks, "burst"),
+                                 None, None, kernel="qgemm_tc_kernel (gate, up, down GEMMs of one rank)",
+                                 ops_per_step=gemm_ops, gemm_ms=gemm_ms,
+                                 frac_of_sustained=achieved / peaks["int16_sustained"],
+                                 step_frac_of_sustained=(gemm_ops / (ms / 1000) / 1e12) / peaks["int16_sustained"],
+                                 note="achieved = the rank's GEMM ops / the three GEMM kernels' event-timed "
+                                      "durations (max over ranks); traffic: see profiles/"),
+            "e2e": {"value": TP_OPS / (e2e / 1000) / 1e12, "unit": "TOPS", "ms_per_step": e2e,
+                    "h2d_bytes_per_step": h2d_b * world, "d2h_bytes_per_step": d2h_b * world,
+                    "per_rank_bytes": {"h2d": h2d_b, "d2h": d2h_b},
+                    "timing": "pipelined steps: each rank's x row block H2D from pinned memory, all-gather "
+                              "over NVLink, the MLP, its result rows D2H; device time of the loop / steps, "
+                              "max over ranks"},
+            "gpu_launches": tp_launches(mode, world) * args.steps,
+            "clocks": clocks.summary(),
+            "per_rank_ms": [{"rank": i, "mean": r[0], "min": r[1], "median": r[2], "max": r[3]}
+                            for i, r in enumerate(rows)],
+            "parity_ok": all(p["ok"] for p in pars),
+            "parity": pars,
+            "cpu_baseline": cpu_base,
+        }
+        if extra_modes:
+            line["reduce_modes"] = {
+                m: {"ms_per_step": max(r[9 + i] for r in rows),
+                    "value": TP_OPS / (max(r[9 + i] for r in rows) / 1000) / 1e12, "overlap": OVERLAP[m]}
+                for i, m in enumerate(extra_modes)}
+        line.update(extras)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        tp.release_peer_buffers()
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def single_gpu_objects(dev, kunlun, peaks, args):
+    import torch
+    scratch = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
+
+    def flush():
+        scratch.fill_(1)
+    cpu = not args.no_cpu_baseline
+    out = {"objects_note": "single-GPU configs measured after the headline; L2 flushed between steps; "
+                           "each object carries the SM clocks sampled while it ran"}
+    jobs = [
+        ("linear_2048x4096x4096",
+         lambda: linear_object(dev, kunlun, flush, peaks, M1, N1, K1, args.steps, args.warmup, True, cpu)),
+        ("linear_4096x4096x4096",
+         lambda: linear_object(dev, kunlun, flush, peaks, 4096, 4096, 4096, args.steps, args.warmup, False, False)),
+        ("bert_block", lambda: bert_object(dev, kunlun, flush, peaks, max(5, args.steps // 4), args.warmup, cpu)),
+        ("bmm_attention_scores", lambda: bmm_object(dev, kunlun, flush, peaks)),
+        ("conv_resnet50", lambda: conv_object(dev, kunlun, flush, peaks, cpu)),
+        ("rowops", lambda: rowops_object(dev, kunlun, flush, peaks)),
+    ]
+    for name, fn in jobs:
+        with ClockSampler(torch.cuda.current_device()) as clocks:
+            r = fn()
+        r["clocks"] = clocks.summary()
+        out[name] = r
+    out["int8_live_tops"] = measured_int8_peak_tops()
+    return out
+
+
+def measured_int8_peak_tops():
+    """cuBLASLt int8 GEMM (torch._int_mm) at 8192^3, best of 5 (burst) --
+    printed beside the roofline denominators, not used as one."""
+    import torch
     n = 8192
     a = torch.randint(-128, 127, (n, n), dtype=torch.int8, device="cuda")
     b = torch.randint(-128, 127, (n, n), dtype=torch.int8, device="cuda").t()
@@ -420,359 +1160,66 @@ def measured_int8_peak_tops(torch):
     return 2 * n ** 3 / best / 1e9
 
 
-def ncu_traffic():
-    """dram bytes per GEMM launch from the committed ncu summary, if present."""
-    p = os.path.join(ROOT, "profiles", "qgemm_linear_2048x4096x4096.md")
-    try:
-        for line in open(p):
-            if line.startswith("traffic_bytes_per_launch:"):
-                return int(line.split(":")[1].strip())
-    except Exception:
-        pass
-    return None
+OVERLAP = {
+    "allreduce": "down projection in 4 row blocks, each block's all-reduce on a second stream",
+    "reduce_scatter": "none: one down GEMM, then the bkcl (NCCL) reduce-scatter",
+    "peer": "down projection one owner's row block at a time; each finished block is copied by a copy "
+            "engine into its owner's buffer (CUDA IPC, NVLink) while the next block computes; a "
+            "one-element all-reduce as the barrier, then each rank sums its slots in rank order (fp32)",
+    "peer_fused": "the down GEMM's epilogue stores each tile into the owning rank's buffer over NVLink "
+                  "(CUDA IPC), a one-element all-reduce as the barrier, then each rank sums its slots",
+}
 
 
-def oracle_sample(rows=256, reps=1):
-    """The oracle's CPU restatement of the quantised fc on a row sample of x
-    (all of W): returns (seconds per sample, ops per sample)."""
-    import numpy as np
-    from oracle import oracle as O
-    x, w, b = make_inputs()
-    xs, wn, bn = x[:rows].numpy(), w.numpy(), b.numpy()
-    O.linear(xs[:8, :64].copy(), wn[:16, :64].copy(), None)  # build / warm the library
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        O.linear(xs, wn, bn)
-    dt = (time.perf_counter() - t0) / reps
-    return dt, 2 * rows * N * K
+# ---- the single-workload lines (profiling) -------------------------------------------
 
-
-def run_reference(args):
-    rank, _, world = dist_env()
-    if rank != 0:
-        return 0
-    import numpy as np  # noqa: F401
-    cores = os.cpu_count() or 1
-    rows = 256
-    for _ in range(max(1, args.warmup)):
-        oracle_sample(rows, 1)
-    times = []
-    for _ in range(args.steps):
-        dt, ops = oracle_sample(rows, 1)
-        times.append(dt)
-    ms = 1000 * statistics.mean(times)
-    value = ops / (ms / 1000) / 1e12
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int16",
-        "data": "synthetic (seeded N(0,1)/N(0,0.02)/N(0,0.01), no dataset)",
-        "config": {"workload": WORKLOAD, "sample": f"x rows 0..{rows} of {M}, all of W",
-                   "parallelism": "replicas only"},
-        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": cores, "kind": "port",
-                         "sample": f"{rows} of {M} rows of x with all of W per step "
-                                   "(oracle: C quantise + exact fp64 BLAS GEMM + C epilogue)"},
-        "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
+def run_single(args):
+    """--workload linear | bert | rowops: one object as its own line (one GPU)."""
+    import torch
+    import torch_kunlun  # noqa: F401
+    kunlun = torch_kunlun.kunlun
+    dev = torch.device("kunlun", 0)
+    peaks = load_peaks()
+    scratch = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush = lambda: scratch.fill_(1)  # noqa: E731
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        if args.workload == "linear":
+            r = linear_object(dev, kunlun, flush, peaks, M1, N1, K1, args.steps, args.warmup, False, False)
+        elif args.workload == "linear4096":
+            r = linear_object(dev, kunlun, flush, peaks, 4096, 4096, 4096, args.steps, args.warmup, False, False)
+        elif args.workload == "bert":
+            r = bert_object(dev, kunlun, flush, peaks, args.steps, args.warmup, False)
+        elif args.workload == "conv":
+            r = conv_object(dev, kunlun, flush, peaks, False, args.steps, args.warmup)
+        elif args.workload == "bmm":
+            r = bmm_object(dev, kunlun, flush, peaks, args.steps, args.warmup)
+        else:
+            r = rowops_object(dev, kunlun, flush, peaks, args.steps, args.warmup)
+    print(json.dumps({"workload": args.workload, "steps": args.steps, "warmup": args.warmup,
+                      "clocks": clocks.summary(), **r}), flush=True)
     return 0
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="kunlun", choices=["kunlun", "reference"])
+    ap.add_argument("--workload", default="tp_mlp",
+                    choices=["tp_mlp", "linear", "linear4096", "bert", "conv", "bmm", "rowops"])
+    ap.add_argument("--reduce", default="reduce_scatter",
+                    choices=["allreduce", "reduce_scatter", "peer", "peer_fused"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-bert", action="store_true", help="skip the encoder-block measurement")
-    ap.add_argument("--no-extra", action="store_true", help="skip the bmm and conv measurements")
-    ap.add_argument("--workload", default="linear", choices=["linear", "tp_mlp", "bert", "rowops"])
-    ap.add_argument("--reduce", default="allreduce", choices=["allreduce", "reduce_scatter", "peer", "peer_fused"])
+    ap.add_argument("--no-extra", action="store_true", help="skip the single-GPU objects on the N=1 line")
+    ap.add_argument("--no-extra-modes", action="store_true", help="time only the default reduction")
     args = ap.parse_args()
-    if args.workload == "tp_mlp" and args.impl != "reference":
-        return run_tp_mlp(args)
+    args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
-    args.warmup = max(args.warmup, 3)
-    if args.workload == "rowops" and args.impl != "reference":
-        return run_rowops(args)
-    if args.workload == "bert":
-        return run_bert(args)
-
-    import torch
-    import torch_kunlun  # noqa: F401
-    kunlun = torch_kunlun.kunlun
-
-    rank, local_rank, world = dist_env()
-    kunlun.set_device(local_rank)
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("kunlun", local_rank)
-    pg = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
-        pg = dist
-
-    x, w, b = make_inputs()
-    xd, wd, bd = x.to(dev), w.to(dev), b.to(dev)
-    out = torch.empty(M, N, dtype=torch.float16, device=dev)
-    scratch = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
-
-    def flush():
-        scratch.fill_(1)
-
-    def step():
-        torch.nn.functional.linear(xd, wd, bd)
-
-    if pg:
-        pg.barrier()
-    kunlun.synchronize()
-    with ClockSampler(torch.cuda.current_device()) as clocks:
-        times = timed_steps(step, args.steps, args.warmup, flush, kunlun)
-    kunlun.synchronize()
-    if pg:
-        pg.barrier()
-    ms = sum(times) / len(times)
-    clock = clocks.summary()
-
-    # end-to-end through the public API with host buffers: every step copies
-    # its inputs from pinned host memory, runs the op and reads the result
-    # back.  Steps are pipelined the way a serving loop runs them: the H2D
-    # copies on one stream, the op on the compute stream, the D2H on a third
-    # (PCIe is full duplex), two buffer sets alternating; the time is the
-    # whole K-step loop on the device (events on the compute stream) / K.
-    xh, wh, bh = x.pin_memory(), w.pin_memory(), b.pin_memory()
-    yh = [torch.empty(M, N, dtype=torch.float16).pin_memory() for _ in range(2)]
-    e2e_ms = e2e_pipelined(xh, wh, bh, yh, dev, kunlun, args.steps, args.warmup)
-
-    parts = kernel_breakdown(xd, wd, bd, out, kunlun, flush)
-    bert = None
-    if not args.no_bert:
-        bert = bert_measure(dev, kunlun, max(5, args.steps // 10), args.warmup, flush)
-    bmm = conv = None
-    if not args.no_extra:
-        bmm = bmm_measure(dev, kunlun, flush)
-        conv = conv_measure(dev, kunlun, flush)
-
-    # max over ranks of the timed quantities
-    if pg:
-        t = torch.tensor([ms, e2e_ms, parts["gemm"], bert["ms_per_block"] if bert else 0.0],
-                         dtype=torch.float64)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        ms, e2e_ms, gemm_ms, bert_ms = t.tolist()
-        if bert:
-            bert["ms_per_block"] = bert_ms
-            bert["tokens_per_s"] = world * BERT_B * BERT_L / (bert_ms / 1000)
-    else:
-        gemm_ms = parts["gemm"]
-
-    int8_peak = measured_int8_peak_tops(torch) if rank == 0 else None
-    cpu_base = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        reps = []
-        for _ in range(3):
-            dt, ops = oracle_sample(256, 1)
-            reps.append(dt)
-        cpu_base = {"value": ops / statistics.mean(reps) / 1e12, "unit": "TOPS",
-                    "cores": os.cpu_count() or 1, "kind": "port",
-                    "sample": "256 of 2048 rows of x with all of W per call, 3 calls "
-                              "(oracle: C quantise + exact fp64 BLAS GEMM + C epilogue)"}
-        if bert:
-            tps, threads = bert_cpu_baseline()
-            bert["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads,
-                                    "kind": "torch CPU aten fp32 eager",
-                                    "sample": "1 of 32 sequences (512 tokens), median of 3"}
-        if conv:
-            cb = conv_cpu_baseline()
-            for name, v in cb.items():
-                conv[name]["cpu_baseline_tops"] = v
-
-    if rank == 0:
-        value = world * OPS_PER_STEP / (ms / 1000) / 1e12
-        achieved = OPS_PER_STEP / (gemm_ms / 1000) / 1e12
-        peak = int8_peak / 4.0
-        line = {
-            "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int16",
-            "data": "synthetic (seeded N(0,1)/N(0,0.02)/N(0,0.01), no dataset)",
-            "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "parallelism":
-                       "replicas only" if world > 1 else "single GPU",
-                       "l2": "flushed between steps (512 MiB device write outside the timed events)",
-                       "step_breakdown_ms": {"gemm": round(gemm_ms, 4),
-                                             "amax_and_quantise": round(ms - gemm_ms, 4)}},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
-                         "unit": "TOPS", "frac": achieved / peak,
-                         "traffic": ncu_traffic(),
-                         "kernel": "qgemm_tc_kernel (tcgen05 kind::i8, 4 limb MMAs per int16 MAC)",
-                         "peak_source": f"int8 dense {int8_peak:.0f} TOPS measured live (cuBLASLt "
-                                        "int8 8192^3 via torch._int_mm, burst) / 4 limb MMAs"},
-            "e2e": {"value": world * OPS_PER_STEP / (e2e_ms / 1000) / 1e12, "unit": "TOPS",
-                    "h2d_bytes_per_step": int(xh.nbytes + wh.nbytes + bh.nbytes),
-                    "d2h_bytes_per_step": int(yh[0].nbytes), "ms_per_step": e2e_ms,
-                    "timing": "K pipelined steps (H2D, op, D2H on three streams, two buffer sets), "
-                              "device time of the whole loop / K"},
-            "gpu_launches": KERNELS_PER_STEP * args.steps,
-            "clocks": clock,
-            "cpu_baseline": cpu_base,
-            "bert_block": bert,
-            "bmm_attention_scores": None if bmm is None else {
-                "workload": "S = A[64,512,128] @ B[64,128,512], P = softmax(S), O = P @ V[64,512,128]",
-                "ops_per_step": BMM_OPS, **bmm},
-            "conv_resnet50": None if conv is None else {
-                "workload": "conv2d NCHW fp16 batch 64, Kaiming-normal weights, ReLU(N(0,1)) inputs",
-                "cpu_baseline": "torch CPU aten fp32 on 4 of 64 images, all host threads",
-                **conv},
-        }
-        print(json.dumps(line), flush=True)
-    if pg:
-        pg.barrier()
-        pg.destroy_process_group()
-    return 0
-
-
-def run_bert(args):
-    """Encoder block alone on one GPU (tokens/s)."""
-    import torch
-    import torch_kunlun  # noqa: F401
-    kunlun = torch_kunlun.kunlun
-    dev = torch.device("kunlun", 0)
-    scratch = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    with ClockSampler(torch.cuda.current_device()) as clocks:
-        r = bert_measure(dev, kunlun, args.steps, args.warmup, lambda: scratch.fill_(1))
-    line = {"metric": "BERT-block tokens/s", "value": r["tokens_per_s"], "unit": "tokens/s",
-            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": r["ms_per_block"], "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int16",
-            "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, no dataset)",
-            "config": {"workload": BERT_WORKLOAD, "parallelism": "single GPU",
-                       "l2": "flushed between steps (512 MiB device write outside the timed events)"},
-            "effective_tops": r["effective_tops"], "clocks": clocks.summary()}
-    print(json.dumps(line), flush=True)
-    return 0
-
-
-def run_rowops(args):
-    """The HBM-bound kernels on their benchmark shapes: softmax over
-    [64, 512, 512] fp16 (the cfg2 scores), layer_norm over [16384, 768] fp16
-    (cfg4), and the cfg1 operands' amax + quantise (one F.linear, whose two
-    quantise launches a profiler separates).  Algorithmic bytes: 2 + 2 B per
-    element for softmax and layer_norm (plus gamma / beta), 2 B read (amax) +
-    2 B read + 2 B written (limbs) per element for the quantise."""
-    import torch
-    import torch_kunlun  # noqa: F401
-    kunlun = torch_kunlun.kunlun
-    dev = torch.device("kunlun", 0)
-    scratch = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    flush = lambda: scratch.fill_(1)  # noqa: E731
-    g = torch.Generator().manual_seed(0)
-    s = torch.randn(64, 512, 512, generator=g).half().to(dev)
-    h = torch.randn(16384, 768, generator=g).half().to(dev)
-    gamma = (1 + 0.1 * torch.randn(768, generator=g)).half().to(dev)
-    beta = (0.1 * torch.randn(768, generator=g)).half().to(dev)
-    x = torch.randn(M, K, generator=g).half().to(dev)
-    w = (torch.randn(N, K, generator=g) * 0.02).half().to(dev)
-    out = {}
-    for name, fn, nbytes in (
-            ("softmax_64x512x512", lambda: torch.softmax(s, -1), 4 * s.numel()),
-            ("layer_norm_16384x768", lambda: torch.nn.functional.layer_norm(h, (768,), gamma, beta, 1e-12),
-             4 * h.numel() + 4 * 768)):
-        ts = timed_steps(fn, args.steps, args.warmup, flush, kunlun)
-        ms = sum(ts) / len(ts)
-        out[name] = {"ms": ms, "gbs": nbytes / (ms / 1000) / 1e9, "bytes": nbytes}
-    torch.nn.functional.linear(x, w)  # the quantise launches, for a profiler
-    kunlun.synchronize()
-    peak = None
-    try:
-        with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")) as f:
-            peak = json.load(f).get("hbm_gbs")
-    except (OSError, ValueError):
-        pass
-    for v in out.values():
-        v["frac_of_8tbs"] = v["gbs"] / 8000.0
-        if peak:
-            v["frac_of_measured"] = v["gbs"] / peak
-    print(json.dumps({"workload": "rowops", "steps": args.steps, "warmup": args.warmup,
-                      "l2": "flushed between steps", "hbm_peak_measured_gbs": peak, **out}), flush=True)
-    return 0
-
-
-def run_tp_mlp(args):
-    """Tensor-parallel MLP (strong scaling: the whole MLP is split over the
-    ranks).  Inputs are larger than L2, so no flush is needed."""
-    import datetime
-
-    import torch
-    import torch.distributed as dist
-    import torch_kunlun  # noqa: F401
-    from torch_kunlun_b200 import tp
-    kunlun = torch_kunlun.kunlun
-    rank, local_rank, world = dist_env()
-    kunlun.set_device(local_rank)
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("kunlun", local_rank)
-    if world > 1:
-        dist.init_process_group("bkcl", timeout=datetime.timedelta(seconds=300))
-    fr = TP_F // world
-
-    def randn_dev(shape, seed, scale):
-        g = torch.Generator(device="cuda").manual_seed(seed)
-        t = (torch.randn(shape, generator=g, device="cuda") * scale).half()
-        out = torch.empty(shape, dtype=torch.float16, device=dev)
-        out.copy_(t)
-        return out
-
-    x = randn_dev((TP_T, TP_H), 0, 1.0)
-    wg = randn_dev((fr, TP_H), 1000 + rank, 0.02)
-    wu = randn_dev((fr, TP_H), 2000 + rank, 0.02)
-    wd = randn_dev((TP_H, fr), 3000 + rank, 0.02)
-    torch.cuda.synchronize()
-    comm = kunlun.Stream(dev)
-
-    def step():
-        tp.tp_mlp_forward(x, wg, wu, wd, reduce=args.reduce, chunks=4, comm_stream=comm)
-
-    if world > 1:
-        dist.barrier()
-    kunlun.synchronize()
-    with ClockSampler(torch.cuda.current_device()) as clocks:
-        times = timed_steps(step, args.steps, args.warmup, lambda: None, kunlun)
-    kunlun.synchronize()
-    ms = sum(times) / len(times)
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float32).to(dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.cpu().item())
-        dist.barrier()
-    if rank == 0:
-        line = {
-            "metric": TP_METRIC, "value": TP_OPS_PER_STEP / (ms / 1000) / 1e12, "unit": "TOPS",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int16",
-            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, no dataset)",
-            "config": {"workload": TP_WORKLOAD, "T": TP_T, "H": TP_H, "F": TP_F,
-                       "parallelism": f"tp{world}", "reduce": args.reduce,
-                       "overlap": OVERLAP[args.reduce], "l2": "inputs larger than L2"},
-            "gpu_launches": None, "clocks": clocks.summary(),
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        tp.release_peer_buffers()
-        dist.destroy_process_group()
-    return 0
-
-
-OVERLAP = {
-    "allreduce": "down projection in 4 row blocks, each block's all-reduce on a second stream",
-    "reduce_scatter": "none: one GEMM, then the bkcl reduce-scatter",
-    "peer": "down projection one owner's row block at a time; each finished block is copied by a copy "
-            "engine into its owner's buffer (CUDA IPC, NVLink) while the next block computes; a "
-            "one-element all-reduce as the barrier, then each rank sums its slots",
-    "peer_fused": "the down GEMM's epilogue stores each tile into the owning rank's buffer over NVLink "
-                  "(CUDA IPC), a one-element all-reduce as the barrier, then each rank sums its slots",
-}
+    if args.workload == "tp_mlp":
+        return run_tp(args)
+    return run_single(args)
 
 
 if __name__ == "__main__":

@@ -41,6 +41,11 @@ F16 = 0
 F32 = 1
 ACT_NONE = 0
 ACT_RELU = 1
+ACT_GELU = 2
+ACT_GELU_TANH = 3
+ACT_SILU = 4
+ACT_CODES = {"none": ACT_NONE, "relu": ACT_RELU, "gelu": ACT_GELU, "gelu_tanh": ACT_GELU_TANH,
+             "silu": ACT_SILU}
 Q = 32767.0
 
 
@@ -80,6 +85,13 @@ def lib():
         L.tko_epilogue.argtypes = [i32, i64, i64, p, f32, f32, f32, p, p, i64, i64,
                                    f32, i32, p, i64]
         L.tko_conv2d_i16.argtypes = [i64] * 14 + [p, p, p]
+        L.tko_act64.argtypes = [f64, i32]
+        L.tko_act64.restype = f64
+        L.tko_act.argtypes = [p, i32, i64, i32, p]
+        L.tko_silu_mul.argtypes = [p, p, i32, i64, p]
+        L.tko_softmax.argtypes = [p, i32, i64, i64, i32, p]
+        L.tko_layer_norm.argtypes = [p, i32, i64, i64, p, p, i32, f64, p, p, p]
+        L.tko_num_threads.restype = i32
         _lib = L
     return _lib
 
@@ -139,6 +151,21 @@ def gemm_i16_exact(qa: np.ndarray, qb: np.ndarray) -> np.ndarray:
     return np.matmul(qa.astype(np.float64), qb.astype(np.float64)).astype(np.int64)
 
 
+def gemm_i16_strided(qa: np.ndarray, qb: np.ndarray) -> np.ndarray:
+    """acc = qa @ qb with the C int64 loop on the arrays' own strides (no
+    copies; host threads over output elements).  Used for skinny products
+    (few rows), where converting the big operand to float64 would dominate."""
+    assert qa.dtype == np.int16 and qb.dtype == np.int16 and qa.ndim == 2 and qb.ndim == 2
+    M, K = qa.shape
+    K2, N = qb.shape
+    assert K == K2
+    acc = np.empty((M, N), dtype=np.int64)
+    sa = [st // 2 for st in qa.strides]
+    sb = [st // 2 for st in qb.strides]
+    lib().tko_gemm_i16(M, N, K, _ptr(qa), sa[0], sa[1], _ptr(qb), sb[0], sb[1], _ptr(acc))
+    return acc
+
+
 def gemm_i16_scalar(qa: np.ndarray, qb: np.ndarray) -> np.ndarray:
     """acc = qa @ qb with the C int64 loop (slow; used to pin the shortcut)."""
     qa = np.ascontiguousarray(qa, dtype=np.int16)
@@ -186,7 +213,12 @@ def fc(x: np.ndarray, w: np.ndarray, w_trans: bool, bias=None, alpha=1.0,
     ax, aw = amax(x), amax(w)
     qx, qw = quant(x, ax), quant(w, aw)
     qb = qw.T if w_trans else qw
-    acc = gemm_i16_scalar(qx, qb) if scalar else gemm_i16_exact(qx, qb)
+    if scalar:
+        acc = gemm_i16_scalar(qx, qb)
+    elif qx.shape[0] <= 64:
+        acc = gemm_i16_strided(qx, qb)
+    else:
+        acc = gemm_i16_exact(qx, qb)
     y = epilogue(acc, ax, aw, x.dtype, alpha, bias, addend, beta, act)
     return y, acc, ax, aw
 
@@ -403,38 +435,71 @@ def conv_weight_grad(x: np.ndarray, grad_out: np.ndarray, w_shape, stride, pad, 
     return y.reshape(acc.shape)
 
 
-# ---- float row ops (tolerance-level references, float64 internally) ----------
+# ---- floating-point ops: the textbook formulas in float64 (C, libm) -----------
+# The device evaluates the same formulas in binary32; tests compare at the
+# bounds they state (one or two binary16 ulps plus the binary32 error of the
+# libm-class functions the device calls).
 
 
-def softmax(x: np.ndarray, axis=-1) -> np.ndarray:
-    xd = x.astype(np.float64)
-    m = xd.max(axis=axis, keepdims=True)
-    e = np.exp(xd - m)
-    return (e / e.sum(axis=axis, keepdims=True)).astype(x.dtype)
+def _out_like(x, dtype=None):
+    return np.empty(x.shape, dtype=x.dtype if dtype is None else dtype)
 
 
-def layer_norm(x: np.ndarray, gamma, beta, eps) -> np.ndarray:
-    xd = x.astype(np.float64)
-    mu = xd.mean(-1, keepdims=True)
-    var = ((xd - mu) ** 2).mean(-1, keepdims=True)
-    y = (xd - mu) / np.sqrt(var + eps)
-    if gamma is not None:
-        y = y * np.asarray(gamma, dtype=np.float64)
-    if beta is not None:
-        y = y + np.asarray(beta, dtype=np.float64)
-    return y.astype(x.dtype)
+def act(x: np.ndarray, kind: str) -> np.ndarray:
+    """T(act(x)) elementwise: relu, gelu (erf), gelu_tanh, silu."""
+    x = np.ascontiguousarray(x)
+    out = _out_like(x)
+    lib().tko_act(_ptr(x), _dt(x), x.size, ACT_CODES[kind], _ptr(out))
+    return out
 
 
-def gelu(x: np.ndarray) -> np.ndarray:
-    from math import erf, sqrt
-    xd = x.astype(np.float64)
-    v = np.vectorize(lambda t: 0.5 * t * (1.0 + erf(t / sqrt(2.0))))(xd)
-    return v.astype(x.dtype)
+def gelu(x: np.ndarray, approximate: str = "none") -> np.ndarray:
+    return act(x, "gelu_tanh" if approximate == "tanh" else "gelu")
 
 
 def silu(x: np.ndarray) -> np.ndarray:
-    xd = x.astype(np.float64)
-    return (xd / (1.0 + np.exp(-xd))).astype(x.dtype)
+    return act(x, "silu")
+
+
+def silu_mul(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    """T(T(silu(gate)) * up): swish stored as T, then mul."""
+    gate = np.ascontiguousarray(gate)
+    up = np.ascontiguousarray(up, dtype=gate.dtype)
+    assert gate.shape == up.shape
+    out = _out_like(gate)
+    lib().tko_silu_mul(_ptr(gate), _ptr(up), _dt(gate), gate.size, _ptr(out))
+    return out
+
+
+def softmax(x: np.ndarray, axis=-1, out_dtype=None) -> np.ndarray:
+    """Softmax along the last axis (axis must be -1 or the last)."""
+    assert axis in (-1, x.ndim - 1)
+    x = np.ascontiguousarray(x)
+    od = np.dtype(out_dtype) if out_dtype is not None else x.dtype
+    out = np.empty(x.shape, dtype=od)
+    cols = x.shape[-1]
+    lib().tko_softmax(_ptr(x), _dt(x), x.size // max(cols, 1), cols, F16 if od == np.float16 else F32, _ptr(out))
+    return out
+
+
+def layer_norm(x: np.ndarray, gamma, beta, eps, return_stats=False):
+    x = np.ascontiguousarray(x)
+    cols = x.shape[-1]
+    rows = x.size // max(cols, 1)
+    wdt = x.dtype
+    g = None if gamma is None else np.ascontiguousarray(gamma)
+    b = None if beta is None else np.ascontiguousarray(beta)
+    if g is not None:
+        wdt = g.dtype
+    if b is not None:
+        b = b.astype(wdt)
+    out = _out_like(x)
+    mean = np.empty(rows, dtype=np.float32)
+    rstd = np.empty(rows, dtype=np.float32)
+    lib().tko_layer_norm(_ptr(x), _dt(x), rows, cols, None if g is None else _ptr(g),
+                         None if b is None else _ptr(b), F16 if wdt == np.float16 else F32, float(eps),
+                         _ptr(out), _ptr(mean), _ptr(rstd))
+    return (out, mean, rstd) if return_stats else out
 
 
 def round_t(v: np.ndarray, dtype) -> np.ndarray:
@@ -449,7 +514,8 @@ def round_t(v: np.ndarray, dtype) -> np.ndarray:
     return bits.view(np.float16).reshape(v.shape)
 
 
-def sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask=None, scale=None, causal=False):
+def sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask=None, scale=None, causal=False,
+         return_p=False):
     """The reference's SDPA composition over [BH, L, E] slices.
 
     Steps (torch_kunlun/kunlun/attention.py:85-106): per-slice quantised bmm
@@ -474,4 +540,5 @@ def sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask=None, scale=None, cau
         s = round_t(s.astype(np.float32) + np.broadcast_to(mask, s.shape).astype(np.float32),
                     q.dtype)
     p = softmax(s, -1)
-    return bmm(p, v)
+    out = bmm(p, v)
+    return (out, p) if return_p else out

@@ -64,8 +64,7 @@ def oracle_qgemm(a, b_nk, *, bias=None, addend=None, alpha=1.0, beta=0.0, act="n
     an = _np(a)
     bn = _np(b_nk)
     B = an.shape[0]
-    act_code = O.ACT_RELU if act == "relu" else O.ACT_NONE
-    assert act in ("none", "relu")
+    act_code = O.ACT_CODES[act]
     outs = []
     if per_slice:
         amax_a = [O.amax(an[i]) for i in range(B)]
