@@ -74,6 +74,13 @@ DW_CASES = [
     (3, 5, 1, 8, 8, 3, 1, 0, 1, True, torch.float32),
     (1, 3, 1, 50, 50, 3, 1, 1, 1, False, torch.float16),   # plane too large for the staged kernels
     (2, 8, 2, 40, 40, 3, 1, 1, 1, True, torch.float16),    # multiplier 2 on planes above 1024
+    # the row kernel (multiplier 1, unit stride and dilation, KW in 3/5/7):
+    (64, 512, 1, 7, 7, 3, 1, 1, 1, True, torch.float16),   # the benchmark shape, with bias
+    (2, 16, 1, 9, 13, 3, 1, 1, 1, False, torch.float32),   # rows longer than one 8-output window
+    (3, 5, 1, 20, 17, 5, 1, 2, 1, True, torch.float16),    # 5x5, ragged plane count per block
+    (1, 7, 1, 11, 11, 7, 1, 3, 1, True, torch.float16),    # 7x7
+    (2, 3, 1, 1, 40, 3, 1, 1, 1, False, torch.float16),    # one-row planes, padding wider than the row
+    (2, 6, 1, 5, 5, 3, 1, 2, 1, True, torch.float32),      # padding 2: outputs beyond the input
 ]
 
 

@@ -303,6 +303,139 @@ depthwise_flat_kernel(const T* __restrict__ x, const T* __restrict__ w, const T*
     }
 }
 
+// Depthwise with multiplier 1, unit stride and unit dilation (the depthwise
+// layers of the benchmark networks): a block takes a run of whole planes --
+// one contiguous span of the NCHW input and of the output -- quantises it
+// into zero-padded planes in shared memory (so the tap loops need no bounds
+// checks), and each thread produces a whole output row: kDwRowOut outputs at
+// a time from a sliding window of KW + kDwRowOut - 1 inputs per filter row,
+// int32 products (|q| <= 32767, so each product is below 2^30) summed exactly
+// in int64, then the shared epilogue.  HBM-bound: every input and output
+// element crosses HBM once.
+constexpr int kDwRowThreads = 256;
+constexpr int kDwRowSpan = 8192;  // padded input elements per block
+constexpr int kDwRowTaps = 1024;  // weight taps per block (planes x KH x KW)
+constexpr int kDwRowOut = 8;      // outputs per window along a row
+
+template <typename T, int DT, int KW>
+__global__ void __launch_bounds__(kDwRowThreads)
+depthwise_rows_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ bias,
+                      T* __restrict__ out, ConvGeom g, int ppb, const float* __restrict__ amax_x,
+                      const float* __restrict__ amax_w) {
+    // slack after the last plane: the last window of a row reads up to
+    // kDwRowOut + KW - 2 elements past the row's last output column
+    __shared__ int16_t xs[kDwRowSpan + kDwRowOut + KW];
+    __shared__ int wsq[kDwRowTaps];
+    const int H = static_cast<int>(g.H), W = static_cast<int>(g.W);
+    const int ph = static_cast<int>(g.ph), pw = static_cast<int>(g.pw);
+    const int Hp = H + 2 * ph, Wp = W + 2 * pw;
+    const int KH = static_cast<int>(g.KH);
+    const int OH = static_cast<int>(g.OH), OW = static_cast<int>(g.OW);
+    const int HW = H * W, PHW = Hp * Wp, taps = KH * KW;
+    const int64_t planes = g.N * g.C;
+    const int64_t pl0 = static_cast<int64_t>(blockIdx.x) * ppb;
+    const int np = static_cast<int>(min(static_cast<int64_t>(ppb), planes - pl0));
+    const float ax = __ldg(amax_x), aw = __ldg(amax_w);
+    const float invx = quant_inv(ax), invw = quant_inv(aw);
+    const double s = dequant_scale(ax, aw);
+    const int span = np * PHW;
+    for (int i = threadIdx.x; i < span + kDwRowOut + KW; i += blockDim.x) xs[i] = 0;
+    __syncthreads();
+    const int C = static_cast<int>(g.C);
+    const int c0 = static_cast<int>(pl0 % g.C);  // channel of the block's first plane
+    // the span's elements [0, n): a scalar head up to the first 16-byte
+    // boundary, 16-byte vectors, a scalar tail (all loads in flight at once)
+    const T* xb = x + pl0 * HW;
+    const int n = np * HW;
+    constexpr int VEC = 16 / sizeof(T);
+    auto put = [&](int i, float v) {
+        const int pp = i / HW, r = i - pp * HW;
+        const int ih = r / W, iw = r - ih * W;
+        xs[pp * PHW + (ih + ph) * Wp + iw + pw] = static_cast<int16_t>(quant_one(v, invx));
+    };
+    const bool aligned = reinterpret_cast<uintptr_t>(x) % 16 == 0;
+    const int head = aligned ? min(n, static_cast<int>((VEC - (pl0 * HW) % VEC) % VEC)) : n;
+    const int nv = (n - head) / VEC;
+    for (int i = threadIdx.x; i < head; i += blockDim.x) put(i, ldx<T>(xb, i));
+    for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+        const int i0 = head + v * VEC;
+        float f[VEC];
+        if constexpr (sizeof(T) == 2) {
+            const uint4 u = __ldg(reinterpret_cast<const uint4*>(xb + i0));
+            const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 t = __half22float2(h2[e]);
+                f[2 * e] = t.x;
+                f[2 * e + 1] = t.y;
+            }
+        } else {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(xb + i0));
+            f[0] = t.x; f[1] = t.y; f[2] = t.z; f[3] = t.w;
+        }
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) put(i0 + e, f[e]);
+    }
+    for (int i = head + nv * VEC + threadIdx.x; i < n; i += blockDim.x) put(i, ldx<T>(xb, i));
+    for (int i = threadIdx.x; i < np * taps; i += blockDim.x) {
+        const int pp = i / taps, t = i - pp * taps;
+        int c = c0 + pp;
+        while (c >= C) c -= C;
+        wsq[i] = quant_one(ldx<T>(w, static_cast<int64_t>(c) * taps + t), invw);
+    }
+    __syncthreads();
+    T* ob = out + pl0 * OH * OW;
+    for (int row = threadIdx.x; row < np * OH; row += blockDim.x) {
+        const int pp = row / OH, oh = row - pp * OH;
+        const int16_t* xr = xs + pp * PHW + oh * Wp;
+        const int* wp = wsq + pp * taps;
+        int c = c0 + pp;
+        while (c >= C) c -= C;
+        const float bv = bias != nullptr ? ldx<T>(bias, c) : 0.0f;
+        T* orow = ob + static_cast<int64_t>(row) * OW;
+        for (int ow0 = 0; ow0 < OW; ow0 += kDwRowOut) {
+            long long acc[kDwRowOut];
+#pragma unroll
+            for (int j = 0; j < kDwRowOut; ++j) acc[j] = 0;
+            for (int r = 0; r < KH; ++r) {
+                int xv[kDwRowOut + KW - 1];
+#pragma unroll
+                for (int j = 0; j < kDwRowOut + KW - 1; ++j) xv[j] = xr[r * Wp + ow0 + j];
+#pragma unroll
+                for (int k = 0; k < KW; ++k) {
+                    const int wv = wp[r * KW + k];
+#pragma unroll
+                    for (int j = 0; j < kDwRowOut; ++j) acc[j] += xv[j + k] * wv;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kDwRowOut; ++j) {
+                if (ow0 + j < OW) {
+                    float v = round_t_from_double(__dmul_rn(static_cast<double>(acc[j]), s), DT);
+                    if (bias != nullptr) v = round_t(__fadd_rn(v, bv), DT);
+                    store_t(orow, DT, ow0 + j, v);
+                }
+            }
+        }
+    }
+}
+
+// Planes per block of depthwise_rows_kernel for this geometry (0: the
+// kernel does not apply): about one output row per thread, within the
+// shared-memory spans.
+int depthwise_rows_ppb(const ConvGeom& g) {
+    if (!(g.D == 1 && g.KD == 1 && g.groups == g.C && g.groups > 1 && g.F == g.C)) return 0;
+    if (g.sh != 1 || g.sw != 1 || g.dh != 1 || g.dw != 1) return 0;
+    if (g.KW != 3 && g.KW != 5 && g.KW != 7) return 0;
+    const int64_t phw = (g.H + 2 * g.ph) * (g.W + 2 * g.pw);
+    const int64_t taps = g.KH * g.KW;
+    if (phw > kDwRowSpan || taps > kDwRowTaps || g.OW > 4096) return 0;
+    int64_t ppb = std::max<int64_t>(1, ceil_div(kDwRowThreads, g.OH));
+    ppb = std::min(ppb, kDwRowSpan / phw);
+    ppb = std::min(ppb, kDwRowTaps / taps);
+    return static_cast<int>(std::max<int64_t>(ppb, 1));
+}
+
 int grid_1d(int64_t n, int threads) {
     const int64_t g = ceil_div(n, threads);
     const int64_t cap = static_cast<int64_t>(sm_count(current_device())) * 32;
@@ -582,6 +715,29 @@ int tk_conv3d_q16(const tk_conv3d_desc_t* desc, void* workspace, size_t workspac
         aw = amax + 1;
     }
     const int64_t P = g.OD * g.OH * g.OW;
+    if (const int ppb = depthwise_rows_ppb(g)) {
+        const int64_t blocks = ceil_div(g.N * g.C, ppb);
+        TK_CHECK_ARG(blocks < (1LL << 31), "conv2d: too many planes");
+        const unsigned grid = static_cast<unsigned>(blocks);
+#define TK_DW_ROWS(KWV)                                                                                  \
+    if (d.dtype == TK_DTYPE_F16)                                                                         \
+        depthwise_rows_kernel<__half, 0, KWV><<<grid, kDwRowThreads, 0, stream>>>(                      \
+            static_cast<const __half*>(d.x), static_cast<const __half*>(d.weight),                      \
+            static_cast<const __half*>(d.bias), static_cast<__half*>(d.out), g, ppb, ax, aw);           \
+    else                                                                                                 \
+        depthwise_rows_kernel<float, 1, KWV><<<grid, kDwRowThreads, 0, stream>>>(                       \
+            static_cast<const float*>(d.x), static_cast<const float*>(d.weight),                        \
+            static_cast<const float*>(d.bias), static_cast<float*>(d.out), g, ppb, ax, aw);
+        if (g.KW == 3) {
+            TK_DW_ROWS(3)
+        } else if (g.KW == 5) {
+            TK_DW_ROWS(5)
+        } else {
+            TK_DW_ROWS(7)
+        }
+#undef TK_DW_ROWS
+        return launch_status("conv2d depthwise");
+    }
     if (is_depthwise(g) && g.F == g.C && g.H * g.W <= kDwFlatElems / 2 &&
         g.KH * g.KW * (kDwFlatElems / (g.H * g.W)) <= kDwFlatElems / 4) {
         const int ppb = static_cast<int>(kDwFlatElems / (g.H * g.W));

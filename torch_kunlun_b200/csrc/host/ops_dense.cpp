@@ -121,6 +121,22 @@ at::Tensor mm(const at::Tensor& self, const at::Tensor& mat2) {
     return out;
 }
 
+// 1-D products on the quantised mm, each vector one per-tensor scale: the
+// matmul cases the reference stages through the CPU
+// (csrc/linalg_extra.cpp:232-236) -- torch's matmul sends 1-D x 1-D to dot
+// and a (folded) matrix x vector to mv.
+at::Tensor dot(const at::Tensor& self, const at::Tensor& other) {
+    TORCH_CHECK(self.dim() == 1 && other.dim() == 1, "kunlun dot requires 1-D tensors");
+    TORCH_CHECK(self.size(0) == other.size(0), "kunlun dot: sizes differ (", self.size(0), " vs ",
+                other.size(0), ")");
+    return ::torch_kunlun::mm(self.unsqueeze(0), other.unsqueeze(1)).view(at::IntArrayRef{});
+}
+
+at::Tensor mv(const at::Tensor& self, const at::Tensor& vec) {
+    TORCH_CHECK(self.dim() == 2 && vec.dim() == 1, "kunlun mv requires a matrix and a vector");
+    return ::torch_kunlun::mm(self, vec.unsqueeze(1)).view({self.size(0)});
+}
+
 at::Tensor addmm(const at::Tensor& self, const at::Tensor& mat1, const at::Tensor& mat2,
                  const at::Scalar& beta, const at::Scalar& alpha) {
     TORCH_CHECK(mat1.dim() == 2 && mat2.dim() == 2, "kunlun addmm requires 2-D matrices");
@@ -587,6 +603,8 @@ at::Tensor conv2d_autograd(const at::Tensor& input, const at::Tensor& weight,
 
 TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
     m.impl("mm", TORCH_FN(torch_kunlun::mm));
+    m.impl("dot", TORCH_FN(torch_kunlun::dot));
+    m.impl("mv", TORCH_FN(torch_kunlun::mv));
     m.impl("addmm", TORCH_FN(torch_kunlun::addmm));
     m.impl("bmm", TORCH_FN(torch_kunlun::bmm));
     m.impl("baddbmm", TORCH_FN(torch_kunlun::baddbmm));

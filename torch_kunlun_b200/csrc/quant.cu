@@ -564,6 +564,28 @@ int amax_pair_launch(tk_dtype_t dtype, const void* x, int64_t nx, const void* w,
     return launch_status("amax");
 }
 
+// One launch of quant_vec_kernel over up to two row-contiguous operands.
+int launch_quant_vec(tk_dtype_t dt, const QVecDesc* vd, int nvec, cudaStream_t stream) {
+    auto warp_items = [](const QVecDesc& d) {
+        return d.items / d.groups * ceil_div(d.groups, kSegGroups);  // rows x segments
+    };
+    const int64_t items0 = warp_items(vd[0]);
+    const int64_t items1 = nvec > 1 ? warp_items(vd[1]) : 0;
+    const int64_t blocks = ceil_div(items0 + items1, 8);
+    TK_CHECK_ARG(blocks < (1LL << 31), "quantise: too many rows");
+    const QVecDesc second = nvec > 1 ? vd[1] : vd[0];
+    const dim3 block(32, 8);
+    if (dt == TK_DTYPE_F16)
+        quant_vec_kernel<__half><<<static_cast<unsigned>(blocks), block, 0, stream>>>(
+            vd[0], second, items0, items0 + items1);
+    else
+        quant_vec_kernel<float><<<static_cast<unsigned>(blocks), block, 0, stream>>>(
+            vd[0], second, items0, items0 + items1);
+    return launch_status("quantise");
+}
+
+bool quant_vec_ok(tk_dtype_t dt, const QuantOperand& o);
+
 int quantize_limbs_launch(tk_dtype_t dtype, const void* x, int64_t batch, int64_t rows,
                           int64_t cols, int64_t sb, int64_t sr, int64_t sc, const float* amax,
                           int64_t amax_stride, int8_t* limbs, cudaStream_t stream) {
@@ -576,6 +598,26 @@ int quantize_limbs_launch(tk_dtype_t dtype, const void* x, int64_t batch, int64_
     const int64_t ld = static_cast<int64_t>(round_up(static_cast<size_t>(cols), 16));
     if (ld == 0) return TK_OK;
     TK_CHECK_ARG(cols == 0 || x != nullptr, "tk_quantize_limbs: x is NULL");
+    {
+        // row-contiguous views: the vectorised kernel (16-byte loads, one
+        // warp per 1024-column row segment)
+        const QuantOperand o = {x, batch, rows, cols, sb, sr, sc, amax_stride != 0, amax, nullptr, limbs};
+        if (cols > 0 && quant_vec_ok(dtype, o)) {
+            QVecDesc d = {};
+            d.x = x;
+            d.rows = rows;
+            d.cols = cols;
+            d.ld = ld;
+            d.sb = sb;
+            d.sr = sr;
+            d.groups = ld / 8;
+            d.items = batch * rows * d.groups;
+            d.amax = amax;
+            d.amax_stride = amax_stride;
+            d.limbs = limbs;
+            return launch_quant_vec(dtype, &d, 1, stream);
+        }
+    }
     dim3 grid(static_cast<unsigned>(ceil_div(ld, kQT)), static_cast<unsigned>(ceil_div(rows, kQT)),
               static_cast<unsigned>(batch));
     TK_CHECK_ARG(grid.y <= 65535, "tk_quantize_limbs: too many rows (%lld)", (long long)rows);
@@ -691,23 +733,7 @@ int quantise_operands(tk_dtype_t dt, const QuantOperand* ops, int nops, cudaStre
             if (rc) return rc;
         }
     }
-    if (nvec > 0) {
-        auto warp_items = [](const QVecDesc& d) {
-            return d.items / d.groups * ceil_div(d.groups, kSegGroups);  // rows x segments
-        };
-        const int64_t items0 = warp_items(vd[0]);
-        const int64_t items1 = nvec > 1 ? warp_items(vd[1]) : 0;
-        const int64_t blocks = ceil_div(items0 + items1, 8);
-        TK_CHECK_ARG(blocks < (1LL << 31), "quantise: too many rows");
-        const dim3 block(32, 8);
-        if (dt == TK_DTYPE_F16)
-            quant_vec_kernel<__half><<<static_cast<unsigned>(blocks), block, 0, stream>>>(
-                vd[0], vd[1], items0, items0 + items1);
-        else
-            quant_vec_kernel<float><<<static_cast<unsigned>(blocks), block, 0, stream>>>(
-                vd[0], vd[1], items0, items0 + items1);
-        return launch_status("quantise");
-    }
+    if (nvec > 0) return launch_quant_vec(dt, vd, nvec, stream);
     return TK_OK;
 }
 

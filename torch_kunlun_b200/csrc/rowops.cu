@@ -6,6 +6,9 @@
 // with warp shuffles in a fixed order (so results are deterministic), and
 // written back once.  Longer rows use a block per row with a shared-memory
 // reduction.  Arithmetic is fp32; outputs are rounded once to the row dtype.
+#include <algorithm>
+#include <mutex>
+
 #include "tk_internal.h"
 
 namespace tk {
@@ -65,6 +68,14 @@ __device__ __forceinline__ void stv(float* p, const float (&v)[N]) {
         *reinterpret_cast<float4*>(p + 4 * c) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
 }
 
+// exp(x) as 2^(x log2 e) on the special-function unit (relative error of a
+// few binary32 ulps, inside the bound the softmax parity tests state).
+__device__ __forceinline__ float exp_sfu(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
+    return y;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -108,7 +119,7 @@ __global__ void softmax_warp_kernel(const TI* __restrict__ x, TO* __restrict__ y
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
-        v[i] = (v[i] == -INFINITY) ? 0.f : expf(v[i] - m);
+        v[i] = (v[i] == -INFINITY) ? 0.f : exp_sfu(v[i] - m);
         s += v[i];
     }
     s = warp_sum(s);
@@ -147,7 +158,7 @@ __global__ void softmax_block_kernel(const TI* __restrict__ x, TO* __restrict__ 
     m = red[0];
     __syncthreads();
     float s = 0.f;
-    for (int c = threadIdx.x; c < cols; c += blockDim.x) s += expf(ldf<TI>(xr, c) - m);
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) s += exp_sfu(ldf<TI>(xr, c) - m);
     s = warp_sum(s);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
     __syncthreads();
@@ -158,7 +169,7 @@ __global__ void softmax_block_kernel(const TI* __restrict__ x, TO* __restrict__ 
     }
     __syncthreads();
     const float inv = 1.0f / red[0];
-    for (int c = threadIdx.x; c < cols; c += blockDim.x) stf<TO>(yr, c, expf(ldf<TI>(xr, c) - m) * inv);
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) stf<TO>(yr, c, exp_sfu(ldf<TI>(xr, c) - m) * inv);
 }
 
 template <typename T, typename TW, int PER>
@@ -270,6 +281,166 @@ __global__ void layer_norm_block_kernel(const T* __restrict__ x, const TW* __res
     }
 }
 
+// ---- persistent row kernels: the next row's loads in flight ----------------
+//
+// One warp per row as above (lane l owns the 16-byte vectors l, l + 32, ...
+// of the row, so the per-lane partial sums and the butterfly reduction run in
+// the same order), but a warp walks rows with a grid stride and issues the
+// next row's loads before it reduces the current one: the HBM latency of a
+// row overlaps the arithmetic of the previous one, and a grid of a few waves
+// of warps replaces one warp per row.
+template <typename T, int NV>
+__device__ __forceinline__ void load_row_vecs(const T* row, int cols, int lane, uint4 (&v)[NV]) {
+    constexpr int VEC = 16 / sizeof(T);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        const int c0 = (j * 32 + lane) * VEC;
+        v[j] = c0 < cols ? __ldg(reinterpret_cast<const uint4*>(row + c0)) : make_uint4(0, 0, 0, 0);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack_vec(const uint4& u, float* o) {
+    if constexpr (sizeof(T) == 2) {
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const float2 f = __half22float2(h[t]);
+            o[2 * t] = f.x;
+            o[2 * t + 1] = f.y;
+        }
+    } else {
+        o[0] = __uint_as_float(u.x); o[1] = __uint_as_float(u.y);
+        o[2] = __uint_as_float(u.z); o[3] = __uint_as_float(u.w);
+    }
+}
+
+template <typename TI, typename TO, int NV>
+__global__ void __launch_bounds__(256) softmax_rows_kernel(const TI* __restrict__ x, TO* __restrict__ y,
+                                                           int64_t rows, int cols) {
+    constexpr int VEC = 16 / sizeof(TI);
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+    int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    uint4 cur[NV];
+    if (row < rows) load_row_vecs<TI, NV>(x + row * cols, cols, lane, cur);
+    for (; row < rows; row += nw) {
+        uint4 nxt[NV];
+        if (row + nw < rows) load_row_vecs<TI, NV>(x + (row + nw) * cols, cols, lane, nxt);
+        float v[NV * VEC];
+        float m = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int c0 = (j * 32 + lane) * VEC;
+            unpack_vec<TI>(cur[j], v + j * VEC);
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+                if (c0 >= cols) v[j * VEC + i] = -INFINITY;
+                m = fmaxf(m, v[j * VEC + i]);
+            }
+        }
+        m = warp_max(m);
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV * VEC; ++i) {
+            v[i] = (v[i] == -INFINITY) ? 0.f : exp_sfu(v[i] - m);
+            s += v[i];
+        }
+        s = warp_sum(s);
+        const float inv = 1.0f / s;
+        TO* yr = y + row * cols;
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int c0 = (j * 32 + lane) * VEC;
+            if (c0 < cols) {
+                float o[VEC];
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) o[i] = v[j * VEC + i] * inv;
+                stv<VEC>(yr + c0, o);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < NV; ++j) cur[j] = nxt[j];
+    }
+}
+
+template <typename T, typename TW, int NV>
+__global__ void __launch_bounds__(256)
+layer_norm_rows_kernel(const T* __restrict__ x, const TW* __restrict__ gamma, const TW* __restrict__ beta,
+                       T* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                       int64_t rows, int cols, float eps) {
+    constexpr int VEC = 16 / sizeof(T);
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+    int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+    uint4 cur[NV];
+    if (row < rows) load_row_vecs<T, NV>(x + row * cols, cols, lane, cur);
+    for (; row < rows; row += nw) {
+        uint4 nxt[NV];
+        if (row + nw < rows) load_row_vecs<T, NV>(x + (row + nw) * cols, cols, lane, nxt);
+        float v[NV * VEC];
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            unpack_vec<T>(cur[j], v + j * VEC);  // columns past the row load as 0
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) s += v[j * VEC + i];
+        }
+        const float mean = warp_sum(s) / cols;
+        float q = 0.f;
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int c0 = (j * 32 + lane) * VEC;
+#pragma unroll
+            for (int t = 0; t < VEC; ++t) {
+                const float d = (c0 < cols) ? v[j * VEC + t] - mean : 0.f;
+                q += d * d;
+            }
+        }
+        const float var = warp_sum(q) / cols;
+        const float rstd = rsqrtf(var + eps);
+        T* yr = y + row * cols;
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int c0 = (j * 32 + lane) * VEC;
+            if (c0 < cols) {
+                // gamma / beta: the same columns for every row, L1-resident
+                float o[VEC], g[VEC], b[VEC];
+                if (gamma) ldv<VEC>(gamma + c0, g);
+                if (beta) ldv<VEC>(beta + c0, b);
+#pragma unroll
+                for (int t = 0; t < VEC; ++t) {
+                    o[t] = (v[j * VEC + t] - mean) * rstd;
+                    if (gamma) o[t] = o[t] * g[t];
+                    if (beta) o[t] = o[t] + b[t];
+                }
+                stv<VEC>(yr + c0, o);
+            }
+        }
+        if (lane == 0) {
+            if (mean_out) mean_out[row] = mean;
+            if (rstd_out) rstd_out[row] = rstd;
+        }
+#pragma unroll
+        for (int j = 0; j < NV; ++j) cur[j] = nxt[j];
+    }
+}
+
+// Blocks of a persistent row kernel: every block resident at once (the
+// occupancy of the instantiation times the SM count), or fewer when there
+// are fewer rows than warps.
+template <auto Kernel>
+int64_t row_grid(int64_t rows) {
+    static std::once_flag once;
+    static int per_sm = 1;
+    std::call_once(once, [] {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, Kernel, 256, 0) == cudaSuccess && n > 0) per_sm = n;
+    });
+    const int64_t resident = static_cast<int64_t>(per_sm) * sm_count(current_device());
+    return std::max<int64_t>(1, std::min<int64_t>(resident, ceil_div(rows, 8)));
+}
+
 template <typename TI, typename TO>
 int softmax_launch(const void* x, void* y, int64_t rows, int64_t cols, cudaStream_t st) {
     const TI* xp = static_cast<const TI*>(x);
@@ -277,6 +448,15 @@ int softmax_launch(const void* x, void* y, int64_t rows, int64_t cols, cudaStrea
     constexpr int VEC = 16 / sizeof(TI);
     if (cols <= kRegCols && (cols % VEC) == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
         reinterpret_cast<uintptr_t>(y) % 16 == 0 && (cols * sizeof(TO)) % 16 == 0) {
+        const int nv = static_cast<int>(ceil_div(cols, 32 * VEC));
+#define TK_SOFTMAX_ROWS(NV)                                                                          \
+    if (nv == NV) {                                                                                   \
+        const unsigned rgrid = static_cast<unsigned>(row_grid<softmax_rows_kernel<TI, TO, NV>>(rows)); \
+        softmax_rows_kernel<TI, TO, NV><<<rgrid, 256, 0, st>>>(xp, yp, rows, (int)cols);             \
+        return launch_status("softmax");                                                              \
+    }
+        TK_SOFTMAX_ROWS(1) TK_SOFTMAX_ROWS(2) TK_SOFTMAX_ROWS(3) TK_SOFTMAX_ROWS(4)
+#undef TK_SOFTMAX_ROWS
         const int warps = 8;
         const unsigned grid = static_cast<unsigned>(ceil_div(rows, warps));
         const int per = static_cast<int>(round_up(static_cast<size_t>(ceil_div(cols, 32)), VEC));
@@ -304,6 +484,16 @@ int layer_norm_launch(const void* x, const void* g, const void* b, void* y, floa
     if (cols <= kRegCols && (cols % VEC) == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
         reinterpret_cast<uintptr_t>(y) % 16 == 0 && reinterpret_cast<uintptr_t>(g) % 16 == 0 &&
         reinterpret_cast<uintptr_t>(b) % 16 == 0) {
+        const int nv = static_cast<int>(ceil_div(cols, 32 * VEC));
+#define TK_LN_ROWS(NV)                                                                                \
+    if (nv == NV) {                                                                                   \
+        const unsigned rgrid = static_cast<unsigned>(row_grid<layer_norm_rows_kernel<T, TW, NV>>(rows)); \
+        layer_norm_rows_kernel<T, TW, NV><<<rgrid, 256, 0, st>>>(xp, gp, bp, yp, mean, rstd, rows,  \
+                                                                 (int)cols, eps);                    \
+        return launch_status("layer_norm");                                                           \
+    }
+        TK_LN_ROWS(1) TK_LN_ROWS(2) TK_LN_ROWS(3) TK_LN_ROWS(4)
+#undef TK_LN_ROWS
         const int warps = 8;
         const unsigned grid = static_cast<unsigned>(ceil_div(rows, warps));
         const int per = static_cast<int>(round_up(static_cast<size_t>(ceil_div(cols, 32)), VEC));
