@@ -189,30 +189,16 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.samples), "source": "NVML, 5 ms"}
 
 
-def device_delay(kunlun, us):
-    """A bounded device-side spin of `us` microseconds on the current kunlun
-    stream (torch's clock-cycle sleep kernel), enqueued outside the timed
-    events: the host then enqueues the next step while the GPU is still busy,
-    so a short step's time is not stretched by host launch latency."""
-    if us <= 0:
-        return
-    import torch
-    s = kunlun.current_stream()
-    ext = torch.cuda.ExternalStream(s.stream_id, device=torch.device("cuda", torch.cuda.current_device()))
-    with torch.cuda.stream(ext):
-        torch.cuda._sleep(int(us * 2000))  # ~2000 cycles per microsecond at the B200 boost clock
-
-
-def timed_steps(step, steps, warmup, flush, kunlun, gate_us=0):
+def timed_steps(step, steps, warmup, flush, kunlun):
     """Per-step device time with CUDA events on the launching stream; the L2
-    flush and the host-latency gate between steps are outside the events."""
+    flush between steps is outside the events (and, being ~80 us of device
+    work, lets the host enqueue the next step before the GPU reaches it)."""
     for _ in range(warmup):
         step()
         flush()
     kunlun.synchronize()
     times = []
     for _ in range(steps):
-        device_delay(kunlun, gate_us)
         e0 = kunlun.Event(enable_timing=True)
         e1 = kunlun.Event(enable_timing=True)
         e0.record()
@@ -225,19 +211,17 @@ def timed_steps(step, steps, warmup, flush, kunlun, gate_us=0):
 
 
 def make_flush(dev, kunlun):
-    """L2 flush between timed steps: a read of a 512 MiB buffer (four times
-    L2) on the launching stream, outside the events.  The step that follows
-    finds none of its data in L2, and the previous step's dirty lines have
-    been written back during the flush rather than inside the next step."""
+    """L2 flush between timed steps: the library's amax kernel reading a
+    512 MiB buffer (four times L2) on the launching stream, outside the
+    events.  The step that follows finds none of its data in L2, and the
+    previous step's dirty lines have been written back during the flush
+    rather than inside the next step."""
     import torch
-    idx = dev.index or 0
-    scratch = torch.ones(128 * 1024 * 1024, dtype=torch.float32, device=torch.device("cuda", idx))
+    from torch_kunlun_b200 import ops
+    scratch = torch.ones(256 * 1024 * 1024, dtype=torch.float16).to(dev)
 
     def flush():
-        s = kunlun.current_stream()
-        ext = torch.cuda.ExternalStream(s.stream_id, device=torch.device("cuda", idx))
-        with torch.cuda.stream(ext):
-            torch.sum(scratch)
+        ops.amax(scratch)
     return flush
 
 
@@ -296,7 +280,7 @@ class LimbGemm:
 
     def ms(self, kunlun, flush, iters=10, warmup=3):
         self.prepare(kunlun)
-        ts = timed_steps(lambda: self.launch(kunlun), iters, warmup, flush, kunlun, gate_us=200)
+        ts = timed_steps(lambda: self.launch(kunlun), iters, warmup, flush, kunlun)
         return sum(ts) / len(ts)
 
     def ops(self):
@@ -500,20 +484,22 @@ def tp_e2e(x_host_rows, wg, wu, wd, dev, kunlun, dist, world, mode, steps, warmu
     return ms, int(x_host_rows.nbytes), int(yh[0].nbytes)
 
 
-# Kernel launches of this library per MLP step (counted from the code path):
-# amax(x); gate and up: weight amax + both operands' quantise + GEMM, each;
-# silu_mul; amax(h); amax(down weight); down: quantise + GEMM per row block.
+# Kernel launches of this library per MLP step (counted from the code path of
+# tp.tp_mlp_forward): amax(x), quantise(x), amax and quantise of each of the
+# gate / up weights, their two GEMMs, the SiLU gate (with its amax), amax of
+# the down weight; then quantise(down weight) and, per row block of the down
+# projection, quantise + GEMM (plus the slot sum of the peer exchanges).
 def tp_launches(mode, world):
-    base = 1 + 3 + 3 + 1 + 1 + 1
-    if world == 1:
-        return base + 2
+    base = 10
+    if world == 1 or mode == "reduce_scatter":
+        return base + 3
     if mode == "allreduce":
-        return base + 4 * 2
+        return base + 1 + 4 * 2
     if mode == "peer":
-        return base + world * 2 + 1  # one GEMM per owner block, then the slot sum
+        return base + 1 + world * 2 + 1
     if mode == "peer_fused":
         return base + 2 + 1
-    return base + 2
+    return base + 3
 
 
 # ---- reference / CPU baseline: the oracle on a token sample ------------------------
@@ -607,7 +593,7 @@ def linear_object(dev, kunlun, flush, peaks, M, N, K, steps, warmup, with_e2e, c
 
     def step():
         torch.nn.functional.linear(xd, wd, bd)
-    ts = timed_steps(step, steps, warmup, flush, kunlun, gate_us=300)
+    ts = timed_steps(step, steps, warmup, flush, kunlun)
     ms = sum(ts) / len(ts)
     out = torch.empty(M, N, dtype=torch.float16, device=dev)
     gemm = LimbGemm(xd, wd, out)
@@ -717,7 +703,7 @@ def bert_object(dev, kunlun, flush, peaks, steps, warmup, cpu):
 
     def block():
         encoder.encoder_block(xd, wd, md, heads=BERT_HEADS, eps=1e-12)
-    ts = timed_steps(block, steps, warmup, flush, kunlun, gate_us=300)
+    ts = timed_steps(block, steps, warmup, flush, kunlun)
     ms = sum(ts) / len(ts)
     macs = encoder.encoder_block_macs(BERT_B, BERT_L, BERT_H, BERT_F)
     T, H, E = BERT_B * BERT_L, BERT_H, BERT_H // BERT_HEADS
@@ -748,13 +734,12 @@ def bert_object(dev, kunlun, flush, peaks, steps, warmup, cpu):
     acc = {n: 0.0 for n in names}
     reps = 5
     for i in range(reps + 2):
-        device_delay(kunlun, 300)
+        flush()  # cold L2, and ~80 us of device work that puts the host ahead
         ev = parts()
         kunlun.synchronize()
         if i >= 2:
             for j, n in enumerate(names):
                 acc[n] += ev[j].elapsed_time(ev[j + 1]) / reps
-        flush()
     total = sum(acc.values())
     lin_ops = {"qkv_linear": 2 * T * H * 3 * H, "out_linear_residual": 2 * T * H * H,
                "ffn1_linear_gelu": 2 * T * H * BERT_F, "ffn2_linear_residual": 2 * T * BERT_F * H}
@@ -839,7 +824,7 @@ def bmm_object(dev, kunlun, flush, peaks, steps=20, warmup=3):
             torch_kunlun.scaled_dot_product_attention(a, kt, v, scale=1.0)
 
         for label, fn in (("composed", composed), ("fused", fused)):
-            ts = timed_steps(fn, steps, warmup, flush, kunlun, gate_us=300)
+            ts = timed_steps(fn, steps, warmup, flush, kunlun)
             ms = sum(ts) / len(ts)
             tops = BMM_OPS / (ms / 1000) / 1e12
             out[f"{name}_{label}"] = {
@@ -884,7 +869,7 @@ def conv_object(dev, kunlun, flush, peaks, cpu, steps=20, warmup=3):
         def fn():
             F.conv2d(xd, wd, bd, padding=pad, groups=groups)
 
-        ts = timed_steps(fn, steps, warmup, flush, kunlun, gate_us=300)
+        ts = timed_steps(fn, steps, warmup, flush, kunlun)
         ms = sum(ts) / len(ts)
         OH = H + 2 * pad - k + 1
         ops = conv_ops(case)
@@ -963,7 +948,7 @@ def rowops_object(dev, kunlun, flush, peaks, steps=20, warmup=3):
             ("layer_norm_16384x768", lambda: torch.nn.functional.layer_norm(h, (768,), gamma, beta, 1e-12),
              4 * h.numel() + 4 * 768),
             ("quantise_cfg1_operands", quantise, 6 * (M1 * K1 + N1 * K1))):
-        ts = timed_steps(fn, steps, warmup, flush, kunlun, gate_us=300)
+        ts = timed_steps(fn, steps, warmup, flush, kunlun)
         ms = sum(ts) / len(ts)
         gbs = nbytes / (ms / 1000) / 1e9
         out[name] = {"ms": ms, "gbs": gbs, "algorithmic_bytes": nbytes,
@@ -986,9 +971,11 @@ def run_tp(args):
     torch.cuda.set_device(local_rank)
     dev = torch.device("kunlun", local_rank)
     if world > 1:
-        # the communicator's init log (ranks, devices, channels) stays visible
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        # the communicator's init log (ranks, devices, channels) stays visible,
+        # whatever level the environment preset
+        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
         dist.init_process_group("bkcl", timeout=datetime.timedelta(seconds=180))
     peaks = load_peaks()
     mode = args.reduce if world > 1 else "none"

@@ -370,6 +370,14 @@ TK_API int tk_unary(int op, tk_dtype_t dtype, const void* x, void* y, int64_t n,
 TK_API int tk_silu_mul(tk_dtype_t dtype, const void* gate, const void* up, void* y, int64_t n,
                        void* stream);
 
+/* tk_silu_mul that also writes amax_out[0] = max |y| (device fp32, NaN
+ * dominating): the per-tensor scale with which the reference's next fc
+ * quantises the gated activation (csrc/ops.cpp:224-227 with a null max
+ * pointer), without a second pass over y.  Replaces swish + mul
+ * (csrc/ops_extra.cpp:71, csrc/autograd.cpp:60-71) and that max-find. */
+TK_API int tk_silu_mul_amax(tk_dtype_t dtype, const void* gate, const void* up, void* y, int64_t n,
+                            float* amax_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

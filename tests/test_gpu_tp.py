@@ -7,6 +7,8 @@ the plain composition, and the last GEMM matches the oracle.  Two GPUs
 TP MLP all-reduce / reduce-scatter against each rank's own partial sums."""
 import socket
 
+import numpy as np
+
 import pytest
 import torch
 
@@ -54,6 +56,31 @@ def test_tp_mlp_world1_matches_composition_and_oracle():
     silu_ref = (g64 / (1 + torch.exp(-g64))).half().double() * u64
     assert torch.allclose(h.cpu().double(), silu_ref, atol=1e-3, rtol=2e-3)
     assert_bits_equal(y.cpu().numpy(), O.linear(h.cpu().numpy(), wd.cpu().numpy()), "down")
+
+
+def test_fused_silu_gate_amax_and_limb_gemms_equal_the_plain_ops():
+    """The TP step's building blocks: silu_mul_amax equals silu_mul then amax
+    (bit for bit, NaN-free); a GEMM on operands quantised once by
+    quantize_limbs equals linear_scaled with the same scales, also on a row
+    block written into a slice of a larger output."""
+    g, u = rnd((300, 520), 20), rnd((300, 520), 21)
+    gd, ud = g.to(DEV), u.to(DEV)
+    h, ah = ops.silu_mul_amax(gd, ud)
+    assert torch.equal(h.cpu().view(torch.int16), ops.silu_mul(gd, ud).cpu().view(torch.int16))
+    assert ah.cpu().item() == ops.amax(h).cpu().item()
+    gh, uh = rnd((301, 520), 22), rnd((301, 520), 23)  # odd count: the element-wise path
+    h2, ah2 = ops.silu_mul_amax(gh.to(DEV), uh.to(DEV))
+    assert ah2.cpu().item() == float(np.abs(h2.cpu().float().numpy()).max())
+    w = rnd((200, 520), 24, 0.02).to(DEV)
+    aw = ops.amax(w)
+    hl, wl = ops.quantize_limbs(h, ah), ops.quantize_limbs(w, aw)
+    got = ops.linear_from_limbs(hl, wl, 520, ah, aw)
+    want = ops.linear_scaled(h, w, amax_x=ah, amax_w=aw)
+    assert torch.equal(got.cpu().view(torch.int16), want.cpu().view(torch.int16))
+    out = torch.zeros(400, 200, dtype=torch.float16, device=DEV)
+    ops.linear_from_limbs(ops.quantize_limbs(h[100:250], ah), wl, 520, ah, aw, out=out[50:200])
+    assert torch.equal(out[50:200].cpu().view(torch.int16), want[100:250].cpu().view(torch.int16))
+    assert_bits_equal(got.cpu().numpy(), O.linear(h.cpu().numpy(), w.cpu().numpy()), "from limbs")
 
 
 def _port():

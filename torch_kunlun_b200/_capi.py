@@ -27,7 +27,7 @@ EXPORTED = [
     "tk_binary", "tk_unary", "tk_silu_mul", "tk_conv2d_workspace_size", "tk_conv2d_q16",
     "tk_softmax", "tk_layer_norm", "tk_qgemm_noalloc", "tk_sdpa_workspace_size", "tk_sdpa_q16",
     "tk_reduce_sum", "tk_conv3d_workspace_size", "tk_conv3d_q16", "tk_qgemm_scatter_rows",
-    "tk_conv3d_wgrad_workspace_size", "tk_conv3d_wgrad_q16",
+    "tk_conv3d_wgrad_workspace_size", "tk_conv3d_wgrad_q16", "tk_silu_mul_amax",
 ]
 
 

@@ -233,6 +233,58 @@ __global__ void silu_mul_kernel(const T* __restrict__ g, const T* __restrict__ u
     }
 }
 
+// The SiLU gate with the per-tensor amax of its output folded in: y as in
+// silu_mul_kernel, and the largest |y| (as the bit pattern of a non-negative
+// binary32, NaN canonicalised above every number, the order tk_amax uses)
+// combined into *amax_bits with one atomicMax per warp.  Eight elements per
+// thread with 16-byte accesses when `vec`.
+template <typename T> __device__ __forceinline__ void ld8f(const T* p, float (&v)[8]);
+template <typename T> __device__ __forceinline__ void st8f(T* p, const float (&v)[8]);
+
+template <typename T>
+__device__ __forceinline__ float silu_mul_one(float gv, float uv) {
+    T hr;  // silu output rounded to T, as the reference stores it
+    st<T>(&hr, 0, un_apply(TK_UN_SILU, gv, 0.f, 0.f));
+    T yr;
+    st<T>(&yr, 0, __fmul_rn(ld<T>(&hr, 0), uv));
+    return ld<T>(&yr, 0);
+}
+
+__device__ __forceinline__ unsigned abs_bits(float v) {
+    const unsigned b = __float_as_uint(v) & 0x7FFFFFFFu;
+    return b > 0x7F800000u ? 0x7FC00000u : b;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+silu_mul_amax_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ y, int64_t n,
+                     int vec, unsigned* __restrict__ amax_bits) {
+    unsigned m = 0;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (vec) {
+        for (int64_t v = t0; v < n / 8; v += stride) {
+            float gv[8], uv[8], out[8];
+            ld8f<T>(g + 8 * v, gv);
+            ld8f<T>(u + 8 * v, uv);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                out[k] = silu_mul_one<T>(gv[k], uv[k]);
+                m = max(m, abs_bits(out[k]));
+            }
+            st8f<T>(y + 8 * v, out);
+        }
+    } else {
+        for (int64_t i = t0; i < n; i += stride) {
+            const float o = silu_mul_one<T>(ld<T>(g, i), ld<T>(u, i));
+            st<T>(y, i, o);
+            m = max(m, abs_bits(o));
+        }
+    }
+    m = __reduce_max_sync(0xffffffffu, m);
+    if ((threadIdx.x & 31) == 0 && m != 0u) atomicMax(amax_bits, m);
+}
+
 int grid_for(int64_t n) {
     int64_t g = ceil_div(n, kThreads);
     const int64_t cap = static_cast<int64_t>(sm_count(current_device())) * 16;
@@ -616,6 +668,31 @@ int tk_unary(int op, tk_dtype_t dt, const void* x, void* y, int64_t n, float p0,
         unary_kernel<float><<<grid, kThreads, 0, stream>>>(op, static_cast<const float*>(x),
                                                             static_cast<float*>(y), n, p0, p1);
     return launch_status("unary");
+}
+
+int tk_silu_mul_amax(tk_dtype_t dt, const void* gate, const void* up, void* y, int64_t n, float* amax_out,
+                     void* stream_) {
+    using namespace tk;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    TK_CHECK_ARG(n >= 0, "tk_silu_mul_amax: negative size");
+    TK_CHECK_ARG(amax_out != nullptr, "tk_silu_mul_amax: amax_out is NULL");
+    TK_CHECK_ARG(dt == TK_DTYPE_F16 || dt == TK_DTYPE_F32, "tk_silu_mul_amax: bad dtype");
+    TK_CUDA_TRY(cudaMemsetAsync(amax_out, 0, sizeof(float), stream));
+    if (n == 0) return TK_OK;
+    TK_CHECK_ARG(gate && up && y, "tk_silu_mul_amax: NULL pointer");
+    const bool vec = n % 8 == 0 && reinterpret_cast<uintptr_t>(gate) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(up) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0;
+    const int grid = grid_for(vec ? n / 8 : n);
+    unsigned* bits = reinterpret_cast<unsigned*>(amax_out);
+    if (dt == TK_DTYPE_F16)
+        silu_mul_amax_kernel<__half><<<grid, kThreads, 0, stream>>>(
+            static_cast<const __half*>(gate), static_cast<const __half*>(up), static_cast<__half*>(y), n,
+            vec ? 1 : 0, bits);
+    else
+        silu_mul_amax_kernel<float><<<grid, kThreads, 0, stream>>>(
+            static_cast<const float*>(gate), static_cast<const float*>(up), static_cast<float*>(y), n,
+            vec ? 1 : 0, bits);
+    return launch_status("silu_mul_amax");
 }
 
 int tk_silu_mul(tk_dtype_t dt, const void* gate, const void* up, void* y, int64_t n, void* stream_) {

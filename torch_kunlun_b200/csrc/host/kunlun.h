@@ -99,6 +99,12 @@ at::Tensor linear_act(const at::Tensor& input, const at::Tensor& weight,
                       const std::optional<at::Tensor>& bias, int64_t act,
                       const std::optional<at::Tensor>& residual);
 at::Tensor silu_mul(const at::Tensor& gate, const at::Tensor& up);
+std::tuple<at::Tensor, at::Tensor> silu_mul_amax(const at::Tensor& gate, const at::Tensor& up);
+at::Tensor quantize_limbs(const at::Tensor& x, const at::Tensor& amax);
+at::Tensor linear_from_limbs(const at::Tensor& a_limbs, const at::Tensor& b_limbs, int64_t k,
+                             const at::Tensor& amax_a, const at::Tensor& amax_b,
+                             const std::optional<at::Tensor>& bias, int64_t act,
+                             const std::optional<at::Tensor>& out, at::ScalarType dtype);
 at::Tensor amax(const at::Tensor& x);
 at::Tensor linear_scaled(const at::Tensor& input, const at::Tensor& weight,
                          const std::optional<at::Tensor>& bias, int64_t act,

@@ -93,6 +93,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("linear_act", &linear_act, py::arg("input"), py::arg("weight"),
           py::arg("bias") = py::none(), py::arg("act") = 0, py::arg("residual") = py::none());
     m.def("silu_mul", &silu_mul);
+    m.def("silu_mul_amax", &silu_mul_amax);
+    m.def("quantize_limbs", &quantize_limbs);
+    m.def("linear_from_limbs", &linear_from_limbs, py::arg("a_limbs"), py::arg("b_limbs"), py::arg("k"),
+          py::arg("amax_a"), py::arg("amax_b"), py::arg("bias") = py::none(), py::arg("act") = 0,
+          py::arg("out") = py::none(), py::arg("dtype") = at::kHalf);
     m.def("amax", &amax);
     m.def("linear_scaled", &linear_scaled, py::arg("input"), py::arg("weight"),
           py::arg("bias") = py::none(), py::arg("act") = 0, py::arg("amax_x") = py::none(),

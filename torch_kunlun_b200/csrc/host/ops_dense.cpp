@@ -559,6 +559,85 @@ at::Tensor linear_scaled(const at::Tensor& input, const at::Tensor& weight,
     return out;
 }
 
+// Two int8 limb planes [2, rows, round_up(cols, 16)] of a 2-D tensor
+// quantised with a given per-tensor scale (1-element fp32 tensor): the form
+// in which an operand used by several GEMMs is quantised once.
+at::Tensor quantize_limbs(const at::Tensor& x_in, const at::Tensor& amax) {
+    TORCH_CHECK(x_in.dim() == 2, "kunlun quantize_limbs: a 2-D tensor");
+    TORCH_CHECK(x_in.device().type() == c10::DeviceType::PrivateUse1, "kunlun quantize_limbs: kunlun tensor");
+    TORCH_CHECK(amax.scalar_type() == at::kFloat && amax.numel() >= 1 && amax.device() == x_in.device(),
+                "kunlun quantize_limbs: the scale must be an fp32 kunlun tensor");
+    at::Tensor x = x_in.stride(1) == 1 ? x_in : x_in.contiguous();
+    const int64_t rows = x.size(0), cols = x.size(1);
+    const int64_t ld = (cols + 15) / 16 * 16;
+    at::Tensor out = at::empty({2, rows, ld}, x.options().dtype(at::kChar));
+    if (rows * ld == 0) return out;
+    const int dev = x.device().index();
+    DeviceScope g(dev);
+    check_tk(tk_quantize_limbs(tk_dtype(x.scalar_type()), x.data_ptr(), 1, rows, cols, 0, x.stride(0), 1,
+                               amax.data_ptr<float>(), 0, out.data_ptr<int8_t>(), current_stream(dev)),
+             "tk_quantize_limbs");
+    return out;
+}
+
+// act(q(a) q(b)^T dequantised + bias) for operands quantised beforehand by
+// quantize_limbs with the scales amax_a / amax_b (K <= 32768); out an
+// optional row-major [M, N] block of `dtype`.
+at::Tensor linear_from_limbs(const at::Tensor& a_limbs, const at::Tensor& b_limbs, int64_t k,
+                             const at::Tensor& amax_a, const at::Tensor& amax_b,
+                             const std::optional<at::Tensor>& bias, int64_t act,
+                             const std::optional<at::Tensor>& out_opt, at::ScalarType dtype) {
+    const int64_t ld = (k + 15) / 16 * 16;
+    TORCH_CHECK(a_limbs.dim() == 3 && b_limbs.dim() == 3 && a_limbs.size(0) == 2 && b_limbs.size(0) == 2 &&
+                    a_limbs.size(2) == ld && b_limbs.size(2) == ld && a_limbs.is_contiguous() &&
+                    b_limbs.is_contiguous() && a_limbs.scalar_type() == at::kChar &&
+                    b_limbs.scalar_type() == at::kChar,
+                "kunlun linear_from_limbs: limbs must be contiguous int8 [2, rows, round_up(k, 16)]");
+    TORCH_CHECK(a_limbs.device() == b_limbs.device() && amax_a.device() == a_limbs.device() &&
+                    amax_b.device() == a_limbs.device() && amax_a.scalar_type() == at::kFloat &&
+                    amax_b.scalar_type() == at::kFloat,
+                "kunlun linear_from_limbs: operands and fp32 scales on one kunlun device");
+    TORCH_CHECK(dtype == at::kHalf || dtype == at::kFloat, "kunlun linear_from_limbs: fp16 or fp32 output");
+    const int64_t M = a_limbs.size(1), N = b_limbs.size(1);
+    at::Tensor out;
+    if (out_opt.has_value() && out_opt->defined()) {
+        out = *out_opt;
+        TORCH_CHECK(out.dim() == 2 && out.size(0) == M && out.size(1) == N && out.stride(1) == 1 &&
+                        out.scalar_type() == dtype && out.device() == a_limbs.device(),
+                    "kunlun linear_from_limbs: out must be a row-major [M, N] block of the output dtype");
+    } else {
+        out = at::empty({M, N}, a_limbs.options().dtype(dtype));
+    }
+    if (out.numel() == 0) return out;
+    TORCH_CHECK(k > 0, "kunlun linear_from_limbs: K must be positive");
+    tk_qgemm_desc_t d = {};
+    d.dtype = dtype == at::kHalf ? TK_DTYPE_F16 : TK_DTYPE_F32;
+    d.batch = 1;
+    d.m = M;
+    d.n = N;
+    d.k = k;
+    d.out = out.data_ptr();
+    d.out_sb = M * out.stride(0);
+    d.out_sm = out.stride(0);
+    at::Tensor b;
+    if (bias.has_value() && bias->defined()) {
+        b = bias->contiguous();
+        TORCH_CHECK(b.numel() == N && b.scalar_type() == dtype && b.device() == out.device(),
+                    "kunlun linear_from_limbs: bias [N] of the output dtype");
+        d.bias = b.data_ptr();
+    }
+    d.alpha = 1.0f;
+    d.beta = 0.0f;
+    d.act = static_cast<tk_act_t>(act);
+    d.per_slice_scales = 1;
+    const int dev = out.device().index();
+    DeviceScope g(dev);
+    check_tk(tk_qgemm_from_limbs(&d, a_limbs.data_ptr<int8_t>(), b_limbs.data_ptr<int8_t>(),
+                                 amax_a.data_ptr<float>(), amax_b.data_ptr<float>(), current_stream(dev)),
+             "tk_qgemm_from_limbs");
+    return out;
+}
+
 namespace {
 
 at::Tensor linear_fwd(const at::Tensor& input, const at::Tensor& weight,

@@ -324,6 +324,22 @@ at::Tensor silu_mul(const at::Tensor& gate, const at::Tensor& up) {
     return out;
 }
 
+// (T(silu(gate)) * up, max |result| as a 1-element fp32 tensor) in one pass:
+// the gate of a SiLU-gated MLP and the scale the next quantised GEMM takes.
+std::tuple<at::Tensor, at::Tensor> silu_mul_amax(const at::Tensor& gate, const at::Tensor& up) {
+    TORCH_CHECK(gate.sizes().equals(up.sizes()) && gate.scalar_type() == up.scalar_type(),
+                "kunlun silu_mul_amax: shape/dtype mismatch");
+    at::Tensor g = gate.contiguous(), u = up.contiguous();
+    at::Tensor out = at::empty(g.sizes(), g.options());
+    at::Tensor amax = at::empty({1}, g.options().dtype(at::kFloat));
+    const int dev = g.device().index();
+    DeviceScope s(dev);
+    check_tk(tk_silu_mul_amax(tk_dtype(g.scalar_type()), g.data_ptr(), u.data_ptr(), out.data_ptr(), g.numel(),
+                              amax.data_ptr<float>(), current_stream(dev)),
+             "tk_silu_mul_amax");
+    return {out, amax};
+}
+
 }  // namespace torch_kunlun
 
 TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {

@@ -46,4 +46,27 @@ def linear_scaled(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Te
     return _C.linear_scaled(x, weight, bias, ACT[act], amax_x, amax_w, out)
 
 
-__all__ = ["linear", "silu_mul", "amax", "linear_scaled", "ACT"]
+def silu_mul_amax(gate: torch.Tensor, up: torch.Tensor):
+    """(T(silu(gate)) * up, its max |value| as a 1-element fp32 tensor) in
+    one pass: the gated activation and the scale the next GEMM quantises it
+    with."""
+    return _C.silu_mul_amax(gate, up)
+
+
+def quantize_limbs(x: torch.Tensor, amax: torch.Tensor) -> torch.Tensor:
+    """The int16 codes of a 2-D tensor under a given per-tensor scale, as two
+    int8 limb planes [2, rows, round_up(cols, 16)] (hi signed, lo unsigned):
+    an operand several GEMMs share is quantised once."""
+    return _C.quantize_limbs(x, amax)
+
+
+def linear_from_limbs(a_limbs: torch.Tensor, b_limbs: torch.Tensor, k: int, amax_a: torch.Tensor,
+                      amax_b: torch.Tensor, bias: Optional[torch.Tensor] = None, act: str = "none",
+                      out: Optional[torch.Tensor] = None, dtype: torch.dtype = torch.float16) -> torch.Tensor:
+    """act(a b^T + bias) on operands from quantize_limbs: the values of
+    linear_scaled(a, b, amax_x=amax_a, amax_w=amax_b) (K <= 32768)."""
+    return _C.linear_from_limbs(a_limbs, b_limbs, k, amax_a, amax_b, bias, ACT[act], out, dtype)
+
+
+__all__ = ["linear", "silu_mul", "silu_mul_amax", "amax", "linear_scaled", "quantize_limbs",
+           "linear_from_limbs", "ACT"]

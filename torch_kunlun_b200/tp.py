@@ -7,7 +7,10 @@ the intermediate activation with no communication, multiplies it by its row
 shard of the down weight and produces a full-size partial sum; the partials
 are summed by an all-reduce (or reduce-scattered by rows).  Every rank
 quantises its own shards with their own per-tensor scales, as separate
-per-rank linear calls of the reference would.
+per-rank linear calls of the reference would.  Each operand is quantised
+once per step: x once for both the gate and the up GEMM (one scale, so the
+same codes), the down weight once for all of its row blocks, and the gated
+activation's scale comes out of the SiLU gate's own pass.
 
 Reductions of the partial sums:
 
@@ -87,6 +90,7 @@ class PeerRowExchange:
 
     def forward_fused(self, h: torch.Tensor, w: torch.Tensor, ah: torch.Tensor,
                       aw: torch.Tensor) -> torch.Tensor:
+        """h [T, F/P] with its scale ah, the whole row-parallel weight w [H, F/P]."""
         b = self._next
         self._next ^= 1
         _C.linear_scatter_rows(h, w, ah, aw, self.dests[b], self.rows)
@@ -94,8 +98,10 @@ class PeerRowExchange:
         dist.all_reduce(self.flag, group=self.group)
         return _C.sum_slots(self.local[b])
 
-    def forward(self, h: torch.Tensor, w: torch.Tensor, ah: torch.Tensor, aw: torch.Tensor,
+    def forward(self, h: torch.Tensor, wl: torch.Tensor, ah: torch.Tensor, aw: torch.Tensor,
                 copy_stream: Optional[kunlun.Stream] = None) -> torch.Tensor:
+        """h [T, F/P] with its scale ah; wl the down weight's limbs
+        (quantize_limbs with aw), shared by every row block."""
         b = self._next
         self._next ^= 1
         R, P, me = self.rows, self.world, self.rank
@@ -107,14 +113,15 @@ class PeerRowExchange:
         es = self._stage[0].element_size()
         for i in range(1, P + 1):
             q = (me + i) % P
-            rows = h[q * R:(q + 1) * R]
+            rows = _C.quantize_limbs(h[q * R:(q + 1) * R], ah)
+            k = h.shape[1]
             if q == me:
-                _C.linear_scaled(rows, w, None, 0, ah, aw, self.local[b][me])
+                _C.linear_from_limbs(rows, wl, k, ah, aw, None, 0, self.local[b][me], h.dtype)
                 break
             s = i % 2
             if self._stage_free[s] is not None:
                 compute.wait_event(self._stage_free[s])
-            _C.linear_scaled(rows, w, None, 0, ah, aw, self._stage[s])
+            _C.linear_from_limbs(rows, wl, k, ah, aw, None, 0, self._stage[s], h.dtype)
             done = kunlun.Event(device=h.device)
             done.record(compute)
             with kunlun.stream(copy):
@@ -173,38 +180,46 @@ def tp_mlp_forward(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
     [T/P, H] for ``reduce="reduce_scatter"``.
     """
     T, H = x.shape
-    ax = _C.amax(x)  # x is quantised once, with one scale, for both gate and up
-    gate = _C.linear_scaled(x, w_gate, None, 0, ax, None)
-    up = _C.linear_scaled(x, w_up, None, 0, ax, None)
-    h = ops.silu_mul(gate, up)
+    dt = x.dtype
+    # x: one scale and one quantisation for both column-parallel GEMMs
+    ax = _C.amax(x)
+    xl = _C.quantize_limbs(x, ax)
+    awg, awu = _C.amax(w_gate), _C.amax(w_up)
+    gate = _C.linear_from_limbs(xl, _C.quantize_limbs(w_gate, awg), H, ax, awg, None, 0, None, dt)
+    up = _C.linear_from_limbs(xl, _C.quantize_limbs(w_up, awu), H, ax, awu, None, 0, None, dt)
+    del xl
+    h, ah = _C.silu_mul_amax(gate, up)  # the gate and its per-tensor scale, one pass
     del gate, up
-    ah, aw = _C.amax(h), _C.amax(w_down)
+    Fl = h.shape[1]
+    aw = _C.amax(w_down)
     world = _world(group)
-    if world == 1:
-        return _C.linear_scaled(h, w_down, None, 0, ah, aw)
-    if reduce in ("peer", "peer_fused"):
+    if reduce == "peer_fused" and world > 1:
         if T % world:
             raise ValueError("peer reduction needs T divisible by the world size")
-        ex = peer_exchange(T // world, H, x.dtype, x.device, group)
-        if reduce == "peer_fused":
-            return ex.forward_fused(h, w_down, ah, aw)
-        return ex.forward(h, w_down, ah, aw, comm_stream)
+        return peer_exchange(T // world, H, dt, x.device, group).forward_fused(h, w_down, ah, aw)
+    wl = _C.quantize_limbs(w_down, aw)  # once, for every row block of h
+    if world == 1:
+        return _C.linear_from_limbs(_C.quantize_limbs(h, ah), wl, Fl, ah, aw, None, 0, None, dt)
+    if reduce == "peer":
+        if T % world:
+            raise ValueError("peer reduction needs T divisible by the world size")
+        return peer_exchange(T // world, H, dt, x.device, group).forward(h, wl, ah, aw, comm_stream)
     if reduce == "reduce_scatter":
         if T % world:
             raise ValueError("reduce_scatter needs T divisible by the world size")
-        partial = _C.linear_scaled(h, w_down, None, 0, ah, aw)
-        out = torch.empty(T // world, H, dtype=x.dtype, device=x.device)
+        partial = _C.linear_from_limbs(_C.quantize_limbs(h, ah), wl, Fl, ah, aw, None, 0, None, dt)
+        out = torch.empty(T // world, H, dtype=dt, device=x.device)
         dist.reduce_scatter_tensor(out, partial, group=group)
         return out
     if reduce != "allreduce":
         raise ValueError(f"unknown reduce mode {reduce!r}")
-    out = torch.empty(T, H, dtype=x.dtype, device=x.device)
+    out = torch.empty(T, H, dtype=dt, device=x.device)
     comm = comm_stream if comm_stream is not None else kunlun.Stream(x.device)
     compute = kunlun.current_stream(x.device)
     chunks = max(1, min(chunks, T))
     bounds = [(i * T // chunks, (i + 1) * T // chunks) for i in range(chunks)]
     for r0, r1 in bounds:
-        _C.linear_scaled(h[r0:r1], w_down, None, 0, ah, aw, out[r0:r1])
+        _C.linear_from_limbs(_C.quantize_limbs(h[r0:r1], ah), wl, Fl, ah, aw, None, 0, out[r0:r1], dt)
         ready = kunlun.Event(device=x.device)
         ready.record(compute)
         with kunlun.stream(comm):
