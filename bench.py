@@ -5,7 +5,11 @@ SiLU-gated MLP of BASELINE's multi-GPU config -- x fp16 [16384, 8192] ~N(0,1),
 gate/up weights [28672, 8192] split by output rows (column-parallel), down
 weight [8192, 28672] split by input columns (row-parallel), all ~N(0,0.02);
 h = T(silu(x Wg^T)) * (x Wu^T), y = sum over ranks of h_r Wd_r^T, the partial
-sums reduce-scattered through the `bkcl` ProcessGroup (NCCL over NVLink).
+sums reduce-scattered by rows: by default over peer memory (each finished
+row block of the down projection copied by copy engines into its owner's
+buffer over NVLink while the next block computes, then summed in rank order
+in fp32 with one rounding), with the `bkcl` (NCCL) reduce-scatter and
+all-reduce measured beside it.
 Every linear is the int16-quantised GEMM; each rank quantises its own shards.
 A step is one forward of the whole MLP over the 16384 tokens.  Metric:
 aggregate int16 TOPS = 3 * 2 * 16384 * 8192 * 28672 / step time (strong
@@ -1212,7 +1216,7 @@ def main():
     ap.add_argument("--impl", default="kunlun", choices=["kunlun", "reference"])
     ap.add_argument("--workload", default="tp_mlp",
                     choices=["tp_mlp", "linear", "linear4096", "bert", "conv", "bmm", "rowops"])
-    ap.add_argument("--reduce", default="reduce_scatter",
+    ap.add_argument("--reduce", default="peer",
                     choices=["allreduce", "reduce_scatter", "peer", "peer_fused"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the single-GPU objects on the N=1 line")

@@ -22,7 +22,8 @@ Reductions of the partial sums:
 - ``"peer"``: receive buffers shared through CUDA IPC; the down projection
   runs one row block (one owner's rows) at a time, starting with the next
   rank's rows, and each finished block is copied into slot r of its owner's
-  buffer by a copy engine over NVLink while the next block computes; the
+  buffer by copy engines over NVLink (four pieces on four streams, so
+  several engines share a block) while the next block computes; the
   owner's own block is computed last, straight into its slot.  After a
   one-element all-reduce as a barrier each rank sums its slots in rank order
   in fp32 and rounds once.  Returns this rank's rows, like
@@ -106,39 +107,49 @@ class PeerRowExchange:
         self._next ^= 1
         R, P, me = self.rows, self.world, self.rank
         compute = kunlun.current_stream(h.device)
-        copy = copy_stream if copy_stream is not None else self._copy_stream(h.device)
+        copies = self._copy_streams(h.device, copy_stream)
         if not hasattr(self, "_stage"):
             self._stage = [torch.empty(R, self.cols, dtype=self.dtype, device=h.device) for _ in range(2)]
             self._stage_free = [None, None]
         es = self._stage[0].element_size()
+        k = h.shape[1]
+        pieces = len(copies)
+        row_bytes = self.cols * es
         for i in range(1, P + 1):
             q = (me + i) % P
             rows = _C.quantize_limbs(h[q * R:(q + 1) * R], ah)
-            k = h.shape[1]
             if q == me:
                 _C.linear_from_limbs(rows, wl, k, ah, aw, None, 0, self.local[b][me], h.dtype)
                 break
             s = i % 2
             if self._stage_free[s] is not None:
-                compute.wait_event(self._stage_free[s])
+                for ev in self._stage_free[s]:
+                    compute.wait_event(ev)
             _C.linear_from_limbs(rows, wl, k, ah, aw, None, 0, self._stage[s], h.dtype)
             done = kunlun.Event(device=h.device)
             done.record(compute)
-            with kunlun.stream(copy):
-                copy.wait_event(done)
-                _C.copy_bytes(self.dests[b][q], self._stage[s].data_ptr(), R * self.cols * es)
-                freed = kunlun.Event(device=h.device)
-                freed.record(copy)
+            freed = []
+            for j, cs in enumerate(copies):
+                r0, r1 = j * R // pieces, (j + 1) * R // pieces
+                with kunlun.stream(cs):
+                    cs.wait_event(done)
+                    _C.copy_bytes(self.dests[b][q] + r0 * row_bytes, self._stage[s].data_ptr() + r0 * row_bytes,
+                                  (r1 - r0) * row_bytes)
+                    ev = kunlun.Event(device=h.device)
+                    ev.record(cs)
+                    freed.append(ev)
             self._stage_free[s] = freed
-        compute.wait_stream(copy)
+        for cs in copies:
+            compute.wait_stream(cs)
         # stream-ordered barrier: every rank's blocks have landed in their slots
         dist.all_reduce(self.flag, group=self.group)
         return _C.sum_slots(self.local[b])
 
-    def _copy_stream(self, device):
-        if not hasattr(self, "_copy"):
-            self._copy = kunlun.Stream(device)
-        return self._copy
+    def _copy_streams(self, device, first=None):
+        if not hasattr(self, "_copies"):
+            self._copies = [first if first is not None else kunlun.Stream(device)] + \
+                [kunlun.Stream(device) for _ in range(3)]
+        return self._copies
 
     def close(self):
         kunlun.synchronize()
