@@ -146,6 +146,35 @@ def test_fused_equals_composed_path():
     assert (fused - composed).abs().max().item() < 2e-2
 
 
+@pytest.mark.parametrize("E,causal,masked", [(64, False, True), (128, False, False), (64, True, False),
+                                             (40, False, True)])
+def test_cluster_kernel_equals_two_kernel_path(E, causal, masked):
+    """Slices of at most 512 queries and keys (fp16) run in one cluster kernel
+    that keeps the scores in shared memory; longer slices run the statistics
+    and output kernels through HBM.  The two are bit-identical: appending
+    copies of query rows 0..127 (and their mask rows) to a 512-query slice
+    sends it down the two-kernel path without changing the slice's amax of q
+    or its largest probability (a copied row has the same probabilities; with
+    a causal mask row 0 already has P = 1), so rows 0..511 must agree bit for
+    bit."""
+    B, H, L, S = 2, 3, 512, 448
+    q, k, v = rnd((B, H, L, E), 21), rnd((B, H, S, E), 22), rnd((B, H, S, E), 23)
+    q2 = torch.cat([q, q[:, :, :128]], dim=2)
+    mask = mask2 = None
+    if masked:
+        mask = (torch.randn(B, 1, L, S, generator=torch.Generator().manual_seed(24)) * 2).half()
+        mask[..., S - 64:] = -1e4
+        mask2 = torch.cat([mask, mask[:, :, :128]], dim=2)
+    one = kunlun.scaled_dot_product_attention(q.to(DEV), k.to(DEV), v.to(DEV),
+                                              attn_mask=None if mask is None else mask.to(DEV),
+                                              is_causal=causal).cpu()
+    two = kunlun.scaled_dot_product_attention(q2.to(DEV), k.to(DEV), v.to(DEV),
+                                              attn_mask=None if mask2 is None else mask2.to(DEV),
+                                              is_causal=causal).cpu()
+    assert torch.equal(one.view(torch.int16), two[:, :, :L].contiguous().view(torch.int16))
+    check(one, oracle_sdpa(q, k, v, mask=mask, causal=causal))
+
+
 def test_fused_reads_strided_head_views():
     """Head-split views of a packed [B, L, 3, H, E] projection give the same
     result as contiguous copies, and the output's heads merge with a view."""

@@ -67,6 +67,7 @@ constexpr int NUM_SOFT_WARPS = 16;                  // four per TMEM lane quarte
 constexpr int NUM_THREADS = 64 + 32 * NUM_SOFT_WARPS;
 constexpr int SUBS = NUM_SOFT_WARPS / 4;             // warps sharing a lane quarter
 constexpr int CW = 64 / SUBS;                        // key (or value) columns per warp
+static_assert(CW == 16, "p_codes16_h and the score chunk layout take 16 keys per warp");
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t COL_S = 0;        // S: HH, MID, LL at +0, +64, +128
 constexpr uint32_t COL_O = 256;      // O: HH, MID, LL at +256, +320, +384
@@ -147,6 +148,41 @@ __device__ __forceinline__ float exp_fast(float x) {
     return y;
 }
 
+// The exact integer 65536*hh + 256*mid + ll of a score's limb accumulators
+// as binary64, for head dims up to 128: the hi limbs lie in [-128, 127] and
+// the lo limbs in [0, 255], so over at most 128 products |256*mid + ll| <
+// 2^31 and the sum fits int32.  The two int32 values become binary64 through
+// their bit patterns (2^52 + 2^31 + x has x + 2^31 in its low word) and one
+// exact fused multiply-add joins them -- fp64-pipe work instead of 64-bit
+// integer shifts and adds.
+__device__ __forceinline__ double score_acc_to_double(uint32_t hh, uint32_t mid, uint32_t ll) {
+    const int32_t t = static_cast<int32_t>(mid) * 256 + static_cast<int32_t>(ll);
+    const double dh = __hiloint2double(0x43300000, static_cast<int>(hh ^ 0x80000000u)) - 4503601774854144.0;
+    const double dt = __hiloint2double(0x43300000, static_cast<int>(static_cast<uint32_t>(t) ^ 0x80000000u)) -
+                      4503601774854144.0;
+    return __fma_rn(dh, 65536.0, dt);
+}
+
+// Probability codes of 16 consecutive fp16 scores of one row: P =
+// T(exp(s - m) * inv) rounded to binary16 in pairs, then quantised with the
+// slice scale inv_p (P <= max P, so quant_code_bits gives quant_one's code);
+// hi and lo limb bytes packed four to a word.
+__device__ __forceinline__ void p_codes16_h(const float (&s)[16], float m, float inv, float inv_p,
+                                            uint32_t (&hw)[4], uint32_t (&lw)[4]) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        uint32_t r[4];
+#pragma unroll
+        for (int k = 0; k < 4; k += 2) {
+            const float2 pr = __half22float2(__floats2half2_rn(exp_fast(s[4 * w + k] - m) * inv,
+                                                               exp_fast(s[4 * w + k + 1] - m) * inv));
+            r[k] = quant_code_bits(pr.x, inv_p);
+            r[k + 1] = quant_code_bits(pr.y, inv_p);
+        }
+        pack_codes4(r[0], r[1], r[2], r[3], hw[w], lw[w]);
+    }
+}
+
 // N consecutive scores j0..j0+N-1 of query row i in the reference
 // composition: the exact limb dot product, T(acc * s_qk), T(. * scale), the
 // causal -1e4 and the additive mask, each rounded to T; padding keys
@@ -158,7 +194,7 @@ __device__ __forceinline__ void scores_n(const uint32_t (&hh)[N], const uint32_t
                                          int64_t i, int64_t j0, const void* mask_row, float (&s)[N]) {
 #pragma unroll
     for (int c = 0; c < N; ++c)
-        s[c] = round_t_from_double(__dmul_rn(limb_acc_to_double(hh[c], mid[c], ll[c]), sqk), DT);
+        s[c] = round_t_from_double(__dmul_rn(score_acc_to_double(hh[c], mid[c], ll[c]), sqk), DT);
     if (p.scale != 1.0f) {
 #pragma unroll
         for (int c = 0; c < N; ++c) s[c] = round_t(__fmul_rn(s[c], p.scale), DT);
@@ -221,12 +257,13 @@ __device__ __forceinline__ void scores_n(const uint32_t (&hh)[N], const uint32_t
 template <int N>
 __device__ __forceinline__ void scores_h(const uint32_t (&hh)[N], const uint32_t (&mid)[N],
                                          const uint32_t (&ll)[N], double sqk, const AttnParams& p,
-                                         int64_t i, int64_t j0, const void* mask_row, __half2 (&sh)[N / 2]) {
+                                         int64_t i, int64_t j0, const void* mask_row, __half2 (&sh)[N / 2],
+                                         const uint4* mask_pre = nullptr) {
 #pragma unroll
     for (int j = 0; j < N / 2; ++j)
         sh[j] = __halves2half2(
-            __double2half(__dmul_rn(limb_acc_to_double(hh[2 * j], mid[2 * j], ll[2 * j]), sqk)),
-            __double2half(__dmul_rn(limb_acc_to_double(hh[2 * j + 1], mid[2 * j + 1], ll[2 * j + 1]), sqk)));
+            __double2half(__dmul_rn(score_acc_to_double(hh[2 * j], mid[2 * j], ll[2 * j]), sqk)),
+            __double2half(__dmul_rn(score_acc_to_double(hh[2 * j + 1], mid[2 * j + 1], ll[2 * j + 1]), sqk)));
     if (p.scale != 1.0f) {
         if (p.scale_h) {
             const __half2 sc = __float2half2_rn(p.scale);
@@ -255,7 +292,7 @@ __device__ __forceinline__ void scores_h(const uint32_t (&hh)[N], const uint32_t
             const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __half*>(mask_row) + j0);
 #pragma unroll
             for (int k = 0; k < N / 8; ++k) {
-                const uint4 u = __ldg(src + k);
+                const uint4 u = mask_pre != nullptr ? mask_pre[k] : __ldg(src + k);
                 const __half2* m2 = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) sh[4 * k + e] = __hadd2(sh[4 * k + e], m2[e]);
@@ -793,13 +830,17 @@ attn_out_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__
                 // limb in [0, 127].
                 // (pr <= max P, so quant_code_bits gives quant_one's code)
                 uint32_t hw[CW / 4], lw[CW / 4];
+                if constexpr (DT == 0) {
+                    p_codes16_h(s, m_i, inv_i, inv_p, hw, lw);
+                } else {
 #pragma unroll
-                for (int w = 0; w < CW / 4; ++w) {
-                    uint32_t r[4];
+                    for (int w = 0; w < CW / 4; ++w) {
+                        uint32_t r[4];
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        r[k] = quant_code_bits(round_t(exp_fast(s[4 * w + k] - m_i) * inv_i, DT), inv_p);
-                    pack_codes4(r[0], r[1], r[2], r[3], hw[w], lw[w]);
+                        for (int k = 0; k < 4; ++k)
+                            r[k] = quant_code_bits(round_t(exp_fast(s[4 * w + k] - m_i) * inv_i, DT), inv_p);
+                        pack_codes4(r[0], r[1], r[2], r[3], hw[w], lw[w]);
+                    }
                 }
                 const uint32_t buf = n_p & 1u;
                 if (!mbar_wait_bounded(smem_u32(p_empty + buf), ((n_p >> 1) & 1u) ^ 1u, abort_flag,
@@ -861,6 +902,490 @@ attn_out_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__
         tc_fence_after();
         tmem_dealloc(tmem_base, TMEM_COLS);
     }
+}
+
+// ---- fused kernel: scores resident in shared memory, one cluster per slice ----
+//
+// For fp16 slices with head dim <= 128 and at most 512 queries and keys, a
+// cluster of ceil(L / 128) CTAs handles a (batch, head) slice, one CTA per
+// 128 query rows; the clusters are persistent and walk the slices with a
+// stride of the grid's cluster count.  Phase A computes S = Q K^T tile by
+// tile on the tensor cores, forms the exact fp16 scores on the CUDA cores
+// (scores_h) and keeps them in this CTA's shared memory (up to 128 KB) with
+// an online row max and sum of exponentials.  The slice's largest
+// probability (the scale of the reference's second bmm) is combined across
+// the cluster through distributed shared memory while the scores turn into
+// the binary16 probabilities in place.  Phase B converts each probability
+// tile in place into the swizzled limb tile of the quantised P and runs P V
+// on the tensor cores; the epilogue dequantises O.  The TMA and MMA warps
+// run ahead into the next slice (its Q, K tiles and first S tile) while the
+// CUDA-core warps finish the current one.  The scores are computed once and
+// never reach HBM; the arithmetic (every rounding, the same exponential) is
+// that of the statistics and output kernels above, so the results are
+// identical.
+constexpr int FUSED_MAX_KT = 8;  // keys <= 512
+
+template <int G>
+struct FusedSmem {
+    static constexpr int RSTAGES = G == 1 ? 8 : 3;
+    static constexpr int RING_STAGE = G * K_CHUNK;  // a K tile, later a V^T tile (64 x 128 B)
+    static_assert(RING_STAGE >= V_TILE, "K and V^T tiles share the ring");
+    static constexpr int OFF_Q = 0;
+    static constexpr int OFF_RING = OFF_Q + G * Q_CHUNK;
+    static constexpr int OFF_S = OFF_RING + RSTAGES * RING_STAGE;     // key tile t at + t * P_TILE
+    static constexpr int OFF_RED = OFF_S + FUSED_MAX_KT * P_TILE;     // float [SUBS][2][BM]
+    static constexpr int OFF_BAR = OFF_RED + SUBS * 2 * BM * 4;
+    // q_full, q_empty, stage_full[], stage_empty[], s_full, s_empty, comb,
+    // stats, cl[2], p_ready[8], o_full, o_empty, drain
+    static constexpr int NUM_BARS = 2 + 2 * RSTAGES + 2 + 2 + 2 + FUSED_MAX_KT + 3;
+    // tmem slot, abort flag, cta max[2], slots[2][4]
+    static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+    static constexpr int ALLOC = OFF_MISC + 64 + 1024;
+    static_assert(ALLOC <= 232448, "shared memory budget");
+    static_assert(OFF_S % 1024 == 0, "128-byte swizzled tiles on 1024-byte boundaries");
+};
+
+template <int G>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+    using L = FusedSmem<G>;
+    constexpr int STAGES = L::RSTAGES;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+    uint64_t* q_full = bars;
+    uint64_t* q_empty = bars + 1;             // Q read by the slice's last S MMA
+    uint64_t* stage_full = bars + 2;
+    uint64_t* stage_empty = stage_full + STAGES;
+    uint64_t* s_full = stage_empty + STAGES;  // S tile in TMEM computed
+    uint64_t* s_empty = s_full + 1;           // S tile read (16 warps)
+    uint64_t* comb = s_full + 2;              // every warp's partial row statistics published (16 warps)
+    uint64_t* stats = s_full + 3;             // this CTA's max probability formed (4 warps)
+    uint64_t* cl_bar = s_full + 4;            // [2] the cluster's max probabilities gathered (CL arrivals)
+    uint64_t* p_ready = s_full + 6;           // [FUSED_MAX_KT] P tile t written (16 warps)
+    uint64_t* o_full = p_ready + FUSED_MAX_KT;
+    uint64_t* o_empty = o_full + 1;
+    uint64_t* drain_bar = o_full + 2;
+    uint32_t* misc = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+    uint32_t* tmem_slot = misc;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
+    unsigned* cta_max = misc + 2;             // [2] by slice parity
+    volatile unsigned* slots = misc + 4;      // [2][4] max probability of each CTA, by slice parity
+    float* red = reinterpret_cast<float*>(smem + L::OFF_RED);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int CL = p.m_tiles;
+    const uint32_t crank = cluster_ctarank();
+    const int mt = static_cast<int>(crank);
+    const int n_cl = static_cast<int>(gridDim.x) / CL;
+    const int cid = static_cast<int>(blockIdx.x) / CL;
+    const int BH = p.B * p.H;
+    const int n_slices = cid < BH ? (BH - cid + n_cl - 1) / n_cl : 0;
+    const int n_kt = p.n_kt;
+
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(q_full), 1);
+        mbar_init(smem_u32(q_empty), 1);
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(stage_full + s), 1);
+            mbar_init(smem_u32(stage_empty + s), 1);
+        }
+        mbar_init(smem_u32(s_full), 1);
+        mbar_init(smem_u32(s_empty), NUM_SOFT_WARPS);
+        mbar_init(smem_u32(comb), NUM_SOFT_WARPS);
+        mbar_init(smem_u32(stats), 4);
+        mbar_init(smem_u32(cl_bar), static_cast<uint32_t>(CL));
+        mbar_init(smem_u32(cl_bar + 1), static_cast<uint32_t>(CL));
+        for (int t = 0; t < FUSED_MAX_KT; ++t) mbar_init(smem_u32(p_ready + t), NUM_SOFT_WARPS);
+        mbar_init(smem_u32(o_full), 1);
+        mbar_init(smem_u32(o_empty), NUM_SOFT_WARPS);
+        mbar_init(smem_u32(drain_bar), 1);
+        *abort_flag = 0;
+        cta_max[0] = 0u;
+        cta_max[1] = 0u;
+        for (int r = 0; r < 8; ++r) slots[r] = 0u;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // every CTA of the cluster has initialised its barriers before any remote arrival
+    cluster_sync_all();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer: per slice Q, K tiles, V^T tiles ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t last_phase[STAGES];
+        bool used[STAGES];
+        for (int s = 0; s < STAGES; ++s) { used[s] = false; last_phase[s] = 0; }
+        int q_loads = 0;
+        bool ok = true;
+        for (int it = 0; it < n_slices && ok; ++it) {
+            const int bh = cid + it * n_cl;
+            if (!mbar_wait_bounded(smem_u32(q_empty), (static_cast<uint32_t>(it) & 1u) ^ 1u, abort_flag, p.err,
+                                   kDevErrWaitEmpty))
+                break;
+            if (lane == 0) {
+                mbar_arrive_expect_tx(smem_u32(q_full), G * Q_CHUNK);
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                    tma_load_3d(smem_u32(smem + L::OFF_Q + g * Q_CHUNK), &tmQ, smem_u32(q_full), g * 128, mt * BM, bh);
+            }
+            __syncwarp();
+            ++q_loads;
+            const int total = n_kt + p.ev_tiles * n_kt;
+            for (int j = 0; j < total; ++j) {
+                if (!mbar_wait_bounded(smem_u32(stage_empty + stage), phase ^ 1u, abort_flag, p.err,
+                                       kDevErrWaitEmpty)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t fb = smem_u32(stage_full + stage);
+                    const uint32_t dst = smem_u32(smem + L::OFF_RING + stage * L::RING_STAGE);
+                    if (j < n_kt) {
+                        mbar_arrive_expect_tx(fb, G * K_CHUNK);
+#pragma unroll
+                        for (int g = 0; g < G; ++g) tma_load_3d(dst + g * K_CHUNK, &tmK, fb, g * 128, j * BKEY, bh);
+                    } else {
+                        const int v = j - n_kt;
+                        mbar_arrive_expect_tx(fb, V_TILE);
+                        tma_load_3d(dst, &tmV, fb, (v % n_kt) * 128, (v / n_kt) * EVT, bh);
+                    }
+                }
+                __syncwarp();
+                used[stage] = true;
+                last_phase[stage] = phase;
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+        }
+        volatile int no_abort = 0;
+        for (int s = 0; s < STAGES; ++s)
+            if (used[s])
+                mbar_wait_bounded(smem_u32(stage_full + s), last_phase[s], &no_abort, p.err, kDevErrWaitDrain);
+        if (q_loads > 0)
+            mbar_wait_bounded(smem_u32(q_full), static_cast<uint32_t>(q_loads - 1) & 1u, &no_abort, p.err,
+                              kDevErrWaitDrain);
+    } else if (warp == 1) {
+        // ---------------- MMA issuer: per slice S = Q K^T, then O += P V ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t n_s = 0, n_o = 0;
+        bool ok = true;
+        const uint32_t s_hh = tmem_base + COL_S, s_mid = s_hh + 64, s_ll = s_hh + 128;
+        const uint32_t o_hh = tmem_base + COL_O, o_mid = o_hh + 64, o_ll = o_hh + 128;
+        const uint32_t q_base = smem_u32(smem + L::OFF_Q);
+        for (int it = 0; it < n_slices && ok; ++it) {
+            if (!mbar_wait_bounded(smem_u32(q_full), static_cast<uint32_t>(it) & 1u, abort_flag, p.err,
+                                   kDevErrWaitFull))
+                break;
+            for (int t = 0; t < n_kt; ++t) {
+                // the S columns are single-buffered: the CUDA-core warps release
+                // them right after their TMEM loads, before the scores' arithmetic
+                if (!mbar_wait_bounded(smem_u32(stage_full + stage), phase, abort_flag, p.err, kDevErrWaitFull) ||
+                    !mbar_wait_bounded(smem_u32(s_empty), (n_s & 1u) ^ 1u, abort_flag, p.err, kDevErrWaitAccEmpty)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t kb = smem_u32(smem + L::OFF_RING + stage * L::RING_STAGE);
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        const uint64_t q0 = smem_desc_kmajor_sw128(q_base + g * Q_CHUNK);
+                        const uint64_t b0 = smem_desc_kmajor_sw128(kb + g * K_CHUNK);
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const uint64_t hi = static_cast<uint64_t>((u * 32) >> 4);
+                            const uint64_t lo = static_cast<uint64_t>((64 + u * 32) >> 4);
+                            const uint32_t acc = (g > 0 || u > 0) ? 1u : 0u;
+                            tc_mma_i8(s_hh, q0 + hi, b0 + hi, IDESC_SS, acc);
+                            tc_mma_i8(s_mid, q0 + hi, b0 + lo, IDESC_SU, acc);
+                            tc_mma_i8(s_mid, q0 + lo, b0 + hi, IDESC_US, 1u);
+                            tc_mma_i8(s_ll, q0 + lo, b0 + lo, IDESC_UU, acc);
+                        }
+                    }
+                    tc_commit(smem_u32(s_full));
+                    tc_commit(smem_u32(stage_empty + stage));
+                    if (t == n_kt - 1) tc_commit(smem_u32(q_empty));
+                }
+                __syncwarp();
+                ++n_s;
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+            for (int evh = 0; evh < p.ev_tiles && ok; ++evh) {
+                if (!mbar_wait_bounded(smem_u32(o_empty), (n_o & 1u) ^ 1u, abort_flag, p.err, kDevErrWaitAccEmpty)) {
+                    ok = false;
+                    break;
+                }
+                for (int t = 0; t < n_kt; ++t) {
+                    if (!mbar_wait_bounded(smem_u32(p_ready + t), static_cast<uint32_t>(it) & 1u, abort_flag, p.err,
+                                           kDevErrWaitFull) ||
+                        !mbar_wait_bounded(smem_u32(stage_full + stage), phase, abort_flag, p.err, kDevErrWaitFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint64_t a0 = smem_desc_kmajor_sw128(smem_u32(smem + L::OFF_S + t * P_TILE));
+                        const uint64_t b0 =
+                            smem_desc_kmajor_sw128(smem_u32(smem + L::OFF_RING + stage * L::RING_STAGE));
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const uint64_t hi = static_cast<uint64_t>((u * 32) >> 4);
+                            const uint64_t lo = static_cast<uint64_t>((64 + u * 32) >> 4);
+                            const uint32_t acc = (t > 0 || u > 0) ? 1u : 0u;
+                            tc_mma_i8(o_hh, a0 + hi, b0 + hi, IDESC_SS, acc);
+                            tc_mma_i8(o_mid, a0 + hi, b0 + lo, IDESC_SU, acc);
+                            tc_mma_i8(o_mid, a0 + lo, b0 + hi, IDESC_US, 1u);
+                            tc_mma_i8(o_ll, a0 + lo, b0 + lo, IDESC_UU, acc);
+                        }
+                        tc_commit(smem_u32(stage_empty + stage));
+                        if (t == n_kt - 1) tc_commit(smem_u32(o_full));
+                    }
+                    __syncwarp();
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+                ++n_o;
+            }
+        }
+        if (lane == 0) tc_commit(smem_u32(drain_bar));
+        __syncwarp();
+        volatile int no_abort = 0;
+        mbar_wait_bounded(smem_u32(drain_bar), 0, &no_abort, p.err, kDevErrWaitDrain);
+    } else {
+        // ---------------- scores, statistics, P and the output (warps 2..17) ----------------
+        const int quarter = warp & 3;
+        const int sub = (warp - 2) >> 2;
+        const int row = quarter * 32 + lane;
+        const int sw = row & 7;
+        const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        const int64_t i = static_cast<int64_t>(mt) * BM + row;
+        const bool row_ok = i < p.L;
+        uint8_t* line0 = smem + L::OFF_S + row * 128;
+        uint32_t n_s = 0, n_o = 0;
+        bool ok = true;
+        for (int it = 0; it < n_slices && ok; ++it) {
+            const int bh = cid + it * n_cl;
+            const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+            const int par = it & 1;
+            const double sqk = dequant_scale(__ldg(p.amax + bh), __ldg(p.amax + BH + bh));
+            const void* mask_row = nullptr;
+            if (p.mask != nullptr && row_ok)
+                mask_row = static_cast<const char*>(p.mask) + (b * p.ms[0] + h * p.ms[1] + i * p.ms[2]) * 2;
+            float m_run = -INFINITY, l_run = 0.0f;
+            for (int t = 0; t < n_kt; ++t) {
+                const int64_t j0 = static_cast<int64_t>(t) * BKEY + CW * sub;
+                // this tile's mask values are loaded before the wait for S
+                uint4 mpre[CW / 8];
+                const bool pre = mask_row != nullptr && p.mask_vec && j0 + CW <= p.S;
+                if (pre) {
+                    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __half*>(mask_row) + j0);
+#pragma unroll
+                    for (int k = 0; k < CW / 8; ++k) mpre[k] = __ldg(src + k);
+                }
+                if (!mbar_wait_bounded(smem_u32(s_full), n_s & 1u, abort_flag, p.err, kDevErrWaitAccFull)) {
+                    ok = false;
+                    break;
+                }
+                ++n_s;
+                tc_fence_after();
+                uint32_t hh[CW], mid[CW], ll[CW];
+                const uint32_t col = COL_S + CW * sub;
+                tmem_ld_cw(t_lane + col, hh);
+                tmem_ld_cw(t_lane + col + 64, mid);
+                tmem_ld_cw(t_lane + col + 128, ll);
+                tc_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(s_empty));
+                __half2 sh[CW / 2];
+                scores_h<CW>(hh, mid, ll, sqk, p, i, j0, mask_row, sh, pre ? mpre : nullptr);
+                // keys j0..j0+7 go to 16-byte chunk sub of the row's line, keys
+                // j0+8..j0+15 to chunk 4 + sub: the chunks that later hold this
+                // warp's hi and lo limbs of P, so each warp converts its own bytes
+                uint8_t* line = line0 + t * P_TILE;
+                const uint4* src = reinterpret_cast<const uint4*>(sh);
+                *reinterpret_cast<uint4*>(line + ((sub ^ sw) << 4)) = src[0];
+                *reinterpret_cast<uint4*>(line + (((4 + sub) ^ sw) << 4)) = src[1];
+                float s[CW];
+#pragma unroll
+                for (int j = 0; j < CW / 2; ++j) {
+                    const float2 f = __half22float2(sh[j]);
+                    s[2 * j] = f.x;
+                    s[2 * j + 1] = f.y;
+                }
+                float tmax = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < CW; ++c) tmax = fmaxf(tmax, s[c]);
+                const float m_new = fmaxf(m_run, tmax);
+                if (m_new != -INFINITY) {
+                    if (m_run != -INFINITY && m_new != m_run) l_run *= exp_fast(m_run - m_new);
+                    m_run = m_new;
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int c = 0; c < CW; ++c) acc += exp_fast(s[c] - m_run);
+                    l_run += acc;
+                }
+            }
+            if (!ok) break;
+            // Every warp publishes its partial (m, l); each warp then combines
+            // the four partials of its rows in the statistics kernel's order
+            // (key quarter 0 first), so all four warps of a row hold the same
+            // m and 1/l.  red is rewritten only in the next slice, after every
+            // warp has passed this slice's P tiles.
+            red[(sub * 2) * BM + row] = m_run;
+            red[(sub * 2 + 1) * BM + row] = l_run;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(comb));
+            if (!mbar_wait_bounded(smem_u32(comb), static_cast<uint32_t>(par), abort_flag, p.err, kDevErrWaitFull)) {
+                ok = false;
+                break;
+            }
+            const float m0 = red[row], l0 = red[BM + row];
+            float m_i = m0;
+#pragma unroll
+            for (int q = 1; q < SUBS; ++q) m_i = fmaxf(m_i, red[(q * 2) * BM + row]);
+            float l = 0.0f;
+            if (m0 != -INFINITY) l += l0 * exp_fast(m0 - m_i);
+#pragma unroll
+            for (int q = 1; q < SUBS; ++q) {
+                const float mq = red[(q * 2) * BM + row], lq = red[(q * 2 + 1) * BM + row];
+                if (mq != -INFINITY) l += lq * exp_fast(mq - m_i);
+            }
+            const float inv_i = 1.0f / l;
+            if (sub == 0) {
+                // the row's largest probability, T(exp(0) / l)
+                unsigned bits = 0;
+                if (row_ok && m_i != -INFINITY) bits = __float_as_uint(round_t(exp_fast(0.0f) * inv_i, 0));
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, o));
+                if (lane == 0) {
+                    if (bits != 0u) atomicMax(cta_max + par, bits);
+                    mbar_arrive(smem_u32(stats));
+                }
+            }
+            // One thread exchanges this CTA's largest probability with the
+            // cluster: slots and barriers alternate with the slice's parity, so
+            // a CTA that runs a slice ahead never touches what a slower one reads.
+            if (warp == 2 && lane == 0) {
+                mbar_wait_bounded(smem_u32(stats), static_cast<uint32_t>(par), abort_flag, p.err, kDevErrWaitFull);
+                const unsigned v = *reinterpret_cast<volatile unsigned*>(cta_max + par);
+                *reinterpret_cast<volatile unsigned*>(cta_max + par) = 0u;  // for the slice after next
+                const uint32_t slot_addr = smem_u32(const_cast<unsigned*>(slots) + par * 4 + crank);
+                const uint32_t bar_addr = smem_u32(cl_bar + par);
+                for (int r = 0; r < CL; ++r) {
+                    if (r == static_cast<int>(crank)) continue;
+                    st_shared_cluster_u32(mapa_shared(slot_addr, static_cast<uint32_t>(r)), v);
+                    mbar_arrive_remote(mapa_shared(bar_addr, static_cast<uint32_t>(r)));
+                }
+                slots[par * 4 + crank] = v;
+                mbar_arrive(bar_addr);
+            }
+            // While the cluster exchanges, P = T(exp(s - m) / l) replaces the
+            // scores in place (binary16, as the reference's softmax output)
+            for (int t = 0; t < n_kt; ++t) {
+                uint4* c0 = reinterpret_cast<uint4*>(line0 + t * P_TILE + ((sub ^ sw) << 4));
+                uint4* c1 = reinterpret_cast<uint4*>(line0 + t * P_TILE + (((4 + sub) ^ sw) << 4));
+                uint4 c[2] = {*c0, *c1};
+                __half2* hv = reinterpret_cast<__half2*>(c);
+#pragma unroll
+                for (int e = 0; e < CW / 2; ++e) {
+                    const float2 f = __half22float2(hv[e]);
+                    hv[e] = __floats2half2_rn(exp_fast(f.x - m_i) * inv_i, exp_fast(f.y - m_i) * inv_i);
+                }
+                *c0 = c[0];
+                *c1 = c[1];
+            }
+            // barrier par completes for the (it >> 1)-th time in this slice
+            if (!mbar_wait_bounded_cluster(smem_u32(cl_bar + par), (static_cast<uint32_t>(it) >> 1) & 1u, abort_flag,
+                                           p.err, kDevErrWaitCluster)) {
+                ok = false;
+                break;
+            }
+            unsigned pm = 0;
+            for (int r = 0; r < CL; ++r) pm = max(pm, slots[par * 4 + r]);
+            const float pmax = __uint_as_float(pm);
+            // rows past L quantise to 0
+            const float inv_p = row_ok ? quant_inv(pmax) : 0.0f;
+            // each P tile becomes its quantised limb tile in place: the warp's
+            // 16 keys' hi limbs in chunk sub, lo limbs in chunk 4 + sub (P <=
+            // max P, so quant_code_bits gives quant_one's code)
+            for (int t = 0; t < n_kt; ++t) {
+                uint4* c0 = reinterpret_cast<uint4*>(line0 + t * P_TILE + ((sub ^ sw) << 4));
+                uint4* c1 = reinterpret_cast<uint4*>(line0 + t * P_TILE + (((4 + sub) ^ sw) << 4));
+                uint4 c[2] = {*c0, *c1};
+                const __half2* hv = reinterpret_cast<const __half2*>(c);
+                uint32_t hw[CW / 4], lw[CW / 4];
+#pragma unroll
+                for (int w = 0; w < CW / 4; ++w) {
+                    const float2 a = __half22float2(hv[2 * w]), b2 = __half22float2(hv[2 * w + 1]);
+                    pack_codes4(quant_code_bits(a.x, inv_p), quant_code_bits(a.y, inv_p),
+                                quant_code_bits(b2.x, inv_p), quant_code_bits(b2.y, inv_p), hw[w], lw[w]);
+                }
+                *c0 = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                *c1 = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(p_ready + t));
+            }
+            // output tiles of 64 value columns
+            for (int evh = 0; evh < p.ev_tiles; ++evh) {
+                if (!mbar_wait_bounded(smem_u32(o_full), n_o & 1u, abort_flag, p.err, kDevErrWaitAccFull)) {
+                    ok = false;
+                    break;
+                }
+                ++n_o;
+                tc_fence_after();
+                uint32_t hh[CW], mid[CW], ll[CW];
+                const uint32_t col = COL_O + CW * sub;
+                tmem_ld_cw(t_lane + col, hh);
+                tmem_ld_cw(t_lane + col + 64, mid);
+                tmem_ld_cw(t_lane + col + 128, ll);
+                tc_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(o_empty));
+                if (row_ok) {
+                    const double spv = dequant_scale(pmax, __ldg(p.amax + 2 * BH + bh));
+                    const int64_t e0 = static_cast<int64_t>(evh) * EVT + CW * sub;
+                    const int64_t obase = b * p.os[0] + h * p.os[1] + i * p.os[2];
+                    float o[CW];
+#pragma unroll
+                    for (int c = 0; c < CW; ++c)
+                        o[c] = round_t_from_double(__dmul_rn(limb_acc_to_double(hh[c], mid[c], ll[c]), spv), 0);
+                    if (p.out_vec && e0 + CW <= p.Ev) {
+                        store_row_n<0, CW>(static_cast<char*>(p.out) + (obase + e0) * 2, o);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < CW; ++c)
+                            if (e0 + c < p.Ev) store_t(p.out, 0, obase + (e0 + c) * p.os[3], o[c]);
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+    // no CTA leaves while another CTA of the cluster may still write to it
+    cluster_sync_all();
 }
 
 // ---- quantisation of q, k, v into limb rows ---------------------------------
@@ -1047,6 +1572,13 @@ struct Layout {
     size_t off_amax, off_amax_p, off_max, off_inv, off_q, off_k, off_v, off_s, total;
 };
 
+// Slices the fused kernel takes: fp16, head dim <= 128, at most 512 queries
+// and keys (the scores of 128 queries fit in shared memory, the slice's CTAs
+// in one portable cluster).
+bool fused_ok(const tk_sdpa_desc_t& d) {
+    return d.dtype == TK_DTYPE_F16 && d.e <= 128 && d.l <= BM * 4 && d.s <= BKEY * FUSED_MAX_KT;
+}
+
 Layout layout_of(const tk_sdpa_desc_t& d) {
     Layout l;
     l.G = static_cast<int>(ceil_div(d.e, 64));
@@ -1068,7 +1600,7 @@ Layout layout_of(const tk_sdpa_desc_t& d) {
     l.off_q = take(static_cast<size_t>(l.BH * d.l * l.ldq));
     l.off_k = take(static_cast<size_t>(l.BH * d.s * l.ldq));
     l.off_v = take(static_cast<size_t>(l.BH * d.ev * l.ldv));
-    l.off_s = take(static_cast<size_t>(l.BH * d.l * l.Spad) * es);
+    l.off_s = take(fused_ok(d) ? 0 : static_cast<size_t>(l.BH * d.l * l.Spad) * es);
     l.total = o + 1024;  // base alignment slack
     return l;
 }
@@ -1136,6 +1668,62 @@ int run_attention(const CUtensorMap& tq, const CUtensorMap& tk_, const CUtensorM
     if (rc) return rc;
     attn_out_kernel<DT><<<std::min(p.tiles, sms), NUM_THREADS, OutSmem<DT>::ALLOC, stream>>>(ts, tv, p);
     return launch_status("attention output");
+}
+
+// Clusters of `cl` CTAs of the fused kernel that fit on device `dev` at
+// once (one CTA per SM), queried once per (device, cluster size).
+template <int G>
+int max_fused_clusters(int cl, int dev) {
+    static std::once_flag once[64][5];
+    static int count[64][5];
+    const int slot = std::min(dev, 63);
+    std::call_once(once[slot][cl], [&] {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(cl * 1024));
+        cfg.blockDim = dim3(NUM_THREADS);
+        cfg.dynamicSmemBytes = FusedSmem<G>::ALLOC;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = static_cast<unsigned>(cl);
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, attn_fused_kernel<G>, &cfg) != cudaSuccess || n <= 0) {
+            (void)cudaGetLastError();
+            n = std::max(1, sm_count(dev) / cl);
+        }
+        count[slot][cl] = n;
+    });
+    return count[slot][cl];
+}
+
+template <int G>
+int run_fused(const CUtensorMap& tq, const CUtensorMap& tk_, const CUtensorMap& tv, AttnParams p,
+              int ev_tiles, int dev, cudaStream_t stream) {
+    using L = FusedSmem<G>;
+    p.ev_tiles = ev_tiles;
+    p.tiles = p.B * p.H * p.m_tiles;
+    int rc = set_smem<attn_fused_kernel<G>>(L::ALLOC, dev);
+    if (rc) return rc;
+    // persistent clusters: as many as fit on the device at once
+    const int n_cl = std::min(p.B * p.H, max_fused_clusters<G>(p.m_tiles, dev));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(n_cl * p.m_tiles));
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = L::ALLOC;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(p.m_tiles);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_fused_kernel<G>, tq, tk_, tv, p);
+    if (e != cudaSuccess) TK_FAIL(TK_ERR_CUDA, "fused attention launch: %s", cudaGetErrorString(e));
+    return launch_status("fused attention");
 }
 
 // Innermost stride 1 and every other stride and the base 16-byte aligned, so
@@ -1209,7 +1797,8 @@ int tk_sdpa_q16(const tk_sdpa_desc_t* desc, void* workspace, size_t workspace_by
     rc = make_map(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + l.off_q, l.ldq, d.l, l.BH, 128, BM);
     if (!rc) rc = make_map(&tk_, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + l.off_k, l.ldq, d.s, l.BH, 128, BKEY);
     if (!rc) rc = make_map(&tv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + l.off_v, l.ldv, d.ev, l.BH, 128, EVT);
-    if (!rc)
+    const bool fused = fused_ok(d);
+    if (!rc && !fused)
         rc = make_map(&ts, stype, es, ws + l.off_s, l.Spad, d.l, l.BH, static_cast<uint32_t>(128 / es), BM);
     if (rc) return rc;
 
@@ -1241,6 +1830,8 @@ int tk_sdpa_q16(const tk_sdpa_desc_t* desc, void* workspace, size_t workspace_by
     p.err = device_error_word(dev);
     const int ev_tiles = static_cast<int>(ceil_div(d.ev, EVT));
     TK_CHECK_ARG(l.BH * p.m_tiles * ev_tiles < (1LL << 31), "tk_sdpa_q16: too many tiles");
+    if (fused) return l.G == 1 ? run_fused<1>(tq, tk_, tv, p, ev_tiles, dev, stream)
+                               : run_fused<2>(tq, tk_, tv, p, ev_tiles, dev, stream);
     if (l.G == 1)
         return d.dtype == TK_DTYPE_F16 ? run_attention<1, 0>(tq, tk_, ts, tv, p, ev_tiles, dev, stream)
                                        : run_attention<1, 1>(tq, tk_, ts, tv, p, ev_tiles, dev, stream);

@@ -421,7 +421,7 @@ depthwise_rows_kernel(const T* __restrict__ x, const T* __restrict__ w, const T*
 }
 
 // Planes per block of depthwise_rows_kernel for this geometry (0: the
-// kernel does not apply): about one output row per thread, within the
+// kernel does not apply): at most one output row per thread, within the
 // shared-memory spans.
 int depthwise_rows_ppb(const ConvGeom& g) {
     if (!(g.D == 1 && g.KD == 1 && g.groups == g.C && g.groups > 1 && g.F == g.C)) return 0;
@@ -430,7 +430,8 @@ int depthwise_rows_ppb(const ConvGeom& g) {
     const int64_t phw = (g.H + 2 * g.ph) * (g.W + 2 * g.pw);
     const int64_t taps = g.KH * g.KW;
     if (phw > kDwRowSpan || taps > kDwRowTaps || g.OW > 4096) return 0;
-    int64_t ppb = std::max<int64_t>(1, ceil_div(kDwRowThreads, g.OH));
+    // whole planes whose output rows fit one round of the block's threads
+    int64_t ppb = std::max<int64_t>(1, kDwRowThreads / g.OH);
     ppb = std::min(ppb, kDwRowSpan / phw);
     ppb = std::min(ppb, kDwRowTaps / taps);
     return static_cast<int>(std::max<int64_t>(ppb, 1));

@@ -20,6 +20,7 @@ enum DeviceError : unsigned {
     kDevErrWaitAccFull = 3,   // epilogue waited too long for the accumulator
     kDevErrWaitAccEmpty = 4,  // MMA warp waited too long for the epilogue
     kDevErrWaitDrain = 5,     // teardown drain timed out
+    kDevErrWaitCluster = 6,   // waited too long for another CTA of the cluster
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -84,6 +85,71 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
 #pragma unroll 1
         for (int i = 0; i < 64; ++i) {
             if (mbar_try_wait(bar, parity)) return true;
+        }
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (err != nullptr) atomicCAS(err, 0u, code);
+            *abort_flag = 1;
+            __threadfence_block();
+            return false;
+        }
+    }
+}
+
+// ---- thread-block clusters ----------------------------------------------------
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Every thread of every CTA of the cluster arrives, then waits for all.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The shared::cluster address of this CTA's shared-memory location `addr`
+// in the CTA of cluster rank `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+// Arrive (release at cluster scope) on an mbarrier of another CTA of the
+// cluster, given its shared::cluster address.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// mbar_wait_bounded for a barrier that other CTAs of the cluster arrive on
+// (acquire at cluster scope): returns false on timeout or abort.
+__device__ __forceinline__ bool mbar_wait_bounded_cluster(uint32_t bar, uint32_t parity,
+                                                          volatile int* abort_flag, unsigned* err,
+                                                          unsigned code) {
+    const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+    while (true) {
+#pragma unroll 1
+        for (int i = 0; i < 64; ++i) {
+            if (mbar_try_wait_cluster(bar, parity)) return true;
         }
         if (*abort_flag) return false;
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
