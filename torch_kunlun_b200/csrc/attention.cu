@@ -916,58 +916,82 @@ attn_out_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__
 // probability (the scale of the reference's second bmm) is combined across
 // the cluster through distributed shared memory while the scores turn into
 // the binary16 probabilities in place.  Phase B converts each probability
-// tile in place into the swizzled limb tile of the quantised P and runs P V
-// on the tensor cores; the epilogue dequantises O.  The TMA and MMA warps
-// run ahead into the next slice (its Q, K tiles and first S tile) while the
-// CUDA-core warps finish the current one.  The scores are computed once and
-// never reach HBM; the arithmetic (every rounding, the same exponential) is
-// that of the statistics and output kernels above, so the results are
-// identical.
-constexpr int FUSED_MAX_KT = 8;  // keys <= 512
+// tile in place into the swizzled limb tile of the quantised P, and P V runs
+// on the tensor cores while the CUDA-core warps already compute the next
+// slice's scores; they dequantise O afterwards.  K and V^T tiles come
+// through separate rings from two TMA warps, and S and P V are issued by two
+// MMA warps, so the next slice's S tiles never queue behind this slice's P V.
+// The scores are computed once and never reach HBM; the arithmetic (every
+// rounding, the same exponential) is that of the statistics and output
+// kernels above, so the results are identical.
+constexpr int FUSED_MAX_KT = 8;                        // keys <= 512
+constexpr int FUSED_THREADS = 128 + 32 * NUM_SOFT_WARPS;  // 4 role warps + 16 CUDA-core warps
 
 template <int G>
 struct FusedSmem {
-    static constexpr int RSTAGES = G == 1 ? 8 : 3;
-    static constexpr int RING_STAGE = G * K_CHUNK;  // a K tile, later a V^T tile (64 x 128 B)
-    static_assert(RING_STAGE >= V_TILE, "K and V^T tiles share the ring");
+    static constexpr int KSTAGES = G == 1 ? 4 : 2;    // K tiles of G * 8 KB
+    static constexpr int VSTAGES = G == 1 ? 4 : 2;    // V^T tiles of 8 KB
     static constexpr int OFF_Q = 0;
-    static constexpr int OFF_RING = OFF_Q + G * Q_CHUNK;
-    static constexpr int OFF_S = OFF_RING + RSTAGES * RING_STAGE;     // key tile t at + t * P_TILE
+    static constexpr int OFF_K = OFF_Q + G * Q_CHUNK;
+    static constexpr int OFF_V = OFF_K + KSTAGES * G * K_CHUNK;
+    static constexpr int OFF_S = OFF_V + VSTAGES * V_TILE;            // key tile t at + t * P_TILE
     static constexpr int OFF_RED = OFF_S + FUSED_MAX_KT * P_TILE;     // float [SUBS][2][BM]
     static constexpr int OFF_BAR = OFF_RED + SUBS * 2 * BM * 4;
-    // q_full, q_empty, stage_full[], stage_empty[], s_full, s_empty, comb,
-    // stats, cl[2], p_ready[8], o_full, o_empty, drain
-    static constexpr int NUM_BARS = 2 + 2 * RSTAGES + 2 + 2 + 2 + FUSED_MAX_KT + 3;
+    // q_full, q_empty, k_full[], k_empty[], v_full[], v_empty[], s_full,
+    // s_empty, comb, stats, cl[2], p_ready[8], p_free[8], o_full, o_empty,
+    // drain_s, drain_o
+    static constexpr int NUM_BARS = 2 + 2 * KSTAGES + 2 * VSTAGES + 6 + 2 * FUSED_MAX_KT + 4;
     // tmem slot, abort flag, cta max[2], slots[2][4]
     static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
     static constexpr int ALLOC = OFF_MISC + 64 + 1024;
     static_assert(ALLOC <= 232448, "shared memory budget");
-    static_assert(OFF_S % 1024 == 0, "128-byte swizzled tiles on 1024-byte boundaries");
+    static_assert(OFF_S % 1024 == 0 && OFF_K % 1024 == 0 && OFF_V % 1024 == 0,
+                  "128-byte swizzled tiles on 1024-byte boundaries");
 };
 
+// The largest probability of this CTA's rows, exchanged with the other CTAs
+// of the cluster: slot crank of every CTA's slot array for the slice's
+// parity, then an arrival on every CTA's barrier of that parity.
+__device__ __forceinline__ void cluster_publish_max(unsigned v, int par, uint32_t crank, int cl,
+                                                    volatile unsigned* slots, uint64_t* cl_bar) {
+    const uint32_t slot_addr = smem_u32(const_cast<unsigned*>(slots) + par * 4 + crank);
+    const uint32_t bar_addr = smem_u32(cl_bar + par);
+    for (int r = 0; r < cl; ++r) {
+        if (r == static_cast<int>(crank)) continue;
+        st_shared_cluster_u32(mapa_shared(slot_addr, static_cast<uint32_t>(r)), v);
+        mbar_arrive_remote(mapa_shared(bar_addr, static_cast<uint32_t>(r)));
+    }
+    slots[par * 4 + crank] = v;
+    mbar_arrive(bar_addr);
+}
+
 template <int G>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(FUSED_THREADS, 1)
 attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
     using L = FusedSmem<G>;
-    constexpr int STAGES = L::RSTAGES;
+    constexpr int KS = L::KSTAGES, VS = L::VSTAGES;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
     uint64_t* q_full = bars;
     uint64_t* q_empty = bars + 1;             // Q read by the slice's last S MMA
-    uint64_t* stage_full = bars + 2;
-    uint64_t* stage_empty = stage_full + STAGES;
-    uint64_t* s_full = stage_empty + STAGES;  // S tile in TMEM computed
+    uint64_t* k_full = bars + 2;
+    uint64_t* k_empty = k_full + KS;
+    uint64_t* v_full = k_empty + KS;
+    uint64_t* v_empty = v_full + VS;
+    uint64_t* s_full = v_empty + VS;          // S tile in TMEM computed
     uint64_t* s_empty = s_full + 1;           // S tile read (16 warps)
     uint64_t* comb = s_full + 2;              // every warp's partial row statistics published (16 warps)
     uint64_t* stats = s_full + 3;             // this CTA's max probability formed (4 warps)
     uint64_t* cl_bar = s_full + 4;            // [2] the cluster's max probabilities gathered (CL arrivals)
     uint64_t* p_ready = s_full + 6;           // [FUSED_MAX_KT] P tile t written (16 warps)
-    uint64_t* o_full = p_ready + FUSED_MAX_KT;
+    uint64_t* p_free = p_ready + FUSED_MAX_KT;  // [FUSED_MAX_KT] P V of tile t complete
+    uint64_t* o_full = p_free + FUSED_MAX_KT;
     uint64_t* o_empty = o_full + 1;
-    uint64_t* drain_bar = o_full + 2;
+    uint64_t* drain_s = o_full + 2;
+    uint64_t* drain_o = o_full + 3;
     uint32_t* misc = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
     uint32_t* tmem_slot = misc;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
@@ -989,9 +1013,13 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(q_full), 1);
         mbar_init(smem_u32(q_empty), 1);
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(smem_u32(stage_full + s), 1);
-            mbar_init(smem_u32(stage_empty + s), 1);
+        for (int s = 0; s < KS; ++s) {
+            mbar_init(smem_u32(k_full + s), 1);
+            mbar_init(smem_u32(k_empty + s), 1);
+        }
+        for (int s = 0; s < VS; ++s) {
+            mbar_init(smem_u32(v_full + s), 1);
+            mbar_init(smem_u32(v_empty + s), 1);
         }
         mbar_init(smem_u32(s_full), 1);
         mbar_init(smem_u32(s_empty), NUM_SOFT_WARPS);
@@ -999,10 +1027,14 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
         mbar_init(smem_u32(stats), 4);
         mbar_init(smem_u32(cl_bar), static_cast<uint32_t>(CL));
         mbar_init(smem_u32(cl_bar + 1), static_cast<uint32_t>(CL));
-        for (int t = 0; t < FUSED_MAX_KT; ++t) mbar_init(smem_u32(p_ready + t), NUM_SOFT_WARPS);
+        for (int t = 0; t < FUSED_MAX_KT; ++t) {
+            mbar_init(smem_u32(p_ready + t), NUM_SOFT_WARPS);
+            mbar_init(smem_u32(p_free + t), 1);
+        }
         mbar_init(smem_u32(o_full), 1);
         mbar_init(smem_u32(o_empty), NUM_SOFT_WARPS);
-        mbar_init(smem_u32(drain_bar), 1);
+        mbar_init(smem_u32(drain_s), 1);
+        mbar_init(smem_u32(drain_o), 1);
         *abort_flag = 0;
         cta_max[0] = 0u;
         cta_max[1] = 0u;
@@ -1024,12 +1056,12 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        // ---------------- TMA producer: per slice Q, K tiles, V^T tiles ----------------
+        // ---------------- TMA: per slice Q, then the K tiles ----------------
         int stage = 0;
         uint32_t phase = 0;
-        uint32_t last_phase[STAGES];
-        bool used[STAGES];
-        for (int s = 0; s < STAGES; ++s) { used[s] = false; last_phase[s] = 0; }
+        uint32_t last_phase[KS];
+        bool used[KS];
+        for (int s = 0; s < KS; ++s) { used[s] = false; last_phase[s] = 0; }
         int q_loads = 0;
         bool ok = true;
         for (int it = 0; it < n_slices && ok; ++it) {
@@ -1045,47 +1077,69 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
             }
             __syncwarp();
             ++q_loads;
-            const int total = n_kt + p.ev_tiles * n_kt;
-            for (int j = 0; j < total; ++j) {
-                if (!mbar_wait_bounded(smem_u32(stage_empty + stage), phase ^ 1u, abort_flag, p.err,
-                                       kDevErrWaitEmpty)) {
+            for (int t = 0; t < n_kt; ++t) {
+                if (!mbar_wait_bounded(smem_u32(k_empty + stage), phase ^ 1u, abort_flag, p.err, kDevErrWaitEmpty)) {
                     ok = false;
                     break;
                 }
                 if (lane == 0) {
-                    const uint32_t fb = smem_u32(stage_full + stage);
-                    const uint32_t dst = smem_u32(smem + L::OFF_RING + stage * L::RING_STAGE);
-                    if (j < n_kt) {
-                        mbar_arrive_expect_tx(fb, G * K_CHUNK);
+                    const uint32_t fb = smem_u32(k_full + stage);
+                    const uint32_t dst = smem_u32(smem + L::OFF_K + stage * G * K_CHUNK);
+                    mbar_arrive_expect_tx(fb, G * K_CHUNK);
 #pragma unroll
-                        for (int g = 0; g < G; ++g) tma_load_3d(dst + g * K_CHUNK, &tmK, fb, g * 128, j * BKEY, bh);
-                    } else {
-                        const int v = j - n_kt;
-                        mbar_arrive_expect_tx(fb, V_TILE);
-                        tma_load_3d(dst, &tmV, fb, (v % n_kt) * 128, (v / n_kt) * EVT, bh);
-                    }
+                    for (int g = 0; g < G; ++g) tma_load_3d(dst + g * K_CHUNK, &tmK, fb, g * 128, t * BKEY, bh);
                 }
                 __syncwarp();
                 used[stage] = true;
                 last_phase[stage] = phase;
-                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                if (++stage == KS) { stage = 0; phase ^= 1u; }
             }
         }
         volatile int no_abort = 0;
-        for (int s = 0; s < STAGES; ++s)
+        for (int s = 0; s < KS; ++s)
             if (used[s])
-                mbar_wait_bounded(smem_u32(stage_full + s), last_phase[s], &no_abort, p.err, kDevErrWaitDrain);
+                mbar_wait_bounded(smem_u32(k_full + s), last_phase[s], &no_abort, p.err, kDevErrWaitDrain);
         if (q_loads > 0)
             mbar_wait_bounded(smem_u32(q_full), static_cast<uint32_t>(q_loads - 1) & 1u, &no_abort, p.err,
                               kDevErrWaitDrain);
-    } else if (warp == 1) {
-        // ---------------- MMA issuer: per slice S = Q K^T, then O += P V ----------------
+    } else if (warp == 2) {
+        // ---------------- TMA: per slice the V^T tiles ----------------
         int stage = 0;
         uint32_t phase = 0;
-        uint32_t n_s = 0, n_o = 0;
+        uint32_t last_phase[VS];
+        bool used[VS];
+        for (int s = 0; s < VS; ++s) { used[s] = false; last_phase[s] = 0; }
+        bool ok = true;
+        for (int it = 0; it < n_slices && ok; ++it) {
+            const int bh = cid + it * n_cl;
+            for (int j = 0; j < p.ev_tiles * n_kt; ++j) {
+                if (!mbar_wait_bounded(smem_u32(v_empty + stage), phase ^ 1u, abort_flag, p.err, kDevErrWaitEmpty)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t fb = smem_u32(v_full + stage);
+                    mbar_arrive_expect_tx(fb, V_TILE);
+                    tma_load_3d(smem_u32(smem + L::OFF_V + stage * V_TILE), &tmV, fb, (j % n_kt) * 128,
+                                (j / n_kt) * EVT, bh);
+                }
+                __syncwarp();
+                used[stage] = true;
+                last_phase[stage] = phase;
+                if (++stage == VS) { stage = 0; phase ^= 1u; }
+            }
+        }
+        volatile int no_abort = 0;
+        for (int s = 0; s < VS; ++s)
+            if (used[s])
+                mbar_wait_bounded(smem_u32(v_full + s), last_phase[s], &no_abort, p.err, kDevErrWaitDrain);
+    } else if (warp == 1) {
+        // ---------------- MMA: S = Q K^T per key tile, running ahead into the next slice ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t n_s = 0;
         bool ok = true;
         const uint32_t s_hh = tmem_base + COL_S, s_mid = s_hh + 64, s_ll = s_hh + 128;
-        const uint32_t o_hh = tmem_base + COL_O, o_mid = o_hh + 64, o_ll = o_hh + 128;
         const uint32_t q_base = smem_u32(smem + L::OFF_Q);
         for (int it = 0; it < n_slices && ok; ++it) {
             if (!mbar_wait_bounded(smem_u32(q_full), static_cast<uint32_t>(it) & 1u, abort_flag, p.err,
@@ -1094,14 +1148,14 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
             for (int t = 0; t < n_kt; ++t) {
                 // the S columns are single-buffered: the CUDA-core warps release
                 // them right after their TMEM loads, before the scores' arithmetic
-                if (!mbar_wait_bounded(smem_u32(stage_full + stage), phase, abort_flag, p.err, kDevErrWaitFull) ||
+                if (!mbar_wait_bounded(smem_u32(k_full + stage), phase, abort_flag, p.err, kDevErrWaitFull) ||
                     !mbar_wait_bounded(smem_u32(s_empty), (n_s & 1u) ^ 1u, abort_flag, p.err, kDevErrWaitAccEmpty)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 if (lane == 0) {
-                    const uint32_t kb = smem_u32(smem + L::OFF_RING + stage * L::RING_STAGE);
+                    const uint32_t kb = smem_u32(smem + L::OFF_K + stage * G * K_CHUNK);
 #pragma unroll
                     for (int g = 0; g < G; ++g) {
                         const uint64_t q0 = smem_desc_kmajor_sw128(q_base + g * Q_CHUNK);
@@ -1118,30 +1172,53 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
                         }
                     }
                     tc_commit(smem_u32(s_full));
-                    tc_commit(smem_u32(stage_empty + stage));
+                    tc_commit(smem_u32(k_empty + stage));
                     if (t == n_kt - 1) tc_commit(smem_u32(q_empty));
                 }
                 __syncwarp();
                 ++n_s;
-                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                if (++stage == KS) { stage = 0; phase ^= 1u; }
             }
+        }
+        if (lane == 0) tc_commit(smem_u32(drain_s));
+        __syncwarp();
+        volatile int no_abort = 0;
+        mbar_wait_bounded(smem_u32(drain_s), 0, &no_abort, p.err, kDevErrWaitDrain);
+    } else if (warp == 3) {
+        // ---------------- MMA: O += P V, and the cluster exchange ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t n_o = 0;
+        bool ok = true;
+        const uint32_t o_hh = tmem_base + COL_O, o_mid = o_hh + 64, o_ll = o_hh + 128;
+        for (int it = 0; it < n_slices && ok; ++it) {
+            const int par = it & 1;
+            // Exchange this CTA's largest probability with the cluster.  Slots
+            // and barriers alternate with the slice's parity, so a CTA that runs
+            // a slice ahead never touches what a slower one still reads.
+            if (lane == 0) {
+                mbar_wait_bounded(smem_u32(stats), static_cast<uint32_t>(par), abort_flag, p.err, kDevErrWaitFull);
+                const unsigned v = *reinterpret_cast<volatile unsigned*>(cta_max + par);
+                *reinterpret_cast<volatile unsigned*>(cta_max + par) = 0u;  // for the slice after next
+                cluster_publish_max(v, par, crank, CL, slots, cl_bar);
+            }
+            __syncwarp();
             for (int evh = 0; evh < p.ev_tiles && ok; ++evh) {
                 if (!mbar_wait_bounded(smem_u32(o_empty), (n_o & 1u) ^ 1u, abort_flag, p.err, kDevErrWaitAccEmpty)) {
                     ok = false;
                     break;
                 }
                 for (int t = 0; t < n_kt; ++t) {
-                    if (!mbar_wait_bounded(smem_u32(p_ready + t), static_cast<uint32_t>(it) & 1u, abort_flag, p.err,
+                    if (!mbar_wait_bounded(smem_u32(p_ready + t), static_cast<uint32_t>(par), abort_flag, p.err,
                                            kDevErrWaitFull) ||
-                        !mbar_wait_bounded(smem_u32(stage_full + stage), phase, abort_flag, p.err, kDevErrWaitFull)) {
+                        !mbar_wait_bounded(smem_u32(v_full + stage), phase, abort_flag, p.err, kDevErrWaitFull)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     if (lane == 0) {
                         const uint64_t a0 = smem_desc_kmajor_sw128(smem_u32(smem + L::OFF_S + t * P_TILE));
-                        const uint64_t b0 =
-                            smem_desc_kmajor_sw128(smem_u32(smem + L::OFF_RING + stage * L::RING_STAGE));
+                        const uint64_t b0 = smem_desc_kmajor_sw128(smem_u32(smem + L::OFF_V + stage * V_TILE));
 #pragma unroll
                         for (int u = 0; u < 2; ++u) {
                             const uint64_t hi = static_cast<uint64_t>((u * 32) >> 4);
@@ -1152,23 +1229,24 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
                             tc_mma_i8(o_mid, a0 + lo, b0 + hi, IDESC_US, 1u);
                             tc_mma_i8(o_ll, a0 + lo, b0 + lo, IDESC_UU, acc);
                         }
-                        tc_commit(smem_u32(stage_empty + stage));
+                        tc_commit(smem_u32(v_empty + stage));
+                        if (evh == p.ev_tiles - 1) tc_commit(smem_u32(p_free + t));
                         if (t == n_kt - 1) tc_commit(smem_u32(o_full));
                     }
                     __syncwarp();
-                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                    if (++stage == VS) { stage = 0; phase ^= 1u; }
                 }
                 ++n_o;
             }
         }
-        if (lane == 0) tc_commit(smem_u32(drain_bar));
+        if (lane == 0) tc_commit(smem_u32(drain_o));
         __syncwarp();
         volatile int no_abort = 0;
-        mbar_wait_bounded(smem_u32(drain_bar), 0, &no_abort, p.err, kDevErrWaitDrain);
+        mbar_wait_bounded(smem_u32(drain_o), 0, &no_abort, p.err, kDevErrWaitDrain);
     } else {
-        // ---------------- scores, statistics, P and the output (warps 2..17) ----------------
+        // ---------------- scores, statistics, P and the output (warps 4..19) ----------------
         const int quarter = warp & 3;
-        const int sub = (warp - 2) >> 2;
+        const int sub = (warp - 4) >> 2;
         const int row = quarter * 32 + lane;
         const int sw = row & 7;
         const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -1177,11 +1255,67 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
         uint8_t* line0 = smem + L::OFF_S + row * 128;
         uint32_t n_s = 0, n_o = 0;
         bool ok = true;
+        // With one output tile the dequantisation of a slice's O waits until
+        // the next slice's scores are formed, so P V runs meanwhile; with more,
+        // the later output tiles reuse the accumulator and it runs at once.
+        const bool defer = p.ev_tiles == 1;
+        // O of slice (b, h): dequantise with the slice's P and v scales, store
+        auto epilogue = [&](int b, int h, float pmax, float amax_v) {
+            for (int evh = 0; evh < p.ev_tiles; ++evh) {
+                if (!mbar_wait_bounded(smem_u32(o_full), n_o & 1u, abort_flag, p.err, kDevErrWaitAccFull)) {
+                    ok = false;
+                    return;
+                }
+                ++n_o;
+                tc_fence_after();
+                uint32_t hh[CW], mid[CW], ll[CW];
+                const uint32_t col = COL_O + CW * sub;
+                tmem_ld_cw(t_lane + col, hh);
+                tmem_ld_cw(t_lane + col + 64, mid);
+                tmem_ld_cw(t_lane + col + 128, ll);
+                tc_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(o_empty));
+                if (row_ok) {
+                    const double spv = dequant_scale(pmax, amax_v);
+                    const int64_t e0 = static_cast<int64_t>(evh) * EVT + CW * sub;
+                    const int64_t obase = b * p.os[0] + h * p.os[1] + i * p.os[2];
+                    float o[CW];
+#pragma unroll
+                    for (int c = 0; c < CW; ++c)
+                        o[c] = round_t_from_double(__dmul_rn(limb_acc_to_double(hh[c], mid[c], ll[c]), spv), 0);
+                    if (p.out_vec && e0 + CW <= p.Ev) {
+                        store_row_n<0, CW>(static_cast<char*>(p.out) + (obase + e0) * 2, o);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < CW; ++c)
+                            if (e0 + c < p.Ev) store_t(p.out, 0, obase + (e0 + c) * p.os[3], o[c]);
+                    }
+                }
+            }
+        };
+        int prev_b = 0, prev_h = 0;
+        float prev_pmax = 0.0f, prev_av = 0.0f;
+        bool have_prev = false;
+        // the slice's q, k, v scales, loaded one slice ahead
+        float aq = 0.0f, ak = 0.0f, av = 0.0f;
+        if (n_slices > 0) {
+            aq = __ldg(p.amax + cid);
+            ak = __ldg(p.amax + BH + cid);
+            av = __ldg(p.amax + 2 * BH + cid);
+        }
         for (int it = 0; it < n_slices && ok; ++it) {
             const int bh = cid + it * n_cl;
             const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
             const int par = it & 1;
-            const double sqk = dequant_scale(__ldg(p.amax + bh), __ldg(p.amax + BH + bh));
+            const double sqk = dequant_scale(aq, ak);
+            const float amax_v = av;
+            if (it + 1 < n_slices) {
+                aq = __ldg(p.amax + bh + n_cl);
+                ak = __ldg(p.amax + BH + bh + n_cl);
+                av = __ldg(p.amax + 2 * BH + bh + n_cl);
+            }
             const void* mask_row = nullptr;
             if (p.mask != nullptr && row_ok)
                 mask_row = static_cast<const char*>(p.mask) + (b * p.ms[0] + h * p.ms[1] + i * p.ms[2]) * 2;
@@ -1213,6 +1347,13 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
                 if (lane == 0) mbar_arrive(smem_u32(s_empty));
                 __half2 sh[CW / 2];
                 scores_h<CW>(hh, mid, ll, sqk, p, i, j0, mask_row, sh, pre ? mpre : nullptr);
+                // the previous slice's P tile t has been read by its P V
+                if (it > 0 &&
+                    !mbar_wait_bounded(smem_u32(p_free + t), static_cast<uint32_t>(par ^ 1), abort_flag, p.err,
+                                       kDevErrWaitEmpty)) {
+                    ok = false;
+                    break;
+                }
                 // keys j0..j0+7 go to 16-byte chunk sub of the row's line, keys
                 // j0+8..j0+15 to chunk 4 + sub: the chunks that later hold this
                 // warp's hi and lo limbs of P, so each warp converts its own bytes
@@ -1241,6 +1382,11 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
                 }
             }
             if (!ok) break;
+            if (have_prev) {
+                epilogue(prev_b, prev_h, prev_pmax, prev_av);
+                have_prev = false;
+                if (!ok) break;
+            }
             // Every warp publishes its partial (m, l); each warp then combines
             // the four partials of its rows in the statistics kernel's order
             // (key quarter 0 first), so all four warps of a row hold the same
@@ -1276,23 +1422,6 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
                     if (bits != 0u) atomicMax(cta_max + par, bits);
                     mbar_arrive(smem_u32(stats));
                 }
-            }
-            // One thread exchanges this CTA's largest probability with the
-            // cluster: slots and barriers alternate with the slice's parity, so
-            // a CTA that runs a slice ahead never touches what a slower one reads.
-            if (warp == 2 && lane == 0) {
-                mbar_wait_bounded(smem_u32(stats), static_cast<uint32_t>(par), abort_flag, p.err, kDevErrWaitFull);
-                const unsigned v = *reinterpret_cast<volatile unsigned*>(cta_max + par);
-                *reinterpret_cast<volatile unsigned*>(cta_max + par) = 0u;  // for the slice after next
-                const uint32_t slot_addr = smem_u32(const_cast<unsigned*>(slots) + par * 4 + crank);
-                const uint32_t bar_addr = smem_u32(cl_bar + par);
-                for (int r = 0; r < CL; ++r) {
-                    if (r == static_cast<int>(crank)) continue;
-                    st_shared_cluster_u32(mapa_shared(slot_addr, static_cast<uint32_t>(r)), v);
-                    mbar_arrive_remote(mapa_shared(bar_addr, static_cast<uint32_t>(r)));
-                }
-                slots[par * 4 + crank] = v;
-                mbar_arrive(bar_addr);
             }
             // While the cluster exchanges, P = T(exp(s - m) / l) replaces the
             // scores in place (binary16, as the reference's softmax output)
@@ -1341,41 +1470,17 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(p_ready + t));
             }
-            // output tiles of 64 value columns
-            for (int evh = 0; evh < p.ev_tiles; ++evh) {
-                if (!mbar_wait_bounded(smem_u32(o_full), n_o & 1u, abort_flag, p.err, kDevErrWaitAccFull)) {
-                    ok = false;
-                    break;
-                }
-                ++n_o;
-                tc_fence_after();
-                uint32_t hh[CW], mid[CW], ll[CW];
-                const uint32_t col = COL_O + CW * sub;
-                tmem_ld_cw(t_lane + col, hh);
-                tmem_ld_cw(t_lane + col + 64, mid);
-                tmem_ld_cw(t_lane + col + 128, ll);
-                tc_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(o_empty));
-                if (row_ok) {
-                    const double spv = dequant_scale(pmax, __ldg(p.amax + 2 * BH + bh));
-                    const int64_t e0 = static_cast<int64_t>(evh) * EVT + CW * sub;
-                    const int64_t obase = b * p.os[0] + h * p.os[1] + i * p.os[2];
-                    float o[CW];
-#pragma unroll
-                    for (int c = 0; c < CW; ++c)
-                        o[c] = round_t_from_double(__dmul_rn(limb_acc_to_double(hh[c], mid[c], ll[c]), spv), 0);
-                    if (p.out_vec && e0 + CW <= p.Ev) {
-                        store_row_n<0, CW>(static_cast<char*>(p.out) + (obase + e0) * 2, o);
-                    } else {
-#pragma unroll
-                        for (int c = 0; c < CW; ++c)
-                            if (e0 + c < p.Ev) store_t(p.out, 0, obase + (e0 + c) * p.os[3], o[c]);
-                    }
-                }
+            if (defer) {
+                prev_b = b;
+                prev_h = h;
+                prev_pmax = pmax;
+                prev_av = amax_v;
+                have_prev = true;
+            } else {
+                epilogue(b, h, pmax, amax_v);
             }
         }
+        if (have_prev && ok) epilogue(prev_b, prev_h, prev_pmax, prev_av);
     }
 
     tc_fence_before();
@@ -1680,7 +1785,7 @@ int max_fused_clusters(int cl, int dev) {
     std::call_once(once[slot][cl], [&] {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(static_cast<unsigned>(cl * 1024));
-        cfg.blockDim = dim3(NUM_THREADS);
+        cfg.blockDim = dim3(FUSED_THREADS);
         cfg.dynamicSmemBytes = FusedSmem<G>::ALLOC;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1711,7 +1816,7 @@ int run_fused(const CUtensorMap& tq, const CUtensorMap& tk_, const CUtensorMap& 
     const int n_cl = std::min(p.B * p.H, max_fused_clusters<G>(p.m_tiles, dev));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(n_cl * p.m_tiles));
-    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.blockDim = dim3(FUSED_THREADS);
     cfg.dynamicSmemBytes = L::ALLOC;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
