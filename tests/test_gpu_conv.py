@@ -33,7 +33,25 @@ CASES = [
     (1, 16, 10, 10, 24, 3, 2, 2, False, torch.float16),    # dilation 2
     (2, 8, 7, 7, 16, 5, 2, 1, True, torch.float32),        # fp32
     (1, 3, 17, 17, 8, 7, 3, 1, True, torch.float16),       # RGB stem-like
+    # 1x1 with the input quantised inside the kernel (fp16, <= 64 filters, <= 256
+    # channels, plane a multiple of 8 pixels):
+    (2, 256, 56, 56, 64, 1, 0, 1, False, torch.float16),   # the ResNet-50 stage shape, ragged last pixel tile
+    (3, 100, 9, 8, 40, 1, 0, 1, True, torch.float16),      # ragged channel group (zero-filled), bias
+    (1, 192, 16, 16, 64, 1, 0, 1, True, torch.float16),    # three channel groups
+    # 1x1 cases that keep the limb pass: plane not a multiple of 8, 320 channels
+    (2, 64, 7, 9, 8, 1, 0, 1, False, torch.float16),
+    (1, 320, 8, 8, 64, 1, 0, 1, True, torch.float16),
 ]
+
+
+def test_1x1_in_kernel_quantisation_non_finite():
+    """A NaN in the input makes its scale non-finite: every output is NaN,
+    on the path that quantises the input inside the 1x1 kernel too."""
+    x = torch.relu(rnd((2, 128, 16, 16), 43))
+    x[1, 127, 15, 15] = float("nan")
+    w = rnd((32, 128, 1, 1), 44, scale=0.1)
+    y = torch.nn.functional.conv2d(x.to(DEV), w.to(DEV)).cpu()
+    assert bool(torch.isnan(y).all())
 
 
 @pytest.mark.parametrize("case", CASES)
@@ -81,7 +99,27 @@ DW_CASES = [
     (1, 7, 1, 11, 11, 7, 1, 3, 1, True, torch.float16),    # 7x7
     (2, 3, 1, 1, 40, 3, 1, 1, 1, False, torch.float16),    # one-row planes, padding wider than the row
     (2, 6, 1, 5, 5, 3, 1, 2, 1, True, torch.float32),      # padding 2: outputs beyond the input
+    # more blocks than fit on the device at once: the two-pass path (amax
+    # launch, then the row kernel) instead of the one cooperative launch
+    (64, 512, 1, 14, 14, 3, 1, 1, 1, True, torch.float16),
 ]
+
+
+def test_depthwise_fused_scales_propagate_non_finite():
+    """A NaN or an infinity anywhere in the input makes the input scale
+    non-finite, so every output is NaN (the library's convention), through
+    the one-launch path whose blocks combine their scales at a grid barrier."""
+    for bad in (float("nan"), float("inf")):
+        x = torch.relu(rnd((4, 32, 7, 7), 49))
+        x[3, 31, 6, 6] = bad
+        w = rnd((32, 1, 3, 3), 50)
+        y = torch.nn.functional.conv2d(x.to(DEV), w.to(DEV), padding=1, groups=32).cpu()
+        assert bool(torch.isnan(y).all()), bad
+    x = torch.relu(rnd((4, 32, 7, 7), 51))
+    w = rnd((32, 1, 3, 3), 52)
+    w[17, 0, 1, 1] = float("nan")
+    y = torch.nn.functional.conv2d(x.to(DEV), w.to(DEV), padding=1, groups=32).cpu()
+    assert bool(torch.isnan(y).all())
 
 
 @pytest.mark.parametrize("case", DW_CASES)

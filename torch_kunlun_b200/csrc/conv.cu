@@ -20,6 +20,7 @@
 //     images), and the epilogue writes the pixels x channels tile into NCHW.
 #include "tk_internal.h"
 #include "tk_numerics.cuh"
+#include "tk_ptx.cuh"
 
 namespace tk {
 
@@ -420,6 +421,227 @@ depthwise_rows_kernel(const T* __restrict__ x, const T* __restrict__ w, const T*
     }
 }
 
+// The same depthwise convolution with the two max-abs reductions folded in:
+// one cooperative launch in which every block loads its planes (and its
+// channels' filters) into shared memory once, folds their magnitudes into
+// the two scale words, waits at a grid-wide barrier for every block's
+// contribution, then quantises from shared memory, convolves and stores the
+// block's contiguous span of the output with 16-byte vectors.  The input
+// crosses HBM once (the separate amax pass read it twice) and the op is one
+// launch after a 16-byte memset of the scale words and the barrier counter.
+// sync[0], sync[1]: fp32 magnitude bits of max |x| and max |w| (atomicMax,
+// NaN above everything, as the amax kernels); sync[2]: blocks arrived.
+struct DwMagic {
+    uint32_t hw, w, taps, ohw, ow;  // floor(2^32 / d) + 1 for i / d with i, d < 2^16
+};
+
+__device__ __forceinline__ int round_up_dev(int v, int a) { return (v + a - 1) / a * a; }
+
+__device__ __forceinline__ int div_magic(int i, uint32_t m) {
+    return static_cast<int>(__umulhi(static_cast<uint32_t>(i), m));
+}
+
+template <typename T>
+__device__ __forceinline__ unsigned mag_bits(T v);
+template <>
+__device__ __forceinline__ unsigned mag_bits<__half>(__half v) {
+    const unsigned h = __half_as_ushort(v) & 0x7FFFu;
+    if ((h & 0x7C00u) == 0x7C00u && (h & 0x3FFu) != 0u) return 0x7FC00000u;  // NaN, canonical
+    return __float_as_uint(__half2float(__ushort_as_half(static_cast<unsigned short>(h))));
+}
+template <>
+__device__ __forceinline__ unsigned mag_bits<float>(float v) {
+    return __float_as_uint(v) & 0x7FFFFFFFu;
+}
+
+__device__ __forceinline__ unsigned block_max_bits(unsigned v, unsigned* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    v = 0u;
+    for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) v = max(v, red[k]);
+    return v;
+}
+
+template <typename T, int DT, int KW>
+__global__ void __launch_bounds__(kDwRowThreads)
+depthwise_fused_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ bias,
+                       T* __restrict__ out, ConvGeom g, int ppb, DwMagic mg, unsigned* sync, unsigned* err) {
+    extern __shared__ __align__(16) uint8_t dsm[];
+    const int H = static_cast<int>(g.H), W = static_cast<int>(g.W);
+    const int ph = static_cast<int>(g.ph), pw = static_cast<int>(g.pw);
+    const int Hp = H + 2 * ph, Wp = W + 2 * pw;
+    const int KH = static_cast<int>(g.KH);
+    const int OH = static_cast<int>(g.OH), OW = static_cast<int>(g.OW);
+    const int HW = H * W, PHW = Hp * Wp, taps = KH * KW;
+    const int64_t planes = g.N * g.C;
+    const int64_t pl0 = static_cast<int64_t>(blockIdx.x) * ppb;
+    const int np = static_cast<int>(min(static_cast<int64_t>(ppb), planes - pl0));
+    const int C = static_cast<int>(g.C);
+    const int c0 = static_cast<int>(pl0 % g.C);
+    // shared memory: raw span (reused for the output span), padded codes,
+    // filter values then codes, reduction scratch
+    const int raw_elems = ppb * max(HW, OH * OW);
+    T* raw = reinterpret_cast<T*>(dsm);
+    int16_t* xs = reinterpret_cast<int16_t*>(dsm + round_up_dev(raw_elems * static_cast<int>(sizeof(T)), 16));
+    float* wf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) +
+                                         round_up_dev((ppb * PHW + kDwRowOut + KW) * 2, 16));
+    int* wsq = reinterpret_cast<int*>(wf);
+    unsigned* red = reinterpret_cast<unsigned*>(wf + ppb * taps);
+
+    // ---- phase 1: the block's input span and filters, and their magnitudes
+    const T* xb = x + pl0 * HW;
+    const int n = np * HW;
+    unsigned mx = 0u, mw = 0u;
+    constexpr int VEC = 16 / sizeof(T);
+    const bool aligned = reinterpret_cast<uintptr_t>(x) % 16 == 0;
+    const int head = aligned ? min(n, static_cast<int>((VEC - (pl0 * HW) % VEC) % VEC)) : n;
+    const int nv = (n - head) / VEC;
+    for (int i = threadIdx.x; i < head; i += blockDim.x) {
+        const T v = xb[i];
+        raw[i] = v;
+        mx = max(mx, mag_bits<T>(v));
+    }
+    for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+        const int i0 = head + v * VEC;
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(xb + i0));
+        const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) {
+            raw[i0 + k] = e[k];
+            mx = max(mx, mag_bits<T>(e[k]));
+        }
+    }
+    for (int i = head + nv * VEC + threadIdx.x; i < n; i += blockDim.x) {
+        const T v = xb[i];
+        raw[i] = v;
+        mx = max(mx, mag_bits<T>(v));
+    }
+    for (int i = threadIdx.x; i < np * taps; i += blockDim.x) {
+        const int pp = div_magic(i, mg.taps), t = i - pp * taps;
+        int c = c0 + pp;
+        while (c >= C) c -= C;
+        const T v = w[static_cast<int64_t>(c) * taps + t];
+        wf[i] = static_cast<float>(v);
+        mw = max(mw, mag_bits<T>(v));
+    }
+    mx = block_max_bits(mx, red);
+    __syncthreads();
+    mw = block_max_bits(mw, red);
+    __syncthreads();
+    // ---- grid-wide barrier (every block is resident: cooperative launch)
+    if (threadIdx.x == 0) {
+        if (mx != 0u) atomicMax(sync, mx);
+        if (mw != 0u) atomicMax(sync + 1, mw);
+        __threadfence();
+        atomicAdd(sync + 2, 1u);
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_gpu_u32(sync + 2) < gridDim.x) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                atomicCAS(err, 0u, static_cast<unsigned>(kDevErrWaitCluster));
+                break;
+            }
+        }
+        red[0] = ld_acquire_gpu_u32(sync);
+        red[1] = ld_acquire_gpu_u32(sync + 1);
+    }
+    __syncthreads();
+    const float ax = __uint_as_float(red[0]), aw = __uint_as_float(red[1]);
+    const float invx = quant_inv(ax), invw = quant_inv(aw);
+    const double s = dequant_scale(ax, aw);
+
+    // ---- phase 2: codes into zero-padded planes, filter codes
+    for (int i = threadIdx.x; i < np * PHW + kDwRowOut + KW; i += blockDim.x) xs[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int pp = div_magic(i, mg.hw), r = i - pp * HW;
+        const int ih = div_magic(r, mg.w), iw = r - ih * W;
+        xs[pp * PHW + (ih + ph) * Wp + iw + pw] = static_cast<int16_t>(quant_one(ldx<T>(raw, i), invx));
+    }
+    // filter codes split as 256 * hi + lo (hi in [-128, 127], lo in [0, 255])
+    // so both partial sums below stay int32: |x| * 128 and |x| * 255 over at
+    // most 49 taps are below 2^29
+    for (int i = threadIdx.x; i < np * taps; i += blockDim.x) {
+        const int q = quant_one(wf[i], invw);
+        wsq[i] = (q >> 8) * 65536 + (q & 255);  // hi in the upper half, lo in the lower
+    }
+    __syncthreads();
+    // ---- each thread a whole output row, into the staged output span
+    for (int row = threadIdx.x; row < np * OH; row += blockDim.x) {
+        const int pp = row / OH, oh = row - pp * OH;
+        const int16_t* xr = xs + pp * PHW + oh * Wp;
+        const int* wp = wsq + pp * taps;
+        int c = c0 + pp;
+        while (c >= C) c -= C;
+        const float bv = bias != nullptr ? ldx<T>(bias, c) : 0.0f;
+        T* orow = raw + row * OW;
+        for (int ow0 = 0; ow0 < OW; ow0 += kDwRowOut) {
+            int acc_hi[kDwRowOut], acc_lo[kDwRowOut];
+#pragma unroll
+            for (int j = 0; j < kDwRowOut; ++j) acc_hi[j] = acc_lo[j] = 0;
+            for (int r = 0; r < KH; ++r) {
+                int xv[kDwRowOut + KW - 1];
+#pragma unroll
+                for (int j = 0; j < kDwRowOut + KW - 1; ++j) xv[j] = xr[r * Wp + ow0 + j];
+#pragma unroll
+                for (int k = 0; k < KW; ++k) {
+                    const int wv = wp[r * KW + k];
+                    const int wh = wv >> 16, wl = wv & 0xFFFF;
+#pragma unroll
+                    for (int j = 0; j < kDwRowOut; ++j) {
+                        acc_hi[j] += xv[j + k] * wh;
+                        acc_lo[j] += xv[j + k] * wl;
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kDwRowOut; ++j) {
+                if (ow0 + j < OW) {
+                    // the exact sum 256 * hi + lo as binary64: both int32 through
+                    // their bit patterns, joined by one exact multiply-add
+                    const double dh = __hiloint2double(0x43300000, acc_hi[j] ^ static_cast<int>(0x80000000u)) -
+                                      4503601774854144.0;
+                    const double dl = __hiloint2double(0x43300000, acc_lo[j] ^ static_cast<int>(0x80000000u)) -
+                                      4503601774854144.0;
+                    float v = round_t_from_double(__dmul_rn(__fma_rn(dh, 256.0, dl), s), DT);
+                    if (bias != nullptr) v = round_t(__fadd_rn(v, bv), DT);
+                    store_t(orow, DT, ow0 + j, v);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    // ---- the block's output span, 16-byte vectors where aligned
+    const int no = np * OH * OW;
+    T* obase = out + pl0 * OH * OW;
+    const bool oal = reinterpret_cast<uintptr_t>(out) % 16 == 0;
+    const int ohead = oal ? min(no, static_cast<int>((VEC - (pl0 * OH * OW) % VEC) % VEC)) : no;
+    const int onv = (no - ohead) / VEC;
+    for (int i = threadIdx.x; i < ohead; i += blockDim.x) obase[i] = raw[i];
+    for (int v = threadIdx.x; v < onv; v += blockDim.x) {
+        const int i0 = ohead + v * VEC;
+        uint4 u;
+        T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) e[k] = raw[i0 + k];
+        *reinterpret_cast<uint4*>(obase + i0) = u;
+    }
+    for (int i = ohead + onv * VEC + threadIdx.x; i < no; i += blockDim.x) obase[i] = raw[i];
+}
+
+// Shared-memory bytes of depthwise_fused_kernel for `ppb` planes.
+size_t depthwise_fused_smem(const ConvGeom& g, int ppb, size_t esize) {
+    const int64_t hw = g.H * g.W, ohw = g.OH * g.OW;
+    const int64_t phw = (g.H + 2 * g.ph) * (g.W + 2 * g.pw);
+    size_t b = round_up(static_cast<size_t>(ppb * std::max(hw, ohw)) * esize, 16);
+    b += round_up(static_cast<size_t>(ppb * phw + kDwRowOut + g.KW) * 2, 16);
+    b += static_cast<size_t>(ppb * g.KH * g.KW) * 4;
+    b += 32 * sizeof(unsigned);
+    return b;
+}
+
 // Planes per block of depthwise_rows_kernel for this geometry (0: the
 // kernel does not apply): at most one output row per thread, within the
 // shared-memory spans.
@@ -435,6 +657,71 @@ int depthwise_rows_ppb(const ConvGeom& g) {
     ppb = std::min(ppb, kDwRowSpan / phw);
     ppb = std::min(ppb, kDwRowTaps / taps);
     return static_cast<int>(std::max<int64_t>(ppb, 1));
+}
+
+uint32_t magic_div(int64_t d) { return static_cast<uint32_t>((1ULL << 32) / static_cast<uint64_t>(d) + 1); }
+
+// The depthwise convolution with its scales in one cooperative launch, when
+// the row kernel's geometry applies and every block fits on the device at
+// once; TK_ERR_UNSUPPORTED otherwise (the caller takes the two-pass path).
+int depthwise_fused_launch(const tk_conv3d_desc_t& d, const ConvGeom& g, unsigned* sync, cudaStream_t stream) {
+    int ppb = depthwise_rows_ppb(g);
+    // the kernel's int32 partial sums hold up to 64 taps
+    if (ppb == 0 || g.KH * g.KW > 64) return TK_ERR_UNSUPPORTED;
+    const int64_t planes = g.N * g.C;
+    const int64_t hw = g.H * g.W, ohw = g.OH * g.OW;
+    const int64_t phw = (g.H + 2 * g.ph) * (g.W + 2 * g.pw), taps = g.KH * g.KW;
+    const size_t esize = d.dtype == TK_DTYPE_F16 ? 2 : 4;
+    const int dev = current_device();
+    const void* fn = nullptr;
+    if (d.dtype == TK_DTYPE_F16) {
+        fn = g.KW == 3 ? reinterpret_cast<const void*>(depthwise_fused_kernel<__half, 0, 3>)
+           : g.KW == 5 ? reinterpret_cast<const void*>(depthwise_fused_kernel<__half, 0, 5>)
+                       : reinterpret_cast<const void*>(depthwise_fused_kernel<__half, 0, 7>);
+    } else {
+        fn = g.KW == 3 ? reinterpret_cast<const void*>(depthwise_fused_kernel<float, 1, 3>)
+           : g.KW == 5 ? reinterpret_cast<const void*>(depthwise_fused_kernel<float, 1, 5>)
+                       : reinterpret_cast<const void*>(depthwise_fused_kernel<float, 1, 7>);
+    }
+    TK_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+    // every block must be resident at once: when the row kernel's planes per
+    // block give more blocks than fit, give each block more planes (threads
+    // then take several rows), within the shared-memory spans
+    int64_t blocks = 0;
+    size_t smem = 0;
+    for (int attempt = 0; attempt < 2; ++attempt) {
+        if (static_cast<int64_t>(ppb) * std::max(hw, ohw) >= 65536 || ppb * phw > kDwRowSpan ||
+            ppb * taps > kDwRowTaps)
+            return TK_ERR_UNSUPPORTED;
+        smem = depthwise_fused_smem(g, ppb, esize);
+        if (smem > 96 * 1024) return TK_ERR_UNSUPPORTED;
+        int per_sm = 0;
+        TK_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kDwRowThreads, smem));
+        const int64_t cap = static_cast<int64_t>(per_sm) * sm_count(dev);
+        blocks = ceil_div(planes, ppb);
+        if (cap > 0 && blocks <= cap) break;
+        if (attempt == 1 || cap <= 0) return TK_ERR_UNSUPPORTED;
+        ppb = static_cast<int>(ceil_div(planes, cap));
+    }
+    TK_CUDA_TRY(cudaMemsetAsync(sync, 0, 4 * sizeof(unsigned), stream));
+    ConvGeom gg = g;
+    int ppb_arg = ppb;
+    DwMagic mg;
+    mg.hw = magic_div(hw);
+    mg.w = magic_div(g.W);
+    mg.taps = magic_div(g.KH * g.KW);
+    mg.ohw = magic_div(ohw);
+    mg.ow = magic_div(g.OW);
+    unsigned* err = device_error_word(dev);
+    const void* xp = d.x;
+    const void* wp = d.weight;
+    const void* bp = d.bias;
+    void* op = d.out;
+    void* args[] = {const_cast<void**>(&xp), const_cast<void**>(&wp), const_cast<void**>(&bp), &op, &gg, &ppb_arg,
+                    &mg, &sync, &err};
+    TK_CUDA_TRY(cudaLaunchCooperativeKernel(fn, dim3(static_cast<unsigned>(blocks)), dim3(kDwRowThreads), args,
+                                            smem, stream));
+    return launch_status("conv2d depthwise (fused scales)");
 }
 
 int grid_1d(int64_t n, int threads) {
@@ -697,6 +984,10 @@ int tk_conv3d_q16(const tk_conv3d_desc_t* desc, void* workspace, size_t workspac
     float* amax = reinterpret_cast<float*>(ws + L.off_amax);  // [0] input, [1] weight
     const float* ax = d.amax_x;
     const float* aw = d.amax_w;
+    if (ax == nullptr && aw == nullptr) {
+        rc = depthwise_fused_launch(d, g, reinterpret_cast<unsigned*>(amax), stream);
+        if (rc != TK_ERR_UNSUPPORTED) return rc;
+    }
     if (ax == nullptr && aw == nullptr) {  // both scales in one launch
         rc = amax_pair_launch(d.dtype, d.x, g.N * g.C * g.D * g.H * g.W, d.weight,
                               g.F * (g.C / g.groups) * g.KD * g.KH * g.KW, amax, stream);

@@ -859,6 +859,264 @@ conv_stk_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__
     }
 }
 
+// ---- 1x1 convolution with the input quantised inside the kernel -------------
+//
+// For a 1x1 filter (stride 1, no padding, groups 1, at most 64 filters, fp16
+// input with a plane of 8k pixels) the implicit GEMM needs no halo, so the
+// input limbs need not be staged in HBM: the TMA warp loads fp16 boxes of
+// 64 channels x 128 consecutive pixels straight from the NCHW input, the 16
+// worker warps quantise them (the library's codes, magic-number rounding)
+// into the swizzled K-major limb tile the MMAs read, and the stacked-limb
+// MMAs of conv_stk_kernel accumulate the tile.  The same workers run the
+// epilogue of the previous tile while the MMA warp works on the next, so
+// the input crosses HBM once after its amax pass (the limb pass read it and
+// wrote and re-read 2 bytes per element).
+constexpr int Q1_NRAW = 4;                         // fp16 input boxes in flight
+constexpr int Q1_NA = 4;                           // limb tiles in flight
+constexpr int Q1_RAW_BYTES = 64 * BM * 2;          // 64 channels x 128 pixels fp16
+// A tile's channel groups must all fit the limb-tile ring: the workers
+// dequantise the previous tile only after quantising the current one, so the
+// MMAs of the current tile cannot free limb tiles before its last group is in.
+constexpr int Q1_MAX_PAIRS = Q1_NA / 2;            // C <= 64 * Q1_NA
+constexpr int Q1_OFF_A = Q1_NRAW * Q1_RAW_BYTES;
+constexpr int Q1_OFF_B = Q1_OFF_A + Q1_NA * A_BYTES;
+constexpr int Q1_OFF_BAR = Q1_OFF_B + Q1_MAX_PAIRS * STK_TILE;
+constexpr int Q1_SMEM = Q1_OFF_BAR + 256 + 1024;
+static_assert(Q1_OFF_A % 1024 == 0 && Q1_OFF_B % 1024 == 0, "swizzled tiles on 1024-byte boundaries");
+static_assert(Q1_SMEM <= 227 * 1024, "fits one CTA's shared memory");
+static_assert(NUM_EPI_WARPS == 16, "four worker warps per lane quarter");
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+conv1x1_q_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                 const ConvWinParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Q1_OFF_BAR);
+    uint64_t* raw_full = bars;
+    uint64_t* raw_empty = raw_full + Q1_NRAW;
+    uint64_t* a_full = raw_empty + Q1_NRAW;
+    uint64_t* a_empty = a_full + Q1_NA;
+    uint64_t* acc_full = a_empty + Q1_NA;
+    uint64_t* acc_empty = acc_full + 1;
+    uint64_t* drain_bar = acc_full + 2;
+    uint64_t* w_full = acc_full + 3;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 4);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int Cg = p.Cg;
+    const int npairs = (Cg + 1) / 2;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < Q1_NRAW; ++i) {
+            mbar_init(smem_u32(raw_full + i), 1);
+            mbar_init(smem_u32(raw_empty + i), NUM_EPI_WARPS);
+        }
+        for (int i = 0; i < Q1_NA; ++i) {
+            mbar_init(smem_u32(a_full + i), NUM_EPI_WARPS);
+            mbar_init(smem_u32(a_empty + i), 1);
+        }
+        mbar_init(smem_u32(acc_full), 1);
+        mbar_init(smem_u32(acc_empty), NUM_EPI_WARPS);
+        mbar_init(smem_u32(drain_bar), 1);
+        mbar_init(smem_u32(w_full), 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmX);
+        tma_prefetch_desc(&tmW);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA: stacked weights once, then fp16 input boxes ----------------
+        int rb = 0;
+        uint32_t rph = 0;
+        uint32_t r_last[Q1_NRAW];
+        bool r_used[Q1_NRAW];
+        for (int i = 0; i < Q1_NRAW; ++i) { r_last[i] = 0; r_used[i] = false; }
+        bool ok = true;
+        if (lane == 0) {
+            const uint32_t fbar = smem_u32(w_full);
+            mbar_arrive_expect_tx(fbar, static_cast<uint32_t>(npairs * STK_TILE));
+            for (int q = 0; q < npairs; ++q)
+                tma_load_3d(smem_u32(smem + Q1_OFF_B + q * STK_TILE), &tmW, fbar, 0, q * STK_N, 0);
+        }
+        __syncwarp();
+        for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+            const int pt = t % p.pos_tiles;
+            const int n = t / p.pos_tiles;
+            for (int g = 0; g < Cg; ++g) {
+                if (!mbar_wait_bounded(smem_u32(raw_empty + rb), rph ^ 1u, abort_flag, p.err, kDevErrWaitEmpty)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t fbar = smem_u32(raw_full + rb);
+                    mbar_arrive_expect_tx(fbar, Q1_RAW_BYTES);
+                    tma_load_3d(smem_u32(smem + rb * Q1_RAW_BYTES), &tmX, fbar, pt * BM, g * 64, n);
+                }
+                __syncwarp();
+                r_used[rb] = true;
+                r_last[rb] = rph;
+                if (++rb == Q1_NRAW) { rb = 0; rph ^= 1u; }
+            }
+        }
+        volatile int no_abort = 0;
+        mbar_wait_bounded(smem_u32(w_full), 0, &no_abort, p.err, kDevErrWaitDrain);
+        for (int i = 0; i < Q1_NRAW; ++i)
+            if (r_used[i]) mbar_wait_bounded(smem_u32(raw_full + i), r_last[i], &no_abort, p.err, kDevErrWaitDrain);
+    } else if (warp == 1) {
+        // ---------------- MMA issuer: two stacked MMAs per 32 channels ----------------
+        int ab = 0;
+        uint32_t aph = 0;
+        bool ok = mbar_wait_bounded(smem_u32(w_full), 0, abort_flag, p.err, kDevErrWaitFull);
+        int local = 0;
+        const uint32_t acc1 = tmem_base, acc2 = tmem_base + STK_N;
+        for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++local) {
+            if (!mbar_wait_bounded(smem_u32(acc_empty), (static_cast<uint32_t>(local) & 1u) ^ 1u, abort_flag,
+                                   p.err, kDevErrWaitAccEmpty))
+                break;
+            tc_fence_after();
+            for (int g = 0; g < Cg && ok; ++g) {
+                if (!mbar_wait_bounded(smem_u32(a_full + ab), aph, abort_flag, p.err, kDevErrWaitFull)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t a_row = smem_u32(smem + Q1_OFF_A + ab * A_BYTES);
+                    const uint32_t b_row = smem_u32(smem + Q1_OFF_B + (g >> 1) * STK_TILE) + (g & 1) * 64;
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const uint64_t a_hi = smem_desc_kmajor_sw128(a_row + u * 32);
+                        const uint64_t a_lo = smem_desc_kmajor_sw128(a_row + 64 + u * 32);
+                        const uint64_t b = smem_desc_kmajor_sw128(b_row + u * 32);
+                        const uint32_t acc = (g > 0 || u > 0) ? 1u : 0u;
+                        tc_mma_i8(acc1, a_hi, b, STK_IDESC_SU, acc);
+                        tc_mma_i8(acc2, a_lo, b, STK_IDESC_UU, acc);
+                    }
+                    tc_commit(smem_u32(a_empty + ab));
+                }
+                __syncwarp();
+                if (++ab == Q1_NA) { ab = 0; aph ^= 1u; }
+            }
+            if (!ok) break;
+            if (lane == 0) tc_commit(smem_u32(acc_full));
+            __syncwarp();
+        }
+        if (lane == 0) tc_commit(smem_u32(drain_bar));
+        __syncwarp();
+        volatile int no_abort = 0;
+        mbar_wait_bounded(smem_u32(drain_bar), 0, &no_abort, p.err, kDevErrWaitDrain);
+    } else {
+        // ---------------- workers (warps 2..17): quantise the input boxes, then the epilogue ----------------
+        const int wt = threadIdx.x - 64;
+        const int px = wt & (BM - 1);          // the pixel (limb-tile row) this thread quantises
+        const int cq = wt >> 7;                // its 16 channels: 16 cq .. 16 cq + 15
+        const int sw = px & 7;
+        const float inv_x = quant_inv(__ldg(p.amax_x));
+        const int quarter = warp & 3;
+        const int sub = (warp - 2) >> 2;
+        const int row = quarter * 32 + lane;
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        const double s = dequant_scale(__ldg(p.amax_x), __ldg(p.amax_w));
+        const int64_t plane = static_cast<int64_t>(p.OH) * p.OW;
+        const int f0 = sub * 16;
+        int rb = 0, ab = 0;
+        uint32_t rph = 0, aph = 0;
+        bool ok = true;
+        // dequantise the accumulators of tile t (the local-th of this CTA)
+        auto epilogue = [&](int t, int local) {
+            const int pt = t % p.pos_tiles;
+            const int n = t / p.pos_tiles;
+            if (!mbar_wait_bounded(smem_u32(acc_full), static_cast<uint32_t>(local) & 1u, abort_flag, p.err,
+                                   kDevErrWaitAccFull)) {
+                ok = false;
+                return;
+            }
+            tc_fence_after();
+            uint32_t h1[16], m1[16], m2[16], l2[16], s_hi, s_lo;
+            tmem_ld_32x32b_x16(t_row + f0, h1);
+            tmem_ld_32x32b_x16(t_row + 64 + f0, m1);
+            tmem_ld_32x32b_x16(t_row + STK_N + f0, m2);
+            tmem_ld_32x32b_x16(t_row + STK_N + 64 + f0, l2);
+            tmem_ld_32x32b_x1(t_row + 128, s_hi);
+            tmem_ld_32x32b_x1(t_row + STK_N + 128, s_lo);
+            tc_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(acc_empty));  // TMEM free for the next tile
+            const int64_t pix = static_cast<int64_t>(pt) * BM + row;
+            if (pix >= plane || f0 >= p.F) return;
+            __half* o = static_cast<__half*>(p.out) + (static_cast<int64_t>(n) * p.F + f0) * plane + pix;
+            const int nf = min(16, p.F - f0);
+            const uint32_t c_hi = 128u * s_hi, c_lo = 128u * s_lo;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const uint32_t hh = h1[j] - c_hi;
+                const uint32_t mid = m1[j] + m2[j] - c_lo;
+                __half h = __double2half(__dmul_rn(limb_acc_to_double(hh, mid, l2[j]), s));
+                if (p.bias != nullptr) h = __hadd(h, static_cast<const __half*>(p.bias)[f0 + j < p.F ? f0 + j : 0]);
+                if (j < nf) o[j * plane] = h;
+            }
+        };
+        int local = 0, prev_t = -1;
+        for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++local) {
+            for (int g = 0; g < Cg; ++g) {
+                if (!mbar_wait_bounded(smem_u32(raw_full + rb), rph, abort_flag, p.err, kDevErrWaitFull) ||
+                    !mbar_wait_bounded(smem_u32(a_empty + ab), aph ^ 1u, abort_flag, p.err, kDevErrWaitEmpty)) {
+                    ok = false;
+                    break;
+                }
+                // channels 16 cq .. 16 cq + 15 of this pixel: codes, then the
+                // hi limbs into 16-byte chunk cq and the lo limbs into chunk
+                // 4 + cq of the pixel's 128-byte row (swizzled by row & 7)
+                const __half* src = reinterpret_cast<const __half*>(smem + rb * Q1_RAW_BYTES) + (16 * cq) * BM + px;
+                uint32_t hw[4], lw[4];
+#pragma unroll
+                for (int w4 = 0; w4 < 4; ++w4) {
+                    uint32_t r[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        r[k] = quant_code_bits_clamped(__half2float(src[(4 * w4 + k) * BM]), inv_x);
+                    pack_codes4(r[0], r[1], r[2], r[3], hw[w4], lw[w4]);
+                }
+                uint8_t* arow = smem + Q1_OFF_A + ab * A_BYTES + px * KB;
+                *reinterpret_cast<uint4*>(arow + ((cq ^ sw) << 4)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                *reinterpret_cast<uint4*>(arow + (((4 + cq) ^ sw) << 4)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(smem_u32(raw_empty + rb));
+                    mbar_arrive(smem_u32(a_full + ab));
+                }
+                if (++rb == Q1_NRAW) { rb = 0; rph ^= 1u; }
+                if (++ab == Q1_NA) { ab = 0; aph ^= 1u; }
+            }
+            if (!ok) break;
+            // the previous tile's epilogue runs while the MMAs of this one do
+            if (prev_t >= 0) epilogue(prev_t, local - 1);
+            prev_t = t;
+        }
+        if (ok && prev_t >= 0) epilogue(prev_t, local - 1);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
 // ---- operand quantisation into 128-byte limb rows ---------------------------
 
 constexpr int XQ_W = 128;   // pixels per block pass
@@ -1137,6 +1395,75 @@ int launch_stk(const CUtensorMap& tx, const CUtensorMap& tw, const ConvWinParams
     return launch_status("conv2d stacked window implicit GEMM");
 }
 
+// 1x1, stride 1, no padding, groups 1, at most 64 filters and 256 channels,
+// fp16: the input
+// is quantised inside conv1x1_q_kernel (no limb pass); weights stacked as
+// for conv_stk_kernel into `ws`.
+int conv1x1_q(const void* x, const void* w, const void* bias, void* out, int64_t N, int64_t C, int64_t HW,
+              int64_t F, const float* amax_x, const float* amax_w, uint8_t* ws, int dev, cudaStream_t stream) {
+    const int64_t Cg = ceil_div(C, 64);
+    const int64_t npairs = ceil_div(Cg, 2);
+    const unsigned sgrid = static_cast<unsigned>(ceil_div(npairs * STK_N * 8, 256));
+    w_stack_kernel<__half><<<sgrid, 256, 0, stream>>>(static_cast<const __half*>(w), (int)F, (int)C, 1, (int)Cg,
+                                                      (int)npairs, amax_w, ws);
+    int rc = launch_status("conv2d 1x1 weight limbs");
+    if (rc) return rc;
+    EncodeTiledFn enc = tensor_map_encoder();
+    if (enc == nullptr) TK_FAIL(TK_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    CUtensorMap tx, tw;
+    {
+        const uint64_t rows = static_cast<uint64_t>(npairs * STK_N);
+        cuuint64_t dims[3] = {128, rows, 1};
+        cuuint64_t strides[2] = {128, 128 * rows};
+        cuuint32_t box[3] = {128, static_cast<cuuint32_t>(STK_N), 1};
+        cuuint32_t estr[3] = {1, 1, 1};
+        CUresult r = enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, ws, dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) TK_FAIL(TK_ERR_CUDA, "conv2d stacked weight tensor map failed (%d)", (int)r);
+    }
+    {
+        // NCHW fp16 as [N][C][HW]: boxes of 128 pixels x 64 channels; pixels
+        // past the plane and channels past C read as zero
+        cuuint64_t dims[3] = {static_cast<cuuint64_t>(HW), static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(N)};
+        cuuint64_t strides[2] = {static_cast<cuuint64_t>(HW * 2), static_cast<cuuint64_t>(C * HW * 2)};
+        cuuint32_t box[3] = {static_cast<cuuint32_t>(BM), 64, 1};
+        cuuint32_t estr[3] = {1, 1, 1};
+        CUresult r = enc(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(x), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) TK_FAIL(TK_ERR_CUDA, "conv2d 1x1 input tensor map failed (%d)", (int)r);
+    }
+    ConvWinParams p = {};
+    p.N = static_cast<int>(N);
+    p.F = static_cast<int>(F);
+    p.OH = 1;
+    p.OW = static_cast<int>(HW);
+    p.Hp = 1;
+    p.Wp = static_cast<int>(HW);
+    p.Cg = static_cast<int>(Cg);
+    p.taps = 1;
+    p.win_rows = BM;
+    p.pos_tiles = static_cast<int>(ceil_div(HW, BM));
+    p.tiles_f = 1;
+    p.tiles = static_cast<int>(N * p.pos_tiles);
+    p.amax_x = amax_x;
+    p.amax_w = amax_w;
+    p.bias = bias;
+    p.out = out;
+    p.err = device_error_word(dev);
+    static std::once_flag once[64];
+    static cudaError_t err[64];
+    const int slot = std::min(dev, 63);
+    std::call_once(once[slot], [&] {
+        err[slot] = cudaFuncSetAttribute(conv1x1_q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Q1_SMEM);
+    });
+    if (err[slot] != cudaSuccess) TK_FAIL(TK_ERR_CUDA, "conv smem attribute: %s", cudaGetErrorString(err[slot]));
+    const int grid = std::min(p.tiles, sm_count(dev));
+    conv1x1_q_kernel<<<grid, NUM_THREADS, Q1_SMEM, stream>>>(tx, tw, p);
+    return launch_status("conv2d 1x1 implicit GEMM (input quantised in the kernel)");
+}
+
 // The window variant applies when one window of 128 + max tap offset rows
 // fits a TMA box.
 bool window_fits(int64_t KH, int64_t KW, int64_t dh, int64_t dw, int64_t Wp) {
@@ -1166,6 +1493,10 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
     const int dev = current_device();
     const int64_t Cg = ceil_div(C, 64);
     const int64_t Hp = H + 2 * ph, Wp = W + 2 * pw;
+    if (dtype == TK_DTYPE_F16 && D == 1 && KD == 1 && KH == 1 && KW == 1 && ph == 0 && pw == 0 && F <= 64 &&
+        Cg <= Q1_NA && (H * W) % 8 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+        N * ceil_div(H * W, BM) < (1LL << 31) && N * C * H * W < (1LL << 40))
+        return conv1x1_q(x, w, bias, out, N, C, H * W, F, amax_x, amax_w, ws, dev, stream);
     // Window variant (input stored zero-padded, one window per channel group)
     // for up to 64 filters.  With 128-filter tiles the per-tap ring measured
     // faster (3x3 256->256 @14, batch 64: 77 vs 83 us).  A 1x1 filter has no

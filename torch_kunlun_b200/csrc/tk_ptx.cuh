@@ -96,6 +96,14 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     }
 }
 
+// Acquire load at GPU scope: sees every write released (or fenced) before
+// the store or atomic it reads from, on any SM.
+__device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // ---- thread-block clusters ----------------------------------------------------
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
