@@ -45,13 +45,15 @@ CASES = [
 
 
 def test_1x1_in_kernel_quantisation_non_finite():
-    """A NaN in the input makes its scale non-finite: every output is NaN,
-    on the path that quantises the input inside the 1x1 kernel too."""
-    x = torch.relu(rnd((2, 128, 16, 16), 43))
-    x[1, 127, 15, 15] = float("nan")
-    w = rnd((32, 128, 1, 1), 44, scale=0.1)
-    y = torch.nn.functional.conv2d(x.to(DEV), w.to(DEV)).cpu()
-    assert bool(torch.isnan(y).all())
+    """A NaN or an infinity in the input makes its scale non-finite: every
+    output is NaN, on the path that quantises the input inside the 1x1 kernel
+    too."""
+    for bad in (float("nan"), float("inf"), -float("inf")):
+        x = torch.relu(rnd((2, 128, 16, 16), 43))
+        x[1, 127, 15, 15] = bad
+        w = rnd((32, 128, 1, 1), 44, scale=0.1)
+        y = torch.nn.functional.conv2d(x.to(DEV), w.to(DEV)).cpu()
+        assert bool(torch.isnan(y).all()), bad
 
 
 @pytest.mark.parametrize("case", CASES)

@@ -43,7 +43,8 @@ size_t conv_tc_workspace(int64_t N, int64_t C, int64_t D, int64_t H, int64_t W, 
 int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, void* out, int64_t N,
             int64_t C, int64_t D, int64_t H, int64_t W, int64_t F, int64_t KD, int64_t KH, int64_t KW,
             int64_t pd, int64_t ph, int64_t pw, int64_t dd, int64_t dh, int64_t dw, int64_t OD, int64_t OH,
-            int64_t OW, const float* amax_x, const float* amax_w, uint8_t* ws, cudaStream_t stream);
+            int64_t OW, const float* amax_x, const float* amax_w, uint8_t* ws, cudaStream_t stream,
+            bool x_scale_own = false);
 
 namespace {
 
@@ -1075,7 +1076,7 @@ int tk_conv3d_q16(const tk_conv3d_desc_t* desc, void* workspace, size_t workspac
     if (is_implicit(g))
         return conv_tc(d.dtype, d.x, d.weight, d.bias, d.out, g.N, g.C, g.D, g.H, g.W, g.F, g.KD, g.KH,
                        g.KW, g.pd, g.ph, g.pw, g.dd, g.dh, g.dw, g.OD, g.OH, g.OW, ax, aw, ws + L.off_la,
-                       stream);
+                       stream, d.amax_x == nullptr);
     int8_t* la = reinterpret_cast<int8_t*>(ws + L.off_la);  // patches [N*groups][2][P][ld]
     int8_t* lb = reinterpret_cast<int8_t*>(ws + L.off_lb);  // weights [groups][2][F/g][ld]
     const int64_t fg = g.F / g.groups;

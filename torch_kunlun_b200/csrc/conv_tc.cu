@@ -375,6 +375,7 @@ struct ConvWinParams {
     const void* bias;
     void* out;
     unsigned* err;
+    int clamp_x;             // conv1x1_q_kernel: the input scale was supplied, clamp the codes
 };
 
 template <class C, int DT>
@@ -1028,6 +1029,7 @@ conv1x1_q_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
         const int row = quarter * 32 + lane;
         const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
         const double s = dequant_scale(__ldg(p.amax_x), __ldg(p.amax_w));
+        const bool s_finite = s <= 1.7976931348623157e308;
         const int64_t plane = static_cast<int64_t>(p.OH) * p.OW;
         const int f0 = sub * 16;
         int rb = 0, ab = 0;
@@ -1064,6 +1066,9 @@ conv1x1_q_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
                 const uint32_t hh = h1[j] - c_hi;
                 const uint32_t mid = m1[j] + m2[j] - c_lo;
                 __half h = __double2half(__dmul_rn(limb_acc_to_double(hh, mid, l2[j]), s));
+                // a non-finite scale (a NaN or an infinity in an operand) gives NaN
+                // everywhere, whatever the codes of the non-finite inputs were
+                h = s_finite ? h : __ushort_as_half(0x7E00);
                 if (p.bias != nullptr) h = __hadd(h, static_cast<const __half*>(p.bias)[f0 + j < p.F ? f0 + j : 0]);
                 if (j < nf) o[j * plane] = h;
             }
@@ -1081,13 +1086,25 @@ conv1x1_q_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
                 // 4 + cq of the pixel's 128-byte row (swizzled by row & 7)
                 const __half* src = reinterpret_cast<const __half*>(smem + rb * Q1_RAW_BYTES) + (16 * cq) * BM + px;
                 uint32_t hw[4], lw[4];
+                if (p.clamp_x) {
 #pragma unroll
-                for (int w4 = 0; w4 < 4; ++w4) {
-                    uint32_t r[4];
+                    for (int w4 = 0; w4 < 4; ++w4) {
+                        uint32_t r[4];
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        r[k] = quant_code_bits_clamped(__half2float(src[(4 * w4 + k) * BM]), inv_x);
-                    pack_codes4(r[0], r[1], r[2], r[3], hw[w4], lw[w4]);
+                        for (int k = 0; k < 4; ++k)
+                            r[k] = quant_code_bits_clamped(__half2float(src[(4 * w4 + k) * BM]), inv_x);
+                        pack_codes4(r[0], r[1], r[2], r[3], hw[w4], lw[w4]);
+                    }
+                } else {
+                    // the scale is this input's own max-abs: |v * inv| <= 32767.004,
+                    // and a non-finite input makes every output NaN whatever its codes
+#pragma unroll
+                    for (int w4 = 0; w4 < 4; ++w4) {
+                        uint32_t r[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) r[k] = quant_code_bits(__half2float(src[(4 * w4 + k) * BM]), inv_x);
+                        pack_codes4(r[0], r[1], r[2], r[3], hw[w4], lw[w4]);
+                    }
                 }
                 uint8_t* arow = smem + Q1_OFF_A + ab * A_BYTES + px * KB;
                 *reinterpret_cast<uint4*>(arow + ((cq ^ sw) << 4)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
@@ -1400,7 +1417,8 @@ int launch_stk(const CUtensorMap& tx, const CUtensorMap& tw, const ConvWinParams
 // is quantised inside conv1x1_q_kernel (no limb pass); weights stacked as
 // for conv_stk_kernel into `ws`.
 int conv1x1_q(const void* x, const void* w, const void* bias, void* out, int64_t N, int64_t C, int64_t HW,
-              int64_t F, const float* amax_x, const float* amax_w, uint8_t* ws, int dev, cudaStream_t stream) {
+              int64_t F, const float* amax_x, const float* amax_w, uint8_t* ws, int dev, cudaStream_t stream,
+              bool x_scale_own) {
     const int64_t Cg = ceil_div(C, 64);
     const int64_t npairs = ceil_div(Cg, 2);
     const unsigned sgrid = static_cast<unsigned>(ceil_div(npairs * STK_N * 8, 256));
@@ -1452,6 +1470,7 @@ int conv1x1_q(const void* x, const void* w, const void* bias, void* out, int64_t
     p.bias = bias;
     p.out = out;
     p.err = device_error_word(dev);
+    p.clamp_x = x_scale_own ? 0 : 1;
     static std::once_flag once[64];
     static cudaError_t err[64];
     const int slot = std::min(dev, 63);
@@ -1489,14 +1508,15 @@ size_t conv_tc_workspace(int64_t N, int64_t C, int64_t D, int64_t H, int64_t W, 
 int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, void* out, int64_t N,
             int64_t C, int64_t D, int64_t H, int64_t W, int64_t F, int64_t KD, int64_t KH, int64_t KW,
             int64_t pd, int64_t ph, int64_t pw, int64_t dd, int64_t dh, int64_t dw, int64_t OD, int64_t OH,
-            int64_t OW, const float* amax_x, const float* amax_w, uint8_t* ws, cudaStream_t stream) {
+            int64_t OW, const float* amax_x, const float* amax_w, uint8_t* ws, cudaStream_t stream,
+            bool x_scale_own) {
     const int dev = current_device();
     const int64_t Cg = ceil_div(C, 64);
     const int64_t Hp = H + 2 * ph, Wp = W + 2 * pw;
     if (dtype == TK_DTYPE_F16 && D == 1 && KD == 1 && KH == 1 && KW == 1 && ph == 0 && pw == 0 && F <= 64 &&
         Cg <= Q1_NA && (H * W) % 8 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
         N * ceil_div(H * W, BM) < (1LL << 31) && N * C * H * W < (1LL << 40))
-        return conv1x1_q(x, w, bias, out, N, C, H * W, F, amax_x, amax_w, ws, dev, stream);
+        return conv1x1_q(x, w, bias, out, N, C, H * W, F, amax_x, amax_w, ws, dev, stream, x_scale_own);
     // Window variant (input stored zero-padded, one window per channel group)
     // for up to 64 filters.  With 128-filter tiles the per-tap ring measured
     // faster (3x3 256->256 @14, batch 64: 77 vs 83 us).  A 1x1 filter has no
