@@ -1087,12 +1087,16 @@ def run_tp(args):
                        "reduce": mode, "overlap": OVERLAP.get(mode, "none (one GPU)"),
                        "l2": "inputs (x 256 MiB, weights 1.4 GiB over the ranks) larger than L2"},
             "roofline": roofline("tensor", achieved, peak, "TOPS", int16_peak_source(peaks, "burst"),
-                                 None, None, kernel="qgemm_tc_kernel (gate, up, down GEMMs of one rank)",
+                                 *(ncu_traffic(f"qgemm_tp_mlp_gate_{TP_T}x{TP_F}x{TP_H}.md") if world == 1
+                                   else (None, None)),
+                                 kernel="qgemm_tc_kernel (gate, up, down GEMMs of one rank)",
                                  ops_per_step=gemm_ops, gemm_ms=gemm_ms,
                                  frac_of_sustained=achieved / peaks["int16_sustained"],
                                  step_frac_of_sustained=(gemm_ops / (ms / 1000) / 1e12) / peaks["int16_sustained"],
                                  note="achieved = the rank's GEMM ops / the three GEMM kernels' event-timed "
-                                      "durations (max over ranks); traffic: see profiles/"),
+                                      "durations (max over ranks); traffic: DRAM bytes of one gate GEMM launch "
+                                      "(16384 x 28672 x 8192, one GPU) from the committed ncu summary, null for "
+                                      "the smaller per-rank shards of N > 1"),
             "e2e": {"value": TP_OPS / (e2e / 1000) / 1e12, "unit": "TOPS", "ms_per_step": e2e,
                     "h2d_bytes_per_step": h2d_b * world, "d2h_bytes_per_step": d2h_b * world,
                     "per_rank_bytes": {"h2d": h2d_b, "d2h": d2h_b},
