@@ -540,6 +540,7 @@ depthwise_fused_kernel(const T* __restrict__ x, const T* __restrict__ w, const T
         atomicAdd(sync + 2, 1u);
         const uint64_t t0 = globaltimer_ns();
         while (ld_acquire_gpu_u32(sync + 2) < gridDim.x) {
+            __nanosleep(128);
             if (globaltimer_ns() - t0 > kWaitLimitNs) {
                 atomicCAS(err, 0u, static_cast<unsigned>(kDevErrWaitCluster));
                 break;
@@ -685,25 +686,26 @@ int depthwise_fused_launch(const tk_conv3d_desc_t& d, const ConvGeom& g, unsigne
                        : reinterpret_cast<const void*>(depthwise_fused_kernel<float, 1, 7>);
     }
     TK_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
-    // every block must be resident at once: when the row kernel's planes per
-    // block give more blocks than fit, give each block more planes (threads
-    // then take several rows), within the shared-memory spans
+    // Every block must be resident at once.  A block's threads take its
+    // output rows in rounds of kDwRowThreads, so whole rounds keep them
+    // balanced: planes per block = the most whole planes in r rounds, for the
+    // fewest rounds r whose grid fits (within the shared-memory spans).
     int64_t blocks = 0;
     size_t smem = 0;
-    for (int attempt = 0; attempt < 2; ++attempt) {
-        if (static_cast<int64_t>(ppb) * std::max(hw, ohw) >= 65536 || ppb * phw > kDwRowSpan ||
-            ppb * taps > kDwRowTaps)
-            return TK_ERR_UNSUPPORTED;
-        smem = depthwise_fused_smem(g, ppb, esize);
-        if (smem > 96 * 1024) return TK_ERR_UNSUPPORTED;
+    bool fits = false;
+    for (int r = 1; r <= 8 && !fits; ++r) {
+        const int64_t cand = std::max<int64_t>(1, (static_cast<int64_t>(r) * kDwRowThreads) / g.OH);
+        if (cand * std::max(hw, ohw) >= 65536 || cand * phw > kDwRowSpan || cand * taps > kDwRowTaps) break;
+        smem = depthwise_fused_smem(g, static_cast<int>(cand), esize);
+        if (smem > 96 * 1024) break;
         int per_sm = 0;
         TK_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kDwRowThreads, smem));
         const int64_t cap = static_cast<int64_t>(per_sm) * sm_count(dev);
-        blocks = ceil_div(planes, ppb);
-        if (cap > 0 && blocks <= cap) break;
-        if (attempt == 1 || cap <= 0) return TK_ERR_UNSUPPORTED;
-        ppb = static_cast<int>(ceil_div(planes, cap));
+        ppb = static_cast<int>(cand);
+        blocks = ceil_div(planes, cand);
+        fits = cap > 0 && blocks <= cap;
     }
+    if (!fits) return TK_ERR_UNSUPPORTED;
     TK_CUDA_TRY(cudaMemsetAsync(sync, 0, 4 * sizeof(unsigned), stream));
     ConvGeom gg = g;
     int ppb_arg = ppb;

@@ -875,10 +875,12 @@ conv_stk_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__
 constexpr int Q1_NRAW = 4;                         // fp16 input boxes in flight
 constexpr int Q1_NA = 4;                           // limb tiles in flight
 constexpr int Q1_RAW_BYTES = 64 * BM * 2;          // 64 channels x 128 pixels fp16
-// A tile's channel groups must all fit the limb-tile ring: the workers
+// A tile's channel groups must all fit the limb-tile ring (the workers
 // dequantise the previous tile only after quantising the current one, so the
-// MMAs of the current tile cannot free limb tiles before its last group is in.
-constexpr int Q1_MAX_PAIRS = Q1_NA / 2;            // C <= 64 * Q1_NA
+// MMAs of the current tile cannot free limb tiles before its last group is
+// in), and its stacked filter block must stay resident: C <= 256.
+constexpr int Q1_MAX_PAIRS = 2;
+static_assert(2 * Q1_MAX_PAIRS <= Q1_NA, "every channel group of a tile fits the limb-tile ring");
 constexpr int Q1_OFF_A = Q1_NRAW * Q1_RAW_BYTES;
 constexpr int Q1_OFF_B = Q1_OFF_A + Q1_NA * A_BYTES;
 constexpr int Q1_OFF_BAR = Q1_OFF_B + Q1_MAX_PAIRS * STK_TILE;
@@ -1514,7 +1516,7 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
     const int64_t Cg = ceil_div(C, 64);
     const int64_t Hp = H + 2 * ph, Wp = W + 2 * pw;
     if (dtype == TK_DTYPE_F16 && D == 1 && KD == 1 && KH == 1 && KW == 1 && ph == 0 && pw == 0 && F <= 64 &&
-        Cg <= Q1_NA && (H * W) % 8 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+        Cg <= 2 * Q1_MAX_PAIRS && (H * W) % 8 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
         N * ceil_div(H * W, BM) < (1LL << 31) && N * C * H * W < (1LL << 40))
         return conv1x1_q(x, w, bias, out, N, C, H * W, F, amax_x, amax_w, ws, dev, stream, x_scale_own);
     // Window variant (input stored zero-padded, one window per channel group)
