@@ -210,10 +210,17 @@ __device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b,
 
 // ---- tensor-core kernel --------------------------------------------------------
 
-template <class C, int DT, int ACT>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+// EW: epilogue warps.  8 for the general epilogue; 16 (four per TMEM lane
+// quarter) for fp16 outputs on the fast path (no alpha, vector bias / addend
+// / stores, no split reduction, N a multiple of 16) with 128x128 tiles, whose
+// epilogue is compiled without the general path so it fits the smaller
+// register budget (BERT FFN1 16384x3072x768 with GELU: 249 -> 224 us).
+template <class C, int DT, int ACT, int EW = NUM_EPI_WARPS>
+__global__ void __launch_bounds__(64 + 32 * EW, 1)
 qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const TileParams tp, const EpiParams ep) {
+    constexpr bool FAST_ONLY = EW != NUM_EPI_WARPS;
+    static_assert(!FAST_ONLY || DT == 0, "the 16-warp epilogue is the fp16 fast path");
     constexpr int STAGES = C::STAGES;
     constexpr int STAGE_BYTES = C::STAGE_BYTES;
     constexpr int BN = C::BN;
@@ -243,7 +250,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         }
         for (int i = 0; i < NBUF; ++i) {
             mbar_init(smem_u32(acc_full + i), 1);
-            mbar_init(smem_u32(acc_empty + i), NUM_EPI_WARPS);
+            mbar_init(smem_u32(acc_empty + i), EW);
         }
         mbar_init(smem_u32(drain_bar), 1);
         *abort_flag = 0;
@@ -399,11 +406,11 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             int64_t out_row;
             void* const obase = row_out(ep, b, m, out_row);
 #pragma unroll 1
-            for (int c = half; c < BN / 16; c += 2) {  // 16-column chunks, alternating halves
+            for (int c = half; c < BN / 16; c += EW / 4) {  // 16-column chunks, the quarter's warps alternating
                 const int64_t n0 = static_cast<int64_t>(nt) * BN + c * 16;
                 const bool full = n0 + 16 <= ep.N;
                 // fp16 fast path: whole chunk, no alpha, vector bias / addend / store
-                const bool fast = DT == 0 && fast_ok && row_ok && full;
+                const bool fast = FAST_ONLY || (DT == 0 && fast_ok && row_ok && full);
                 uint4 add_q[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
                 if (fast && has_add) {  // issued before the TMEM loads to hide its latency
                     const uint4* src = reinterpret_cast<const uint4*>(
@@ -417,7 +424,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 tmem_ld_32x32b_x16(t_buf + 2 * BN + c * 16, ll);
                 tc_wait_ld();
                 if (!row_ok || n0 >= ep.N) continue;
-                if (tp.acc64 != nullptr) {
+                if (!FAST_ONLY && tp.acc64 != nullptr) {
                     // K chunk of a split reduction: add its exact int64 sums
                     const int64_t slice = tp.acc_mod ? b % tp.acc_mod : b;
                     unsigned long long* dst = tp.acc64 + (slice * ep.M + m) * ep.N + n0;
@@ -470,6 +477,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                         continue;
                     }
                 }
+                if constexpr (!FAST_ONLY) {
                 float v[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
@@ -558,6 +566,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     for (int j = 0; j < 16; ++j)
                         if (full || n0 + j < ep.N) store_t(obase, ep.dtype, out_row + (n0 + j) * ep.out_sn, v[j]);
                 }
+                }  // !FAST_ONLY
             }
             tc_fence_before();
             __syncwarp();
@@ -775,32 +784,54 @@ struct RowScatter {
 
 enum class Path { TensorCore, Simt };
 
-template <class C, int DT, int ACT>
+template <class C, int DT, int ACT, int EW = NUM_EPI_WARPS>
 int launch_one(int dev, int grid, const CUtensorMap& tmA, const CUtensorMap& tmB,
                const TileParams& tp, const EpiParams& ep, cudaStream_t stream) {
     static std::once_flag attr_once[64];
     if (dev >= 0 && dev < 64) {
         std::call_once(attr_once[dev], [] {
-            cudaFuncSetAttribute(qgemm_tc_kernel<C, DT, ACT>,
+            cudaFuncSetAttribute(qgemm_tc_kernel<C, DT, ACT, EW>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         });
     }
-    qgemm_tc_kernel<C, DT, ACT><<<grid, NUM_THREADS, C::SMEM, stream>>>(tmA, tmB, tp, ep);
+    qgemm_tc_kernel<C, DT, ACT, EW><<<grid, 64 + 32 * EW, C::SMEM, stream>>>(tmA, tmB, tp, ep);
     return TK_OK;
+}
+
+template <class C, int DT, int EW>
+int dispatch_act_ew(int act, int dev, int grid, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                    const TileParams& tp, const EpiParams& ep, cudaStream_t stream) {
+    switch (act) {
+        case TK_ACT_NONE: return launch_one<C, DT, TK_ACT_NONE, EW>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_RELU: return launch_one<C, DT, TK_ACT_RELU, EW>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_GELU: return launch_one<C, DT, TK_ACT_GELU, EW>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_GELU_TANH:
+            return launch_one<C, DT, TK_ACT_GELU_TANH, EW>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_SILU: return launch_one<C, DT, TK_ACT_SILU, EW>(dev, grid, tmA, tmB, tp, ep, stream);
+        default: TK_FAIL(TK_ERR_INVALID_ARG, "qgemm: bad act %d", act);
+    }
+}
+
+// Whether the whole problem takes the fp16 fast epilogue (every chunk full,
+// no alpha, vector bias / addend / stores, no split reduction): then the
+// 16-warp epilogue runs.
+bool fast_epilogue(const TileParams& tp, const EpiParams& ep) {
+    return ep.dtype == 0 && tp.acc64 == nullptr && ep.vec_store && ep.alpha == 1.0f && ep.dbg == nullptr &&
+           (ep.bias == nullptr || (ep.bias_vec && ep.bias_mod == 0)) &&
+           (ep.addend == nullptr || ep.beta == 0.0f || (ep.add_vec && ep.beta == 1.0f)) && ep.N % 16 == 0;
 }
 
 template <class C, int DT>
 int dispatch_act(int act, int dev, int grid, const CUtensorMap& tmA, const CUtensorMap& tmB,
                  const TileParams& tp, const EpiParams& ep, cudaStream_t stream) {
-    switch (act) {
-        case TK_ACT_NONE: return launch_one<C, DT, TK_ACT_NONE>(dev, grid, tmA, tmB, tp, ep, stream);
-        case TK_ACT_RELU: return launch_one<C, DT, TK_ACT_RELU>(dev, grid, tmA, tmB, tp, ep, stream);
-        case TK_ACT_GELU: return launch_one<C, DT, TK_ACT_GELU>(dev, grid, tmA, tmB, tp, ep, stream);
-        case TK_ACT_GELU_TANH:
-            return launch_one<C, DT, TK_ACT_GELU_TANH>(dev, grid, tmA, tmB, tp, ep, stream);
-        case TK_ACT_SILU: return launch_one<C, DT, TK_ACT_SILU>(dev, grid, tmA, tmB, tp, ep, stream);
-        default: TK_FAIL(TK_ERR_INVALID_ARG, "qgemm: bad act %d", act);
+    // Short reductions only (128x128 tiles, K < 2048), where the epilogue
+    // outweighs the tile's MMAs; with K >= 2048 the 16-warp epilogue measured
+    // no faster (2048x4096x4096) or slower (the TP MLP's K = 8192 GEMMs, 3 %).
+    if constexpr (DT == 0 && C::BN == 128) {
+        if (fast_epilogue(tp, ep))
+            return dispatch_act_ew<C, DT, 2 * NUM_EPI_WARPS>(act, dev, grid, tmA, tmB, tp, ep, stream);
     }
+    return dispatch_act_ew<C, DT, NUM_EPI_WARPS>(act, dev, grid, tmA, tmB, tp, ep, stream);
 }
 
 // Tile configuration for a problem: 128x160 tiles for K >= 2048, else
