@@ -316,7 +316,7 @@ __device__ __forceinline__ void unpack_vec(const uint4& u, float* o) {
 }
 
 template <typename TI, typename TO, int NV>
-__global__ void __launch_bounds__(256) softmax_rows_kernel(const TI* __restrict__ x, TO* __restrict__ y,
+__global__ void __launch_bounds__(256, NV <= 3 ? 4 : 2) softmax_rows_kernel(const TI* __restrict__ x, TO* __restrict__ y,
                                                            int64_t rows, int cols) {
     constexpr int VEC = 16 / sizeof(TI);
     const int lane = threadIdx.x & 31;
