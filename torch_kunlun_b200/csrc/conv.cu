@@ -433,7 +433,7 @@ depthwise_rows_kernel(const T* __restrict__ x, const T* __restrict__ w, const T*
 // sync[0], sync[1]: fp32 magnitude bits of max |x| and max |w| (atomicMax,
 // NaN above everything, as the amax kernels); sync[2]: blocks arrived.
 struct DwMagic {
-    uint32_t hw, w, taps, ohw, ow;  // floor(2^32 / d) + 1 for i / d with i, d < 2^16
+    uint32_t hw, w, taps, ohw, ow, h, oh;  // floor(2^32 / d) + 1 for i / d with i, d < 2^16
 };
 
 __device__ __forceinline__ int round_up_dev(int v, int a) { return (v + a - 1) / a * a; }
@@ -554,25 +554,44 @@ depthwise_fused_kernel(const T* __restrict__ x, const T* __restrict__ w, const T
     const float invx = quant_inv(ax), invw = quant_inv(aw);
     const double s = dequant_scale(ax, aw);
 
-    // ---- phase 2: codes into zero-padded planes, filter codes
-    for (int i = threadIdx.x; i < np * PHW + kDwRowOut + KW; i += blockDim.x) xs[i] = 0;
-    __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int pp = div_magic(i, mg.hw), r = i - pp * HW;
-        const int ih = div_magic(r, mg.w), iw = r - ih * W;
-        xs[pp * PHW + (ih + ph) * Wp + iw + pw] = static_cast<int16_t>(quant_one(ldx<T>(raw, i), invx));
+    // ---- phase 2: codes into zero-padded planes, filter codes.  The scales
+    // are the operands' own max-abs, so every |v * inv| <= 32767.004 and the
+    // magic-number codes need no clamp; a non-finite scale (a NaN or an
+    // infinity in an operand) turns every output into NaN below, whatever
+    // the codes of the non-finite values were.
+    // One thread per input row writes the whole padded row (left and right
+    // padding included); the rows next to the top and bottom padding also
+    // zero those padding rows; thread 0 zeroes the slack after the last plane.
+    for (int rr = threadIdx.x; rr < np * H; rr += blockDim.x) {
+        const int pp = div_magic(rr, mg.h), ih = rr - pp * H;
+        const T* src = raw + pp * HW + ih * W;
+        int16_t* plane = xs + pp * PHW;
+        int16_t* dst = plane + (ih + ph) * Wp;
+        for (int k = 0; k < pw; ++k) {
+            dst[k] = 0;
+            dst[pw + W + k] = 0;
+        }
+        for (int iw = 0; iw < W; ++iw)
+            dst[pw + iw] = static_cast<int16_t>(quant_code_bits(ldx<T>(src, iw), invx) & 0xFFFFu);
+        if (ih == 0)
+            for (int k = 0; k < ph * Wp; ++k) plane[k] = 0;
+        if (ih == H - 1)
+            for (int k = 0; k < ph * Wp; ++k) plane[(ph + H) * Wp + k] = 0;
     }
+    if (threadIdx.x == 0)
+        for (int k = 0; k < kDwRowOut + KW; ++k) xs[np * PHW + k] = 0;
     // filter codes split as 256 * hi + lo (hi in [-128, 127], lo in [0, 255])
     // so both partial sums below stay int32: |x| * 128 and |x| * 255 over at
     // most 49 taps are below 2^29
     for (int i = threadIdx.x; i < np * taps; i += blockDim.x) {
-        const int q = quant_one(wf[i], invw);
+        const int q = static_cast<int16_t>(quant_code_bits(wf[i], invw) & 0xFFFFu);
         wsq[i] = (q >> 8) * 65536 + (q & 255);  // hi in the upper half, lo in the lower
     }
+    const bool s_finite = s <= 1.7976931348623157e308;
     __syncthreads();
     // ---- each thread a whole output row, into the staged output span
     for (int row = threadIdx.x; row < np * OH; row += blockDim.x) {
-        const int pp = row / OH, oh = row - pp * OH;
+        const int pp = div_magic(row, mg.oh), oh = row - pp * OH;
         const int16_t* xr = xs + pp * PHW + oh * Wp;
         const int* wp = wsq + pp * taps;
         int c = c0 + pp;
@@ -608,6 +627,7 @@ depthwise_fused_kernel(const T* __restrict__ x, const T* __restrict__ w, const T
                     const double dl = __hiloint2double(0x43300000, acc_lo[j] ^ static_cast<int>(0x80000000u)) -
                                       4503601774854144.0;
                     float v = round_t_from_double(__dmul_rn(__fma_rn(dh, 256.0, dl), s), DT);
+                    v = s_finite ? v : __int_as_float(0x7FC00000);
                     if (bias != nullptr) v = round_t(__fadd_rn(v, bv), DT);
                     store_t(orow, DT, ow0 + j, v);
                 }
@@ -715,6 +735,8 @@ int depthwise_fused_launch(const tk_conv3d_desc_t& d, const ConvGeom& g, unsigne
     mg.taps = magic_div(g.KH * g.KW);
     mg.ohw = magic_div(ohw);
     mg.ow = magic_div(g.OW);
+    mg.h = magic_div(g.H);
+    mg.oh = magic_div(g.OH);
     unsigned* err = device_error_word(dev);
     const void* xp = d.x;
     const void* wp = d.weight;
