@@ -1669,6 +1669,122 @@ attn_quant_kernel(QuantParams p) {
     }
 }
 
+// The same quantisation with the whole slice staged in shared memory (fp16
+// slices of at most 32 KB elements, e.g. 512 x 64): the slice crosses HBM
+// once -- loaded with eight 16-byte loads in flight per thread while its
+// max-abs is folded -- and the codes are formed from shared memory.  Codes,
+// layouts and the max-abs convention are those of attn_quant_kernel.
+constexpr int QS_MAX_BYTES = 64 * 1024;
+
+__global__ void __launch_bounds__(QT_THREADS)
+attn_quant_staged_kernel(QuantParams p) {
+    extern __shared__ __align__(16) uint8_t qsm[];
+    __shared__ unsigned red[QT_THREADS / 32];
+    const __half* raw = reinterpret_cast<const __half*>(qsm);
+    const int bh = blockIdx.x, z = blockIdx.y;
+    const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+    const __half* x = static_cast<const __half*>(p.src[z]) + b * p.st[z][0] + h * p.st[z][1];
+    const int64_t sr = p.st[z][2];
+    const int rows = p.rows[z], cols = p.cols[z];
+    const int pcs = cols / 8;  // 16-byte pieces per row (cols % 8 == 0, rows 16-byte aligned)
+    const int n = rows * pcs;
+    unsigned mx = 0;  // max of |x| bit patterns: NaN dominates, then Inf
+    for (int it0 = threadIdx.x; it0 < n; it0 += 8 * QT_THREADS) {
+        uint4 u[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int it = it0 + k * QT_THREADS;
+            if (it < n) {
+                const int r = it / pcs, pc = it - (it / pcs) * pcs;
+                u[k] = __ldg(reinterpret_cast<const uint4*>(x + r * sr + pc * 8));
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int it = it0 + k * QT_THREADS;
+            if (it < n) {
+                reinterpret_cast<uint4*>(qsm)[it] = u[k];
+                const __half2* h2 = reinterpret_cast<const __half2*>(&u[k]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(h2[e]);
+                    mx = max(mx, max(__float_as_uint(fabsf(f.x)), __float_as_uint(fabsf(f.y))));
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = 0;
+#pragma unroll
+    for (int w = 0; w < QT_THREADS / 32; ++w) mx = max(mx, red[w]);
+    const float amax = __uint_as_float(mx);
+    if (threadIdx.x == 0) {
+        p.amax[z * p.BH + bh] = amax;
+        if (z == 0) p.amax_p[bh] = 0u;
+    }
+    const float inv = quant_inv(amax);
+    uint8_t* out = p.dst[z] + bh * p.slice[z];
+    const int64_t ld = p.ld[z];
+    if (z < 2) {
+        // rows x (ld / 2) values in 16-value pieces: hi at g*128 + c%64, lo at +64
+        const int pieces = static_cast<int>(ld / 32);
+        for (int it = threadIdx.x; it < rows * pieces; it += QT_THREADS) {
+            const int r = it / pieces, pc = it - (it / pieces) * pieces;
+            const int c0 = pc * 16;
+            uint32_t cb[16];
+            if (inv != 0.0f && c0 + 16 <= cols) {
+                const uint4* src = reinterpret_cast<const uint4*>(raw + r * cols + c0);
+                const uint4 a = src[0], b2 = src[1];
+                const __half2* ha = reinterpret_cast<const __half2*>(&a);
+                const __half2* hb = reinterpret_cast<const __half2*>(&b2);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 fa = __half22float2(ha[e]), fb = __half22float2(hb[e]);
+                    cb[2 * e] = quant_code_bits(fa.x, inv);
+                    cb[2 * e + 1] = quant_code_bits(fa.y, inv);
+                    cb[8 + 2 * e] = quant_code_bits(fb.x, inv);
+                    cb[8 + 2 * e + 1] = quant_code_bits(fb.y, inv);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    cb[e] = quant_code_bits(
+                        (inv != 0.0f && c0 + e < cols) ? __half2float(raw[r * cols + c0 + e]) : 0.0f, inv);
+            }
+            uint4 hi, lo;
+            pack_codes4(cb[0], cb[1], cb[2], cb[3], hi.x, lo.x);
+            pack_codes4(cb[4], cb[5], cb[6], cb[7], hi.y, lo.y);
+            pack_codes4(cb[8], cb[9], cb[10], cb[11], hi.z, lo.z);
+            pack_codes4(cb[12], cb[13], cb[14], cb[15], hi.w, lo.w);
+            uint8_t* dst = out + r * ld + (c0 / 64) * 128 + (c0 % 64);
+            *reinterpret_cast<uint4*>(dst) = hi;
+            *reinterpret_cast<uint4*>(dst + 64) = lo;
+        }
+    } else {
+        // v^T: row e holds, per key tile kt, [hi of keys 64kt.. | lo of the same]
+        const int n_kt = static_cast<int>(ld / 128);
+        for (int it = threadIdx.x; it < n_kt * cols * 4; it += QT_THREADS) {
+            const int kt = it / (cols * 4), rem = it - kt * (cols * 4);
+            const int e = rem >> 2, pc = rem & 3;
+            int q[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const int j = kt * BKEY + pc * 16 + k;
+                const float v = (inv != 0.0f && j < rows) ? __half2float(raw[j * cols + e]) : 0.0f;
+                q[k] = static_cast<int>(static_cast<int16_t>(quant_code_bits(v, inv) & 0xFFFFu));
+            }
+            uint4 hi, lo;
+            pack16(q, hi, lo);
+            uint8_t* dst = out + e * ld + kt * 128 + pc * 16;
+            *reinterpret_cast<uint4*>(dst) = hi;
+            *reinterpret_cast<uint4*>(dst + 64) = lo;
+        }
+    }
+}
+
 // ---- host side ---------------------------------------------------------------
 
 struct Layout {
@@ -1889,10 +2005,19 @@ int tk_sdpa_q16(const tk_sdpa_desc_t* desc, void* workspace, size_t workspace_by
     qp.amax = reinterpret_cast<float*>(ws + l.off_amax);
     qp.amax_p = reinterpret_cast<unsigned*>(ws + l.off_amax_p);
     const dim3 qgrid(static_cast<unsigned>(l.BH), 3);
-    if (d.dtype == TK_DTYPE_F16)
+    // fp16 slices whose rows are contiguous 16-byte aligned runs and that fit
+    // 64 KB are staged in shared memory (one HBM read)
+    const int64_t stage_bytes = std::max(d.l * d.e, std::max(d.s * d.e, d.s * d.ev)) * 2;
+    const bool staged = d.dtype == TK_DTYPE_F16 && stage_bytes <= QS_MAX_BYTES && qp.vec[0] && qp.vec[1] && qp.vec[2];
+    if (staged) {
+        rc = set_smem<attn_quant_staged_kernel>(QS_MAX_BYTES, dev);
+        if (rc) return rc;
+        attn_quant_staged_kernel<<<qgrid, QT_THREADS, static_cast<size_t>(stage_bytes), stream>>>(qp);
+    } else if (d.dtype == TK_DTYPE_F16) {
         attn_quant_kernel<__half><<<qgrid, QT_THREADS, 0, stream>>>(qp);
-    else
+    } else {
         attn_quant_kernel<float><<<qgrid, QT_THREADS, 0, stream>>>(qp);
+    }
     rc = launch_status("attention quantise");
     if (rc) return rc;
 
