@@ -1,7 +1,7 @@
 """Benchmark of torch_kunlun's int16-quantised dense-op path on B200.
 
 Headline, at every GPU count (N = 1 included): the tensor-parallel
-SiLU-gated MLP of BASELINE's multi-GPU config -- x fp16 [16384, 8192] ~N(0,1),
+SiLU-gated MLP (the multi-GPU workload) -- x fp16 [16384, 8192] ~N(0,1),
 gate/up weights [28672, 8192] split by output rows (column-parallel), down
 weight [8192, 28672] split by input columns (row-parallel), all ~N(0,0.02);
 h = T(silu(x Wg^T)) * (x Wu^T), y = sum over ranks of h_r Wd_r^T, the partial
