@@ -6,28 +6,37 @@
 // q @ k^T (csrc/ops_nn.cpp:199-221), mul.Scalar by the scale, add of the
 // causal / additive mask, softmax (csrc/ops_nn.cpp:73-83) and a per-slice
 // quantised bmm with v, each a kernel writing and re-reading [L, S] tensors.
-// Here three kernels do the same arithmetic:
+// Here the same arithmetic runs as:
 //
-//   attn_quant_kernel   per (batch, head) slice of q, k, v: max-abs, then
+//   attn_quant_kernel / attn_quant_staged_kernel
+//                       per (batch, head) slice of q, k, v: max-abs, then
 //                       int16 quantisation into int8 limb rows laid out for
 //                       the tensor cores (v transposed); zeroes the slice's
-//                       probability amax.
-//   attn_stats_kernel   S = q k^T on the tensor cores (three limb
-//                       accumulators in TMEM); on the CUDA cores the exact
-//                       dequantised, scaled, masked scores (each step rounded
-//                       to T as the reference's separate launches round),
-//                       written once as T, the row max and sum of
+//                       probability amax.  The staged form holds an fp16
+//                       slice of up to 64 KB in shared memory (one HBM read).
+//   attn_fused_kernel   fp16 slices of at most 512 queries and keys, head dim
+//                       <= 128: one persistent thread-block cluster per slice
+//                       keeps the scores in shared memory, exchanges the
+//                       slice's largest probability through distributed
+//                       shared memory and runs P v on the tensor cores
+//                       (details above the kernel).
+//   attn_stats_kernel   longer slices and fp32: S = q k^T on the tensor cores
+//                       (three limb accumulators in TMEM); on the CUDA cores
+//                       the exact dequantised, scaled, masked scores (each
+//                       step rounded to T as the reference's separate launches
+//                       round), written once as T, the row max and sum of
 //                       exponentials, and the slice's largest probability --
 //                       the per-slice amax with which the reference's second
 //                       bmm quantises P.
-//   attn_out_kernel     reads the scores back by TMA, forms
+//   attn_out_kernel     reads those scores back by TMA, forms
 //                       P = T(exp(s - m) / l), quantises it with the slice
 //                       scale into shared memory as limb tiles and
 //                       accumulates P v on the tensor cores; the epilogue
 //                       dequantises O and stores it through its strides.
-// Compared with the composition, the softmax pass, the probability tensor
-// (written, read for its amax, read again to quantise) and its limb planes
-// never reach HBM, and the score epilogue runs once.
+// Both paths give identical bits.  Compared with the composition, the softmax
+// pass, the probability tensor (written, read for its amax, read again to
+// quantise) and its limb planes never reach HBM, and the score epilogue runs
+// once; the fused path keeps the scores on chip as well.
 //
 // Limb layout ("64-interleaved"): an int16 row of 64*G values is stored as G
 // chunks of 128 bytes, chunk g = [hi of values 64g..64g+63 | lo of the same],
@@ -39,8 +48,8 @@
 //   HH += hi*hi,  MID += hi*lo + lo*hi,  LL += lo*lo
 // which recombine exactly as 65536*HH + 256*MID + LL.
 //
-// CTA roles of both tensor-core kernels (320 threads, one CTA per SM,
-// persistent over 128-row query tiles):
+// CTA roles of the statistics and output kernels (576 threads, one CTA per
+// SM, persistent over 128-row query tiles):
 //   warp 0      TMA producer (4-stage ring);
 //   warp 1      TMEM owner and MMA issuer;
 //   warps 2..17 CUDA-core work: warp w owns TMEM lane quarter w % 4 (32
