@@ -8,8 +8,12 @@
 // convolution is handled as the 3-D one with D = KD = 1.
 //
 // Paths:
-//   * 2-D, groups == C == F/mult (depthwise): a CUDA-core kernel, one output
-//     per thread, exact int64 accumulation of the KHxKW taps.  HBM-bound.
+//   * 2-D, groups == C == F/mult (depthwise): CUDA-core kernels with exact
+//     integer sums of the KHxKW taps.  Multiplier 1, unit stride and
+//     dilation: one cooperative launch that also forms both scales
+//     (depthwise_fused_kernel) when its grid is resident at once, else the
+//     amax launch and the row kernel; other depthwise shapes use the plane,
+//     flat or per-output kernels.
 //   * groups == 1, stride 1: implicit GEMM on the tensor cores (conv_tc.cu),
 //     no patch matrix in HBM.
 //   * otherwise a GEMM per (image, group) on the tensor-core limb kernel:

@@ -37,6 +37,11 @@
 //                    window per channel group that every tap reads at its
 //                    own row offset; when the filter block fits (<= 96 KB)
 //                    it stays resident in shared memory.
+//   conv_stk_kernel  the window kernel with both weight limbs stacked along
+//                    N (two N = 144 MMAs per sub-block instead of four).
+//   conv1x1_q_kernel 1x1 filters (fp16, <= 64 filters, <= 256 channels):
+//                    no limb pass -- the input is read as fp16 NCHW boxes
+//                    and quantised into the limb tiles inside the kernel.
 // Every wait is bounded; no TMA multicast is used.
 #include <cuda.h>
 
