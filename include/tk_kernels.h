@@ -130,6 +130,12 @@ typedef struct {
      * x_maxptr / w_maxptr, csrc/ops.cpp:227). */
     const float* amax_a;
     const float* amax_b;
+    /* Optional (device, one float): receives max |out| over the whole output
+     * after the epilogue (NaN above everything), the scale the next quantised
+     * op on out would compute -- folded into the epilogue for fp16 outputs on
+     * the vector path, else one extra pass over out (which must then be
+     * contiguous).  NULL: not computed. */
+    float* amax_out;
 } tk_qgemm_desc_t;
 
 TK_API size_t tk_qgemm_workspace_size(const tk_qgemm_desc_t* desc);

@@ -48,6 +48,41 @@ def test_linear_residual_equals_linear_then_add():
     assert torch.equal(fused.view(torch.int16), unfused.view(torch.int16))
 
 
+@pytest.mark.parametrize("dtype,M,K,N,act,bias,res,poison", [
+    (torch.float16, 200, 256, 96, "gelu", True, False, None),     # folded into the fp16 epilogue
+    (torch.float16, 1030, 768, 3072, "gelu", True, False, None),
+    (torch.float16, 64, 128, 48, "none", False, True, None),
+    (torch.float16, 64, 128, 40, "relu", True, False, None),      # N % 16 != 0: separate pass
+    (torch.float32, 77, 96, 64, "none", True, True, None),        # fp32: separate pass
+    (torch.float16, 130, 64, 32, "none", True, False, float("inf")),
+    (torch.float16, 130, 64, 32, "none", True, False, float("nan")),
+])
+def test_linear_amax_out_equals_amax_of_output(dtype, M, K, N, act, bias, res, poison):
+    x, w = rnd((M, K), 21, dtype=dtype), rnd((N, K), 22, 0.05, dtype=dtype)
+    if poison is not None:
+        x[M // 2, 3] = poison
+    b = rnd((N,), 23, 0.02, dtype=dtype).to(DEV) if bias else None
+    r = rnd((M, N), 24, dtype=dtype).to(DEV) if res else None
+    xd, wd = x.to(DEV), w.to(DEV)
+    a_out = torch.full((1,), -1.0, dtype=torch.float32, device=DEV)
+    y = ops.linear(xd, wd, b, act=act, residual=r, amax_out=a_out)
+    y_plain = ops.linear(xd, wd, b, act=act, residual=r)
+    bits = lambda t: t.cpu().view(torch.int16 if t.element_size() == 2 else torch.int32)
+    assert torch.equal(bits(y), bits(y_plain))
+    assert torch.equal(bits(a_out), bits(ops.amax(y)))
+
+
+def test_ffn_scale_handoff_keeps_values():
+    h, w1, b1 = rnd((384, 256), 31), rnd((1024, 256), 32, 0.05), rnd((1024,), 33, 0.02)
+    w2, b2 = rnd((256, 1024), 34, 0.03), rnd((256,), 35, 0.02)
+    hd, w1d, b1d, w2d, b2d = (t.to(DEV) for t in (h, w1, b1, w2, b2))
+    a1 = torch.empty(1, dtype=torch.float32, device=DEV)
+    f1 = ops.linear(hd, w1d, b1d, act="gelu", amax_out=a1)
+    handed = ops.linear(f1, w2d, b2d, residual=hd, amax_x=a1).cpu()
+    own = ops.linear(f1, w2d, b2d, residual=hd).cpu()
+    assert torch.equal(handed.view(torch.int16), own.view(torch.int16))
+
+
 def _reference_block(x, w, mask, heads, eps):
     """torch CPU fp32 composition of the same encoder layers."""
     f = {k: v.float() for k, v in vars(w).items()}

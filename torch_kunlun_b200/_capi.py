@@ -51,6 +51,7 @@ class QGemmDesc(ctypes.Structure):
         ("per_slice_scales", ctypes.c_int),
         ("amax_a", ctypes.c_void_p),
         ("amax_b", ctypes.c_void_p),
+        ("amax_out", ctypes.c_void_p),
     ]
 
 

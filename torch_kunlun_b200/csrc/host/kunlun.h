@@ -97,7 +97,9 @@ void xccl_barrier(int device);
 // ---- fused ops exposed to Python ----
 at::Tensor linear_act(const at::Tensor& input, const at::Tensor& weight,
                       const std::optional<at::Tensor>& bias, int64_t act,
-                      const std::optional<at::Tensor>& residual);
+                      const std::optional<at::Tensor>& residual,
+                      const std::optional<at::Tensor>& amax_x,
+                      const std::optional<at::Tensor>& amax_out);
 at::Tensor silu_mul(const at::Tensor& gate, const at::Tensor& up);
 std::tuple<at::Tensor, at::Tensor> silu_mul_amax(const at::Tensor& gate, const at::Tensor& up);
 at::Tensor quantize_limbs(const at::Tensor& x, const at::Tensor& amax);

@@ -91,7 +91,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("xccl_barrier", &xccl_barrier);
 
     m.def("linear_act", &linear_act, py::arg("input"), py::arg("weight"),
-          py::arg("bias") = py::none(), py::arg("act") = 0, py::arg("residual") = py::none());
+          py::arg("bias") = py::none(), py::arg("act") = 0, py::arg("residual") = py::none(),
+          py::arg("amax_x") = py::none(), py::arg("amax_out") = py::none());
     m.def("silu_mul", &silu_mul);
     m.def("silu_mul_amax", &silu_mul_amax);
     m.def("quantize_limbs", &quantize_limbs);

@@ -53,7 +53,7 @@ at::Tensor dense_slices(const at::Tensor& t, bool whole_block) {
 void run_qgemm(const at::Tensor& a_in, const at::Tensor& b_in, at::Tensor& out,
                const std::optional<at::Tensor>& bias, const at::Tensor* addend, double alpha,
                double beta, int act, bool per_slice, const float* amax_a = nullptr,
-               const float* amax_b = nullptr) {
+               const float* amax_b = nullptr, float* amax_out = nullptr) {
     const int dev = out.device().index();
     DeviceScope g(dev);
     const bool whole = !per_slice;
@@ -103,6 +103,7 @@ void run_qgemm(const at::Tensor& a_in, const at::Tensor& b_in, at::Tensor& out,
     d.per_slice_scales = per_slice ? 1 : 0;
     d.amax_a = amax_a;
     d.amax_b = amax_b;
+    d.amax_out = amax_out;
     const size_t ws_bytes = tk_qgemm_workspace_size(&d);
     at::Tensor ws = workspace(ws_bytes, out.device());
     check_tk(tk_qgemm(&d, aligned_base(ws), ws_bytes, current_stream(dev)), "tk_qgemm");
@@ -481,15 +482,28 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable
 
 }  // namespace
 
-// y = act(x @ W^T + b) for x [..., K], W [N, K] in one call.
+// y = act(x @ W^T + b) [+ residual] for x [..., K], W [N, K] in one call.
+// amax_x (1-element fp32) replaces x's own max |x| as its scale; amax_out
+// (1-element fp32) receives max |y|, the scale of the GEMM that consumes y.
 at::Tensor linear_act(const at::Tensor& input, const at::Tensor& weight,
                       const std::optional<at::Tensor>& bias, int64_t act,
-                      const std::optional<at::Tensor>& residual) {
+                      const std::optional<at::Tensor>& residual,
+                      const std::optional<at::Tensor>& amax_x,
+                      const std::optional<at::Tensor>& amax_out) {
     TORCH_CHECK(input.dim() >= 1 && weight.dim() == 2, "kunlun linear: bad ranks");
     check_operand(weight, input, "linear");
     const int64_t K = input.size(-1);
     TORCH_CHECK(weight.size(1) == K, "kunlun linear: in_features mismatch (", K, " vs ",
                 weight.size(1), ")");
+    auto scale_tensor = [&](const std::optional<at::Tensor>& t, const char* what) -> float* {
+        if (!t.has_value() || !t->defined()) return nullptr;
+        TORCH_CHECK(t->scalar_type() == at::kFloat && t->numel() >= 1 && t->is_contiguous() &&
+                        t->device() == input.device(),
+                    "kunlun linear: ", what, " must be a 1-element fp32 kunlun tensor");
+        return t->data_ptr<float>();
+    };
+    const float* sx = scale_tensor(amax_x, "amax_x");
+    float* so = scale_tensor(amax_out, "amax_out");
     const int64_t N = weight.size(0);
     at::Tensor x2 = input.reshape({-1, K});
     std::vector<int64_t> out_shape = input.sizes().vec();
@@ -504,7 +518,9 @@ at::Tensor linear_act(const at::Tensor& input, const at::Tensor& weight,
             r3 = residual->reshape({1, x2.size(0), N});
         }
         run_qgemm(x2.unsqueeze(0), weight.unsqueeze(0), o3, bias, r3.defined() ? &r3 : nullptr,
-                  1.0, r3.defined() ? 1.0 : 0.0, static_cast<int>(act), true);
+                  1.0, r3.defined() ? 1.0 : 0.0, static_cast<int>(act), true, sx, nullptr, so);
+    } else if (so != nullptr) {
+        amax_out->zero_();
     }
     return out.view(out_shape);
 }
@@ -642,7 +658,7 @@ namespace {
 
 at::Tensor linear_fwd(const at::Tensor& input, const at::Tensor& weight,
                       const std::optional<at::Tensor>& bias) {
-    return linear_act(input, weight, bias, TK_ACT_NONE, std::nullopt);
+    return linear_act(input, weight, bias, TK_ACT_NONE, std::nullopt, std::nullopt, std::nullopt);
 }
 
 // Autograd entry for linear: without gradients the fused kernel runs below

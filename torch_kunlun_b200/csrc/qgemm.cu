@@ -122,6 +122,7 @@ struct EpiParams {
     bool bias_vec;  // bias is 16-byte aligned: vector loads per 16-column chunk
     bool add_vec;   // addend rows contiguous and 16-byte aligned: vector loads
     int32_t* dbg;  // [3][M][N] raw accumulators of slice 0, or null
+    unsigned* amax_out;  // fp32 magnitude bits of max |out| (atomicMax), or null; fast path only
     // Row scatter (batch 1): rows [q*R, (q+1)*R) go to row_dest[q] at local
     // row m - q*R (row stride out_sm) instead of out; R = row_dest_rows > 0.
     // The destinations may be other GPUs' memory (CUDA IPC over NVLink).
@@ -386,6 +387,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                              (!has_bias || (ep.bias_vec && ep.bias_mod == 0)) &&
                              (!has_add || (ep.add_vec && ep.beta == 1.0f));
         const void* bias_base = ep.bias;
+        uint32_t out_mag2 = 0;  // max |out| of this thread's fast-path outputs, two 16-bit lanes
         int local = 0;
         for (int t = blockIdx.x; t < tp.num_tiles; t += gridDim.x, ++local) {
             int b, mt, nt, ks;
@@ -469,6 +471,12 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                                 const float2 f = __half22float2(hv[j]);
                                 hv[j] = __floats2half2_rn(act_t<ACT>(f.x, DT), act_t<ACT>(f.y, DT));
                             }
+                        }
+                        if (ep.amax_out != nullptr) {
+                            // magnitudes as 16-bit patterns: NaN > Inf > finite
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                out_mag2 = __vmaxu2(out_mag2, *reinterpret_cast<const uint32_t*>(&hv[j]) & 0x7FFF7FFFu);
                         }
                         uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(obase) + out_row + n0);
                         const uint4* w = reinterpret_cast<const uint4*>(hv);
@@ -571,6 +579,19 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(acc_empty + buf));
+        }
+        if (ep.amax_out != nullptr) {
+            unsigned hmag = max(out_mag2 & 0xFFFFu, out_mag2 >> 16);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) hmag = max(hmag, __shfl_xor_sync(0xffffffffu, hmag, o));
+            if (lane == 0 && hmag != 0u) {
+                // widened to the fp32 magnitude bits (NaN canonical), as the amax kernels
+                const unsigned bits = ((hmag & 0x7C00u) == 0x7C00u && (hmag & 0x3FFu) != 0u)
+                                          ? 0x7FC00000u
+                                          : (__float_as_uint(__half2float(__ushort_as_half(
+                                                 static_cast<unsigned short>(hmag)))) & 0x7FFFFFFFu);
+                atomicMax(ep.amax_out, bits);
+            }
         }
         // stores into other GPUs' memory are ordered before anything this
         // GPU does after the kernel
@@ -769,6 +790,7 @@ EpiParams make_epi(const tk_qgemm_desc_t& d, const float* amax_a, const float* a
                  d.add_sn == 1 && (d.add_sm * static_cast<int64_t>(es)) % 16 == 0 &&
                  (d.add_sb * static_cast<int64_t>(es)) % 16 == 0;
     ep.dbg = dbg;
+    ep.amax_out = nullptr;
     for (int i = 0; i < kMaxRowDests; ++i) ep.row_dest[i] = nullptr;
     ep.row_dest_rows = 0;
     ep.row_dest_n = 0;
@@ -815,10 +837,14 @@ int dispatch_act_ew(int act, int dev, int grid, const CUtensorMap& tmA, const CU
 // Whether the whole problem takes the fp16 fast epilogue (every chunk full,
 // no alpha, vector bias / addend / stores, no split reduction): then the
 // 16-warp epilogue runs.
-bool fast_epilogue(const TileParams& tp, const EpiParams& ep) {
-    return ep.dtype == 0 && tp.acc64 == nullptr && ep.vec_store && ep.alpha == 1.0f && ep.dbg == nullptr &&
+bool fast_epilogue_ep(const EpiParams& ep) {
+    return ep.dtype == 0 && ep.vec_store && ep.alpha == 1.0f && ep.dbg == nullptr &&
            (ep.bias == nullptr || (ep.bias_vec && ep.bias_mod == 0)) &&
            (ep.addend == nullptr || ep.beta == 0.0f || (ep.add_vec && ep.beta == 1.0f)) && ep.N % 16 == 0;
+}
+
+bool fast_epilogue(const TileParams& tp, const EpiParams& ep) {
+    return tp.acc64 == nullptr && fast_epilogue_ep(ep);
 }
 
 template <class C, int DT>
@@ -966,6 +992,25 @@ int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t str
         ep.vec_store = vec;
     }
 
+    // max |out| for the caller: folded into the fp16 vector epilogue, or one
+    // pass over the finished output
+    bool amax_folded = false;
+    if (d.amax_out != nullptr) {
+        TK_CHECK_ARG(scatter == nullptr, "qgemm: amax_out with scattered rows is not supported");
+        amax_folded = path == Path::TensorCore && d.k > 0 && !(L.split && dbg == nullptr) && fast_epilogue_ep(ep);
+        if (amax_folded) {
+            TK_CUDA_TRY(cudaMemsetAsync(d.amax_out, 0, sizeof(float), stream));
+            ep.amax_out = reinterpret_cast<unsigned*>(d.amax_out);
+        } else {
+            TK_CHECK_ARG(d.out_sm == d.n && (d.batch <= 1 || d.out_sb == d.m * d.n),
+                         "qgemm: amax_out needs a contiguous output on this path");
+        }
+    }
+    auto out_amax_pass = [&]() -> int {
+        if (d.amax_out == nullptr || amax_folded) return TK_OK;
+        return amax_launch(d.dtype, d.out, 1, 0, d.batch * d.m * d.n, d.amax_out, stream);
+    };
+
     if (path == Path::Simt || d.k == 0) {
         dim3 grid(static_cast<unsigned>(ceil_div(d.n, 128)), static_cast<unsigned>(d.m),
                   static_cast<unsigned>(d.batch));
@@ -973,7 +1018,8 @@ int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t str
                      "qgemm_simt: m must be <= 65535");
         if (d.m > 65535) TK_FAIL(TK_ERR_UNSUPPORTED, "qgemm: K=0 with m > 65535");
         qgemm_simt_kernel<<<grid, 128, 0, stream>>>(la, lb, d.batch, d.k, L.ld, ep);
-        return launch_status("qgemm_simt");
+        rc = launch_status("qgemm_simt");
+        return rc ? rc : out_amax_pass();
     }
 
     if (L.split && dbg == nullptr && scatter == nullptr) {
@@ -983,9 +1029,11 @@ int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t str
                                     stream));
         rc = launch_tc(d, la, lb, L.ld, ep, stream, 0, sa);
         if (rc) return rc;
-        return launch_finish(reinterpret_cast<const long long*>(sa.acc64), d.batch, ep, stream);
+        rc = launch_finish(reinterpret_cast<const long long*>(sa.acc64), d.batch, ep, stream);
+        return rc ? rc : out_amax_pass();
     }
-    return launch_tc(d, la, lb, L.ld, ep, stream);
+    rc = launch_tc(d, la, lb, L.ld, ep, stream);
+    return rc ? rc : out_amax_pass();
 }
 
 }  // namespace
@@ -1005,6 +1053,7 @@ int qgemm_limbs_acc64(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* 
     if (rc) return rc;
     if (d.batch == 0 || d.m == 0 || d.n == 0 || d.k == 0) return TK_OK;
     TK_CHECK_ARG(acc64 != nullptr && la != nullptr && lb != nullptr, "qgemm_acc64: NULL pointer");
+    TK_CHECK_ARG(d.amax_out == nullptr, "qgemm_acc64: amax_out is not supported");
     const int64_t ld = static_cast<int64_t>(round_up(static_cast<size_t>(d.k), 16));
     EpiParams ep = make_epi(d, nullptr, nullptr, nullptr);
     SplitAcc sa;
@@ -1020,6 +1069,7 @@ int qgemm_acc64_finish(const tk_qgemm_desc_t& d, const long long* acc64, int64_t
                        const float* amax_a, const float* amax_b, int64_t out_sn, cudaStream_t stream) {
     int rc = validate(d);
     if (rc) return rc;
+    TK_CHECK_ARG(d.amax_out == nullptr, "qgemm_acc64_finish: amax_out is not supported");
     EpiParams ep = make_epi(d, amax_a, amax_b, nullptr);
     ep.out_sn = out_sn;
     ep.scale_stride = 0;
@@ -1037,6 +1087,7 @@ int qgemm_limbs_ex(const tk_qgemm_desc_t& d, const int8_t* la, const int8_t* lb,
     if (rc) return rc;
     if (d.batch == 0 || d.m == 0 || d.n == 0) return TK_OK;
     TK_CHECK_ARG(d.k > 0, "qgemm: K must be positive");
+    TK_CHECK_ARG(d.amax_out == nullptr, "qgemm_limbs_ex: amax_out is not supported");
     const int64_t ld = static_cast<int64_t>(round_up(static_cast<size_t>(d.k), 16));
     EpiParams ep = make_epi(d, amax_a, amax_b, nullptr);
     ep.out_sn = out_sn;
@@ -1078,6 +1129,7 @@ int tk_qgemm_from_limbs(const tk_qgemm_desc_t* desc, const int8_t* a_limbs, cons
     if (d.batch == 0 || d.m == 0 || d.n == 0) return TK_OK;
     TK_CHECK_ARG(d.k > 0, "qgemm_from_limbs: K must be positive");
     TK_CHECK_ARG(a_limbs && b_limbs && amax_a && amax_b, "qgemm_from_limbs: NULL pointer");
+    TK_CHECK_ARG(d.amax_out == nullptr, "qgemm_from_limbs: amax_out is not supported");
     TK_CHECK_ARG(reinterpret_cast<uintptr_t>(a_limbs) % 16 == 0 &&
                      reinterpret_cast<uintptr_t>(b_limbs) % 16 == 0,
                  "qgemm_from_limbs: limb planes must be 16-byte aligned");

@@ -12,7 +12,9 @@ applied in the GEMM epilogue in the reference's order (linear rounds to T,
 then the bias add, then the residual add, then gelu, each rounded to T), so
 the block's values equal the unfused sequence linear -> add -> add / gelu.
 The Q, K and V heads are strided views of the QKV projection (no copies), and
-the attention output is read back as [tokens, hidden] through a view.
+the attention output is read back as [tokens, hidden] through a view.  The
+FFN1 GEMM hands max |f1| (the per-tensor scale FFN2 quantises f1 with) out of
+its epilogue, so FFN2 does not read f1 an extra time for it.
 """
 
 from __future__ import annotations
@@ -84,8 +86,9 @@ def encoder_block(x: torch.Tensor, w: EncoderWeights, mask: Optional[torch.Tenso
     ctx = ctx.transpose(1, 2).reshape(B * L, H)
     a = ops.linear(ctx, w.w_o, w.b_o, residual=x2)                # x + attn_out
     h = F.layer_norm(a, (H,), w.ln1_w, w.ln1_b, eps)
-    f1 = ops.linear(h, w.w_1, w.b_1, act="gelu")
-    f2 = ops.linear(f1, w.w_2, w.b_2, residual=h)                 # h + ffn_out
+    a1 = torch.empty(1, dtype=torch.float32, device=x.device)
+    f1 = ops.linear(h, w.w_1, w.b_1, act="gelu", amax_out=a1)     # a1 = max |f1|
+    f2 = ops.linear(f1, w.w_2, w.b_2, residual=h, amax_x=a1)      # h + ffn_out
     y = F.layer_norm(f2, (H,), w.ln2_w, w.ln2_b, eps)
     return y.view(B, L, H)
 

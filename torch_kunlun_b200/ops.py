@@ -21,11 +21,19 @@ ACT = {"none": 0, "relu": 1, "gelu": 2, "gelu_tanh": 3, "silu": 4}
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
-           act: str = "none", residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+           act: str = "none", residual: Optional[torch.Tensor] = None,
+           amax_x: Optional[torch.Tensor] = None,
+           amax_out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """act(x @ w^T + b) [+ residual]: with a residual the epilogue adds it
     after the bias (rounded to T), giving the values of linear followed by a
-    separate add (csrc/ops.cpp:480-495 then csrc/ops.cpp:117-149)."""
-    return _C.linear_act(x, weight, bias, ACT[act], residual)
+    separate add (csrc/ops.cpp:480-495 then csrc/ops.cpp:117-149).
+
+    amax_x (1-element fp32) is x's per-tensor scale when the caller already
+    has it (skips the pass over x); amax_out (1-element fp32, written)
+    receives max |y| — folded into the fp16 epilogue where it applies, one
+    pass over y otherwise — so the GEMM that consumes y skips its own pass.
+    """
+    return _C.linear_act(x, weight, bias, ACT[act], residual, amax_x, amax_out)
 
 
 def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
