@@ -433,9 +433,17 @@ depthwise_rows_kernel(const T* __restrict__ x, const T* __restrict__ w, const T*
 // contribution, then quantises from shared memory, convolves and stores the
 // block's contiguous span of the output with 16-byte vectors.  The input
 // crosses HBM once (the separate amax pass read it twice) and the op is one
-// launch after a 16-byte memset of the scale words and the barrier counter.
+// launch after a memset of the scale words and the barrier words.
 // sync[0], sync[1]: fp32 magnitude bits of max |x| and max |w| (atomicMax,
-// NaN above everything, as the amax kernels); sync[2]: blocks arrived.
+// NaN above everything, as the amax kernels); sync[kDwSyncCount]: blocks
+// arrived; sync[kDwSyncFlag]: set by the last block to arrive.  The three
+// live on separate 128-byte lines, so the blocks polling the flag do not
+// slow the arrivals' atomics.
+constexpr int kDwSyncCount = 32;
+constexpr int kDwSyncFlag = 64;
+constexpr int kDwSyncWords = kDwSyncFlag + 1;
+constexpr int kDwMaxThreads = 512;
+
 struct DwMagic {
     uint32_t hw, w, taps, ohw, ow, h, oh;  // floor(2^32 / d) + 1 for i / d with i, d < 2^16
 };
@@ -471,7 +479,7 @@ __device__ __forceinline__ unsigned block_max_bits(unsigned v, unsigned* red) {
 }
 
 template <typename T, int DT, int KW>
-__global__ void __launch_bounds__(kDwRowThreads)
+__global__ void __launch_bounds__(kDwMaxThreads)
 depthwise_fused_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ bias,
                        T* __restrict__ out, ConvGeom g, int ppb, DwMagic mg, unsigned* sync, unsigned* err) {
     extern __shared__ __align__(16) uint8_t dsm[];
@@ -539,15 +547,22 @@ depthwise_fused_kernel(const T* __restrict__ x, const T* __restrict__ w, const T
     // ---- grid-wide barrier (every block is resident: cooperative launch)
     if (threadIdx.x == 0) {
         if (mx != 0u) atomicMax(sync, mx);
-        if (mw != 0u) atomicMax(sync + 1, mw);
+        // every channel's filter lies in the first C planes, so the blocks
+        // holding those planes carry max |w|
+        if (mw != 0u && pl0 < C) atomicMax(sync + 1, mw);
         __threadfence();
-        atomicAdd(sync + 2, 1u);
-        const uint64_t t0 = globaltimer_ns();
-        while (ld_acquire_gpu_u32(sync + 2) < gridDim.x) {
-            __nanosleep(128);
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                atomicCAS(err, 0u, static_cast<unsigned>(kDevErrWaitCluster));
-                break;
+        if (atomicAdd(sync + kDwSyncCount, 1u) == gridDim.x - 1) {
+            // the last block: every other block's maxima are visible here
+            __threadfence();
+            st_release_gpu_u32(sync + kDwSyncFlag, 1u);
+        } else {
+            const uint64_t t0 = globaltimer_ns();
+            while (ld_acquire_gpu_u32(sync + kDwSyncFlag) == 0u) {
+                __nanosleep(64);
+                if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                    atomicCAS(err, 0u, static_cast<unsigned>(kDevErrWaitCluster));
+                    break;
+                }
             }
         }
         red[0] = ld_acquire_gpu_u32(sync);
@@ -696,7 +711,7 @@ int depthwise_fused_launch(const tk_conv3d_desc_t& d, const ConvGeom& g, unsigne
     if (ppb == 0 || g.KH * g.KW > 64) return TK_ERR_UNSUPPORTED;
     const int64_t planes = g.N * g.C;
     const int64_t hw = g.H * g.W, ohw = g.OH * g.OW;
-    const int64_t phw = (g.H + 2 * g.ph) * (g.W + 2 * g.pw), taps = g.KH * g.KW;
+    const int64_t taps = g.KH * g.KW;
     const size_t esize = d.dtype == TK_DTYPE_F16 ? 2 : 4;
     const int dev = current_device();
     const void* fn = nullptr;
@@ -710,27 +725,49 @@ int depthwise_fused_launch(const tk_conv3d_desc_t& d, const ConvGeom& g, unsigne
                        : reinterpret_cast<const void*>(depthwise_fused_kernel<float, 1, 7>);
     }
     TK_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
-    // Every block must be resident at once.  A block's threads take its
-    // output rows in rounds of kDwRowThreads, so whole rounds keep them
-    // balanced: planes per block = the most whole planes in r rounds, for the
-    // fewest rounds r whose grid fits (within the shared-memory spans).
+    // Every block must be resident at once.  Preferred: a balanced grid, the
+    // same number k of blocks on every SM (planes per block = planes / (k x
+    // SMs), rounded up) with enough threads that each block's input and
+    // output rows take two rounds of its threads.  Else the planes per block
+    // fill whole rounds of kDwRowThreads threads, for the fewest rounds r
+    // whose grid fits.  Both within the shared-memory spans.
+    const int sms = sm_count(dev);
+    const int64_t rows_pp = std::max(g.H, g.OH);
+    // the kernel's magic-number divisions hold for indices below 2^16; its
+    // spans are all in dynamic shared memory
+    auto spans_ok = [&](int64_t cand) {
+        return cand * std::max(hw, ohw) < 65536 && cand * taps < 65536 &&
+               depthwise_fused_smem(g, static_cast<int>(cand), esize) <= 96 * 1024;
+    };
     int64_t blocks = 0;
     size_t smem = 0;
+    int threads = kDwRowThreads;
     bool fits = false;
+    for (int k = 2; k <= 4 && !fits; ++k) {
+        const int64_t cand = ceil_div(planes, static_cast<int64_t>(k) * sms);
+        const int64_t t = static_cast<int64_t>(round_up(static_cast<size_t>(ceil_div(cand * rows_pp, 2)), 32));
+        if (t > kDwMaxThreads || !spans_ok(cand)) continue;
+        smem = depthwise_fused_smem(g, static_cast<int>(cand), esize);
+        int per_sm = 0;
+        TK_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, static_cast<int>(t), smem));
+        ppb = static_cast<int>(cand);
+        threads = static_cast<int>(t);
+        blocks = ceil_div(planes, cand);
+        fits = per_sm > 0 && blocks <= static_cast<int64_t>(per_sm) * sms;
+    }
     for (int r = 1; r <= 8 && !fits; ++r) {
         const int64_t cand = std::max<int64_t>(1, (static_cast<int64_t>(r) * kDwRowThreads) / g.OH);
-        if (cand * std::max(hw, ohw) >= 65536 || cand * phw > kDwRowSpan || cand * taps > kDwRowTaps) break;
+        if (!spans_ok(cand)) break;
         smem = depthwise_fused_smem(g, static_cast<int>(cand), esize);
-        if (smem > 96 * 1024) break;
         int per_sm = 0;
         TK_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kDwRowThreads, smem));
-        const int64_t cap = static_cast<int64_t>(per_sm) * sm_count(dev);
         ppb = static_cast<int>(cand);
+        threads = kDwRowThreads;
         blocks = ceil_div(planes, cand);
-        fits = cap > 0 && blocks <= cap;
+        fits = per_sm > 0 && blocks <= static_cast<int64_t>(per_sm) * sms;
     }
     if (!fits) return TK_ERR_UNSUPPORTED;
-    TK_CUDA_TRY(cudaMemsetAsync(sync, 0, 4 * sizeof(unsigned), stream));
+    TK_CUDA_TRY(cudaMemsetAsync(sync, 0, kDwSyncWords * sizeof(unsigned), stream));
     ConvGeom gg = g;
     int ppb_arg = ppb;
     DwMagic mg;
@@ -748,7 +785,7 @@ int depthwise_fused_launch(const tk_conv3d_desc_t& d, const ConvGeom& g, unsigne
     void* op = d.out;
     void* args[] = {const_cast<void**>(&xp), const_cast<void**>(&wp), const_cast<void**>(&bp), &op, &gg, &ppb_arg,
                     &mg, &sync, &err};
-    TK_CUDA_TRY(cudaLaunchCooperativeKernel(fn, dim3(static_cast<unsigned>(blocks)), dim3(kDwRowThreads), args,
+    TK_CUDA_TRY(cudaLaunchCooperativeKernel(fn, dim3(static_cast<unsigned>(blocks)), dim3(threads), args,
                                             smem, stream));
     return launch_status("conv2d depthwise (fused scales)");
 }

@@ -381,6 +381,9 @@ struct ConvWinParams {
     void* out;
     unsigned* err;
     int clamp_x;             // conv1x1_q_kernel: the input scale was supplied, clamp the codes
+    const __half* w;         // conv1x1_q_kernel: fp16 weights [F][C], stacked in the kernel
+    int C;                   // conv1x1_q_kernel: input channels
+    int w_vec;               // conv1x1_q_kernel: 16-byte weight loads (C % 8 == 0, aligned)
 };
 
 template <class C, int DT>
@@ -894,9 +897,61 @@ static_assert(Q1_OFF_A % 1024 == 0 && Q1_OFF_B % 1024 == 0, "swizzled tiles on 1
 static_assert(Q1_SMEM <= 227 * 1024, "fits one CTA's shared memory");
 static_assert(NUM_EPI_WARPS == 16, "four worker warps per lane quarter");
 
+// The stacked filter block of conv1x1_q_kernel (the layout of
+// w_stack_kernel, swizzled as the MMAs read it) written by the 512 worker
+// threads into `stk`: 16-byte piece `pc8` of row n of pair `pair`, one piece
+// per thread at a time.  Out of line, so its temporaries do not crowd the
+// registers of the quantise / epilogue loop.
+__device__ __noinline__ void stack_weights_1x1(uint8_t* stk, const __half* w, const float* amax_w, int F, int C,
+                                               bool w_vec, int npairs, int Cg, int wt) {
+    const float inv_w = quant_inv(__ldg(amax_w));
+    const int pieces = npairs * STK_N * 8;
+    for (int it = wt; it < pieces; it += NUM_EPI_WARPS * 32) {
+        const int pc8 = it & 7, r = it >> 3;
+        const int n = r % STK_N, pair = r / STK_N;
+        const int kb = 2 * pair + (pc8 >> 2);  // the channel group
+        const int c0 = kb * 64 + (pc8 & 3) * 16;
+        uint32_t word[4];
+        if (n >= 128) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) word[j] = 0x01010101u;
+        } else {
+            const int f = n & 63;
+            const bool live = kb < Cg && f < F;
+            const __half* wrow = w + static_cast<int64_t>(f) * C + c0;
+            uint4 u0 = make_uint4(0, 0, 0, 0), u1 = make_uint4(0, 0, 0, 0);
+            const bool vec = live && w_vec && c0 + 16 <= C;
+            if (vec) {
+                u0 = __ldg(reinterpret_cast<const uint4*>(wrow));
+                u1 = __ldg(reinterpret_cast<const uint4*>(wrow) + 1);
+            }
+            const uint32_t wd[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t b = 0;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int c = 4 * j + e;
+                    int v = 0;
+                    if (vec)
+                        v = quant_one(__half2float(__ushort_as_half(
+                                          static_cast<unsigned short>(wd[c >> 1] >> (16 * (c & 1))))),
+                                      inv_w);
+                    else if (live && c0 + c < C) v = quant_one(__half2float(__ldg(wrow + c)), inv_w);
+                    const uint32_t byte = n < 64 ? static_cast<uint32_t>(((v >> 8) + 128) & 0xFF)
+                                                 : static_cast<uint32_t>(v & 0xFF);
+                    b |= byte << (8 * e);
+                }
+                word[j] = b;
+            }
+        }
+        *reinterpret_cast<uint4*>(stk + pair * STK_TILE + n * KB + ((pc8 ^ (n & 7)) << 4)) =
+            make_uint4(word[0], word[1], word[2], word[3]);
+    }
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-conv1x1_q_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-                 const ConvWinParams p) {
+conv1x1_q_kernel(const __grid_constant__ CUtensorMap tmX, const ConvWinParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -928,11 +983,10 @@ conv1x1_q_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
         mbar_init(smem_u32(acc_full), 1);
         mbar_init(smem_u32(acc_empty), NUM_EPI_WARPS);
         mbar_init(smem_u32(drain_bar), 1);
-        mbar_init(smem_u32(w_full), 1);
+        mbar_init(smem_u32(w_full), NUM_EPI_WARPS);
         *abort_flag = 0;
         fence_mbar_init();
         tma_prefetch_desc(&tmX);
-        tma_prefetch_desc(&tmW);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
@@ -944,20 +998,13 @@ conv1x1_q_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        // ---------------- TMA: stacked weights once, then fp16 input boxes ----------------
+        // ---------------- TMA: fp16 input boxes ----------------
         int rb = 0;
         uint32_t rph = 0;
         uint32_t r_last[Q1_NRAW];
         bool r_used[Q1_NRAW];
         for (int i = 0; i < Q1_NRAW; ++i) { r_last[i] = 0; r_used[i] = false; }
         bool ok = true;
-        if (lane == 0) {
-            const uint32_t fbar = smem_u32(w_full);
-            mbar_arrive_expect_tx(fbar, static_cast<uint32_t>(npairs * STK_TILE));
-            for (int q = 0; q < npairs; ++q)
-                tma_load_3d(smem_u32(smem + Q1_OFF_B + q * STK_TILE), &tmW, fbar, 0, q * STK_N, 0);
-        }
-        __syncwarp();
         for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
             const int pt = t % p.pos_tiles;
             const int n = t / p.pos_tiles;
@@ -978,7 +1025,6 @@ conv1x1_q_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
             }
         }
         volatile int no_abort = 0;
-        mbar_wait_bounded(smem_u32(w_full), 0, &no_abort, p.err, kDevErrWaitDrain);
         for (int i = 0; i < Q1_NRAW; ++i)
             if (r_used[i]) mbar_wait_bounded(smem_u32(raw_full + i), r_last[i], &no_abort, p.err, kDevErrWaitDrain);
     } else if (warp == 1) {
@@ -1080,6 +1126,11 @@ conv1x1_q_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant_
                 if (j < nf) o[j * plane] = h;
             }
         };
+        // the stacked filter block, while the TMA warp brings the first input boxes
+        stack_weights_1x1(smem + Q1_OFF_B, p.w, p.amax_w, p.F, p.C, p.w_vec != 0, npairs, Cg, wt);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(w_full));
         int local = 0, prev_t = -1;
         for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++local) {
             for (int g = 0; g < Cg; ++g) {
@@ -1427,26 +1478,9 @@ int conv1x1_q(const void* x, const void* w, const void* bias, void* out, int64_t
               int64_t F, const float* amax_x, const float* amax_w, uint8_t* ws, int dev, cudaStream_t stream,
               bool x_scale_own) {
     const int64_t Cg = ceil_div(C, 64);
-    const int64_t npairs = ceil_div(Cg, 2);
-    const unsigned sgrid = static_cast<unsigned>(ceil_div(npairs * STK_N * 8, 256));
-    w_stack_kernel<__half><<<sgrid, 256, 0, stream>>>(static_cast<const __half*>(w), (int)F, (int)C, 1, (int)Cg,
-                                                      (int)npairs, amax_w, ws);
-    int rc = launch_status("conv2d 1x1 weight limbs");
-    if (rc) return rc;
     EncodeTiledFn enc = tensor_map_encoder();
     if (enc == nullptr) TK_FAIL(TK_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-    CUtensorMap tx, tw;
-    {
-        const uint64_t rows = static_cast<uint64_t>(npairs * STK_N);
-        cuuint64_t dims[3] = {128, rows, 1};
-        cuuint64_t strides[2] = {128, 128 * rows};
-        cuuint32_t box[3] = {128, static_cast<cuuint32_t>(STK_N), 1};
-        cuuint32_t estr[3] = {1, 1, 1};
-        CUresult r = enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, ws, dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (r != CUDA_SUCCESS) TK_FAIL(TK_ERR_CUDA, "conv2d stacked weight tensor map failed (%d)", (int)r);
-    }
+    CUtensorMap tx;
     {
         // NCHW fp16 as [N][C][HW]: boxes of 128 pixels x 64 channels; pixels
         // past the plane and channels past C read as zero
@@ -1478,6 +1512,9 @@ int conv1x1_q(const void* x, const void* w, const void* bias, void* out, int64_t
     p.out = out;
     p.err = device_error_word(dev);
     p.clamp_x = x_scale_own ? 0 : 1;
+    p.w = static_cast<const __half*>(w);
+    p.C = static_cast<int>(C);
+    p.w_vec = C % 8 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0;
     static std::once_flag once[64];
     static cudaError_t err[64];
     const int slot = std::min(dev, 63);
@@ -1486,7 +1523,7 @@ int conv1x1_q(const void* x, const void* w, const void* bias, void* out, int64_t
     });
     if (err[slot] != cudaSuccess) TK_FAIL(TK_ERR_CUDA, "conv smem attribute: %s", cudaGetErrorString(err[slot]));
     const int grid = std::min(p.tiles, sm_count(dev));
-    conv1x1_q_kernel<<<grid, NUM_THREADS, Q1_SMEM, stream>>>(tx, tw, p);
+    conv1x1_q_kernel<<<grid, NUM_THREADS, Q1_SMEM, stream>>>(tx, p);
     return launch_status("conv2d 1x1 implicit GEMM (input quantised in the kernel)");
 }
 

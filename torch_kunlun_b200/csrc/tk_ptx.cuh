@@ -104,6 +104,12 @@ __device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
     return v;
 }
 
+// Release store at GPU scope: every write this thread made (or observed
+// through an acquire) before it is visible to an acquire load that reads it.
+__device__ __forceinline__ void st_release_gpu_u32(unsigned* p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // ---- thread-block clusters ----------------------------------------------------
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
