@@ -1131,8 +1131,18 @@ conv1x1_q_kernel(const __grid_constant__ CUtensorMap tmX, const ConvWinParams p)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(w_full));
+        // Half the warps of each SMSP (odd `sub`) run the previous tile's
+        // epilogue before quantising this tile, the other half after it, so
+        // the two latency-bound phases interleave on every SMSP.  Either
+        // order only waits for work the other warps finished in their
+        // previous iteration.
+        const bool epi_first = (sub & 1) != 0;
         int local = 0, prev_t = -1;
         for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++local) {
+            if (epi_first && prev_t >= 0) {
+                epilogue(prev_t, local - 1);
+                if (!ok) break;
+            }
             for (int g = 0; g < Cg; ++g) {
                 if (!mbar_wait_bounded(smem_u32(raw_full + rb), rph, abort_flag, p.err, kDevErrWaitFull) ||
                     !mbar_wait_bounded(smem_u32(a_empty + ab), aph ^ 1u, abort_flag, p.err, kDevErrWaitEmpty)) {
@@ -1178,7 +1188,7 @@ conv1x1_q_kernel(const __grid_constant__ CUtensorMap tmX, const ConvWinParams p)
             }
             if (!ok) break;
             // the previous tile's epilogue runs while the MMAs of this one do
-            if (prev_t >= 0) epilogue(prev_t, local - 1);
+            if (!epi_first && prev_t >= 0) epilogue(prev_t, local - 1);
             prev_t = t;
         }
         if (ok && prev_t >= 0) epilogue(prev_t, local - 1);
