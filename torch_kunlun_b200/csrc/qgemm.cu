@@ -211,17 +211,23 @@ __device__ __forceinline__ void decode_tile(const TileParams& tp, int t, int& b,
 
 // ---- tensor-core kernel --------------------------------------------------------
 
-// EW: epilogue warps.  8 for the general epilogue; 16 (four per TMEM lane
-// quarter) for fp16 outputs on the fast path (no alpha, vector bias / addend
-// / stores, no split reduction, N a multiple of 16) with 128x128 tiles, whose
-// epilogue is compiled without the general path so it fits the smaller
-// register budget (BERT FFN1 16384x3072x768 with GELU: 249 -> 224 us).
-template <class C, int DT, int ACT, int EW = NUM_EPI_WARPS>
+// EW: epilogue warps.  FO: the fast-only epilogue, for fp16 outputs on the
+// fast path for the whole problem (no alpha, vector bias / addend / stores,
+// no split reduction, N a multiple of 16), compiled without the general
+// path.  It reads each of its chunks out of TMEM into binary16 values (the
+// one rounding of the dequantised product), releases the accumulator buffer,
+// and only then adds bias / addend, applies the activation and stores, so
+// the next tile's MMAs overlap that work.  128x128 tiles run it on 16 warps
+// (four per TMEM lane quarter; 96 registers), 128x160 tiles on 8.  Measured:
+// BERT FFN1 16384x3072x768 + GELU 249 -> 208 us, the TP MLP's K = 8192
+// GEMMs +2.5 %, 2048x4096x4096 and 4096^3 -3 % step time.
+template <class C, int DT, int ACT, int EW = NUM_EPI_WARPS, bool FO = false>
 __global__ void __launch_bounds__(64 + 32 * EW, 1)
 qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const TileParams tp, const EpiParams ep) {
-    constexpr bool FAST_ONLY = EW != NUM_EPI_WARPS;
-    static_assert(!FAST_ONLY || DT == 0, "the 16-warp epilogue is the fp16 fast path");
+    constexpr bool FAST_ONLY = FO;
+    static_assert(!FAST_ONLY || DT == 0, "the fast-only epilogue is the fp16 fast path");
+    static_assert(!FAST_ONLY || (C::BN / 16) % (EW / 4) == 0, "every warp takes the same number of chunks");
     constexpr int STAGES = C::STAGES;
     constexpr int STAGE_BYTES = C::STAGE_BYTES;
     constexpr int BN = C::BN;
@@ -407,178 +413,252 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             const bool row_ok = m < ep.M;
             int64_t out_row;
             void* const obase = row_out(ep, b, m, out_row);
-#pragma unroll 1
-            for (int c = half; c < BN / 16; c += EW / 4) {  // 16-column chunks, the quarter's warps alternating
-                const int64_t n0 = static_cast<int64_t>(nt) * BN + c * 16;
-                const bool full = n0 + 16 <= ep.N;
-                // fp16 fast path: whole chunk, no alpha, vector bias / addend / store
-                const bool fast = FAST_ONLY || (DT == 0 && fast_ok && row_ok && full);
-                uint4 add_q[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-                if (fast && has_add) {  // issued before the TMEM loads to hide its latency
-                    const uint4* src = reinterpret_cast<const uint4*>(
-                        static_cast<const __half*>(ep.addend) + b * ep.add_sb + m * ep.add_sm + n0);
-                    add_q[0] = __ldg(src);
-                    add_q[1] = __ldg(src + 1);
-                }
-                uint32_t hh[16], mid[16], ll[16];
-                tmem_ld_32x32b_x16(t_buf + c * 16, hh);
-                tmem_ld_32x32b_x16(t_buf + BN + c * 16, mid);
-                tmem_ld_32x32b_x16(t_buf + 2 * BN + c * 16, ll);
-                tc_wait_ld();
-                if (!row_ok || n0 >= ep.N) continue;
-                if (!FAST_ONLY && tp.acc64 != nullptr) {
-                    // K chunk of a split reduction: add its exact int64 sums
-                    const int64_t slice = tp.acc_mod ? b % tp.acc_mod : b;
-                    unsigned long long* dst = tp.acc64 + (slice * ep.M + m) * ep.N + n0;
+            if constexpr (FAST_ONLY) {
+                // Two phases: the accumulators of this warp's chunks become
+                // their binary16 values (the one rounding of the dequantised
+                // product) and the TMEM buffer is released at once, so the
+                // next tile's MMAs run during the bias / addend / activation
+                // arithmetic and the stores.
+                constexpr int NCH = (BN / 16) / (EW / 4);
+                __half2 hv[NCH][8];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        if (full || n0 + j < ep.N)
-                            atomicAdd(dst + j, static_cast<unsigned long long>(
-                                                   limb_acc_to_i64(hh[j], mid[j], ll[j])));
-                    continue;
+                for (int i = 0; i < NCH; ++i) {
+                    const int c = half + i * (EW / 4);
+                    uint32_t hh[16], mid[16], ll[16];
+                    tmem_ld_32x32b_x16(t_buf + c * 16, hh);
+                    tmem_ld_32x32b_x16(t_buf + BN + c * 16, mid);
+                    tmem_ld_32x32b_x16(t_buf + 2 * BN + c * 16, ll);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        hv[i][j] = __halves2half2(
+                            __double2half(__dmul_rn(limb_acc_to_double(hh[2 * j], mid[2 * j], ll[2 * j]), s)),
+                            __double2half(__dmul_rn(limb_acc_to_double(hh[2 * j + 1], mid[2 * j + 1], ll[2 * j + 1]), s)));
                 }
-                if constexpr (DT == 0) {
-                    if (fast) {
-                        // One binary64 -> binary16 rounding, then the bias and
-                        // addend in binary16: each add of two binary16 values
-                        // rounded once equals the binary32 add rounded to
-                        // binary16 (binary32 has more than 2*11 + 2 bits).
-                        __half2 hv[8];
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(acc_empty + buf));
+                if (!row_ok) continue;
+#pragma unroll
+                for (int i = 0; i < NCH; ++i) {
+                    const int64_t n0 = static_cast<int64_t>(nt) * BN + (half + i * (EW / 4)) * 16;
+                    if (n0 >= ep.N) continue;
+                    // the fast path's order: bias, then addend, then activation,
+                    // each a binary16 operation rounded once
+                    if (has_bias) {
+                        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __half*>(bias_base) + n0);
+                        const uint4 q0 = __ldg(src), q1 = __ldg(src + 1);
+                        const __half2* b0 = reinterpret_cast<const __half2*>(&q0);
+                        const __half2* b1 = reinterpret_cast<const __half2*>(&q1);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            hv[i][j] = __hadd2(hv[i][j], b0[j]);
+                            hv[i][4 + j] = __hadd2(hv[i][4 + j], b1[j]);
+                        }
+                    }
+                    if (has_add) {
+                        const uint4* src = reinterpret_cast<const uint4*>(
+                            static_cast<const __half*>(ep.addend) + b * ep.add_sb + m * ep.add_sm + n0);
+                        const uint4 q0 = __ldg(src), q1 = __ldg(src + 1);
+                        const __half2* a0 = reinterpret_cast<const __half2*>(&q0);
+                        const __half2* a1 = reinterpret_cast<const __half2*>(&q1);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            hv[i][j] = __hadd2(hv[i][j], a0[j]);
+                            hv[i][4 + j] = __hadd2(hv[i][4 + j], a1[j]);
+                        }
+                    }
+                    if constexpr (ACT != TK_ACT_NONE) {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const float2 f = __half22float2(hv[i][j]);
+                            hv[i][j] = __floats2half2_rn(act_t<ACT>(f.x, DT), act_t<ACT>(f.y, DT));
+                        }
+                    }
+                    if (ep.amax_out != nullptr) {
 #pragma unroll
                         for (int j = 0; j < 8; ++j)
-                            hv[j] = __halves2half2(
-                                __double2half(__dmul_rn(limb_acc_to_double(hh[2 * j], mid[2 * j], ll[2 * j]), s)),
-                                __double2half(__dmul_rn(limb_acc_to_double(hh[2 * j + 1], mid[2 * j + 1], ll[2 * j + 1]), s)));
-                        if (has_bias) {
-                            const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __half*>(bias_base) + n0);
-                            const uint4 q0 = __ldg(src), q1 = __ldg(src + 1);
-                            const __half2* b0 = reinterpret_cast<const __half2*>(&q0);
-                            const __half2* b1 = reinterpret_cast<const __half2*>(&q1);
+                            out_mag2 = __vmaxu2(out_mag2, *reinterpret_cast<const uint32_t*>(&hv[i][j]) & 0x7FFF7FFFu);
+                    }
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(obase) + out_row + n0);
+                    const uint4* w = reinterpret_cast<const uint4*>(hv[i]);
+                    dst[0] = w[0];
+                    dst[1] = w[1];
+                }
+            } else {
+#pragma unroll 1
+                for (int c = half; c < BN / 16; c += EW / 4) {  // 16-column chunks, the quarter's warps alternating
+                    const int64_t n0 = static_cast<int64_t>(nt) * BN + c * 16;
+                    const bool full = n0 + 16 <= ep.N;
+                    // fp16 fast path: whole chunk, no alpha, vector bias / addend / store
+                    const bool fast = FAST_ONLY || (DT == 0 && fast_ok && row_ok && full);
+                    uint4 add_q[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+                    if (fast && has_add) {  // issued before the TMEM loads to hide its latency
+                        const uint4* src = reinterpret_cast<const uint4*>(
+                            static_cast<const __half*>(ep.addend) + b * ep.add_sb + m * ep.add_sm + n0);
+                        add_q[0] = __ldg(src);
+                        add_q[1] = __ldg(src + 1);
+                    }
+                    uint32_t hh[16], mid[16], ll[16];
+                    tmem_ld_32x32b_x16(t_buf + c * 16, hh);
+                    tmem_ld_32x32b_x16(t_buf + BN + c * 16, mid);
+                    tmem_ld_32x32b_x16(t_buf + 2 * BN + c * 16, ll);
+                    tc_wait_ld();
+                    if (!row_ok || n0 >= ep.N) continue;
+                    if (!FAST_ONLY && tp.acc64 != nullptr) {
+                        // K chunk of a split reduction: add its exact int64 sums
+                        const int64_t slice = tp.acc_mod ? b % tp.acc_mod : b;
+                        unsigned long long* dst = tp.acc64 + (slice * ep.M + m) * ep.N + n0;
 #pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                hv[j] = __hadd2(hv[j], b0[j]);
-                                hv[4 + j] = __hadd2(hv[4 + j], b1[j]);
-                            }
-                        }
-                        if (has_add) {
-                            const __half2* a2 = reinterpret_cast<const __half2*>(add_q);
-#pragma unroll
-                            for (int j = 0; j < 8; ++j) hv[j] = __hadd2(hv[j], a2[j]);
-                        }
-                        if constexpr (ACT != TK_ACT_NONE) {
-#pragma unroll
-                            for (int j = 0; j < 8; ++j) {
-                                const float2 f = __half22float2(hv[j]);
-                                hv[j] = __floats2half2_rn(act_t<ACT>(f.x, DT), act_t<ACT>(f.y, DT));
-                            }
-                        }
-                        if (ep.amax_out != nullptr) {
-                            // magnitudes as 16-bit patterns: NaN > Inf > finite
-#pragma unroll
-                            for (int j = 0; j < 8; ++j)
-                                out_mag2 = __vmaxu2(out_mag2, *reinterpret_cast<const uint32_t*>(&hv[j]) & 0x7FFF7FFFu);
-                        }
-                        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(obase) + out_row + n0);
-                        const uint4* w = reinterpret_cast<const uint4*>(hv);
-                        dst[0] = w[0];
-                        dst[1] = w[1];
+                        for (int j = 0; j < 16; ++j)
+                            if (full || n0 + j < ep.N)
+                                atomicAdd(dst + j, static_cast<unsigned long long>(
+                                                       limb_acc_to_i64(hh[j], mid[j], ll[j])));
                         continue;
                     }
-                }
-                if constexpr (!FAST_ONLY) {
-                float v[16];
+                    if constexpr (DT == 0) {
+                        if (fast) {
+                            // One binary64 -> binary16 rounding, then the bias and
+                            // addend in binary16: each add of two binary16 values
+                            // rounded once equals the binary32 add rounded to
+                            // binary16 (binary32 has more than 2*11 + 2 bits).
+                            __half2 hv[8];
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    v[j] = round_t_from_double(__dmul_rn(limb_acc_to_double(hh[j], mid[j], ll[j]), s), DT);
-                if (has_alpha) {
+                            for (int j = 0; j < 8; ++j)
+                                hv[j] = __halves2half2(
+                                    __double2half(__dmul_rn(limb_acc_to_double(hh[2 * j], mid[2 * j], ll[2 * j]), s)),
+                                    __double2half(__dmul_rn(limb_acc_to_double(hh[2 * j + 1], mid[2 * j + 1], ll[2 * j + 1]), s)));
+                            if (has_bias) {
+                                const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __half*>(bias_base) + n0);
+                                const uint4 q0 = __ldg(src), q1 = __ldg(src + 1);
+                                const __half2* b0 = reinterpret_cast<const __half2*>(&q0);
+                                const __half2* b1 = reinterpret_cast<const __half2*>(&q1);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = round_t(__fmul_rn(v[j], ep.alpha), DT);
-                }
-                if (has_bias) {
-                    float bv[16];
-                    const void* bias_base = ep.bias_mod
-                        ? static_cast<const void*>(static_cast<const char*>(ep.bias) +
-                              (b % ep.bias_mod) * ep.N * (DT == 0 ? 2 : 4))
-                        : ep.bias;
-                    if (full && ep.bias_vec) {
-                        // 16 consecutive bias values with 128-bit loads (the
-                        // same addresses for the whole warp: one broadcast).
-                        if constexpr (DT == 0) {
-                            const uint4* src = reinterpret_cast<const uint4*>(
-                                static_cast<const __half*>(bias_base) + n0);
-                            uint4 q[2] = {__ldg(src), __ldg(src + 1)};
-                            const __half2* h2 = reinterpret_cast<const __half2*>(q);
+                                for (int j = 0; j < 4; ++j) {
+                                    hv[j] = __hadd2(hv[j], b0[j]);
+                                    hv[4 + j] = __hadd2(hv[4 + j], b1[j]);
+                                }
+                            }
+                            if (has_add) {
+                                const __half2* a2 = reinterpret_cast<const __half2*>(add_q);
 #pragma unroll
-                            for (int j = 0; j < 8; ++j) {
-                                const float2 f = __half22float2(h2[j]);
-                                bv[2 * j] = f.x;
-                                bv[2 * j + 1] = f.y;
+                                for (int j = 0; j < 8; ++j) hv[j] = __hadd2(hv[j], a2[j]);
+                            }
+                            if constexpr (ACT != TK_ACT_NONE) {
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) {
+                                    const float2 f = __half22float2(hv[j]);
+                                    hv[j] = __floats2half2_rn(act_t<ACT>(f.x, DT), act_t<ACT>(f.y, DT));
+                                }
+                            }
+                            if (ep.amax_out != nullptr) {
+                                // magnitudes as 16-bit patterns: NaN > Inf > finite
+#pragma unroll
+                                for (int j = 0; j < 8; ++j)
+                                    out_mag2 = __vmaxu2(out_mag2, *reinterpret_cast<const uint32_t*>(&hv[j]) & 0x7FFF7FFFu);
+                            }
+                            uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(obase) + out_row + n0);
+                            const uint4* w = reinterpret_cast<const uint4*>(hv);
+                            dst[0] = w[0];
+                            dst[1] = w[1];
+                            continue;
+                        }
+                    }
+                    if constexpr (!FAST_ONLY) {
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        v[j] = round_t_from_double(__dmul_rn(limb_acc_to_double(hh[j], mid[j], ll[j]), s), DT);
+                    if (has_alpha) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = round_t(__fmul_rn(v[j], ep.alpha), DT);
+                    }
+                    if (has_bias) {
+                        float bv[16];
+                        const void* bias_base = ep.bias_mod
+                            ? static_cast<const void*>(static_cast<const char*>(ep.bias) +
+                                  (b % ep.bias_mod) * ep.N * (DT == 0 ? 2 : 4))
+                            : ep.bias;
+                        if (full && ep.bias_vec) {
+                            // 16 consecutive bias values with 128-bit loads (the
+                            // same addresses for the whole warp: one broadcast).
+                            if constexpr (DT == 0) {
+                                const uint4* src = reinterpret_cast<const uint4*>(
+                                    static_cast<const __half*>(bias_base) + n0);
+                                uint4 q[2] = {__ldg(src), __ldg(src + 1)};
+                                const __half2* h2 = reinterpret_cast<const __half2*>(q);
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) {
+                                    const float2 f = __half22float2(h2[j]);
+                                    bv[2 * j] = f.x;
+                                    bv[2 * j + 1] = f.y;
+                                }
+                            } else {
+                                const float4* src = reinterpret_cast<const float4*>(
+                                    static_cast<const float*>(bias_base) + n0);
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) {
+                                    const float4 f = __ldg(src + j);
+                                    bv[4 * j] = f.x; bv[4 * j + 1] = f.y;
+                                    bv[4 * j + 2] = f.z; bv[4 * j + 3] = f.w;
+                                }
                             }
                         } else {
-                            const float4* src = reinterpret_cast<const float4*>(
-                                static_cast<const float*>(bias_base) + n0);
 #pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                const float4 f = __ldg(src + j);
-                                bv[4 * j] = f.x; bv[4 * j + 1] = f.y;
-                                bv[4 * j + 2] = f.z; bv[4 * j + 3] = f.w;
+                            for (int j = 0; j < 16; ++j)
+                                bv[j] = (n0 + j < ep.N) ? load_t(bias_base, DT, n0 + j) : 0.0f;
+                        }
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = round_t(__fadd_rn(v[j], bv[j]), DT);
+                    }
+                    if (has_add) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            if (!full && n0 + j >= ep.N) continue;
+                            float a = load_t(ep.addend, DT, b * ep.add_sb + m * ep.add_sm + (n0 + j) * ep.add_sn);
+                            if (ep.beta != 1.0f) a = round_t(__fmul_rn(a, ep.beta), DT);
+                            v[j] = round_t(__fadd_rn(v[j], a), DT);
+                        }
+                    }
+                    if constexpr (ACT != TK_ACT_NONE) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = act_t<ACT>(v[j], DT);
+                    }
+                    if (ep.dbg != nullptr && b == 0) {
+                        for (int j = 0; j < 16 && n0 + j < ep.N; ++j) {
+                            ep.dbg[(0 * ep.M + m) * ep.N + n0 + j] = static_cast<int32_t>(hh[j]);
+                            ep.dbg[(1 * ep.M + m) * ep.N + n0 + j] = static_cast<int32_t>(mid[j]);
+                            ep.dbg[(2 * ep.M + m) * ep.N + n0 + j] = static_cast<int32_t>(ll[j]);
+                        }
+                    }
+                    if (ep.vec_store && full) {
+                        if constexpr (DT == 0) {
+                            uint32_t w[8];
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                __half2 h2 = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+                                w[j] = *reinterpret_cast<uint32_t*>(&h2);
                             }
+                            uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(obase) + out_row + n0);
+                            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                        } else {
+                            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(obase) + out_row + n0);
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
                         }
                     } else {
 #pragma unroll
                         for (int j = 0; j < 16; ++j)
-                            bv[j] = (n0 + j < ep.N) ? load_t(bias_base, DT, n0 + j) : 0.0f;
+                            if (full || n0 + j < ep.N) store_t(obase, ep.dtype, out_row + (n0 + j) * ep.out_sn, v[j]);
                     }
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = round_t(__fadd_rn(v[j], bv[j]), DT);
+                    }  // !FAST_ONLY
                 }
-                if (has_add) {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        if (!full && n0 + j >= ep.N) continue;
-                        float a = load_t(ep.addend, DT, b * ep.add_sb + m * ep.add_sm + (n0 + j) * ep.add_sn);
-                        if (ep.beta != 1.0f) a = round_t(__fmul_rn(a, ep.beta), DT);
-                        v[j] = round_t(__fadd_rn(v[j], a), DT);
-                    }
-                }
-                if constexpr (ACT != TK_ACT_NONE) {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = act_t<ACT>(v[j], DT);
-                }
-                if (ep.dbg != nullptr && b == 0) {
-                    for (int j = 0; j < 16 && n0 + j < ep.N; ++j) {
-                        ep.dbg[(0 * ep.M + m) * ep.N + n0 + j] = static_cast<int32_t>(hh[j]);
-                        ep.dbg[(1 * ep.M + m) * ep.N + n0 + j] = static_cast<int32_t>(mid[j]);
-                        ep.dbg[(2 * ep.M + m) * ep.N + n0 + j] = static_cast<int32_t>(ll[j]);
-                    }
-                }
-                if (ep.vec_store && full) {
-                    if constexpr (DT == 0) {
-                        uint32_t w[8];
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            __half2 h2 = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-                            w[j] = *reinterpret_cast<uint32_t*>(&h2);
-                        }
-                        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(obase) + out_row + n0);
-                        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-                    } else {
-                        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(obase) + out_row + n0);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        if (full || n0 + j < ep.N) store_t(obase, ep.dtype, out_row + (n0 + j) * ep.out_sn, v[j]);
-                }
-                }  // !FAST_ONLY
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(acc_empty + buf));
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(acc_empty + buf));
         }
         if (ep.amax_out != nullptr) {
             unsigned hmag = max(out_mag2 & 0xFFFFu, out_mag2 >> 16);
@@ -806,30 +886,30 @@ struct RowScatter {
 
 enum class Path { TensorCore, Simt };
 
-template <class C, int DT, int ACT, int EW = NUM_EPI_WARPS>
+template <class C, int DT, int ACT, int EW, bool FO>
 int launch_one(int dev, int grid, const CUtensorMap& tmA, const CUtensorMap& tmB,
                const TileParams& tp, const EpiParams& ep, cudaStream_t stream) {
     static std::once_flag attr_once[64];
     if (dev >= 0 && dev < 64) {
         std::call_once(attr_once[dev], [] {
-            cudaFuncSetAttribute(qgemm_tc_kernel<C, DT, ACT, EW>,
+            cudaFuncSetAttribute(qgemm_tc_kernel<C, DT, ACT, EW, FO>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         });
     }
-    qgemm_tc_kernel<C, DT, ACT, EW><<<grid, 64 + 32 * EW, C::SMEM, stream>>>(tmA, tmB, tp, ep);
+    qgemm_tc_kernel<C, DT, ACT, EW, FO><<<grid, 64 + 32 * EW, C::SMEM, stream>>>(tmA, tmB, tp, ep);
     return TK_OK;
 }
 
-template <class C, int DT, int EW>
+template <class C, int DT, int EW, bool FO>
 int dispatch_act_ew(int act, int dev, int grid, const CUtensorMap& tmA, const CUtensorMap& tmB,
                     const TileParams& tp, const EpiParams& ep, cudaStream_t stream) {
     switch (act) {
-        case TK_ACT_NONE: return launch_one<C, DT, TK_ACT_NONE, EW>(dev, grid, tmA, tmB, tp, ep, stream);
-        case TK_ACT_RELU: return launch_one<C, DT, TK_ACT_RELU, EW>(dev, grid, tmA, tmB, tp, ep, stream);
-        case TK_ACT_GELU: return launch_one<C, DT, TK_ACT_GELU, EW>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_NONE: return launch_one<C, DT, TK_ACT_NONE, EW, FO>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_RELU: return launch_one<C, DT, TK_ACT_RELU, EW, FO>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_GELU: return launch_one<C, DT, TK_ACT_GELU, EW, FO>(dev, grid, tmA, tmB, tp, ep, stream);
         case TK_ACT_GELU_TANH:
-            return launch_one<C, DT, TK_ACT_GELU_TANH, EW>(dev, grid, tmA, tmB, tp, ep, stream);
-        case TK_ACT_SILU: return launch_one<C, DT, TK_ACT_SILU, EW>(dev, grid, tmA, tmB, tp, ep, stream);
+            return launch_one<C, DT, TK_ACT_GELU_TANH, EW, FO>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_SILU: return launch_one<C, DT, TK_ACT_SILU, EW, FO>(dev, grid, tmA, tmB, tp, ep, stream);
         default: TK_FAIL(TK_ERR_INVALID_ARG, "qgemm: bad act %d", act);
     }
 }
@@ -850,14 +930,19 @@ bool fast_epilogue(const TileParams& tp, const EpiParams& ep) {
 template <class C, int DT>
 int dispatch_act(int act, int dev, int grid, const CUtensorMap& tmA, const CUtensorMap& tmB,
                  const TileParams& tp, const EpiParams& ep, cudaStream_t stream) {
-    // Short reductions only (128x128 tiles, K < 2048), where the epilogue
-    // outweighs the tile's MMAs; with K >= 2048 the 16-warp epilogue measured
-    // no faster (2048x4096x4096) or slower (the TP MLP's K = 8192 GEMMs, 3 %).
-    if constexpr (DT == 0 && C::BN == 128) {
-        if (fast_epilogue(tp, ep))
-            return dispatch_act_ew<C, DT, 2 * NUM_EPI_WARPS>(act, dev, grid, tmA, tmB, tp, ep, stream);
+    // The fast-only epilogue (fp16 fast path for the whole problem) frees the
+    // accumulators as soon as they are binary16 values.  Short reductions
+    // (128x128 tiles, K < 2048), where the epilogue outweighs the tile's
+    // MMAs, run it on sixteen warps; with K >= 2048 sixteen warps measured no
+    // faster (2048x4096x4096) or slower (the TP MLP's K = 8192 GEMMs, 3 %),
+    // so the 128x160 tiles keep eight.
+    if constexpr (DT == 0 && (C::BN == 128 || C::BN == 160)) {
+        if (fast_epilogue(tp, ep)) {
+            constexpr int EWF = C::BN == 128 ? 2 * NUM_EPI_WARPS : NUM_EPI_WARPS;
+            return dispatch_act_ew<C, DT, EWF, true>(act, dev, grid, tmA, tmB, tp, ep, stream);
+        }
     }
-    return dispatch_act_ew<C, DT, NUM_EPI_WARPS>(act, dev, grid, tmA, tmB, tp, ep, stream);
+    return dispatch_act_ew<C, DT, NUM_EPI_WARPS, false>(act, dev, grid, tmA, tmB, tp, ep, stream);
 }
 
 // Tile configuration for a problem: 128x160 tiles for K >= 2048, else
