@@ -36,42 +36,6 @@ __device__ __forceinline__ unsigned block_max_u32(unsigned v) {
     return v;
 }
 
-// |x| of an fp16 pair as two 16-bit magnitudes; the unsigned order of the
-// magnitudes is the float order, with every NaN above +Inf.
-__global__ void amax_f16_kernel(const __half* __restrict__ x, int64_t slice_stride,
-                                int64_t slice_len, int64_t chunk, bool vec,
-                                unsigned* __restrict__ out_bits) {
-    const int64_t s = blockIdx.y;
-    const unsigned short* base = reinterpret_cast<const unsigned short*>(x + s * slice_stride);
-    const int64_t start = static_cast<int64_t>(blockIdx.x) * chunk;
-    const int64_t end = min(start + chunk, slice_len);
-    unsigned m2 = 0;  // two packed 16-bit maxima
-    int64_t i = start;
-    if (vec) {
-        const int64_t nv = (end - start) / 8;
-        const uint4* pv = reinterpret_cast<const uint4*>(base + start);
-        for (int64_t j = threadIdx.x; j < nv; j += blockDim.x) {
-            uint4 w = __ldg(pv + j);
-            m2 = __vmaxu2(m2, w.x & 0x7FFF7FFFu);
-            m2 = __vmaxu2(m2, w.y & 0x7FFF7FFFu);
-            m2 = __vmaxu2(m2, w.z & 0x7FFF7FFFu);
-            m2 = __vmaxu2(m2, w.w & 0x7FFF7FFFu);
-        }
-        i = start + nv * 8;
-    }
-    for (int64_t j = i + threadIdx.x; j < end; j += blockDim.x) {
-        m2 = __vmaxu2(m2, static_cast<unsigned>(base[j] & 0x7FFFu));
-    }
-    unsigned h = max(m2 & 0xFFFFu, m2 >> 16);
-    h = block_max_u32(h);
-    if (threadIdx.x == 0 && h != 0u) {
-        float f = __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
-        unsigned bits = __float_as_uint(f) & 0x7FFFFFFFu;
-        if ((h & 0x7C00u) == 0x7C00u && (h & 0x3FFu) != 0u) bits = 0x7FC00000u;  // NaN
-        atomicMax(out_bits + s, bits);
-    }
-}
-
 __global__ void amax_f32_kernel(const float* __restrict__ x, int64_t slice_stride,
                                 int64_t slice_len, int64_t chunk, bool vec,
                                 unsigned* __restrict__ out_bits) {
@@ -471,6 +435,8 @@ __global__ void __launch_bounds__(256) quant_vec_kernel(QVecDesc d0, QVecDesc d1
 
 }  // namespace
 
+int amax_wave_blocks(tk_dtype_t dtype, int dev);
+
 int amax_launch(tk_dtype_t dtype, const void* x, int64_t nslices, int64_t slice_stride,
                 int64_t slice_len, float* amax_out, cudaStream_t stream) {
     TK_CHECK_ARG(nslices >= 0 && slice_len >= 0, "tk_amax: negative size");
@@ -483,6 +449,25 @@ int amax_launch(tk_dtype_t dtype, const void* x, int64_t nslices, int64_t slice_
     TK_CHECK_ARG(x != nullptr, "tk_amax: x is NULL");
     const size_t es = dtype_size(dtype);
     const int dev = current_device();
+    if (dtype == TK_DTYPE_F16) {
+        // One resident wave of amax_multi_kernel blocks (eight 128-bit loads
+        // per thread in flight), shared evenly by the slices.
+        AmaxDesc d = {};
+        d.x = x;
+        d.nslices = nslices;
+        d.slice_stride = slice_stride;
+        d.slice_len = slice_len;
+        const int64_t per_slice = std::max<int64_t>(1, (amax_wave_blocks(dtype, dev) - 2) / nslices);
+        d.chunk = std::max<int64_t>(static_cast<int64_t>(kAmaxThreads) * 64, ceil_div(slice_len, per_slice));
+        d.chunk = (d.chunk + 7) / 8 * 8;
+        d.chunks = ceil_div(slice_len, d.chunk);
+        d.out = reinterpret_cast<unsigned*>(amax_out);
+        d.vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((slice_stride * static_cast<int64_t>(es)) % 16 == 0);
+        const int64_t total = d.chunks * nslices;
+        TK_CHECK_ARG(total < (1LL << 31), "tk_amax: too many blocks");
+        amax_multi_kernel<__half><<<static_cast<unsigned>(total), kAmaxThreads, 0, stream>>>(d, d, total);
+        return launch_status("amax");
+    }
     const int64_t per_block = static_cast<int64_t>(kAmaxThreads) * 32;  // elements
     int64_t blocks = ceil_div(slice_len, per_block);
     const int64_t want = std::max<int64_t>(1, (4LL * sm_count(dev)) / nslices);
@@ -495,13 +480,8 @@ int amax_launch(tk_dtype_t dtype, const void* x, int64_t nslices, int64_t slice_
                      ((slice_stride * static_cast<int64_t>(es)) % 16 == 0);
     dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(nslices));
     unsigned* ob = reinterpret_cast<unsigned*>(amax_out);
-    if (dtype == TK_DTYPE_F16) {
-        amax_f16_kernel<<<grid, kAmaxThreads, 0, stream>>>(static_cast<const __half*>(x),
-                                                           slice_stride, slice_len, chunk, vec, ob);
-    } else {
-        amax_f32_kernel<<<grid, kAmaxThreads, 0, stream>>>(static_cast<const float*>(x),
-                                                           slice_stride, slice_len, chunk, vec, ob);
-    }
+    amax_f32_kernel<<<grid, kAmaxThreads, 0, stream>>>(static_cast<const float*>(x), slice_stride, slice_len,
+                                                       chunk, vec, ob);
     return launch_status("amax");
 }
 
