@@ -51,7 +51,14 @@ typedef enum {
     TK_ACT_RELU = 1,
     TK_ACT_GELU = 2,      /* erf form */
     TK_ACT_GELU_TANH = 3, /* tanh approximation */
-    TK_ACT_SILU = 4
+    TK_ACT_SILU = 4,
+    /* The gated-MLP activation (silu(gate) * up) fused into the up
+     * projection: the addend operand holds the gate, and the epilogue
+     * multiplies by T(silu(gate)) instead of adding (beta must be 1); each
+     * product rounds once to T, as the separate swish + mul.  fp16 output on
+     * the vector epilogue path only (16-byte aligned out, bias and gate rows,
+     * unit column stride, N a multiple of 16, no split reduction). */
+    TK_ACT_SILU_GATE = 5
 } tk_act_t;
 
 /* ---- library ------------------------------------------------------------- */
@@ -106,7 +113,8 @@ TK_API int tk_quantize_limbs(tk_dtype_t dtype, const void* x, int64_t batch, int
  * multiply by alpha and round; if bias add bias[n] and round; if addend and
  * beta != 0 add beta*addend (addend element (b,m,n) at
  * addend[b*add_sb + m*add_sm + n*add_sn], strides may be 0 to broadcast) and
- * round; apply act.  K is any size: reductions longer than 32768 (and long
+ * round; apply act (TK_ACT_SILU_GATE replaces the addend step: multiply by
+ * T(silu(addend)) and round).  K is any size: reductions longer than 32768 (and long
  * reductions with few output tiles) are split into chunks whose exact int64
  * sums are added in the workspace before the one dequantising rounding.
  */
@@ -149,7 +157,8 @@ TK_API int tk_qgemm(const tk_qgemm_desc_t* desc, void* workspace, size_t workspa
  * quantised form of an operand that does not change between calls (weights)
  * -- XDNN's fc accepts precomputed max pointers for the same purpose
  * (csrc/ops.cpp:227 passes them as null).  K must be <= 32768 (no workspace
- * for a split reduction). */
+ * for a split reduction).  amax_out is supported when the epilogue is the
+ * fp16 vector path (it is folded into the epilogue). */
 TK_API int tk_qgemm_from_limbs(const tk_qgemm_desc_t* desc, const int8_t* a_limbs,
                                const int8_t* b_limbs, const float* amax_a, const float* amax_b,
                                void* stream);

@@ -38,6 +38,36 @@ def test_row_blocks_with_shared_scales_equal_one_call():
     assert ops.amax(x).cpu().item() == float(O.amax(x.cpu().numpy()))
 
 
+@pytest.mark.parametrize("M,K,N,bias", [(300, 256, 384, False), (130, 768, 96, True),
+                                        (256, 2048, 320, False), (64, 4096, 160, True)])
+def test_silu_gate_epilogue_equals_separate_gate(M, K, N, bias):
+    """silu_mul(gate, up) fused into the up projection's epilogue: the same
+    bits, and max |h| from the epilogue equals the separate pass's (128x128
+    tiles for K < 2048, 128x160 above)."""
+    x, wg, wu = rnd((M, K), 11).to(DEV), rnd((N, K), 12, 0.05).to(DEV), rnd((N, K), 13, 0.05).to(DEV)
+    b = rnd((N,), 14, 0.1).to(DEV) if bias else None
+    ax, awg, awu = ops.amax(x), ops.amax(wg), ops.amax(wu)
+    xl, wgl, wul = ops.quantize_limbs(x, ax), ops.quantize_limbs(wg, awg), ops.quantize_limbs(wu, awu)
+    gate = ops.linear_from_limbs(xl, wgl, K, ax, awg)
+    up = ops.linear_from_limbs(xl, wul, K, ax, awu, bias=b)
+    h_ref, ah_ref = ops.silu_mul_amax(gate, up)
+    ah = torch.full((1,), -1.0, dtype=torch.float32, device=DEV)
+    h = ops.linear_from_limbs(xl, wul, K, ax, awu, bias=b, act="silu_gate", gate=gate, amax_out=ah)
+    assert torch.equal(h.cpu().view(torch.int16), h_ref.cpu().view(torch.int16))
+    assert torch.equal(ah.cpu().view(torch.int32), ah_ref.cpu().view(torch.int32))
+
+
+def test_silu_gate_epilogue_rejects_unsupported_forms():
+    x, w = rnd((64, 256), 15).to(DEV), rnd((40, 256), 16, 0.05).to(DEV)  # N % 16 != 0
+    ax, aw = ops.amax(x), ops.amax(w)
+    xl, wl = ops.quantize_limbs(x, ax), ops.quantize_limbs(w, aw)
+    gate = torch.zeros(64, 40, dtype=torch.float16, device=DEV)
+    with pytest.raises(RuntimeError):
+        ops.linear_from_limbs(xl, wl, 256, ax, aw, act="silu_gate", gate=gate)
+    with pytest.raises(RuntimeError):  # the gate operand is required
+        ops.linear_from_limbs(xl, wl, 256, ax, aw, act="silu_gate")
+
+
 def test_tp_mlp_world1_matches_composition_and_oracle():
     T, H, F = 256, 128, 384
     x = rnd((T, H), 3).to(DEV)

@@ -106,7 +106,8 @@ at::Tensor quantize_limbs(const at::Tensor& x, const at::Tensor& amax);
 at::Tensor linear_from_limbs(const at::Tensor& a_limbs, const at::Tensor& b_limbs, int64_t k,
                              const at::Tensor& amax_a, const at::Tensor& amax_b,
                              const std::optional<at::Tensor>& bias, int64_t act,
-                             const std::optional<at::Tensor>& out, at::ScalarType dtype);
+                             const std::optional<at::Tensor>& out, at::ScalarType dtype,
+                             const std::optional<at::Tensor>& gate, const std::optional<at::Tensor>& amax_out);
 at::Tensor amax(const at::Tensor& x);
 at::Tensor linear_scaled(const at::Tensor& input, const at::Tensor& weight,
                          const std::optional<at::Tensor>& bias, int64_t act,

@@ -98,7 +98,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("quantize_limbs", &quantize_limbs);
     m.def("linear_from_limbs", &linear_from_limbs, py::arg("a_limbs"), py::arg("b_limbs"), py::arg("k"),
           py::arg("amax_a"), py::arg("amax_b"), py::arg("bias") = py::none(), py::arg("act") = 0,
-          py::arg("out") = py::none(), py::arg("dtype") = at::kHalf);
+          py::arg("out") = py::none(), py::arg("dtype") = at::kHalf, py::arg("gate") = py::none(),
+          py::arg("amax_out") = py::none());
     m.def("amax", &amax);
     m.def("linear_scaled", &linear_scaled, py::arg("input"), py::arg("weight"),
           py::arg("bias") = py::none(), py::arg("act") = 0, py::arg("amax_x") = py::none(),

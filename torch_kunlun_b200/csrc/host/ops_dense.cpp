@@ -602,7 +602,8 @@ at::Tensor quantize_limbs(const at::Tensor& x_in, const at::Tensor& amax) {
 at::Tensor linear_from_limbs(const at::Tensor& a_limbs, const at::Tensor& b_limbs, int64_t k,
                              const at::Tensor& amax_a, const at::Tensor& amax_b,
                              const std::optional<at::Tensor>& bias, int64_t act,
-                             const std::optional<at::Tensor>& out_opt, at::ScalarType dtype) {
+                             const std::optional<at::Tensor>& out_opt, at::ScalarType dtype,
+                             const std::optional<at::Tensor>& gate, const std::optional<at::Tensor>& amax_out) {
     const int64_t ld = (k + 15) / 16 * 16;
     TORCH_CHECK(a_limbs.dim() == 3 && b_limbs.dim() == 3 && a_limbs.size(0) == 2 && b_limbs.size(0) == 2 &&
                     a_limbs.size(2) == ld && b_limbs.size(2) == ld && a_limbs.is_contiguous() &&
@@ -646,6 +647,25 @@ at::Tensor linear_from_limbs(const at::Tensor& a_limbs, const at::Tensor& b_limb
     d.beta = 0.0f;
     d.act = static_cast<tk_act_t>(act);
     d.per_slice_scales = 1;
+    at::Tensor gt;
+    if (gate.has_value() && gate->defined()) {
+        // act TK_ACT_SILU_GATE: y = T(silu(gate)) * (a b^T + bias), gate [M, N] row-major
+        gt = *gate;
+        TORCH_CHECK(gt.dim() == 2 && gt.size(0) == M && gt.size(1) == N && gt.stride(1) == 1 &&
+                        gt.scalar_type() == dtype && gt.device() == out.device(),
+                    "kunlun linear_from_limbs: gate must be a row-major [M, N] tensor of the output dtype");
+        d.addend = gt.data_ptr();
+        d.add_sb = M * gt.stride(0);
+        d.add_sm = gt.stride(0);
+        d.add_sn = 1;
+        d.beta = 1.0f;
+    }
+    if (amax_out.has_value() && amax_out->defined()) {
+        TORCH_CHECK(amax_out->scalar_type() == at::kFloat && amax_out->numel() >= 1 && amax_out->is_contiguous() &&
+                        amax_out->device() == out.device(),
+                    "kunlun linear_from_limbs: amax_out must be a 1-element fp32 kunlun tensor");
+        d.amax_out = amax_out->data_ptr<float>();
+    }
     const int dev = out.device().index();
     DeviceScope g(dev);
     check_tk(tk_qgemm_from_limbs(&d, a_limbs.data_ptr<int8_t>(), b_limbs.data_ptr<int8_t>(),

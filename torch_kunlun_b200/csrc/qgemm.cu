@@ -462,13 +462,24 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                         const uint4 q0 = __ldg(src), q1 = __ldg(src + 1);
                         const __half2* a0 = reinterpret_cast<const __half2*>(&q0);
                         const __half2* a1 = reinterpret_cast<const __half2*>(&q1);
+                        if constexpr (ACT == TK_ACT_SILU_GATE) {
+                            // y = T(T(silu(gate)) * up): the product of two binary16
+                            // values is exact in binary32, so the packed multiply
+                            // rounds it once, as the separate swish + mul
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            hv[i][j] = __hadd2(hv[i][j], a0[j]);
-                            hv[i][4 + j] = __hadd2(hv[i][4 + j], a1[j]);
+                            for (int j = 0; j < 8; ++j) {
+                                const float2 g = __half22float2(j < 4 ? a0[j] : a1[j - 4]);
+                                hv[i][j] = __hmul2(hv[i][j], __floats2half2_rn(silu_f(g.x), silu_f(g.y)));
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                hv[i][j] = __hadd2(hv[i][j], a0[j]);
+                                hv[i][4 + j] = __hadd2(hv[i][4 + j], a1[j]);
+                            }
                         }
                     }
-                    if constexpr (ACT != TK_ACT_NONE) {
+                    if constexpr (ACT != TK_ACT_NONE && ACT != TK_ACT_SILU_GATE) {
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
                             const float2 f = __half22float2(hv[i][j]);
@@ -812,7 +823,10 @@ int validate(const tk_qgemm_desc_t& d) {
     TK_CHECK_ARG(d.batch >= 0 && d.m >= 0 && d.n >= 0 && d.k >= 0, "qgemm: negative size");
     TK_CHECK_ARG(d.batch <= 65535 && d.m < (1LL << 31) && d.n < (1LL << 31) && d.k < (1LL << 31),
                  "qgemm: size out of range");
-    TK_CHECK_ARG(d.act >= TK_ACT_NONE && d.act <= TK_ACT_SILU, "qgemm: bad act %d", (int)d.act);
+    TK_CHECK_ARG(d.act >= TK_ACT_NONE && d.act <= TK_ACT_SILU_GATE, "qgemm: bad act %d", (int)d.act);
+    if (d.act == TK_ACT_SILU_GATE)
+        TK_CHECK_ARG(d.dtype == TK_DTYPE_F16 && d.addend != nullptr && d.beta == 1.0f,
+                     "qgemm: TK_ACT_SILU_GATE needs fp16, the gate as addend and beta == 1");
     if (d.batch * d.m * d.n > 0) TK_CHECK_ARG(d.out != nullptr, "qgemm: out is NULL");
     return TK_OK;
 }
@@ -910,6 +924,12 @@ int dispatch_act_ew(int act, int dev, int grid, const CUtensorMap& tmA, const CU
         case TK_ACT_GELU_TANH:
             return launch_one<C, DT, TK_ACT_GELU_TANH, EW, FO>(dev, grid, tmA, tmB, tp, ep, stream);
         case TK_ACT_SILU: return launch_one<C, DT, TK_ACT_SILU, EW, FO>(dev, grid, tmA, tmB, tp, ep, stream);
+        case TK_ACT_SILU_GATE:
+            if constexpr (FO) {
+                return launch_one<C, DT, TK_ACT_SILU_GATE, EW, FO>(dev, grid, tmA, tmB, tp, ep, stream);
+            } else {
+                TK_FAIL(TK_ERR_UNSUPPORTED, "qgemm: TK_ACT_SILU_GATE runs on the fp16 vector epilogue only");
+            }
         default: TK_FAIL(TK_ERR_INVALID_ARG, "qgemm: bad act %d", act);
     }
 }
@@ -1097,6 +1117,7 @@ int run(const tk_qgemm_desc_t* desc, void* ws, size_t ws_bytes, cudaStream_t str
     };
 
     if (path == Path::Simt || d.k == 0) {
+        if (d.act == TK_ACT_SILU_GATE) TK_FAIL(TK_ERR_UNSUPPORTED, "qgemm: TK_ACT_SILU_GATE needs K > 0 on the tensor-core path");
         dim3 grid(static_cast<unsigned>(ceil_div(d.n, 128)), static_cast<unsigned>(d.m),
                   static_cast<unsigned>(d.batch));
         TK_CHECK_ARG(d.m <= 65535 || path == Path::TensorCore,
@@ -1214,12 +1235,17 @@ int tk_qgemm_from_limbs(const tk_qgemm_desc_t* desc, const int8_t* a_limbs, cons
     if (d.batch == 0 || d.m == 0 || d.n == 0) return TK_OK;
     TK_CHECK_ARG(d.k > 0, "qgemm_from_limbs: K must be positive");
     TK_CHECK_ARG(a_limbs && b_limbs && amax_a && amax_b, "qgemm_from_limbs: NULL pointer");
-    TK_CHECK_ARG(d.amax_out == nullptr, "qgemm_from_limbs: amax_out is not supported");
     TK_CHECK_ARG(reinterpret_cast<uintptr_t>(a_limbs) % 16 == 0 &&
                      reinterpret_cast<uintptr_t>(b_limbs) % 16 == 0,
                  "qgemm_from_limbs: limb planes must be 16-byte aligned");
     const int64_t ld = static_cast<int64_t>(round_up(static_cast<size_t>(d.k), 16));
     EpiParams ep = make_epi(d, amax_a, amax_b, nullptr);
+    if (d.amax_out != nullptr) {
+        // folded into the fp16 vector epilogue, which every output takes
+        TK_CHECK_ARG(fast_epilogue_ep(ep), "qgemm_from_limbs: amax_out needs the fp16 vector epilogue");
+        TK_CUDA_TRY(cudaMemsetAsync(d.amax_out, 0, sizeof(float), static_cast<cudaStream_t>(stream)));
+        ep.amax_out = reinterpret_cast<unsigned*>(d.amax_out);
+    }
     return launch_tc(d, a_limbs, b_limbs, ld, ep, static_cast<cudaStream_t>(stream));
 }
 

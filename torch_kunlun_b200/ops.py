@@ -17,7 +17,7 @@ import torch
 
 from . import _C
 
-ACT = {"none": 0, "relu": 1, "gelu": 2, "gelu_tanh": 3, "silu": 4}
+ACT = {"none": 0, "relu": 1, "gelu": 2, "gelu_tanh": 3, "silu": 4, "silu_gate": 5}
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
@@ -70,10 +70,17 @@ def quantize_limbs(x: torch.Tensor, amax: torch.Tensor) -> torch.Tensor:
 
 def linear_from_limbs(a_limbs: torch.Tensor, b_limbs: torch.Tensor, k: int, amax_a: torch.Tensor,
                       amax_b: torch.Tensor, bias: Optional[torch.Tensor] = None, act: str = "none",
-                      out: Optional[torch.Tensor] = None, dtype: torch.dtype = torch.float16) -> torch.Tensor:
+                      out: Optional[torch.Tensor] = None, dtype: torch.dtype = torch.float16,
+                      gate: Optional[torch.Tensor] = None,
+                      amax_out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """act(a b^T + bias) on operands from quantize_limbs: the values of
-    linear_scaled(a, b, amax_x=amax_a, amax_w=amax_b) (K <= 32768)."""
-    return _C.linear_from_limbs(a_limbs, b_limbs, k, amax_a, amax_b, bias, ACT[act], out, dtype)
+    linear_scaled(a, b, amax_x=amax_a, amax_w=amax_b) (K <= 32768).
+
+    act="silu_gate" with `gate` [M, N]: T(silu(gate)) * (a b^T + bias), each
+    product rounded once -- silu_mul(gate, up) fused into the up projection.
+    amax_out (1-element fp32, written) receives max |y| from the epilogue
+    (fp16 outputs on the vector path)."""
+    return _C.linear_from_limbs(a_limbs, b_limbs, k, amax_a, amax_b, bias, ACT[act], out, dtype, gate, amax_out)
 
 
 __all__ = ["linear", "silu_mul", "silu_mul_amax", "amax", "linear_scaled", "quantize_limbs",

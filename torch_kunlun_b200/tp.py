@@ -9,8 +9,10 @@ are summed by an all-reduce (or reduce-scattered by rows).  Every rank
 quantises its own shards with their own per-tensor scales, as separate
 per-rank linear calls of the reference would.  Each operand is quantised
 once per step: x once for both the gate and the up GEMM (one scale, so the
-same codes), the down weight once for all of its row blocks, and the gated
-activation's scale comes out of the SiLU gate's own pass.
+same codes), the down weight once for all of its row blocks.  The SiLU gate
+runs in the up projection's epilogue (``T(silu(gate)) * up``, each product
+rounded once as the separate swish and mul), which also folds the gated
+activation's per-tensor scale, so ``up`` is never stored.
 
 Reductions of the partial sums:
 
@@ -197,10 +199,18 @@ def tp_mlp_forward(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
     xl = _C.quantize_limbs(x, ax)
     awg, awu = _C.amax(w_gate), _C.amax(w_up)
     gate = _C.linear_from_limbs(xl, _C.quantize_limbs(w_gate, awg), H, ax, awg, None, 0, None, dt)
-    up = _C.linear_from_limbs(xl, _C.quantize_limbs(w_up, awu), H, ax, awu, None, 0, None, dt)
-    del xl
-    h, ah = _C.silu_mul_amax(gate, up)  # the gate and its per-tensor scale, one pass
-    del gate, up
+    wul = _C.quantize_limbs(w_up, awu)
+    if dt == torch.float16 and gate.shape[1] % 16 == 0:
+        # h = T(silu(gate)) * up and its per-tensor scale from the up
+        # projection's epilogue: up itself is never stored
+        ah = torch.empty(1, dtype=torch.float32, device=x.device)
+        h = _C.linear_from_limbs(xl, wul, H, ax, awu, None, ops.ACT["silu_gate"], None, dt, gate, ah)
+        del xl, wul, gate
+    else:
+        up = _C.linear_from_limbs(xl, wul, H, ax, awu, None, 0, None, dt)
+        del xl, wul
+        h, ah = _C.silu_mul_amax(gate, up)  # the gate and its per-tensor scale, one pass
+        del gate, up
     Fl = h.shape[1]
     aw = _C.amax(w_down)
     world = _world(group)
