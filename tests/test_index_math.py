@@ -5,7 +5,7 @@ import itertools
 
 
 def ring_positions(H, W, ph, pw):
-    """zero_ring_kernel (conv_tc.cu): ring index -> (hp, wp) of the padded plane."""
+    """zero_ring_blocks (conv_tc.cu): ring index -> (hp, wp) of the padded plane."""
     Hp, Wp = H + 2 * ph, W + 2 * pw
     band = ph * Wp
     out = []
@@ -33,7 +33,7 @@ def test_zero_ring_enumerates_exactly_the_padding():
 
 
 def test_input_limb_rows_swizzle():
-    """x_limbs_kernel (conv_tc.cu): thread t covers pixel group pg and channel
+    """x_limbs_block (conv_tc.cu): thread t covers pixel group pg and channel
     quad cc4; its hi / lo words land in 32 distinct banks per warp store and
     phase 2 reads logical 16-byte chunk ch at physical chunk ch ^ (pg & 7)."""
     cover = set()
@@ -62,7 +62,7 @@ def test_input_limb_rows_swizzle():
 
 
 def test_stacked_weight_layout_covers_every_k_step_once():
-    """w_stack_kernel / conv_stk_kernel (conv_tc.cu): K step kb = tap*Cg + g
+    """w_stack_blocks / conv_stk_kernel (conv_tc.cu): K step kb = tap*Cg + g
     lives in pair kb // 2 at byte offset 64 * (kb % 2); the MMA for sub-block u
     reads bytes [64h + 32u, 64h + 32u + 32) of the pair's rows."""
     for taps, Cg in itertools.product((1, 2, 3, 9), (1, 2, 4)):

@@ -9,11 +9,14 @@
 // weight, exact integer MAC, T(acc * s), then the bias added and rounded.
 //
 // Data flow (no patch matrix in HBM):
-//   x_limbs_kernel   NC(D)HW input -> quantised N(D)HWC limb rows: per pixel, per
+//   conv_prep_kernel one launch whose blocks do three disjoint jobs:
+//     x_limbs_block  NC(D)HW input -> quantised N(D)HWC limb rows: per pixel, per
 //                    group of 64 channels, 128 bytes [hi of the 64 | lo of
 //                    the 64] (hi = q >> 8 signed, lo = q & 255 unsigned);
-//   w_limbs_kernel   OI(D)HW weight -> [F][KD][KH][KW][channel groups] limb rows of
-//                    the same 128-byte form;
+//     w_limbs_block  OI(D)HW weight -> [F][KD][KH][KW][channel groups] limb rows of
+//                    the same 128-byte form (w_stack_blocks: the stacked
+//                    tiles of the stacked-limb kernel);
+//     zero_ring_blocks the zero ring of the padded planes (window kernels);
 //   conv_tc_kernel   one CTA per SM, persistent over output tiles of
 //                    TH x TW pixels of one (image, output depth) x BN
 //                    filters.  Each K step is one (tap, 64-channel group):
@@ -49,6 +52,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "tk_internal.h"
 #include "tk_numerics.cuh"
@@ -898,7 +902,7 @@ static_assert(Q1_SMEM <= 227 * 1024, "fits one CTA's shared memory");
 static_assert(NUM_EPI_WARPS == 16, "four worker warps per lane quarter");
 
 // The stacked filter block of conv1x1_q_kernel (the layout of
-// w_stack_kernel, swizzled as the MMAs read it) written by the 512 worker
+// w_stack_blocks, swizzled as the MMAs read it) written by the 512 worker
 // threads into `stk`: 16-byte piece `pc8` of row n of pair `pair`, one piece
 // per thread at a time.  Out of line, so its temporaries do not crowd the
 // registers of the quantise / epilogue loop.
@@ -1245,14 +1249,14 @@ __device__ __forceinline__ void pack16(const int16_t* q, int stride, uint4& hi, 
 // 16-byte chunks are XOR-swizzled by the pixel group, so each of its stores
 // hits 32 different banks.
 template <typename T>
-__global__ void __launch_bounds__(XQ_THREADS)
-x_limbs_kernel(const T* __restrict__ x, int C, int64_t HW, int W, int ph, int pw, int Hp, int Wp,
-               int Cg, int vec, const float* __restrict__ amax, uint8_t* __restrict__ xl) {
+__device__ __forceinline__ void x_limbs_block(const T* __restrict__ x, int C, int64_t HW, int W, int ph, int pw,
+                                              int Hp, int Wp, int Cg, int vec, const float* __restrict__ amax,
+                                              uint8_t* __restrict__ xl, int64_t bid) {
     static_assert(XQ_THREADS == 256 && XQ_W == 128, "16 channel quads x 16 pixel groups of 8");
     __shared__ __align__(16) uint32_t rows[XQ_W][32];
     const int64_t runs = ceil_div_dev(HW, XQ_W);
-    const int g = blockIdx.x % Cg;
-    const int64_t r = blockIdx.x / Cg;
+    const int g = static_cast<int>(bid % Cg);
+    const int64_t r = bid / Cg;
     const int64_t p0 = (r % runs) * XQ_W;
     const int64_t n = r / runs;
     const int pn = static_cast<int>(HW - p0 < XQ_W ? HW - p0 : XQ_W);
@@ -1322,16 +1326,16 @@ x_limbs_kernel(const T* __restrict__ x, int C, int64_t HW, int W, int ph, int pw
 }
 
 // Zero the padding ring of the zero-padded limb planes [N][Hp][Wp][Cg*128]
-// (x_limbs_kernel writes the interior): thread per 16-byte piece of a ring
+// (x_limbs_block writes the interior): thread per 16-byte piece of a ring
 // position; the ring of one image is ph full rows at the top and bottom and
 // pw columns at both ends of the H rows between.
-__global__ void zero_ring_kernel(uint8_t* __restrict__ xl, int64_t N, int H, int W, int ph, int pw, int Cg) {
+__device__ __forceinline__ void zero_ring_blocks(uint8_t* __restrict__ xl, int64_t N, int H, int W, int ph, int pw,
+                                                 int Cg, int64_t bid, int64_t nblocks) {
     const int Hp = H + 2 * ph, Wp = W + 2 * pw;
     const int64_t ring = static_cast<int64_t>(Hp) * Wp - static_cast<int64_t>(H) * W;
     const int pieces = Cg * 8;
     const int64_t total = N * ring * pieces;
-    for (int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < total;
-         it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    for (int64_t it = bid * blockDim.x + threadIdx.x; it < total; it += nblocks * blockDim.x) {
         const int piece = static_cast<int>(it % pieces);
         const int64_t r = it / pieces;
         const int64_t n = r / ring;
@@ -1362,13 +1366,13 @@ __global__ void zero_ring_kernel(uint8_t* __restrict__ xl, int64_t N, int H, int
 // (q >> 8) + 128 of filter n, rows 64-127 q & 255 of filter n - 64, rows
 // 128-143 ones.  Thread per 16-byte piece.
 template <typename T>
-__global__ void w_stack_kernel(const T* __restrict__ w, int F, int C, int taps, int Cg, int npairs,
-                               const float* __restrict__ amax, uint8_t* __restrict__ ws) {
+__device__ __forceinline__ void w_stack_blocks(const T* __restrict__ w, int F, int C, int taps, int Cg, int npairs,
+                                               const float* __restrict__ amax, uint8_t* __restrict__ ws,
+                                               int64_t bid, int64_t nblocks) {
     const int64_t total = static_cast<int64_t>(npairs) * STK_N * 8;
     const float inv = quant_inv(__ldg(amax));
     const int nkb = taps * Cg;
-    for (int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < total;
-         it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    for (int64_t it = bid * blockDim.x + threadIdx.x; it < total; it += nblocks * blockDim.x) {
         const int piece = static_cast<int>(it & 7);  // 16-byte piece of the 128-byte row
         const int64_t r = it >> 3;
         const int n = static_cast<int>(r % STK_N);
@@ -1404,18 +1408,18 @@ __global__ void w_stack_kernel(const T* __restrict__ w, int F, int C, int taps, 
 constexpr int WQ_TAPS = 32;
 
 template <typename T>
-__global__ void __launch_bounds__(128)
-w_limbs_kernel(const T* __restrict__ w, int F, int C, int taps, int Cg, const float* __restrict__ amax,
-               uint8_t* __restrict__ wl) {
+__device__ __forceinline__ void w_limbs_block(const T* __restrict__ w, int F, int C, int taps, int Cg,
+                                              const float* __restrict__ amax, uint8_t* __restrict__ wl,
+                                              int bid) {
     __shared__ int16_t q[64][WQ_TAPS + 2];
     const int runs = (taps + WQ_TAPS - 1) / WQ_TAPS;
-    const int run = blockIdx.x % runs;
-    const int g = (blockIdx.x / runs) % Cg;
-    const int f = blockIdx.x / (runs * Cg);
+    const int run = bid % runs;
+    const int g = (bid / runs) % Cg;
+    const int f = bid / (runs * Cg);
     const int t0 = run * WQ_TAPS;
     const int nt = min(WQ_TAPS, taps - t0);
     const float inv = quant_inv(__ldg(amax));
-    for (int it = threadIdx.x; it < 64 * WQ_TAPS; it += 128) {
+    for (int it = threadIdx.x; it < 64 * WQ_TAPS; it += blockDim.x) {
         const int cc = it / WQ_TAPS, t = it - (it / WQ_TAPS) * WQ_TAPS;
         const int c = g * 64 + cc;
         int v = 0;
@@ -1423,7 +1427,7 @@ w_limbs_kernel(const T* __restrict__ w, int F, int C, int taps, int Cg, const fl
         q[cc][t] = static_cast<int16_t>(v);
     }
     __syncthreads();
-    for (int it = threadIdx.x; it < nt * 4; it += 128) {
+    for (int it = threadIdx.x; it < nt * 4; it += blockDim.x) {
         const int t = it >> 2, pc = it & 3;
         uint4 hi, lo;
         pack16(&q[pc * 16][t], WQ_TAPS + 2, hi, lo);
@@ -1431,6 +1435,48 @@ w_limbs_kernel(const T* __restrict__ w, int F, int C, int taps, int Cg, const fl
         *reinterpret_cast<uint4*>(dst) = hi;
         *reinterpret_cast<uint4*>(dst + 64) = lo;
     }
+}
+
+// Everything the implicit-GEMM kernels read, prepared by one launch of
+// 256-thread blocks split by block index into three independent parts: the
+// weight's limb rows (stacked tiles or per-filter rows), the zero ring of the
+// padded input planes, and the input's limb rows.  The parts write disjoint
+// bytes.  The weight blocks come first, so their short, latency-bound work
+// starts at once and overlaps the input blocks instead of following them as
+// separate launches.
+template <typename T>
+struct ConvPrepArgs {
+    const T* x;
+    const T* w;
+    const float* amax_x;
+    const float* amax_w;
+    uint8_t* xl;
+    uint8_t* wl;
+    int64_t N, DHW;
+    int C, F, H, W, ph, pw, sh, sw, Cg, taps, npairs, xvec;
+    int stk;          // stacked weight tiles (w_stack) instead of per-filter rows (w_limbs)
+    unsigned wgrid;   // blocks of the weight part
+    unsigned zgrid;   // blocks of the ring part (0 without padding)
+};
+
+template <typename T>
+__global__ void __launch_bounds__(XQ_THREADS) conv_prep_kernel(ConvPrepArgs<T> a) {
+    unsigned b = blockIdx.x;
+    if (b < a.wgrid) {
+        if (a.stk)
+            w_stack_blocks<T>(a.w, a.F, a.C, a.taps, a.Cg, a.npairs, a.amax_w, a.wl, b, a.wgrid);
+        else
+            w_limbs_block<T>(a.w, a.F, a.C, a.taps, a.Cg, a.amax_w, a.wl, static_cast<int>(b));
+        return;
+    }
+    b -= a.wgrid;
+    if (b < a.zgrid) {
+        zero_ring_blocks(a.xl, a.N, a.H, a.W, a.ph, a.pw, a.Cg, b, a.zgrid);
+        return;
+    }
+    b -= a.zgrid;
+    x_limbs_block<T>(a.x, a.C, a.DHW, a.W, a.ph, a.pw, a.sh, a.sw, a.Cg, a.xvec, a.amax_x, a.xl,
+                     static_cast<int64_t>(b));
 }
 
 template <class C, int DT>
@@ -1587,50 +1633,51 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
     const size_t x_bytes = static_cast<size_t>(N * sh * sw * Cg * 128);
     uint8_t* xl = ws;
     uint8_t* wl = ws + round_up(x_bytes, 1024);
+    int64_t zblocks = 0;
     if (win && (ph > 0 || pw > 0)) {
         const int64_t ring = Hp * Wp - H * W;
         const int64_t total = N * ring * Cg * 8;
-        const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), 8LL * sm_count(dev)));
-        zero_ring_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(xl, N, (int)H, (int)W, (int)ph, (int)pw,
-                                                                           (int)Cg);
+        zblocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), 8LL * sm_count(dev)));
     }
     const int64_t DHW = D * H * W;  // the image's flattened volume (rows of limbs)
     const int64_t runs = ceil_div(DHW, XQ_W);
     TK_CHECK_ARG(N * runs * Cg < (1LL << 31) && DHW < (1LL << 31), "conv: input too large");
-    const unsigned xgrid = static_cast<unsigned>(N * runs * Cg);
+    const int64_t xblocks = N * runs * Cg;
     const size_t es = dtype_size(dtype);
     const int xvec = (DHW % static_cast<int64_t>(16 / es) == 0 &&
                       reinterpret_cast<uintptr_t>(x) % 16 == 0) ? 1 : 0;
-    const int oph = win ? static_cast<int>(ph) : 0, opw = win ? static_cast<int>(pw) : 0;
     const int64_t taps = KD * KH * KW;
     // stacked-limb window kernel when the stacked filter block stays resident
     // (the four-MMA window kernel otherwise)
     const bool stk = win && stk_fits;
-    const int64_t wblocks = F * Cg * ceil_div(taps, WQ_TAPS);
-    TK_CHECK_ARG(wblocks < (1LL << 31), "conv: weight too large");
-    const unsigned wgrid = static_cast<unsigned>(wblocks);
-    const unsigned sgrid = static_cast<unsigned>(ceil_div(npairs * STK_N * 8, 256));
-    if (dtype == TK_DTYPE_F16) {
-        x_limbs_kernel<__half><<<xgrid, XQ_THREADS, 0, stream>>>(
-            static_cast<const __half*>(x), (int)C, DHW, (int)W, oph, opw, (int)sh, (int)sw, (int)Cg, xvec,
-            amax_x, xl);
-        if (stk)
-            w_stack_kernel<__half><<<sgrid, 256, 0, stream>>>(static_cast<const __half*>(w), (int)F, (int)C,
-                                                              (int)taps, (int)Cg, (int)npairs, amax_w, wl);
-        else
-            w_limbs_kernel<__half><<<wgrid, 128, 0, stream>>>(static_cast<const __half*>(w), (int)F, (int)C,
-                                                              (int)taps, (int)Cg, amax_w, wl);
-    } else {
-        x_limbs_kernel<float><<<xgrid, XQ_THREADS, 0, stream>>>(
-            static_cast<const float*>(x), (int)C, DHW, (int)W, oph, opw, (int)sh, (int)sw, (int)Cg, xvec,
-            amax_x, xl);
-        if (stk)
-            w_stack_kernel<float><<<sgrid, 256, 0, stream>>>(static_cast<const float*>(w), (int)F, (int)C,
-                                                             (int)taps, (int)Cg, (int)npairs, amax_w, wl);
-        else
-            w_limbs_kernel<float><<<wgrid, 128, 0, stream>>>(static_cast<const float*>(w), (int)F, (int)C,
-                                                             (int)taps, (int)Cg, amax_w, wl);
-    }
+    const int64_t wblocks = stk ? ceil_div(npairs * STK_N * 8, 256) : F * Cg * ceil_div(taps, WQ_TAPS);
+    TK_CHECK_ARG(wblocks + zblocks + xblocks < (1LL << 31), "conv: weight or input too large");
+    auto prep = [&](auto* tag) {
+        using T = std::remove_pointer_t<decltype(tag)>;
+        ConvPrepArgs<T> a;
+        a.x = static_cast<const T*>(x);
+        a.w = static_cast<const T*>(w);
+        a.amax_x = amax_x;
+        a.amax_w = amax_w;
+        a.xl = xl;
+        a.wl = wl;
+        a.N = N;
+        a.DHW = DHW;
+        a.C = (int)C; a.F = (int)F; a.H = (int)H; a.W = (int)W;
+        a.ph = win ? (int)ph : 0;  // the stored planes are padded only for the window kernels
+        a.pw = win ? (int)pw : 0;
+        a.sh = (int)sh; a.sw = (int)sw; a.Cg = (int)Cg; a.taps = (int)taps; a.npairs = (int)npairs;
+        a.xvec = xvec;
+        a.stk = stk ? 1 : 0;
+        a.wgrid = static_cast<unsigned>(wblocks);
+        a.zgrid = static_cast<unsigned>(zblocks);
+        const unsigned grid = static_cast<unsigned>(wblocks + zblocks + xblocks);
+        conv_prep_kernel<T><<<grid, XQ_THREADS, 0, stream>>>(a);
+    };
+    if (dtype == TK_DTYPE_F16)
+        prep(static_cast<__half*>(nullptr));
+    else
+        prep(static_cast<float*>(nullptr));
     int rc = launch_status("conv2d limbs");
     if (rc) return rc;
 

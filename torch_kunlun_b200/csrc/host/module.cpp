@@ -38,10 +38,12 @@ void register_peer(pybind11::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     using namespace torch_kunlun;
+    // The blocking waits release the GIL, so other Python threads (a clock
+    // sampler, a data loader) keep running while the host waits on the GPU.
     m.def("device_count", &device_count);
     m.def("current_device", &current_device);
     m.def("set_device", &set_device);
-    m.def("synchronize", &synchronize_all);
+    m.def("synchronize", &synchronize_all, py::call_guard<py::gil_scoped_release>());
     m.def("memory_allocated", [](int d) { return memory_allocated(d); }, py::arg("device") = -1);
     m.def("max_memory_allocated", [](int d) { return max_memory_allocated(d); },
           py::arg("device") = -1);
@@ -67,13 +69,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("create_stream", &create_stream, py::arg("device"), py::arg("priority") = 0);
     m.def("destroy_stream", &destroy_stream);
     m.def("set_stream", &set_current_stream);
-    m.def("synchronize_stream", &synchronize_stream);
+    m.def("synchronize_stream", &synchronize_stream, py::call_guard<py::gil_scoped_release>());
     m.def("stream_query", &stream_query);
     m.def("event_create", &event_create, py::arg("device"), py::arg("timing") = false);
     m.def("event_destroy", &event_destroy);
     m.def("event_record", &event_record);
     m.def("stream_wait_event", &stream_wait_event);
-    m.def("event_synchronize", &event_synchronize);
+    m.def("event_synchronize", &event_synchronize, py::call_guard<py::gil_scoped_release>());
     m.def("event_query", &event_query);
     m.def("event_elapsed_time", &event_elapsed_ms);
 
