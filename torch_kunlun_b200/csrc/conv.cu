@@ -10,10 +10,11 @@
 // Paths:
 //   * 2-D, groups == C == F/mult (depthwise): CUDA-core kernels with exact
 //     integer sums of the KHxKW taps.  Multiplier 1, unit stride and
-//     dilation: one cooperative launch that also forms both scales
-//     (depthwise_fused_kernel) when its grid is resident at once, else the
-//     amax launch and the row kernel; other depthwise shapes use the plane,
-//     flat or per-output kernels.
+//     dilation: the amax-partials kernel and depthwise_scaled_kernel,
+//     which starts loading its planes while the partials form (programmatic
+//     dependent launch) and quantises from shared memory, when its grid fits
+//     in one wave; else the amax launch and the row kernel; other depthwise
+//     shapes use the plane, flat or per-output kernels.
 //   * groups == 1, stride 1: implicit GEMM on the tensor cores (conv_tc.cu),
 //     no patch matrix in HBM.
 //   * otherwise a GEMM per (image, group) on the tensor-core limb kernel:
@@ -426,23 +427,21 @@ depthwise_rows_kernel(const T* __restrict__ x, const T* __restrict__ w, const T*
     }
 }
 
-// The same depthwise convolution with the two max-abs reductions folded in:
-// one cooperative launch in which every block loads its planes (and its
-// channels' filters) into shared memory once, folds their magnitudes into
-// the two scale words, waits at a grid-wide barrier for every block's
-// contribution, then quantises from shared memory, convolves and stores the
-// block's contiguous span of the output with 16-byte vectors.  The input
-// crosses HBM once (the separate amax pass read it twice) and the op is one
-// launch after a memset of the scale words and the barrier words.
-// sync[0], sync[1]: fp32 magnitude bits of max |x| and max |w| (atomicMax,
-// NaN above everything, as the amax kernels); sync[kDwSyncCount]: blocks
-// arrived; sync[kDwSyncFlag]: set by the last block to arrive.  The three
-// live on separate 128-byte lines, so the blocks polling the flag do not
-// slow the arrivals' atomics.
-constexpr int kDwSyncCount = 32;
-constexpr int kDwSyncFlag = 64;
-constexpr int kDwSyncWords = kDwSyncFlag + 1;
+// The same depthwise convolution as two launches that overlap through
+// programmatic dependent launch.  depthwise_amax_kernel folds the fp32
+// magnitude bits (NaN above everything, as the amax kernels) of one chunk of
+// the input and one chunk of the filters per block into its own partial
+// word -- plain stores, so no memset is needed -- and first of all lets the
+// dependent launch start.  depthwise_scaled_kernel, launched with
+// programmatic stream serialisation, loads its block's planes and filters
+// into shared memory while the partials are still being formed, waits
+// (griddepcontrol.wait: the first grid has completed and its stores are
+// visible) and folds the partials; then it quantises from shared memory,
+// convolves and stores the block's contiguous span of the output with
+// 16-byte vectors.  No grid barrier and no co-residency requirement.
 constexpr int kDwMaxThreads = 512;
+constexpr int kDwAmaxThreads = 256;
+constexpr int kDwAmaxMaxBlocks = 512;  // partial words per operand in the workspace
 
 struct DwMagic {
     uint32_t hw, w, taps, ohw, ow, h, oh;  // floor(2^32 / d) + 1 for i / d with i, d < 2^16
@@ -478,10 +477,53 @@ __device__ __forceinline__ unsigned block_max_bits(unsigned v, unsigned* red) {
     return v;
 }
 
+// Magnitude bits (mag_bits) of p[b0, b1): 16-byte loads when `vec` (p
+// 16-byte aligned and b0 a multiple of the vector width).
+template <typename T>
+__device__ __forceinline__ unsigned span_max_bits(const T* __restrict__ p, int64_t b0, int64_t b1, bool vec) {
+    constexpr int VEC = 16 / sizeof(T);
+    unsigned m = 0u;
+    if (vec) {
+        const int64_t nv = (b1 - b0) / VEC;
+        const uint4* pv = reinterpret_cast<const uint4*>(p + b0);
+        for (int64_t j = threadIdx.x; j < nv; j += blockDim.x) {
+            const uint4 u = __ldg(pv + j);
+            const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) m = max(m, mag_bits<T>(e[k]));
+        }
+        b0 += nv * VEC;
+    }
+    for (int64_t i = b0 + threadIdx.x; i < b1; i += blockDim.x) m = max(m, mag_bits<T>(p[i]));
+    return m;
+}
+
+// Block b: part[b] = magnitude bits of max |x| over x[b*cx, (b+1)*cx),
+// part[gridDim.x + b] the same of w over w[b*cw, (b+1)*cw).
+template <typename T>
+__global__ void __launch_bounds__(kDwAmaxThreads)
+depthwise_amax_kernel(const T* __restrict__ x, int64_t nx, int64_t cx, int vx, const T* __restrict__ w,
+                      int64_t nw, int64_t cw, int vw, unsigned* __restrict__ part) {
+    __shared__ unsigned red[kDwAmaxThreads / 32];
+    // the convolution kernel may be scheduled now: it only loads its inputs
+    // until it waits for this grid
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int64_t b = blockIdx.x;
+    unsigned mx = span_max_bits<T>(x, min(nx, b * cx), min(nx, (b + 1) * cx), vx != 0);
+    unsigned mw = span_max_bits<T>(w, min(nw, b * cw), min(nw, (b + 1) * cw), vw != 0);
+    mx = block_max_bits(mx, red);
+    __syncthreads();
+    mw = block_max_bits(mw, red);
+    if (threadIdx.x == 0) {
+        part[b] = mx;
+        part[gridDim.x + b] = mw;
+    }
+}
+
 template <typename T, int DT, int KW>
 __global__ void __launch_bounds__(kDwMaxThreads)
-depthwise_fused_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ bias,
-                       T* __restrict__ out, ConvGeom g, int ppb, DwMagic mg, unsigned* sync, unsigned* err) {
+depthwise_scaled_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ bias,
+                        T* __restrict__ out, ConvGeom g, int ppb, DwMagic mg, const unsigned* part, int nparts) {
     extern __shared__ __align__(16) uint8_t dsm[];
     const int H = static_cast<int>(g.H), W = static_cast<int>(g.W);
     const int ph = static_cast<int>(g.ph), pw = static_cast<int>(g.pw);
@@ -504,72 +546,42 @@ depthwise_fused_kernel(const T* __restrict__ x, const T* __restrict__ w, const T
     int* wsq = reinterpret_cast<int*>(wf);
     unsigned* red = reinterpret_cast<unsigned*>(wf + ppb * taps);
 
-    // ---- phase 1: the block's input span and filters, and their magnitudes
+    // ---- phase 1: the block's input span and filters (neither is written
+    // by the amax grid, so they load before the wait)
     const T* xb = x + pl0 * HW;
     const int n = np * HW;
-    unsigned mx = 0u, mw = 0u;
     constexpr int VEC = 16 / sizeof(T);
     const bool aligned = reinterpret_cast<uintptr_t>(x) % 16 == 0;
     const int head = aligned ? min(n, static_cast<int>((VEC - (pl0 * HW) % VEC) % VEC)) : n;
     const int nv = (n - head) / VEC;
-    for (int i = threadIdx.x; i < head; i += blockDim.x) {
-        const T v = xb[i];
-        raw[i] = v;
-        mx = max(mx, mag_bits<T>(v));
-    }
+    for (int i = threadIdx.x; i < head; i += blockDim.x) raw[i] = xb[i];
     for (int v = threadIdx.x; v < nv; v += blockDim.x) {
-        const int i0 = head + v * VEC;
+        const int i0 = head + v * VEC;  // 16-byte aligned in global memory, not in the span
         const uint4 u = __ldg(reinterpret_cast<const uint4*>(xb + i0));
         const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
-        for (int k = 0; k < VEC; ++k) {
-            raw[i0 + k] = e[k];
-            mx = max(mx, mag_bits<T>(e[k]));
-        }
+        for (int k = 0; k < VEC; ++k) raw[i0 + k] = e[k];
     }
-    for (int i = head + nv * VEC + threadIdx.x; i < n; i += blockDim.x) {
-        const T v = xb[i];
-        raw[i] = v;
-        mx = max(mx, mag_bits<T>(v));
-    }
+    for (int i = head + nv * VEC + threadIdx.x; i < n; i += blockDim.x) raw[i] = xb[i];
     for (int i = threadIdx.x; i < np * taps; i += blockDim.x) {
         const int pp = div_magic(i, mg.taps), t = i - pp * taps;
         int c = c0 + pp;
         while (c >= C) c -= C;
-        const T v = w[static_cast<int64_t>(c) * taps + t];
-        wf[i] = static_cast<float>(v);
-        mw = max(mw, mag_bits<T>(v));
+        wf[i] = static_cast<float>(w[static_cast<int64_t>(c) * taps + t]);
+    }
+    // ---- the scales: wait for the amax grid, fold its partials (plain
+    // loads of words that grid stored)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    unsigned mx = 0u, mw = 0u;
+    for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
+        mx = max(mx, part[i]);
+        mw = max(mw, part[nparts + i]);
     }
     mx = block_max_bits(mx, red);
     __syncthreads();
     mw = block_max_bits(mw, red);
     __syncthreads();
-    // ---- grid-wide barrier (every block is resident: cooperative launch)
-    if (threadIdx.x == 0) {
-        if (mx != 0u) atomicMax(sync, mx);
-        // every channel's filter lies in the first C planes, so the blocks
-        // holding those planes carry max |w|
-        if (mw != 0u && pl0 < C) atomicMax(sync + 1, mw);
-        __threadfence();
-        if (atomicAdd(sync + kDwSyncCount, 1u) == gridDim.x - 1) {
-            // the last block: every other block's maxima are visible here
-            __threadfence();
-            st_release_gpu_u32(sync + kDwSyncFlag, 1u);
-        } else {
-            const uint64_t t0 = globaltimer_ns();
-            while (ld_acquire_gpu_u32(sync + kDwSyncFlag) == 0u) {
-                __nanosleep(64);
-                if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                    atomicCAS(err, 0u, static_cast<unsigned>(kDevErrWaitCluster));
-                    break;
-                }
-            }
-        }
-        red[0] = ld_acquire_gpu_u32(sync);
-        red[1] = ld_acquire_gpu_u32(sync + 1);
-    }
-    __syncthreads();
-    const float ax = __uint_as_float(red[0]), aw = __uint_as_float(red[1]);
+    const float ax = __uint_as_float(mx), aw = __uint_as_float(mw);
     const float invx = quant_inv(ax), invw = quant_inv(aw);
     const double s = dequant_scale(ax, aw);
 
@@ -672,8 +684,8 @@ depthwise_fused_kernel(const T* __restrict__ x, const T* __restrict__ w, const T
     for (int i = ohead + onv * VEC + threadIdx.x; i < no; i += blockDim.x) obase[i] = raw[i];
 }
 
-// Shared-memory bytes of depthwise_fused_kernel for `ppb` planes.
-size_t depthwise_fused_smem(const ConvGeom& g, int ppb, size_t esize) {
+// Shared-memory bytes of depthwise_scaled_kernel for `ppb` planes.
+size_t depthwise_scaled_smem(const ConvGeom& g, int ppb, size_t esize) {
     const int64_t hw = g.H * g.W, ohw = g.OH * g.OW;
     const int64_t phw = (g.H + 2 * g.ph) * (g.W + 2 * g.pw);
     size_t b = round_up(static_cast<size_t>(ppb * std::max(hw, ohw)) * esize, 16);
@@ -702,10 +714,12 @@ int depthwise_rows_ppb(const ConvGeom& g) {
 
 uint32_t magic_div(int64_t d) { return static_cast<uint32_t>((1ULL << 32) / static_cast<uint64_t>(d) + 1); }
 
-// The depthwise convolution with its scales in one cooperative launch, when
-// the row kernel's geometry applies and every block fits on the device at
-// once; TK_ERR_UNSUPPORTED otherwise (the caller takes the two-pass path).
-int depthwise_fused_launch(const tk_conv3d_desc_t& d, const ConvGeom& g, unsigned* sync, cudaStream_t stream) {
+// The depthwise convolution with its scales from the amax grid and the
+// convolution grid overlapping (programmatic dependent launch), when the row
+// kernel's geometry applies and the grid fits the device in one wave;
+// TK_ERR_UNSUPPORTED otherwise (the caller takes the two-pass path).
+// `part` holds 2 * kDwAmaxMaxBlocks words.
+int depthwise_scaled_launch(const tk_conv3d_desc_t& d, const ConvGeom& g, unsigned* part, cudaStream_t stream) {
     int ppb = depthwise_rows_ppb(g);
     // the kernel's int32 partial sums hold up to 64 taps
     if (ppb == 0 || g.KH * g.KW > 64) return TK_ERR_UNSUPPORTED;
@@ -716,16 +730,17 @@ int depthwise_fused_launch(const tk_conv3d_desc_t& d, const ConvGeom& g, unsigne
     const int dev = current_device();
     const void* fn = nullptr;
     if (d.dtype == TK_DTYPE_F16) {
-        fn = g.KW == 3 ? reinterpret_cast<const void*>(depthwise_fused_kernel<__half, 0, 3>)
-           : g.KW == 5 ? reinterpret_cast<const void*>(depthwise_fused_kernel<__half, 0, 5>)
-                       : reinterpret_cast<const void*>(depthwise_fused_kernel<__half, 0, 7>);
+        fn = g.KW == 3 ? reinterpret_cast<const void*>(depthwise_scaled_kernel<__half, 0, 3>)
+           : g.KW == 5 ? reinterpret_cast<const void*>(depthwise_scaled_kernel<__half, 0, 5>)
+                       : reinterpret_cast<const void*>(depthwise_scaled_kernel<__half, 0, 7>);
     } else {
-        fn = g.KW == 3 ? reinterpret_cast<const void*>(depthwise_fused_kernel<float, 1, 3>)
-           : g.KW == 5 ? reinterpret_cast<const void*>(depthwise_fused_kernel<float, 1, 5>)
-                       : reinterpret_cast<const void*>(depthwise_fused_kernel<float, 1, 7>);
+        fn = g.KW == 3 ? reinterpret_cast<const void*>(depthwise_scaled_kernel<float, 1, 3>)
+           : g.KW == 5 ? reinterpret_cast<const void*>(depthwise_scaled_kernel<float, 1, 5>)
+                       : reinterpret_cast<const void*>(depthwise_scaled_kernel<float, 1, 7>);
     }
     TK_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
-    // Every block must be resident at once.  Preferred: a balanced grid, the
+    // One resident wave (its blocks start loading while the partials form).
+    // Preferred: a balanced grid, the
     // same number k of blocks on every SM (planes per block = planes / (k x
     // SMs), rounded up) with enough threads that each block's input and
     // output rows take two rounds of its threads.  Else the planes per block
@@ -737,7 +752,7 @@ int depthwise_fused_launch(const tk_conv3d_desc_t& d, const ConvGeom& g, unsigne
     // spans are all in dynamic shared memory
     auto spans_ok = [&](int64_t cand) {
         return cand * std::max(hw, ohw) < 65536 && cand * taps < 65536 &&
-               depthwise_fused_smem(g, static_cast<int>(cand), esize) <= 96 * 1024;
+               depthwise_scaled_smem(g, static_cast<int>(cand), esize) <= 96 * 1024;
     };
     int64_t blocks = 0;
     size_t smem = 0;
@@ -747,7 +762,7 @@ int depthwise_fused_launch(const tk_conv3d_desc_t& d, const ConvGeom& g, unsigne
         const int64_t cand = ceil_div(planes, static_cast<int64_t>(k) * sms);
         const int64_t t = static_cast<int64_t>(round_up(static_cast<size_t>(ceil_div(cand * rows_pp, 2)), 32));
         if (t > kDwMaxThreads || !spans_ok(cand)) continue;
-        smem = depthwise_fused_smem(g, static_cast<int>(cand), esize);
+        smem = depthwise_scaled_smem(g, static_cast<int>(cand), esize);
         int per_sm = 0;
         TK_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, static_cast<int>(t), smem));
         ppb = static_cast<int>(cand);
@@ -758,7 +773,7 @@ int depthwise_fused_launch(const tk_conv3d_desc_t& d, const ConvGeom& g, unsigne
     for (int r = 1; r <= 8 && !fits; ++r) {
         const int64_t cand = std::max<int64_t>(1, (static_cast<int64_t>(r) * kDwRowThreads) / g.OH);
         if (!spans_ok(cand)) break;
-        smem = depthwise_fused_smem(g, static_cast<int>(cand), esize);
+        smem = depthwise_scaled_smem(g, static_cast<int>(cand), esize);
         int per_sm = 0;
         TK_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kDwRowThreads, smem));
         ppb = static_cast<int>(cand);
@@ -767,7 +782,24 @@ int depthwise_fused_launch(const tk_conv3d_desc_t& d, const ConvGeom& g, unsigne
         fits = per_sm > 0 && blocks <= static_cast<int64_t>(per_sm) * sms;
     }
     if (!fits) return TK_ERR_UNSUPPORTED;
-    TK_CUDA_TRY(cudaMemsetAsync(sync, 0, kDwSyncWords * sizeof(unsigned), stream));
+    // the partials: chunks of about 4 KB of the input per block (one or two
+    // 16-byte loads per thread), in whole 16-byte vectors
+    const int64_t nx = planes * hw, nw = g.C * taps;
+    const int64_t vecw = static_cast<int64_t>(16 / esize);
+    const int64_t nparts = std::max<int64_t>(
+        1, std::min<int64_t>(kDwAmaxMaxBlocks, ceil_div(nx * static_cast<int64_t>(esize), 4 * 1024)));
+    const int64_t cx = round_up(static_cast<size_t>(ceil_div(nx, nparts)), static_cast<size_t>(vecw));
+    const int64_t cw = round_up(static_cast<size_t>(ceil_div(nw, nparts)), static_cast<size_t>(vecw));
+    const int vx = reinterpret_cast<uintptr_t>(d.x) % 16 == 0 ? 1 : 0;
+    const int vw = reinterpret_cast<uintptr_t>(d.weight) % 16 == 0 ? 1 : 0;
+    if (d.dtype == TK_DTYPE_F16)
+        depthwise_amax_kernel<__half><<<static_cast<unsigned>(nparts), kDwAmaxThreads, 0, stream>>>(
+            static_cast<const __half*>(d.x), nx, cx, vx, static_cast<const __half*>(d.weight), nw, cw, vw, part);
+    else
+        depthwise_amax_kernel<float><<<static_cast<unsigned>(nparts), kDwAmaxThreads, 0, stream>>>(
+            static_cast<const float*>(d.x), nx, cx, vx, static_cast<const float*>(d.weight), nw, cw, vw, part);
+    int rc = launch_status("conv2d depthwise (amax partials)");
+    if (rc) return rc;
     ConvGeom gg = g;
     int ppb_arg = ppb;
     DwMagic mg;
@@ -778,16 +810,26 @@ int depthwise_fused_launch(const tk_conv3d_desc_t& d, const ConvGeom& g, unsigne
     mg.ow = magic_div(g.OW);
     mg.h = magic_div(g.H);
     mg.oh = magic_div(g.OH);
-    unsigned* err = device_error_word(dev);
     const void* xp = d.x;
     const void* wp = d.weight;
     const void* bp = d.bias;
     void* op = d.out;
+    const unsigned* pp = part;
+    int np_arg = static_cast<int>(nparts);
     void* args[] = {const_cast<void**>(&xp), const_cast<void**>(&wp), const_cast<void**>(&bp), &op, &gg, &ppb_arg,
-                    &mg, &sync, &err};
-    TK_CUDA_TRY(cudaLaunchCooperativeKernel(fn, dim3(static_cast<unsigned>(blocks)), dim3(threads), args,
-                                            smem, stream));
-    return launch_status("conv2d depthwise (fused scales)");
+                    &mg, &pp, &np_arg};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+    cfg.blockDim = dim3(static_cast<unsigned>(threads));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    TK_CUDA_TRY(cudaLaunchKernelExC(&cfg, fn, args));
+    return launch_status("conv2d depthwise (scaled)");
 }
 
 int grid_1d(int64_t n, int threads) {
@@ -855,8 +897,9 @@ ConvLayout conv_layout(const ConvGeom& g) {
     L.off_amax = 0;
     L.off_la = 1024;
     if (is_depthwise(g)) {
+        // the partial maxima of depthwise_scaled_launch follow the amax slots
         L.off_lb = L.off_la;
-        L.total = L.off_la;
+        L.total = L.off_la + 2 * kDwAmaxMaxBlocks * sizeof(unsigned);
         return L;
     }
     if (is_implicit(g)) {
@@ -1051,7 +1094,7 @@ int tk_conv3d_q16(const tk_conv3d_desc_t* desc, void* workspace, size_t workspac
     const float* ax = d.amax_x;
     const float* aw = d.amax_w;
     if (ax == nullptr && aw == nullptr) {
-        rc = depthwise_fused_launch(d, g, reinterpret_cast<unsigned*>(amax), stream);
+        rc = depthwise_scaled_launch(d, g, reinterpret_cast<unsigned*>(ws + L.off_la), stream);
         if (rc != TK_ERR_UNSUPPORTED) return rc;
     }
     if (ax == nullptr && aw == nullptr) {  // both scales in one launch
