@@ -1379,11 +1379,9 @@ __device__ __forceinline__ void w_stack_blocks(const T* __restrict__ w, int F, i
         const int pair = static_cast<int>(r / STK_N);
         const int h = piece >> 2, pc = piece & 3;
         const int kb = 2 * pair + h;
-        uint8_t b[16];
-        if (n >= 128) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) b[j] = 1;
-        } else {
+        // the 16 bytes as four little-endian words, built in registers
+        uint32_t b4[4] = {0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u};
+        if (n < 128) {
             const int f = n & 63;
             const int tap = kb / Cg, g = kb - (kb / Cg) * Cg;
 #pragma unroll
@@ -1392,12 +1390,12 @@ __device__ __forceinline__ void w_stack_blocks(const T* __restrict__ w, int F, i
                 int q = 0;
                 if (kb < nkb && f < F && c < C)
                     q = quant_one(ldt<T>(w, (static_cast<int64_t>(f) * C + c) * taps + tap), inv);
-                b[j] = static_cast<uint8_t>(n < 64 ? ((q >> 8) + 128) & 0xFF : q & 0xFF);
+                const uint32_t byte = static_cast<uint32_t>(n < 64 ? ((q >> 8) + 128) & 0xFF : q & 0xFF);
+                if ((j & 3) == 0) b4[j >> 2] = 0u;
+                b4[j >> 2] |= byte << (8 * (j & 3));
             }
         }
-        uint4 v;
-        memcpy(&v, b, 16);
-        *reinterpret_cast<uint4*>(ws + r * KB + piece * 16) = v;
+        *reinterpret_cast<uint4*>(ws + r * KB + piece * 16) = make_uint4(b4[0], b4[1], b4[2], b4[3]);
     }
 }
 
@@ -1419,11 +1417,13 @@ __device__ __forceinline__ void w_limbs_block(const T* __restrict__ w, int F, in
     const int t0 = run * WQ_TAPS;
     const int nt = min(WQ_TAPS, taps - t0);
     const float inv = quant_inv(__ldg(amax));
-    for (int it = threadIdx.x; it < 64 * WQ_TAPS; it += blockDim.x) {
-        const int cc = it / WQ_TAPS, t = it - (it / WQ_TAPS) * WQ_TAPS;
+    // only the run's nt taps (columns t >= nt of q are never packed); for one
+    // run the 64 x nt values are one contiguous span of w
+    for (int it = threadIdx.x; it < 64 * nt; it += blockDim.x) {
+        const int cc = it / nt, t = it - (it / nt) * nt;
         const int c = g * 64 + cc;
         int v = 0;
-        if (c < C && t < nt) v = quant_one(ldt<T>(w, (static_cast<int64_t>(f) * C + c) * taps + t0 + t), inv);
+        if (c < C) v = quant_one(ldt<T>(w, (static_cast<int64_t>(f) * C + c) * taps + t0 + t), inv);
         q[cc][t] = static_cast<int16_t>(v);
     }
     __syncthreads();
