@@ -273,6 +273,10 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // launched with programmatic stream serialisation: the prologue above
+    // touched only shared memory, TMEM and the kernel's parameters; the
+    // limbs, amax values, bias and residual are read after this
+    pdl_wait();
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -910,7 +914,19 @@ int launch_one(int dev, int grid, const CUtensorMap& tmA, const CUtensorMap& tmB
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         });
     }
-    qgemm_tc_kernel<C, DT, ACT, EW, FO><<<grid, 64 + 32 * EW, C::SMEM, stream>>>(tmA, tmB, tp, ep);
+    // programmatic stream serialisation: the CTAs may be placed and run
+    // their prologue while the quantise kernel before them drains
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(64 + 32 * EW);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    TK_CUDA_TRY(cudaLaunchKernelEx(&cfg, qgemm_tc_kernel<C, DT, ACT, EW, FO>, tmA, tmB, tp, ep));
     return TK_OK;
 }
 

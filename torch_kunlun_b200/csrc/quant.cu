@@ -12,6 +12,7 @@
 
 #include "tk_internal.h"
 #include "tk_numerics.cuh"
+#include "tk_ptx.cuh"
 
 namespace tk {
 namespace {
@@ -217,6 +218,7 @@ __device__ __forceinline__ unsigned amax_range<float>(const float* xf, int64_t s
 template <typename T>
 __global__ void __launch_bounds__(kAmaxThreads)
 amax_multi_kernel(AmaxDesc d0, AmaxDesc d1, int64_t blocks0) {
+    pdl_trigger();  // a quantise kernel launched next may be placed now (it waits for this grid)
     int64_t b = blockIdx.x;
     const AmaxDesc& d = b < blocks0 ? d0 : d1;
     if (b >= blocks0) b -= blocks0;
@@ -424,6 +426,8 @@ __device__ __forceinline__ void quant_vec_segment(const QVecDesc& d, int64_t row
 template <typename T>
 __global__ void __launch_bounds__(256) quant_vec_kernel(QVecDesc d0, QVecDesc d1, int64_t items0,
                                                         int64_t items_total) {
+    pdl_trigger();  // the GEMM that consumes the limbs may begin its prologue
+    pdl_wait();     // the amax (and whatever wrote x) has completed
     const int64_t item = static_cast<int64_t>(blockIdx.x) * 8 + threadIdx.y;
     if (item >= items_total) return;
     const bool first = item < items0;
@@ -554,13 +558,21 @@ int launch_quant_vec(tk_dtype_t dt, const QVecDesc* vd, int nvec, cudaStream_t s
     const int64_t blocks = ceil_div(items0 + items1, 8);
     TK_CHECK_ARG(blocks < (1LL << 31), "quantise: too many rows");
     const QVecDesc second = nvec > 1 ? vd[1] : vd[0];
-    const dim3 block(32, 8);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+    cfg.blockDim = dim3(32, 8);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const int64_t total = items0 + items1;
     if (dt == TK_DTYPE_F16)
-        quant_vec_kernel<__half><<<static_cast<unsigned>(blocks), block, 0, stream>>>(
-            vd[0], second, items0, items0 + items1);
+        TK_CUDA_TRY(cudaLaunchKernelEx(&cfg, quant_vec_kernel<__half>, vd[0], second, items0, total));
     else
-        quant_vec_kernel<float><<<static_cast<unsigned>(blocks), block, 0, stream>>>(
-            vd[0], second, items0, items0 + items1);
+        TK_CUDA_TRY(cudaLaunchKernelEx(&cfg, quant_vec_kernel<float>, vd[0], second, items0, total));
     return launch_status("quantise");
 }
 

@@ -33,6 +33,20 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
+// ---- programmatic dependent launch ------------------------------------------
+// A kernel launched with programmatic stream serialisation may start before
+// the previous kernel on its stream has finished; pdl_wait() blocks until
+// that kernel has completed and its memory operations are visible (a no-op
+// for a kernel launched without the attribute).  Every such kernel calls it
+// before its first access to global memory.  pdl_trigger() lets the next
+// kernel's launch begin before this one ends; kernels that allocate TMEM
+// never call it, so a dependent TMEM user starts only after their CTAs have
+// exited.
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- mbarrier ---------------------------------------------------------------
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
