@@ -53,6 +53,7 @@
 #include <cstring>
 #include <mutex>
 #include <type_traits>
+#include <utility>
 
 #include "tk_internal.h"
 #include "tk_numerics.cuh"
@@ -158,6 +159,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();  // prologue done; the limbs (or fp16 input), weights and scales are read after this
     const uint32_t a_bytes = static_cast<uint32_t>(p.TH * p.TW * KB);
 
     if (warp == 0) {
@@ -443,6 +445,7 @@ conv_win_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();  // prologue done; the limbs (or fp16 input), weights and scales are read after this
     const int64_t plane = static_cast<int64_t>(p.Hp) * p.Wp;
 
     if (warp == 0) {
@@ -721,6 +724,7 @@ conv_stk_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();  // prologue done; the limbs (or fp16 input), weights and scales are read after this
     const int64_t plane = static_cast<int64_t>(p.Hp) * p.Wp;
 
     if (warp == 0) {
@@ -1000,6 +1004,7 @@ conv1x1_q_kernel(const __grid_constant__ CUtensorMap tmX, const ConvWinParams p)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();  // prologue done; the limbs (or fp16 input), weights and scales are read after this
 
     if (warp == 0) {
         // ---------------- TMA: fp16 input boxes ----------------
@@ -1461,6 +1466,8 @@ struct ConvPrepArgs {
 
 template <typename T>
 __global__ void __launch_bounds__(XQ_THREADS) conv_prep_kernel(ConvPrepArgs<T> a) {
+    pdl_trigger();  // the convolution kernel may begin its prologue
+    pdl_wait();     // the amax pass has completed
     unsigned b = blockIdx.x;
     if (b < a.wgrid) {
         if (a.stk)
@@ -1479,6 +1486,25 @@ __global__ void __launch_bounds__(XQ_THREADS) conv_prep_kernel(ConvPrepArgs<T> a
                      static_cast<int64_t>(b));
 }
 
+// Launch with programmatic stream serialisation: the kernel may be placed
+// while the kernel before it on the stream drains; it waits (pdl_wait) before
+// reading anything that kernel wrote.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 template <class C, int DT>
 int launch_conv(const CUtensorMap& tx, const CUtensorMap& tw, const ConvTcParams& p, int dev,
                 cudaStream_t stream) {
@@ -1491,7 +1517,7 @@ int launch_conv(const CUtensorMap& tx, const CUtensorMap& tw, const ConvTcParams
     });
     if (err[slot] != cudaSuccess) TK_FAIL(TK_ERR_CUDA, "conv smem attribute: %s", cudaGetErrorString(err[slot]));
     const int grid = std::min(p.tiles, sm_count(dev));
-    conv_tc_kernel<C, DT><<<grid, NUM_THREADS, C::SMEM, stream>>>(tx, tw, p);
+    TK_CUDA_TRY(launch_pdl(conv_tc_kernel<C, DT>, grid, NUM_THREADS, C::SMEM, stream, tx, tw, p));
     return launch_status("conv2d implicit GEMM");
 }
 
@@ -1507,7 +1533,7 @@ int launch_win(const CUtensorMap& tx, const CUtensorMap& tw, const ConvWinParams
     });
     if (err[slot] != cudaSuccess) TK_FAIL(TK_ERR_CUDA, "conv smem attribute: %s", cudaGetErrorString(err[slot]));
     const int grid = std::min(p.tiles, sm_count(dev));
-    conv_win_kernel<C, DT><<<grid, NUM_THREADS, C::SMEM, stream>>>(tx, tw, p);
+    TK_CUDA_TRY(launch_pdl(conv_win_kernel<C, DT>, grid, NUM_THREADS, C::SMEM, stream, tx, tw, p));
     return launch_status("conv2d window implicit GEMM");
 }
 
@@ -1522,7 +1548,7 @@ int launch_stk(const CUtensorMap& tx, const CUtensorMap& tw, const ConvWinParams
     if (err[slot] != cudaSuccess) TK_FAIL(TK_ERR_CUDA, "conv smem attribute: %s", cudaGetErrorString(err[slot]));
     TK_CHECK_ARG(p.tiles_f == 1, "conv stacked kernel: at most 64 filters");
     const int grid = std::min(p.tiles, sm_count(dev));
-    conv_stk_kernel<DT><<<grid, NUM_THREADS, STK_SMEM, stream>>>(tx, tw, p);
+    TK_CUDA_TRY(launch_pdl(conv_stk_kernel<DT>, grid, NUM_THREADS, STK_SMEM, stream, tx, tw, p));
     return launch_status("conv2d stacked window implicit GEMM");
 }
 
@@ -1579,7 +1605,7 @@ int conv1x1_q(const void* x, const void* w, const void* bias, void* out, int64_t
     });
     if (err[slot] != cudaSuccess) TK_FAIL(TK_ERR_CUDA, "conv smem attribute: %s", cudaGetErrorString(err[slot]));
     const int grid = std::min(p.tiles, sm_count(dev));
-    conv1x1_q_kernel<<<grid, NUM_THREADS, Q1_SMEM, stream>>>(tx, p);
+    TK_CUDA_TRY(launch_pdl(conv1x1_q_kernel, grid, NUM_THREADS, Q1_SMEM, stream, tx, p));
     return launch_status("conv2d 1x1 implicit GEMM (input quantised in the kernel)");
 }
 
@@ -1672,12 +1698,11 @@ int conv_tc(tk_dtype_t dtype, const void* x, const void* w, const void* bias, vo
         a.wgrid = static_cast<unsigned>(wblocks);
         a.zgrid = static_cast<unsigned>(zblocks);
         const unsigned grid = static_cast<unsigned>(wblocks + zblocks + xblocks);
-        conv_prep_kernel<T><<<grid, XQ_THREADS, 0, stream>>>(a);
+        return launch_pdl(conv_prep_kernel<T>, grid, XQ_THREADS, 0, stream, a);
     };
-    if (dtype == TK_DTYPE_F16)
-        prep(static_cast<__half*>(nullptr));
-    else
-        prep(static_cast<float*>(nullptr));
+    const cudaError_t le = dtype == TK_DTYPE_F16 ? prep(static_cast<__half*>(nullptr))
+                                                 : prep(static_cast<float*>(nullptr));
+    if (le != cudaSuccess) TK_FAIL(TK_ERR_CUDA, "conv2d limbs launch: %s", cudaGetErrorString(le));
     int rc = launch_status("conv2d limbs");
     if (rc) return rc;
 
