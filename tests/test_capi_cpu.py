@@ -107,3 +107,29 @@ def test_cluster_budget_roundtrip_api():
         assert k.cluster_budget() == 2 and k.sdnn_budget() == 2
     finally:
         k.set_cluster_budget(orig)
+
+
+class _Conv3dDesc(ctypes.Structure):
+    """tk_conv3d_desc_t, as include/tk_kernels.h declares it."""
+    _fields_ = ([("dtype", ctypes.c_int)] +
+                [(n, ctypes.c_int64) for n in ("n", "c", "d", "h", "w", "f", "kd", "kh", "kw", "stride_d",
+                                               "stride_h", "stride_w", "pad_d", "pad_h", "pad_w", "dil_d",
+                                               "dil_h", "dil_w", "groups")] +
+                [(n, ctypes.c_void_p) for n in ("x", "weight", "bias", "out", "amax_x", "amax_w")])
+
+
+def test_depthwise_workspace_holds_the_partial_maxima():
+    """The depthwise path keeps its two amax slots and 2 x 512 partial words
+    (one per depthwise_amax_kernel block and operand) in the workspace."""
+    L = C.lib()
+    L.tk_conv3d_workspace_size.argtypes = [ctypes.POINTER(_Conv3dDesc)]
+    L.tk_conv3d_workspace_size.restype = ctypes.c_size_t
+    d = _Conv3dDesc()
+    d.dtype = 0
+    d.n, d.c, d.d, d.h, d.w, d.f = 64, 512, 1, 7, 7, 512
+    d.kd, d.kh, d.kw = 1, 3, 3
+    d.stride_d = d.stride_h = d.stride_w = 1
+    d.pad_d, d.pad_h, d.pad_w = 0, 1, 1
+    d.dil_d = d.dil_h = d.dil_w = 1
+    d.groups = 512
+    assert L.tk_conv3d_workspace_size(ctypes.byref(d)) >= 1024 + 2 * 512 * 4

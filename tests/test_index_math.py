@@ -105,3 +105,80 @@ def test_stacked_limb_recombination_is_exact():
         mid = wrap(acc1_m + acc2_f - 128 * s_lo)
         ll = acc2_m
         assert 65536 * hh + 256 * mid + ll == sum(x * y for x, y in zip(a, b))
+
+
+def _ceil_div(a, b):
+    return (a + b - 1) // b
+
+
+def test_conv_prep_block_split_covers_each_job_once():
+    """conv_prep_kernel (conv_tc.cu): blocks [0, wgrid) prepare the weight,
+    [wgrid, wgrid + zgrid) zero the padding ring, the rest quantise the input.
+    Restates the host grid sizes and the kernel's split: every x block maps to
+    one (image, pixel run, channel group), every w_limbs block to one (filter,
+    group, tap run) whose 64 x nt items each hit one (channel, tap) slot, and
+    the grid-strided ring and stacked-tile loops visit every item once."""
+    WQ_TAPS, XQ_W, STK_N = 32, 128, 144
+    for N, C, H, W, F, k, pad, stk in [(2, 64, 7, 9, 64, 3, 1, True), (1, 200, 5, 5, 96, 3, 1, False),
+                                       (3, 70, 4, 6, 256, 5, 2, False), (2, 64, 9, 9, 48, 1, 0, True)]:
+        taps = k * k
+        Cg = _ceil_div(C, 64)
+        Hp, Wp = H + 2 * pad, W + 2 * pad
+        npairs = _ceil_div(taps * Cg, 2)
+        ring = Hp * Wp - H * W
+        zblocks = max(1, min(_ceil_div(N * ring * Cg * 8, 256), 8 * 148)) if pad else 0
+        runs = _ceil_div(H * W, XQ_W)
+        xblocks = N * runs * Cg
+        wblocks = _ceil_div(npairs * STK_N * 8, 256) if stk else F * Cg * _ceil_div(taps, WQ_TAPS)
+        grid = wblocks + zblocks + xblocks
+        seen_x, seen_w, seen_z, seen_s = set(), set(), [], []
+        for blk in range(grid):
+            b = blk
+            if b < wblocks:
+                if stk:
+                    seen_s += [b * 256 + t + s * wblocks * 256 for t in range(256)
+                               for s in range(_ceil_div(npairs * STK_N * 8, wblocks * 256))
+                               if b * 256 + t + s * wblocks * 256 < npairs * STK_N * 8]
+                else:
+                    r = _ceil_div(taps, WQ_TAPS)
+                    run, g, f = b % r, (b // r) % Cg, b // (r * Cg)
+                    nt = min(WQ_TAPS, taps - run * WQ_TAPS)
+                    items = [(it // nt, it - (it // nt) * nt) for it in range(64 * nt)]
+                    assert sorted(items) == [(cc, t) for cc in range(64) for t in range(nt)]
+                    seen_w.add((f, g, run))
+                continue
+            b -= wblocks
+            if b < zblocks:
+                total = N * ring * Cg * 8
+                it = b * 256
+                while it < total:
+                    seen_z += [i for i in range(it, min(it + 256, total))]
+                    it += zblocks * 256
+                continue
+            b -= zblocks
+            seen_x.add((b // Cg // runs, (b // Cg) % runs, b % Cg))
+        assert len(seen_x) == xblocks == N * runs * Cg
+        if stk:
+            assert sorted(seen_s) == list(range(npairs * STK_N * 8))
+        else:
+            assert len(seen_w) == wblocks
+        if pad:
+            assert sorted(seen_z) == list(range(N * ring * Cg * 8))
+
+
+def test_depthwise_partials_cover_input_and_filters():
+    """depthwise_scaled_launch (conv.cu): nparts blocks of depthwise_amax_kernel
+    take chunks [b*cx, (b+1)*cx) of the input and [b*cw, (b+1)*cw) of the
+    filters, clipped to the ends; chunks are whole 16-byte vectors, cover each
+    element once, and nparts never exceeds the 512 partial words per operand
+    that the workspace holds."""
+    for nx, nw, esize in [(64 * 512 * 49, 512 * 9, 2), (7, 3, 2), (1000003, 25, 4), (16 * 1024 * 1024, 7 * 7 * 64, 2)]:
+        vec = 16 // esize
+        nparts = max(1, min(512, _ceil_div(nx * esize, 4 * 1024)))
+        cx = _ceil_div(_ceil_div(nx, nparts), vec) * vec
+        cw = _ceil_div(_ceil_div(nw, nparts), vec) * vec
+        assert nparts <= 512 and cx % vec == 0 and cw % vec == 0
+        for n, c in ((nx, cx), (nw, cw)):
+            spans = [(min(n, b * c), min(n, (b + 1) * c)) for b in range(nparts)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(nparts - 1))
