@@ -1486,25 +1486,6 @@ __global__ void __launch_bounds__(XQ_THREADS) conv_prep_kernel(ConvPrepArgs<T> a
                      static_cast<int64_t>(b));
 }
 
-// Launch with programmatic stream serialisation: the kernel may be placed
-// while the kernel before it on the stream drains; it waits (pdl_wait) before
-// reading anything that kernel wrote.
-template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
-                       Args&&... args) {
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(block);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
-
 template <class C, int DT>
 int launch_conv(const CUtensorMap& tx, const CUtensorMap& tw, const ConvTcParams& p, int dev,
                 cudaStream_t stream) {

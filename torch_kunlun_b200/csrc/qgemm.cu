@@ -916,17 +916,8 @@ int launch_one(int dev, int grid, const CUtensorMap& tmA, const CUtensorMap& tmB
     }
     // programmatic stream serialisation: the CTAs may be placed and run
     // their prologue while the quantise kernel before them drains
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(grid));
-    cfg.blockDim = dim3(64 + 32 * EW);
-    cfg.dynamicSmemBytes = C::SMEM;
-    cfg.stream = stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    TK_CUDA_TRY(cudaLaunchKernelEx(&cfg, qgemm_tc_kernel<C, DT, ACT, EW, FO>, tmA, tmB, tp, ep));
+    TK_CUDA_TRY(launch_pdl(qgemm_tc_kernel<C, DT, ACT, EW, FO>, static_cast<unsigned>(grid), 64 + 32 * EW,
+                           C::SMEM, stream, tmA, tmB, tp, ep));
     return TK_OK;
 }
 

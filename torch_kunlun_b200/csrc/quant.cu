@@ -558,21 +558,12 @@ int launch_quant_vec(tk_dtype_t dt, const QVecDesc* vd, int nvec, cudaStream_t s
     const int64_t blocks = ceil_div(items0 + items1, 8);
     TK_CHECK_ARG(blocks < (1LL << 31), "quantise: too many rows");
     const QVecDesc second = nvec > 1 ? vd[1] : vd[0];
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(blocks));
-    cfg.blockDim = dim3(32, 8);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
     const int64_t total = items0 + items1;
+    const dim3 grid(static_cast<unsigned>(blocks)), block(32, 8);  // 8 warps, one item (row segment) each
     if (dt == TK_DTYPE_F16)
-        TK_CUDA_TRY(cudaLaunchKernelEx(&cfg, quant_vec_kernel<__half>, vd[0], second, items0, total));
+        TK_CUDA_TRY(launch_pdl(quant_vec_kernel<__half>, grid, block, 0, stream, vd[0], second, items0, total));
     else
-        TK_CUDA_TRY(cudaLaunchKernelEx(&cfg, quant_vec_kernel<float>, vd[0], second, items0, total));
+        TK_CUDA_TRY(launch_pdl(quant_vec_kernel<float>, grid, block, 0, stream, vd[0], second, items0, total));
     return launch_status("quantise");
 }
 
