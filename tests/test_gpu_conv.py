@@ -101,16 +101,17 @@ DW_CASES = [
     (1, 7, 1, 11, 11, 7, 1, 3, 1, True, torch.float16),    # 7x7
     (2, 3, 1, 1, 40, 3, 1, 1, 1, False, torch.float16),    # one-row planes, padding wider than the row
     (2, 6, 1, 5, 5, 3, 1, 2, 1, True, torch.float32),      # padding 2: outputs beyond the input
-    # more blocks than fit on the device at once: the two-pass path (amax
-    # launch, then the row kernel) instead of the one cooperative launch
+    # more blocks than fit on the device in one wave: the two-pass path (amax
+    # launch, then the row kernel) instead of the partials + scaled kernels
     (64, 512, 1, 14, 14, 3, 1, 1, 1, True, torch.float16),
 ]
 
 
-def test_depthwise_fused_scales_propagate_non_finite():
+def test_depthwise_scaled_path_propagates_non_finite():
     """A NaN or an infinity anywhere in the input makes the input scale
     non-finite, so every output is NaN (the library's convention), through
-    the one-launch path whose blocks combine their scales at a grid barrier."""
+    the path whose convolution kernel folds the partial maxima of the amax
+    kernel before it."""
     for bad in (float("nan"), float("inf")):
         x = torch.relu(rnd((4, 32, 7, 7), 49))
         x[3, 31, 6, 6] = bad
