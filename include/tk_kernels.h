@@ -10,6 +10,10 @@
  *   - all pointers are device pointers unless stated; `stream` is a
  *     cudaStream_t (NULL = legacy default stream of the current device);
  *   - work is enqueued asynchronously on `stream`; nothing synchronises;
+ *   - some kernels are launched with programmatic dependent launch: they may
+ *     be placed while the previous kernel on `stream` is still running, but
+ *     touch global memory only after it has completed, so stream order holds
+ *     exactly as for ordinary launches;
  *   - element strides are in elements, not bytes;
  *   - functions are reentrant and keep no per-call global state, except
  *     tk_qgemm_noalloc, whose scratch is one array shared by all its calls.
